@@ -1,0 +1,410 @@
+#!/usr/bin/env python
+"""Benchmark of the relation-typed sparse hop path (MiniKG proof loop) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload kg_mid] [--impl ours|reference]
+
+A step is one training pass of the hop loop over one query batch: the forward of every
+hop (op + concat + mass normalisation, then the sum over rules) and its backward to the
+per-hop rule weights and the edge scores, on the 17,050-entity / 51-relation /
+206,205-triple synthetic graph with 256 queries x 3 rules x 3 hops, uncapped.  The
+metric is edge-messages per second (GTEPS): the messages of all hops (frontier entries x
+their taken out-edges, both directions) divided by the fwd+bwd step time.  Under torchrun
+every rank runs its own 256 queries on a replica of the graph (query-batch sharding, weak
+scaling, no collective in the data path); ``value`` sums all ranks' messages over the
+slowest rank's time.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference algorithm
+(the numpy oracle port of the reference's CPU path) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from minikg_dev_b200.synth import WORKLOADS, hop_inputs, workload_graph  # noqa: E402
+
+METRIC = "GTEPS (edge-msgs/s) per hop fwd+bwd & argmax decode; % of HBM roofline"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="kg_mid")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-queries", type=int, default=0, help="0: pick automatically")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU side
+_W = {}
+
+
+def _worker_init(head, rel, tail, E, R, heads, w_hops, scores, cap):
+    """Spawned worker: keeps the graph, its oracle CSR and the batch inputs."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import fastlog_oracle as O
+    _W.update(head=head, E=E, R=R, heads=heads, w_hops=w_hops, scores=scores, cap=cap,
+              csr=O.build_csr_structure(head, tail, rel, E))
+
+
+def _oracle_queries(query_ids):
+    """One fwd+bwd of the hop loop on a query subset with the numpy oracle; returns messages."""
+    from oracle import fastlog_oracle as O
+    q = np.asarray(query_ids, np.int64)
+    heads = _W["heads"][q]
+    w_hops = np.ascontiguousarray(_W["w_hops"][:, q])
+    E, R, csr, scores, cap = _W["E"], _W["R"], _W["csr"], _W["scores"], _W["cap"]
+    B, L = heads.shape[0], w_hops.shape[2]
+    mask = np.ones(_W["head"].shape[0], bool)
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R, cap=cap)
+    seed = np.random.default_rng(0).standard_normal(final[0].shape[0]).astype(np.float32)
+    O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
+                         num_facts=_W["head"].shape[0])
+    return sum(O.count_messages(tr["state"], csr, w_hops[k], L, E, R, cap) for k, tr in enumerate(trace))
+
+
+def cpu_sample(kg, inp, queries: int, cap: int):
+    """(messages, seconds) of the oracle on the first ``queries`` queries, one thread."""
+    _worker_init(kg.head, kg.rel, kg.tail, kg.num_entities, kg.num_relations, inp.heads, inp.rule_weights,
+                 inp.edge_scores, cap)
+    t0 = time.perf_counter()
+    msgs = _oracle_queries(list(range(queries)))
+    return msgs, time.perf_counter() - t0
+
+
+def run_reference(a, wl, kg, rank, world):
+    """The reference arm: the reference algorithm (oracle port) on all host cores, rank 0 only."""
+    if rank != 0:
+        return
+    import multiprocessing as mp
+    inp = hop_inputs(kg, wl.B, wl.L, wl.hops, seed=0)
+    cores = os.cpu_count() or 1
+    per = max(1, a.cpu_sample_queries or 2)
+    n_q = min(wl.B, per * cores)
+    chunks = [list(range(i, min(i + per, n_q))) for i in range(0, n_q, per)]
+    ctx = mp.get_context("spawn")
+    times, msgs_all = [], []
+    with ctx.Pool(processes=min(cores, len(chunks)), initializer=_worker_init,
+                  initargs=(kg.head, kg.rel, kg.tail, kg.num_entities, kg.num_relations, inp.heads,
+                            inp.rule_weights, inp.edge_scores, wl.topk_edges)) as pool:
+        for it in range(a.warmup + a.steps):
+            t0 = time.perf_counter()
+            msgs = sum(pool.map(_oracle_queries, chunks))
+            dt = time.perf_counter() - t0
+            if it >= a.warmup:
+                times.append(dt)
+                msgs_all.append(msgs)
+    value = sum(msgs_all) / sum(times) / 1e9
+    line = {"metric": METRIC, "value": value, "unit": "GTEPS", "n_gpus": a.gpus, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": 1e3 * statistics.mean(times), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": wl.name, "queries_per_step": n_q, "rules": wl.L, "hops": wl.hops,
+                       "entities": wl.E, "relations": wl.R, "triples": wl.T, "edge_cap": "uncapped"},
+            "cpu_baseline": {"value": value, "unit": "GTEPS", "cores": min(cores, len(chunks)), "kind": "port",
+                             "sample": f"{n_q} of {wl.B} queries per step, fwd+bwd of all {wl.hops} hops, numpy "
+                                       f"oracle port of the reference CPU path in {len(chunks)} spawned processes"},
+            "e2e": {"value": value, "unit": "GTEPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU side
+def run_ours(a, wl, kg, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import ProofRunner
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    inp = hop_inputs(kg, wl.B, wl.L, wl.hops, seed=rank)
+    head = torch.from_numpy(kg.head).to(dev)
+    rel = torch.from_numpy(kg.rel).to(dev)
+    tail = torch.from_numpy(kg.tail).to(dev)
+    g = DeviceGraph.from_triples(head, rel, tail, kg.num_entities, kg.num_relations)
+    g.adjacency()
+    B, L, K, E, T = wl.B, wl.L, wl.hops, kg.num_entities, kg.num_triples
+    n = 2 * kg.num_relations + 1
+    heads = torch.from_numpy(inp.heads).to(dev)
+    w_hops = torch.from_numpy(inp.rule_weights).to(dev)
+    scores = torch.from_numpy(inp.edge_scores).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    G = torch.randn((B, E), device=dev, generator=gen)  # d loss / d scores on the result's keys
+    runner = ProofRunner(g, B, L, K)
+    out = torch.empty((B, E), device=dev)
+    msgs = torch.zeros(K, dtype=torch.int64, device=dev)
+    grad_w = torch.empty((K, B, L, n), device=dev)
+    grad_edge = torch.empty(T, device=dev)
+    ev_f = [torch.cuda.Event(enable_timing=True) for _ in range(2 * K)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(2 * K)]
+    for e in ev_f + ev_b:
+        e.record()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > 126 MB L2
+
+    def step(events=True):
+        g.set_edge_factor(None, scores, True, 1.0)
+        runner.forward(heads, w_hops, out, msgs, ev_f if events else None)
+        runner.backward(G, None, scores, True, 1.0, True, grad_w, grad_edge, ev_b if events else None)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    from minikg_dev_b200 import _native
+    _native.raise_device_errors(dev)
+    msgs_host = [int(x) for x in msgs.cpu()]
+    M = sum(msgs_host)
+
+    # compulsory bytes per hop (pull of hop h reads the state entering hop h)
+    push_deg = g.push_degree()
+    c = g.csr
+    grp = ((c[8][1:] - c[8][:-1]) + (c[12][1:] - c[12][:-1])).to(torch.int64)
+    graph_bytes = []
+    for h in range(K):
+        act = runner.row_activity(h).bool()
+        graph_bytes.append(int((push_deg[act] * 8 + grp[act] * 10 + 16).sum().item()))
+    BL = B * L
+    dense = E * BL * 4
+    fwd_bytes = [gb + 2 * dense + BL * n * 4 for gb in graph_bytes]
+    bwd_bytes = [gb + 3 * dense + BL * n * 4 + T * 4 for gb in graph_bytes]
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    step_ms, fwd_ms, bwd_ms = [], [], []
+    with ClockSampler(local_rank) as clocks:
+        for _ in range(a.steps):
+            flush.zero_()
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record()
+            step()
+            s1.record()
+            s1.synchronize()
+            step_ms.append(s0.elapsed_time(s1))
+            fwd_ms.append([ev_f[2 * h].elapsed_time(ev_f[2 * h + 1]) for h in range(K)])
+            bwd_ms.append([ev_b[2 * h].elapsed_time(ev_b[2 * h + 1]) for h in range(K)])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = float(sum(step_ms))
+    M_all = M
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        mm = torch.tensor([M], device=dev, dtype=torch.int64)
+        dist.all_reduce(mm, op=dist.ReduceOp.SUM)
+        M_all = int(mm.item())
+    value = M_all * a.steps / (total_ms / 1e3) / 1e9
+
+    # end to end through the public API, host buffers, copies inside the timed region
+    heads_h = torch.from_numpy(inp.heads).pin_memory()
+    w_h = torch.from_numpy(inp.rule_weights).pin_memory()
+    scores_h = torch.from_numpy(inp.edge_scores).pin_memory()
+    loss_h = torch.empty(1, pin_memory=True)
+    gw_h = torch.empty((K, B, L, n), pin_memory=True)
+    ge_h = torch.empty(T, pin_memory=True)
+    h2d = heads_h.numel() * 8 + w_h.numel() * 4 + scores_h.numel() * 4
+    d2h = 4 + gw_h.numel() * 4 + ge_h.numel() * 4
+
+    def e2e_step():
+        heads.copy_(heads_h, non_blocking=True)
+        w_hops.copy_(w_h, non_blocking=True)
+        scores.copy_(scores_h, non_blocking=True)
+        g.set_edge_factor(None, scores, True, 1.0)
+        runner.forward(heads, w_hops, out, msgs)
+        loss = (out * G).sum()
+        runner.backward(G, None, scores, True, 1.0, True, grad_w, grad_edge)
+        loss_h.copy_(loss.view(1), non_blocking=True)
+        gw_h.copy_(grad_w, non_blocking=True)
+        ge_h.copy_(grad_edge, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_ms = []
+    for _ in range(a.steps):
+        flush.zero_()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        e2e_step()
+        s1.record()
+        s1.synchronize()
+        e2e_ms.append(s0.elapsed_time(s1))
+    e2e_total = float(sum(e2e_ms))
+    if world > 1:
+        t = torch.tensor([e2e_total], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e_value = M_all * a.steps / (e2e_total / 1e3) / 1e9
+
+    # max-argmax decode (forward only) of the same batch, top-100 answers per query
+    from minikg_dev_b200.proof import decode_max
+    for _ in range(2):
+        decode_max(g, heads, w_hops, 100, scores)
+    torch.cuda.synchronize()
+    dec_ms = []
+    for _ in range(max(3, a.steps // 2)):
+        flush.zero_()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        decode_max(g, heads, w_hops, 100, scores)
+        s1.record()
+        s1.synchronize()
+        dec_ms.append(s0.elapsed_time(s1))
+
+    if rank != 0:
+        return
+    hbm, peak_kind = peaks()
+    fwd_avg = [statistics.mean(x[h] for x in fwd_ms) for h in range(K)]
+    bwd_avg = [statistics.mean(x[h] for x in bwd_ms) for h in range(K)]
+    kernels = {
+        "fwd_pull_kernel": {"ms_per_launch": sum(fwd_avg) / K, "bytes_per_launch": sum(fwd_bytes) / K,
+                            "gbs": sum(fwd_bytes) / (sum(fwd_avg) / 1e3) / 1e9, "ms_per_hop": fwd_avg},
+        "bwd_pull_kernel": {"ms_per_launch": sum(bwd_avg) / K, "bytes_per_launch": sum(bwd_bytes) / K,
+                            "gbs": sum(bwd_bytes) / (sum(bwd_avg) / 1e3) / 1e9, "ms_per_hop": bwd_avg},
+    }
+    dom = max(kernels, key=lambda k: kernels[k]["ms_per_launch"])
+    traffic = None
+    tfile = ROOT / "profiles" / f"traffic_{wl.name}.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(dom)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GTEPS", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": total_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded; shapes of the reference workload)",
+        "config": {"workload": wl.name, "entities": E, "relations": kg.num_relations, "triples": T,
+                   "queries_per_gpu": B, "global_queries": B * world, "rules": L, "hops": K,
+                   "edge_cap": "uncapped", "parallelism": f"query-batch x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed (256 MB write) before every timed step",
+                   "messages_per_step": M_all, "messages_per_hop": msgs_host},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": kernels[dom]["gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": kernels[dom]["gbs"] / hbm, "peak_kind": peak_kind, "traffic": traffic},
+        "kernels": kernels,
+        "decode": {"ms": statistics.mean(dec_ms), "topk": 100,
+                   "gteps": M / (statistics.mean(dec_ms) / 1e3) / 1e9},
+        "e2e": {"value": e2e_value, "unit": "GTEPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_total / a.steps},
+        "gpu_launches": (7 + 7 * K) * a.steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not a.no_cpu_baseline:
+        q = a.cpu_sample_queries or 24
+        msgs_cpu, secs = cpu_sample(kg, inp, q, wl.topk_edges)
+        line["cpu_baseline"] = {"value": msgs_cpu / secs / 1e9, "unit": "GTEPS", "cores": 1, "kind": "port",
+                                "sample": f"{q} of {B} queries, fwd+bwd of all {K} hops ({msgs_cpu} messages in "
+                                          f"{secs:.1f} s), numpy oracle port of the reference CPU path"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    wl = WORKLOADS[a.workload]
+    kg = workload_graph(a.workload, seed=0)
+    if a.impl == "reference":
+        run_reference(a, wl, kg, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(a, wl, kg, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

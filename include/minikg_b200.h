@@ -1,0 +1,279 @@
+/*
+ * minikg_b200 — C ABI of the B200 (sm_100a) relation-typed sparse hop library.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream, returns an
+ * int status (MKG_OK = 0) and leaves a message for mkg_last_error() on failure.  The
+ * library never allocates device memory: callers pass output buffers and a workspace
+ * sized by the matching *_workspace_bytes() query.  Kernels that meet a bad index do
+ * not fault; they skip the access and set a bit in the caller's device error word.
+ *
+ * Each declaration names the reference interface (majh3/miniKG_dev) it replaces.
+ */
+#ifndef MINIKG_B200_H
+#define MINIKG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* mkg_stream; /* a cudaStream_t; NULL = legacy default stream */
+
+enum {
+  MKG_OK = 0,
+  MKG_ERR_ARG = 1,       /* bad shape / size / pointer / parameter */
+  MKG_ERR_INDEX = 2,     /* a device kernel reported an out-of-range index */
+  MKG_ERR_CAPACITY = 3,  /* workspace or output smaller than required */
+  MKG_ERR_CUDA = 4,      /* a CUDA runtime call failed */
+  MKG_ERR_TIMEOUT = 5,   /* a bounded device wait gave up */
+  MKG_ERR_UNSUPPORTED = 6
+};
+
+enum { MKG_MASK_NONE = 0, MKG_MASK_U8 = 1, MKG_MASK_F32 = 2 };
+
+/* bits of the device error word */
+enum {
+  MKG_DEV_BAD_ENTRY = 1u,  /* frontier (batch, level, entity) outside [B, L, E] */
+  MKG_DEV_BAD_COL = 2u,    /* CSR column / neighbour outside [0, E) */
+  MKG_DEV_BAD_FACT = 4u,   /* CSR order / fact id outside [0, T) */
+  MKG_DEV_BAD_KEY = 8u,    /* gradient COO key outside [B, L, E] */
+  MKG_DEV_BAD_REL = 16u    /* relation id outside [0, R) */
+};
+
+/* One direction of the reference CSR pair (fastlog_kernel.py:403-410 tuple order). */
+typedef struct mkg_csr_dir {
+  const int32_t* row_ptr;          /* [E+1] */
+  const int32_t* col_ind;          /* [T]   neighbour per CSR position */
+  const int16_t* r_ind;            /* [T]   relation per CSR position */
+  const int32_t* order;            /* [T]   original fact id per CSR position */
+  const int32_t* row_group_ptr;    /* [E+1] */
+  const int16_t* group_rel;        /* [G] */
+  const int32_t* group_edge_start; /* [G] */
+  const int32_t* group_edge_count; /* [G] */
+  int64_t num_groups;
+} mkg_csr_dir;
+
+typedef struct mkg_graph {
+  int64_t num_entities;  /* E */
+  int64_t num_relations; /* R (relation ids lie in [0, R)) */
+  int64_t num_facts;     /* T */
+  mkg_csr_dir ori;       /* rows = head, sorted by (head, rel, fact id) */
+  mkg_csr_dir inv;       /* rows = tail, sorted by (tail, rel, fact id) */
+} mkg_graph;
+
+/* Edge factor m = bool(mask[f]) * score(f) (fastlog.cu:2303-2309). */
+typedef struct mkg_edge_factor {
+  const void* mask;           /* NULL: all facts on */
+  int32_t mask_kind;          /* MKG_MASK_* */
+  int64_t mask_numel;         /* T, or 1 to broadcast one value to every fact */
+  const float* edge_weight;   /* [T] or NULL */
+  int64_t edge_weight_numel;  /* 0: no score factor */
+  int32_t is_score;           /* 1: score = weight; 0: score = sigmoid(weight * scale) */
+  float scale;
+} mkg_edge_factor;
+
+/* Sparse [B, L, E] frontier in COO (the op's sp_batch/sp_level/sp_entity/sp_value). */
+typedef struct mkg_frontier {
+  const int64_t* batch;
+  const int64_t* level;
+  const int64_t* entity;
+  const float* value;
+  int64_t nnz;
+} mkg_frontier;
+
+/* Sparse [B, L, E] gradient / output in COO: indices [3, nnz] row-major, values [nnz]. */
+typedef struct mkg_coo3 {
+  const int64_t* indices;
+  const float* values;
+  int64_t nnz;
+} mkg_coo3;
+
+const char* mkg_last_error(void);
+int mkg_abi_version(void);
+
+/* ------------------------------------------------------------------ graph build */
+
+/* Caller-allocated outputs of mkg_csr_build; group arrays are sized T (upper bound). */
+typedef struct mkg_csr_dir_out {
+  int32_t* row_ptr;
+  int32_t* col_ind;
+  int16_t* r_ind;
+  int32_t* order;
+  int32_t* row_group_ptr;
+  int16_t* group_rel;
+  int32_t* group_edge_start;
+  int32_t* group_edge_count;
+} mkg_csr_dir_out;
+
+/* Replaces build_csr_structure (src/fastlog_kernel/fastlog_kernel.py:371-411) and its
+ * helpers _build_group_metadata (:354-368) / _ind2ptr_cpu (:346-351): device radix
+ * sort to a stable (row, rel, fact id) order for both directions.  Writes the two
+ * group counts to num_groups_out (device int64[2]). */
+size_t mkg_csr_build_workspace_bytes(int64_t num_facts, int64_t num_entities, int64_t num_relations);
+int mkg_csr_build(const int32_t* head, const int32_t* rel, const int32_t* tail, int64_t num_facts,
+                  int64_t num_entities, int64_t num_relations, mkg_csr_dir_out ori,
+                  mkg_csr_dir_out inv, int64_t* num_groups_out, void* workspace,
+                  size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+
+/* Replaces ind2ptr (src/fastlog_kernel/source/fastlog.cpp:9-16, fastlog.h:13):
+ * ptr[0..size] = exclusive prefix of the per-row counts of index[0..n), ptr[size] = n. */
+size_t mkg_ind2ptr_workspace_bytes(int64_t size);
+int mkg_ind2ptr(const int64_t* index, int64_t n, int64_t size, int64_t* ptr, void* workspace,
+                size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+
+/* Per-fact endpoints recovered from the ori CSR (used by the argmax backward):
+ * fact_head[f], fact_tail[f], fact_rel[f].  No reference counterpart: the reference
+ * keeps them per raw message (meta_entry / meta_rel, fastlog.cu:2314-2317). */
+int mkg_fact_table(const mkg_graph* g, int32_t* fact_head, int32_t* fact_tail, int16_t* fact_rel,
+                   unsigned* dev_err, mkg_stream stream);
+
+/* Merged neighbour lists of the fused engine.  pull row d = every message that can reach
+ * d: facts with tail d (neighbour = head, channel = rel) then facts with head d
+ * (neighbour = tail, channel = R + rel); push row s = every message s can send.  Records
+ * are 16 bytes: {neighbour, channel, fact id, edge factor}. */
+typedef struct mkg_adj_edge {
+  int32_t nbr;
+  int32_t channel;
+  int32_t fact;
+  float factor;
+} mkg_adj_edge;
+
+/* Rows are cut into tasks of at most 64 records: int32 quadruples {row, begin, end, flags}
+ * (flags: 1 = first task of its row, 2 = the row spans several tasks). */
+typedef struct mkg_adjacency {
+  int32_t* pull_ptr;      /* [E+1] */
+  mkg_adj_edge* pull;     /* [2T] */
+  int32_t* push_ptr;      /* [E+1] */
+  mkg_adj_edge* push;     /* [2T] */
+  int32_t* pull_tasks;    /* [4 * mkg_adjacency_max_tasks(E, T)] */
+  int64_t num_pull_tasks; /* filled by the caller from num_tasks_out[0] */
+  int32_t* push_tasks;    /* [4 * mkg_adjacency_max_tasks(E, T)] */
+  int64_t num_push_tasks; /* filled by the caller from num_tasks_out[1] */
+} mkg_adjacency;
+
+int64_t mkg_adjacency_max_tasks(int64_t num_entities, int64_t num_facts);
+size_t mkg_adjacency_workspace_bytes(int64_t num_entities);
+/* Builds both neighbour lists and their task lists; writes the two task counts to
+ * num_tasks_out (device int64[2]).  No reference counterpart (the reference pushes raw
+ * messages per frontier entry, fastlog.cu:2197-2323). */
+int mkg_adjacency_build(const mkg_graph* g, mkg_adjacency adj, int64_t* num_tasks_out, void* workspace,
+                        size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+/* Rewrites the factor field of every record from the current mask / edge scores. */
+int mkg_adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, const mkg_edge_factor* f,
+                             mkg_stream stream);
+
+/* ------------------------------------------------------------------ per-hop op */
+
+typedef struct mkg_hop_params {
+  int64_t B, L, E;
+  int64_t r_size;      /* channel offset of the inverse direction (= R) */
+  int64_t n;           /* channels of w: w is [B, L, n], identity channel n-1 */
+  int32_t wot_i;       /* 1: identity channel contributes zeros */
+  int32_t agg_mode;    /* 0 sum, 1 max with argmax */
+  int64_t topk_edges;  /* per-entry edge cap; >= 2^60 means uncapped */
+} mkg_hop_params;
+
+/* Forward of one hop, coalesced: replaces fastlog_forward_sparse3d_topk_cuda
+ * (src/fastlog_kernel/source/fastlog.h:78-93, fastlog.cu:2678-2806) together with the
+ * torch coalescing that follows it (fastlog_kernel.py:951-966, _coalesce_sparse3d_reduce
+ * :81-104, _coalesce_sparse3d_max_with_arg :107-150).  Raw messages are never
+ * materialised: they are reduced in HBM slabs indexed by the key b*L*E + l*E + e.
+ * Writes the output sizes (ori, inv, ind) to counts_out (device int64[3]).  The
+ * workspace must stay alive and unmodified until mkg_hop_emit has run for all three. */
+size_t mkg_hop_forward_workspace_bytes(const mkg_hop_params* p, int64_t nnz);
+int mkg_hop_forward(const mkg_graph* g, const mkg_frontier* f, const float* w,
+                    const mkg_edge_factor* ef, const mkg_hop_params* p, void* workspace,
+                    size_t workspace_bytes, int64_t* counts_out, unsigned* dev_err, mkg_stream stream);
+
+/* Writes output `which` (0 ori, 1 inv, 2 ind) as sorted coalesced COO: indices [3, count]
+ * (int64), values [count]; for agg_mode 1 and which < 2 also arg_fact [count] = fact id of
+ * the argmax message (smallest fact id among equal maxima).  nnz = the forward's frontier size. */
+int mkg_hop_emit(const mkg_hop_params* p, int64_t nnz, const void* workspace, size_t workspace_bytes,
+                 int which, int64_t count, int64_t* indices, float* values, int64_t* arg_fact,
+                 mkg_stream stream);
+
+/* Backward of one hop: replaces fastlog_backward_sparse3d_topk_cuda (fastlog.h:123-134,
+ * fastlog.cu:3037-3109) for agg_mode 0 and fastlog_backward_sparse3d_topk_aligned_cuda
+ * (fastlog.h:136-145, fastlog.cu:3111-3181) with _align_sparse_grad_to_raw_argmax
+ * (fastlog_kernel.py:153-167) for agg_mode 1, plus the edge-score gradient of
+ * fastlog_kernel.py:1032-1098.  grad_ori / grad_inv / grad_ind are the incoming COO
+ * gradients; for agg_mode 1, out_ori / out_inv are the forward outputs (indices) with
+ * their arg_fact arrays.  Writes grad_sp [nnz], grad_w [B, L, n] and, when not NULL,
+ * grad_edge [T] (all overwritten). */
+size_t mkg_hop_backward_workspace_bytes(const mkg_hop_params* p, int64_t nnz);
+int mkg_hop_backward(const mkg_graph* g, const mkg_frontier* f, const float* w,
+                     const mkg_edge_factor* ef, const mkg_hop_params* p, const mkg_coo3* grad_ori,
+                     const mkg_coo3* grad_inv, const mkg_coo3* grad_ind, const mkg_coo3* out_ori,
+                     const int64_t* arg_ori, const mkg_coo3* out_inv, const int64_t* arg_inv,
+                     const int32_t* fact_head, const int32_t* fact_tail, const int16_t* fact_rel,
+                     float* grad_sp, float* grad_w, float* grad_edge, void* workspace,
+                     size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+
+/* ------------------------------------------------------------------ fused hop loop */
+
+typedef struct mkg_proof_params {
+  int64_t B, L, E, R;
+  int64_t hops;
+  int64_t topk_edges;      /* per-entry edge cap (>= 2^60: uncapped) */
+  float state_threshold;   /* >0: drop normalised state values below it after each hop */
+  int32_t reserved;
+  /* Optional caller-owned cudaEvent_t arrays of 2*hops events each (NULL: none).  The
+   * library records event 2h before and 2h+1 after the pull kernel of hop h (forward) /
+   * the transposed pull of hop h (backward), on the call's stream. */
+  void* const* fwd_events;
+  void* const* bwd_events;
+} mkg_proof_params;
+
+/* The whole hop loop of kernel_sparse_scores (proof.py:467-614, dropout off, no entity
+ * pruning) on a dense entity-major state: per hop the op, sum_sparse3d_concat
+ * (fastlog_bridge.py:26-42), normalize_sparse3d(.., 0, "mass") (drum.py:31-51); then
+ * sum_sp_3d (fastlog_bridge.py:17-23) into out [B, E].  w_hops is [hops, B, L, 2R+1].
+ * The workspace keeps every hop's state for mkg_proof_backward; messages_out (device
+ * int64[hops], may be NULL) receives the per-hop message counts. */
+size_t mkg_proof_workspace_bytes(const mkg_proof_params* p);
+int mkg_proof_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64_t* heads,
+                      const float* w_hops, const mkg_proof_params* p, void* workspace,
+                      size_t workspace_bytes, float* out, int64_t* messages_out, unsigned* dev_err,
+                      mkg_stream stream);
+
+/* Row activity of the state that entered hop h of the last mkg_proof_forward /
+ * mkg_proof_decode_max run in this workspace: row_flags[e] = 1 when entity e holds a
+ * non-zero value for some (query, rule).  Used to count the compulsory bytes of a hop. */
+int mkg_proof_row_activity(const mkg_proof_params* p, const void* workspace, size_t workspace_bytes, int64_t h,
+                           uint8_t* row_flags, mkg_stream stream);
+
+/* Gradients of mkg_proof_forward: grad_out [B, E] (only entries where out != 0 count, as
+ * for the reference's sparse result) -> grad_w_hops [hops, B, L, n] and, when not NULL,
+ * grad_edge [T] (edge-score gradient, fastlog_kernel.py:1032-1098).  Outputs are
+ * overwritten.  Needs the workspace of the matching forward. */
+int mkg_proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_hops,
+                       const mkg_proof_params* p, const mkg_edge_factor* ef, const float* grad_out,
+                       float* grad_w_hops, float* grad_edge, void* workspace, size_t workspace_bytes,
+                       unsigned* dev_err, mkg_stream stream);
+
+/* Max-aggregation hop loop and decode (src/model_mmDRUM_kernel_sp.py:388-445 with the
+ * "max" transition: op agg_mode 1 -> sparse3d_max(ind, ori, inv) -> norm_sp_3d between
+ * hops, norm_sp_3d_max after the last), then bound_sparse_scores (proof.py:642-649) and
+ * the decode order of ordered_tail_scores (decode_core.py:350-363): per query the
+ * `topk` best (score desc, tail asc).  out_scores [B, E] receives the raw max scores;
+ * tails [B, topk] (-1 padded), scores [B, topk], counts [B]. */
+size_t mkg_decode_workspace_bytes(const mkg_proof_params* p, int64_t topk);
+int mkg_proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int64_t* heads,
+                         const float* w_hops, const mkg_proof_params* p, int64_t topk,
+                         float* out_scores, int64_t* tails, float* scores, int64_t* counts,
+                         void* workspace, size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+
+/* Decode ordering alone on a dense [B, E] raw score matrix (entries != 0 are candidates):
+ * bound 1 - exp(-max(x, 0)), order (score desc, tail asc), keep topk per row.  Replaces
+ * bound_sparse_scores + sparse_candidate_rows + ordered_tail_scores (proof.py:642-649,
+ * 729-758, decode_core.py:350-363). */
+int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails,
+                    float* scores, int64_t* counts, mkg_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINIKG_B200_H */

@@ -1,0 +1,939 @@
+// The fused hop loop on a dense entity-major state (B200, sm_100a).
+//
+// State X_h is [E][BLP] fp32 (row = entity, column = b*L + l, BLP = B*L rounded up to 4),
+// so one entity's frontier across every (query, rule) is a contiguous 128-bit-loadable row.
+// A hop is a pull over the merged neighbour list (every message that can reach a row):
+//
+//   Y[d][c] = X[d][c] * w[n-1][c] + sum_{(s, ch, m) in pull(d)} (X[s][c] * w[ch][c]) * m
+//
+// which fuses the op's three outputs and sum_sparse3d_concat; the column sums of Y give the
+// normalize_sparse3d denominators.  Rows are cut into tasks of at most kSeg edges (a row
+// longer than that becomes several tasks that add into the row with fp32 atomics), so hub
+// rows never serialise one warp.  Warps take tasks from a queue; each block works on one
+// 128-column chunk and keeps the chunk of the rule weights (and, backward, of their
+// gradient) in shared memory.  The backward is the same walk over the push list.
+#include <cub/cub.cuh>
+
+#include "mkg_common.cuh"
+
+namespace mkg {
+
+
+constexpr int kChunk = 128;      // columns per block (32 lanes x float4)
+constexpr int kFwdWarps = 8;
+constexpr int kBwdWarps = 16;
+constexpr int kTaskFirst = 1;    // task holds the row's first edges (adds the identity term)
+constexpr int kTaskPartial = 2;  // row split over several tasks: accumulate with atomics
+
+struct ProofDims {
+  int64_t B, L, E, R, n, hops, BL, BLP, nch;
+};
+
+inline ProofDims proof_dims(const mkg_proof_params& p) {
+  ProofDims d;
+  d.B = p.B; d.L = p.L; d.E = p.E; d.R = p.R; d.n = 2 * p.R + 1; d.hops = p.hops;
+  d.BL = p.B * p.L;
+  d.BLP = (d.BL + 3) / 4 * 4;
+  d.nch = (d.BLP + kChunk - 1) / kChunk;
+  return d;
+}
+
+namespace {
+
+size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct ProofLayout {
+  size_t wt, x, y, d, act, dxa, dxb, dy, s, dwt, queue, msgs, total;
+};
+
+ProofLayout proof_layout(const ProofDims& q) {
+  ProofLayout L{};
+  size_t o = 0;
+  const size_t slab = 4 * (size_t)q.E * q.BLP;
+  L.wt = o; o += a256(4 * (size_t)q.hops * q.n * q.BLP);
+  L.x = o; o += a256(slab) * (q.hops + 1);
+  L.y = o; o += a256(slab) * q.hops;
+  L.d = o; o += a256(4 * (size_t)q.hops * q.BLP);
+  L.act = o; o += a256((size_t)(q.hops + 1) * q.E * q.nch);
+  L.dxa = o; o += a256(slab);
+  L.dxb = o; o += a256(slab);
+  L.dy = o; o += a256(slab);
+  L.s = o; o += a256(4 * (size_t)q.hops * q.BLP);
+  L.dwt = o; o += a256(4 * (size_t)q.n * q.BLP);
+  L.queue = o; o += a256(4 * (size_t)(2 * q.hops * q.nch));
+  L.msgs = o; o += a256(8 * (size_t)(q.hops + 1));
+  L.total = o;
+  return L;
+}
+
+struct Slab {
+  char* base;
+  ProofLayout lay;
+  ProofDims q;
+  float* wt(int64_t h) const { return reinterpret_cast<float*>(base + lay.wt) + h * q.n * q.BLP; }
+  float* x(int64_t h) const { return reinterpret_cast<float*>(base + lay.x + a256(4 * (size_t)q.E * q.BLP) * h); }
+  float* y(int64_t h) const { return reinterpret_cast<float*>(base + lay.y + a256(4 * (size_t)q.E * q.BLP) * h); }
+  float* d(int64_t h) const { return reinterpret_cast<float*>(base + lay.d) + h * q.BLP; }
+  uint8_t* act(int64_t h) const { return reinterpret_cast<uint8_t*>(base + lay.act) + h * q.E * q.nch; }
+  float* dxa() const { return reinterpret_cast<float*>(base + lay.dxa); }
+  float* dxb() const { return reinterpret_cast<float*>(base + lay.dxb); }
+  float* dy() const { return reinterpret_cast<float*>(base + lay.dy); }
+  float* s(int64_t h) const { return reinterpret_cast<float*>(base + lay.s) + h * q.BLP; }
+  float* dwt() const { return reinterpret_cast<float*>(base + lay.dwt); }
+  int32_t* queue() const { return reinterpret_cast<int32_t*>(base + lay.queue); }
+  int64_t* msgs() const { return reinterpret_cast<int64_t*>(base + lay.msgs); }
+};
+
+// ------------------------------------------------------------------ setup kernels
+// Wt[h][ch][c] = w_hops[h][b][l][ch] for c = b*L + l (zero in the padding columns).
+__global__ void transpose_w_kernel(const float* __restrict__ w, ProofDims q, float* __restrict__ wt) {
+  const int64_t total = q.hops * q.n * q.BLP;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t c = i % q.BLP, rest = i / q.BLP, ch = rest % q.n, h = rest / q.n;
+    wt[i] = c < q.BL ? w[(h * q.BL + c) * q.n + ch] : 0.0f;
+  }
+}
+
+// grad_w_hops[h][b][l][ch] = dWt[ch][b*L + l]
+__global__ void untranspose_dw_kernel(const float* __restrict__ dwt, ProofDims q, int64_t h,
+                                      float* __restrict__ gw) {
+  const int64_t total = q.BL * q.n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t ch = i % q.n, c = i / q.n;
+    gw[h * total + i] = dwt[ch * q.BLP + c];
+  }
+}
+
+// One-hot start: X0[head_b][b*L + l] = 1 for every rule l (proof.py:511-523).
+__global__ void init_state_kernel(const int64_t* __restrict__ heads, ProofDims q, float* __restrict__ x0,
+                                  uint8_t* __restrict__ act0, const int32_t* __restrict__ push_ptr,
+                                  int64_t* __restrict__ msgs, unsigned* err) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < q.BL;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b = c / q.L;
+    int64_t e = heads[b];
+    if (e < 0 || e >= q.E) { raise_flag(err, MKG_DEV_BAD_ENTRY); continue; }
+    x0[e * q.BLP + c] = 1.0f;
+    act0[e * q.nch + c / kChunk] = 1;
+    atomicAdd(reinterpret_cast<unsigned long long*>(msgs), (unsigned long long)(push_ptr[e + 1] - push_ptr[e]));
+  }
+}
+
+// Zeroes the rows that several tasks add into (their first task carries both flags).
+__global__ void zero_partial_rows_kernel(const int4* __restrict__ tasks, int64_t ntasks, ProofDims q,
+                                         float* __restrict__ slab) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t t = warp0; t < ntasks; t += nwarps) {
+    int4 tk = tasks[t];
+    if ((tk.w & (kTaskFirst | kTaskPartial)) != (kTaskFirst | kTaskPartial)) continue;
+    float4* row = reinterpret_cast<float4*>(slab + (int64_t)tk.x * q.BLP);
+    for (int64_t j = lane; j < q.BLP / 4; j += 32) row[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+__device__ __forceinline__ void f4_fma(float4& acc, const float4& a, const float4& b, float m) {
+  acc.x = fmaf(a.x * b.x, m, acc.x);
+  acc.y = fmaf(a.y * b.y, m, acc.y);
+  acc.z = fmaf(a.z * b.z, m, acc.z);
+  acc.w = fmaf(a.w * b.w, m, acc.w);
+}
+__device__ __forceinline__ float4 f4_mul(const float4& a, const float4& b) {
+  return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
+}
+__device__ __forceinline__ void f4_max_msg(float4& acc, const float4& x, const float4& w, float m) {
+  // message value (x * w) * m exactly as the reference forms it, then max
+  acc.x = fmaxf(acc.x, (x.x * w.x) * m);
+  acc.y = fmaxf(acc.y, (x.y * w.y) * m);
+  acc.z = fmaxf(acc.z, (x.z * w.z) * m);
+  acc.w = fmaxf(acc.w, (x.w * w.w) * m);
+}
+__device__ __forceinline__ bool f4_any(const float4& v) {
+  return v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f;
+}
+__device__ __forceinline__ int f4_count(const float4& v) {
+  return (v.x != 0.f) + (v.y != 0.f) + (v.z != 0.f) + (v.w != 0.f);
+}
+
+// Loads this block's 128-column chunk of the rule weights into shared memory:
+// ws[ch * 128 + c] = Wt[ch][col0 + c].
+__device__ __forceinline__ void stage_weights(const float* __restrict__ wt, const ProofDims& q, int64_t col0,
+                                              float* ws) {
+  for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) {
+    int64_t ch = i / kChunk, c = i % kChunk;
+    ws[i] = (col0 + c < q.BLP) ? wt[ch * q.BLP + col0 + c] : 0.0f;
+  }
+}
+
+__device__ __forceinline__ int next_task(int32_t* queue, int lane) {
+  int t = 0;
+  if (lane == 0) t = atomicAdd(queue, 1);
+  return __shfl_sync(0xffffffffu, t, 0);
+}
+
+// ------------------------------------------------------------------ forward pull
+// MAX = false: sum aggregation (+ column sums into dsum); MAX = true: max of the message
+// values (sparse3d_max over ind / ori / inv of max-coalesced messages).
+template <bool MAX>
+__global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
+    const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
+    const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
+    float* __restrict__ y, float* __restrict__ dsum, int32_t* __restrict__ queue, unsigned* err) {
+  extern __shared__ float smem[];
+  float* ws = smem;                       // [n][128]
+  float* cs = smem + q.n * kChunk;        // [4][32] column partial sums (conflict-free layout)
+  const int lane = threadIdx.x & 31;
+  const int64_t chunk = blockIdx.y;
+  const int64_t col0 = chunk * kChunk;
+  const int64_t col = col0 + 4 * lane;
+  const bool colok = col < q.BLP;
+  stage_weights(wt, q, col0, ws);
+  if (!MAX)
+    for (int i = threadIdx.x; i < kChunk; i += blockDim.x) cs[i] = 0.0f;
+  __syncthreads();
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 csum = zero;
+  const float4* wsv = reinterpret_cast<const float4*>(ws);
+  for (;;) {
+    const int t = next_task(queue + chunk, lane);
+    if (t >= ntasks) break;
+    const int4 tk = tasks[t];
+    const int64_t row = tk.x;
+    float4 acc = zero;
+    if ((tk.w & kTaskFirst) && act[row * q.nch + chunk] && colok) {
+      float4 xr = *reinterpret_cast<const float4*>(x + row * q.BLP + col);
+      float4 wi = wsv[(q.n - 1) * 32 + lane];
+      acc = f4_mul(xr, wi);
+    }
+    for (int base = tk.y; base < tk.z; base += 32) {
+      const int cnt = min(32, tk.z - base);
+      int4 rec = make_int4(0, 0, 0, 0);
+      if (lane < cnt) rec = reinterpret_cast<const int4*>(edges)[base + lane];
+      for (int j = 0; j < cnt; j += 4) {
+        int nb[4], ch[4];
+        float m[4];
+        bool ok[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int jj = (j + u) & 31;
+          nb[u] = __shfl_sync(0xffffffffu, rec.x, jj);
+          ch[u] = __shfl_sync(0xffffffffu, rec.y, jj);
+          m[u] = __int_as_float(__shfl_sync(0xffffffffu, rec.w, jj));
+          ok[u] = (j + u) < cnt;
+          if (ok[u] && (nb[u] < 0 || nb[u] >= q.E || ch[u] < 0 || ch[u] >= q.n - 1)) {
+            if (lane == 0) raise_flag(err, MKG_DEV_BAD_COL);
+            ok[u] = false;
+          }
+          ok[u] = ok[u] && act[(int64_t)nb[u] * q.nch + chunk];
+        }
+        float4 xv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          xv[u] = (ok[u] && colok) ? *reinterpret_cast<const float4*>(x + (int64_t)nb[u] * q.BLP + col) : zero;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (!ok[u]) continue;
+          const float4 wv = wsv[ch[u] * 32 + lane];
+          if (MAX) f4_max_msg(acc, xv[u], wv, m[u]);
+          else f4_fma(acc, xv[u], wv, m[u]);
+        }
+      }
+    }
+    if (colok) {
+      float* yr = y + row * q.BLP + col;
+      if (tk.w & kTaskPartial) {
+        if (MAX) {
+          atomicMax(reinterpret_cast<int*>(yr) + 0, __float_as_int(acc.x));
+          atomicMax(reinterpret_cast<int*>(yr) + 1, __float_as_int(acc.y));
+          atomicMax(reinterpret_cast<int*>(yr) + 2, __float_as_int(acc.z));
+          atomicMax(reinterpret_cast<int*>(yr) + 3, __float_as_int(acc.w));
+        } else {
+          atomicAdd(yr + 0, acc.x); atomicAdd(yr + 1, acc.y);
+          atomicAdd(yr + 2, acc.z); atomicAdd(yr + 3, acc.w);
+        }
+      } else {
+        *reinterpret_cast<float4*>(yr) = acc;
+      }
+      if (!MAX) { csum.x += acc.x; csum.y += acc.y; csum.z += acc.z; csum.w += acc.w; }
+    }
+  }
+  if (!MAX) {
+    atomicAdd(cs + 0 * 32 + lane, csum.x);
+    atomicAdd(cs + 1 * 32 + lane, csum.y);
+    atomicAdd(cs + 2 * 32 + lane, csum.z);
+    atomicAdd(cs + 3 * 32 + lane, csum.w);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {
+      const int l = i % 32, k = i / 32;          // cs[k*32 + l] holds column 4*l + k
+      const int64_t c = col0 + 4 * l + k;
+      if (c < q.BLP && cs[i] != 0.0f) atomicAdd(dsum + c, cs[i]);
+    }
+  }
+}
+
+// normalize_sparse3d(.., 0, "mass") (drum.py:31-51) on the dense state:
+// x = (y / d) * min(d, 1) where y != 0; optional threshold; activity flags and the
+// message count of the next hop (present entries x push degree).
+__global__ void normalize_mass_kernel(const float* __restrict__ y, const float* __restrict__ dsum, ProofDims q,
+                                      float threshold, float* __restrict__ x, uint8_t* __restrict__ act,
+                                      const int32_t* __restrict__ push_ptr, int64_t* __restrict__ msgs) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  long long local_msgs = 0;
+  for (int64_t task = warp0; task < q.E * q.nch; task += nwarps) {
+    const int64_t row = task / q.nch, chunk = task % q.nch;
+    const int64_t col = chunk * kChunk + 4 * lane;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col < q.BLP) {
+      const float4 v = *reinterpret_cast<const float4*>(y + row * q.BLP + col);
+      const float4 d = *reinterpret_cast<const float4*>(dsum + col);
+      float vi[4] = {v.x, v.y, v.z, v.w}, di[4] = {d.x, d.y, d.z, d.w}, oi[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float r = 0.0f;
+        if (vi[k] != 0.0f) {
+          r = __fdiv_rn(vi[k], di[k]) * fminf(di[k], 1.0f);
+          if (threshold > 0.0f && r < threshold) r = 0.0f;
+        }
+        oi[k] = r;
+      }
+      o = make_float4(oi[0], oi[1], oi[2], oi[3]);
+      *reinterpret_cast<float4*>(x + row * q.BLP + col) = o;
+    }
+    const int nz = f4_count(o);
+    const unsigned any = __ballot_sync(0xffffffffu, nz > 0);
+    int tot = nz;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
+    if (lane == 0) {
+      act[row * q.nch + chunk] = any ? 1 : 0;
+      if (tot) local_msgs += (long long)tot * (push_ptr[row + 1] - push_ptr[row]);
+    }
+  }
+  if (lane == 0 && local_msgs) atomicAdd(reinterpret_cast<unsigned long long*>(msgs), (unsigned long long)local_msgs);
+}
+
+// norm_sp_3d (src/model_mmDRUM_kernel_sp.py:39-52) column sums, bit-exact: one thread per
+// column adds the column top to bottom in fp32 (the reference's index_put_ order), then
+// clamps at 1e-7.
+__global__ void sequential_colsum_kernel(const float* __restrict__ y, ProofDims q, float* __restrict__ d) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < q.BLP;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    int64_t e = 0;
+    for (; e + 8 <= q.E; e += 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = y[(e + k) * q.BLP + c];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+    }
+    for (; e < q.E; ++e) s = __fadd_rn(s, y[e * q.BLP + c]);
+    d[c] = fmaxf(s, 1e-7f);
+  }
+}
+
+__global__ void normalize_plain_kernel(const float* __restrict__ y, const float* __restrict__ d, ProofDims q,
+                                       float* __restrict__ x, uint8_t* __restrict__ act,
+                                       const int32_t* __restrict__ push_ptr, int64_t* __restrict__ msgs) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  long long local_msgs = 0;
+  for (int64_t task = warp0; task < q.E * q.nch; task += nwarps) {
+    const int64_t row = task / q.nch, chunk = task % q.nch;
+    const int64_t col = chunk * kChunk + 4 * lane;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col < q.BLP) {
+      const float4 v = *reinterpret_cast<const float4*>(y + row * q.BLP + col);
+      const float4 dd = *reinterpret_cast<const float4*>(d + col);
+      o.x = v.x != 0.f ? __fdiv_rn(v.x, dd.x) : 0.f;
+      o.y = v.y != 0.f ? __fdiv_rn(v.y, dd.y) : 0.f;
+      o.z = v.z != 0.f ? __fdiv_rn(v.z, dd.z) : 0.f;
+      o.w = v.w != 0.f ? __fdiv_rn(v.w, dd.w) : 0.f;
+      *reinterpret_cast<float4*>(x + row * q.BLP + col) = o;
+    }
+    const int nz = f4_count(o);
+    const unsigned any = __ballot_sync(0xffffffffu, nz > 0);
+    int tot = nz;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
+    if (lane == 0) {
+      act[row * q.nch + chunk] = any ? 1 : 0;
+      if (tot) local_msgs += (long long)tot * (push_ptr[row + 1] - push_ptr[row]);
+    }
+  }
+  if (lane == 0 && local_msgs) atomicAdd(reinterpret_cast<unsigned long long*>(msgs), (unsigned long long)local_msgs);
+}
+
+// out[b][e] = reduce_l X[e][b*L + l] (sum: sum_sp_3d; max: max over rules of the
+// normalised state, norm_sp_3d_max).  A 32-entity x 32-query tile goes through shared
+// memory so that both the reads and the [B][E] writes are coalesced.  For the max the
+// value is divided by d first (norm_sp_3d), the division is fused here.
+template <bool MAX>
+__global__ void rows_to_queries_kernel(const float* __restrict__ x, const float* __restrict__ d, ProofDims q,
+                                       float* __restrict__ out) {
+  __shared__ float tile[32][33];
+  const int64_t e0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t e = e0 + r, b = b0 + tx;
+    float v = 0.0f;
+    if (e < q.E && b < q.B) {
+      const float* src = x + e * q.BLP + b * q.L;
+      if (MAX) {
+        v = 0.0f;
+        for (int64_t l = 0; l < q.L; ++l) {
+          float t = src[l];
+          if (t != 0.0f) t = __fdiv_rn(t, d[b * q.L + l]);
+          v = fmaxf(v, t);
+        }
+      } else {
+        for (int64_t l = 0; l < q.L; ++l) v = __fadd_rn(v, src[l]);
+      }
+    }
+    tile[r][tx] = v;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t b = b0 + r, e = e0 + tx;
+    if (b < q.B && e < q.E) out[b * q.E + e] = tile[tx][r];
+  }
+}
+
+// ------------------------------------------------------------------ backward
+// Seed: dX_K[e][c] = G[b][e] where X_K[e][c] != 0 (the reference's sparse result carries
+// gradient only on its keys), and S[c] = sum_e dX_K[e][c] * Y_{K-1}[e][c].
+__global__ void seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
+                                 const float* __restrict__ ylast, ProofDims q, float* __restrict__ dx,
+                                 float* __restrict__ s) {
+  __shared__ float tile[32][33];
+  const int64_t e0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t b = b0 + r, e = e0 + tx;
+    tile[r][tx] = (b < q.B && e < q.E) ? g[b * q.E + e] : 0.0f;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t e = e0 + r, b = b0 + tx;
+    if (e >= q.E || b >= q.B) continue;
+    const float gv = tile[tx][r];
+    for (int64_t l = 0; l < q.L; ++l) {
+      const int64_t c = b * q.L + l;
+      const float xv = xk[e * q.BLP + c];
+      const float dv = xv != 0.0f ? gv : 0.0f;
+      dx[e * q.BLP + c] = dv;
+      if (dv != 0.0f) atomicAdd(s + c, dv * ylast[e * q.BLP + c]);
+    }
+  }
+}
+
+// Zero the padding columns of a slab that seed_grad_kernel does not write.
+__global__ void zero_pad_columns_kernel(float* __restrict__ slab, ProofDims q) {
+  const int64_t pad = q.BLP - q.BL;
+  if (pad <= 0) return;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < q.E * pad;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t e = i / pad, k = i % pad;
+    slab[e * q.BLP + q.BL + k] = 0.0f;
+  }
+}
+
+// Gradient of x = (y / d) * min(d, 1) with d = column sum of y (only y != 0 entries):
+// dy = dx * (c / d) + S * coef, coef = -1 / d^2 when d > 1 and 0 when d <= 1 (where
+// min(d, 1) = d and the two terms cancel).
+__global__ void normalize_mass_backward_kernel(const float* __restrict__ dx, const float* __restrict__ y,
+                                               const float* __restrict__ dsum, const float* __restrict__ s,
+                                               ProofDims q, float* __restrict__ dy) {
+  const int64_t n4 = q.E * q.BLP / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t col = (i * 4) % q.BLP;
+    const float4 g = reinterpret_cast<const float4*>(dx)[i];
+    const float4 v = reinterpret_cast<const float4*>(y)[i];
+    const float4 d = *reinterpret_cast<const float4*>(dsum + col);
+    const float4 sv = *reinterpret_cast<const float4*>(s + col);
+    float gi[4] = {g.x, g.y, g.z, g.w}, vi[4] = {v.x, v.y, v.z, v.w};
+    float di[4] = {d.x, d.y, d.z, d.w}, si[4] = {sv.x, sv.y, sv.z, sv.w}, o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float r = 0.0f;
+      if (vi[k] != 0.0f) {
+        const float dd = di[k];
+        const float c = fminf(dd, 1.0f);
+        const float coef = dd <= 1.0f ? 0.0f : -__fdiv_rn(1.0f, dd * dd);
+        r = gi[k] * __fdiv_rn(c, dd) + si[k] * coef;
+      }
+      o[k] = r;
+    }
+    reinterpret_cast<float4*>(dy)[i] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__device__ __forceinline__ float edge_grad_scale(const EdgeFactor& f, int64_t fact) {
+  if (f.weight == nullptr) return 0.0f;
+  const float ew = f.weight[fact];
+  if (f.is_score) return 1.0f / fmaxf(ew, 1e-12f);
+  const float z = -ew * f.scale;
+  const float sg = static_cast<float>(1.0 / (1.0 + exp(static_cast<double>(z))));
+  return f.scale * (1.0f - sg);
+}
+
+// Transposed hop over the push list (row = sending entity s, records = its messages):
+//   dX[s][c]   = [X[s][c] != 0] (dY[s][c] w[n-1][c] + sum (dY[d][c] m) w[ch][c])
+//   dW[ch][c] += (dY[d][c] m) X[s][c]           (shared-memory partial per block)
+//   dEdge[f]  += (sum_c dY[d][c] X[s][c] w[ch][c]) m g(f)
+//   S_prev[c] += dX[s][c] Y_prev[s][c]           (for the next lower hop)
+__global__ void __launch_bounds__(kBwdWarps * 32) bwd_pull_kernel(
+    const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
+    const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
+    const float* __restrict__ dy, const float* __restrict__ yprev, float* __restrict__ dx,
+    float* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge, int64_t num_facts, EdgeFactor ef,
+    int32_t* __restrict__ queue, unsigned* err) {
+  extern __shared__ float smem[];
+  float* ws = smem;                         // [n][128] rule weights
+  float* dws = smem + q.n * kChunk;         // [n][128] their gradient (conflict-free: [ch][k][lane])
+  float* cs = dws + q.n * kChunk;           // [4][32] S_prev partials
+  const int lane = threadIdx.x & 31;
+  const int64_t chunk = blockIdx.y;
+  const int64_t col0 = chunk * kChunk;
+  const int64_t col = col0 + 4 * lane;
+  const bool colok = col < q.BLP;
+  stage_weights(wt, q, col0, ws);
+  for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) dws[i] = 0.0f;
+  for (int i = threadIdx.x; i < kChunk; i += blockDim.x) cs[i] = 0.0f;
+  __syncthreads();
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4* wsv = reinterpret_cast<const float4*>(ws);
+  float4 spart = zero;
+  for (;;) {
+    const int t = next_task(queue + chunk, lane);
+    if (t >= ntasks) break;
+    const int4 tk = tasks[t];
+    const int64_t row = tk.x;
+    const bool active = act[row * q.nch + chunk] != 0;
+    float4 gx = zero;
+    if (active) {
+      const float4 xr = colok ? *reinterpret_cast<const float4*>(x + row * q.BLP + col) : zero;
+      if ((tk.w & kTaskFirst) && colok) {
+        const float4 ds = *reinterpret_cast<const float4*>(dy + row * q.BLP + col);
+        const float4 wi = wsv[(q.n - 1) * 32 + lane];
+        gx = f4_mul(ds, wi);
+        float* dwi = dws + (q.n - 1) * kChunk;
+        atomicAdd(dwi + 0 * 32 + lane, ds.x * xr.x);
+        atomicAdd(dwi + 1 * 32 + lane, ds.y * xr.y);
+        atomicAdd(dwi + 2 * 32 + lane, ds.z * xr.z);
+        atomicAdd(dwi + 3 * 32 + lane, ds.w * xr.w);
+      }
+      for (int base = tk.y; base < tk.z; base += 32) {
+        const int cnt = min(32, tk.z - base);
+        int4 rec = make_int4(0, 0, 0, 0);
+        if (lane < cnt) rec = reinterpret_cast<const int4*>(edges)[base + lane];
+        for (int j = 0; j < cnt; j += 4) {
+          int nb[4], ch[4], fa[4];
+          float m[4];
+          bool ok[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int jj = (j + u) & 31;
+            nb[u] = __shfl_sync(0xffffffffu, rec.x, jj);
+            ch[u] = __shfl_sync(0xffffffffu, rec.y, jj);
+            fa[u] = __shfl_sync(0xffffffffu, rec.z, jj);
+            m[u] = __int_as_float(__shfl_sync(0xffffffffu, rec.w, jj));
+            ok[u] = (j + u) < cnt;
+            if (ok[u] && (nb[u] < 0 || nb[u] >= q.E || ch[u] < 0 || ch[u] >= q.n - 1)) {
+              if (lane == 0) raise_flag(err, MKG_DEV_BAD_COL);
+              ok[u] = false;
+            }
+          }
+          float4 gv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            gv[u] = (ok[u] && colok) ? *reinterpret_cast<const float4*>(dy + (int64_t)nb[u] * q.BLP + col) : zero;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (!ok[u]) continue;
+            const float4 wv = wsv[ch[u] * 32 + lane];
+            const float4 gm = make_float4(gv[u].x * m[u], gv[u].y * m[u], gv[u].z * m[u], gv[u].w * m[u]);
+            gx.x = fmaf(gm.x, wv.x, gx.x); gx.y = fmaf(gm.y, wv.y, gx.y);
+            gx.z = fmaf(gm.z, wv.z, gx.z); gx.w = fmaf(gm.w, wv.w, gx.w);
+            float* dwc = dws + ch[u] * kChunk;
+            if (gm.x != 0.f) atomicAdd(dwc + 0 * 32 + lane, gm.x * xr.x);
+            if (gm.y != 0.f) atomicAdd(dwc + 1 * 32 + lane, gm.y * xr.y);
+            if (gm.z != 0.f) atomicAdd(dwc + 2 * 32 + lane, gm.z * xr.z);
+            if (gm.w != 0.f) atomicAdd(dwc + 3 * 32 + lane, gm.w * xr.w);
+            if (grad_edge != nullptr) {
+              float dot = gv[u].x * xr.x * wv.x + gv[u].y * xr.y * wv.y + gv[u].z * xr.z * wv.z +
+                          gv[u].w * xr.w * wv.w;
+              dot = warp_sum(dot);
+              if (lane == 0 && dot != 0.0f) {
+                if (fa[u] >= 0 && fa[u] < num_facts) atomicAdd(grad_edge + fa[u], dot * m[u] * edge_grad_scale(ef, fa[u]));
+                else raise_flag(err, MKG_DEV_BAD_FACT);
+              }
+            }
+          }
+        }
+      }
+      // only present entries of X carry a gradient
+      gx.x = xr.x != 0.f ? gx.x : 0.f; gx.y = xr.y != 0.f ? gx.y : 0.f;
+      gx.z = xr.z != 0.f ? gx.z : 0.f; gx.w = xr.w != 0.f ? gx.w : 0.f;
+    }
+    if (colok) {
+      float* dr = dx + row * q.BLP + col;
+      if (tk.w & kTaskPartial) {
+        if (active) { atomicAdd(dr + 0, gx.x); atomicAdd(dr + 1, gx.y); atomicAdd(dr + 2, gx.z); atomicAdd(dr + 3, gx.w); }
+      } else {
+        *reinterpret_cast<float4*>(dr) = gx;
+      }
+      if (sprev != nullptr && active) {
+        const float4 yp = *reinterpret_cast<const float4*>(yprev + row * q.BLP + col);
+        spart.x = fmaf(gx.x, yp.x, spart.x); spart.y = fmaf(gx.y, yp.y, spart.y);
+        spart.z = fmaf(gx.z, yp.z, spart.z); spart.w = fmaf(gx.w, yp.w, spart.w);
+      }
+    }
+  }
+  atomicAdd(cs + 0 * 32 + lane, spart.x);
+  atomicAdd(cs + 1 * 32 + lane, spart.y);
+  atomicAdd(cs + 2 * 32 + lane, spart.z);
+  atomicAdd(cs + 3 * 32 + lane, spart.w);
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) {
+    const int64_t ch = i / kChunk, r = i % kChunk, l = r % 32, k = r / 32;
+    const int64_t c = col0 + 4 * l + k;
+    if (c < q.BLP && dws[i] != 0.0f) atomicAdd(dwt + ch * q.BLP + c, dws[i]);
+  }
+  if (sprev != nullptr) {
+    for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {
+      const int l = i % 32, k = i / 32;
+      const int64_t c = col0 + 4 * l + k;
+      if (c < q.BLP && cs[i] != 0.0f) atomicAdd(sprev + c, cs[i]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ decode top-k
+// One block per query row: candidate keys (bounded score << 32 | ~tail), MSB radix select
+// of the k-th largest, then a bitonic sort of the selected keys in shared memory.
+constexpr int kTopkThreads = 1024;
+constexpr int kTopkMax = 1024;
+
+__device__ __forceinline__ unsigned long long candidate_key(float raw, int64_t e) {
+  if (!(raw != 0.0f)) return 0ull;
+  const float xv = fmaxf(raw, 0.0f);
+  const float ex = static_cast<float>(exp(-static_cast<double>(xv)));
+  const float score = 1.0f - ex;  // bound_sparse_scores, float32 arithmetic
+  return (static_cast<unsigned long long>(__float_as_uint(score)) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(e));
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __restrict__ raw, int64_t B,
+                                                                 int64_t E, int64_t k, int64_t* __restrict__ tails,
+                                                                 float* __restrict__ scores,
+                                                                 int64_t* __restrict__ counts) {
+  typedef cub::BlockReduce<long long, kTopkThreads> CandReduce;
+  __shared__ typename CandReduce::TempStorage reduce_tmp;
+  __shared__ unsigned int hist[256];
+  __shared__ unsigned long long sel[kTopkMax];
+  __shared__ unsigned long long prefix_s;
+  __shared__ long long need_s;
+  __shared__ int nsel;
+  __shared__ long long ncand_s;
+  const int64_t b = blockIdx.x;
+  const float* row = raw + b * E;
+  if (threadIdx.x == 0) { ncand_s = 0; nsel = 0; prefix_s = 0ull; }
+  __syncthreads();
+  long long my = 0;
+  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) my += row[e] != 0.0f;
+  my = CandReduce(reduce_tmp).Sum(my);
+  if (threadIdx.x == 0) { ncand_s = my; need_s = my < k ? my : k; }
+  __syncthreads();
+  const long long ncand = ncand_s;
+  const long long kk = need_s;
+  unsigned long long thresh = 1ull;  // every candidate key is > 0
+  if (ncand > k) {
+    // MSB radix select: the kk-th largest key among the candidates
+    unsigned long long prefix = 0ull, mask = 0ull;
+    long long need = kk;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+      __syncthreads();
+      for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
+        unsigned long long key = candidate_key(row[e], e);
+        if (key != 0ull && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        long long acc = 0;
+        int dsel = 0;
+        for (int dgt = 255; dgt >= 0; --dgt) {
+          if (acc + hist[dgt] >= need) { dsel = dgt; break; }
+          acc += hist[dgt];
+        }
+        need_s = need - acc;
+        prefix_s = prefix | (static_cast<unsigned long long>(dsel) << shift);
+      }
+      __syncthreads();
+      need = need_s;
+      prefix = prefix_s;
+      mask |= 0xffull << shift;
+      __syncthreads();
+    }
+    thresh = prefix;  // keys are unique (distinct tails): exactly kk keys are >= thresh
+  }
+  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
+    unsigned long long key = candidate_key(row[e], e);
+    if (key != 0ull && key >= thresh) {
+      int pos = atomicAdd(&nsel, 1);
+      if (pos < kTopkMax) sel[pos] = key;
+    }
+  }
+  __syncthreads();
+  const int m = min(nsel, kTopkMax);
+  int p2 = 1;
+  while (p2 < m) p2 <<= 1;
+  for (int i = threadIdx.x; i < p2; i += blockDim.x)
+    if (i >= m) sel[i] = 0ull;
+  __syncthreads();
+  // bitonic sort, descending
+  for (int size = 2; size <= p2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < p2; i += blockDim.x) {
+        int j = i ^ stride;
+        if (j > i) {
+          bool desc = (i & size) == 0;
+          unsigned long long a = sel[i], c = sel[j];
+          if (desc ? (a < c) : (a > c)) { sel[i] = c; sel[j] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) {
+    if (j < m) {
+      unsigned long long key = sel[j];
+      tails[b * k + j] = static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+      scores[b * k + j] = __uint_as_float(static_cast<uint32_t>(key >> 32));
+    } else {
+      tails[b * k + j] = -1;
+      scores[b * k + j] = 0.0f;
+    }
+  }
+  if (threadIdx.x == 0) counts[b] = m;
+}
+
+size_t fwd_smem(const ProofDims& q) { return 4 * ((size_t)q.n * kChunk + kChunk); }
+size_t bwd_smem(const ProofDims& q) { return 4 * (2 * (size_t)q.n * kChunk + kChunk); }
+
+int check_proof(const mkg_graph* g, const mkg_adjacency* adj, const mkg_proof_params* p) {
+  MKG_REQUIRE(g && adj && p, "proof: null argument");
+  MKG_REQUIRE(p->B >= 1 && p->L >= 1 && p->hops >= 1 && p->R >= 1, "proof: B, L, R, hops must be positive");
+  MKG_REQUIRE(p->E == g->num_entities, "proof: E does not match the graph");
+  MKG_REQUIRE(adj->pull_tasks && adj->push_tasks && adj->num_pull_tasks > 0 && adj->num_push_tasks > 0 &&
+                  adj->pull && adj->push && adj->pull_ptr && adj->push_ptr,
+              "proof: adjacency has no task lists (call mkg_adjacency_build and read the task counts)");
+  MKG_REQUIRE(p->topk_edges >= (int64_t(1) << 60),
+              "proof: the fused loop runs uncapped hops; capped hops go through mkg_hop_forward");
+  ProofDims q = proof_dims(*p);
+  MKG_REQUIRE(bwd_smem(q) <= 200 * 1024, "proof: too many relation channels (%lld) for the shared-memory "
+              "staging of the rule weights", (long long)q.n);
+  return MKG_OK;
+}
+
+}  // namespace
+
+size_t proof_workspace_bytes(const mkg_proof_params* p) {
+  return proof_layout(proof_dims(*p)).total + 256;
+}
+
+static int set_smem(const void* fn, size_t bytes) {
+  MKG_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return MKG_OK;
+}
+
+// Forward of the hop loop (sum) or of the max loop; keeps every hop in the workspace.
+static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64_t* heads, const float* w_hops,
+                       const mkg_proof_params* p, bool max_mode, void* ws, size_t ws_bytes, float* out,
+                       int64_t* messages_out, unsigned* err, cudaStream_t st) {
+  int rc = check_proof(g, adj, p);
+  if (rc) return rc;
+  MKG_REQUIRE(heads && w_hops && out, "proof: null input / output");
+  const ProofDims q = proof_dims(*p);
+  Slab S{static_cast<char*>(ws), proof_layout(q), q};
+  MKG_REQUIRE(ws && ws_bytes >= S.lay.total, "proof: workspace too small (%zu < %zu)", ws_bytes, S.lay.total);
+  const size_t slab = 4 * (size_t)q.E * q.BLP;
+  const int pb = persistent_blocks(4);
+  transpose_w_kernel<<<grid_for(q.hops * q.n * q.BLP, 256, pb), 256, 0, st>>>(w_hops, q, S.wt(0));
+  MKG_LAUNCHED("transpose_w_kernel");
+  MKG_CUDA(cudaMemsetAsync(S.x(0), 0, slab, st));
+  MKG_CUDA(cudaMemsetAsync(S.act(0), 0, (size_t)q.E * q.nch, st));
+  MKG_CUDA(cudaMemsetAsync(S.d(0), 0, 4 * (size_t)q.hops * q.BLP, st));
+  MKG_CUDA(cudaMemsetAsync(S.queue(), 0, 4 * (size_t)(q.hops * q.nch), st));
+  MKG_CUDA(cudaMemsetAsync(S.msgs(), 0, 8 * (size_t)(q.hops + 1), st));
+  init_state_kernel<<<grid_for(q.BL, 256, pb), 256, 0, st>>>(heads, q, S.x(0), S.act(0), adj->push_ptr, S.msgs(), err);
+  MKG_LAUNCHED("init_state_kernel");
+  const size_t sm = fwd_smem(q);
+  rc = max_mode ? set_smem((const void*)fwd_pull_kernel<true>, sm) : set_smem((const void*)fwd_pull_kernel<false>, sm);
+  if (rc) return rc;
+  int resident = 0;
+  if (max_mode)
+    MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fwd_pull_kernel<true>, kFwdWarps * 32, sm));
+  else
+    MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fwd_pull_kernel<false>, kFwdWarps * 32, sm));
+  // one wave of resident blocks, split evenly over the column chunks
+  const int blocks_per_chunk = grid_for(adj->num_pull_tasks, kFwdWarps,
+                                        (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / q.nch) + 1);
+  for (int64_t h = 0; h < q.hops; ++h) {
+    float* y = S.y(h);
+    zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, q, y);
+    MKG_LAUNCHED("zero_partial_rows_kernel");
+    dim3 grid(blocks_per_chunk, (unsigned)q.nch);
+    if (p->fwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->fwd_events[2 * h]), st));
+    if (max_mode)
+      fwd_pull_kernel<true><<<grid, kFwdWarps * 32, sm, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, adj->pull, q,
+                                                              S.wt(h), S.x(h), S.act(h), y, nullptr,
+                                                              S.queue() + h * q.nch, err);
+    else
+      fwd_pull_kernel<false><<<grid, kFwdWarps * 32, sm, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, adj->pull, q,
+                                                               S.wt(h), S.x(h), S.act(h), y, S.d(h),
+                                                               S.queue() + h * q.nch, err);
+    MKG_LAUNCHED("fwd_pull_kernel");
+    if (p->fwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->fwd_events[2 * h + 1]), st));
+    if (max_mode) {
+      sequential_colsum_kernel<<<grid_for(q.BLP, 128, pb), 128, 0, st>>>(y, q, S.d(h));
+      MKG_LAUNCHED("sequential_colsum_kernel");
+      if (h + 1 < q.hops) {
+        normalize_plain_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, S.x(h + 1), S.act(h + 1), adj->push_ptr,
+                                                   S.msgs() + h + 1);
+        MKG_LAUNCHED("normalize_plain_kernel");
+      }
+    } else {
+      normalize_mass_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, p->state_threshold, S.x(h + 1), S.act(h + 1),
+                                                adj->push_ptr, S.msgs() + h + 1);
+      MKG_LAUNCHED("normalize_mass_kernel");
+    }
+  }
+  dim3 tgrid((unsigned)((q.E + 31) / 32), (unsigned)((q.B + 31) / 32));
+  if (max_mode)
+    rows_to_queries_kernel<true><<<tgrid, dim3(32, 8), 0, st>>>(S.y(q.hops - 1), S.d(q.hops - 1), q, out);
+  else
+    rows_to_queries_kernel<false><<<tgrid, dim3(32, 8), 0, st>>>(S.x(q.hops), nullptr, q, out);
+  MKG_LAUNCHED("rows_to_queries_kernel");
+  if (messages_out) MKG_CUDA(cudaMemcpyAsync(messages_out, S.msgs(), 8 * (size_t)q.hops, cudaMemcpyDeviceToDevice, st));
+  return MKG_OK;
+}
+
+int proof_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64_t* heads, const float* w_hops,
+                  const mkg_proof_params* p, void* ws, size_t ws_bytes, float* out, int64_t* messages_out,
+                  unsigned* err, cudaStream_t st) {
+  return run_forward(g, adj, heads, w_hops, p, false, ws, ws_bytes, out, messages_out, err, st);
+}
+
+int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_hops, const mkg_proof_params* p,
+                   const mkg_edge_factor* ef, const float* grad_out, float* grad_w_hops, float* grad_edge, void* ws,
+                   size_t ws_bytes, unsigned* err, cudaStream_t st) {
+  int rc = check_proof(g, adj, p);
+  if (rc) return rc;
+  MKG_REQUIRE(grad_out && grad_w_hops && ef, "proof_backward: null argument");
+  (void)w_hops;  // the transposed weights of the forward are still in the workspace
+  const ProofDims q = proof_dims(*p);
+  Slab S{static_cast<char*>(ws), proof_layout(q), q};
+  MKG_REQUIRE(ws && ws_bytes >= S.lay.total, "proof_backward: workspace too small");
+  const size_t slab = 4 * (size_t)q.E * q.BLP;
+  const int pb = persistent_blocks(4);
+  EdgeFactor f = make_factor(*ef);
+  if (grad_edge) MKG_CUDA(cudaMemsetAsync(grad_edge, 0, 4 * (size_t)g->num_facts, st));
+  MKG_CUDA(cudaMemsetAsync(S.s(0), 0, 4 * (size_t)q.hops * q.BLP, st));
+  MKG_CUDA(cudaMemsetAsync(S.queue() + q.hops * q.nch, 0, 4 * (size_t)(q.hops * q.nch), st));
+  float* dx_cur = S.dxa();
+  float* dx_next = S.dxb();
+  zero_pad_columns_kernel<<<pb, 256, 0, st>>>(dx_cur, q);
+  MKG_LAUNCHED("zero_pad_columns_kernel");
+  dim3 tgrid((unsigned)((q.E + 31) / 32), (unsigned)((q.B + 31) / 32));
+  seed_grad_kernel<<<tgrid, dim3(32, 8), 0, st>>>(grad_out, S.x(q.hops), S.y(q.hops - 1), q, dx_cur, S.s(q.hops - 1));
+  MKG_LAUNCHED("seed_grad_kernel");
+  const size_t sm = bwd_smem(q);
+  rc = set_smem((const void*)bwd_pull_kernel, sm);
+  if (rc) return rc;
+  int resident = 0;
+  MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, bwd_pull_kernel, kBwdWarps * 32, sm));
+  const int blocks_per_chunk = grid_for(adj->num_push_tasks, kBwdWarps,
+                                        (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / q.nch) + 1);
+  for (int64_t h = q.hops - 1; h >= 0; --h) {
+    // dY_h from dX_{h+1}
+    normalize_mass_backward_kernel<<<grid_for(q.E * q.BLP / 4, 256, pb * 2), 256, 0, st>>>(
+        dx_cur, S.y(h), S.d(h), S.s(h), q, S.dy());
+    MKG_LAUNCHED("normalize_mass_backward_kernel");
+    MKG_CUDA(cudaMemsetAsync(S.dwt(), 0, 4 * (size_t)q.n * q.BLP, st));
+    zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, q, dx_next);
+    MKG_LAUNCHED("zero_partial_rows_kernel");
+    (void)slab;
+    dim3 grid(blocks_per_chunk, (unsigned)q.nch);
+    if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h]), st));
+    bwd_pull_kernel<<<grid, kBwdWarps * 32, sm, st>>>(
+        reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.dy(),
+        h > 0 ? S.y(h - 1) : nullptr, dx_next, S.dwt(), h > 0 ? S.s(h - 1) : nullptr, grad_edge, g->num_facts, f,
+        S.queue() + (q.hops + h) * q.nch, err);
+    MKG_LAUNCHED("bwd_pull_kernel");
+    if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h + 1]), st));
+    untranspose_dw_kernel<<<grid_for(q.BL * q.n, 256, pb), 256, 0, st>>>(S.dwt(), q, h, grad_w_hops);
+    MKG_LAUNCHED("untranspose_dw_kernel");
+    float* t = dx_cur; dx_cur = dx_next; dx_next = t;
+  }
+  return MKG_OK;
+}
+
+namespace {
+__global__ void row_activity_kernel(const uint8_t* __restrict__ act, ProofDims q, uint8_t* __restrict__ flags) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < q.E; e += (int64_t)gridDim.x * blockDim.x) {
+    uint8_t any = 0;
+    for (int64_t c = 0; c < q.nch; ++c) any |= act[e * q.nch + c];
+    flags[e] = any ? 1 : 0;
+  }
+}
+}  // namespace
+
+int proof_row_activity(const mkg_proof_params* p, const void* ws, size_t ws_bytes, int64_t h, uint8_t* flags,
+                       cudaStream_t st) {
+  MKG_REQUIRE(p && ws && flags, "proof_row_activity: null argument");
+  const ProofDims q = proof_dims(*p);
+  MKG_REQUIRE(h >= 0 && h <= q.hops, "proof_row_activity: hop out of range");
+  Slab S{static_cast<char*>(const_cast<void*>(ws)), proof_layout(q), q};
+  MKG_REQUIRE(ws_bytes >= S.lay.total, "proof_row_activity: workspace too small");
+  row_activity_kernel<<<grid_for(q.E, 256, persistent_blocks(4)), 256, 0, st>>>(S.act(h), q, flags);
+  MKG_LAUNCHED("row_activity_kernel");
+  return MKG_OK;
+}
+
+size_t decode_workspace_bytes(const mkg_proof_params* p, int64_t topk) {
+  (void)topk;
+  return proof_layout(proof_dims(*p)).total + 256;
+}
+
+int proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int64_t* heads, const float* w_hops,
+                     const mkg_proof_params* p, int64_t topk, float* out_scores, int64_t* tails, float* scores,
+                     int64_t* counts, void* ws, size_t ws_bytes, unsigned* err, cudaStream_t st) {
+  MKG_REQUIRE(topk >= 1 && topk <= kTopkMax, "decode: topk must lie in [1, %d]", kTopkMax);
+  MKG_REQUIRE(tails && scores && counts, "decode: null output");
+  int rc = run_forward(g, adj, heads, w_hops, p, true, ws, ws_bytes, out_scores, nullptr, err, st);
+  if (rc) return rc;
+  topk_rows_kernel<<<(unsigned)p->B, kTopkThreads, 0, st>>>(out_scores, p->B, p->E, topk, tails, scores, counts);
+  MKG_LAUNCHED("topk_rows_kernel");
+  return MKG_OK;
+}
+
+int decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails, float* scores,
+                int64_t* counts, cudaStream_t st) {
+  MKG_REQUIRE(raw && tails && scores && counts, "decode_topk: null argument");
+  MKG_REQUIRE(topk >= 1 && topk <= kTopkMax, "decode_topk: topk must lie in [1, %d]", kTopkMax);
+  MKG_REQUIRE(B >= 1 && E >= 1 && E < (int64_t(1) << 32) - 1, "decode_topk: bad sizes");
+  topk_rows_kernel<<<(unsigned)B, kTopkThreads, 0, st>>>(raw, B, E, topk, tails, scores, counts);
+  MKG_LAUNCHED("topk_rows_kernel");
+  return MKG_OK;
+}
+
+}  // namespace mkg

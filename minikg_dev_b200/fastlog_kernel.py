@@ -1,0 +1,176 @@
+"""The per-hop operator behind the reference's ``fastlog_bridge`` API, on the B200 library.
+
+``FastLogFunctionSparse3DTopK`` keeps the reference signature, argument meaning, tuple
+order and return values (src/fastlog_kernel/fastlog_kernel.py:900-1107): three coalesced
+sparse COO ``[B, L, E]`` tensors (ori, inv, ind), and gradients for ``sp_value``, ``w`` and
+the edge weights.  Forward and backward each run in the C library (``mkg_hop_forward`` /
+``mkg_hop_emit`` / ``mkg_hop_backward``); raw messages are never materialised and no torch
+sort-coalesce runs.
+
+Semantics kept from the reference's CUDA path:
+* edge factor ``bool(mask[f]) * score(f)``; messages with a zero factor still create their
+  output key (explicit zeros), as the fill kernel does (fastlog.cu:2300-2318);
+* the 256-bucket per-entry edge cap with in-order threshold groups;
+* ``agg_mode == 1``: max per key, argmax = smallest original fact id among equal maxima
+  (``tie_break=meta_edge``, fastlog_kernel.py:954-959); the backward sends each key's
+  gradient to that message only.
+Differences: a ``mask_values`` of one element (the reference's 0-d ones tensor for huge
+graphs) is broadcast to every fact; the max path compares values through an
+order-preserving integer key, so ``-0.0`` ranks below ``+0.0``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+from torch import autograd
+
+from . import _native as N
+from .graph import build_csr_structure, graph_from_csr  # noqa: F401  (re-exported)
+
+
+def _frontier(sp_batch, sp_level, sp_entity, sp_value, keep):
+    b = sp_batch.to(torch.int64).contiguous()
+    l = sp_level.to(torch.int64).contiguous()
+    e = sp_entity.to(torch.int64).contiguous()
+    v = sp_value.detach().to(torch.float32).contiguous()
+    keep += [b, l, e, v]
+    return N.Frontier(b.data_ptr(), l.data_ptr(), e.data_ptr(), v.data_ptr(), b.numel()), (b, l, e, v)
+
+
+def _coo(t: torch.Tensor | None, B, L, E, like_indices: torch.Tensor | None, keep):
+    """(indices [3, nnz] int64, values fp32) of a gradient; dense gradients are read at the
+    forward output's keys (the only keys any message reached)."""
+    if t is None:
+        z = torch.empty((3, 0), dtype=torch.int64, device=like_indices.device if like_indices is not None else "cuda")
+        v = torch.empty(0, dtype=torch.float32, device=z.device)
+    elif t.is_sparse:
+        t = t.coalesce()
+        z = t.indices().to(torch.int64).contiguous()
+        v = t.values().to(torch.float32).contiguous()
+    else:
+        z = like_indices.contiguous()
+        v = t[z[0], z[1], z[2]].to(torch.float32).contiguous()
+    keep += [z, v]
+    return N.Coo3(z.data_ptr(), v.data_ptr(), int(v.numel()))
+
+
+class FastLogFunctionSparse3DTopK(autograd.Function):
+    """One relation-typed hop (reference: fastlog_kernel.py:900-1107)."""
+
+    @staticmethod
+    def forward(ctx, sp_batch, sp_level, sp_entity, sp_value, w,
+                ori_row_ptr, ori_col_ind, ori_r_ind, ori_order,
+                inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
+                mask_values, weight, B, L, E, r_size, wot_i, topk_edges, agg_mode=0,
+                edge_weight_is_score=False, edge_weight_scale=1.0):
+        lib = N.load()
+        N.require_cuda(sp_value, "sp_value")
+        dev = sp_value.device
+        B, L, E, r_size = int(B), int(L), int(E), int(r_size)
+        csr = (ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+               ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+               inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count)
+        g = graph_from_csr(csr, E, r_size)
+        keep = []
+        fr, (b, l, e, v) = _frontier(sp_batch, sp_level, sp_entity, sp_value, keep)
+        wf = w.detach().to(torch.float32).contiguous()
+        if wf.dim() != 3 or wf.shape[0] != B or wf.shape[1] != L:
+            raise ValueError(f"w must be [B, L, n], got {tuple(wf.shape)}")
+        n = int(wf.shape[2])
+        edge_weight = weight if (weight is not None and weight.numel() > 0) else None
+        f = N.edge_factor(mask_values, edge_weight, bool(edge_weight_is_score), float(edge_weight_scale), keep)
+        p = N.HopParams(B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges))
+        nnz = int(b.numel())
+        ws = N.workspace(lib.mkg_hop_forward_workspace_bytes(ctypes.byref(p), nnz), dev)
+        counts = torch.zeros(3, dtype=torch.int64, device=dev)
+        err = N.error_word(dev)
+        st = N.stream_handle(dev)
+        N.check(lib.mkg_hop_forward(ctypes.byref(g.struct), ctypes.byref(fr), wf.data_ptr(), ctypes.byref(f),
+                                    ctypes.byref(p), ws.data_ptr(), ws.numel(), counts.data_ptr(), err.data_ptr(),
+                                    st), "hop_forward")
+        sizes = counts.tolist()  # the one host sync of the hop (the reference has one too)
+        N.raise_device_errors(dev)
+        outs, args = [], []
+        for which, U in enumerate(sizes):
+            idx = torch.empty((3, U), dtype=torch.int64, device=dev)
+            val = torch.empty(U, dtype=torch.float32, device=dev)
+            arg = torch.empty(U, dtype=torch.int64, device=dev) if (agg_mode == 1 and which < 2) else None
+            N.check(lib.mkg_hop_emit(ctypes.byref(p), nnz, ws.data_ptr(), ws.numel(), which, U, idx.data_ptr(),
+                                     val.data_ptr(), arg.data_ptr() if arg is not None else None, st), "hop_emit")
+            outs.append(torch.sparse_coo_tensor(idx, val, (B, L, E), is_coalesced=True))
+            args.append(arg)
+        del ws
+        has_edge_weight = weight is not None and bool(getattr(weight, "requires_grad", False))
+        if any(ctx.needs_input_grad):
+            saved = [b, l, e, v, wf]
+            saved += [outs[0]._indices(), outs[1]._indices()]
+            saved += [args[0] if args[0] is not None else torch.empty(0, dtype=torch.int64, device=dev),
+                      args[1] if args[1] is not None else torch.empty(0, dtype=torch.int64, device=dev)]
+            saved += [mask_values if mask_values is not None else torch.empty(0, device=dev)]
+            saved += [weight.detach() if edge_weight is not None else torch.empty(0, device=dev)]
+            ctx.save_for_backward(*saved)
+            ctx.g = g
+            ctx.params = (B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges))
+            ctx.has_mask = mask_values is not None
+            ctx.has_edge_weight = has_edge_weight
+            ctx.edge_weight_present = edge_weight is not None
+            ctx.edge_weight_is_score = bool(edge_weight_is_score)
+            ctx.edge_weight_scale = float(edge_weight_scale)
+            ctx.weight_shape = tuple(weight.shape) if weight is not None else None
+            ctx.weight_dtype = weight.dtype if weight is not None else None
+        return outs[0], outs[1], outs[2]
+
+    @staticmethod
+    def backward(ctx, grad_ori, grad_inv, grad_ind):
+        lib = N.load()
+        b, l, e, v, wf, oi_ori, oi_inv, arg_ori, arg_inv, mask_values, weight = ctx.saved_tensors
+        B, L, E, r_size, n, wot_i, agg_mode, topk = ctx.params
+        g = ctx.g
+        dev = v.device
+        keep = []
+        fr = N.Frontier(b.data_ptr(), l.data_ptr(), e.data_ptr(), v.data_ptr(), b.numel())
+        f = N.edge_factor(mask_values if ctx.has_mask else None, weight if ctx.edge_weight_present else None,
+                          ctx.edge_weight_is_score, ctx.edge_weight_scale, keep)
+        p = N.HopParams(B, L, E, r_size, n, wot_i, agg_mode, topk)
+        go = _coo(grad_ori, B, L, E, oi_ori, keep)
+        gi = _coo(grad_inv, B, L, E, oi_inv, keep)
+        gd = _coo(grad_ind, B, L, E, torch.stack([b, l, e]), keep)
+        grad_sp = torch.empty(b.numel(), dtype=torch.float32, device=dev)
+        grad_w = torch.empty((B, L, n), dtype=torch.float32, device=dev)
+        grad_edge = torch.empty(g.num_facts, dtype=torch.float32, device=dev) if ctx.has_edge_weight else None
+        out_o = N.Coo3(oi_ori.data_ptr(), None, int(oi_ori.shape[1]))
+        out_i = N.Coo3(oi_inv.data_ptr(), None, int(oi_inv.shape[1]))
+        fh = ft = frl = None
+        if agg_mode == 1:
+            fh, ft, frl = g.fact_table()
+        ws = N.workspace(lib.mkg_hop_backward_workspace_bytes(ctypes.byref(p), b.numel()), dev)
+        N.check(lib.mkg_hop_backward(ctypes.byref(g.struct), ctypes.byref(fr), wf.data_ptr(), ctypes.byref(f),
+                                     ctypes.byref(p), ctypes.byref(go), ctypes.byref(gi), ctypes.byref(gd),
+                                     ctypes.byref(out_o), N.ptr(arg_ori) if arg_ori.numel() else None,
+                                     ctypes.byref(out_i), N.ptr(arg_inv) if arg_inv.numel() else None,
+                                     N.ptr(fh), N.ptr(ft), N.ptr(frl), grad_sp.data_ptr(), grad_w.data_ptr(),
+                                     N.ptr(grad_edge), ws.data_ptr(), ws.numel(), N.error_word(dev).data_ptr(),
+                                     N.stream_handle(dev)), "hop_backward")
+        grad_edge_weight = None
+        if ctx.has_edge_weight:
+            if os.environ.get("FASTLOG_SPARSE_EDGE_GRAD", "0") == "1":
+                nz = torch.nonzero(grad_edge, as_tuple=True)[0]
+                if len(ctx.weight_shape) == 2 and ctx.weight_shape[1] == 1:
+                    idx = torch.stack([nz, torch.zeros_like(nz)])
+                else:
+                    idx = nz.view(1, -1)
+                grad_edge_weight = torch.sparse_coo_tensor(idx, grad_edge[nz].to(ctx.weight_dtype),
+                                                           ctx.weight_shape, device=dev).coalesce()
+            else:
+                grad_edge_weight = grad_edge.view(ctx.weight_shape).to(ctx.weight_dtype)
+        return (None, None, None, grad_sp.to(v.dtype), grad_w,
+                None, None, None, None,
+                None, None, None, None,
+                None, None, None, None,
+                None, None, None, None,
+                None, grad_edge_weight,
+                None, None, None, None, None, None, None, None, None)

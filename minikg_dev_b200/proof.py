@@ -1,0 +1,256 @@
+"""The multi-hop proof engine: ``kernel_sparse_scores`` on the fused CUDA hop loop.
+
+``HopLoopSum`` runs every hop of proof.py:467-614 (the op, ``sum_sparse3d_concat``,
+``normalize_sparse3d(.., 0, "mass")``, then ``sum_sp_3d``) in one library call
+(``mkg_proof_forward``) on a dense entity-major state, and its backward
+(``mkg_proof_backward``) returns gradients for the per-hop rule weights and the edge
+scores.  ``decode_max`` runs the max-aggregation loop (op with ``agg_mode=1`` →
+``sparse3d_max(ind, ori, inv)`` → ``norm_sp_3d`` / ``norm_sp_3d_max``) and the decode
+ordering (bound, score desc, tail asc, top-k) in ``mkg_proof_decode_max``.
+
+``kernel_sparse_scores(model, heads, rels, graph, args, is_training)`` keeps the
+reference signature.  Hops the fused loop does not cover (an edge cap, entity pruning
+that is not a no-op, dropout while training) run hop by hop through
+``FastLogFunctionSparse3DTopK`` and the reducers, exactly as the reference composes them.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as N
+from .fastlog_kernel import FastLogFunctionSparse3DTopK
+from .graph import DeviceGraph, build_csr_structure
+from .sparse_reducers import normalize_sparse3d, prune_sparse3d_active_entities, sum_sp_3d, sum_sparse3d_concat
+
+UNCAPPED = 1 << 60
+
+
+def _params(B, L, E, R, hops, threshold=0.0, topk_edges=UNCAPPED):
+    return N.ProofParams(int(B), int(L), int(E), int(R), int(hops), int(topk_edges), float(threshold), 0, None, None)
+
+
+class ProofRunner:
+    """One hop-loop configuration on one graph with its workspace (reused across calls).
+
+    ``forward`` keeps every hop's state in the workspace; ``backward`` consumes it, so a
+    forward must precede each backward.  Optional ``torch.cuda.Event`` lists (2 per hop)
+    are recorded around the pull kernels of each hop.
+    """
+
+    def __init__(self, graph: DeviceGraph, B: int, L: int, hops: int, threshold: float = 0.0):
+        lib = N.load()
+        self.graph = graph
+        self.B, self.L, self.K = int(B), int(L), int(hops)
+        self.n = 2 * graph.num_relations + 1
+        self.p = _params(B, L, graph.num_entities, graph.num_relations, hops, threshold)
+        self.ws = N.workspace(lib.mkg_proof_workspace_bytes(ctypes.byref(self.p)), graph.device)
+        self._keep = []
+
+    def _events(self, events):
+        if events is None:
+            return None
+        arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+        self._keep.append(arr)
+        return ctypes.cast(arr, ctypes.c_void_p)
+
+    def forward(self, heads, w_hops, out=None, msgs=None, events=None):
+        lib = N.load()
+        g = self.graph
+        dev = g.device
+        if tuple(w_hops.shape) != (self.K, self.B, self.L, self.n):
+            raise ValueError(f"w_hops must be {(self.K, self.B, self.L, self.n)}, got {tuple(w_hops.shape)}")
+        wf = w_hops.detach().to(torch.float32).contiguous()
+        hd = heads.to(device=dev, dtype=torch.int64).contiguous()
+        out = torch.empty((self.B, g.num_entities), dtype=torch.float32, device=dev) if out is None else out
+        msgs = torch.zeros(self.K, dtype=torch.int64, device=dev) if msgs is None else msgs
+        self._keep = [wf, hd]
+        self.p.fwd_events, self.p.bwd_events = self._events(events), None
+        adj = g.adjacency()
+        N.check(lib.mkg_proof_forward(ctypes.byref(g.struct), ctypes.byref(adj), hd.data_ptr(), wf.data_ptr(),
+                                      ctypes.byref(self.p), self.ws.data_ptr(), self.ws.numel(), out.data_ptr(),
+                                      msgs.data_ptr(), N.error_word(dev).data_ptr(), N.stream_handle(dev)),
+                "proof_forward")
+        self.p.fwd_events = None
+        return out, msgs
+
+    def backward(self, grad_out, mask, edge_scores, is_score, scale, want_edge_grad: bool, grad_w=None,
+                 grad_edge=None, events=None):
+        lib = N.load()
+        g = self.graph
+        dev = g.device
+        keep = []
+        f = N.edge_factor(mask, edge_scores, is_score, scale, keep)
+        go = grad_out.detach().to(torch.float32).contiguous()
+        if grad_w is None:
+            grad_w = torch.empty((self.K, self.B, self.L, self.n), dtype=torch.float32, device=dev)
+        if want_edge_grad and grad_edge is None:
+            grad_edge = torch.empty(g.num_facts, dtype=torch.float32, device=dev)
+        self.p.bwd_events = self._events(events)
+        adj = g.adjacency()
+        N.check(lib.mkg_proof_backward(ctypes.byref(g.struct), ctypes.byref(adj), None, ctypes.byref(self.p),
+                                       ctypes.byref(f), go.data_ptr(), grad_w.data_ptr(),
+                                       N.ptr(grad_edge) if want_edge_grad else None, self.ws.data_ptr(),
+                                       self.ws.numel(), N.error_word(dev).data_ptr(), N.stream_handle(dev)),
+                "proof_backward")
+        self.p.bwd_events = None
+        return grad_w, (grad_edge if want_edge_grad else None)
+
+    def row_activity(self, hop: int) -> torch.Tensor:
+        """uint8 [E]: entities holding a non-zero state value when hop ``hop`` starts."""
+        lib = N.load()
+        flags = torch.empty(self.graph.num_entities, dtype=torch.uint8, device=self.graph.device)
+        N.check(lib.mkg_proof_row_activity(ctypes.byref(self.p), self.ws.data_ptr(), self.ws.numel(), int(hop),
+                                           flags.data_ptr(), N.stream_handle(self.graph.device)), "row_activity")
+        return flags
+
+
+class HopLoopSum(torch.autograd.Function):
+    """Sum-aggregation hop loop: ``(w_hops [K,B,L,n], edge_scores [T]) -> out [B,E]``."""
+
+    @staticmethod
+    def forward(ctx, w_hops, edge_scores, heads, graph: DeviceGraph, mask, is_score: bool, scale: float,
+                threshold: float):
+        K, B, L, n = (int(s) for s in w_hops.shape)
+        if n != 2 * graph.num_relations + 1:
+            raise ValueError(f"w_hops has {n} channels, expected 2R+1 = {2 * graph.num_relations + 1}")
+        graph.set_edge_factor(mask, edge_scores, is_score, scale)
+        runner = ProofRunner(graph, B, L, K, threshold)
+        out, msgs = runner.forward(heads, w_hops)
+        ctx.runner = runner
+        ctx.mask, ctx.is_score, ctx.scale = mask, bool(is_score), float(scale)
+        ctx.edge_scores = edge_scores.detach() if edge_scores is not None else None
+        ctx.want_edge = edge_scores is not None and ctx.needs_input_grad[1]
+        ctx.mark_non_differentiable(msgs)
+        return out, msgs
+
+    @staticmethod
+    def backward(ctx, grad_out, _grad_msgs):
+        runner: ProofRunner = ctx.runner
+        # the factor column of the neighbour lists may have been rewritten by a later forward
+        runner.graph.set_edge_factor(ctx.mask, ctx.edge_scores, ctx.is_score, ctx.scale)
+        grad_w, grad_edge = runner.backward(grad_out, ctx.mask, ctx.edge_scores, ctx.is_score, ctx.scale,
+                                            ctx.want_edge)
+        ge = None
+        if grad_edge is not None:
+            ge = grad_edge.view(ctx.edge_scores.shape).to(ctx.edge_scores.dtype)
+        return grad_w, ge, None, None, None, None, None, None
+
+
+def proof_scores(graph: DeviceGraph, heads: torch.Tensor, w_hops: torch.Tensor, edge_scores: torch.Tensor | None,
+                 mask: torch.Tensor | None = None, is_score: bool = True, scale: float = 1.0,
+                 threshold: float = 0.0):
+    """Dense raw scores ``[B, E]`` of the hop loop and the per-hop message counts ``[K]``."""
+    return HopLoopSum.apply(w_hops, edge_scores, heads, graph, mask, is_score, scale, threshold)
+
+
+@dataclass
+class DecodeResult:
+    raw: torch.Tensor      # [B, E] raw max scores (0 = no proof)
+    tails: torch.Tensor    # [B, k] int64, -1 padded
+    scores: torch.Tensor   # [B, k] float32 bounded scores
+    counts: torch.Tensor   # [B] int64
+
+
+def decode_max(graph: DeviceGraph, heads: torch.Tensor, w_hops: torch.Tensor, topk: int,
+               edge_scores: torch.Tensor | None, mask: torch.Tensor | None = None, is_score: bool = True,
+               scale: float = 1.0) -> DecodeResult:
+    """Max-aggregation hop loop + decode order (score desc, tail asc), top-``topk`` per query."""
+    lib = N.load()
+    dev = graph.device
+    K, B, L, n = (int(s) for s in w_hops.shape)
+    E, R = graph.num_entities, graph.num_relations
+    wf = w_hops.detach().to(torch.float32).contiguous()
+    hd = heads.to(device=dev, dtype=torch.int64).contiguous()
+    graph.set_edge_factor(mask, edge_scores, is_score, scale)
+    p = _params(B, L, E, R, K)
+    ws = N.workspace(lib.mkg_decode_workspace_bytes(ctypes.byref(p), int(topk)), dev)
+    raw = torch.empty((B, E), dtype=torch.float32, device=dev)
+    tails = torch.empty((B, int(topk)), dtype=torch.int64, device=dev)
+    scores = torch.empty((B, int(topk)), dtype=torch.float32, device=dev)
+    counts = torch.empty(B, dtype=torch.int64, device=dev)
+    adj = graph.adjacency()
+    N.check(lib.mkg_proof_decode_max(ctypes.byref(graph.struct), ctypes.byref(adj), hd.data_ptr(), wf.data_ptr(),
+                                     ctypes.byref(p), int(topk), raw.data_ptr(), tails.data_ptr(),
+                                     scores.data_ptr(), counts.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     N.error_word(dev).data_ptr(), N.stream_handle(dev)), "proof_decode_max")
+    return DecodeResult(raw, tails, scores, counts)
+
+
+def decode_topk(raw: torch.Tensor, topk: int):
+    """bound_sparse_scores + sparse_candidate_rows + ordered_tail_scores on a dense [B, E]
+    score matrix (entries != 0 are the candidates): (tails, scores, counts)."""
+    lib = N.load()
+    N.require_cuda(raw, "raw")
+    r = raw.detach().to(torch.float32).contiguous()
+    B, E = (int(s) for s in r.shape)
+    tails = torch.empty((B, int(topk)), dtype=torch.int64, device=r.device)
+    scores = torch.empty((B, int(topk)), dtype=torch.float32, device=r.device)
+    counts = torch.empty(B, dtype=torch.int64, device=r.device)
+    N.check(lib.mkg_decode_topk(r.data_ptr(), B, E, int(topk), tails.data_ptr(), scores.data_ptr(),
+                                counts.data_ptr(), N.stream_handle(r.device)), "decode_topk")
+    return tails, scores, counts
+
+
+# ---------------------------------------------------------------------------- drop-in
+def _device_graph_for(model, graph) -> DeviceGraph:
+    """The model-level CSR cache of proof.py:496-506, holding a ``DeviceGraph``."""
+    cache_key = (graph.e2triple[0].data_ptr(), graph.triple2e[1].data_ptr(), graph.r2triple[0].data_ptr())
+    if getattr(model, "_b200_graph_key", None) != cache_key:
+        csr = build_csr_structure(graph.e2triple[0], graph.triple2e[1], graph.r2triple[0], model.entity_count,
+                                  model.relation_count)
+        model._kernel_csr = csr
+        model._b200_graph = DeviceGraph(csr, model.entity_count, model.relation_count)
+        model._b200_graph_key = cache_key
+    return model._b200_graph
+
+
+def _edge_inputs(model, graph, is_training):
+    """Edge scores / mask exactly as proof.py:525-550 picks them (score path)."""
+    edge_scores = model.weight
+    if is_training and torch.is_grad_enabled():
+        edge_scores = edge_scores.reshape(-1).clone()
+    else:
+        edge_scores = edge_scores.reshape(-1)
+    mask = graph.mask_float if getattr(graph, "mask_float", None) is not None else None
+    return edge_scores, mask, True, 1.0
+
+
+def kernel_sparse_scores(model, heads, rels, graph, args, is_training: bool, dense: bool = False):
+    """Drop-in for proof.py:467-614 (score edge-weight path).
+
+    Returns the sparse ``[B, E]`` result of the reference (``dense=True``: the dense
+    matrix, which the reference's consumers also accept).
+    """
+    g = _device_graph_for(model, graph)
+    B, L, E, R, K = heads.shape[0], model.rules, model.entity_count, model.relation_count, model.step
+    rule_logits = model.build_rule_logits(rels)
+    edge_scores, mask, is_score, scale = _edge_inputs(model, graph, is_training)
+    topk_edges = int(args.kernel_topk_edges)
+    topk_nodes = int(args.kernel_topk_nodes)
+    p_drop = float(getattr(getattr(model, "dropout", None), "p", 0.0) or 0.0)
+    fused = topk_edges >= UNCAPPED and (topk_nodes <= 0 or topk_nodes >= E) and not (is_training and p_drop > 0)
+    if fused:
+        w_hops = torch.stack([torch.softmax(rule_logits[:, h] / model.tau_1, dim=-1) for h in range(K)])
+        out, _ = HopLoopSum.apply(w_hops, edge_scores, heads, g, mask, is_score, scale, 0.0)
+        return out if dense else out.to_sparse_coo().coalesce()
+    # hop by hop, as the reference composes it
+    dev = g.device
+    state = torch.sparse_coo_tensor(
+        torch.stack([torch.arange(B, device=dev).repeat_interleave(L), torch.arange(L, device=dev).repeat(B),
+                     heads.to(dev).long().repeat_interleave(L)]),
+        torch.ones(B * L, device=dev), [B, L, E], is_coalesced=True)
+    mvals = mask if mask is not None else torch.ones((), dtype=torch.float32, device=dev)
+    for hop in range(K):
+        state = prune_sparse3d_active_entities(state, topk_nodes)
+        w_t = torch.softmax(rule_logits[:, hop] / model.tau_1, dim=-1)
+        o, i, d = FastLogFunctionSparse3DTopK.apply(state.indices()[0], state.indices()[1], state.indices()[2],
+                                                    state.values(), w_t, *g.csr, mvals, edge_scores, B, L, E, R,
+                                                    False, topk_edges, 0, is_score, scale)
+        state = normalize_sparse3d(sum_sparse3d_concat(o, i, d), 0.0, "mass")
+        if is_training:
+            state = torch.sparse_coo_tensor(state.indices(), model.dropout(state.values()), state.shape).coalesce()
+    out = sum_sp_3d(state)
+    return out.to_dense() if dense else out

@@ -1,0 +1,439 @@
+"""Parity of the CUDA path (through the C ABI) against the oracle and the golden vectors.
+
+Bar: integer / index / argmax / bucketing / decode results bit-exact; fp32 sums and
+gradients within rtol 1e-5, atol 1e-6 (multi-hop gradients, whose error compounds over
+three hops of sums, within rtol 1e-4, atol 1e-5).
+"""
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fastlog_oracle as O
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+UNC = O.UNCAPPED
+DEV = torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    from minikg_dev_b200 import _native
+    _native.load()
+
+
+def T(x, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    return t.to(DEV, dtype=dtype) if dtype is not None else t.to(DEV)
+
+
+def coo_np(sp, L, E):
+    sp = sp.coalesce()
+    idx = sp.indices().cpu().numpy()
+    return O.keys3(idx[0], idx[1], idx[2], L, E), sp.values().detach().cpu().numpy()
+
+
+def csr_dev(csr_np):
+    return tuple(T(a) for a in csr_np)
+
+
+def graphs():
+    from minikg_dev_b200.synth import sample_graph
+    out = {}
+    for name in ("g1", "g2"):
+        g = load_golden(name)
+        out[name] = (g["head"], g["rel"], g["tail"], int(g["E"][0]), int(g["R"][0]))
+    kg = sample_graph(2500, 14, 60000, (("rel", ("zipf", 1.0)), ("head", (1.2, 3.0)), ("tail", (1.2, 3.0)),
+                                        ("hubs", (0.02, 0.5))), seed=5, name="hubby")
+    out["hubby"] = (kg.head, kg.rel, kg.tail, kg.num_entities, kg.num_relations)
+    return out
+
+
+GRAPHS = graphs()
+
+
+# ----------------------------------------------------------------------------- CSR build
+@pytest.mark.parametrize("name", list(GRAPHS))
+def test_csr_build_bit_exact(name):
+    from minikg_dev_b200.graph import build_csr_structure
+    h, r, t, E, R = GRAPHS[name]
+    mine = build_csr_structure(T(h), T(t), T(r), E, R)
+    want = O.build_csr_structure(h, t, r, E)
+    for k in range(16):
+        np.testing.assert_array_equal(mine[k].cpu().numpy().astype(np.int64), want[k].astype(np.int64),
+                                      err_msg=f"csr{k}")
+
+
+def test_ind2ptr():
+    from minikg_dev_b200.graph import ind2ptr
+    rng = np.random.default_rng(3)
+    idx = np.sort(rng.integers(0, 50, 400))
+    np.testing.assert_array_equal(ind2ptr(T(idx), 60).cpu().numpy(), O.ind2ptr(idx, 60))
+    np.testing.assert_array_equal(ind2ptr(T(np.empty(0, np.int64)), 5).cpu().numpy(), np.zeros(6))
+
+
+# ----------------------------------------------------------------------------- per-hop op
+def run_op(csr_np, E, R, fb, fl, fe, fv, w, mask, ew, cap, agg, is_score, wot_i=False, scale=1.0,
+           seeds=None):
+    from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
+    B, L, n = w.shape
+    sv = T(fv).requires_grad_(True)
+    wt = T(w).requires_grad_(True)
+    ewt = T(ew).requires_grad_(True) if ew is not None else None
+    mk = T(mask.astype(np.float32)) if mask is not None else torch.ones((), device=DEV)
+    o, i, d = FastLogFunctionSparse3DTopK.apply(T(fb), T(fl), T(fe), sv, wt, *csr_dev(csr_np), mk, ewt, B, L, E,
+                                                R, wot_i, int(cap), int(agg), bool(is_score), float(scale))
+    res = {"ori": coo_np(o, L, E), "inv": coo_np(i, L, E), "ind": coo_np(d, L, E)}
+    if seeds is not None:
+        loss = 0
+        for name, t in (("ori", o), ("inv", i), ("ind", d)):
+            t = t.coalesce()
+            loss = loss + (t.values() * T(seeds[name])).sum()
+        loss.backward()
+        res["grad_sp"] = sv.grad.cpu().numpy()
+        res["grad_w"] = wt.grad.cpu().numpy()
+        res["grad_edge"] = ewt.grad.cpu().numpy() if ewt is not None else None
+    return res
+
+
+OP_CASES = [("sum_unc", UNC, 0, True), ("sum_cap", 7, 0, True), ("max_unc", UNC, 1, True),
+            ("max_cap", 7, 1, True), ("sum_logit", UNC, 0, False), ("sum_cap0", 0, 0, True)]
+
+
+@pytest.mark.parametrize("gname", ["g1", "g2"])
+@pytest.mark.parametrize("tag,cap,agg,is_score", OP_CASES)
+def test_hop_op_vs_golden(gname, tag, cap, agg, is_score):
+    """The op against the reference's own outputs on the golden inputs."""
+    g = load_golden(gname)
+    E, R = int(g["E"][0]), int(g["R"][0])
+    w = g["op_w"]
+    B, L, _ = w.shape
+    csr = tuple(g[f"csr{k}"] for k in range(16))
+    seeds = {n: g[f"{tag}_seed_{n}"] for n in ("ori", "inv", "ind")}
+    res = run_op(csr, E, R, g["op_b"], g["op_l"], g["op_e"], g["op_v"], w, np.ones(g["head"].shape[0], bool),
+                 g[tag + "_ew"], cap, agg, is_score, seeds=seeds)
+    for name in ("ori", "inv", "ind"):
+        idx = g[f"{tag}_{name}_idx"]
+        want_k = O.keys3(idx[0], idx[1], idx[2], L, E)
+        np.testing.assert_array_equal(res[name][0], want_k, err_msg=name)
+        if agg == 1 and name != "ind":
+            np.testing.assert_array_equal(res[name][1], g[f"{tag}_{name}_val"], err_msg=name)
+        else:
+            tol = 1e-6 if is_score else 2e-6  # sigmoid path: CUDA double-rounded sigmoid vs torch's
+            np.testing.assert_allclose(res[name][1], g[f"{tag}_{name}_val"], rtol=tol, atol=1e-7, err_msg=name)
+    np.testing.assert_allclose(res["grad_sp"], g[tag + "_grad_sp"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(res["grad_w"], g[tag + "_grad_w"], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(res["grad_edge"], g[tag + "_grad_edge"], rtol=RTOL, atol=ATOL)
+
+
+def _frontier(rng, B, L, E, per_row, dup_values=True):
+    rows = []
+    for b in range(B):
+        for l in range(L):
+            for e in rng.choice(E, size=min(per_row, E), replace=False):
+                rows.append((b, l, int(e)))
+    a = np.array(sorted(rows), np.int64).reshape(-1, 3)
+    v = rng.uniform(0.05, 1.0, a.shape[0]).astype(np.float32)
+    if dup_values:
+        v[::5] = np.float32(0.25)
+    return a[:, 0].copy(), a[:, 1].copy(), a[:, 2].copy(), v
+
+
+@pytest.mark.parametrize("gname", ["hubby", "g2"])
+@pytest.mark.parametrize("cap,agg", [(UNC, 0), (UNC, 1), (3, 0), (3, 1), (40, 0), (1, 1), (0, 0)])
+@pytest.mark.parametrize("variant", ["plain", "zero_mask", "wot_i", "logit"])
+def test_hop_op_vs_oracle(gname, cap, agg, variant):
+    """Synthetic inputs with hubs (block-per-entry path), masked facts (explicit zero
+    outputs), the wot_i flag and the sigmoid edge path."""
+    h, r, t, E, R = GRAPHS[gname]
+    rng = np.random.default_rng(zlib.crc32(f"{gname}/{cap}/{agg}/{variant}".encode()))
+    csr = O.build_csr_structure(h, t, r, E)
+    B, L = 3, 2
+    n = 2 * R + 1
+    w = O.F32(1.0) * (rng.dirichlet(np.ones(n), size=(B, L))).astype(np.float32)
+    w[0, 0, :] = w[0, 0, 0]  # equal weights: many exact message ties
+    fb, fl, fe, fv = _frontier(rng, B, L, E, per_row=40)
+    # make sure the biggest hubs are in the frontier
+    deg = np.bincount(h, minlength=E) + np.bincount(t, minlength=E)
+    hubs = np.argsort(-deg)[:3]
+    extra = np.array([(0, 1, int(x)) for x in hubs], np.int64)
+    allk = np.unique(np.concatenate([O.keys3(fb, fl, fe, L, E), O.keys3(extra[:, 0], extra[:, 1], extra[:, 2], L, E)]))
+    fb, fl, fe = O.split3(allk, L, E)
+    fv = rng.uniform(0.05, 1.0, allk.shape[0]).astype(np.float32)
+    T_ = h.shape[0]
+    mask = np.ones(T_, bool)
+    if variant == "zero_mask":
+        mask[rng.random(T_) < 0.3] = False
+    is_score = variant != "logit"
+    ew = rng.uniform(0.05, 1.0, T_).astype(np.float32) if is_score else rng.standard_normal(T_).astype(np.float32)
+    if is_score:
+        ew[::4] = np.float32(0.5)
+    wot_i = variant == "wot_i"
+    scale = 0.7 if variant == "logit" else 1.0
+    fwd = O.sparse3d_forward(fb, fl, fe, fv, w, csr, mask, ew, B, L, E, R, wot_i=wot_i, cap=cap, agg_mode=agg,
+                             is_score=is_score, scale=scale)
+    seeds = {name: rng.standard_normal(fwd[name][0].shape[0]).astype(np.float32) for name in ("ori", "inv", "ind")}
+    res = run_op(csr, E, R, fb, fl, fe, fv, w, mask, ew, cap, agg, is_score, wot_i=wot_i, scale=scale, seeds=seeds)
+    for name in ("ori", "inv", "ind"):
+        np.testing.assert_array_equal(res[name][0], fwd[name][0], err_msg=name)
+        if agg == 1 and name != "ind" and is_score:
+            np.testing.assert_array_equal(res[name][1], fwd[name][1], err_msg=name)
+        else:
+            np.testing.assert_allclose(res[name][1], fwd[name][1], rtol=RTOL, atol=ATOL, err_msg=name)
+    grads = {name: (fwd[name][0], seeds[name]) for name in ("ori", "inv", "ind")}
+    gsp, gw, ge = O.sparse3d_backward(fwd, grads, fb, fl, fe, fv, w, B, L, E, R, wot_i=wot_i, agg_mode=agg,
+                                      edge_weight=ew, is_score=is_score, scale=scale, want_edge_grad=True,
+                                      num_facts=T_)
+    np.testing.assert_allclose(res["grad_sp"], gsp, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(res["grad_w"], gw, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(res["grad_edge"], ge, rtol=RTOL, atol=ATOL)
+
+
+def test_hop_op_argmax_facts_bit_exact():
+    """The argmax message per key (smallest fact id among equal maxima) through the C ABI."""
+    import ctypes
+    from minikg_dev_b200 import _native as N
+    from minikg_dev_b200.graph import DeviceGraph
+    h, r, t, E, R = GRAPHS["hubby"]
+    csr = O.build_csr_structure(h, t, r, E)
+    rng = np.random.default_rng(9)
+    B, L, n = 2, 2, 2 * R + 1
+    w = np.full((B, L, n), 0.05, np.float32)  # all channels equal: ties everywhere
+    fb, fl, fe, fv = _frontier(rng, B, L, E, per_row=30)
+    fv[:] = np.float32(0.5)
+    ew = np.full(h.shape[0], 0.5, np.float32)
+    fwd = O.sparse3d_forward(fb, fl, fe, fv, w, csr, np.ones(h.shape[0], bool), ew, B, L, E, R, agg_mode=1,
+                             is_score=True)
+    g = DeviceGraph(csr_dev(csr), E, R)
+    keep = [T(fb), T(fl), T(fe), T(fv)]
+    fr = N.Frontier(*(x.data_ptr() for x in keep), fb.shape[0])
+    wt = T(w)
+    f = N.edge_factor(None, T(ew), True, 1.0, keep)
+    p = N.HopParams(B, L, E, R, n, 0, 1, UNC)
+    lib = N.load()
+    ws = N.workspace(lib.mkg_hop_forward_workspace_bytes(ctypes.byref(p), fb.shape[0]), DEV)
+    counts = torch.zeros(3, dtype=torch.int64, device=DEV)
+    N.check(lib.mkg_hop_forward(ctypes.byref(g.struct), ctypes.byref(fr), wt.data_ptr(), ctypes.byref(f),
+                                ctypes.byref(p), ws.data_ptr(), ws.numel(), counts.data_ptr(),
+                                N.error_word(DEV).data_ptr(), None), "hop_forward")
+    sizes = counts.tolist()
+    for which, name in ((0, "ori"), (1, "inv")):
+        U = sizes[which]
+        idx = torch.empty((3, U), dtype=torch.int64, device=DEV)
+        val = torch.empty(U, dtype=torch.float32, device=DEV)
+        arg = torch.empty(U, dtype=torch.int64, device=DEV)
+        N.check(lib.mkg_hop_emit(ctypes.byref(p), fb.shape[0], ws.data_ptr(), ws.numel(), which, U, idx.data_ptr(),
+                                 val.data_ptr(), arg.data_ptr(), None), "hop_emit")
+        raw = fwd["raw_" + name]
+        np.testing.assert_array_equal(arg.cpu().numpy(), raw["edge"][fwd[name + "_arg"]])
+        np.testing.assert_array_equal(val.cpu().numpy(), fwd[name][1])
+
+
+def test_hop_op_empty_frontier():
+    from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
+    h, r, t, E, R = GRAPHS["g1"]
+    csr = csr_dev(O.build_csr_structure(h, t, r, E))
+    e = torch.empty(0, dtype=torch.int64, device=DEV)
+    w = torch.full((2, 2, 2 * R + 1), 0.1, device=DEV)
+    o, i, d = FastLogFunctionSparse3DTopK.apply(e, e, e, torch.empty(0, device=DEV), w, *csr,
+                                                torch.ones(h.shape[0], device=DEV), None, 2, 2, E, R, False, UNC, 0)
+    assert o._nnz() == 0 and i._nnz() == 0 and d._nnz() == 0
+
+
+def test_bad_index_is_reported_not_faulted():
+    from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
+    h, r, t, E, R = GRAPHS["g1"]
+    csr = csr_dev(O.build_csr_structure(h, t, r, E))
+    b = torch.tensor([0, 0], device=DEV)
+    l = torch.tensor([0, 0], device=DEV)
+    ent = torch.tensor([1, E + 5], device=DEV)  # second entity is out of range
+    w = torch.full((1, 1, 2 * R + 1), 0.1, device=DEV)
+    with pytest.raises(RuntimeError, match="outside"):
+        FastLogFunctionSparse3DTopK.apply(b, l, ent, torch.ones(2, device=DEV), w, *csr, torch.ones((), device=DEV),
+                                          None, 1, 1, E, R, False, UNC, 0)
+    torch.cuda.synchronize()  # the context is still usable
+    assert torch.ones(4, device=DEV).sum().item() == 4.0
+
+
+# ----------------------------------------------------------------------------- fused loop
+def _w_hops_from_logits(logits):
+    lg = torch.from_numpy(logits)
+    return np.stack([torch.softmax(lg[:, t], dim=-1).numpy() for t in range(lg.shape[1])])
+
+
+@pytest.mark.parametrize("gname", ["g1", "g2"])
+def test_fused_loop_vs_golden(gname):
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import proof_scores
+    g = load_golden(gname)
+    E, R = int(g["E"][0]), int(g["R"][0])
+    heads, logits, scores = g["pr_heads"], g["pr_logits"], g["pr_scores"]
+    B, K, L, n = logits.shape
+    dg = DeviceGraph(csr_dev(tuple(g[f"csr{k}"] for k in range(16))), E, R)
+    lg = T(logits).requires_grad_(True)
+    w_hops = torch.stack([torch.softmax(lg[:, t], dim=-1) for t in range(K)])
+    sc = T(scores).requires_grad_(True)
+    out, msgs = proof_scores(dg, T(heads), w_hops, sc, mask=torch.ones(g["head"].shape[0], device=DEV))
+    idx = g["pr_unc_final_idx"]
+    dense = np.zeros((B, E), np.float32)
+    dense[idx[0], idx[1]] = g["pr_unc_final_val"]
+    got = out.detach().cpu().numpy()
+    np.testing.assert_array_equal(got != 0, dense != 0)
+    np.testing.assert_allclose(got, dense, rtol=RTOL, atol=ATOL)
+    seed = np.zeros((B, E), np.float32)
+    seed[idx[0], idx[1]] = g["pr_unc_seed"]
+    (out * T(seed)).sum().backward()
+    np.testing.assert_allclose(lg.grad.cpu().numpy(), g["pr_unc_grad_logits"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), g["pr_unc_grad_edge"], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("gname", ["hubby", "g2"])
+@pytest.mark.parametrize("B,L,K", [(5, 3, 3), (40, 4, 2)])
+def test_fused_loop_vs_oracle(gname, B, L, K):
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import proof_scores
+    h, r, t, E, R = GRAPHS[gname]
+    rng = np.random.default_rng(B * 100 + K)
+    csr = O.build_csr_structure(h, t, r, E)
+    n = 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    scores = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    mask = np.ones(h.shape[0], bool)
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    wt = T(w_hops).requires_grad_(True)
+    sc = T(scores).requires_grad_(True)
+    out, msgs = proof_scores(dg, T(heads), wt, sc, mask=None)
+    want = np.zeros((B, E), np.float32)
+    b, e = final[0] // E, final[0] % E
+    want[b, e] = final[1]
+    got = out.detach().cpu().numpy()
+    np.testing.assert_array_equal(got != 0, want != 0)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    exp_msgs = [O.count_messages(tr["state"], csr, w_hops[k], L, E, R) for k, tr in enumerate(trace)]
+    assert msgs.cpu().tolist() == exp_msgs
+    seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
+    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
+                                  num_facts=h.shape[0])
+    gd = np.zeros((B, E), np.float32)
+    gd[b, e] = seed
+    (out * T(gd)).sum().backward()
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("gname", ["g1", "g2"])
+def test_max_decode_vs_golden_bit_exact(gname):
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import decode_max
+    g = load_golden(gname)
+    E, R = int(g["E"][0]), int(g["R"][0])
+    heads, logits, scores = g["pr_heads"], g["pr_logits"], g["pr_scores"]
+    B, K, L, n = logits.shape
+    w_hops = _w_hops_from_logits(logits)
+    dg = DeviceGraph(csr_dev(tuple(g[f"csr{k}"] for k in range(16))), E, R)
+    k = g["dec_unc_tails"].shape[1]
+    res = decode_max(dg, T(heads), T(w_hops), k, T(scores), mask=None)
+    idx = g["dec_unc_final_idx"]
+    want = np.zeros((B, E), np.float32)
+    want[idx[0], idx[1]] = g["dec_unc_final_val"]
+    np.testing.assert_array_equal(res.raw.cpu().numpy(), want)
+    # oracle decode of the same raw scores: bit-exact; golden: tails exact, scores within one exp ulp
+    ot, osc, oc = O.decode_topk((idx[0] * E + idx[1], g["dec_unc_final_val"]), B, E, k)
+    np.testing.assert_array_equal(res.tails.cpu().numpy(), ot)
+    np.testing.assert_array_equal(res.scores.cpu().numpy(), osc)
+    np.testing.assert_array_equal(res.counts.cpu().numpy(), oc)
+    np.testing.assert_array_equal(res.tails.cpu().numpy(), g["dec_unc_tails"])
+    np.testing.assert_allclose(res.scores.cpu().numpy(), g["dec_unc_scores"], rtol=0, atol=6e-8)
+
+
+@pytest.mark.parametrize("gname", ["hubby", "g2"])
+def test_max_decode_vs_oracle_bit_exact(gname):
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import decode_max
+    h, r, t, E, R = GRAPHS[gname]
+    rng = np.random.default_rng(17)
+    csr = O.build_csr_structure(h, t, r, E)
+    B, L, K, n = 24, 3, 3, 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    w_hops[:, 0, 0, :] = np.float32(1.0 / n)  # a tie-heavy query
+    scores = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    scores[::3] = np.float32(0.5)
+    final, _ = O.proof_max_forward(heads, w_hops, csr, np.ones(h.shape[0], bool), scores, B, L, E, R)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    res = decode_max(dg, T(heads), T(w_hops), 100, T(scores))
+    want = np.zeros((B, E), np.float32)
+    want[final[0] // E, final[0] % E] = final[1]
+    np.testing.assert_array_equal(res.raw.cpu().numpy(), want)
+    ot, osc, oc = O.decode_topk(final, B, E, 100)
+    np.testing.assert_array_equal(res.tails.cpu().numpy(), ot)
+    np.testing.assert_array_equal(res.scores.cpu().numpy(), osc)
+    np.testing.assert_array_equal(res.counts.cpu().numpy(), oc)
+
+
+def test_decode_topk_ties_and_short_rows():
+    from minikg_dev_b200.proof import decode_topk
+    rng = np.random.default_rng(4)
+    B, E = 6, 3000
+    raw = np.zeros((B, E), np.float32)
+    for b in range(B):
+        m = [5, 150, 2999, 0, 1000, 7][b]
+        cols = rng.choice(E, m, replace=False)
+        raw[b, cols] = rng.choice(np.array([0.5, 0.25, 1.5, 3.0, 1e-9], np.float32), m)
+    for k in (1, 10, 100, 1024):
+        tails, scores, counts = decode_topk(T(raw), k)
+        keys = np.nonzero(raw.reshape(-1))[0]
+        ot, osc, oc = O.decode_topk((keys, raw.reshape(-1)[keys]), B, E, k)
+        np.testing.assert_array_equal(tails.cpu().numpy(), ot)
+        np.testing.assert_array_equal(scores.cpu().numpy(), osc)
+        np.testing.assert_array_equal(counts.cpu().numpy(), oc)
+
+
+# ----------------------------------------------------------------------------- drop-in
+@pytest.mark.parametrize("gname", ["g1", "g2"])
+@pytest.mark.parametrize("tag,cap,topk_nodes", [("pr_unc", UNC, 0), ("pr_cap", 9, 0), ("pr_prune", UNC, 40)])
+def test_kernel_sparse_scores_drop_in(gname, tag, cap, topk_nodes):
+    """The reference's hop driver signature, with a duck-typed model / graph / args."""
+    from types import SimpleNamespace
+    from minikg_dev_b200.proof import kernel_sparse_scores
+    g = load_golden(gname)
+    E, R = int(g["E"][0]), int(g["R"][0])
+    heads, logits, scores = g["pr_heads"], g["pr_logits"], g["pr_scores"]
+    B, K, L, n = logits.shape
+    lg = T(logits).requires_grad_(True)
+    wt = T(scores).requires_grad_(True)
+    model = SimpleNamespace(rules=L, entity_count=E, relation_count=R, step=K, tau_1=1.0, weight=wt,
+                            dropout=torch.nn.Identity(), build_rule_logits=lambda rels: lg)
+    head_t, rel_t, tail_t = T(g["head"]), T(g["rel"]), T(g["tail"])
+    mask = torch.ones(head_t.shape[0], dtype=torch.bool, device=DEV)
+    graph = SimpleNamespace(e2triple=(head_t, None, mask), triple2e=(None, tail_t, mask), r2triple=(rel_t, None, mask),
+                            mask=mask, mask_float=mask.float())
+    args = SimpleNamespace(kernel_topk_edges=cap, kernel_topk_nodes=topk_nodes)
+    out = kernel_sparse_scores(model, T(heads), T(np.zeros(B, np.int64)), graph, args, is_training=True)
+    out = out.coalesce()
+    idx = out.indices().cpu().numpy()
+    gi = g[tag + "_final_idx"]
+    if cap >= UNC:  # the build's CSR order inside a (row, rel) group may differ only when a cap cuts a group
+        np.testing.assert_array_equal(idx, gi)
+        np.testing.assert_allclose(out.values().detach().cpu().numpy(), g[tag + "_final_val"], rtol=RTOL, atol=ATOL)
+        (out.values() * T(g[tag + "_seed"])).sum().backward()
+        np.testing.assert_allclose(lg.grad.cpu().numpy(), g[tag + "_grad_logits"], rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(wt.grad.cpu().numpy(), g[tag + "_grad_edge"], rtol=1e-4, atol=1e-5)
+    else:
+        # capped: compare against the oracle on the build's own (stable) CSR
+        csr = O.build_csr_structure(g["head"], g["tail"], g["rel"], E)
+        w_hops = _w_hops_from_logits(logits)
+        final, _ = O.proof_sum_forward(heads, w_hops, csr, np.ones(g["head"].shape[0], bool), scores, B, L, E, R,
+                                       cap=cap, topk_nodes=topk_nodes)
+        np.testing.assert_array_equal(idx[0] * E + idx[1], final[0])
+        np.testing.assert_allclose(out.values().detach().cpu().numpy(), final[1], rtol=RTOL, atol=ATOL)
