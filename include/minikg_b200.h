@@ -123,6 +123,17 @@ size_t mkg_ind2ptr_workspace_bytes(int64_t size);
 int mkg_ind2ptr(const int64_t* index, int64_t n, int64_t size, int64_t* ptr, void* workspace,
                 size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
 
+/* ind2ptr for callers that cannot allocate device memory (for example a C or FFI host
+ * holding only the device pointers it was given): same inputs and output as mkg_ind2ptr,
+ * no workspace argument.  No counterpart in the reference.  Its scratch is one static
+ * device array of about 8.3 MiB that every GPU loading the library keeps until exit;
+ * size is limited to MKG_NOALLOC_MAX_ROWS rows (larger: MKG_ERR_CAPACITY).  The first call
+ * on a device looks the array up and should come before any stream capture; calls that
+ * overlap on the GPU share the array and race. */
+#define MKG_NOALLOC_MAX_ROWS (1 << 20)
+int mkg_ind2ptr_noalloc(const int64_t* index, int64_t n, int64_t size, int64_t* ptr, unsigned* dev_err,
+                        mkg_stream stream);
+
 /* Per-fact endpoints recovered from the ori CSR (used by the argmax backward):
  * fact_head[f], fact_tail[f], fact_rel[f].  No reference counterpart: the reference
  * keeps them per raw message (meta_entry / meta_rel, fastlog.cu:2314-2317). */

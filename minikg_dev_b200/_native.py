@@ -78,6 +78,7 @@ SIGNATURES = {
     "mkg_csr_build": (C.c_int, [vp, vp, vp, i64, i64, i64, CsrDirOut, CsrDirOut, vp, vp, C.c_size_t, vp, vp]),
     "mkg_ind2ptr_workspace_bytes": (C.c_size_t, [i64]),
     "mkg_ind2ptr": (C.c_int, [vp, i64, i64, vp, vp, C.c_size_t, vp, vp]),
+    "mkg_ind2ptr_noalloc": (C.c_int, [vp, i64, i64, vp, vp, vp]),
     "mkg_fact_table": (C.c_int, [P(Graph), vp, vp, vp, vp, vp]),
     "mkg_adjacency_max_tasks": (i64, [i64, i64]),
     "mkg_adjacency_workspace_bytes": (C.c_size_t, [i64]),
