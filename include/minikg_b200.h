@@ -39,7 +39,8 @@ enum {
   MKG_DEV_BAD_COL = 2u,    /* CSR column / neighbour outside [0, E) */
   MKG_DEV_BAD_FACT = 4u,   /* CSR order / fact id outside [0, T) */
   MKG_DEV_BAD_KEY = 8u,    /* gradient COO key outside [B, L, E] */
-  MKG_DEV_BAD_REL = 16u    /* relation id outside [0, R) */
+  MKG_DEV_BAD_REL = 16u,   /* relation id outside [0, R) */
+  MKG_DEV_TIMEOUT = 32u    /* a bounded wait inside a kernel gave up */
 };
 
 /* One direction of the reference CSR pair (fastlog_kernel.py:403-410 tuple order). */

@@ -19,7 +19,7 @@ MKG_OK = 0
 MASK_NONE, MASK_U8, MASK_F32 = 0, 1, 2
 DEV_ERR_NAMES = {1: "frontier entry outside [B, L, E]", 2: "CSR column outside [0, E)",
                  4: "fact id outside [0, T)", 8: "gradient key outside [B, L, E]",
-                 16: "relation id outside its range"}
+                 16: "relation id outside its range", 32: "a bounded wait inside a kernel gave up"}
 
 vp = C.c_void_p
 i64 = C.c_int64

@@ -21,9 +21,12 @@ namespace mkg {
 
 constexpr int kChunk = 128;      // columns per block (32 lanes x float4)
 constexpr int kFwdWarps = 8;
-constexpr int kBwdWarps = 16;
+constexpr int kBwdWarps = 8;
 constexpr int kTaskFirst = 1;    // task holds the row's first edges (adds the identity term)
 constexpr int kTaskPartial = 2;  // row split over several tasks: accumulate with atomics
+constexpr int kBatch = 8;        // edges whose rows are loaded together (8 x 16 B in flight per lane)
+constexpr int kGrab = 4;         // tasks per queue atomic
+constexpr int kQueueStride = 32; // ints between two queue counters
 
 struct ProofDims {
   int64_t B, L, E, R, n, hops, BL, BLP, nch;
@@ -43,7 +46,7 @@ namespace {
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct ProofLayout {
-  size_t wt, x, y, d, act, dxa, dxb, dy, s, dwt, queue, msgs, total;
+  size_t wt, x, y, d, act, yact, dxa, dxb, dy, s, dwt, queue, msgs, total;
 };
 
 ProofLayout proof_layout(const ProofDims& q) {
@@ -55,12 +58,13 @@ ProofLayout proof_layout(const ProofDims& q) {
   L.y = o; o += a256(slab) * q.hops;
   L.d = o; o += a256(4 * (size_t)q.hops * q.BLP);
   L.act = o; o += a256((size_t)(q.hops + 1) * q.E * q.nch);
+  L.yact = o; o += a256((size_t)q.hops * q.E * q.nch);
   L.dxa = o; o += a256(slab);
   L.dxb = o; o += a256(slab);
   L.dy = o; o += a256(slab);
   L.s = o; o += a256(4 * (size_t)q.hops * q.BLP);
   L.dwt = o; o += a256(4 * (size_t)q.n * q.BLP);
-  L.queue = o; o += a256(4 * (size_t)(2 * q.hops * q.nch));
+  L.queue = o; o += a256(4 * (size_t)(2 * q.hops * q.nch * kQueueStride));
   L.msgs = o; o += a256(8 * (size_t)(q.hops + 1));
   L.total = o;
   return L;
@@ -75,6 +79,8 @@ struct Slab {
   float* y(int64_t h) const { return reinterpret_cast<float*>(base + lay.y + a256(4 * (size_t)q.E * q.BLP) * h); }
   float* d(int64_t h) const { return reinterpret_cast<float*>(base + lay.d) + h * q.BLP; }
   uint8_t* act(int64_t h) const { return reinterpret_cast<uint8_t*>(base + lay.act) + h * q.E * q.nch; }
+  // non-zero pattern of Y_h per (row, chunk): where the backward's dY_h can be non-zero
+  uint8_t* yact(int64_t h) const { return reinterpret_cast<uint8_t*>(base + lay.yact) + h * q.E * q.nch; }
   float* dxa() const { return reinterpret_cast<float*>(base + lay.dxa); }
   float* dxb() const { return reinterpret_cast<float*>(base + lay.dxb); }
   float* dy() const { return reinterpret_cast<float*>(base + lay.dy); }
@@ -168,107 +174,210 @@ __device__ __forceinline__ void stage_weights(const float* __restrict__ wt, cons
   }
 }
 
-__device__ __forceinline__ int next_task(int32_t* queue, int lane) {
-  int t = 0;
-  if (lane == 0) t = atomicAdd(queue, 1);
-  return __shfl_sync(0xffffffffu, t, 0);
+// Dynamic task queue: a warp takes kGrab consecutive tasks per atomic and requests the
+// next group as soon as it starts one, so the atomic's latency overlaps the work.  Each
+// counter sits on its own 128-byte line (kQueueStride ints apart).
+
+struct TaskCursor {
+  int32_t* counter;
+  int64_t ntasks;
+  int64_t base;
+  int pending;  // lane 0: the next group's first task, not yet broadcast
+  int i;
+  __device__ __forceinline__ TaskCursor(int32_t* c, int64_t n) : counter(c), ntasks(n), i(0) {
+    const int lane = threadIdx.x & 31;
+    int b = 0;
+    if (lane == 0) b = atomicAdd(counter, kGrab);
+    base = __shfl_sync(0xffffffffu, b, 0);
+    pending = lane == 0 ? atomicAdd(counter, kGrab) : 0;
+  }
+  __device__ __forceinline__ bool next(int64_t& t) {
+    if (i == kGrab) {
+      base = __shfl_sync(0xffffffffu, pending, 0);
+      if (base < ntasks && (threadIdx.x & 31) == 0) pending = atomicAdd(counter, kGrab);
+      i = 0;
+    }
+    t = base + i;
+    ++i;
+    return t < ntasks;
+  }
+};
+
+// VEC float4 of one lane: columns col0 + 4*lane + 128*v, v < VEC.
+template <int VEC>
+struct Lanes {
+  float4 v[VEC];
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+};
+
+// Activity flags are kept per 128-column chunk; a VEC-wide chunk is active if any of its
+// VEC sub-chunks is.
+template <int VEC>
+__device__ __forceinline__ bool active_vec(const uint8_t* __restrict__ act, int64_t row, int64_t chunk, int64_t nch) {
+  bool a = false;
+#pragma unroll
+  for (int v = 0; v < VEC; ++v)
+    if (chunk * VEC + v < nch) a = a || act[row * nch + chunk * VEC + v] != 0;
+  return a;
+}
+
+template <int VEC>
+__device__ __forceinline__ void load_lanes(Lanes<VEC>& out, const float* __restrict__ rowp, int64_t col,
+                                           int64_t BLP) {
+#pragma unroll
+  for (int k = 0; k < VEC; ++k)
+    out.v[k] = (col + 128 * k < BLP) ? *reinterpret_cast<const float4*>(rowp + col + 128 * k)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // ------------------------------------------------------------------ forward pull
-// MAX = false: sum aggregation (+ column sums into dsum); MAX = true: max of the message
-// values (sparse3d_max over ind / ori / inv of max-coalesced messages).
-template <bool MAX>
+// One warp per task (a segment of <= 64 records of one pull row) and column chunk of
+// 128*VEC columns.  Per batch of 32 records, the records whose source row is active in this
+// chunk are compacted into shared memory (one ballot), then walked four at a time.
+// MAX = false: sum aggregation.  Records of a row come grouped by channel, so m * X[src]
+// is summed per channel run and multiplied by the run's rule weights once (fp32 order
+// differs from the per-message products; the sum is within tolerance).  Column sums of
+// the output feed normalize_sparse3d.
+// MAX = true: max of the exact message values (X[src] * w[ch]) * m (sparse3d_max over the
+// op's ind / ori / inv outputs), rule weights read per record.
+template <bool MAX, int VEC>
 __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
     float* __restrict__ y, float* __restrict__ dsum, int32_t* __restrict__ queue, unsigned* err) {
-  extern __shared__ float smem[];
-  float* ws = smem;                       // [n][128]
-  float* cs = smem + q.n * kChunk;        // [4][32] column partial sums (conflict-free layout)
-  const int lane = threadIdx.x & 31;
+  __shared__ int4 recs[kFwdWarps][32];
+  __shared__ float cs[4 * 32 * VEC];  // column partial sums: cs[(v*4 + k)*32 + lane] = column 4*lane + k + 128*v
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t chunk = blockIdx.y;
-  const int64_t col0 = chunk * kChunk;
+  const int64_t col0 = chunk * (128 * VEC);
   const int64_t col = col0 + 4 * lane;
-  const bool colok = col < q.BLP;
-  stage_weights(wt, q, col0, ws);
   if (!MAX)
-    for (int i = threadIdx.x; i < kChunk; i += blockDim.x) cs[i] = 0.0f;
+    for (int i = threadIdx.x; i < 4 * 32 * VEC; i += blockDim.x) cs[i] = 0.0f;
   __syncthreads();
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 csum = zero;
-  const float4* wsv = reinterpret_cast<const float4*>(ws);
-  for (;;) {
-    const int t = next_task(queue + chunk, lane);
-    if (t >= ntasks) break;
+  Lanes<VEC> csum;
+  csum.zero();
+  TaskCursor cursor(queue + chunk * kQueueStride, ntasks);
+  int64_t t;
+  while (cursor.next(t)) {
     const int4 tk = tasks[t];
     const int64_t row = tk.x;
-    float4 acc = zero;
-    if ((tk.w & kTaskFirst) && act[row * q.nch + chunk] && colok) {
-      float4 xr = *reinterpret_cast<const float4*>(x + row * q.BLP + col);
-      float4 wi = wsv[(q.n - 1) * 32 + lane];
-      acc = f4_mul(xr, wi);
+    Lanes<VEC> acc, run;
+    acc.zero();
+    run.zero();
+    if ((tk.w & kTaskFirst) && active_vec<VEC>(act, row, chunk, q.nch)) {
+      Lanes<VEC> xr, wi;
+      load_lanes(xr, x + row * q.BLP, col, q.BLP);
+      load_lanes(wi, wt + (q.n - 1) * q.BLP, col, q.BLP);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) acc.v[k] = f4_mul(xr.v[k], wi.v[k]);
     }
+    int cur = -1;
     for (int base = tk.y; base < tk.z; base += 32) {
       const int cnt = min(32, tk.z - base);
       int4 rec = make_int4(0, 0, 0, 0);
-      if (lane < cnt) rec = reinterpret_cast<const int4*>(edges)[base + lane];
-      for (int j = 0; j < cnt; j += 4) {
-        int nb[4], ch[4];
-        float m[4];
-        bool ok[4];
+      bool live = false;
+      if (lane < cnt) {
+        rec = reinterpret_cast<const int4*>(edges)[base + lane];
+        if (rec.x < 0 || rec.x >= q.E || rec.y < 0 || rec.y >= q.n - 1) raise_flag(err, MKG_DEV_BAD_COL);
+        else live = active_vec<VEC>(act, rec.x, chunk, q.nch);
+      }
+      const unsigned mask = __ballot_sync(0xffffffffu, live);
+      const int nact = __popc(mask);
+      if (live) recs[warp][__popc(mask & ((1u << lane) - 1u))] = rec;
+      __syncwarp();
+      for (int k0 = 0; k0 < nact; k0 += 4) {
+        int4 r[4];
+        Lanes<VEC> xv[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int jj = (j + u) & 31;
-          nb[u] = __shfl_sync(0xffffffffu, rec.x, jj);
-          ch[u] = __shfl_sync(0xffffffffu, rec.y, jj);
-          m[u] = __int_as_float(__shfl_sync(0xffffffffu, rec.w, jj));
-          ok[u] = (j + u) < cnt;
-          if (ok[u] && (nb[u] < 0 || nb[u] >= q.E || ch[u] < 0 || ch[u] >= q.n - 1)) {
-            if (lane == 0) raise_flag(err, MKG_DEV_BAD_COL);
-            ok[u] = false;
+          r[u] = (k0 + u < nact) ? recs[warp][k0 + u] : make_int4(0, -1, 0, 0);
+          if (r[u].y >= 0) load_lanes(xv[u], x + (int64_t)r[u].x * q.BLP, col, q.BLP);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (r[u].y < 0) continue;
+          const float m = __int_as_float(r[u].w);
+          if (MAX) {
+            Lanes<VEC> wv;
+            load_lanes(wv, wt + (int64_t)r[u].y * q.BLP, col, q.BLP);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) f4_max_msg(acc.v[k], xv[u].v[k], wv.v[k], m);
+          } else {
+            if (r[u].y != cur) {
+              if (cur >= 0) {
+                Lanes<VEC> wc;
+                load_lanes(wc, wt + (int64_t)cur * q.BLP, col, q.BLP);
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) {
+                  acc.v[k].x = fmaf(run.v[k].x, wc.v[k].x, acc.v[k].x);
+                  acc.v[k].y = fmaf(run.v[k].y, wc.v[k].y, acc.v[k].y);
+                  acc.v[k].z = fmaf(run.v[k].z, wc.v[k].z, acc.v[k].z);
+                  acc.v[k].w = fmaf(run.v[k].w, wc.v[k].w, acc.v[k].w);
+                }
+                run.zero();
+              }
+              cur = r[u].y;
+            }
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+              run.v[k].x = fmaf(xv[u].v[k].x, m, run.v[k].x);
+              run.v[k].y = fmaf(xv[u].v[k].y, m, run.v[k].y);
+              run.v[k].z = fmaf(xv[u].v[k].z, m, run.v[k].z);
+              run.v[k].w = fmaf(xv[u].v[k].w, m, run.v[k].w);
+            }
           }
-          ok[u] = ok[u] && act[(int64_t)nb[u] * q.nch + chunk];
         }
-        float4 xv[4];
+      }
+      __syncwarp();
+    }
+    if (!MAX && cur >= 0) {
+      Lanes<VEC> wc;
+      load_lanes(wc, wt + (int64_t)cur * q.BLP, col, q.BLP);
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          xv[u] = (ok[u] && colok) ? *reinterpret_cast<const float4*>(x + (int64_t)nb[u] * q.BLP + col) : zero;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (!ok[u]) continue;
-          const float4 wv = wsv[ch[u] * 32 + lane];
-          if (MAX) f4_max_msg(acc, xv[u], wv, m[u]);
-          else f4_fma(acc, xv[u], wv, m[u]);
-        }
+      for (int k = 0; k < VEC; ++k) {
+        acc.v[k].x = fmaf(run.v[k].x, wc.v[k].x, acc.v[k].x);
+        acc.v[k].y = fmaf(run.v[k].y, wc.v[k].y, acc.v[k].y);
+        acc.v[k].z = fmaf(run.v[k].z, wc.v[k].z, acc.v[k].z);
+        acc.v[k].w = fmaf(run.v[k].w, wc.v[k].w, acc.v[k].w);
       }
     }
-    if (colok) {
-      float* yr = y + row * q.BLP + col;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      const int64_t c = col + 128 * k;
+      if (c >= q.BLP) continue;
+      float* yr = y + row * q.BLP + c;
+      const float4 a = acc.v[k];
       if (tk.w & kTaskPartial) {
         if (MAX) {
-          atomicMax(reinterpret_cast<int*>(yr) + 0, __float_as_int(acc.x));
-          atomicMax(reinterpret_cast<int*>(yr) + 1, __float_as_int(acc.y));
-          atomicMax(reinterpret_cast<int*>(yr) + 2, __float_as_int(acc.z));
-          atomicMax(reinterpret_cast<int*>(yr) + 3, __float_as_int(acc.w));
+          atomicMax(reinterpret_cast<int*>(yr) + 0, __float_as_int(a.x));
+          atomicMax(reinterpret_cast<int*>(yr) + 1, __float_as_int(a.y));
+          atomicMax(reinterpret_cast<int*>(yr) + 2, __float_as_int(a.z));
+          atomicMax(reinterpret_cast<int*>(yr) + 3, __float_as_int(a.w));
         } else {
-          atomicAdd(yr + 0, acc.x); atomicAdd(yr + 1, acc.y);
-          atomicAdd(yr + 2, acc.z); atomicAdd(yr + 3, acc.w);
+          atomicAdd(yr + 0, a.x); atomicAdd(yr + 1, a.y);
+          atomicAdd(yr + 2, a.z); atomicAdd(yr + 3, a.w);
         }
       } else {
-        *reinterpret_cast<float4*>(yr) = acc;
+        *reinterpret_cast<float4*>(yr) = a;
       }
-      if (!MAX) { csum.x += acc.x; csum.y += acc.y; csum.z += acc.z; csum.w += acc.w; }
+      if (!MAX) { csum.v[k].x += a.x; csum.v[k].y += a.y; csum.v[k].z += a.z; csum.v[k].w += a.w; }
     }
   }
   if (!MAX) {
-    atomicAdd(cs + 0 * 32 + lane, csum.x);
-    atomicAdd(cs + 1 * 32 + lane, csum.y);
-    atomicAdd(cs + 2 * 32 + lane, csum.z);
-    atomicAdd(cs + 3 * 32 + lane, csum.w);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      atomicAdd(cs + (k * 4 + 0) * 32 + lane, csum.v[k].x);
+      atomicAdd(cs + (k * 4 + 1) * 32 + lane, csum.v[k].y);
+      atomicAdd(cs + (k * 4 + 2) * 32 + lane, csum.v[k].z);
+      atomicAdd(cs + (k * 4 + 3) * 32 + lane, csum.v[k].w);
+    }
     __syncthreads();
-    for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {
-      const int l = i % 32, k = i / 32;          // cs[k*32 + l] holds column 4*l + k
-      const int64_t c = col0 + 4 * l + k;
+    for (int i = threadIdx.x; i < 4 * 32 * VEC; i += blockDim.x) {
+      const int l = i % 32, kk = (i / 32) % 4, v = i / 128;
+      const int64_t c = col0 + 4 * l + kk + 128 * v;
       if (c < q.BLP && cs[i] != 0.0f) atomicAdd(dsum + c, cs[i]);
     }
   }
@@ -279,7 +388,8 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
 // message count of the next hop (present entries x push degree).
 __global__ void normalize_mass_kernel(const float* __restrict__ y, const float* __restrict__ dsum, ProofDims q,
                                       float threshold, float* __restrict__ x, uint8_t* __restrict__ act,
-                                      const int32_t* __restrict__ push_ptr, int64_t* __restrict__ msgs) {
+                                      uint8_t* __restrict__ yact, const int32_t* __restrict__ push_ptr,
+                                      int64_t* __restrict__ msgs) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -288,8 +398,10 @@ __global__ void normalize_mass_kernel(const float* __restrict__ y, const float* 
     const int64_t row = task / q.nch, chunk = task % q.nch;
     const int64_t col = chunk * kChunk + 4 * lane;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool ynz = false;
     if (col < q.BLP) {
       const float4 v = *reinterpret_cast<const float4*>(y + row * q.BLP + col);
+      ynz = v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f;
       const float4 d = *reinterpret_cast<const float4*>(dsum + col);
       float vi[4] = {v.x, v.y, v.z, v.w}, di[4] = {d.x, d.y, d.z, d.w}, oi[4];
 #pragma unroll
@@ -306,11 +418,13 @@ __global__ void normalize_mass_kernel(const float* __restrict__ y, const float* 
     }
     const int nz = f4_count(o);
     const unsigned any = __ballot_sync(0xffffffffu, nz > 0);
+    const unsigned yany = __ballot_sync(0xffffffffu, ynz);
     int tot = nz;
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
     if (lane == 0) {
       act[row * q.nch + chunk] = any ? 1 : 0;
+      yact[row * q.nch + chunk] = yany ? 1 : 0;
       if (tot) local_msgs += (long long)tot * (push_ptr[row + 1] - push_ptr[row]);
     }
   }
@@ -320,21 +434,64 @@ __global__ void normalize_mass_kernel(const float* __restrict__ y, const float* 
 // norm_sp_3d (src/model_mmDRUM_kernel_sp.py:39-52) column sums, bit-exact: one thread per
 // column adds the column top to bottom in fp32 (the reference's index_put_ order), then
 // clamps at 1e-7.
-__global__ void sequential_colsum_kernel(const float* __restrict__ y, ProofDims q, float* __restrict__ d) {
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < q.BLP;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    int64_t e = 0;
-    for (; e + 8 <= q.E; e += 8) {
-      float v[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = y[(e + k) * q.BLP + c];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
-    }
-    for (; e < q.E; ++e) s = __fadd_rn(s, y[e * q.BLP + c]);
-    d[c] = fmaxf(s, 1e-7f);
+// A block owns 32 columns.  Warp 1 stages 128-row tiles of those columns into shared memory
+// with TMA bulk copies (one 128-byte copy per row, completed on an mbarrier,
+// double-buffered); warp 0 waits for a tile and adds it row by row, one lane per column,
+// so the fp32 order stays strictly top to bottom.  Waits are bounded: a wait that gives up
+// sets MKG_DEV_TIMEOUT and the kernel runs on to its end.
+constexpr int kColsumRows = 128;
+constexpr uint32_t kWaitPolls = 1u << 22;
+
+__global__ void __launch_bounds__(64) sequential_colsum_kernel(const float* __restrict__ y, ProofDims q,
+                                                               float* __restrict__ d, unsigned* err) {
+  __shared__ __align__(128) float buf[2][kColsumRows][32];
+  __shared__ __align__(8) uint64_t bar[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c0 = (int64_t)blockIdx.x * 32;
+  const int ncols = (int)((q.BLP - c0) < 32 ? (q.BLP - c0) : 32);  // a multiple of 4
+  const uint32_t row_bytes = 4u * ncols;                           // a multiple of 16
+  const int64_t ntiles = (q.E + kColsumRows - 1) / kColsumRows;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_init_fence();
   }
+  __syncthreads();
+  auto issue = [&](int64_t t) {  // warp 1
+    const int slot = (int)(t & 1);
+    const int64_t r0 = t * kColsumRows;
+    const int nrows = (int)((q.E - r0) < kColsumRows ? (q.E - r0) : kColsumRows);
+    if (lane == 0) mbar_expect_tx(&bar[slot], (uint32_t)nrows * row_bytes);
+    __syncwarp();
+    fence_proxy_async_smem();
+    for (int r = lane; r < nrows; r += 32)
+      bulk_copy_g2s(&buf[slot][r][0], y + (r0 + r) * q.BLP + c0, row_bytes, &bar[slot]);
+  };
+  if (warp == 1) issue(0);
+  float s = 0.0f;
+  for (int64_t t = 0; t < ntiles; ++t) {
+    if (warp == 1) {
+      if (t + 1 < ntiles) issue(t + 1);
+    } else {
+      const int slot = (int)(t & 1);
+      if (!mbar_wait_bounded(&bar[slot], (uint32_t)((t >> 1) & 1), kWaitPolls)) {
+        if (lane == 0) raise_flag(err, MKG_DEV_TIMEOUT);
+      }
+      const int64_t left = q.E - t * kColsumRows;
+      const int rows = left < kColsumRows ? (int)left : kColsumRows;
+      int r = 0;
+      for (; r + 8 <= rows; r += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = buf[slot][r + k][lane];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+      }
+      for (; r < rows; ++r) s = __fadd_rn(s, buf[slot][r][lane]);
+    }
+    __syncthreads();  // the slot read in this round is refilled in the next one
+  }
+  if (warp == 0 && lane < ncols) d[c0 + lane] = fmaxf(s, 1e-7f);
 }
 
 __global__ void normalize_plain_kernel(const float* __restrict__ y, const float* __restrict__ d, ProofDims q,
@@ -408,27 +565,49 @@ __global__ void rows_to_queries_kernel(const float* __restrict__ x, const float*
 // ------------------------------------------------------------------ backward
 // Seed: dX_K[e][c] = G[b][e] where X_K[e][c] != 0 (the reference's sparse result carries
 // gradient only on its keys), and S[c] = sum_e dX_K[e][c] * Y_{K-1}[e][c].
+constexpr int kSeedTiles = 8;   // 32-entity tiles per block of seed_grad_kernel
+constexpr int kSeedMaxL = 16;   // rules whose column partials fit the block's shared memory
+
 __global__ void seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
                                  const float* __restrict__ ylast, ProofDims q, float* __restrict__ dx,
                                  float* __restrict__ s) {
   __shared__ float tile[32][33];
-  const int64_t e0 = blockIdx.x * 32, b0 = blockIdx.y * 32;
+  __shared__ float part[32 * kSeedMaxL];  // this block's share of S for its 32 queries
+  const int64_t b0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
-  for (int r = ty; r < 32; r += 8) {
-    const int64_t b = b0 + r, e = e0 + tx;
-    tile[r][tx] = (b < q.B && e < q.E) ? g[b * q.E + e] : 0.0f;
-  }
+  const bool local = q.L <= kSeedMaxL;
+  for (int i = ty * 32 + tx; i < 32 * kSeedMaxL; i += 256) part[i] = 0.0f;
   __syncthreads();
-  for (int r = ty; r < 32; r += 8) {
-    const int64_t e = e0 + r, b = b0 + tx;
-    if (e >= q.E || b >= q.B) continue;
-    const float gv = tile[tx][r];
-    for (int64_t l = 0; l < q.L; ++l) {
-      const int64_t c = b * q.L + l;
-      const float xv = xk[e * q.BLP + c];
-      const float dv = xv != 0.0f ? gv : 0.0f;
-      dx[e * q.BLP + c] = dv;
-      if (dv != 0.0f) atomicAdd(s + c, dv * ylast[e * q.BLP + c]);
+  for (int t = 0; t < kSeedTiles; ++t) {
+    const int64_t e0 = ((int64_t)blockIdx.x * kSeedTiles + t) * 32;
+    if (e0 >= q.E) break;
+    for (int r = ty; r < 32; r += 8) {
+      const int64_t b = b0 + r, e = e0 + tx;
+      tile[r][tx] = (b < q.B && e < q.E) ? g[b * q.E + e] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+      const int64_t e = e0 + r, b = b0 + tx;
+      if (e >= q.E || b >= q.B) continue;
+      const float gv = tile[tx][r];
+      for (int64_t l = 0; l < q.L; ++l) {
+        const int64_t c = b * q.L + l;
+        const float xv = xk[e * q.BLP + c];
+        const float dv = xv != 0.0f ? gv : 0.0f;
+        dx[e * q.BLP + c] = dv;
+        if (dv != 0.0f) {
+          const float contrib = dv * ylast[e * q.BLP + c];
+          if (local) atomicAdd(part + tx * q.L + l, contrib);
+          else atomicAdd(s + c, contrib);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (local) {
+    for (int i = ty * 32 + tx; i < 32 * q.L; i += 256) {
+      const int64_t b = b0 + i / q.L;
+      if (b < q.B && part[i] != 0.0f) atomicAdd(s + b0 * q.L + i, part[i]);
     }
   }
 }
@@ -484,17 +663,44 @@ __device__ __forceinline__ float edge_grad_scale(const EdgeFactor& f, int64_t fa
   return f.scale * (1.0f - sg);
 }
 
+// Reduce-scatter of 8 per-lane partial sums: afterwards lane l holds, for edge
+// ((l >> 2) & 7), the sum of that edge's partials over all 32 lanes (9 shuffles).
+__device__ __forceinline__ float reduce_scatter8(const float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  float a[4], b[2];
+  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float send = h4 ? v[k] : v[k + 4];
+    const float keep = h4 ? v[k + 4] : v[k];
+    a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float send = h3 ? a[k] : a[k + 2];
+    const float keep = h3 ? a[k + 2] : a[k];
+    b[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float c = (h2 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h2 ? b[0] : b[1], 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
+}
+
 // Transposed hop over the push list (row = sending entity s, records = its messages):
-//   dX[s][c]   = [X[s][c] != 0] (dY[s][c] w[n-1][c] + sum (dY[d][c] m) w[ch][c])
-//   dW[ch][c] += (dY[d][c] m) X[s][c]           (shared-memory partial per block)
+//   dX[s][c]   = [X[s][c] != 0] (dY[s][c] w[n-1][c] + sum_ch w[ch][c] sum_{e in ch} dY[d_e][c] m_e)
+//   dW[ch][c] += X[s][c] sum_{e in ch} dY[d_e][c] m_e     (shared-memory partial per block)
 //   dEdge[f]  += (sum_c dY[d][c] X[s][c] w[ch][c]) m g(f)
-//   S_prev[c] += dX[s][c] Y_prev[s][c]           (for the next lower hop)
-__global__ void __launch_bounds__(kBwdWarps * 32) bwd_pull_kernel(
+//   S_prev[c] += dX[s][c] Y_prev[s][c]                   (for the next lower hop)
+// Records of a push row come grouped by channel, so dY * m is summed per channel run and
+// folded into dX and dW once per run.  Only records whose destination row holds a
+// non-zero Y_h value in this chunk are visited (dY_h is zero elsewhere).
+__global__ void __launch_bounds__(kBwdWarps * 32, 2) bwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
-    const float* __restrict__ dy, const float* __restrict__ yprev, float* __restrict__ dx,
-    float* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge, int64_t num_facts, EdgeFactor ef,
-    int32_t* __restrict__ queue, unsigned* err) {
+    const uint8_t* __restrict__ yact, const float* __restrict__ dy, const float* __restrict__ yprev,
+    float* __restrict__ dx, float* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge,
+    int64_t num_facts, EdgeFactor ef, int32_t* __restrict__ queue, unsigned* err) {
   extern __shared__ float smem[];
   float* ws = smem;                         // [n][128] rule weights
   float* dws = smem + q.n * kChunk;         // [n][128] their gradient (conflict-free: [ch][k][lane])
@@ -511,9 +717,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32) bwd_pull_kernel(
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   const float4* wsv = reinterpret_cast<const float4*>(ws);
   float4 spart = zero;
-  for (;;) {
-    const int t = next_task(queue + chunk, lane);
-    if (t >= ntasks) break;
+  TaskCursor cursor(queue + chunk * kQueueStride, ntasks);
+  int64_t t;
+  while (cursor.next(t)) {
     const int4 tk = tasks[t];
     const int64_t row = tk.x;
     const bool active = act[row * q.nch + chunk] != 0;
@@ -525,60 +731,82 @@ __global__ void __launch_bounds__(kBwdWarps * 32) bwd_pull_kernel(
         const float4 wi = wsv[(q.n - 1) * 32 + lane];
         gx = f4_mul(ds, wi);
         float* dwi = dws + (q.n - 1) * kChunk;
-        atomicAdd(dwi + 0 * 32 + lane, ds.x * xr.x);
-        atomicAdd(dwi + 1 * 32 + lane, ds.y * xr.y);
-        atomicAdd(dwi + 2 * 32 + lane, ds.z * xr.z);
-        atomicAdd(dwi + 3 * 32 + lane, ds.w * xr.w);
+        if (ds.x != 0.f) atomicAdd(dwi + 0 * 32 + lane, ds.x * xr.x);
+        if (ds.y != 0.f) atomicAdd(dwi + 1 * 32 + lane, ds.y * xr.y);
+        if (ds.z != 0.f) atomicAdd(dwi + 2 * 32 + lane, ds.z * xr.z);
+        if (ds.w != 0.f) atomicAdd(dwi + 3 * 32 + lane, ds.w * xr.w);
       }
+      float4 run = zero;  // sum of dY * m over the current channel run
+      int cur = -1;
+      auto flush = [&]() {
+        if (cur < 0) return;
+        const float4 wc = wsv[cur * 32 + lane];
+        gx.x = fmaf(run.x, wc.x, gx.x); gx.y = fmaf(run.y, wc.y, gx.y);
+        gx.z = fmaf(run.z, wc.z, gx.z); gx.w = fmaf(run.w, wc.w, gx.w);
+        float* dwc = dws + cur * kChunk;
+        if (run.x != 0.f) atomicAdd(dwc + 0 * 32 + lane, run.x * xr.x);
+        if (run.y != 0.f) atomicAdd(dwc + 1 * 32 + lane, run.y * xr.y);
+        if (run.z != 0.f) atomicAdd(dwc + 2 * 32 + lane, run.z * xr.z);
+        if (run.w != 0.f) atomicAdd(dwc + 3 * 32 + lane, run.w * xr.w);
+        run = zero;
+      };
       for (int base = tk.y; base < tk.z; base += 32) {
         const int cnt = min(32, tk.z - base);
         int4 rec = make_int4(0, 0, 0, 0);
-        if (lane < cnt) rec = reinterpret_cast<const int4*>(edges)[base + lane];
-        for (int j = 0; j < cnt; j += 4) {
-          int nb[4], ch[4], fa[4];
-          float m[4];
-          bool ok[4];
+        bool live = false;
+        if (lane < cnt) {
+          rec = reinterpret_cast<const int4*>(edges)[base + lane];
+          if (rec.x < 0 || rec.x >= q.E || rec.y < 0 || rec.y >= q.n - 1) raise_flag(err, MKG_DEV_BAD_COL);
+          else live = yact[(int64_t)rec.x * q.nch + chunk] != 0;  // dY is zero where Y is
+        }
+        unsigned pending = __ballot_sync(0xffffffffu, live);
+        while (pending) {
+          int nb[kBatch], ch[kBatch], fa[kBatch];
+          float m[kBatch];
+          bool ok[kBatch];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int jj = (j + u) & 31;
+          for (int u = 0; u < kBatch; ++u) {
+            ok[u] = pending != 0;
+            const int jj = ok[u] ? __ffs(pending) - 1 : 0;
+            pending &= pending - 1;
             nb[u] = __shfl_sync(0xffffffffu, rec.x, jj);
             ch[u] = __shfl_sync(0xffffffffu, rec.y, jj);
             fa[u] = __shfl_sync(0xffffffffu, rec.z, jj);
             m[u] = __int_as_float(__shfl_sync(0xffffffffu, rec.w, jj));
-            ok[u] = (j + u) < cnt;
-            if (ok[u] && (nb[u] < 0 || nb[u] >= q.E || ch[u] < 0 || ch[u] >= q.n - 1)) {
-              if (lane == 0) raise_flag(err, MKG_DEV_BAD_COL);
-              ok[u] = false;
+          }
+          float4 gv[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u)
+            gv[u] = (ok[u] && colok) ? *reinterpret_cast<const float4*>(dy + (int64_t)nb[u] * q.BLP + col) : zero;
+          float ep[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            ep[u] = 0.0f;
+            if (!ok[u]) continue;
+            if (ch[u] != cur) { flush(); cur = ch[u]; }
+            run.x = fmaf(gv[u].x, m[u], run.x); run.y = fmaf(gv[u].y, m[u], run.y);
+            run.z = fmaf(gv[u].z, m[u], run.z); run.w = fmaf(gv[u].w, m[u], run.w);
+            if (grad_edge != nullptr) {
+              const float4 wv = wsv[ch[u] * 32 + lane];
+              ep[u] = gv[u].x * xr.x * wv.x + gv[u].y * xr.y * wv.y + gv[u].z * xr.z * wv.z + gv[u].w * xr.w * wv.w;
             }
           }
-          float4 gv[4];
+          if (grad_edge != nullptr) {
+            const float tot = reduce_scatter8(ep);
+            const int idx = (lane >> 2) & 7;
+            int f = -1;
+            float mm = 0.0f;
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            gv[u] = (ok[u] && colok) ? *reinterpret_cast<const float4*>(dy + (int64_t)nb[u] * q.BLP + col) : zero;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (!ok[u]) continue;
-            const float4 wv = wsv[ch[u] * 32 + lane];
-            const float4 gm = make_float4(gv[u].x * m[u], gv[u].y * m[u], gv[u].z * m[u], gv[u].w * m[u]);
-            gx.x = fmaf(gm.x, wv.x, gx.x); gx.y = fmaf(gm.y, wv.y, gx.y);
-            gx.z = fmaf(gm.z, wv.z, gx.z); gx.w = fmaf(gm.w, wv.w, gx.w);
-            float* dwc = dws + ch[u] * kChunk;
-            if (gm.x != 0.f) atomicAdd(dwc + 0 * 32 + lane, gm.x * xr.x);
-            if (gm.y != 0.f) atomicAdd(dwc + 1 * 32 + lane, gm.y * xr.y);
-            if (gm.z != 0.f) atomicAdd(dwc + 2 * 32 + lane, gm.z * xr.z);
-            if (gm.w != 0.f) atomicAdd(dwc + 3 * 32 + lane, gm.w * xr.w);
-            if (grad_edge != nullptr) {
-              float dot = gv[u].x * xr.x * wv.x + gv[u].y * xr.y * wv.y + gv[u].z * xr.z * wv.z +
-                          gv[u].w * xr.w * wv.w;
-              dot = warp_sum(dot);
-              if (lane == 0 && dot != 0.0f) {
-                if (fa[u] >= 0 && fa[u] < num_facts) atomicAdd(grad_edge + fa[u], dot * m[u] * edge_grad_scale(ef, fa[u]));
-                else raise_flag(err, MKG_DEV_BAD_FACT);
-              }
+            for (int u = 0; u < kBatch; ++u)
+              if (idx == u && ok[u]) { f = fa[u]; mm = m[u]; }
+            if ((lane & 3) == 0 && f >= 0 && tot != 0.0f) {
+              if (f < num_facts) atomicAdd(grad_edge + f, tot * mm * edge_grad_scale(ef, f));
+              else raise_flag(err, MKG_DEV_BAD_FACT);
             }
           }
         }
       }
+      flush();
       // only present entries of X carry a gradient
       gx.x = xr.x != 0.f ? gx.x : 0.f; gx.y = xr.y != 0.f ? gx.y : 0.f;
       gx.z = xr.z != 0.f ? gx.z : 0.f; gx.w = xr.w != 0.f ? gx.w : 0.f;
@@ -729,6 +957,17 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __
 size_t fwd_smem(const ProofDims& q) { return 4 * ((size_t)q.n * kChunk + kChunk); }
 size_t bwd_smem(const ProofDims& q) { return 4 * (2 * (size_t)q.n * kChunk + kChunk); }
 
+// Columns per lane of the forward pull: 8 (two float4) for batches wider than 128
+// columns; MKG_FWD_VEC=1|2 overrides (a tuning knob).
+int fwd_vec_knob(const ProofDims& q) {
+  static int forced = [] {
+    const char* v = getenv("MKG_FWD_VEC");
+    return v ? atoi(v) : 0;
+  }();
+  if (forced == 1 || forced == 2) return forced;
+  return q.BLP > kChunk ? 2 : 1;
+}
+
 int check_proof(const mkg_graph* g, const mkg_adjacency* adj, const mkg_proof_params* p) {
   MKG_REQUIRE(g && adj && p, "proof: null argument");
   MKG_REQUIRE(p->B >= 1 && p->L >= 1 && p->hops >= 1 && p->R >= 1, "proof: B, L, R, hops must be positive");
@@ -772,39 +1011,43 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
   MKG_CUDA(cudaMemsetAsync(S.x(0), 0, slab, st));
   MKG_CUDA(cudaMemsetAsync(S.act(0), 0, (size_t)q.E * q.nch, st));
   MKG_CUDA(cudaMemsetAsync(S.d(0), 0, 4 * (size_t)q.hops * q.BLP, st));
-  MKG_CUDA(cudaMemsetAsync(S.queue(), 0, 4 * (size_t)(q.hops * q.nch), st));
+  MKG_CUDA(cudaMemsetAsync(S.queue(), 0, 4 * (size_t)(q.hops * q.nch * kQueueStride), st));
   MKG_CUDA(cudaMemsetAsync(S.msgs(), 0, 8 * (size_t)(q.hops + 1), st));
   init_state_kernel<<<grid_for(q.BL, 256, pb), 256, 0, st>>>(heads, q, S.x(0), S.act(0), adj->push_ptr, S.msgs(), err);
   MKG_LAUNCHED("init_state_kernel");
-  const size_t sm = fwd_smem(q);
-  rc = max_mode ? set_smem((const void*)fwd_pull_kernel<true>, sm) : set_smem((const void*)fwd_pull_kernel<false>, sm);
-  if (rc) return rc;
+  // 256-column chunks (8 columns per lane) when the batch is wide enough
+  const int vec = fwd_vec_knob(q);
+  const int64_t nfch = (q.BLP + 128 * vec - 1) / (128 * vec);
+  const void* fwd_fn = max_mode ? (vec == 2 ? (const void*)fwd_pull_kernel<true, 2> : (const void*)fwd_pull_kernel<true, 1>)
+                                : (vec == 2 ? (const void*)fwd_pull_kernel<false, 2> : (const void*)fwd_pull_kernel<false, 1>);
   int resident = 0;
-  if (max_mode)
-    MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fwd_pull_kernel<true>, kFwdWarps * 32, sm));
-  else
-    MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fwd_pull_kernel<false>, kFwdWarps * 32, sm));
+  MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fwd_fn, kFwdWarps * 32, 0));
   // one wave of resident blocks, split evenly over the column chunks
   const int blocks_per_chunk = grid_for(adj->num_pull_tasks, kFwdWarps,
-                                        (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / q.nch) + 1);
+                                        (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / nfch) + 1);
   for (int64_t h = 0; h < q.hops; ++h) {
     float* y = S.y(h);
     zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, q, y);
     MKG_LAUNCHED("zero_partial_rows_kernel");
-    dim3 grid(blocks_per_chunk, (unsigned)q.nch);
+    dim3 grid(blocks_per_chunk, (unsigned)nfch);
     if (p->fwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->fwd_events[2 * h]), st));
-    if (max_mode)
-      fwd_pull_kernel<true><<<grid, kFwdWarps * 32, sm, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, adj->pull, q,
-                                                              S.wt(h), S.x(h), S.act(h), y, nullptr,
-                                                              S.queue() + h * q.nch, err);
-    else
-      fwd_pull_kernel<false><<<grid, kFwdWarps * 32, sm, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, adj->pull, q,
-                                                               S.wt(h), S.x(h), S.act(h), y, S.d(h),
-                                                               S.queue() + h * q.nch, err);
+    {
+      const int4* tk = reinterpret_cast<const int4*>(adj->pull_tasks);
+      const int64_t nt = adj->num_pull_tasks;
+      float* ds = max_mode ? nullptr : S.d(h);
+      if (max_mode && vec == 2)
+        fwd_pull_kernel<true, 2><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
+      else if (max_mode)
+        fwd_pull_kernel<true, 1><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
+      else if (vec == 2)
+        fwd_pull_kernel<false, 2><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
+      else
+        fwd_pull_kernel<false, 1><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
+    }
     MKG_LAUNCHED("fwd_pull_kernel");
     if (p->fwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->fwd_events[2 * h + 1]), st));
     if (max_mode) {
-      sequential_colsum_kernel<<<grid_for(q.BLP, 128, pb), 128, 0, st>>>(y, q, S.d(h));
+      sequential_colsum_kernel<<<(unsigned)((q.BLP + 31) / 32), 64, 0, st>>>(y, q, S.d(h), err);
       MKG_LAUNCHED("sequential_colsum_kernel");
       if (h + 1 < q.hops) {
         normalize_plain_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, S.x(h + 1), S.act(h + 1), adj->push_ptr,
@@ -813,7 +1056,7 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
       }
     } else {
       normalize_mass_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, p->state_threshold, S.x(h + 1), S.act(h + 1),
-                                                adj->push_ptr, S.msgs() + h + 1);
+                                                S.yact(h), adj->push_ptr, S.msgs() + h + 1);
       MKG_LAUNCHED("normalize_mass_kernel");
     }
   }
@@ -848,13 +1091,13 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
   EdgeFactor f = make_factor(*ef);
   if (grad_edge) MKG_CUDA(cudaMemsetAsync(grad_edge, 0, 4 * (size_t)g->num_facts, st));
   MKG_CUDA(cudaMemsetAsync(S.s(0), 0, 4 * (size_t)q.hops * q.BLP, st));
-  MKG_CUDA(cudaMemsetAsync(S.queue() + q.hops * q.nch, 0, 4 * (size_t)(q.hops * q.nch), st));
+  MKG_CUDA(cudaMemsetAsync(S.queue() + q.hops * q.nch * kQueueStride, 0, 4 * (size_t)(q.hops * q.nch * kQueueStride), st));
   float* dx_cur = S.dxa();
   float* dx_next = S.dxb();
   zero_pad_columns_kernel<<<pb, 256, 0, st>>>(dx_cur, q);
   MKG_LAUNCHED("zero_pad_columns_kernel");
-  dim3 tgrid((unsigned)((q.E + 31) / 32), (unsigned)((q.B + 31) / 32));
-  seed_grad_kernel<<<tgrid, dim3(32, 8), 0, st>>>(grad_out, S.x(q.hops), S.y(q.hops - 1), q, dx_cur, S.s(q.hops - 1));
+  dim3 sgrid((unsigned)((q.E + 32 * kSeedTiles - 1) / (32 * kSeedTiles)), (unsigned)((q.B + 31) / 32));
+  seed_grad_kernel<<<sgrid, dim3(32, 8), 0, st>>>(grad_out, S.x(q.hops), S.y(q.hops - 1), q, dx_cur, S.s(q.hops - 1));
   MKG_LAUNCHED("seed_grad_kernel");
   const size_t sm = bwd_smem(q);
   rc = set_smem((const void*)bwd_pull_kernel, sm);
@@ -875,9 +1118,9 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
     dim3 grid(blocks_per_chunk, (unsigned)q.nch);
     if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h]), st));
     bwd_pull_kernel<<<grid, kBwdWarps * 32, sm, st>>>(
-        reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.dy(),
+        reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.yact(h), S.dy(),
         h > 0 ? S.y(h - 1) : nullptr, dx_next, S.dwt(), h > 0 ? S.s(h - 1) : nullptr, grad_edge, g->num_facts, f,
-        S.queue() + (q.hops + h) * q.nch, err);
+        S.queue() + (q.hops + h) * q.nch * kQueueStride, err);
     MKG_LAUNCHED("bwd_pull_kernel");
     if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h + 1]), st));
     untranspose_dw_kernel<<<grid_for(q.BL * q.n, 256, pb), 256, 0, st>>>(S.dwt(), q, h, grad_w_hops);
