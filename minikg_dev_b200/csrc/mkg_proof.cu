@@ -141,12 +141,6 @@ __global__ void zero_partial_rows_kernel(const int4* __restrict__ tasks, int64_t
   }
 }
 
-__device__ __forceinline__ void f4_fma(float4& acc, const float4& a, const float4& b, float m) {
-  acc.x = fmaf(a.x * b.x, m, acc.x);
-  acc.y = fmaf(a.y * b.y, m, acc.y);
-  acc.z = fmaf(a.z * b.z, m, acc.z);
-  acc.w = fmaf(a.w * b.w, m, acc.w);
-}
 __device__ __forceinline__ float4 f4_mul(const float4& a, const float4& b) {
   return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
 }
@@ -156,9 +150,6 @@ __device__ __forceinline__ void f4_max_msg(float4& acc, const float4& x, const f
   acc.y = fmaxf(acc.y, (x.y * w.y) * m);
   acc.z = fmaxf(acc.z, (x.z * w.z) * m);
   acc.w = fmaxf(acc.w, (x.w * w.w) * m);
-}
-__device__ __forceinline__ bool f4_any(const float4& v) {
-  return v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f;
 }
 __device__ __forceinline__ int f4_count(const float4& v) {
   return (v.x != 0.f) + (v.y != 0.f) + (v.z != 0.f) + (v.w != 0.f);
@@ -177,7 +168,6 @@ __device__ __forceinline__ void stage_weights(const float* __restrict__ wt, cons
 // Dynamic task queue: a warp takes kGrab consecutive tasks per atomic and requests the
 // next group as soon as it starts one, so the atomic's latency overlaps the work.  Each
 // counter sits on its own 128-byte line (kQueueStride ints apart).
-
 struct TaskCursor {
   int32_t* counter;
   int64_t ntasks;
@@ -954,7 +944,6 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __
   if (threadIdx.x == 0) counts[b] = m;
 }
 
-size_t fwd_smem(const ProofDims& q) { return 4 * ((size_t)q.n * kChunk + kChunk); }
 size_t bwd_smem(const ProofDims& q) { return 4 * (2 * (size_t)q.n * kChunk + kChunk); }
 
 // Columns per lane of the forward pull: 8 (two float4) for batches wider than 128
