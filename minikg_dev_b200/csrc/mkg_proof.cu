@@ -12,6 +12,9 @@
 // rows never serialise one warp.  Warps take tasks from a queue; each block works on one
 // 128-column chunk and keeps the chunk of the rule weights (and, backward, of their
 // gradient) in shared memory.  The backward is the same walk over the push list.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cub/cub.cuh>
 
 #include "mkg_common.cuh"
@@ -424,47 +427,65 @@ __global__ void normalize_mass_kernel(const float* __restrict__ y, const float* 
 // norm_sp_3d (src/model_mmDRUM_kernel_sp.py:39-52) column sums, bit-exact: one thread per
 // column adds the column top to bottom in fp32 (the reference's index_put_ order), then
 // clamps at 1e-7.
-// A block owns 32 columns.  Warp 1 stages 128-row tiles of those columns into shared memory
-// with TMA bulk copies (one 128-byte copy per row, completed on an mbarrier,
-// double-buffered); warp 0 waits for a tile and adds it row by row, one lane per column,
-// so the fp32 order stays strictly top to bottom.  Waits are bounded: a wait that gives up
-// sets MKG_DEV_TIMEOUT and the kernel runs on to its end.
-constexpr int kColsumRows = 128;
+// A block owns 32 columns.  Lane 0 of warp 1 streams 64-row x 32-column tiles of Y into a
+// ring of kColsumStages shared-memory slots with 2D TMA tensor copies (one instruction per
+// 8 KB tile, each completing a "full" mbarrier); warp 0 waits for each tile in order, adds
+// it row by row (one lane per column, so the fp32 order stays strictly top to bottom) and
+// frees the slot on its "empty" mbarrier.  Every wait is bounded: one that gives up sets
+// MKG_DEV_TIMEOUT and the kernel runs on to its end.
+constexpr int kColsumRows = 64;
+constexpr int kColsumStages = 5;  // 5 x 8 KB ring (static shared memory stays under 48 KB)
 constexpr uint32_t kWaitPolls = 1u << 22;
 
-__global__ void __launch_bounds__(64) sequential_colsum_kernel(const float* __restrict__ y, ProofDims q,
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 2D tiled TMA load of box (x = column, y = row) of `map` into shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__global__ void __launch_bounds__(64) sequential_colsum_kernel(const __grid_constant__ CUtensorMap ymap, ProofDims q,
                                                                float* __restrict__ d, unsigned* err) {
-  __shared__ __align__(128) float buf[2][kColsumRows][32];
-  __shared__ __align__(8) uint64_t bar[2];
+  __shared__ __align__(128) float buf[kColsumStages][kColsumRows][32];
+  __shared__ __align__(8) uint64_t full[kColsumStages];
+  __shared__ __align__(8) uint64_t empty[kColsumStages];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t c0 = (int64_t)blockIdx.x * 32;
-  const int ncols = (int)((q.BLP - c0) < 32 ? (q.BLP - c0) : 32);  // a multiple of 4
-  const uint32_t row_bytes = 4u * ncols;                           // a multiple of 16
+  const int ncols = (int)((q.BLP - c0) < 32 ? (q.BLP - c0) : 32);
   const int64_t ntiles = (q.E + kColsumRows - 1) / kColsumRows;
+  constexpr uint32_t kTileBytes = kColsumRows * 32 * 4;  // out-of-range rows / columns arrive as zeros
   if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int k = 0; k < kColsumStages; ++k) {
+      mbar_init(&full[k], 1);
+      mbar_init(&empty[k], 1);
+    }
     mbar_init_fence();
   }
   __syncthreads();
-  auto issue = [&](int64_t t) {  // warp 1
-    const int slot = (int)(t & 1);
-    const int64_t r0 = t * kColsumRows;
-    const int nrows = (int)((q.E - r0) < kColsumRows ? (q.E - r0) : kColsumRows);
-    if (lane == 0) mbar_expect_tx(&bar[slot], (uint32_t)nrows * row_bytes);
-    __syncwarp();
-    fence_proxy_async_smem();
-    for (int r = lane; r < nrows; r += 32)
-      bulk_copy_g2s(&buf[slot][r][0], y + (r0 + r) * q.BLP + c0, row_bytes, &bar[slot]);
-  };
-  if (warp == 1) issue(0);
-  float s = 0.0f;
-  for (int64_t t = 0; t < ntiles; ++t) {
-    if (warp == 1) {
-      if (t + 1 < ntiles) issue(t + 1);
-    } else {
-      const int slot = (int)(t & 1);
-      if (!mbar_wait_bounded(&bar[slot], (uint32_t)((t >> 1) & 1), kWaitPolls)) {
+  if (warp == 1) {  // producer
+    if (lane == 0) {
+      for (int64_t t = 0; t < ntiles; ++t) {
+        const int slot = (int)(t % kColsumStages);
+        const int64_t round = t / kColsumStages;
+        if (round > 0) {
+          if (!mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1), kWaitPolls)) raise_flag(err, MKG_DEV_TIMEOUT);
+          fence_proxy_async_smem();
+        }
+        mbar_expect_tx(&full[slot], kTileBytes);
+        tma_load_2d(&buf[slot][0][0], &ymap, (int32_t)c0, (int32_t)(t * kColsumRows), &full[slot]);
+      }
+    }
+  } else {  // consumer
+    float s = 0.0f;
+    for (int64_t t = 0; t < ntiles; ++t) {
+      const int slot = (int)(t % kColsumStages);
+      const int64_t round = t / kColsumStages;
+      if (!mbar_wait_bounded(&full[slot], (uint32_t)(round & 1), kWaitPolls)) {
         if (lane == 0) raise_flag(err, MKG_DEV_TIMEOUT);
       }
       const int64_t left = q.E - t * kColsumRows;
@@ -478,10 +499,34 @@ __global__ void __launch_bounds__(64) sequential_colsum_kernel(const float* __re
         for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
       }
       for (; r < rows; ++r) s = __fadd_rn(s, buf[slot][r][lane]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    __syncthreads();  // the slot read in this round is refilled in the next one
+    if (lane < ncols) d[c0 + lane] = fmaxf(s, 1e-7f);
   }
-  if (warp == 0 && lane < ncols) d[c0 + lane] = fmaxf(s, 1e-7f);
+}
+
+// Tensor map of a row-major [rows][cols] fp32 matrix with a 64 x 32 box (cols is a multiple
+// of 4, so every row stride and box start is 16-byte aligned).
+int make_rows_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) != cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }();
+  if (encode == nullptr) { set_error("cuTensorMapEncodeTiled is unavailable"); return MKG_ERR_CUDA; }
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+  const cuuint32_t box[2] = {32, kColsumRows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled failed (%d)", (int)r); return MKG_ERR_CUDA; }
+  return MKG_OK;
 }
 
 __global__ void normalize_plain_kernel(const float* __restrict__ y, const float* __restrict__ d, ProofDims q,
@@ -1036,7 +1081,10 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
     MKG_LAUNCHED("fwd_pull_kernel");
     if (p->fwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->fwd_events[2 * h + 1]), st));
     if (max_mode) {
-      sequential_colsum_kernel<<<(unsigned)((q.BLP + 31) / 32), 64, 0, st>>>(y, q, S.d(h), err);
+      CUtensorMap ymap;
+      rc = make_rows_map(&ymap, y, q.E, q.BLP);
+      if (rc) return rc;
+      sequential_colsum_kernel<<<(unsigned)((q.BLP + 31) / 32), 64, 0, st>>>(ymap, q, S.d(h), err);
       MKG_LAUNCHED("sequential_colsum_kernel");
       if (h + 1 < q.hops) {
         normalize_plain_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, S.x(h + 1), S.act(h + 1), adj->push_ptr,
