@@ -692,3 +692,49 @@ def count_messages(state, csr, w, L, E, R, cap=UNCAPPED):
                                     off, cap)
         total += int(take.sum())
     return total
+
+
+# ----------------------------------------------------------------------------
+# query planning (decode_core.py:287-348, tnb_batching.py:12-20)
+# ----------------------------------------------------------------------------
+
+def tnb_batch_plan(dataset: str, nominal_batch_size: int):
+    """(true_target_batch_size, false_main_batch_count) (tnb_batching.py:12-20)."""
+    nominal = max(1, int(nominal_batch_size))
+    false_count = 0 if dataset == "family" else min(nominal - 1, int(round(nominal * 0.5)))
+    return max(1, nominal - false_count), false_count
+
+
+def rule_first_hop_channels(logits, tau, threshold):
+    """Channels c with max_l softmax(logits[0, l, :] / tau)[c] >= threshold (decode_core.py:302-307).
+
+    ``logits`` [K, L, n] float32 for one relation; the softmax is taken in float64 and
+    rounded to float32 (the reference's float32 softmax agrees to an ulp)."""
+    z = np.asarray(logits[0], np.float64) / np.float64(np.float32(tau))
+    z = z - z.max(axis=-1, keepdims=True)
+    w = np.exp(z)
+    w = (w / w.sum(axis=-1, keepdims=True)).astype(np.float32)
+    return np.nonzero(w.max(axis=0) >= np.float32(threshold))[0].astype(np.int64)
+
+
+def rule_first_hop_cache(head, rel, tail, supply, wanted, R):
+    """channel -> sorted unique endpoints of the supplied facts (decode_core.py:308-331):
+    heads of relation c under channel c, tails under channel c + R, for each wanted c."""
+    head, rel, tail = (np.asarray(a, np.int64) for a in (head, rel, tail))
+    supply = np.asarray(supply, bool)
+    cache = {}
+    for c in sorted(set(int(x) for x in wanted)):
+        sel = supply & (rel == c)
+        cache[c] = np.unique(head[sel])
+        cache[c + R] = np.unique(tail[sel])
+    return cache
+
+
+def rule_first_hop_query_heads(channels, cache, query_heads):
+    """Query heads (in order, duplicates kept) in the union of the channels' sets
+    (decode_core.py:334-347); [] when no channel has a set."""
+    sets = [cache[int(c)] for c in channels if int(c) in cache]
+    if not sets:
+        return np.zeros(0, np.int64)
+    q = np.asarray(query_heads, np.int64)
+    return q[np.isin(q, np.concatenate(sets))]

@@ -346,13 +346,60 @@ def reducer_case(ref, out, rng):
     out["ord_tails"] = ot; out["ord_scores"] = os_
 
 
+def prune_case(ref, out, kg, rng):
+    """First-hop query pruning (decode_core.py:287-348) with a per-relation fake rule model."""
+    R, E = kg.num_relations, kg.num_entities
+    n = 2 * R + 1
+    K, L = 2, 3
+    logits = (rng.standard_normal((R, K, L, n)) * 2.5).astype(np.float32)
+    logits[3] = 0.0                      # flat weights: no channel reaches the threshold
+    logits[4] = 0.0
+    logits[4, 0, :, 2 * R] = 20.0        # only the identity channel is active
+    model = SimpleNamespace(relation_count=R, tau_1=0.8, emb=torch.zeros(1))
+    model.build_rule_logits = lambda rels: torch.from_numpy(logits[int(rels[0])][None])
+    facts = np.stack([kg.head, kg.rel, kg.tail], 1).astype(np.int64)
+    supply = rng.random(kg.num_triples) < 0.8
+    relations = [0, 1, 3, 4, 5, R - 1]
+    args = SimpleNamespace(decode_query_prune="rule_first_hop", decode_query_rule_threshold=0.2)
+    ref.decode_core.prepare_rule_first_hop_prune(model, relations, facts, supply, args)
+    act, act_off, qs, q_off, kept, kept_off = [], [0], [], [0], [], [0]
+    for r in relations:
+        a = list(args._decode_query_active_channels[r])
+        q = rng.integers(0, E, 300).astype(np.int64)
+        k = ref.decode_core.rule_first_hop_query_heads(r, q.tolist(), args)
+        act += a; act_off.append(len(act))
+        qs.append(q); q_off.append(q_off[-1] + q.size)
+        kept += k; kept_off.append(len(kept))
+    cache = args._decode_query_channel_heads
+    keys = sorted(cache)
+    out.update(pf_logits=logits, pf_tau=np.array([0.8], np.float32), pf_threshold=np.array([0.2], np.float32),
+               pf_head=kg.head, pf_rel=kg.rel, pf_tail=kg.tail, pf_E=np.array([E]), pf_R=np.array([R]),
+               pf_supply=supply, pf_relations=np.array(relations, np.int64),
+               pf_active=np.array(act, np.int64), pf_active_off=np.array(act_off, np.int64),
+               pf_queries=np.concatenate(qs), pf_queries_off=np.array(q_off, np.int64),
+               pf_kept=np.array(kept, np.int64), pf_kept_off=np.array(kept_off, np.int64),
+               pf_cache_keys=np.array(keys, np.int64),
+               pf_cache=np.concatenate([cache[c] for c in keys]) if keys else np.zeros(0, np.int64),
+               pf_cache_off=np.cumsum([0] + [cache[c].size for c in keys]).astype(np.int64))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--only", choices=("all", "prune"), default="all")
     a = ap.parse_args()
     torch.set_num_threads(1)  # index_put_/scatter_add_ are then sequential in index order
     ref = import_reference(a.ref)
+    if a.only in ("all", "prune"):
+        kg = sample_graph(900, 9, 9000, (("rel", ("zipf", 1.0)), ("head", (0.9, 2.0)), ("tail", (0.9, 2.0)),
+                                         ("hubs", (0.05, 0.4))), seed=12, name="g2")
+        pf = {}
+        prune_case(ref, pf, kg, np.random.default_rng(7))
+        np.savez_compressed(os.path.join(a.out, "golden_prune.npz"), **pf)
+        print("wrote prune", len(pf))
+        if a.only == "prune":
+            return
     rng = np.random.default_rng(0)
 
     graphs = {
