@@ -185,6 +185,13 @@ typedef struct mkg_hop_params {
   int32_t wot_i;       /* 1: identity channel contributes zeros */
   int32_t agg_mode;    /* 0 sum, 1 max with argmax */
   int64_t topk_edges;  /* per-entry edge cap; >= 2^60 means uncapped */
+  /* Destination range [dst_lo, dst_hi): only messages whose destination entity (the
+   * identity channel's is the entry itself) lies in it are produced, and the output key
+   * space is B x L x (dst_hi - dst_lo).  Caps are still decided on the whole CSR row, so
+   * the union over a partition of [0, E) equals the full-range output.  dst_hi <= dst_lo
+   * (e.g. both 0) means [0, E).  No counterpart in the reference (single GPU); used by the
+   * destination-partitioned multi-GPU hop.  agg_mode 1 backward needs the full range. */
+  int64_t dst_lo, dst_hi;
 } mkg_hop_params;
 
 /* Forward of one hop, coalesced: replaces fastlog_forward_sparse3d_topk_cuda

@@ -61,7 +61,7 @@ class Adjacency(C.Structure):
 
 class HopParams(C.Structure):
     _fields_ = [("B", i64), ("L", i64), ("E", i64), ("r_size", i64), ("n", i64), ("wot_i", i32),
-                ("agg_mode", i32), ("topk_edges", i64)]
+                ("agg_mode", i32), ("topk_edges", i64), ("dst_lo", i64), ("dst_hi", i64)]
 
 
 class ProofParams(C.Structure):

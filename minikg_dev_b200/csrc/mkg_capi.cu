@@ -38,7 +38,7 @@ using mkg::set_error;
 static cudaStream_t S(mkg_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 
 MKG_API const char* mkg_last_error(void) { return mkg::g_last_error; }
-MKG_API int mkg_abi_version(void) { return 1; }
+MKG_API int mkg_abi_version(void) { return 2; }
 
 MKG_API size_t mkg_csr_build_workspace_bytes(int64_t T, int64_t E, int64_t R) {
   return mkg::csr_build_workspace_bytes(T, E, R);

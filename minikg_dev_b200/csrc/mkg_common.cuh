@@ -142,7 +142,7 @@ inline DirCSR make_dir(const mkg_csr_dir& d) {
 }
 
 // ---------------------------------------------------------------- TMA bulk copies
-// One-dimensional bulk copies global -> shared completed on an mbarrier (no multicast).
+// One-dimensional bulk copies global -> shared completed on an mbarrier (this CTA only).
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

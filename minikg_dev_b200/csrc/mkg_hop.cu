@@ -37,9 +37,13 @@ size_t scan_bytes(int64_t nblk) {
 
 // Forward workspace: value slabs (sum: ori, inv, ind; max: ind), hit slabs, packed slabs
 // (max: ori, inv), class lists, per-tile counts and offsets for the three outputs.
+// Output entities: the destination range [lo, lo + extent) (the whole [0, E) by default).
+int64_t range_lo(const mkg_hop_params& p) { return p.dst_hi > p.dst_lo ? p.dst_lo : 0; }
+int64_t range_extent(const mkg_hop_params& p) { return p.dst_hi > p.dst_lo ? p.dst_hi - p.dst_lo : p.E; }
+
 HopLayout forward_layout(const mkg_hop_params& p, int64_t F) {
   HopLayout L{};
-  L.BLE = p.B * p.L * p.E;
+  L.BLE = p.B * p.L * range_extent(p);
   L.F = F;
   L.nblk = (L.BLE + kTile - 1) / kTile;
   const int nval = p.agg_mode == 1 ? 1 : 3;
@@ -64,14 +68,14 @@ HopLayout forward_layout(const mkg_hop_params& p, int64_t F) {
 // Backward workspace: gradient slabs (ori, inv, ind), class lists, the key -> entry map.
 HopLayout backward_layout(const mkg_hop_params& p, int64_t F) {
   HopLayout L{};
-  L.BLE = p.B * p.L * p.E;
+  L.BLE = p.B * p.L * range_extent(p);
   L.F = F;
   L.sval = a256(4 * (size_t)L.BLE) / 4;
   size_t o = 0;
   L.off_val = o; o += 4 * (size_t)L.sval * 3;
   L.off_lists = o; o += a256(4 * (size_t)(3 * F + 3));
   L.off_counts = o; o += a256(4 * 4);
-  L.off_map = o; o += p.agg_mode == 1 ? a256(4 * (size_t)L.BLE) : 0;
+  L.off_map = o; o += p.agg_mode == 1 ? a256(4 * (size_t)(p.B * p.L * p.E)) : 0;
   L.total = o;
   return L;
 }
@@ -86,6 +90,7 @@ struct Frontier {
 
 struct HopCtx {
   int64_t B, L, E, T, n, r_size, cap;
+  int64_t lo, Eo;  // destination range [lo, lo + Eo); output keys are (b * L + l) * Eo + (dst - lo)
   int wot_i;
   DirCSR dir[2];
   EdgeFactor factor;
@@ -110,6 +115,12 @@ struct MaxSink {
     atomicMax(pk[d] + key, pack_value_rank(v, static_cast<uint32_t>(fact)));
   }
 };
+
+// Output key of (b, l, dst), or -1 when dst lies outside the destination range.
+__device__ __forceinline__ int64_t out_key0(const HopCtx& c, int64_t b, int64_t l) { return (b * c.L + l) * c.Eo - c.lo; }
+__device__ __forceinline__ bool in_range(const HopCtx& c, int64_t e) {
+  return static_cast<uint64_t>(e - c.lo) < static_cast<uint64_t>(c.Eo);
+}
 
 // ------------------------------------------------------------------ entry classes
 __device__ __forceinline__ bool load_entry(const Frontier& f, const HopCtx& c, int64_t i, int64_t& b,
@@ -136,8 +147,8 @@ __global__ void classify_kernel(Frontier f, HopCtx c, int32_t* __restrict__ list
     if (i < f.F) {
       int64_t b, l, e;
       if (load_entry(f, c, i, b, l, e)) {
-        const int64_t key = (b * c.L + l) * c.E + e;
-        if (ind_val != nullptr) {
+        const int64_t key = out_key0(c, b, l) + e;
+        if (ind_val != nullptr && in_range(c, e)) {
           float v = c.wot_i ? 0.0f : f.v[i] * c.w[(b * c.L + l) * c.n + (c.n - 1)];
           atomicAdd(ind_val + key, v);
           ind_hit[key] = 1;
@@ -270,7 +281,9 @@ struct FwdVisit {
   float sv;
   int64_t key0;
   const EdgeFactor* f;
+  int64_t lo, Eo;
   __device__ __forceinline__ void operator()(int d, int64_t dst, int64_t /*ch*/, float wv, int64_t fact) {
+    if (static_cast<uint64_t>(dst - lo) >= static_cast<uint64_t>(Eo)) return;  // another shard's destination
     float m = (*f)(fact);
     sink.msg(d, key0 + dst, (sv * wv) * m, fact);
   }
@@ -286,7 +299,7 @@ __global__ void push_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) continue;
     const float* wrow = c.w + (b * c.L + l) * c.n;
-    FwdVisit<Sink> vis{sink, f.v[i], (b * c.L + l) * c.E, &c.factor};
+    FwdVisit<Sink> vis{sink, f.v[i], out_key0(c, b, l), &c.factor, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       for (int64_t p = p0; p < p1; ++p) visit_position(c, d, p, wrow, vis);
@@ -310,7 +323,7 @@ __global__ void __launch_bounds__(kMidWarps * 32) push_mid_kernel(Frontier f, Ho
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) continue;
     const float* wrow = c.w + (b * c.L + l) * c.n;
-    FwdVisit<Sink> vis{sink, f.v[i], (b * c.L + l) * c.E, &c.factor};
+    FwdVisit<Sink> vis{sink, f.v[i], out_key0(c, b, l), &c.factor, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       if (p1 - p0 <= c.cap) {
@@ -341,7 +354,7 @@ __global__ void __launch_bounds__(kHubThreads) push_hub_kernel(Frontier f, HopCt
       __syncthreads();
       wrow = wstage;
     }
-    FwdVisit<Sink> vis{sink, f.v[i], (b * c.L + l) * c.E, &c.factor};
+    FwdVisit<Sink> vis{sink, f.v[i], out_key0(c, b, l), &c.factor, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       if (p1 - p0 <= c.cap) {
@@ -395,7 +408,7 @@ __global__ void store_total_kernel(const int64_t* __restrict__ offs, int64_t nbl
 }
 
 __global__ void __launch_bounds__(kTileThreads) tile_emit_kernel(
-    int kind, const void* src, const float* __restrict__ vals, int64_t BLE, int64_t L, int64_t E,
+    int kind, const void* src, const float* __restrict__ vals, int64_t BLE, int64_t L, int64_t E, int64_t lo,
     const int64_t* __restrict__ blk_off, int64_t count, int64_t* __restrict__ idx,
     float* __restrict__ out_val, int64_t* __restrict__ arg) {
   typedef cub::BlockScan<int, kTileThreads> Scan;
@@ -415,7 +428,7 @@ __global__ void __launch_bounds__(kTileThreads) tile_emit_kernel(
       int64_t be = key / (L * E), rem = key % (L * E);
       idx[pos] = be;
       idx[count + pos] = rem / E;
-      idx[2 * count + pos] = rem % E;
+      idx[2 * count + pos] = rem % E + lo;
       if (kind == 0) {
         out_val[pos] = vals[key];
       } else {
@@ -429,13 +442,14 @@ __global__ void __launch_bounds__(kTileThreads) tile_emit_kernel(
 }
 
 // ---------------------------------------------------------------- backward
-__global__ void scatter_grad_kernel(mkg_coo3 g, int64_t B, int64_t L, int64_t E, float* __restrict__ slab,
-                                    unsigned* err) {
+// Incoming gradient keys must lie in the destination range (the forward produced no others).
+__global__ void scatter_grad_kernel(mkg_coo3 g, int64_t B, int64_t L, int64_t lo, int64_t Eo,
+                                    float* __restrict__ slab, unsigned* err) {
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < g.nnz;
        k += (int64_t)gridDim.x * blockDim.x) {
-    int64_t b = g.indices[k], l = g.indices[g.nnz + k], e = g.indices[2 * g.nnz + k];
-    if (b < 0 || b >= B || l < 0 || l >= L || e < 0 || e >= E) { raise_flag(err, MKG_DEV_BAD_KEY); continue; }
-    atomicAdd(slab + (b * L + l) * E + e, g.values[k]);
+    int64_t b = g.indices[k], l = g.indices[g.nnz + k], e = g.indices[2 * g.nnz + k] - lo;
+    if (b < 0 || b >= B || l < 0 || l >= L || e < 0 || e >= Eo) { raise_flag(err, MKG_DEV_BAD_KEY); continue; }
+    atomicAdd(slab + (b * L + l) * Eo + e, g.values[k]);
   }
 }
 
@@ -448,12 +462,11 @@ __global__ void backward_entry_init_kernel(Frontier f, HopCtx c, const float* __
        i += (int64_t)gridDim.x * blockDim.x) {
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) { grad_sp[i] = 0.0f; continue; }
-    const int64_t key = (b * c.L + l) * c.E + e;
-    if (entry_map) entry_map[key] = static_cast<int32_t>(i);
+    if (entry_map) entry_map[(b * c.L + l) * c.E + e] = static_cast<int32_t>(i);
     float gsp = 0.0f;
-    if (!c.wot_i) {
+    if (!c.wot_i && in_range(c, e)) {
       const int64_t wi = (b * c.L + l) * c.n + (c.n - 1);
-      float g = g_ind[key];
+      float g = g_ind[out_key0(c, b, l) + e];
       if (g != 0.0f) {
         gsp = g * c.w[wi];
         atomicAdd(grad_w + wi, g * f.v[i]);
@@ -482,7 +495,9 @@ struct BwdVisit {
   float sv;
   int64_t key0, wbase;
   float acc;
+  int64_t lo, Eo;
   __device__ __forceinline__ void operator()(int d, int64_t dst, int64_t ch, float wv, int64_t fact) {
+    if (static_cast<uint64_t>(dst - lo) >= static_cast<uint64_t>(Eo)) return;  // another shard's destination
     float g = gslab[d][key0 + dst];
     if (g == 0.0f) return;
     float m = (*f)(fact);
@@ -504,8 +519,8 @@ __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict_
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) continue;
     const float* wrow = c.w + (b * c.L + l) * c.n;
-    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], (b * c.L + l) * c.E,
-                 (b * c.L + l) * c.n, 0.0f};
+    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l),
+                 (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       for (int64_t p = p0; p < p1; ++p) visit_position(c, d, p, wrow, vis);
@@ -529,8 +544,8 @@ __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) continue;
     const float* wrow = c.w + (b * c.L + l) * c.n;
-    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], (b * c.L + l) * c.E,
-                 (b * c.L + l) * c.n, 0.0f};
+    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l),
+                 (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       if (p1 - p0 <= c.cap) {
@@ -563,8 +578,8 @@ __global__ void __launch_bounds__(kHubThreads) bwd_hub_kernel(
       __syncthreads();
       wrow = wstage;
     }
-    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], (b * c.L + l) * c.E,
-                 (b * c.L + l) * c.n, 0.0f};
+    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l),
+                 (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       if (p1 - p0 <= c.cap) {
@@ -621,6 +636,7 @@ HopCtx make_ctx(const mkg_graph* g, const float* w, const mkg_edge_factor* ef, c
   HopCtx c;
   c.B = p->B; c.L = p->L; c.E = p->E; c.T = g->num_facts; c.n = p->n; c.r_size = p->r_size;
   c.cap = p->topk_edges; c.wot_i = p->wot_i;
+  c.lo = range_lo(*p); c.Eo = range_extent(*p);
   c.dir[0] = make_dir(g->ori);
   c.dir[1] = make_dir(g->inv);
   c.factor = make_factor(*ef);
@@ -639,6 +655,9 @@ int check_hop_args(const mkg_graph* g, const mkg_frontier* f, const float* w, co
   MKG_REQUIRE(f->nnz >= 0 && f->nnz < (int64_t(1) << 31), "hop: frontier size out of range");
   MKG_REQUIRE(p->r_size >= 0, "hop: r_size must be non-negative");
   MKG_REQUIRE(g->num_facts < (int64_t(1) << 31) - 1, "hop: too many facts for 32-bit argmax ranks");
+  MKG_REQUIRE(p->dst_hi <= p->dst_lo || (p->dst_lo >= 0 && p->dst_hi <= p->E),
+              "hop: destination range [%lld, %lld) outside [0, E=%lld)", (long long)p->dst_lo,
+              (long long)p->dst_hi, (long long)p->E);
   return MKG_OK;
 }
 
@@ -736,8 +755,9 @@ int hop_emit(const mkg_hop_params* p, int64_t nnz, const void* ws, size_t ws_byt
     int slot = p->agg_mode == 1 ? 0 : which;
     kind = 0; src = hit + lay.shit * slot; vals = val + lay.sval * slot;
   }
-  tile_emit_kernel<<<(unsigned)lay.nblk, kTileThreads, 0, st>>>(kind, src, vals, BLE, p->L, p->E, blkoff, count,
-                                                               indices, values, kind == 1 ? arg : nullptr);
+  tile_emit_kernel<<<(unsigned)lay.nblk, kTileThreads, 0, st>>>(kind, src, vals, BLE, p->L, range_extent(*p),
+                                                               range_lo(*p), blkoff, count, indices, values,
+                                                               kind == 1 ? arg : nullptr);
   MKG_LAUNCHED("tile_emit_kernel");
   return MKG_OK;
 }
@@ -754,6 +774,8 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
   int rc = check_hop_args(g, fr, w, ef, p);
   if (rc) return rc;
   MKG_REQUIRE(g_ori && g_inv && g_ind && grad_w && (grad_sp || fr->nnz == 0), "hop_backward: null argument");
+  if (p->agg_mode == 1)
+    MKG_REQUIRE(range_extent(*p) == p->E, "hop_backward: agg_mode 1 needs the full destination range");
   if (p->agg_mode == 1)
     MKG_REQUIRE(out_ori && out_inv && (arg_ori || out_ori->nnz == 0) && (arg_inv || out_inv->nnz == 0) &&
                     fhead && ftail && frel,
@@ -775,7 +797,7 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
   for (int k = 0; k < 3; ++k) {
     if (gl[k]->nnz <= 0) continue;
     scatter_grad_kernel<<<grid_for(gl[k]->nnz, 256, persistent_blocks(8)), 256, 0, st>>>(
-        *gl[k], p->B, p->L, p->E, gs + lay.sval * k, err);
+        *gl[k], p->B, p->L, range_lo(*p), range_extent(*p), gs + lay.sval * k, err);
     MKG_LAUNCHED("scatter_grad_kernel");
   }
   if (F == 0) return MKG_OK;

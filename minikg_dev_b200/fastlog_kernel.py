@@ -56,6 +56,110 @@ def _coo(t: torch.Tensor | None, B, L, E, like_indices: torch.Tensor | None, kee
     return N.Coo3(z.data_ptr(), v.data_ptr(), int(v.numel()))
 
 
+def _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values, weight, B, L, r_size, wot_i,
+                 topk_edges, agg_mode, edge_weight_is_score, edge_weight_scale, dst_lo=0, dst_hi=0):
+    """Forward of one hop on a ``DeviceGraph``; outputs hold the keys with e in [dst_lo, dst_hi)
+    (the whole [0, E) when dst_hi <= dst_lo)."""
+    lib = N.load()
+    N.require_cuda(sp_value, "sp_value")
+    dev = sp_value.device
+    B, L, E, r_size = int(B), int(L), int(g.num_entities), int(r_size)
+    keep = []
+    fr, (b, l, e, v) = _frontier(sp_batch, sp_level, sp_entity, sp_value, keep)
+    wf = w.detach().to(torch.float32).contiguous()
+    if wf.dim() != 3 or wf.shape[0] != B or wf.shape[1] != L:
+        raise ValueError(f"w must be [B, L, n], got {tuple(wf.shape)}")
+    n = int(wf.shape[2])
+    edge_weight = weight if (weight is not None and weight.numel() > 0) else None
+    f = N.edge_factor(mask_values, edge_weight, bool(edge_weight_is_score), float(edge_weight_scale), keep)
+    params = (B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges), int(dst_lo), int(dst_hi))
+    p = N.HopParams(*params)
+    nnz = int(b.numel())
+    ws = N.workspace(lib.mkg_hop_forward_workspace_bytes(ctypes.byref(p), nnz), dev)
+    counts = torch.zeros(3, dtype=torch.int64, device=dev)
+    err = N.error_word(dev)
+    st = N.stream_handle(dev)
+    N.check(lib.mkg_hop_forward(ctypes.byref(g.struct), ctypes.byref(fr), wf.data_ptr(), ctypes.byref(f),
+                                ctypes.byref(p), ws.data_ptr(), ws.numel(), counts.data_ptr(), err.data_ptr(), st),
+            "hop_forward")
+    sizes = counts.tolist()  # the one host sync of the hop (the reference has one too)
+    N.raise_device_errors(dev)
+    outs, args = [], []
+    for which, U in enumerate(sizes):
+        idx = torch.empty((3, U), dtype=torch.int64, device=dev)
+        val = torch.empty(U, dtype=torch.float32, device=dev)
+        arg = torch.empty(U, dtype=torch.int64, device=dev) if (agg_mode == 1 and which < 2) else None
+        N.check(lib.mkg_hop_emit(ctypes.byref(p), nnz, ws.data_ptr(), ws.numel(), which, U, idx.data_ptr(),
+                                 val.data_ptr(), arg.data_ptr() if arg is not None else None, st), "hop_emit")
+        outs.append(torch.sparse_coo_tensor(idx, val, (B, L, E), is_coalesced=True))
+        args.append(arg)
+    del ws
+    has_edge_weight = weight is not None and bool(getattr(weight, "requires_grad", False))
+    if any(ctx.needs_input_grad):
+        empty_i = torch.empty(0, dtype=torch.int64, device=dev)
+        saved = [b, l, e, v, wf, outs[0]._indices(), outs[1]._indices(), outs[2]._indices()]
+        saved += [args[0] if args[0] is not None else empty_i, args[1] if args[1] is not None else empty_i]
+        saved += [mask_values if mask_values is not None else torch.empty(0, device=dev)]
+        saved += [weight.detach() if edge_weight is not None else torch.empty(0, device=dev)]
+        ctx.save_for_backward(*saved)
+        ctx.g = g
+        ctx.params = params
+        ctx.has_mask = mask_values is not None
+        ctx.has_edge_weight = has_edge_weight
+        ctx.edge_weight_present = edge_weight is not None
+        ctx.edge_weight_is_score = bool(edge_weight_is_score)
+        ctx.edge_weight_scale = float(edge_weight_scale)
+        ctx.weight_shape = tuple(weight.shape) if weight is not None else None
+        ctx.weight_dtype = weight.dtype if weight is not None else None
+    return outs[0], outs[1], outs[2]
+
+
+def _hop_backward(ctx, grad_ori, grad_inv, grad_ind):
+    """(grad_sp, grad_w, grad_edge_weight) of ``_hop_forward``."""
+    lib = N.load()
+    b, l, e, v, wf, oi_ori, oi_inv, oi_ind, arg_ori, arg_inv, mask_values, weight = ctx.saved_tensors
+    B, L, E, r_size, n, wot_i, agg_mode, topk, dst_lo, dst_hi = ctx.params
+    g = ctx.g
+    dev = v.device
+    keep = []
+    fr = N.Frontier(b.data_ptr(), l.data_ptr(), e.data_ptr(), v.data_ptr(), b.numel())
+    f = N.edge_factor(mask_values if ctx.has_mask else None, weight if ctx.edge_weight_present else None,
+                      ctx.edge_weight_is_score, ctx.edge_weight_scale, keep)
+    p = N.HopParams(*ctx.params)
+    go = _coo(grad_ori, B, L, E, oi_ori, keep)
+    gi = _coo(grad_inv, B, L, E, oi_inv, keep)
+    gd = _coo(grad_ind, B, L, E, oi_ind, keep)
+    grad_sp = torch.empty(b.numel(), dtype=torch.float32, device=dev)
+    grad_w = torch.empty((B, L, n), dtype=torch.float32, device=dev)
+    grad_edge = torch.empty(g.num_facts, dtype=torch.float32, device=dev) if ctx.has_edge_weight else None
+    out_o = N.Coo3(oi_ori.data_ptr(), None, int(oi_ori.shape[1]))
+    out_i = N.Coo3(oi_inv.data_ptr(), None, int(oi_inv.shape[1]))
+    fh = ft = frl = None
+    if agg_mode == 1:
+        fh, ft, frl = g.fact_table()
+    ws = N.workspace(lib.mkg_hop_backward_workspace_bytes(ctypes.byref(p), b.numel()), dev)
+    N.check(lib.mkg_hop_backward(ctypes.byref(g.struct), ctypes.byref(fr), wf.data_ptr(), ctypes.byref(f),
+                                 ctypes.byref(p), ctypes.byref(go), ctypes.byref(gi), ctypes.byref(gd),
+                                 ctypes.byref(out_o), N.ptr(arg_ori) if arg_ori.numel() else None,
+                                 ctypes.byref(out_i), N.ptr(arg_inv) if arg_inv.numel() else None,
+                                 N.ptr(fh), N.ptr(ft), N.ptr(frl), grad_sp.data_ptr(), grad_w.data_ptr(),
+                                 N.ptr(grad_edge), ws.data_ptr(), ws.numel(), N.error_word(dev).data_ptr(),
+                                 N.stream_handle(dev)), "hop_backward")
+    grad_edge_weight = None
+    if ctx.has_edge_weight:
+        if os.environ.get("FASTLOG_SPARSE_EDGE_GRAD", "0") == "1":
+            nz = torch.nonzero(grad_edge, as_tuple=True)[0]
+            if len(ctx.weight_shape) == 2 and ctx.weight_shape[1] == 1:
+                idx = torch.stack([nz, torch.zeros_like(nz)])
+            else:
+                idx = nz.view(1, -1)
+            grad_edge_weight = torch.sparse_coo_tensor(idx, grad_edge[nz].to(ctx.weight_dtype),
+                                                       ctx.weight_shape, device=dev).coalesce()
+        else:
+            grad_edge_weight = grad_edge.view(ctx.weight_shape).to(ctx.weight_dtype)
+    return grad_sp.to(v.dtype), grad_w, grad_edge_weight
+
+
 class FastLogFunctionSparse3DTopK(autograd.Function):
     """One relation-typed hop (reference: fastlog_kernel.py:900-1107)."""
 
@@ -67,110 +171,40 @@ class FastLogFunctionSparse3DTopK(autograd.Function):
                 inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
                 mask_values, weight, B, L, E, r_size, wot_i, topk_edges, agg_mode=0,
                 edge_weight_is_score=False, edge_weight_scale=1.0):
-        lib = N.load()
-        N.require_cuda(sp_value, "sp_value")
-        dev = sp_value.device
-        B, L, E, r_size = int(B), int(L), int(E), int(r_size)
         csr = (ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count)
-        g = graph_from_csr(csr, E, r_size)
-        keep = []
-        fr, (b, l, e, v) = _frontier(sp_batch, sp_level, sp_entity, sp_value, keep)
-        wf = w.detach().to(torch.float32).contiguous()
-        if wf.dim() != 3 or wf.shape[0] != B or wf.shape[1] != L:
-            raise ValueError(f"w must be [B, L, n], got {tuple(wf.shape)}")
-        n = int(wf.shape[2])
-        edge_weight = weight if (weight is not None and weight.numel() > 0) else None
-        f = N.edge_factor(mask_values, edge_weight, bool(edge_weight_is_score), float(edge_weight_scale), keep)
-        p = N.HopParams(B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges))
-        nnz = int(b.numel())
-        ws = N.workspace(lib.mkg_hop_forward_workspace_bytes(ctypes.byref(p), nnz), dev)
-        counts = torch.zeros(3, dtype=torch.int64, device=dev)
-        err = N.error_word(dev)
-        st = N.stream_handle(dev)
-        N.check(lib.mkg_hop_forward(ctypes.byref(g.struct), ctypes.byref(fr), wf.data_ptr(), ctypes.byref(f),
-                                    ctypes.byref(p), ws.data_ptr(), ws.numel(), counts.data_ptr(), err.data_ptr(),
-                                    st), "hop_forward")
-        sizes = counts.tolist()  # the one host sync of the hop (the reference has one too)
-        N.raise_device_errors(dev)
-        outs, args = [], []
-        for which, U in enumerate(sizes):
-            idx = torch.empty((3, U), dtype=torch.int64, device=dev)
-            val = torch.empty(U, dtype=torch.float32, device=dev)
-            arg = torch.empty(U, dtype=torch.int64, device=dev) if (agg_mode == 1 and which < 2) else None
-            N.check(lib.mkg_hop_emit(ctypes.byref(p), nnz, ws.data_ptr(), ws.numel(), which, U, idx.data_ptr(),
-                                     val.data_ptr(), arg.data_ptr() if arg is not None else None, st), "hop_emit")
-            outs.append(torch.sparse_coo_tensor(idx, val, (B, L, E), is_coalesced=True))
-            args.append(arg)
-        del ws
-        has_edge_weight = weight is not None and bool(getattr(weight, "requires_grad", False))
-        if any(ctx.needs_input_grad):
-            saved = [b, l, e, v, wf]
-            saved += [outs[0]._indices(), outs[1]._indices()]
-            saved += [args[0] if args[0] is not None else torch.empty(0, dtype=torch.int64, device=dev),
-                      args[1] if args[1] is not None else torch.empty(0, dtype=torch.int64, device=dev)]
-            saved += [mask_values if mask_values is not None else torch.empty(0, device=dev)]
-            saved += [weight.detach() if edge_weight is not None else torch.empty(0, device=dev)]
-            ctx.save_for_backward(*saved)
-            ctx.g = g
-            ctx.params = (B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges))
-            ctx.has_mask = mask_values is not None
-            ctx.has_edge_weight = has_edge_weight
-            ctx.edge_weight_present = edge_weight is not None
-            ctx.edge_weight_is_score = bool(edge_weight_is_score)
-            ctx.edge_weight_scale = float(edge_weight_scale)
-            ctx.weight_shape = tuple(weight.shape) if weight is not None else None
-            ctx.weight_dtype = weight.dtype if weight is not None else None
-        return outs[0], outs[1], outs[2]
+        g = graph_from_csr(csr, int(E), int(r_size))
+        return _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values, weight, B, L, r_size,
+                            wot_i, topk_edges, agg_mode, edge_weight_is_score, edge_weight_scale)
 
     @staticmethod
     def backward(ctx, grad_ori, grad_inv, grad_ind):
-        lib = N.load()
-        b, l, e, v, wf, oi_ori, oi_inv, arg_ori, arg_inv, mask_values, weight = ctx.saved_tensors
-        B, L, E, r_size, n, wot_i, agg_mode, topk = ctx.params
-        g = ctx.g
-        dev = v.device
-        keep = []
-        fr = N.Frontier(b.data_ptr(), l.data_ptr(), e.data_ptr(), v.data_ptr(), b.numel())
-        f = N.edge_factor(mask_values if ctx.has_mask else None, weight if ctx.edge_weight_present else None,
-                          ctx.edge_weight_is_score, ctx.edge_weight_scale, keep)
-        p = N.HopParams(B, L, E, r_size, n, wot_i, agg_mode, topk)
-        go = _coo(grad_ori, B, L, E, oi_ori, keep)
-        gi = _coo(grad_inv, B, L, E, oi_inv, keep)
-        gd = _coo(grad_ind, B, L, E, torch.stack([b, l, e]), keep)
-        grad_sp = torch.empty(b.numel(), dtype=torch.float32, device=dev)
-        grad_w = torch.empty((B, L, n), dtype=torch.float32, device=dev)
-        grad_edge = torch.empty(g.num_facts, dtype=torch.float32, device=dev) if ctx.has_edge_weight else None
-        out_o = N.Coo3(oi_ori.data_ptr(), None, int(oi_ori.shape[1]))
-        out_i = N.Coo3(oi_inv.data_ptr(), None, int(oi_inv.shape[1]))
-        fh = ft = frl = None
-        if agg_mode == 1:
-            fh, ft, frl = g.fact_table()
-        ws = N.workspace(lib.mkg_hop_backward_workspace_bytes(ctypes.byref(p), b.numel()), dev)
-        N.check(lib.mkg_hop_backward(ctypes.byref(g.struct), ctypes.byref(fr), wf.data_ptr(), ctypes.byref(f),
-                                     ctypes.byref(p), ctypes.byref(go), ctypes.byref(gi), ctypes.byref(gd),
-                                     ctypes.byref(out_o), N.ptr(arg_ori) if arg_ori.numel() else None,
-                                     ctypes.byref(out_i), N.ptr(arg_inv) if arg_inv.numel() else None,
-                                     N.ptr(fh), N.ptr(ft), N.ptr(frl), grad_sp.data_ptr(), grad_w.data_ptr(),
-                                     N.ptr(grad_edge), ws.data_ptr(), ws.numel(), N.error_word(dev).data_ptr(),
-                                     N.stream_handle(dev)), "hop_backward")
-        grad_edge_weight = None
-        if ctx.has_edge_weight:
-            if os.environ.get("FASTLOG_SPARSE_EDGE_GRAD", "0") == "1":
-                nz = torch.nonzero(grad_edge, as_tuple=True)[0]
-                if len(ctx.weight_shape) == 2 and ctx.weight_shape[1] == 1:
-                    idx = torch.stack([nz, torch.zeros_like(nz)])
-                else:
-                    idx = nz.view(1, -1)
-                grad_edge_weight = torch.sparse_coo_tensor(idx, grad_edge[nz].to(ctx.weight_dtype),
-                                                           ctx.weight_shape, device=dev).coalesce()
-            else:
-                grad_edge_weight = grad_edge.view(ctx.weight_shape).to(ctx.weight_dtype)
-        return (None, None, None, grad_sp.to(v.dtype), grad_w,
+        grad_sp, grad_w, grad_edge_weight = _hop_backward(ctx, grad_ori, grad_inv, grad_ind)
+        return (None, None, None, grad_sp, grad_w,
                 None, None, None, None,
                 None, None, None, None,
                 None, None, None, None,
                 None, None, None, None,
                 None, grad_edge_weight,
+                None, None, None, None, None, None, None, None, None)
+
+
+class HopRange(autograd.Function):
+    """One hop on a resident ``DeviceGraph`` restricted to destinations in [dst_lo, dst_hi):
+    ``(ori, inv, ind)`` hold only those keys (shape [B, L, E]); caps are decided on whole
+    CSR rows, so the outputs over a partition of [0, E) add up to the full-range op.
+    Gradients flow to ``sp_value``, ``w`` and ``weight``."""
+
+    @staticmethod
+    def forward(ctx, sp_batch, sp_level, sp_entity, sp_value, w, graph, mask_values, weight, B, L, wot_i,
+                topk_edges, agg_mode, edge_weight_is_score, edge_weight_scale, dst_lo, dst_hi):
+        return _hop_forward(ctx, graph, sp_batch, sp_level, sp_entity, sp_value, w, mask_values, weight, B, L,
+                            graph.num_relations, wot_i, topk_edges, agg_mode, edge_weight_is_score,
+                            edge_weight_scale, dst_lo, dst_hi)
+
+    @staticmethod
+    def backward(ctx, grad_ori, grad_inv, grad_ind):
+        grad_sp, grad_w, grad_edge_weight = _hop_backward(ctx, grad_ori, grad_inv, grad_ind)
+        return (None, None, None, grad_sp, grad_w, None, None, grad_edge_weight,
                 None, None, None, None, None, None, None, None, None)

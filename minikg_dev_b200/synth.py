@@ -142,7 +142,14 @@ def _draw(probs: np.ndarray, count: int, rng) -> np.ndarray:
     cdf = np.cumsum(probs)
     cdf /= cdf[-1]
     u = rng.random(count)
-    return np.minimum(np.searchsorted(cdf, u, side="right"), probs.shape[0] - 1)
+    if probs.shape[0] > 65536 and count > 65536:
+        # same result; sorted queries keep the binary searches cache-resident on large CDFs
+        order = np.argsort(u, kind="stable")
+        idx = np.empty(count, dtype=np.int64)
+        idx[order] = np.searchsorted(cdf, u[order], side="right")
+    else:
+        idx = np.searchsorted(cdf, u, side="right")
+    return np.minimum(idx, probs.shape[0] - 1)
 
 
 def sample_graph(E: int, R: int, T: int, gen, seed: int = 0, name: str = "kg") -> KG:

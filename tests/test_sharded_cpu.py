@@ -1,0 +1,178 @@
+"""The destination-partitioned hop loop's host logic on CPU: world_size 2 (and 3) over gloo.
+
+The per-rank hop here is the oracle's op restricted to the rank's destination range (an
+autograd function around ``sparse3d_forward`` / ``sparse3d_backward``), so these tests check
+the partition, the frontier all-gather and its gradient, the globally normalised columns,
+the cross-rank prune and the top-k merge against the single-process oracle loop.  The CUDA
+op in the same loop is checked on two GPUs in ``test_sharded_gpu.py``.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import fastlog_oracle as O
+from tests.conftest import load_golden
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(seed=0, B=5, L=3, K=3):
+    g = load_golden("g2")
+    h, r, t = g["head"], g["rel"], g["tail"]
+    E, R = int(g["E"][0]), int(g["R"][0])
+    rng = np.random.default_rng(seed)
+    n = 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    heads[1] = heads[0]  # two queries from one head
+    w = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    scores = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    return h, r, t, E, R, heads, w, scores
+
+
+class _OracleRangeHop(torch.autograd.Function):
+    """The oracle hop with outputs restricted to destinations in [lo, hi)."""
+
+    @staticmethod
+    def forward(ctx, b, l, e, v, w_h, ew, csr, E, R, cap, lo, hi):
+        B, L, _ = w_h.shape
+        bn, ln, en, vn = (x.detach().numpy() for x in (b, l, e, v))
+        wn, ewn = w_h.detach().numpy(), ew.detach().numpy()
+        mask = np.ones(ewn.shape[0], bool)
+        fwd = O.sparse3d_forward(bn, ln, en, vn, wn, csr, mask, ewn, B, L, E, R, cap=cap, agg_mode=0, is_score=True)
+        outs = []
+        for name in ("ori", "inv", "ind"):
+            k, val = fwd[name]
+            keep = ((k % E) >= lo) & ((k % E) < hi)
+            kb, kl, ke = O.split3(k[keep], L, E)
+            idx = torch.from_numpy(np.stack([kb, kl, ke]).astype(np.int64).reshape(3, -1))
+            outs.append(torch.sparse_coo_tensor(idx, torch.from_numpy(val[keep].astype(np.float32)), (B, L, E),
+                                                is_coalesced=True))
+        ctx.fwd, ctx.args = fwd, (bn, ln, en, vn, wn, ewn, B, L, E, R)
+        ctx.keys = [o.indices() for o in outs]
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, go, gi, gd):
+        bn, ln, en, vn, wn, ewn, B, L, E, R = ctx.args
+        grads = {}
+        for name, g, idx in zip(("ori", "inv", "ind"), (go, gi, gd), ctx.keys):
+            k = O.keys3(idx[0].numpy(), idx[1].numpy(), idx[2].numpy(), L, E)
+            if g is None:
+                gv = np.zeros(k.shape[0], np.float32)
+            elif g.is_sparse:
+                g = g.coalesce()
+                gk = O.keys3(*(g.indices().numpy()), L, E)
+                gv = O.lookup(gk, g.values().numpy().astype(np.float32), k)
+            else:
+                gv = g[idx[0], idx[1], idx[2]].numpy().astype(np.float32)
+            grads[name] = (k, gv)
+        gsp, gw, ge = O.sparse3d_backward(ctx.fwd, grads, bn, ln, en, vn, wn, B, L, E, R, agg_mode=0,
+                                          edge_weight=ewn, is_score=True, want_edge_grad=True,
+                                          num_facts=ewn.shape[0])
+        return (None, None, None, torch.from_numpy(gsp), torch.from_numpy(gw), torch.from_numpy(ge),
+                None, None, None, None, None, None)
+
+
+def _worker(rank, world, port, cfg, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from minikg_dev_b200 import sharded as S
+        h, r, t, E, R, heads, w, scores = _case(**cfg["case"])
+        csr = O.build_csr_structure(h, t, r, E)
+        bounds = S.plan_dst_ranges(S.message_in_counts(torch.from_numpy(h), torch.from_numpy(t), E), world)
+        spec = S.ShardSpec(rank, world, bounds)
+        wt = torch.from_numpy(w).requires_grad_(True)
+        ew = torch.from_numpy(scores).requires_grad_(True)
+        ew_rep = S.replicated(ew)
+
+        def hop(b, l, e, v, w_h, lo, hi):
+            return _OracleRangeHop.apply(b, l, e, v, w_h, ew_rep, csr, E, R, cfg["cap"], lo, hi)
+
+        keys, vals = S.sharded_proof_scores(spec, hop, torch.from_numpy(heads), wt, E, threshold=cfg["threshold"],
+                                            topk_nodes=cfg["topk_nodes"])
+        B = heads.shape[0]
+        seed_all = np.random.default_rng(99).standard_normal(B * E).astype(np.float32)
+        (vals * torch.from_numpy(seed_all)[keys]).sum().backward()
+        tails, sc, cnt = S.merge_topk(spec, keys, vals, B, E, cfg["k"])
+        out_q.put((rank, bounds, keys.numpy(), vals.detach().numpy(), wt.grad.numpy(), ew.grad.numpy(),
+                   tails.numpy(), sc.numpy(), cnt.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(world, cfg):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return sorted(res, key=lambda x: x[0])
+
+
+@pytest.mark.parametrize("world,cfg", [
+    (2, dict(case=dict(seed=0), cap=O.UNCAPPED, threshold=0.0, topk_nodes=0, k=10)),
+    (2, dict(case=dict(seed=1), cap=9, threshold=0.0, topk_nodes=0, k=25)),
+    (3, dict(case=dict(seed=2), cap=O.UNCAPPED, threshold=1e-4, topk_nodes=0, k=10)),
+    (2, dict(case=dict(seed=3), cap=O.UNCAPPED, threshold=0.0, topk_nodes=40, k=10)),
+])
+def test_sharded_loop_matches_single_process_oracle(world, cfg):
+    h, r, t, E, R, heads, w, scores = _case(**cfg["case"])
+    B, L = heads.shape[0], w.shape[2]
+    csr = O.build_csr_structure(h, t, r, E)
+    mask = np.ones(h.shape[0], bool)
+    final, trace = O.proof_sum_forward(heads, w, csr, mask, scores, B, L, E, R, cap=cfg["cap"],
+                                       topk_nodes=cfg["topk_nodes"], threshold=cfg["threshold"])
+    res = _run(world, cfg)
+    bounds = res[0][1]
+    assert bounds[0] == 0 and bounds[-1] == E and all(a < b for a, b in zip(bounds, bounds[1:]))
+    keys = np.concatenate([x[2] for x in res])
+    vals = np.concatenate([x[3] for x in res])
+    order = np.argsort(keys, kind="stable")  # ranks hold entity ranges; keys are b * E + e
+    keys, vals = keys[order], vals[order]
+    for rank, x in enumerate(res):  # every rank holds only its own entities
+        assert ((x[2] % E >= bounds[rank]) & (x[2] % E < bounds[rank + 1])).all()
+    np.testing.assert_array_equal(keys, final[0])
+    np.testing.assert_allclose(vals, final[1], rtol=1e-5, atol=1e-6)
+    seed_all = np.random.default_rng(99).standard_normal(B * E).astype(np.float32)
+    gw, ge = O.proof_sum_backward(trace, (final[0], seed_all[final[0]]), w, csr, mask, scores, B, L, E, R,
+                                  num_facts=h.shape[0])
+    for x in res:  # the replicated inputs carry the full gradient on every rank
+        np.testing.assert_allclose(x[4], gw, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(x[5], ge, rtol=1e-4, atol=1e-5)
+    # the merge is exact: compare with the oracle's decode of the same (gathered) raw scores
+    ot, osc, oc = O.decode_topk((keys, vals), B, E, cfg["k"])
+    for x in res:
+        np.testing.assert_array_equal(x[6], ot)
+        np.testing.assert_array_equal(x[7], osc)
+        np.testing.assert_array_equal(x[8], oc)
+
+
+def test_plan_dst_ranges_balances_messages():
+    from minikg_dev_b200.sharded import message_in_counts, plan_dst_ranges
+    h, r, t, E, R, *_ = _case()
+    m = message_in_counts(torch.from_numpy(h), torch.from_numpy(t), E)
+    for world in (1, 2, 4, 8):
+        b = plan_dst_ranges(m, world)
+        assert b[0] == 0 and b[-1] == E and len(b) == world + 1
+        assert all(x < y for x, y in zip(b, b[1:]))
+        load = [int((m[b[k]:b[k + 1]] + 1).sum()) for k in range(world)]
+        assert max(load) <= (int((m + 1).sum()) / world) + int(m.max()) + 1
+    with pytest.raises(ValueError):
+        plan_dst_ranges(torch.zeros(3, dtype=torch.int64), 4)
