@@ -40,7 +40,8 @@ enum {
   MKG_DEV_BAD_FACT = 4u,   /* CSR order / fact id outside [0, T) */
   MKG_DEV_BAD_KEY = 8u,    /* gradient COO key outside [B, L, E] */
   MKG_DEV_BAD_REL = 16u,   /* relation id outside [0, R) */
-  MKG_DEV_TIMEOUT = 32u    /* a bounded wait inside a kernel gave up */
+  MKG_DEV_TIMEOUT = 32u,   /* a bounded wait inside a kernel gave up */
+  MKG_DEV_TABLE_FULL = 64u /* a message hash table ran out of slots (msg_bound too small) */
 };
 
 /* One direction of the reference CSR pair (fastlog_kernel.py:403-410 tuple order). */
@@ -192,7 +193,25 @@ typedef struct mkg_hop_params {
    * (e.g. both 0) means [0, E).  No counterpart in the reference (single GPU); used by the
    * destination-partitioned multi-GPU hop.  agg_mode 1 backward needs the full range. */
   int64_t dst_lo, dst_hi;
+  /* Upper bound on the messages of one direction (ori or inv) of this hop, e.g. the larger
+   * count written by mkg_hop_count_messages; 0 = unknown.  Messages are reduced in a dense
+   * slab indexed by the output key unless the bound is far below the key space
+   * (32 * msg_bound < B * L * extent): then in open-addressing hash tables of
+   * 2^ceil(log2(2 * bound)) slots, sorted by key for the output.  The forward, emit and
+   * backward calls of one hop must all see the same value. */
+  int64_t msg_bound;
+  /* 0: choose as above; 1: always the dense slab; 2: hash tables (needs msg_bound >= the
+   * real message count of each direction, else MKG_DEV_TABLE_FULL). */
+  int64_t accum;
 } mkg_hop_params;
+
+/* Exact message counts of one hop (no counterpart in the reference, whose count kernels
+ * fastlog.cu:2721-2730 feed a device cumsum): counts_out[0] / [1] (device int64) = the
+ * frontier's ori / inv messages, per entry min(out-degree, cap) (the 256-bucket cap takes
+ * exactly cap edges of a longer row; cap <= 0 takes none).  Destination ranges do not
+ * change the count (every rank of a partition walks the same messages). */
+int mkg_hop_count_messages(const mkg_graph* g, const mkg_frontier* f, const mkg_hop_params* p,
+                           int64_t* counts_out, unsigned* dev_err, mkg_stream stream);
 
 /* Forward of one hop, coalesced: replaces fastlog_forward_sparse3d_topk_cuda
  * (src/fastlog_kernel/source/fastlog.h:78-93, fastlog.cu:2678-2806) together with the

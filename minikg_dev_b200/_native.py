@@ -19,7 +19,8 @@ MKG_OK = 0
 MASK_NONE, MASK_U8, MASK_F32 = 0, 1, 2
 DEV_ERR_NAMES = {1: "frontier entry outside [B, L, E]", 2: "CSR column outside [0, E)",
                  4: "fact id outside [0, T)", 8: "gradient key outside [B, L, E]",
-                 16: "relation id outside its range", 32: "a bounded wait inside a kernel gave up"}
+                 16: "relation id outside its range", 32: "a bounded wait inside a kernel gave up",
+                 64: "a message hash table ran out of slots (msg_bound too small)"}
 
 vp = C.c_void_p
 i64 = C.c_int64
@@ -61,7 +62,8 @@ class Adjacency(C.Structure):
 
 class HopParams(C.Structure):
     _fields_ = [("B", i64), ("L", i64), ("E", i64), ("r_size", i64), ("n", i64), ("wot_i", i32),
-                ("agg_mode", i32), ("topk_edges", i64), ("dst_lo", i64), ("dst_hi", i64)]
+                ("agg_mode", i32), ("topk_edges", i64), ("dst_lo", i64), ("dst_hi", i64), ("msg_bound", i64),
+                ("accum", i64)]
 
 
 class ProofParams(C.Structure):
@@ -88,6 +90,7 @@ SIGNATURES = {
     "mkg_hop_forward": (C.c_int, [P(Graph), P(Frontier), vp, P(EdgeFactor), P(HopParams), vp, C.c_size_t, vp,
                                   vp, vp]),
     "mkg_hop_emit": (C.c_int, [P(HopParams), i64, vp, C.c_size_t, C.c_int, i64, vp, vp, vp, vp]),
+    "mkg_hop_count_messages": (C.c_int, [P(Graph), P(Frontier), P(HopParams), vp, vp, vp]),
     "mkg_hop_backward_workspace_bytes": (C.c_size_t, [P(HopParams), i64]),
     "mkg_hop_backward": (C.c_int, [P(Graph), P(Frontier), vp, P(EdgeFactor), P(HopParams), P(Coo3), P(Coo3),
                                    P(Coo3), P(Coo3), vp, P(Coo3), vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t,

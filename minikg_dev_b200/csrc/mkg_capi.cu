@@ -38,7 +38,7 @@ using mkg::set_error;
 static cudaStream_t S(mkg_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 
 MKG_API const char* mkg_last_error(void) { return mkg::g_last_error; }
-MKG_API int mkg_abi_version(void) { return 2; }
+MKG_API int mkg_abi_version(void) { return 3; }
 
 MKG_API size_t mkg_csr_build_workspace_bytes(int64_t T, int64_t E, int64_t R) {
   return mkg::csr_build_workspace_bytes(T, E, R);
@@ -73,6 +73,10 @@ MKG_API int mkg_adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, cons
   return mkg::adjacency_set_factor(g, adj, f, S(st));
 }
 
+MKG_API int mkg_hop_count_messages(const mkg_graph* g, const mkg_frontier* f, const mkg_hop_params* p,
+                                   int64_t* counts, unsigned* err, mkg_stream st) {
+  return mkg::hop_count_messages(g, f, p, counts, err, S(st));
+}
 MKG_API size_t mkg_hop_forward_workspace_bytes(const mkg_hop_params* p, int64_t nnz) {
   return p ? mkg::hop_forward_workspace_bytes(p, nnz) : 0;
 }

@@ -1,8 +1,15 @@
 // The per-hop op behind FastLogFunctionSparse3DTopK: degree-bucketed push expansion of a
 // sparse [B, L, E] frontier over the ori / inv CSR with the exact 256-bucket edge cap,
-// reduced on the fly into key-major HBM slabs (sum: fp32 atomics + a hit byte per key;
-// max: packed 64-bit (value, fact id) atomicMax), then compacted into coalesced COO in key
-// order.  The backward walks the same messages and gathers the gradient from a dense slab.
+// reduced on the fly (sum: fp32 atomics; max: packed 64-bit (value, fact id) atomicMax) into
+// one of two key stores, then written as coalesced COO in key order:
+//  * dense: slabs indexed by the output key (plus a hit byte per key for sums), compacted
+//    by a tile scan -- for frontiers that touch a good share of the B x L x E key space;
+//  * hash: open-addressing tables of 2^ceil(log2(2 * msg_bound)) slots (keys claimed with
+//    atomicCAS, linear probing), radix-sorted by key -- when the message bound is far below
+//    the key space (sparse frontiers on large graphs), so cost follows the messages.
+// The backward walks the same messages and gathers the gradient from the same kind of store.
+#include <algorithm>
+
 #include <cub/cub.cuh>
 
 #include "mkg_common.cuh"
@@ -17,17 +24,58 @@ constexpr int kMidWarps = 8;     // warps per block in the warp-per-entry kernel
 constexpr int kTile = 4096;      // keys per compaction block (256 threads x 16)
 constexpr int kTileThreads = 256;
 constexpr int kHubStageMax = 4096;  // rule-weight rows up to this many channels are staged in smem
+constexpr int64_t kHashRatio = 32;  // hash tables when 32 * msg_bound < key space
+constexpr int64_t kMinSlots = 1024;
 
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Output entities: the destination range [lo, lo + extent) (the whole [0, E) by default).
+int64_t range_lo(const mkg_hop_params& p) { return p.dst_hi > p.dst_lo ? p.dst_lo : 0; }
+int64_t range_extent(const mkg_hop_params& p) { return p.dst_hi > p.dst_lo ? p.dst_hi - p.dst_lo : p.E; }
+
+int64_t pow2_at_least(int64_t x) {
+  int64_t c = kMinSlots;
+  while (c < x) c <<= 1;
+  return c;
+}
+int log2_exact(int64_t c) {
+  int k = 0;
+  while ((int64_t(1) << k) < c) ++k;
+  return k;
+}
+
 struct HopLayout {
+  bool hash;
+  int bits;                // hash: keys < empty = 2^bits - 1 (radix sort over these bits)
   int64_t BLE, F, nblk;
-  // per-slab strides in elements; every slab starts 256-byte aligned (the compaction
+  int64_t capm, capf;      // hash slots: ori / inv tables, ind table (and the entry map)
+  // dense: per-slab strides in elements; every slab starts 256-byte aligned (the compaction
   // reads 16 hit bytes at a time as one uint4)
   int64_t sval, shit, spk;
   size_t off_val, off_hit, off_pk, off_lists, off_counts, off_blk, off_blkoff, off_cub, off_map, total;
+  // hash: claimed keys, values (f32 / packed u64), their key-sorted copies, entry map values
+  size_t off_tkey, off_tval, off_tpk, off_skey, off_sval, off_spk, off_mapkey;
   size_t cub_bytes;
+
+  int64_t slots(int t) const { return t < 2 ? capm : capf; }
+  int64_t base(int t) const { return t < 2 ? capm * t : 2 * capm; }
+  unsigned long long empty() const { return (1ull << bits) - 1ull; }
 };
+
+bool use_hash(const mkg_hop_params& p) {
+  if (p.accum == 1) return false;
+  if (p.accum == 2) return true;
+  const int64_t BLE = p.B * p.L * range_extent(p);
+  return p.msg_bound > 0 && kHashRatio * p.msg_bound < BLE;
+}
+
+void hash_dims(HopLayout& L, const mkg_hop_params& p, int64_t F) {
+  L.capm = pow2_at_least(2 * (p.msg_bound > 0 ? p.msg_bound : 1));
+  L.capf = pow2_at_least(2 * (F > 0 ? F : 1));
+  L.bits = 1;
+  const int64_t key_space = std::max(L.BLE, p.B * p.L * p.E);  // the entry map uses full-range keys
+  while (L.bits < 63 && (1ull << L.bits) - 1ull <= static_cast<unsigned long long>(key_space)) ++L.bits;
+}
 
 size_t scan_bytes(int64_t nblk) {
   size_t b = 0;
@@ -35,47 +83,77 @@ size_t scan_bytes(int64_t nblk) {
   return b;
 }
 
-// Forward workspace: value slabs (sum: ori, inv, ind; max: ind), hit slabs, packed slabs
-// (max: ori, inv), class lists, per-tile counts and offsets for the three outputs.
-// Output entities: the destination range [lo, lo + extent) (the whole [0, E) by default).
-int64_t range_lo(const mkg_hop_params& p) { return p.dst_hi > p.dst_lo ? p.dst_lo : 0; }
-int64_t range_extent(const mkg_hop_params& p) { return p.dst_hi > p.dst_lo ? p.dst_hi - p.dst_lo : p.E; }
+template <class V>
+size_t sort_bytes(int64_t n) {
+  size_t b = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, b, (const unsigned long long*)nullptr, (unsigned long long*)nullptr,
+                                  (const V*)nullptr, (V*)nullptr, (int)n);
+  return b;
+}
 
+// Forward workspace.  Dense: value slabs (sum: ori, inv, ind; max: ind), hit slabs, packed
+// slabs (max: ori, inv), per-tile counts and offsets.  Hash: three tables (ori, inv, ind)
+// of claimed keys with f32 values (max: packed u64 for ori / inv) and their sorted copies.
+// Both: the class lists.
 HopLayout forward_layout(const mkg_hop_params& p, int64_t F) {
   HopLayout L{};
   L.BLE = p.B * p.L * range_extent(p);
   L.F = F;
-  L.nblk = (L.BLE + kTile - 1) / kTile;
-  const int nval = p.agg_mode == 1 ? 1 : 3;
-  L.sval = a256(4 * (size_t)L.BLE) / 4;
-  L.shit = a256((size_t)L.BLE);
-  L.spk = a256(8 * (size_t)L.BLE) / 8;
+  L.hash = use_hash(p);
   size_t o = 0;
-  L.off_val = o; o += 4 * (size_t)L.sval * nval;
-  L.off_hit = o; o += (size_t)L.shit * nval;
-  L.off_pk = o; o += p.agg_mode == 1 ? 8 * (size_t)L.spk * 2 : 0;
+  if (!L.hash) {
+    L.nblk = (L.BLE + kTile - 1) / kTile;
+    const int nval = p.agg_mode == 1 ? 1 : 3;
+    L.sval = a256(4 * (size_t)L.BLE) / 4;
+    L.shit = a256((size_t)L.BLE);
+    L.spk = a256(8 * (size_t)L.BLE) / 8;
+    L.off_val = o; o += 4 * (size_t)L.sval * nval;
+    L.off_hit = o; o += (size_t)L.shit * nval;
+    L.off_pk = o; o += p.agg_mode == 1 ? 8 * (size_t)L.spk * 2 : 0;
+    L.off_blk = o; o += a256(8 * (size_t)(L.nblk + 1) * 3);
+    L.off_blkoff = o; o += a256(8 * (size_t)(L.nblk + 1) * 3);
+    L.cub_bytes = scan_bytes(L.nblk);
+  } else {
+    hash_dims(L, p, F);
+    const size_t all = (size_t)(2 * L.capm + L.capf);
+    L.off_tkey = o; o += a256(8 * all);
+    L.off_tval = o; o += a256(4 * all);
+    L.off_tpk = o; o += p.agg_mode == 1 ? a256(8 * (size_t)(2 * L.capm)) : 0;
+    L.off_skey = o; o += a256(8 * all);
+    L.off_sval = o; o += a256(4 * all);
+    L.off_spk = o; o += p.agg_mode == 1 ? a256(8 * (size_t)(2 * L.capm)) : 0;
+    L.cub_bytes = std::max(std::max(sort_bytes<float>(L.capm), sort_bytes<float>(L.capf)),
+                           p.agg_mode == 1 ? sort_bytes<unsigned long long>(L.capm) : size_t(0));
+  }
   L.off_lists = o; o += a256(4 * (size_t)(3 * F + 3));
   L.off_counts = o; o += a256(4 * 4);
-  L.off_blk = o; o += a256(8 * (size_t)(L.nblk + 1) * 3);
-  L.off_blkoff = o; o += a256(8 * (size_t)(L.nblk + 1) * 3);
-  L.cub_bytes = scan_bytes(L.nblk);
   L.off_cub = o; o += a256(L.cub_bytes);
   L.off_map = 0;
   L.total = o;
   return L;
 }
 
-// Backward workspace: gradient slabs (ori, inv, ind), class lists, the key -> entry map.
+// Backward workspace: gradient stores (ori, inv, ind), class lists, the entry map (max).
 HopLayout backward_layout(const mkg_hop_params& p, int64_t F) {
   HopLayout L{};
   L.BLE = p.B * p.L * range_extent(p);
   L.F = F;
-  L.sval = a256(4 * (size_t)L.BLE) / 4;
+  L.hash = use_hash(p);
   size_t o = 0;
-  L.off_val = o; o += 4 * (size_t)L.sval * 3;
+  if (!L.hash) {
+    L.sval = a256(4 * (size_t)L.BLE) / 4;
+    L.off_val = o; o += 4 * (size_t)L.sval * 3;
+    L.off_map = o; o += p.agg_mode == 1 ? a256(4 * (size_t)(p.B * p.L * p.E)) : 0;
+  } else {
+    hash_dims(L, p, F);
+    const size_t all = (size_t)(2 * L.capm + L.capf);
+    L.off_tkey = o; o += a256(8 * all);
+    L.off_tval = o; o += a256(4 * all);
+    L.off_mapkey = o; o += p.agg_mode == 1 ? a256(8 * (size_t)L.capf) : 0;
+    L.off_map = o; o += p.agg_mode == 1 ? a256(4 * (size_t)L.capf) : 0;
+  }
   L.off_lists = o; o += a256(4 * (size_t)(3 * F + 3));
   L.off_counts = o; o += a256(4 * 4);
-  L.off_map = o; o += p.agg_mode == 1 ? a256(4 * (size_t)(p.B * p.L * p.E)) : 0;
   L.total = o;
   return L;
 }
@@ -98,25 +176,80 @@ struct HopCtx {
   unsigned* err;
 };
 
+// ------------------------------------------------------------------ key stores
+// Dense (keys == nullptr): the slot of a key is the key.  Hash: open addressing with linear
+// probing over 2^k slots; a key claims its slot with atomicCAS from `empty`.  Probing is
+// bounded by the table size; a full table sets MKG_DEV_TABLE_FULL and drops the message.
+struct KeyTable {
+  unsigned long long* keys;
+  unsigned long long empty;
+  int64_t mask;
+  int shift;
+
+  __device__ __forceinline__ int64_t home(unsigned long long key) const {
+    return static_cast<int64_t>((key * 0x9E3779B97F4A7C15ull) >> shift);
+  }
+  __device__ __forceinline__ int64_t insert(unsigned long long key, unsigned* err) const {
+    if (keys == nullptr) return static_cast<int64_t>(key);
+    int64_t s = home(key);
+    for (int64_t probe = 0; probe <= mask; ++probe) {
+      unsigned long long cur = keys[s];
+      if (cur == key) return s;
+      if (cur == empty) {
+        unsigned long long prev = atomicCAS(keys + s, empty, key);
+        if (prev == empty || prev == key) return s;
+      }
+      s = (s + 1) & mask;
+    }
+    raise_flag(err, MKG_DEV_TABLE_FULL);
+    return -1;
+  }
+  __device__ __forceinline__ int64_t find(unsigned long long key) const {
+    if (keys == nullptr) return static_cast<int64_t>(key);
+    int64_t s = home(key);
+    for (int64_t probe = 0; probe <= mask; ++probe) {
+      unsigned long long cur = keys[s];
+      if (cur == key) return s;
+      if (cur == empty) return -1;
+      s = (s + 1) & mask;
+    }
+    return -1;
+  }
+};
+
+KeyTable dense_table() { return KeyTable{nullptr, 0ull, 0, 64}; }
+KeyTable hash_table(unsigned long long* keys, const HopLayout& L, int t) {
+  const int64_t n = L.slots(t);
+  return KeyTable{keys + L.base(t), L.empty(), n - 1, 64 - log2_exact(n)};
+}
+
 // ------------------------------------------------------------------ message sinks
 // Each sink receives one message: direction d, output key, value inputs and fact id.
 struct SumSink {
   float* val[2];
-  uint8_t* hit[2];
+  uint8_t* hit[2];  // dense only
+  KeyTable tab[2];
+  unsigned* err;
   __device__ __forceinline__ void msg(int d, int64_t key, float v, int64_t /*fact*/) {
-    atomicAdd(val[d] + key, v);
-    hit[d][key] = 1;
+    const int64_t s = tab[d].insert(static_cast<unsigned long long>(key), err);
+    if (s < 0) return;
+    atomicAdd(val[d] + s, v);
+    if (hit[d] != nullptr) hit[d][s] = 1;
   }
 };
 
 struct MaxSink {
   unsigned long long* pk[2];
+  KeyTable tab[2];
+  unsigned* err;
   __device__ __forceinline__ void msg(int d, int64_t key, float v, int64_t fact) {
-    atomicMax(pk[d] + key, pack_value_rank(v, static_cast<uint32_t>(fact)));
+    const int64_t s = tab[d].insert(static_cast<unsigned long long>(key), err);
+    if (s < 0) return;
+    atomicMax(pk[d] + s, pack_value_rank(v, static_cast<uint32_t>(fact)));
   }
 };
 
-// Output key of (b, l, dst), or -1 when dst lies outside the destination range.
+// Output key of (b, l, dst) is out_key0 + dst; dst must lie in the destination range.
 __device__ __forceinline__ int64_t out_key0(const HopCtx& c, int64_t b, int64_t l) { return (b * c.L + l) * c.Eo - c.lo; }
 __device__ __forceinline__ bool in_range(const HopCtx& c, int64_t e) {
   return static_cast<uint64_t>(e - c.lo) < static_cast<uint64_t>(c.Eo);
@@ -134,10 +267,10 @@ __device__ __forceinline__ bool load_entry(const Frontier& f, const HopCtx& c, i
 }
 
 // Sorts every frontier entry into tail / mid / hub lists (warp-aggregated appends) and
-// emits its identity-channel message into the ind slab (sum).
+// emits its identity-channel message into the ind store (sum).
 __global__ void classify_kernel(Frontier f, HopCtx c, int32_t* __restrict__ lists,
                                 int32_t* __restrict__ counts, float* __restrict__ ind_val,
-                                uint8_t* __restrict__ ind_hit) {
+                                uint8_t* __restrict__ ind_hit, KeyTable ind_tab) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -147,11 +280,13 @@ __global__ void classify_kernel(Frontier f, HopCtx c, int32_t* __restrict__ list
     if (i < f.F) {
       int64_t b, l, e;
       if (load_entry(f, c, i, b, l, e)) {
-        const int64_t key = out_key0(c, b, l) + e;
         if (ind_val != nullptr && in_range(c, e)) {
-          float v = c.wot_i ? 0.0f : f.v[i] * c.w[(b * c.L + l) * c.n + (c.n - 1)];
-          atomicAdd(ind_val + key, v);
-          ind_hit[key] = 1;
+          const int64_t s = ind_tab.insert(static_cast<unsigned long long>(out_key0(c, b, l) + e), c.err);
+          if (s >= 0) {
+            float v = c.wot_i ? 0.0f : f.v[i] * c.w[(b * c.L + l) * c.n + (c.n - 1)];
+            atomicAdd(ind_val + s, v);
+            if (ind_hit != nullptr) ind_hit[s] = 1;
+          }
         }
         int64_t d0 = c.dir[0].row_ptr[e + 1] - c.dir[0].row_ptr[e];
         int64_t d1 = c.dir[1].row_ptr[e + 1] - c.dir[1].row_ptr[e];
@@ -170,6 +305,27 @@ __global__ void classify_kernel(Frontier f, HopCtx c, int32_t* __restrict__ list
       pos0 = __shfl_sync(0xffffffffu, pos0, leader);
       if (cls == k) lists[k * f.F + pos0 + __popc(m & ((1u << lane) - 1u))] = static_cast<int32_t>(i);
     }
+  }
+}
+
+// Exact message counts: per entry min(out-degree, cap) per direction (cap <= 0: none).
+__global__ void count_messages_kernel(Frontier f, HopCtx c, unsigned long long* __restrict__ out) {
+  typedef cub::BlockReduce<long long, 256> Reduce;
+  __shared__ typename Reduce::TempStorage tmp;
+  long long m[2] = {0, 0};
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < f.F;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t b, l, e;
+    if (!load_entry(f, c, i, b, l, e)) continue;
+    for (int d = 0; d < 2; ++d) {
+      const int64_t deg = c.dir[d].row_ptr[e + 1] - c.dir[d].row_ptr[e];
+      m[d] += c.cap <= 0 ? 0 : (deg < c.cap ? deg : c.cap);
+    }
+  }
+  for (int d = 0; d < 2; ++d) {
+    long long t = Reduce(tmp).Sum(m[d]);
+    if (threadIdx.x == 0 && t != 0) atomicAdd(out + d, static_cast<unsigned long long>(t));
+    __syncthreads();
   }
 }
 
@@ -441,32 +597,83 @@ __global__ void __launch_bounds__(kTileThreads) tile_emit_kernel(
   }
 }
 
+// ---------------------------------------------------------------- hash compaction
+__global__ void fill_u64_kernel(unsigned long long* __restrict__ p, int64_t n, unsigned long long v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+// Claimed slots of a key-sorted table = position of the first empty key (empties sort last).
+__global__ void count_claimed_kernel(const unsigned long long* __restrict__ sorted, int64_t n,
+                                     unsigned long long empty, int64_t* __restrict__ out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int64_t lo = 0, hi = n;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (sorted[mid] < empty) lo = mid + 1; else hi = mid;
+  }
+  *out = lo;
+}
+
+__global__ void hash_emit_kernel(const unsigned long long* __restrict__ skey, const float* __restrict__ sval,
+                                 const unsigned long long* __restrict__ spk, int64_t count, int64_t L, int64_t Eo,
+                                 int64_t lo, int64_t* __restrict__ idx, float* __restrict__ out_val,
+                                 int64_t* __restrict__ arg) {
+  for (int64_t pos = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; pos < count;
+       pos += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t key = static_cast<int64_t>(skey[pos]);
+    const int64_t be = key / (L * Eo), rem = key % (L * Eo);
+    idx[pos] = be;
+    idx[count + pos] = rem / Eo;
+    idx[2 * count + pos] = rem % Eo + lo;
+    if (spk != nullptr) {
+      const unsigned long long p = spk[pos];
+      out_val[pos] = packed_value(p);
+      if (arg) arg[pos] = static_cast<int64_t>(packed_rank(p));
+    } else {
+      out_val[pos] = sval[pos];
+    }
+  }
+}
+
 // ---------------------------------------------------------------- backward
+// Gradient store of one hop: values per output key of ori / inv (dense slab or hash table).
+struct GradStore {
+  const float* val[2];
+  KeyTable tab[2];
+};
+
 // Incoming gradient keys must lie in the destination range (the forward produced no others).
-__global__ void scatter_grad_kernel(mkg_coo3 g, int64_t B, int64_t L, int64_t lo, int64_t Eo,
-                                    float* __restrict__ slab, unsigned* err) {
+__global__ void scatter_grad_kernel(mkg_coo3 g, int64_t B, int64_t L, int64_t lo, int64_t Eo, KeyTable tab,
+                                    float* __restrict__ vals, unsigned* err) {
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < g.nnz;
        k += (int64_t)gridDim.x * blockDim.x) {
     int64_t b = g.indices[k], l = g.indices[g.nnz + k], e = g.indices[2 * g.nnz + k] - lo;
     if (b < 0 || b >= B || l < 0 || l >= L || e < 0 || e >= Eo) { raise_flag(err, MKG_DEV_BAD_KEY); continue; }
-    atomicAdd(slab + (b * L + l) * Eo + e, g.values[k]);
+    const int64_t s = tab.insert(static_cast<unsigned long long>((b * L + l) * Eo + e), err);
+    if (s >= 0) atomicAdd(vals + s, g.values[k]);
   }
 }
 
 // Identity channel: grad_sp[i] = g_ind(key_i) * w[b,l,n-1] (initialises grad_sp) and
-// grad_w[b,l,n-1] += g_ind * sv (fastlog.cu:2608-2644); also fills the key -> entry map.
-__global__ void backward_entry_init_kernel(Frontier f, HopCtx c, const float* __restrict__ g_ind,
+// grad_w[b,l,n-1] += g_ind * sv (fastlog.cu:2608-2644); also fills the key -> entry map
+// (full-range keys) used by the argmax backward.
+__global__ void backward_entry_init_kernel(Frontier f, HopCtx c, KeyTable ind_tab, const float* __restrict__ g_ind,
                                            float* __restrict__ grad_sp, float* __restrict__ grad_w,
-                                           int32_t* __restrict__ entry_map) {
+                                           KeyTable map_tab, int32_t* __restrict__ entry_map) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < f.F;
        i += (int64_t)gridDim.x * blockDim.x) {
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) { grad_sp[i] = 0.0f; continue; }
-    if (entry_map) entry_map[(b * c.L + l) * c.E + e] = static_cast<int32_t>(i);
+    if (entry_map) {
+      const int64_t s = map_tab.insert(static_cast<unsigned long long>((b * c.L + l) * c.E + e), c.err);
+      if (s >= 0) entry_map[s] = static_cast<int32_t>(i);
+    }
     float gsp = 0.0f;
     if (!c.wot_i && in_range(c, e)) {
       const int64_t wi = (b * c.L + l) * c.n + (c.n - 1);
-      float g = g_ind[out_key0(c, b, l) + e];
+      const int64_t s = ind_tab.find(static_cast<unsigned long long>(out_key0(c, b, l) + e));
+      float g = s >= 0 ? g_ind[s] : 0.0f;
       if (g != 0.0f) {
         gsp = g * c.w[wi];
         atomicAdd(grad_w + wi, g * f.v[i]);
@@ -488,7 +695,7 @@ __device__ __forceinline__ float edge_grad_factor(const EdgeFactor& f, int64_t f
 // Sum backward per message: g at the output key, grad_sp += (g*m)*w (accumulated per
 // entry), grad_w += (g*m)*sv, grad_edge[fact] += (((g*sv)*w)*m)*factor.
 struct BwdVisit {
-  const float* gslab[2];
+  GradStore gs;
   float* grad_w;
   float* grad_edge;
   const EdgeFactor* f;
@@ -498,7 +705,9 @@ struct BwdVisit {
   int64_t lo, Eo;
   __device__ __forceinline__ void operator()(int d, int64_t dst, int64_t ch, float wv, int64_t fact) {
     if (static_cast<uint64_t>(dst - lo) >= static_cast<uint64_t>(Eo)) return;  // another shard's destination
-    float g = gslab[d][key0 + dst];
+    const int64_t s = gs.tab[d].find(static_cast<unsigned long long>(key0 + dst));
+    if (s < 0) return;
+    float g = gs.val[d][s];
     if (g == 0.0f) return;
     float m = (*f)(fact);
     float gm = g * m;
@@ -509,9 +718,8 @@ struct BwdVisit {
 };
 
 __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict__ list,
-                                const int32_t* __restrict__ count, const float* gori, const float* ginv,
-                                float* __restrict__ grad_sp, float* __restrict__ grad_w,
-                                float* __restrict__ grad_edge) {
+                                const int32_t* __restrict__ count, GradStore gs, float* __restrict__ grad_sp,
+                                float* __restrict__ grad_w, float* __restrict__ grad_edge) {
   const int64_t n = *count;
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n;
        k += (int64_t)gridDim.x * blockDim.x) {
@@ -519,8 +727,7 @@ __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict_
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) continue;
     const float* wrow = c.w + (b * c.L + l) * c.n;
-    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l),
-                 (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
+    BwdVisit vis{gs, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l), (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       for (int64_t p = p0; p < p1; ++p) visit_position(c, d, p, wrow, vis);
@@ -530,9 +737,8 @@ __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict_
 }
 
 __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
-    Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count,
-    const float* gori, const float* ginv, float* __restrict__ grad_sp, float* __restrict__ grad_w,
-    float* __restrict__ grad_edge) {
+    Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count, GradStore gs,
+    float* __restrict__ grad_sp, float* __restrict__ grad_w, float* __restrict__ grad_edge) {
   __shared__ int hist_all[kMidWarps][kNumBuckets];
   int* hist = hist_all[threadIdx.x >> 5];
   const int lane = threadIdx.x & 31;
@@ -544,8 +750,7 @@ __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
     int64_t b, l, e;
     if (!load_entry(f, c, i, b, l, e)) continue;
     const float* wrow = c.w + (b * c.L + l) * c.n;
-    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l),
-                 (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
+    BwdVisit vis{gs, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l), (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       if (p1 - p0 <= c.cap) {
@@ -560,9 +765,8 @@ __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
 }
 
 __global__ void __launch_bounds__(kHubThreads) bwd_hub_kernel(
-    Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count,
-    const float* gori, const float* ginv, float* __restrict__ grad_sp, float* __restrict__ grad_w,
-    float* __restrict__ grad_edge) {
+    Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count, GradStore gs,
+    float* __restrict__ grad_sp, float* __restrict__ grad_w, float* __restrict__ grad_edge) {
   __shared__ float wstage[kHubStageMax];
   __shared__ int hist[kNumBuckets];
   __shared__ float part[kHubThreads / 32];
@@ -578,8 +782,7 @@ __global__ void __launch_bounds__(kHubThreads) bwd_hub_kernel(
       __syncthreads();
       wrow = wstage;
     }
-    BwdVisit vis{{gori, ginv}, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l),
-                 (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
+    BwdVisit vis{gs, grad_w, grad_edge, &c.factor, f.v[i], out_key0(c, b, l), (b * c.L + l) * c.n, 0.0f, c.lo, c.Eo};
     for (int d = 0; d < 2; ++d) {
       const int64_t p0 = c.dir[d].row_ptr[e], p1 = c.dir[d].row_ptr[e + 1];
       if (p1 - p0 <= c.cap) {
@@ -600,25 +803,28 @@ __global__ void __launch_bounds__(kHubThreads) bwd_hub_kernel(
   }
 }
 
-// Max backward: the gradient of every output key goes to its argmax message only
-// (fastlog_kernel.py:153-167 + fastlog.cu:2646-2676).
+// Max backward (full destination range): the gradient of every output key goes to its
+// argmax message only (fastlog_kernel.py:153-167 + fastlog.cu:2646-2676).
 __global__ void bwd_argmax_kernel(int d, mkg_coo3 out, const int64_t* __restrict__ arg, Frontier f, HopCtx c,
-                                  const float* __restrict__ gslab, const int32_t* __restrict__ entry_map,
-                                  const int32_t* __restrict__ fhead, const int32_t* __restrict__ ftail,
-                                  const int16_t* __restrict__ frel, float* __restrict__ grad_sp,
-                                  float* __restrict__ grad_w, float* __restrict__ grad_edge) {
+                                  KeyTable gtab, const float* __restrict__ gvals, KeyTable map_tab,
+                                  const int32_t* __restrict__ entry_map, const int32_t* __restrict__ fhead,
+                                  const int32_t* __restrict__ ftail, const int16_t* __restrict__ frel,
+                                  float* __restrict__ grad_sp, float* __restrict__ grad_w,
+                                  float* __restrict__ grad_edge) {
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < out.nnz;
        k += (int64_t)gridDim.x * blockDim.x) {
     int64_t b = out.indices[k], l = out.indices[out.nnz + k], dst = out.indices[2 * out.nnz + k];
     if (b < 0 || b >= c.B || l < 0 || l >= c.L || dst < 0 || dst >= c.E) { raise_flag(c.err, MKG_DEV_BAD_KEY); continue; }
-    float g = gslab[(b * c.L + l) * c.E + dst];
+    const int64_t gs = gtab.find(static_cast<unsigned long long>((b * c.L + l) * c.E + dst));
+    float g = gs >= 0 ? gvals[gs] : 0.0f;
     if (g == 0.0f) continue;
     int64_t fact = arg[k];
     if (fact < 0 || fact >= c.T) { raise_flag(c.err, MKG_DEV_BAD_FACT); continue; }
     int64_t src = d ? ftail[fact] : fhead[fact];
     int64_t ch = (d ? c.r_size : 0) + frel[fact];
     if (src < 0 || src >= c.E || ch < 0 || ch >= c.n - 1) { raise_flag(c.err, MKG_DEV_BAD_COL); continue; }
-    int32_t i = entry_map[(b * c.L + l) * c.E + src];
+    const int64_t ms = map_tab.find(static_cast<unsigned long long>((b * c.L + l) * c.E + src));
+    int32_t i = ms >= 0 ? entry_map[ms] : -1;
     if (i < 0 || i >= f.F) { raise_flag(c.err, MKG_DEV_BAD_ENTRY); continue; }
     float m = c.factor(fact);
     float sv = f.v[i];
@@ -658,10 +864,31 @@ int check_hop_args(const mkg_graph* g, const mkg_frontier* f, const float* w, co
   MKG_REQUIRE(p->dst_hi <= p->dst_lo || (p->dst_lo >= 0 && p->dst_hi <= p->E),
               "hop: destination range [%lld, %lld) outside [0, E=%lld)", (long long)p->dst_lo,
               (long long)p->dst_hi, (long long)p->E);
+  MKG_REQUIRE(p->msg_bound >= 0 && p->msg_bound < (int64_t(1) << 40), "hop: msg_bound out of range");
+  MKG_REQUIRE(p->accum >= 0 && p->accum <= 2, "hop: accum must be 0, 1 or 2");
+  MKG_REQUIRE(p->B * p->L * p->E < (int64_t(1) << 62), "hop: key space B*L*E too large");
   return MKG_OK;
 }
 
 }  // namespace
+
+int hop_count_messages(const mkg_graph* g, const mkg_frontier* fr, const mkg_hop_params* p, int64_t* counts_out,
+                       unsigned* err, cudaStream_t st) {
+  MKG_REQUIRE(g && fr && p && counts_out, "hop_count_messages: null argument");
+  MKG_REQUIRE(p->B >= 1 && p->L >= 1 && p->E == g->num_entities, "hop_count_messages: bad shape");
+  MKG_REQUIRE(fr->nnz >= 0, "hop_count_messages: negative frontier size");
+  MKG_CUDA(cudaMemsetAsync(counts_out, 0, 2 * sizeof(int64_t), st));
+  if (fr->nnz == 0) return MKG_OK;
+  HopCtx c{};
+  c.B = p->B; c.L = p->L; c.E = p->E; c.cap = p->topk_edges; c.err = err;
+  c.dir[0] = make_dir(g->ori);
+  c.dir[1] = make_dir(g->inv);
+  Frontier f{fr->batch, fr->level, fr->entity, fr->value, fr->nnz};
+  count_messages_kernel<<<grid_for(fr->nnz, 256, persistent_blocks(4)), 256, 0, st>>>(
+      f, c, reinterpret_cast<unsigned long long*>(counts_out));
+  MKG_LAUNCHED("count_messages_kernel");
+  return MKG_OK;
+}
 
 size_t hop_forward_workspace_bytes(const mkg_hop_params* p, int64_t nnz) {
   return forward_layout(*p, nnz).total + 256;
@@ -677,58 +904,106 @@ int hop_forward(const mkg_graph* g, const mkg_frontier* fr, const float* w, cons
   MKG_REQUIRE(ws && ws_bytes >= lay.total, "hop_forward: workspace too small (%zu < %zu)", ws_bytes, lay.total);
   char* base = static_cast<char*>(ws);
   const int64_t BLE = lay.BLE, F = fr->nnz;
-  float* val = reinterpret_cast<float*>(base + lay.off_val);
-  uint8_t* hit = reinterpret_cast<uint8_t*>(base + lay.off_hit);
-  unsigned long long* pk = reinterpret_cast<unsigned long long*>(base + lay.off_pk);
   int32_t* lists = reinterpret_cast<int32_t*>(base + lay.off_lists);
   int32_t* counts = reinterpret_cast<int32_t*>(base + lay.off_counts);
-  int64_t* blk = reinterpret_cast<int64_t*>(base + lay.off_blk);
-  int64_t* blkoff = reinterpret_cast<int64_t*>(base + lay.off_blkoff);
   void* cubtmp = base + lay.off_cub;
-  const int nval = p->agg_mode == 1 ? 1 : 3;
-  const int64_t SV = lay.sval, SH = lay.shit, SP = lay.spk;
-  MKG_CUDA(cudaMemsetAsync(val, 0, 4 * (size_t)SV * nval, st));
-  MKG_CUDA(cudaMemsetAsync(hit, 0, (size_t)SH * nval, st));
-  if (p->agg_mode == 1) MKG_CUDA(cudaMemsetAsync(pk, 0, 8 * (size_t)SP * 2, st));
   MKG_CUDA(cudaMemsetAsync(counts, 0, 16, st));
-
   HopCtx c = make_ctx(g, w, ef, p, err);
   Frontier f{fr->batch, fr->level, fr->entity, fr->value, F};
-  // ind slab: the last value slab (index 2 for sum, 0 for max)
-  float* ind_val = val + SV * (nval - 1);
-  uint8_t* ind_hit = hit + SH * (nval - 1);
+  const int tb = persistent_blocks(8), mb = persistent_blocks(4), hb = persistent_blocks(2);
+
+  if (!lay.hash) {
+    float* val = reinterpret_cast<float*>(base + lay.off_val);
+    uint8_t* hit = reinterpret_cast<uint8_t*>(base + lay.off_hit);
+    unsigned long long* pk = reinterpret_cast<unsigned long long*>(base + lay.off_pk);
+    int64_t* blk = reinterpret_cast<int64_t*>(base + lay.off_blk);
+    int64_t* blkoff = reinterpret_cast<int64_t*>(base + lay.off_blkoff);
+    const int nval = p->agg_mode == 1 ? 1 : 3;
+    const int64_t SV = lay.sval, SH = lay.shit, SP = lay.spk;
+    MKG_CUDA(cudaMemsetAsync(val, 0, 4 * (size_t)SV * nval, st));
+    MKG_CUDA(cudaMemsetAsync(hit, 0, (size_t)SH * nval, st));
+    if (p->agg_mode == 1) MKG_CUDA(cudaMemsetAsync(pk, 0, 8 * (size_t)SP * 2, st));
+    // ind slab: the last value slab (index 2 for sum, 0 for max)
+    float* ind_val = val + SV * (nval - 1);
+    uint8_t* ind_hit = hit + SH * (nval - 1);
+    const KeyTable dn = dense_table();
+    if (F > 0) {
+      classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts, ind_val, ind_hit, dn);
+      MKG_LAUNCHED("classify_kernel");
+      if (p->agg_mode == 0) {
+        SumSink s{{val, val + SV}, {hit, hit + SH}, {dn, dn}, err};
+        push_tail_kernel<SumSink><<<tb, 256, 0, st>>>(f, c, lists, counts, s);
+        push_mid_kernel<SumSink><<<mb, kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, s);
+        push_hub_kernel<SumSink><<<hb, kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, s);
+      } else {
+        MaxSink s{{pk, pk + SP}, {dn, dn}, err};
+        push_tail_kernel<MaxSink><<<tb, 256, 0, st>>>(f, c, lists, counts, s);
+        push_mid_kernel<MaxSink><<<mb, kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, s);
+        push_hub_kernel<MaxSink><<<hb, kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, s);
+      }
+      MKG_LAUNCHED("push kernels");
+    }
+    // per-tile counts and offsets of the three outputs
+    for (int which = 0; which < 3; ++which) {
+      int kind;
+      const void* src;
+      if (p->agg_mode == 1 && which < 2) { kind = 1; src = pk + SP * which; }
+      else { kind = 0; src = hit + SH * (p->agg_mode == 1 ? 0 : which); }
+      int64_t* bc = blk + (lay.nblk + 1) * which;
+      int64_t* bo = blkoff + (lay.nblk + 1) * which;
+      MKG_CUDA(cudaMemsetAsync(bc + lay.nblk, 0, 8, st));
+      tile_count_kernel<<<(unsigned)lay.nblk, kTileThreads, 0, st>>>(kind, src, BLE, bc);
+      MKG_LAUNCHED("tile_count_kernel");
+      size_t b = lay.cub_bytes;
+      MKG_CUDA(cub::DeviceScan::ExclusiveSum(cubtmp, b, bc, bo, (int)(lay.nblk + 1), st));
+      store_total_kernel<<<1, 32, 0, st>>>(bo, lay.nblk, counts_out + which);
+      MKG_LAUNCHED("store_total_kernel");
+    }
+    return MKG_OK;
+  }
+
+  // hash tables
+  unsigned long long* tkey = reinterpret_cast<unsigned long long*>(base + lay.off_tkey);
+  float* tval = reinterpret_cast<float*>(base + lay.off_tval);
+  unsigned long long* tpk = reinterpret_cast<unsigned long long*>(base + lay.off_tpk);
+  unsigned long long* skey = reinterpret_cast<unsigned long long*>(base + lay.off_skey);
+  float* sval = reinterpret_cast<float*>(base + lay.off_sval);
+  unsigned long long* spk = reinterpret_cast<unsigned long long*>(base + lay.off_spk);
+  const int64_t all = 2 * lay.capm + lay.capf;
+  fill_u64_kernel<<<grid_for(all, 256, persistent_blocks(8)), 256, 0, st>>>(tkey, all, lay.empty());
+  MKG_LAUNCHED("fill_u64_kernel");
+  MKG_CUDA(cudaMemsetAsync(tval, 0, 4 * (size_t)all, st));
+  if (p->agg_mode == 1) MKG_CUDA(cudaMemsetAsync(tpk, 0, 8 * (size_t)(2 * lay.capm), st));
+  const KeyTable t0 = hash_table(tkey, lay, 0), t1 = hash_table(tkey, lay, 1), t2 = hash_table(tkey, lay, 2);
   if (F > 0) {
-    classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts, ind_val, ind_hit);
+    classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts,
+                                                                             tval + lay.base(2), nullptr, t2);
     MKG_LAUNCHED("classify_kernel");
-    const int tb = persistent_blocks(8), mb = persistent_blocks(4), hb = persistent_blocks(2);
     if (p->agg_mode == 0) {
-      SumSink s{{val, val + SV}, {hit, hit + SH}};
+      SumSink s{{tval + lay.base(0), tval + lay.base(1)}, {nullptr, nullptr}, {t0, t1}, err};
       push_tail_kernel<SumSink><<<tb, 256, 0, st>>>(f, c, lists, counts, s);
       push_mid_kernel<SumSink><<<mb, kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, s);
       push_hub_kernel<SumSink><<<hb, kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, s);
     } else {
-      MaxSink s{{pk, pk + SP}};
+      MaxSink s{{tpk + lay.base(0), tpk + lay.base(1)}, {t0, t1}, err};
       push_tail_kernel<MaxSink><<<tb, 256, 0, st>>>(f, c, lists, counts, s);
       push_mid_kernel<MaxSink><<<mb, kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, s);
       push_hub_kernel<MaxSink><<<hb, kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, s);
     }
     MKG_LAUNCHED("push kernels");
   }
-  // per-tile counts and offsets of the three outputs
-  for (int which = 0; which < 3; ++which) {
-    int kind;
-    const void* src;
-    if (p->agg_mode == 1 && which < 2) { kind = 1; src = pk + SP * which; }
-    else { kind = 0; src = hit + SH * (p->agg_mode == 1 ? 0 : which); }
-    int64_t* bc = blk + (lay.nblk + 1) * which;
-    int64_t* bo = blkoff + (lay.nblk + 1) * which;
-    MKG_CUDA(cudaMemsetAsync(bc + lay.nblk, 0, 8, st));
-    tile_count_kernel<<<(unsigned)lay.nblk, kTileThreads, 0, st>>>(kind, src, BLE, bc);
-    MKG_LAUNCHED("tile_count_kernel");
+  for (int t = 0; t < 3; ++t) {
+    const int64_t n = lay.slots(t), o = lay.base(t);
     size_t b = lay.cub_bytes;
-    MKG_CUDA(cub::DeviceScan::ExclusiveSum(cubtmp, b, bc, bo, (int)(lay.nblk + 1), st));
-    store_total_kernel<<<1, 32, 0, st>>>(bo, lay.nblk, counts_out + which);
-    MKG_LAUNCHED("store_total_kernel");
+    if (p->agg_mode == 1 && t < 2) {
+      MKG_CUDA(cub::DeviceRadixSort::SortPairs(cubtmp, b, tkey + o, skey + o, tpk + o, spk + o, (int)n, 0,
+                                               lay.bits, st));
+    } else {
+      MKG_CUDA(cub::DeviceRadixSort::SortPairs(cubtmp, b, tkey + o, skey + o, tval + o, sval + o, (int)n, 0,
+                                               lay.bits, st));
+    }
+    count_claimed_kernel<<<1, 32, 0, st>>>(skey + o, n, lay.empty(), counts_out + t);
+    MKG_LAUNCHED("count_claimed_kernel");
   }
   return MKG_OK;
 }
@@ -742,6 +1017,18 @@ int hop_emit(const mkg_hop_params* p, int64_t nnz, const void* ws, size_t ws_byt
   if (count == 0) return MKG_OK;
   MKG_REQUIRE(indices && values, "hop_emit: null output");
   const char* base = static_cast<const char*>(ws);
+  if (lay.hash) {
+    MKG_REQUIRE(count <= lay.slots(which), "hop_emit: count exceeds the table");
+    const int64_t o = lay.base(which);
+    const unsigned long long* skey = reinterpret_cast<const unsigned long long*>(base + lay.off_skey) + o;
+    const float* sval = reinterpret_cast<const float*>(base + lay.off_sval) + o;
+    const unsigned long long* spk =
+        (p->agg_mode == 1 && which < 2) ? reinterpret_cast<const unsigned long long*>(base + lay.off_spk) + o : nullptr;
+    hash_emit_kernel<<<grid_for(count, 256, persistent_blocks(8)), 256, 0, st>>>(
+        skey, sval, spk, count, p->L, range_extent(*p), range_lo(*p), indices, values, spk ? arg : nullptr);
+    MKG_LAUNCHED("hash_emit_kernel");
+    return MKG_OK;
+  }
   const int64_t BLE = lay.BLE;
   const float* val = reinterpret_cast<const float*>(base + lay.off_val);
   const uint8_t* hit = reinterpret_cast<const uint8_t*>(base + lay.off_hit);
@@ -782,39 +1069,65 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
                 "hop_backward: agg_mode 1 needs the forward outputs, their argmax facts and the fact table");
   HopLayout lay = backward_layout(*p, fr->nnz);
   MKG_REQUIRE(ws && ws_bytes >= lay.total, "hop_backward: workspace too small (%zu < %zu)", ws_bytes, lay.total);
+  const mkg_coo3* gl[3] = {g_ori, g_inv, g_ind};
+  if (lay.hash) {
+    for (int k = 0; k < 3; ++k)
+      MKG_REQUIRE(gl[k]->nnz <= lay.slots(k) / 2, "hop_backward: %lld gradient keys exceed msg_bound",
+                  (long long)gl[k]->nnz);
+  }
   char* base = static_cast<char*>(ws);
-  const int64_t BLE = lay.BLE, F = fr->nnz;
-  float* gs = reinterpret_cast<float*>(base + lay.off_val);
+  const int64_t F = fr->nnz;
   int32_t* lists = reinterpret_cast<int32_t*>(base + lay.off_lists);
   int32_t* counts = reinterpret_cast<int32_t*>(base + lay.off_counts);
+  float* vals[3];
+  KeyTable tabs[3];
+  KeyTable map_tab = dense_table();
   int32_t* emap = p->agg_mode == 1 ? reinterpret_cast<int32_t*>(base + lay.off_map) : nullptr;
-  MKG_CUDA(cudaMemsetAsync(gs, 0, 4 * (size_t)lay.sval * 3, st));
+  if (!lay.hash) {
+    float* gs = reinterpret_cast<float*>(base + lay.off_val);
+    MKG_CUDA(cudaMemsetAsync(gs, 0, 4 * (size_t)lay.sval * 3, st));
+    if (emap) MKG_CUDA(cudaMemsetAsync(emap, 0xff, 4 * (size_t)(p->B * p->L * p->E), st));
+    for (int k = 0; k < 3; ++k) { vals[k] = gs + lay.sval * k; tabs[k] = dense_table(); }
+  } else {
+    unsigned long long* tkey = reinterpret_cast<unsigned long long*>(base + lay.off_tkey);
+    float* tval = reinterpret_cast<float*>(base + lay.off_tval);
+    const int64_t all = 2 * lay.capm + lay.capf;
+    fill_u64_kernel<<<grid_for(all, 256, persistent_blocks(8)), 256, 0, st>>>(tkey, all, lay.empty());
+    MKG_LAUNCHED("fill_u64_kernel");
+    MKG_CUDA(cudaMemsetAsync(tval, 0, 4 * (size_t)all, st));
+    for (int k = 0; k < 3; ++k) { vals[k] = tval + lay.base(k); tabs[k] = hash_table(tkey, lay, k); }
+    if (emap) {
+      unsigned long long* mkey = reinterpret_cast<unsigned long long*>(base + lay.off_mapkey);
+      fill_u64_kernel<<<grid_for(lay.capf, 256, persistent_blocks(8)), 256, 0, st>>>(mkey, lay.capf, lay.empty());
+      MKG_LAUNCHED("fill_u64_kernel");
+      map_tab = KeyTable{mkey, lay.empty(), lay.capf - 1, 64 - log2_exact(lay.capf)};
+    }
+  }
   MKG_CUDA(cudaMemsetAsync(counts, 0, 16, st));
-  if (emap) MKG_CUDA(cudaMemsetAsync(emap, 0xff, 4 * (size_t)BLE, st));
   MKG_CUDA(cudaMemsetAsync(grad_w, 0, 4 * (size_t)(p->B * p->L * p->n), st));
   if (grad_edge) MKG_CUDA(cudaMemsetAsync(grad_edge, 0, 4 * (size_t)g->num_facts, st));
-  const mkg_coo3* gl[3] = {g_ori, g_inv, g_ind};
   for (int k = 0; k < 3; ++k) {
     if (gl[k]->nnz <= 0) continue;
     scatter_grad_kernel<<<grid_for(gl[k]->nnz, 256, persistent_blocks(8)), 256, 0, st>>>(
-        *gl[k], p->B, p->L, range_lo(*p), range_extent(*p), gs + lay.sval * k, err);
+        *gl[k], p->B, p->L, range_lo(*p), range_extent(*p), tabs[k], vals[k], err);
     MKG_LAUNCHED("scatter_grad_kernel");
   }
   if (F == 0) return MKG_OK;
   HopCtx c = make_ctx(g, w, ef, p, err);
   Frontier f{fr->batch, fr->level, fr->entity, fr->value, F};
   backward_entry_init_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(
-      f, c, gs + 2 * lay.sval, grad_sp, grad_w, emap);
+      f, c, tabs[2], vals[2], grad_sp, grad_w, map_tab, emap);
   MKG_LAUNCHED("backward_entry_init_kernel");
   if (p->agg_mode == 0) {
-    classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts, nullptr, nullptr);
+    classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts, nullptr, nullptr,
+                                                                             dense_table());
     MKG_LAUNCHED("classify_kernel");
-    bwd_tail_kernel<<<persistent_blocks(8), 256, 0, st>>>(f, c, lists, counts, gs, gs + lay.sval, grad_sp, grad_w,
-                                                          grad_edge);
-    bwd_mid_kernel<<<persistent_blocks(4), kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, gs, gs + lay.sval,
-                                                                    grad_sp, grad_w, grad_edge);
-    bwd_hub_kernel<<<persistent_blocks(2), kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, gs, gs + lay.sval,
-                                                                 grad_sp, grad_w, grad_edge);
+    GradStore gs{{vals[0], vals[1]}, {tabs[0], tabs[1]}};
+    bwd_tail_kernel<<<persistent_blocks(8), 256, 0, st>>>(f, c, lists, counts, gs, grad_sp, grad_w, grad_edge);
+    bwd_mid_kernel<<<persistent_blocks(4), kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, gs, grad_sp, grad_w,
+                                                                    grad_edge);
+    bwd_hub_kernel<<<persistent_blocks(2), kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, gs, grad_sp, grad_w,
+                                                                 grad_edge);
     MKG_LAUNCHED("backward push kernels");
   } else {
     const mkg_coo3* outs[2] = {out_ori, out_inv};
@@ -822,7 +1135,8 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
     for (int d = 0; d < 2; ++d) {
       if (outs[d]->nnz <= 0) continue;
       bwd_argmax_kernel<<<grid_for(outs[d]->nnz, 256, persistent_blocks(8)), 256, 0, st>>>(
-          d, *outs[d], args[d], f, c, gs + lay.sval * d, emap, fhead, ftail, frel, grad_sp, grad_w, grad_edge);
+          d, *outs[d], args[d], f, c, tabs[d], vals[d], map_tab, emap, fhead, ftail, frel, grad_sp, grad_w,
+          grad_edge);
       MKG_LAUNCHED("bwd_argmax_kernel");
     }
   }

@@ -23,6 +23,8 @@ int adjacency_build(const mkg_graph* g, mkg_adjacency adj, int64_t* num_tasks, v
 int adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, const mkg_edge_factor* f, cudaStream_t st);
 
 // mkg_hop.cu
+int hop_count_messages(const mkg_graph* g, const mkg_frontier* fr, const mkg_hop_params* p, int64_t* counts_out,
+                       unsigned* err, cudaStream_t st);
 size_t hop_forward_workspace_bytes(const mkg_hop_params* p, int64_t nnz);
 int hop_forward(const mkg_graph* g, const mkg_frontier* fr, const float* w, const mkg_edge_factor* ef,
                 const mkg_hop_params* p, void* ws, size_t ws_bytes, int64_t* counts_out, unsigned* err,

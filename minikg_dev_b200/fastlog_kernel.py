@@ -30,6 +30,14 @@ from . import _native as N
 from .graph import build_csr_structure, graph_from_csr  # noqa: F401  (re-exported)
 
 
+# Message store of the op: "auto" (key spaces above _HASH_MIN_KEYS count their messages -- one
+# extra host sync per hop -- and take hash tables when the count is far below the key space),
+# "dense" (always the key slab) or "hash" (always hash tables).
+ACCUM = "auto"
+ACCUM_MODES = {"auto": 0, "dense": 1, "hash": 2}
+_HASH_MIN_KEYS = 1 << 24
+
+
 def _frontier(sp_batch, sp_level, sp_entity, sp_value, keep):
     b = sp_batch.to(torch.int64).contiguous()
     l = sp_level.to(torch.int64).contiguous()
@@ -72,9 +80,19 @@ def _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values
     n = int(wf.shape[2])
     edge_weight = weight if (weight is not None and weight.numel() > 0) else None
     f = N.edge_factor(mask_values, edge_weight, bool(edge_weight_is_score), float(edge_weight_scale), keep)
-    params = (B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges), int(dst_lo), int(dst_hi))
+    params = [B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges), int(dst_lo), int(dst_hi), 0,
+              ACCUM_MODES[ACCUM]]
     p = N.HopParams(*params)
     nnz = int(b.numel())
+    extent = (int(dst_hi) - int(dst_lo)) if int(dst_hi) > int(dst_lo) else E
+    if ACCUM == "hash" or (ACCUM == "auto" and B * L * extent > _HASH_MIN_KEYS):
+        # exact message counts decide between the dense key slab and hash tables
+        mc = torch.empty(2, dtype=torch.int64, device=dev)
+        N.check(lib.mkg_hop_count_messages(ctypes.byref(g.struct), ctypes.byref(fr), ctypes.byref(p), mc.data_ptr(),
+                                           N.error_word(dev).data_ptr(), N.stream_handle(dev)), "hop_count_messages")
+        params[10] = max(1, int(mc.max().item()))
+        p = N.HopParams(*params)
+    params = tuple(params)
     ws = N.workspace(lib.mkg_hop_forward_workspace_bytes(ctypes.byref(p), nnz), dev)
     counts = torch.zeros(3, dtype=torch.int64, device=dev)
     err = N.error_word(dev)
@@ -118,7 +136,7 @@ def _hop_backward(ctx, grad_ori, grad_inv, grad_ind):
     """(grad_sp, grad_w, grad_edge_weight) of ``_hop_forward``."""
     lib = N.load()
     b, l, e, v, wf, oi_ori, oi_inv, oi_ind, arg_ori, arg_inv, mask_values, weight = ctx.saved_tensors
-    B, L, E, r_size, n, wot_i, agg_mode, topk, dst_lo, dst_hi = ctx.params
+    B, L, E, r_size, n, wot_i, agg_mode, topk, dst_lo, dst_hi, msg_bound, accum = ctx.params
     g = ctx.g
     dev = v.device
     keep = []

@@ -30,6 +30,14 @@ def _lib():
     _native.load()
 
 
+@pytest.fixture(params=["dense", "hash"])
+def accum(request, monkeypatch):
+    """The per-hop op's message store: key slab or hash tables."""
+    from minikg_dev_b200 import fastlog_kernel
+    monkeypatch.setattr(fastlog_kernel, "ACCUM", request.param)
+    return request.param
+
+
 def T(x, dtype=None):
     t = torch.from_numpy(np.ascontiguousarray(x))
     return t.to(DEV, dtype=dtype) if dtype is not None else t.to(DEV)
@@ -110,7 +118,7 @@ OP_CASES = [("sum_unc", UNC, 0, True), ("sum_cap", 7, 0, True), ("max_unc", UNC,
 
 @pytest.mark.parametrize("gname", ["g1", "g2"])
 @pytest.mark.parametrize("tag,cap,agg,is_score", OP_CASES)
-def test_hop_op_vs_golden(gname, tag, cap, agg, is_score):
+def test_hop_op_vs_golden(gname, tag, cap, agg, is_score, accum):
     """The op against the reference's own outputs on the golden inputs."""
     g = load_golden(gname)
     E, R = int(g["E"][0]), int(g["R"][0])
@@ -150,7 +158,7 @@ def _frontier(rng, B, L, E, per_row, dup_values=True):
 @pytest.mark.parametrize("gname", ["hubby", "g2"])
 @pytest.mark.parametrize("cap,agg", [(UNC, 0), (UNC, 1), (3, 0), (3, 1), (40, 0), (1, 1), (0, 0)])
 @pytest.mark.parametrize("variant", ["plain", "zero_mask", "wot_i", "logit"])
-def test_hop_op_vs_oracle(gname, cap, agg, variant):
+def test_hop_op_vs_oracle(gname, cap, agg, variant, accum):
     """Synthetic inputs with hubs (block-per-entry path), masked facts (explicit zero
     outputs), the wot_i flag and the sigmoid edge path."""
     h, r, t, E, R = GRAPHS[gname]
@@ -197,7 +205,8 @@ def test_hop_op_vs_oracle(gname, cap, agg, variant):
     np.testing.assert_allclose(res["grad_edge"], ge, rtol=RTOL, atol=ATOL)
 
 
-def test_hop_op_argmax_facts_bit_exact():
+@pytest.mark.parametrize("mode", ["dense", "hash"])
+def test_hop_op_argmax_facts_bit_exact(mode):
     """The argmax message per key (smallest fact id among equal maxima) through the C ABI."""
     import ctypes
     from minikg_dev_b200 import _native as N
@@ -219,6 +228,12 @@ def test_hop_op_argmax_facts_bit_exact():
     f = N.edge_factor(None, T(ew), True, 1.0, keep)
     p = N.HopParams(B, L, E, R, n, 0, 1, UNC)
     lib = N.load()
+    if mode == "hash":
+        mc = torch.empty(2, dtype=torch.int64, device=DEV)
+        N.check(lib.mkg_hop_count_messages(ctypes.byref(g.struct), ctypes.byref(fr), ctypes.byref(p), mc.data_ptr(),
+                                           N.error_word(DEV).data_ptr(), None), "count")
+        p.msg_bound, p.accum = int(mc.max()), 2
+        assert int(mc.sum()) == O.count_messages((O.keys3(fb, fl, fe, L, E), fv), csr, w, L, E, R)
     ws = N.workspace(lib.mkg_hop_forward_workspace_bytes(ctypes.byref(p), fb.shape[0]), DEV)
     counts = torch.zeros(3, dtype=torch.int64, device=DEV)
     N.check(lib.mkg_hop_forward(ctypes.byref(g.struct), ctypes.byref(fr), wt.data_ptr(), ctypes.byref(f),
@@ -237,7 +252,7 @@ def test_hop_op_argmax_facts_bit_exact():
         np.testing.assert_array_equal(val.cpu().numpy(), fwd[name][1])
 
 
-def test_hop_op_empty_frontier():
+def test_hop_op_empty_frontier(accum):
     from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
     h, r, t, E, R = GRAPHS["g1"]
     csr = csr_dev(O.build_csr_structure(h, t, r, E))
@@ -246,6 +261,34 @@ def test_hop_op_empty_frontier():
     o, i, d = FastLogFunctionSparse3DTopK.apply(e, e, e, torch.empty(0, device=DEV), w, *csr,
                                                 torch.ones(h.shape[0], device=DEV), None, 2, 2, E, R, False, UNC, 0)
     assert o._nnz() == 0 and i._nnz() == 0 and d._nnz() == 0
+
+
+def test_hash_table_overflow_is_reported_not_faulted():
+    """A message bound below the real count fills the table: flagged, messages dropped, no fault."""
+    import ctypes
+    from minikg_dev_b200 import _native as N
+    from minikg_dev_b200.graph import DeviceGraph
+    h, r, t, E, R = GRAPHS["hubby"]
+    csr = O.build_csr_structure(h, t, r, E)
+    g = DeviceGraph(csr_dev(csr), E, R)
+    rng = np.random.default_rng(2)
+    B, L, n = 4, 4, 2 * R + 1
+    fb, fl, fe, fv = _frontier(rng, B, L, E, per_row=40)
+    keep = [T(fb), T(fl), T(fe), T(fv)]
+    fr = N.Frontier(*(x.data_ptr() for x in keep), fb.shape[0])
+    w = T(np.full((B, L, n), 0.05, np.float32))
+    f = N.edge_factor(None, None, True, 1.0, keep)
+    p = N.HopParams(B, L, E, R, n, 0, 0, UNC, 0, 0, 1, 2)  # bound 1: a 1024-slot table per direction
+    lib = N.load()
+    ws = N.workspace(lib.mkg_hop_forward_workspace_bytes(ctypes.byref(p), fb.shape[0]), DEV)
+    counts = torch.zeros(3, dtype=torch.int64, device=DEV)
+    N.check(lib.mkg_hop_forward(ctypes.byref(g.struct), ctypes.byref(fr), w.data_ptr(), ctypes.byref(f),
+                                ctypes.byref(p), ws.data_ptr(), ws.numel(), counts.data_ptr(),
+                                N.error_word(DEV).data_ptr(), None), "hop_forward")
+    with pytest.raises(RuntimeError, match="ran out of slots"):
+        N.raise_device_errors(DEV)
+    assert counts.tolist()[0] <= 1024
+    assert torch.ones(4, device=DEV).sum().item() == 4.0
 
 
 def test_bad_index_is_reported_not_faulted():
@@ -402,7 +445,7 @@ def test_decode_topk_ties_and_short_rows():
 # ----------------------------------------------------------------------------- drop-in
 @pytest.mark.parametrize("gname", ["g1", "g2"])
 @pytest.mark.parametrize("tag,cap,topk_nodes", [("pr_unc", UNC, 0), ("pr_cap", 9, 0), ("pr_prune", UNC, 40)])
-def test_kernel_sparse_scores_drop_in(gname, tag, cap, topk_nodes):
+def test_kernel_sparse_scores_drop_in(gname, tag, cap, topk_nodes, accum):
     """The reference's hop driver signature, with a duck-typed model / graph / args."""
     from types import SimpleNamespace
     from minikg_dev_b200.proof import kernel_sparse_scores

@@ -39,9 +39,16 @@ def _golden_g2():
     return g["head"], g["rel"], g["tail"], int(g["E"][0]), int(g["R"][0])
 
 
+@pytest.fixture(params=["dense", "hash"])
+def accum(request, monkeypatch):
+    from minikg_dev_b200 import fastlog_kernel
+    monkeypatch.setattr(fastlog_kernel, "ACCUM", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("graph", ["g2", "hubby"])
 @pytest.mark.parametrize("cap,agg", [(O.UNCAPPED, 0), (3, 0), (40, 0), (O.UNCAPPED, 1), (3, 1)])
-def test_hop_range_partition_union(graph, cap, agg):
+def test_hop_range_partition_union(graph, cap, agg, accum):
     from minikg_dev_b200.fastlog_kernel import HopRange
     from minikg_dev_b200.graph import DeviceGraph
     from minikg_dev_b200.sharded import message_in_counts, plan_dst_ranges
