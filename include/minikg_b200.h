@@ -203,6 +203,11 @@ typedef struct mkg_hop_params {
   /* 0: choose as above; 1: always the dense slab; 2: hash tables (needs msg_bound >= the
    * real message count of each direction, else MKG_DEV_TABLE_FULL). */
   int64_t accum;
+  /* 1 (agg_mode 0 only): ori, inv and ind are reduced into one output (which = 0; outputs
+   * 1 and 2 are empty), i.e. sum_sparse3d_concat(ori, inv, ind) of the hop loop
+   * (src/fastlog_bridge.py:26-42) done by the op; msg_bound must then bound ori + inv +
+   * entries.  The backward takes that output's gradient as g_ori (g_inv, g_ind ignored). */
+  int64_t merge_outputs;
 } mkg_hop_params;
 
 /* Exact message counts of one hop (no counterpart in the reference, whose count kernels
@@ -309,6 +314,14 @@ int mkg_proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int
  * 729-758, decode_core.py:350-363). */
 int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails,
                     float* scores, int64_t* counts, mkg_stream stream);
+
+/* out[s] = values[seg_ptr[s]] + values[seg_ptr[s] + 1] + ... + values[seg_ptr[s+1] - 1],
+ * added one by one in index order in fp32 (device pointers; seg_ptr [nseg + 1], int64).
+ * The row sums of norm_sp_3d (src/model_mmDRUM_kernel_sp.py:39-52) over a coalesced COO
+ * whose (b, l) rows are contiguous, in the order the reference's CPU index_put_
+ * accumulates them, so the max-aggregation decode stays bit-exact on sparse frontiers. */
+int mkg_segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out,
+                            mkg_stream stream);
 
 #ifdef __cplusplus
 }

@@ -63,7 +63,7 @@ class Adjacency(C.Structure):
 class HopParams(C.Structure):
     _fields_ = [("B", i64), ("L", i64), ("E", i64), ("r_size", i64), ("n", i64), ("wot_i", i32),
                 ("agg_mode", i32), ("topk_edges", i64), ("dst_lo", i64), ("dst_hi", i64), ("msg_bound", i64),
-                ("accum", i64)]
+                ("accum", i64), ("merge_outputs", i64)]
 
 
 class ProofParams(C.Structure):
@@ -105,6 +105,7 @@ SIGNATURES = {
     "mkg_proof_decode_max": (C.c_int, [P(Graph), P(Adjacency), vp, vp, P(ProofParams), i64, vp, vp, vp, vp, vp,
                                        C.c_size_t, vp, vp]),
     "mkg_decode_topk": (C.c_int, [vp, i64, i64, i64, vp, vp, vp, vp]),
+    "mkg_segment_sum_ordered": (C.c_int, [vp, i64, vp, vp, vp]),
 }
 
 _lib = None

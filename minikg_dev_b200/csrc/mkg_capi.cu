@@ -38,7 +38,7 @@ using mkg::set_error;
 static cudaStream_t S(mkg_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 
 MKG_API const char* mkg_last_error(void) { return mkg::g_last_error; }
-MKG_API int mkg_abi_version(void) { return 3; }
+MKG_API int mkg_abi_version(void) { return 4; }
 
 MKG_API size_t mkg_csr_build_workspace_bytes(int64_t T, int64_t E, int64_t R) {
   return mkg::csr_build_workspace_bytes(T, E, R);
@@ -133,4 +133,8 @@ MKG_API int mkg_proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, c
 MKG_API int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails, float* scores,
                             int64_t* counts, mkg_stream st) {
   return mkg::decode_topk(raw, B, E, topk, tails, scores, counts, S(st));
+}
+MKG_API int mkg_segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out,
+                                    mkg_stream st) {
+  return mkg::segment_sum_ordered(seg_ptr, nseg, values, out, S(st));
 }

@@ -866,6 +866,8 @@ int check_hop_args(const mkg_graph* g, const mkg_frontier* f, const float* w, co
               (long long)p->dst_hi, (long long)p->E);
   MKG_REQUIRE(p->msg_bound >= 0 && p->msg_bound < (int64_t(1) << 40), "hop: msg_bound out of range");
   MKG_REQUIRE(p->accum >= 0 && p->accum <= 2, "hop: accum must be 0, 1 or 2");
+  MKG_REQUIRE(p->merge_outputs == 0 || (p->merge_outputs == 1 && p->agg_mode == 0),
+              "hop: merge_outputs needs agg_mode 0");
   MKG_REQUIRE(p->B * p->L * p->E < (int64_t(1) << 62), "hop: key space B*L*E too large");
   return MKG_OK;
 }
@@ -923,15 +925,16 @@ int hop_forward(const mkg_graph* g, const mkg_frontier* fr, const float* w, cons
     MKG_CUDA(cudaMemsetAsync(val, 0, 4 * (size_t)SV * nval, st));
     MKG_CUDA(cudaMemsetAsync(hit, 0, (size_t)SH * nval, st));
     if (p->agg_mode == 1) MKG_CUDA(cudaMemsetAsync(pk, 0, 8 * (size_t)SP * 2, st));
-    // ind slab: the last value slab (index 2 for sum, 0 for max)
-    float* ind_val = val + SV * (nval - 1);
-    uint8_t* ind_hit = hit + SH * (nval - 1);
+    // ind slab: the last value slab (index 2 for sum, 0 for max); merged: all into slab 0
+    const bool merge = p->merge_outputs != 0;
+    float* ind_val = merge ? val : val + SV * (nval - 1);
+    uint8_t* ind_hit = merge ? hit : hit + SH * (nval - 1);
     const KeyTable dn = dense_table();
     if (F > 0) {
       classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts, ind_val, ind_hit, dn);
       MKG_LAUNCHED("classify_kernel");
       if (p->agg_mode == 0) {
-        SumSink s{{val, val + SV}, {hit, hit + SH}, {dn, dn}, err};
+        SumSink s{{val, merge ? val : val + SV}, {hit, merge ? hit : hit + SH}, {dn, dn}, err};
         push_tail_kernel<SumSink><<<tb, 256, 0, st>>>(f, c, lists, counts, s);
         push_mid_kernel<SumSink><<<mb, kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, s);
         push_hub_kernel<SumSink><<<hb, kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, s);
@@ -943,8 +946,9 @@ int hop_forward(const mkg_graph* g, const mkg_frontier* fr, const float* w, cons
       }
       MKG_LAUNCHED("push kernels");
     }
-    // per-tile counts and offsets of the three outputs
-    for (int which = 0; which < 3; ++which) {
+    // per-tile counts and offsets of the three outputs (merged: output 0 only)
+    if (merge) MKG_CUDA(cudaMemsetAsync(counts_out + 1, 0, 2 * sizeof(int64_t), st));
+    for (int which = 0; which < (merge ? 1 : 3); ++which) {
       int kind;
       const void* src;
       if (p->agg_mode == 1 && which < 2) { kind = 1; src = pk + SP * which; }
@@ -974,13 +978,15 @@ int hop_forward(const mkg_graph* g, const mkg_frontier* fr, const float* w, cons
   MKG_LAUNCHED("fill_u64_kernel");
   MKG_CUDA(cudaMemsetAsync(tval, 0, 4 * (size_t)all, st));
   if (p->agg_mode == 1) MKG_CUDA(cudaMemsetAsync(tpk, 0, 8 * (size_t)(2 * lay.capm), st));
-  const KeyTable t0 = hash_table(tkey, lay, 0), t1 = hash_table(tkey, lay, 1), t2 = hash_table(tkey, lay, 2);
+  const bool merge = p->merge_outputs != 0;
+  const KeyTable t0 = hash_table(tkey, lay, 0);
+  const KeyTable t1 = merge ? t0 : hash_table(tkey, lay, 1), t2 = merge ? t0 : hash_table(tkey, lay, 2);
   if (F > 0) {
-    classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts,
-                                                                             tval + lay.base(2), nullptr, t2);
+    classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(
+        f, c, lists, counts, tval + lay.base(merge ? 0 : 2), nullptr, t2);
     MKG_LAUNCHED("classify_kernel");
     if (p->agg_mode == 0) {
-      SumSink s{{tval + lay.base(0), tval + lay.base(1)}, {nullptr, nullptr}, {t0, t1}, err};
+      SumSink s{{tval + lay.base(0), tval + lay.base(merge ? 0 : 1)}, {nullptr, nullptr}, {t0, t1}, err};
       push_tail_kernel<SumSink><<<tb, 256, 0, st>>>(f, c, lists, counts, s);
       push_mid_kernel<SumSink><<<mb, kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, s);
       push_hub_kernel<SumSink><<<hb, kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, s);
@@ -992,7 +998,8 @@ int hop_forward(const mkg_graph* g, const mkg_frontier* fr, const float* w, cons
     }
     MKG_LAUNCHED("push kernels");
   }
-  for (int t = 0; t < 3; ++t) {
+  if (merge) MKG_CUDA(cudaMemsetAsync(counts_out + 1, 0, 2 * sizeof(int64_t), st));
+  for (int t = 0; t < (merge ? 1 : 3); ++t) {
     const int64_t n = lay.slots(t), o = lay.base(t);
     size_t b = lay.cub_bytes;
     if (p->agg_mode == 1 && t < 2) {
@@ -1069,9 +1076,10 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
                 "hop_backward: agg_mode 1 needs the forward outputs, their argmax facts and the fact table");
   HopLayout lay = backward_layout(*p, fr->nnz);
   MKG_REQUIRE(ws && ws_bytes >= lay.total, "hop_backward: workspace too small (%zu < %zu)", ws_bytes, lay.total);
+  const bool merge = p->merge_outputs != 0;
   const mkg_coo3* gl[3] = {g_ori, g_inv, g_ind};
   if (lay.hash) {
-    for (int k = 0; k < 3; ++k)
+    for (int k = 0; k < (merge ? 1 : 3); ++k)
       MKG_REQUIRE(gl[k]->nnz <= lay.slots(k) / 2, "hop_backward: %lld gradient keys exceed msg_bound",
                   (long long)gl[k]->nnz);
   }
@@ -1106,7 +1114,11 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
   MKG_CUDA(cudaMemsetAsync(counts, 0, 16, st));
   MKG_CUDA(cudaMemsetAsync(grad_w, 0, 4 * (size_t)(p->B * p->L * p->n), st));
   if (grad_edge) MKG_CUDA(cudaMemsetAsync(grad_edge, 0, 4 * (size_t)g->num_facts, st));
-  for (int k = 0; k < 3; ++k) {
+  if (merge) {  // one gradient store serves ori, inv and ind
+    vals[1] = vals[2] = vals[0];
+    tabs[1] = tabs[2] = tabs[0];
+  }
+  for (int k = 0; k < (merge ? 1 : 3); ++k) {
     if (gl[k]->nnz <= 0) continue;
     scatter_grad_kernel<<<grid_for(gl[k]->nnz, 256, persistent_blocks(8)), 256, 0, st>>>(
         *gl[k], p->B, p->L, range_lo(*p), range_extent(*p), tabs[k], vals[k], err);

@@ -1206,6 +1206,28 @@ int proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int64_t
   return MKG_OK;
 }
 
+namespace {
+// One thread per segment: a sequential fp32 chain in index order.
+__global__ void segment_sum_ordered_kernel(const int64_t* __restrict__ seg_ptr, int64_t nseg,
+                                           const float* __restrict__ values, float* __restrict__ out) {
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < nseg;
+       s += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.0f;
+    for (int64_t i = seg_ptr[s]; i < seg_ptr[s + 1]; ++i) acc = __fadd_rn(acc, values[i]);
+    out[s] = acc;
+  }
+}
+}  // namespace
+
+int segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st) {
+  MKG_REQUIRE(nseg >= 0, "segment_sum_ordered: negative segment count");
+  if (nseg == 0) return MKG_OK;
+  MKG_REQUIRE(seg_ptr && values && out, "segment_sum_ordered: null argument");
+  segment_sum_ordered_kernel<<<grid_for(nseg, 128, persistent_blocks(8)), 128, 0, st>>>(seg_ptr, nseg, values, out);
+  MKG_LAUNCHED("segment_sum_ordered_kernel");
+  return MKG_OK;
+}
+
 int decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails, float* scores,
                 int64_t* counts, cudaStream_t st) {
   MKG_REQUIRE(raw && tails && scores && counts, "decode_topk: null argument");

@@ -81,7 +81,7 @@ def _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values
     edge_weight = weight if (weight is not None and weight.numel() > 0) else None
     f = N.edge_factor(mask_values, edge_weight, bool(edge_weight_is_score), float(edge_weight_scale), keep)
     params = [B, L, E, r_size, n, 1 if wot_i else 0, int(agg_mode), int(topk_edges), int(dst_lo), int(dst_hi), 0,
-              ACCUM_MODES[ACCUM]]
+              ACCUM_MODES[ACCUM], 0]
     p = N.HopParams(*params)
     nnz = int(b.numel())
     extent = (int(dst_hi) - int(dst_lo)) if int(dst_hi) > int(dst_lo) else E
@@ -136,7 +136,7 @@ def _hop_backward(ctx, grad_ori, grad_inv, grad_ind):
     """(grad_sp, grad_w, grad_edge_weight) of ``_hop_forward``."""
     lib = N.load()
     b, l, e, v, wf, oi_ori, oi_inv, oi_ind, arg_ori, arg_inv, mask_values, weight = ctx.saved_tensors
-    B, L, E, r_size, n, wot_i, agg_mode, topk, dst_lo, dst_hi, msg_bound, accum = ctx.params
+    B, L, E, r_size, n, wot_i, agg_mode, topk, dst_lo, dst_hi, msg_bound, accum, merge = ctx.params
     g = ctx.g
     dev = v.device
     keep = []

@@ -7,6 +7,9 @@
 scores.  ``decode_max`` runs the max-aggregation loop (op with ``agg_mode=1`` →
 ``sparse3d_max(ind, ori, inv)`` → ``norm_sp_3d`` / ``norm_sp_3d_max``) and the decode
 ordering (bound, score desc, tail asc, top-k) in ``mkg_proof_decode_max``.
+``decode_max_sparse`` runs the same loop hop by hop on sparse states (any edge cap, graphs
+whose dense state does not fit), with ``norm_sp_3d`` row sums added in key order
+(``mkg_segment_sum_ordered``) so its result stays bit-exact too.
 
 ``kernel_sparse_scores(model, heads, rels, graph, args, is_training)`` keeps the
 reference signature.  Hops the fused loop does not cover (an edge cap, entity pruning
@@ -21,9 +24,10 @@ from dataclasses import dataclass
 import torch
 
 from . import _native as N
-from .fastlog_kernel import FastLogFunctionSparse3DTopK
+from .fastlog_kernel import HopRange
 from .graph import DeviceGraph, build_csr_structure
-from .sparse_reducers import normalize_sparse3d, prune_sparse3d_active_entities, sum_sp_3d, sum_sparse3d_concat
+from .sparse_reducers import (max_sp_3d, normalize_sparse3d, prune_sparse3d_active_entities, sparse3d_max, sum_sp_3d,
+                              sum_sparse3d_concat)
 
 UNCAPPED = 1 << 60
 
@@ -194,6 +198,78 @@ def decode_topk(raw: torch.Tensor, topk: int):
     return tails, scores, counts
 
 
+def norm_sp_3d_ordered(s: torch.Tensor) -> torch.Tensor:
+    """norm_sp_3d (src/model_mmDRUM_kernel_sp.py:39-52) with each (b, l) row sum added in key
+    order, as the reference's CPU index_put_ accumulates: value / clamp(row sum, 1e-7),
+    zeros dropped."""
+    lib = N.load()
+    s = s.coalesce()
+    idx, val = s.indices(), s.values().to(torch.float32).contiguous()
+    B, L, _ = s.shape
+    rows = (idx[0] * L + idx[1]).contiguous()
+    seg = torch.searchsorted(rows, torch.arange(B * L + 1, device=rows.device, dtype=rows.dtype)).contiguous()
+    denom = torch.empty(B * L, dtype=torch.float32, device=val.device)
+    N.check(lib.mkg_segment_sum_ordered(seg.data_ptr(), B * L, val.data_ptr(), denom.data_ptr(),
+                                        N.stream_handle(val.device)), "segment_sum_ordered")
+    out = val / denom.clamp(min=1e-7)[rows]
+    keep = out != 0
+    return torch.sparse_coo_tensor(idx[:, keep], out[keep], s.shape, is_coalesced=True)
+
+
+def sparse_topk(keys: torch.Tensor, vals: torch.Tensor, B: int, E: int, k: int):
+    """Decode order on sparse raw scores (keys ``b * E + e``): bound ``1 - exp(-max(x, 0))``
+    (exp rounded from double, then the fp32 difference), score descending, tail ascending,
+    ``k`` per query (proof.py:642-649, 729-758; decode_core.py:350-363).
+    Returns (tails [B, k] -1 padded, scores [B, k], counts [B])."""
+    dev = vals.device
+    sc = 1.0 - torch.exp(-vals.detach().clamp_min(0.0).double()).float()
+    b, t = keys // E, keys % E
+    o = torch.sort(t, stable=True).indices
+    o = o[torch.sort(sc[o], descending=True, stable=True).indices]
+    o = o[torch.sort(b[o], stable=True).indices]
+    bs = b[o]
+    pos = torch.arange(bs.numel(), device=dev) - torch.searchsorted(bs, bs)
+    take = pos < k
+    tails = torch.full((B, k), -1, dtype=torch.int64, device=dev)
+    scores = torch.zeros((B, k), dtype=torch.float32, device=dev)
+    tails[bs[take], pos[take]] = t[o][take]
+    scores[bs[take], pos[take]] = sc[o][take]
+    return tails, scores, torch.bincount(bs[take], minlength=B)
+
+
+@torch.no_grad()
+def decode_max_sparse(graph: DeviceGraph, heads: torch.Tensor, w_hops: torch.Tensor, topk: int,
+                      edge_scores: torch.Tensor | None, mask: torch.Tensor | None = None, cap: int = UNCAPPED,
+                      is_score: bool = True, scale: float = 1.0):
+    """The max-aggregation loop of src/model_mmDRUM_kernel_sp.py:388-445 hop by hop on sparse
+    states (op with ``agg_mode=1`` and the edge cap -> ``sparse3d_max(ind, ori, inv)`` ->
+    ``norm_sp_3d`` between hops, ``norm_sp_3d_max`` after the last), then ``sparse_topk``.
+    Returns (final sparse [B, E] raw scores, tails, scores, counts)."""
+    K, B, L, n = (int(x) for x in w_hops.shape)
+    E = graph.num_entities
+    dev = graph.device
+    hd = heads.to(device=dev, dtype=torch.int64)
+    state = torch.sparse_coo_tensor(
+        torch.stack([torch.arange(B, device=dev).repeat_interleave(L), torch.arange(L, device=dev).repeat(B),
+                     hd.repeat_interleave(L)]), torch.ones(B * L, device=dev), [B, L, E]).coalesce()
+    mk = mask if mask is not None else torch.ones((), dtype=torch.float32, device=dev)
+    wf = w_hops.to(device=dev, dtype=torch.float32)
+    final = None
+    for h in range(K):
+        idx = state.indices()
+        o, i, d = HopRange.apply(idx[0], idx[1], idx[2], state.values(), wf[h], graph, mk, edge_scores, B, L, False,
+                                 int(cap), 1, bool(is_score), float(scale), 0, 0)
+        s = sparse3d_max(d, o, i)
+        if h < K - 1:
+            state = norm_sp_3d_ordered(s)
+        else:
+            final = max_sp_3d(norm_sp_3d_ordered(s)).coalesce()
+    fi = final.indices()
+    keys = fi[0] * E + fi[1]
+    tails, scores, counts = sparse_topk(keys, final.values(), B, E, int(topk))
+    return final, tails, scores, counts
+
+
 # ---------------------------------------------------------------------------- drop-in
 def _device_graph_for(model, graph) -> DeviceGraph:
     """The model-level CSR cache of proof.py:496-506, holding a ``DeviceGraph``."""
@@ -236,21 +312,46 @@ def kernel_sparse_scores(model, heads, rels, graph, args, is_training: bool, den
         w_hops = torch.stack([torch.softmax(rule_logits[:, h] / model.tau_1, dim=-1) for h in range(K)])
         out, _ = HopLoopSum.apply(w_hops, edge_scores, heads, g, mask, is_score, scale, 0.0)
         return out if dense else out.to_sparse_coo().coalesce()
-    # hop by hop, as the reference composes it
+    w_hops = [torch.softmax(rule_logits[:, hop] / model.tau_1, dim=-1) for hop in range(K)]
+    if not (is_training and p_drop > 0):
+        # any cap / prune: the sparse loop fused around the op (merged outputs, written-out backward)
+        from .sparse_loop import sparse_proof_scores
+        out, _ = sparse_proof_scores(g, heads, torch.stack(w_hops), edge_scores, mask, is_score, scale, topk_edges,
+                                     topk_nodes, 0.0, dense=dense)
+        return out
+    # dropout while training: hop by hop, as the reference composes it
+    out = sparse_hop_loop(g, heads, w_hops, edge_scores, mask, is_score, scale, topk_edges, topk_nodes,
+                          dropout=model.dropout)
+    return out.to_dense() if dense else out
+
+
+def sparse_hop_loop(g: DeviceGraph, heads: torch.Tensor, w_hops, edge_scores: torch.Tensor | None,
+                    mask: torch.Tensor | None, is_score: bool = True, scale: float = 1.0, topk_edges: int = UNCAPPED,
+                    topk_nodes: int = 0, dropout=None, msgs_out: list | None = None) -> torch.Tensor:
+    """The sum hop loop of proof.py:569-609 on sparse states: per hop the prune, the op
+    (``FastLogFunctionSparse3DTopK`` semantics: any cap, dense or hash message store),
+    ``sum_sparse3d_concat`` and ``normalize_sparse3d(.., 0, "mass")`` (+ dropout when
+    given), then ``sum_sp_3d``.  Differentiable in ``w_hops`` and ``edge_scores``.  With
+    ``msgs_out`` the exact message count of every hop is appended (device scalars)."""
+    B, L, _ = (int(x) for x in w_hops[0].shape)
+    E, R = g.num_entities, g.num_relations
     dev = g.device
     state = torch.sparse_coo_tensor(
         torch.stack([torch.arange(B, device=dev).repeat_interleave(L), torch.arange(L, device=dev).repeat(B),
                      heads.to(dev).long().repeat_interleave(L)]),
-        torch.ones(B * L, device=dev), [B, L, E], is_coalesced=True)
+        torch.ones(B * L, device=dev), [B, L, E]).coalesce()
     mvals = mask if mask is not None else torch.ones((), dtype=torch.float32, device=dev)
-    for hop in range(K):
+    if msgs_out is not None:
+        c = g.csr
+        deg = [(c[0][1:] - c[0][:-1]).long(), (c[4][1:] - c[4][:-1]).long()]
+    for w_t in w_hops:
         state = prune_sparse3d_active_entities(state, topk_nodes)
-        w_t = torch.softmax(rule_logits[:, hop] / model.tau_1, dim=-1)
-        o, i, d = FastLogFunctionSparse3DTopK.apply(state.indices()[0], state.indices()[1], state.indices()[2],
-                                                    state.values(), w_t, *g.csr, mvals, edge_scores, B, L, E, R,
-                                                    False, topk_edges, 0, is_score, scale)
+        idx = state.indices()
+        if msgs_out is not None:
+            msgs_out.append(sum(torch.clamp(d_[idx[2]], max=max(int(topk_edges), 0)).sum() for d_ in deg))
+        o, i, d = HopRange.apply(idx[0], idx[1], idx[2], state.values(), w_t, g, mvals, edge_scores, B, L, False,
+                                 int(topk_edges), 0, bool(is_score), float(scale), 0, 0)
         state = normalize_sparse3d(sum_sparse3d_concat(o, i, d), 0.0, "mass")
-        if is_training:
-            state = torch.sparse_coo_tensor(state.indices(), model.dropout(state.values()), state.shape).coalesce()
-    out = sum_sp_3d(state)
-    return out.to_dense() if dense else out
+        if dropout is not None:
+            state = torch.sparse_coo_tensor(state.indices(), dropout(state.values()), state.shape).coalesce()
+    return sum_sp_3d(state)

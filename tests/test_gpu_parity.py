@@ -374,6 +374,39 @@ def test_fused_loop_vs_oracle(gname, B, L, K):
     np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("gname", ["hubby", "g2"])
+@pytest.mark.parametrize("cap,topk_nodes", [(UNC, 0), (9, 0), (40, 150), (3, 0), (0, 0)])
+def test_sparse_loop_vs_oracle(gname, cap, topk_nodes, accum):
+    """The fused sparse hop loop (merged op outputs, written-out backward) against the oracle."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.sparse_loop import sparse_proof_scores
+    h, r, t, E, R = GRAPHS[gname]
+    rng = np.random.default_rng(cap % 997 + topk_nodes)
+    csr = O.build_csr_structure(h, t, r, E)
+    B, L, K, n = 6, 3, 3, 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    scores = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    mask = np.ones(h.shape[0], bool)
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R, cap=cap, topk_nodes=topk_nodes)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    wt = T(w_hops).requires_grad_(True)
+    sc = T(scores).requires_grad_(True)
+    out, msgs = sparse_proof_scores(dg, T(heads), wt, sc, None, True, 1.0, cap, topk_nodes)
+    out = out.coalesce()
+    idx = out.indices().cpu().numpy()
+    np.testing.assert_array_equal(idx[0] * E + idx[1], final[0])
+    np.testing.assert_allclose(out.values().detach().cpu().numpy(), final[1], rtol=RTOL, atol=ATOL)
+    assert msgs.cpu().tolist() == [O.count_messages(tr["state"], csr, w_hops[k], L, E, R, cap=cap)
+                                   for k, tr in enumerate(trace)]
+    seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
+    (out.values() * T(seed)).sum().backward()
+    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
+                                  num_facts=h.shape[0])
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+
+
 @pytest.mark.parametrize("gname", ["g1", "g2"])
 def test_max_decode_vs_golden_bit_exact(gname):
     from minikg_dev_b200.graph import DeviceGraph
@@ -422,6 +455,33 @@ def test_max_decode_vs_oracle_bit_exact(gname):
     np.testing.assert_array_equal(res.tails.cpu().numpy(), ot)
     np.testing.assert_array_equal(res.scores.cpu().numpy(), osc)
     np.testing.assert_array_equal(res.counts.cpu().numpy(), oc)
+
+
+@pytest.mark.parametrize("gname", ["g1", "g2"])
+@pytest.mark.parametrize("tag,cap", [("dec_unc", UNC), ("dec_cap", 9)])
+def test_max_decode_sparse_vs_golden_bit_exact(gname, tag, cap, accum):
+    """The hop-by-hop max decode (any cap) against the reference's own outputs, on the
+    reference's CSR (its order inside a capped group decides which edges are taken)."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import decode_max_sparse
+    g = load_golden(gname)
+    E, R = int(g["E"][0]), int(g["R"][0])
+    heads, logits, scores = g["pr_heads"], g["pr_logits"], g["pr_scores"]
+    B, K, L, n = logits.shape
+    dg = DeviceGraph(csr_dev(tuple(g[f"csr{k}"] for k in range(16))), E, R)
+    k = g[tag + "_tails"].shape[1]
+    final, tails, sc, counts = decode_max_sparse(dg, T(heads), T(_w_hops_from_logits(logits)), k, T(scores),
+                                                 mask=torch.ones(g["head"].shape[0], device=DEV), cap=cap)
+    idx = final.indices().cpu().numpy()
+    np.testing.assert_array_equal(idx, g[tag + "_final_idx"])
+    np.testing.assert_array_equal(final.values().cpu().numpy(), g[tag + "_final_val"])
+    keys = idx[0] * E + idx[1]
+    ot, osc, oc = O.decode_topk((keys, final.values().cpu().numpy()), B, E, k)
+    np.testing.assert_array_equal(tails.cpu().numpy(), ot)
+    np.testing.assert_array_equal(sc.cpu().numpy(), osc)
+    np.testing.assert_array_equal(counts.cpu().numpy(), oc)
+    np.testing.assert_array_equal(tails.cpu().numpy(), g[tag + "_tails"])
+    np.testing.assert_allclose(sc.cpu().numpy(), g[tag + "_scores"], rtol=0, atol=6e-8)
 
 
 def test_decode_topk_ties_and_short_rows():

@@ -66,7 +66,8 @@ STRUCTS = {
     "mkg_adjacency": ("Adjacency", ["pull_ptr", "pull", "push_ptr", "push", "pull_tasks", "num_pull_tasks",
                                     "push_tasks", "num_push_tasks"]),
     "mkg_hop_params": ("HopParams", ["B", "L", "E", "r_size", "n", "wot_i", "agg_mode", "topk_edges", "dst_lo",
-                                    "dst_hi", "msg_bound", "accum"]),
+                                    "dst_hi", "msg_bound", "accum",
+                                    "merge_outputs"]),
     "mkg_proof_params": ("ProofParams", ["B", "L", "E", "R", "hops", "topk_edges", "state_threshold", "reserved",
                                          "fwd_events", "bwd_events"]),
 }

@@ -155,6 +155,26 @@ def _duck(kg, wl, logits, scores_t):
     return model, graph, args
 
 
+@pytest.mark.parametrize("name", ["kg_large", "kg_web@0.02"])
+def test_capped_max_decode_subset_vs_oracle(name):
+    """The capped hop-by-hop max decode (the large graphs' decode path) bit-exact on a query subset."""
+    from minikg_dev_b200.proof import decode_max_sparse
+    wl, kg, csr, dg, inp = workload(name)
+    E, R, L = kg.num_entities, kg.num_relations, wl.L
+    w = inp.rule_weights[:, :SUB]
+    final, tails, sc, counts = decode_max_sparse(dg, T(inp.heads[:SUB]), T(w), 100, T(inp.edge_scores),
+                                                 cap=wl.topk_edges)
+    want, _ = O.proof_max_forward(inp.heads[:SUB], w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
+                                  cap=wl.topk_edges)
+    idx = final.indices().cpu().numpy()
+    np.testing.assert_array_equal(idx[0] * E + idx[1], want[0])
+    np.testing.assert_array_equal(final.values().cpu().numpy(), want[1])
+    ot, osc, oc = O.decode_topk(want, SUB, E, 100)
+    np.testing.assert_array_equal(tails.cpu().numpy(), ot)
+    np.testing.assert_array_equal(sc.cpu().numpy(), osc)
+    np.testing.assert_array_equal(counts.cpu().numpy(), oc)
+
+
 def test_hop_op_keys_beyond_32_bits():
     """kg_large at its full B x L: output keys b*L*E + l*E + e exceed 2^32 (256 x 4 x 4.59M)."""
     from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
