@@ -323,6 +323,12 @@ int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_
 int mkg_segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out,
                             mkg_stream stream);
 
+/* out[s] = sum of values[seg_ptr[s] .. seg_ptr[s+1]) (fp32, tree order; one block per
+ * segment): the row sums of normalize_sparse3d (drum.py:31-50) and of its gradient on a
+ * key-sorted sparse state, without atomics on the few row bins.  No reference counterpart
+ * (the reference coalesces and index_puts). */
+int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, mkg_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

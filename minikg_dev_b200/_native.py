@@ -106,6 +106,7 @@ SIGNATURES = {
                                        C.c_size_t, vp, vp]),
     "mkg_decode_topk": (C.c_int, [vp, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_segment_sum_ordered": (C.c_int, [vp, i64, vp, vp, vp]),
+    "mkg_segment_sum": (C.c_int, [vp, i64, vp, vp, vp]),
 }
 
 _lib = None
@@ -179,6 +180,18 @@ def raise_device_errors(device: torch.device) -> None:
         w.zero_()
         names = [v for k, v in DEV_ERR_NAMES.items() if bits & k]
         raise RuntimeError("minikg_b200 kernel rejected its input: " + "; ".join(names))
+
+
+def segment_sum(seg_ptr: torch.Tensor, values: torch.Tensor, ordered: bool = False) -> torch.Tensor:
+    """Per-segment sums of ``values`` (``seg_ptr`` int64 [nseg + 1], device tensors);
+    ``ordered``: each segment added one by one in index order (bit-reproducible)."""
+    v = values.detach().to(torch.float32).contiguous()
+    sp = seg_ptr.to(torch.int64).contiguous()
+    nseg = int(sp.numel()) - 1
+    out = torch.empty(max(nseg, 0), dtype=torch.float32, device=v.device)
+    fn = load().mkg_segment_sum_ordered if ordered else load().mkg_segment_sum
+    check(fn(sp.data_ptr(), nseg, v.data_ptr(), out.data_ptr(), stream_handle(v.device)), "segment_sum")
+    return out
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:

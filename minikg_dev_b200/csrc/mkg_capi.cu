@@ -134,6 +134,9 @@ MKG_API int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk
                             int64_t* counts, mkg_stream st) {
   return mkg::decode_topk(raw, B, E, topk, tails, scores, counts, S(st));
 }
+MKG_API int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, mkg_stream st) {
+  return mkg::segment_sum(seg_ptr, nseg, values, out, S(st));
+}
 MKG_API int mkg_segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out,
                                     mkg_stream st) {
   return mkg::segment_sum_ordered(seg_ptr, nseg, values, out, S(st));

@@ -55,5 +55,6 @@ int proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int64_t
 int decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails, float* scores,
                 int64_t* counts, cudaStream_t st);
 int segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st);
+int segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st);
 
 }  // namespace mkg

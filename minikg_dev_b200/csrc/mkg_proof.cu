@@ -1217,7 +1217,30 @@ __global__ void segment_sum_ordered_kernel(const int64_t* __restrict__ seg_ptr, 
     out[s] = acc;
   }
 }
+// One block per segment: strided partial sums, then a block reduction.
+__global__ void __launch_bounds__(256) segment_sum_kernel(const int64_t* __restrict__ seg_ptr, int64_t nseg,
+                                                          const float* __restrict__ values, float* __restrict__ out) {
+  typedef cub::BlockReduce<float, 256> Reduce;
+  __shared__ typename Reduce::TempStorage tmp;
+  for (int64_t s = blockIdx.x; s < nseg; s += gridDim.x) {
+    const int64_t b = seg_ptr[s], e = seg_ptr[s + 1];
+    float acc = 0.0f;
+    for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) acc += values[i];
+    const float tot = Reduce(tmp).Sum(acc);
+    if (threadIdx.x == 0) out[s] = tot;
+    __syncthreads();
+  }
+}
 }  // namespace
+
+int segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st) {
+  MKG_REQUIRE(nseg >= 0, "segment_sum: negative segment count");
+  if (nseg == 0) return MKG_OK;
+  MKG_REQUIRE(seg_ptr && values && out, "segment_sum: null argument");
+  segment_sum_kernel<<<grid_for(nseg, 1, persistent_blocks(8)), 256, 0, st>>>(seg_ptr, nseg, values, out);
+  MKG_LAUNCHED("segment_sum_kernel");
+  return MKG_OK;
+}
 
 int segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st) {
   MKG_REQUIRE(nseg >= 0, "segment_sum_ordered: negative segment count");

@@ -202,15 +202,12 @@ def norm_sp_3d_ordered(s: torch.Tensor) -> torch.Tensor:
     """norm_sp_3d (src/model_mmDRUM_kernel_sp.py:39-52) with each (b, l) row sum added in key
     order, as the reference's CPU index_put_ accumulates: value / clamp(row sum, 1e-7),
     zeros dropped."""
-    lib = N.load()
     s = s.coalesce()
     idx, val = s.indices(), s.values().to(torch.float32).contiguous()
     B, L, _ = s.shape
     rows = (idx[0] * L + idx[1]).contiguous()
-    seg = torch.searchsorted(rows, torch.arange(B * L + 1, device=rows.device, dtype=rows.dtype)).contiguous()
-    denom = torch.empty(B * L, dtype=torch.float32, device=val.device)
-    N.check(lib.mkg_segment_sum_ordered(seg.data_ptr(), B * L, val.data_ptr(), denom.data_ptr(),
-                                        N.stream_handle(val.device)), "segment_sum_ordered")
+    seg = torch.searchsorted(rows, torch.arange(B * L + 1, device=rows.device, dtype=rows.dtype))
+    denom = N.segment_sum(seg, val, ordered=True)
     out = val / denom.clamp(min=1e-7)[rows]
     keep = out != 0
     return torch.sparse_coo_tensor(idx[:, keep], out[keep], s.shape, is_coalesced=True)

@@ -30,7 +30,7 @@ from .graph import DeviceGraph
 
 
 class _HopState:
-    __slots__ = ("keys_in", "vals_in", "prune_sel", "idx_y", "keys_y", "y", "d", "keep", "params", "n_pre")
+    __slots__ = ("keys_in", "vals_in", "prune_sel", "idx_y", "keys_y", "y", "d", "keep", "params", "n_pre", "seg")
 
 
 def _frontier_arrays(keys: torch.Tensor, L: int, E: int):
@@ -149,8 +149,9 @@ class SparseHopLoop(autograd.Function):
             msgs.append(m)
             y = st.y
             rows = st.keys_y // E
+            st.seg = torch.searchsorted(rows, torch.arange(B * L + 1, device=dev, dtype=rows.dtype))
             nz = y != 0
-            d = torch.zeros(B * L, dtype=torch.float32, device=dev).index_add_(0, rows[nz], y[nz])
+            d = N.segment_sum(st.seg, y)  # rows are contiguous in key order; zeros add nothing
             x = y / d[rows] * d.clamp_max(1.0)[rows]
             keep = nz & (x != 0)
             if threshold > 0:
@@ -193,9 +194,9 @@ class SparseHopLoop(autograd.Function):
             c = d.clamp_max(1.0)
             q = y / dr
             g_q = gx * c[rows]
-            g_c = torch.zeros(B * L, dtype=torch.float32, device=dev).index_add_(0, rows[nz], (gx * q)[nz])
-            g_d = torch.zeros(B * L, dtype=torch.float32, device=dev).index_add_(
-                0, rows[nz], (-(g_q * y) / (dr * dr))[nz])
+            zero = torch.zeros_like(y)
+            g_c = N.segment_sum(st.seg, torch.where(nz, gx * q, zero))
+            g_d = N.segment_sum(st.seg, torch.where(nz, -(g_q * y) / (dr * dr), zero))
             g_d = g_d + torch.where(d <= 1.0, g_c, torch.zeros_like(g_c))
             gy = torch.where(nz, g_q / dr + g_d[rows], torch.zeros_like(y))
             grad_sp, gw, ge = _op_backward(g, st, ctx.wf[h], ctx.factor, gy, ctx.want_edge)
