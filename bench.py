@@ -48,8 +48,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-queries", type=int, default=0, help="0: pick automatically")
-    ap.add_argument("--engine", default="fused", choices=["fused", "sharded"],
-                    help="sharded: destination-partitioned capped hop loop (kg_large / kg_web shapes)")
+    ap.add_argument("--engine", default="fused", choices=["fused", "sharded", "capped"],
+                    help="sharded: destination-partitioned capped hop loop (kg_large / kg_web shapes); "
+                         "capped: only the capped sparse loop of the workload (for profiling)")
     return ap.parse_args()
 
 
@@ -482,6 +483,46 @@ def run_sharded(a, wl, kg, rank, world, local_rank):
             "messages_per_step": M, "clocks": clocks.summary()}), flush=True)
 
 
+def run_capped(a, wl, kg):
+    """Only the capped (cap 100) sparse hop loop, fwd+bwd: the command profiles use."""
+    import torch
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.sparse_loop import sparse_proof_scores
+    dev = torch.device("cuda", 0)
+    B, L, K, E = wl.B, wl.L, wl.hops, kg.num_entities
+    inp = hop_inputs(kg, B, L, K, seed=0)
+    g = DeviceGraph.from_triples(torch.from_numpy(kg.head).to(dev), torch.from_numpy(kg.rel).to(dev),
+                                 torch.from_numpy(kg.tail).to(dev), E, kg.num_relations)
+    heads = torch.from_numpy(inp.heads).to(dev)
+    w0 = torch.from_numpy(inp.rule_weights).to(dev)
+    s0 = torch.from_numpy(inp.edge_scores).to(dev)
+    G = torch.randn((B, E), device=dev, generator=torch.Generator(device=dev).manual_seed(1234))
+
+    def step():
+        wt = w0.detach().requires_grad_(True)
+        sc = s0.detach().requires_grad_(True)
+        out, msgs = sparse_proof_scores(g, heads, wt, sc, None, True, 1.0, 100, 0)
+        oi = out.indices()
+        (out.values() * G[oi[0], oi[1]]).sum().backward()
+        return msgs
+
+    for _ in range(max(3, a.warmup)):
+        msgs = step()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(a.steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    M = int(msgs.sum().item())
+    print(json.dumps({"engine": "capped", "workload": wl.name, "edge_cap": 100, "messages_per_step": M,
+                      "ms_per_step": statistics.mean(ms), "gteps": M / (statistics.mean(ms) / 1e3) / 1e9}))
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -491,6 +532,9 @@ def main():
     kg = workload_graph(a.workload, seed=0)
     if a.impl == "reference":
         run_reference(a, wl, kg, rank, world)
+        return
+    if a.engine == "capped":
+        run_capped(a, wl, kg)
         return
     distributed = world > 1 or a.engine == "sharded"
     if distributed:
