@@ -7,11 +7,12 @@ complete rows).  Per hop:
 
 1. the sparse frontier is all-gathered: sizes first, then one padded payload of
    ``(key, value)`` per rank (``key = (b * L + l) * E + e``);
-2. ``HopRange`` expands every gathered entry but produces only messages whose destination
-   rank k owns, into a key space of ``B x L x (hi_k - lo_k)``; outputs of different ranks are
-   disjoint, so no reduction of messages is needed;
-3. the concat-sum of (ori, inv, ind) is local; the mass normalisation (drum.py:31-50) divides
-   by per-(b, l) column sums that are all-reduced; the optional state threshold is local;
+2. the per-hop op (``MergedHop``: ori, inv and ind reduced into one store, i.e. the concat-sum)
+   expands every gathered entry but produces only messages whose destination rank k owns,
+   into a key space of ``B x L x (hi_k - lo_k)``; outputs of different ranks are disjoint, so
+   no reduction of messages is needed;
+3. the mass normalisation (drum.py:31-50) divides by per-(b, l) column sums that are
+   all-reduced; the optional state threshold is local;
 4. what remains is rank k's part of the next frontier.
 
 After the last hop the per-query sum over rules (proof.py:609) is local, and top-k decoding
@@ -163,25 +164,20 @@ class ShardSpec:
         return self.bounds[self.rank + 1]
 
 
+# hop_fn(frontier keys, frontier values, w_h [B, L, n], lo, hi) -> (keys, values): the sum of
+# the op's ori, inv and ind outputs whose destinations lie in [lo, hi), keys ascending
 HopFn = Callable[..., tuple]
 
 
-def cuda_hop_fn(graph, mask, edge_scores, cap: int, is_score: bool, scale: float, agg_mode: int = 0) -> HopFn:
-    """The per-hop op of this package (``HopRange`` on the resident ``DeviceGraph``)."""
-    from .fastlog_kernel import HopRange
+def cuda_hop_fn(graph, mask, edge_scores, cap: int, is_score: bool, scale: float) -> HopFn:
+    """The per-hop op of this package on the resident ``DeviceGraph``: ``MergedHop`` (ori, inv
+    and ind reduced into one key-sorted output) restricted to the rank's destinations."""
+    from .sparse_loop import MergedHop
 
-    def hop(b, l, e, v, w_h, lo, hi):
-        B, L = int(w_h.shape[0]), int(w_h.shape[1])
-        mk = mask if mask is not None else torch.ones((), dtype=torch.float32, device=v.device)
-        return HopRange.apply(b, l, e, v, w_h, graph, mk, edge_scores, B, L, False, int(cap), int(agg_mode),
-                              bool(is_score), float(scale), int(lo), int(hi))
+    def hop(keys, vals, w_h, lo, hi):
+        return MergedHop.apply(keys, vals, w_h, edge_scores, graph, mask, bool(is_score), float(scale), int(cap),
+                               int(lo), int(hi))
     return hop
-
-
-def _keys_vals(sp: torch.Tensor, L: int, E: int):
-    sp = sp.coalesce()
-    idx = sp.indices()
-    return (idx[0] * L + idx[1]) * E + idx[2], sp.values()
 
 
 def _coalesce_sum(keys: torch.Tensor, vals: torch.Tensor):
@@ -252,12 +248,10 @@ def sharded_proof_scores(spec: ShardSpec, hop_fn: HopFn, heads: torch.Tensor, w_
         if topk_nodes > 0:
             keys, vals = _prune_global(keys, vals, E, topk_nodes, spec)
         k_all, v_all = _GatherFrontier.apply(keys, vals, spec.group)
-        be, e = k_all // E, k_all % E
         if msg_counter is not None:
-            msgs_out.append(msg_counter(e))
-        o, i, d = hop_fn(be // L, be % L, e, v_all, w_rep[h], lo, hi)
-        parts = [_keys_vals(t, L, E) for t in (o, i, d)]
-        keys, y = _coalesce_sum(torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts]))
+            msgs_out.append(msg_counter(k_all % E))
+        # the op's (ori + inv + ind) for this rank's destinations, coalesced in key order
+        keys, y = hop_fn(k_all, v_all, w_rep[h], lo, hi)
         # normalize_sparse3d(.., 0, "mass") with global column sums
         nz = y != 0
         keys, y = keys[nz], y[nz]

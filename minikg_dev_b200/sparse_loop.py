@@ -55,8 +55,9 @@ def _prune(keys, vals, E: int, topk_nodes: int):
     return keys[sel], vals[sel], sel
 
 
-def _op_forward(g: DeviceGraph, keys, vals, w_h, factor, B, L, cap, keep_alive):
-    """The merged op: returns (indices [3, U], keys [U], values [U], params, message count)."""
+def _op_forward(g: DeviceGraph, keys, vals, w_h, factor, B, L, cap, keep_alive, lo: int = 0, hi: int = 0):
+    """The merged op (destinations in [lo, hi) when hi > lo): returns (indices [3, U], keys [U],
+    values [U], params, message count)."""
     lib = N.load()
     dev = vals.device
     E = g.num_entities
@@ -65,7 +66,7 @@ def _op_forward(g: DeviceGraph, keys, vals, w_h, factor, B, L, cap, keep_alive):
     keep_alive += [b, l, e, v]
     fr = N.Frontier(b.data_ptr(), l.data_ptr(), e.data_ptr(), v.data_ptr(), int(keys.numel()))
     n = int(w_h.shape[-1])
-    params = [B, L, E, g.num_relations, n, 0, 0, int(cap), 0, 0, 0, FK.ACCUM_MODES[FK.ACCUM], 1]
+    params = [B, L, E, g.num_relations, n, 0, 0, int(cap), int(lo), int(hi), 0, FK.ACCUM_MODES[FK.ACCUM], 1]
     p = N.HopParams(*params)
     st = N.stream_handle(dev)
     mc = torch.empty(2, dtype=torch.int64, device=dev)
@@ -116,6 +117,39 @@ def _op_backward(g: DeviceGraph, st: _HopState, w_h, factor, gy, want_edge: bool
                                  N.ptr(grad_edge), ws.data_ptr(), ws.numel(), N.error_word(dev).data_ptr(),
                                  N.stream_handle(dev)), "hop_backward")
     return grad_sp, grad_w, grad_edge
+
+
+class MergedHop(autograd.Function):
+    """One hop with ori, inv and ind reduced into one output (``sum_sparse3d_concat`` of the
+    three), restricted to destinations in [lo, hi) when hi > lo: ``(keys, values)`` with keys
+    ``(b * L + l) * E + e`` in ascending order.  Gradients for the frontier values, ``w`` and
+    the edge scores.  The frontier keys need not be sorted."""
+
+    @staticmethod
+    def forward(ctx, keys, vals, w_h, edge_scores, graph: DeviceGraph, mask, is_score: bool, scale: float, cap: int,
+                lo: int, hi: int):
+        B, L = int(w_h.shape[0]), int(w_h.shape[1])
+        keep_alive = []
+        ew = edge_scores.detach().reshape(-1) if edge_scores is not None else None
+        factor = N.edge_factor(mask, ew, bool(is_score), float(scale), keep_alive)
+        wf = w_h.detach().to(torch.float32).contiguous()
+        st = _HopState()
+        st.keys_in, st.vals_in = keys, vals.detach()
+        st.idx_y, st.keys_y, y, st.params, _ = _op_forward(graph, keys, vals, wf, factor, B, L, cap, keep_alive,
+                                                           lo, hi)
+        ctx.st, ctx.g, ctx.factor, ctx.keep_alive, ctx.wf = st, graph, factor, keep_alive, wf
+        ctx.want_edge = edge_scores is not None and ctx.needs_input_grad[3]
+        ctx.edge_shape = tuple(edge_scores.shape) if edge_scores is not None else None
+        ctx.edge_dtype = edge_scores.dtype if edge_scores is not None else None
+        ctx.mark_non_differentiable(st.keys_y)
+        return st.keys_y, y
+
+    @staticmethod
+    def backward(ctx, _g_keys, gy):
+        grad_sp, gw, ge = _op_backward(ctx.g, ctx.st, ctx.wf, ctx.factor, gy, ctx.want_edge)
+        N.raise_device_errors(gy.device)
+        ge = ge.view(ctx.edge_shape).to(ctx.edge_dtype) if ge is not None else None
+        return None, grad_sp, gw, ge, None, None, None, None, None, None, None
 
 
 class SparseHopLoop(autograd.Function):

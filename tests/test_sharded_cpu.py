@@ -41,46 +41,38 @@ def _case(seed=0, B=5, L=3, K=3):
 
 
 class _OracleRangeHop(torch.autograd.Function):
-    """The oracle hop with outputs restricted to destinations in [lo, hi)."""
+    """The oracle hop (ori + inv + ind, concat-summed) with outputs restricted to destinations
+    in [lo, hi): ``(keys, values)``, keys ascending."""
 
     @staticmethod
-    def forward(ctx, b, l, e, v, w_h, ew, csr, E, R, cap, lo, hi):
+    def forward(ctx, keys, v, w_h, ew, csr, E, R, cap, lo, hi):
         B, L, _ = w_h.shape
-        bn, ln, en, vn = (x.detach().numpy() for x in (b, l, e, v))
+        bn, ln, en = O.split3(keys.numpy(), L, E)
+        vn = v.detach().numpy()
         wn, ewn = w_h.detach().numpy(), ew.detach().numpy()
         mask = np.ones(ewn.shape[0], bool)
         fwd = O.sparse3d_forward(bn, ln, en, vn, wn, csr, mask, ewn, B, L, E, R, cap=cap, agg_mode=0, is_score=True)
-        outs = []
+        parts = []
         for name in ("ori", "inv", "ind"):
             k, val = fwd[name]
             keep = ((k % E) >= lo) & ((k % E) < hi)
-            kb, kl, ke = O.split3(k[keep], L, E)
-            idx = torch.from_numpy(np.stack([kb, kl, ke]).astype(np.int64).reshape(3, -1))
-            outs.append(torch.sparse_coo_tensor(idx, torch.from_numpy(val[keep].astype(np.float32)), (B, L, E),
-                                                is_coalesced=True))
+            parts.append((k[keep], val[keep]))
+        mk, mv = O.sum_sparse3d_concat(*parts)
         ctx.fwd, ctx.args = fwd, (bn, ln, en, vn, wn, ewn, B, L, E, R)
-        ctx.keys = [o.indices() for o in outs]
-        return tuple(outs)
+        ctx.mk = mk
+        out_k = torch.from_numpy(mk.astype(np.int64))
+        ctx.mark_non_differentiable(out_k)
+        return out_k, torch.from_numpy(mv.astype(np.float32))
 
     @staticmethod
-    def backward(ctx, go, gi, gd):
+    def backward(ctx, _gk, gv):
         bn, ln, en, vn, wn, ewn, B, L, E, R = ctx.args
-        grads = {}
-        for name, g, idx in zip(("ori", "inv", "ind"), (go, gi, gd), ctx.keys):
-            k = O.keys3(idx[0].numpy(), idx[1].numpy(), idx[2].numpy(), L, E)
-            if g is None:
-                gv = np.zeros(k.shape[0], np.float32)
-            elif g.is_sparse:
-                g = g.coalesce()
-                gk = O.keys3(*(g.indices().numpy()), L, E)
-                gv = O.lookup(gk, g.values().numpy().astype(np.float32), k)
-            else:
-                gv = g[idx[0], idx[1], idx[2]].numpy().astype(np.float32)
-            grads[name] = (k, gv)
+        g = gv.numpy().astype(np.float32)
+        grads = {name: (ctx.fwd[name][0], O.lookup(ctx.mk, g, ctx.fwd[name][0])) for name in ("ori", "inv", "ind")}
         gsp, gw, ge = O.sparse3d_backward(ctx.fwd, grads, bn, ln, en, vn, wn, B, L, E, R, agg_mode=0,
                                           edge_weight=ewn, is_score=True, want_edge_grad=True,
                                           num_facts=ewn.shape[0])
-        return (None, None, None, torch.from_numpy(gsp), torch.from_numpy(gw), torch.from_numpy(ge),
+        return (None, torch.from_numpy(gsp), torch.from_numpy(gw), torch.from_numpy(ge),
                 None, None, None, None, None, None)
 
 
@@ -97,8 +89,8 @@ def _worker(rank, world, port, cfg, out_q):
         ew = torch.from_numpy(scores).requires_grad_(True)
         ew_rep = S.replicated(ew)
 
-        def hop(b, l, e, v, w_h, lo, hi):
-            return _OracleRangeHop.apply(b, l, e, v, w_h, ew_rep, csr, E, R, cfg["cap"], lo, hi)
+        def hop(keys, v, w_h, lo, hi):
+            return _OracleRangeHop.apply(keys, v, w_h, ew_rep, csr, E, R, cfg["cap"], lo, hi)
 
         keys, vals = S.sharded_proof_scores(spec, hop, torch.from_numpy(heads), wt, E, threshold=cfg["threshold"],
                                             topk_nodes=cfg["topk_nodes"])

@@ -108,6 +108,57 @@ def test_hop_range_partition_union(graph, cap, agg, accum):
             np.testing.assert_allclose(a, b, rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("cap", [O.UNCAPPED, 3, 40])
+def test_merged_hop_partition_union(cap, accum):
+    """MergedHop (ori + inv + ind in one store) over a 3-way destination partition: the union is
+    the full-range merged output, the gradients add up to the full-range ones, and the full
+    output equals the oracle's concat-sum."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.sharded import message_in_counts, plan_dst_ranges
+    from minikg_dev_b200.sparse_loop import MergedHop
+    h, r, t, E, R = _hubby()
+    g = DeviceGraph.from_triples(T(h), T(r), T(t), E, R)
+    rng = np.random.default_rng(cap % 991)
+    B, L, n = 3, 2, 2 * R + 1
+    w = rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32)
+    deg = np.bincount(h, minlength=E) + np.bincount(t, minlength=E)
+    keys = np.unique(np.concatenate([rng.integers(0, B * L * E, 300), np.argsort(-deg)[:3] + E]))
+    rng.shuffle(keys)  # the op takes frontier keys in any order
+    fv = rng.uniform(0.05, 1.0, keys.shape[0]).astype(np.float32)
+    ew = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    csr = O.build_csr_structure(h, t, r, E)
+    fb, fl, fe = O.split3(keys, L, E)
+    fwd = O.sparse3d_forward(fb, fl, fe, fv, w, csr, np.ones(h.shape[0], bool), ew, B, L, E, R, cap=cap,
+                             is_score=True)
+    want_k, want_v = O.sum_sparse3d_concat(fwd["ori"], fwd["inv"], fwd["ind"])
+    seeds = rng.standard_normal(want_k.shape[0]).astype(np.float32)
+    bounds = plan_dst_ranges(message_in_counts(torch.from_numpy(h), torch.from_numpy(t), E), 3)
+
+    def run(lo, hi):
+        sv = T(fv).requires_grad_(True)
+        wt = T(w).requires_grad_(True)
+        et = T(ew).requires_grad_(True)
+        k, v = MergedHop.apply(T(keys), sv, wt, et, g, None, True, 1.0, cap, lo, hi)
+        kn = k.cpu().numpy()
+        assert (np.diff(kn) > 0).all()
+        (v * T(O.lookup(want_k, seeds, kn))).sum().backward()
+        return kn, v.detach().cpu().numpy(), (sv.grad.cpu().numpy(), wt.grad.cpu().numpy(), et.grad.cpu().numpy())
+
+    fk, fvv, fg = run(0, 0)
+    np.testing.assert_array_equal(fk, want_k)
+    np.testing.assert_allclose(fvv, want_v, rtol=RTOL, atol=ATOL)
+    ks, vs, gsum = [], [], None
+    for k in range(3):
+        kk, vv, gr = run(bounds[k], bounds[k + 1])
+        assert ((kk % E >= bounds[k]) & (kk % E < bounds[k + 1])).all()
+        ks.append(kk)
+        vs.append(vv)
+        gsum = gr if gsum is None else tuple(a + b for a, b in zip(gsum, gr))
+    np.testing.assert_array_equal(np.concatenate(ks)[np.argsort(np.concatenate(ks), kind="stable")], fk)
+    for a, b in zip(gsum, fg):  # fp32 atomics in different orders over hub rows: gradient tolerance
+        np.testing.assert_allclose(a, b, rtol=1e-4, atol=1e-5)
+
+
 def test_hop_range_rejects_bad_range():
     from minikg_dev_b200.fastlog_kernel import HopRange
     from minikg_dev_b200.graph import DeviceGraph
