@@ -540,3 +540,52 @@ def test_kernel_sparse_scores_drop_in(gname, tag, cap, topk_nodes, accum):
                                        cap=cap, topk_nodes=topk_nodes)
         np.testing.assert_array_equal(idx[0] * E + idx[1], final[0])
         np.testing.assert_allclose(out.values().detach().cpu().numpy(), final[1], rtol=RTOL, atol=ATOL)
+
+
+# ----------------------------------------------------------------------------- degenerate graphs
+def test_isolated_entities_and_factless_graph():
+    """Entities without edges send nothing but their identity message, through the op, the
+    fused loop, the sparse loop and the decode; on a graph with no facts at all the op emits the
+    identity output only (the reference's CSR build cannot take an empty fact list either)."""
+    from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import decode_max, proof_scores
+    from minikg_dev_b200.sparse_loop import sparse_proof_scores
+    E, R = 50, 3
+    B, L, n = 2, 2, 2 * R + 1
+    w = np.full((B, L, n), 1.0 / n, np.float32)
+    fb = np.array([0, 0, 1], np.int64)
+    fl = np.array([0, 1, 1], np.int64)
+    fe = np.array([10, 0, 49], np.int64)  # 10 and 49 have no edges
+    fv = np.array([0.5, 1.0, 0.25], np.float32)
+    for hh, rr, tt in ((np.array([0, 1, 2]), np.array([0, 1, 2]), np.array([1, 2, 3])),
+                       (np.zeros(0, np.int64), np.zeros(0, np.int64), np.zeros(0, np.int64))):
+        csr = O.build_csr_structure(hh, tt, rr, E)
+        dg = DeviceGraph(csr_dev(csr), E, R)
+        scores = np.full(hh.size, 0.5, np.float32)
+        ew = T(scores) if hh.size else None
+        o, i, d = FastLogFunctionSparse3DTopK.apply(T(fb), T(fl), T(fe), T(fv), T(w), *dg.csr,
+                                                    torch.ones((), device=DEV), ew, B, L, E, R, False, UNC, 0,
+                                                    True, 1.0)
+        fwd = O.sparse3d_forward(fb, fl, fe, fv, w, csr, np.ones(hh.size, bool), scores if hh.size else None,
+                                 B, L, E, R, is_score=True)
+        for name, tns in (("ori", o), ("inv", i), ("ind", d)):
+            k3, v3 = coo_np(tns, L, E)
+            np.testing.assert_array_equal(k3, fwd[name][0])
+            np.testing.assert_allclose(v3, fwd[name][1], rtol=RTOL, atol=ATOL)
+        if not hh.size:
+            assert o._nnz() == 0 and i._nnz() == 0 and d._nnz() == 3
+            continue
+        heads = T(np.array([10, 0], np.int64))
+        w_hops = T(np.stack([w, w]))
+        out, msgs = proof_scores(dg, heads, w_hops, ew)
+        sp, _ = sparse_proof_scores(dg, heads, w_hops, ew, cap=2)
+        final, trace = O.proof_sum_forward(np.array([10, 0]), np.stack([w, w]), csr, np.ones(3, bool), scores,
+                                           B, L, E, R)
+        want = np.zeros((B, E), np.float32)
+        want[final[0] // E, final[0] % E] = final[1]
+        np.testing.assert_allclose(out.cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+        np.testing.assert_allclose(sp.to_dense().cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+        assert out[0, 10].item() > 0  # the isolated head keeps its identity mass
+        res = decode_max(dg, heads, w_hops, 5, ew)
+        assert int(res.tails[0, 0]) == 10 and int(res.counts[0]) == 1
