@@ -428,11 +428,18 @@ def run_sharded(a, wl, kg, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    if kg is None:  # web-scale shapes: drawn on the device (every rank draws the same graph)
+        from minikg_dev_b200.synth import KG, sample_graph_device
+        head_d, rel_d, tail_d = sample_graph_device(wl.E, wl.R, wl.T, wl.gen, seed=0, device=dev)
+        kg = KG(wl.name, wl.E, wl.R, np.broadcast_to(np.int8(0), (wl.T,)), np.empty(0), np.empty(0),
+                meta={"generator": "device"})
+    else:
+        head_d, rel_d, tail_d = (torch.from_numpy(a).to(dev) for a in (kg.head, kg.rel, kg.tail))
     B, L, K, E, T = wl.B, wl.L, wl.hops, kg.num_entities, kg.num_triples
     inp = hop_inputs(kg, B, L, K, seed=0)
-    g = DeviceGraph.from_triples(torch.from_numpy(kg.head).to(dev), torch.from_numpy(kg.rel).to(dev),
-                                 torch.from_numpy(kg.tail).to(dev), E, kg.num_relations)
-    bounds = S.plan_dst_ranges(S.message_in_counts(torch.from_numpy(kg.head), torch.from_numpy(kg.tail), E), world)
+    g = DeviceGraph.from_triples(head_d, rel_d, tail_d, E, kg.num_relations)
+    bounds = S.plan_dst_ranges(S.message_in_counts(head_d, tail_d, E), world)
+    del head_d, rel_d, tail_d
     spec = S.ShardSpec(rank, world, bounds)
     heads = torch.from_numpy(inp.heads).to(dev)
     w0 = torch.from_numpy(inp.rule_weights).to(dev)
@@ -478,6 +485,7 @@ def run_sharded(a, wl, kg, rank, world, local_rank):
             "data": "synthetic", "engine": "sharded",
             "config": {"workload": wl.name, "entities": E, "relations": kg.num_relations, "triples": T,
                        "queries": B, "rules": L, "hops": K, "topk_edges": wl.topk_edges,
+                       "graph_generator": kg.meta.get("generator", "host"),
                        "parallelism": f"dst-partition x{world}", "bounds": bounds,
                        "l2": "state and inputs exceed L2"},
             "messages_per_step": M, "clocks": clocks.summary()}), flush=True)
@@ -529,7 +537,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     wl = WORKLOADS[a.workload]
-    kg = workload_graph(a.workload, seed=0)
+    # graphs above 5e7 facts are drawn on the GPU by the sharded engine itself
+    kg = None if (a.engine == "sharded" and wl.T > 50_000_000) else workload_graph(a.workload, seed=0)
     if a.impl == "reference":
         run_reference(a, wl, kg, rank, world)
         return
