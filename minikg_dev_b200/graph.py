@@ -121,6 +121,38 @@ class DeviceGraph:
         csr = build_csr_structure(head, tail, rel, num_entities, num_relations)
         return cls(csr, num_entities, num_relations)
 
+    @classmethod
+    def from_npy(cls, path, device: torch.device | str = "cuda", num_entities: int | None = None,
+                 num_relations: int | None = None, chunk: int = 1 << 24) -> "DeviceGraph":
+        """The graph of an ``N x 3`` (head, rel, tail) ``.npy`` fact file (the reference's
+        ``load_facts(.., "npy")``, data.py:14-21, memory-mapped), streamed to the device in
+        ``chunk``-row pieces through one pinned buffer, then built on the device.  Entity and
+        relation counts default to max id + 1 (facts.py:19-23), taken on the device."""
+        import numpy as np
+        facts = np.load(path, mmap_mode="r")
+        if facts.ndim != 2 or facts.shape[1] < 3:
+            raise ValueError(f"expected an Nx3 fact array in {path}, got shape={facts.shape}")
+        dev = torch.device(device)
+        T = int(facts.shape[0])
+        cols = [torch.empty(T, dtype=torch.int32, device=dev) for _ in range(3)]
+        stage = torch.empty((min(chunk, max(T, 1)), 3), dtype=torch.int32, pin_memory=True)
+        for a in range(0, T, chunk):
+            b = min(T, a + chunk)
+            piece = np.asarray(facts[a:b, :3])
+            if piece.size and (piece.min() < 0 or piece.max() > np.iinfo(np.int32).max):
+                raise ValueError("fact ids must lie in [0, 2^31)")
+            stage[: b - a].copy_(torch.from_numpy(piece.astype(np.int32, copy=False)))
+            dv = stage[: b - a].to(dev, non_blocking=True)
+            for k in range(3):
+                cols[k][a:b] = dv[:, k]
+            torch.cuda.current_stream(dev).synchronize()  # the pinned buffer is reused
+        head, rel, tail = cols
+        if num_entities is None:
+            num_entities = int(torch.maximum(head.max(), tail.max()).item()) + 1 if T else 1
+        if num_relations is None:
+            num_relations = int(rel.max().item()) + 1 if T else 1
+        return cls.from_triples(head, rel, tail, int(num_entities), int(num_relations))
+
     # -------------------------------------------------------------- fused-engine lists
     def adjacency(self) -> N.Adjacency:
         if self._adj is None:

@@ -738,3 +738,60 @@ def rule_first_hop_query_heads(channels, cache, query_heads):
         return np.zeros(0, np.int64)
     q = np.asarray(query_heads, np.int64)
     return q[np.isin(q, np.concatenate(sets))]
+
+
+# ----------------------------------------------------------------------------
+# decode accumulator: best-k cut per query row (decode.py:45-116)
+# ----------------------------------------------------------------------------
+
+def oracle_best_k(not_base, in_true, base_true):
+    """The cut k in [0, n] of one ordered candidate row that maximises (base true + new true)
+    - new wrong; ties: more true, then fewer wrong, then the smaller k (decode.py:45-69).
+    Returns (k, wrong at k)."""
+    nb = np.asarray(not_base, bool)
+    nt = nb & np.asarray(in_true, bool)
+    pn = np.concatenate([[0], np.cumsum(nb, dtype=np.int64)])
+    pt = np.concatenate([[0], np.cumsum(nt, dtype=np.int64)])
+    true_count = int(base_true) + pt
+    wrong = pn - pt
+    gain = true_count - wrong
+    j = int(np.lexsort((np.arange(gain.shape[0]), wrong, -true_count, -gain))[0])
+    return j, int(wrong[j])
+
+
+class RelationAccumulator:
+    """Counters of decode.py:72-116 (``_OracleRelationAccumulator``) restated."""
+
+    def __init__(self):
+        self.candidate_total = self.max_candidate_count = self.query_count = 0
+        self.selected = self.selected_wrong = self.new = self.new_true = 0
+
+    def add_row(self, ordered_tails, true_tails, base_tails) -> int:
+        t = np.asarray(ordered_tails, np.int64)
+        true = np.asarray(true_tails, np.int64)
+        base = np.asarray(base_tails, np.int64)
+        n = t.shape[0]
+        self.candidate_total += n
+        self.max_candidate_count = max(self.max_candidate_count, n)
+        not_base = ~np.isin(t, base)
+        in_true = np.isin(t, true)
+        first = np.zeros(n, bool)
+        if n:
+            first[np.unique(t, return_index=True)[1]] = True
+        new_unit = first & not_base
+        cn = np.concatenate([[0], np.cumsum(new_unit, dtype=np.int64)])
+        cnt = np.concatenate([[0], np.cumsum(new_unit & in_true, dtype=np.int64)])
+        if n == 0 or true.shape[0] == 0:
+            k, wrong = 0, 0
+        else:
+            k, wrong = oracle_best_k(not_base, in_true, int(np.isin(base, true).sum()))
+        self.query_count += int(k > 0)
+        self.selected += k
+        self.selected_wrong += wrong
+        self.new += int(cn[k])
+        self.new_true += int(cnt[k])
+        return k
+
+    def counters(self):
+        return [self.candidate_total, self.max_candidate_count, self.query_count, self.selected,
+                self.selected_wrong, self.new, self.new_true]

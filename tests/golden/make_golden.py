@@ -383,14 +383,50 @@ def prune_case(ref, out, kg, rng):
                pf_cache_off=np.cumsum([0] + [cache[c].size for c in keys]).astype(np.int64))
 
 
+def accum_case(ref, out, rng):
+    """The decode accumulator's best-k selection (decode.py:45-116) on synthetic rows:
+    ordered candidate tails, per-query true and base (supplied) tail sets, empty cases and a
+    repeated tail included."""
+    import decode as ref_decode  # the reference's decode module (imports resolved via sys.path)
+    acc = ref_decode._OracleRelationAccumulator()
+    rows_t, rows_true, rows_base, best = [], [], [], []
+    for q in range(60):
+        n = int(rng.integers(0, 40)) if q % 7 else 0
+        tails = rng.permutation(200)[:n].astype(np.int64)
+        if q % 11 == 3 and n > 2:
+            tails[-1] = tails[0]  # a repeated tail
+        hits = tails[: min(n, 12)][rng.random(min(n, 12)) < 0.6]  # early candidates are often true
+        true = np.unique(np.concatenate([hits, rng.choice(200, int(rng.integers(0, 25)), replace=False)])) \
+            .astype(np.int64) if q % 5 else np.zeros(0, np.int64)
+        base = rng.choice(200, int(rng.integers(0, 15)), replace=False).astype(np.int64)
+        if q % 9 == 2:
+            base = np.concatenate([base, base[:2]])  # duplicated base ids
+        best.append(acc.add_row(tails, true, base))
+        rows_t.append(tails); rows_true.append(true); rows_base.append(base)
+    off = lambda rows: np.cumsum([0] + [r.size for r in rows]).astype(np.int64)  # noqa: E731
+    out.update(ac_tails=np.concatenate(rows_t), ac_tails_off=off(rows_t),
+               ac_true=np.concatenate(rows_true), ac_true_off=off(rows_true),
+               ac_base=np.concatenate(rows_base), ac_base_off=off(rows_base),
+               ac_best=np.array(best, np.int64),
+               ac_counters=np.array([acc.candidate_total, acc.max_candidate_count, acc.query_count, acc.selected,
+                                     acc.selected_wrong, acc.new, acc.new_true], np.int64))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
     ap.add_argument("--out", default=str(HERE))
-    ap.add_argument("--only", choices=("all", "prune"), default="all")
+    ap.add_argument("--only", choices=("all", "prune", "accum"), default="all")
     a = ap.parse_args()
     torch.set_num_threads(1)  # index_put_/scatter_add_ are then sequential in index order
     ref = import_reference(a.ref)
+    if a.only in ("all", "accum"):
+        ac = {}
+        accum_case(ref, ac, np.random.default_rng(8))
+        np.savez_compressed(os.path.join(a.out, "golden_accum.npz"), **ac)
+        print("wrote accum", len(ac))
+        if a.only == "accum":
+            return
     if a.only in ("all", "prune"):
         kg = sample_graph(900, 9, 9000, (("rel", ("zipf", 1.0)), ("head", (0.9, 2.0)), ("tail", (0.9, 2.0)),
                                          ("hubs", (0.05, 0.4))), seed=12, name="g2")

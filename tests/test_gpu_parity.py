@@ -589,3 +589,17 @@ def test_isolated_entities_and_factless_graph():
         assert out[0, 10].item() > 0  # the isolated head keeps its identity mass
         res = decode_max(dg, heads, w_hops, 5, ew)
         assert int(res.tails[0, 0]) == 10 and int(res.counts[0]) == 1
+
+
+def test_device_graph_from_npy(tmp_path):
+    """The .npy fact-file loader streams in chunks and builds the same CSR as the oracle."""
+    from minikg_dev_b200.graph import DeviceGraph
+    h, r, t, E, R = GRAPHS["g2"]
+    facts = np.stack([h, r, t], 1).astype(np.int64)
+    path = tmp_path / "all_id.npy"
+    np.save(path, facts)
+    g = DeviceGraph.from_npy(path, DEV, chunk=1000)
+    assert g.num_entities == int(max(h.max(), t.max())) + 1 and g.num_relations == int(r.max()) + 1
+    want = O.build_csr_structure(h, t, r, g.num_entities)
+    for k, (got, exp) in enumerate(zip(g.csr, want)):
+        np.testing.assert_array_equal(got.cpu().numpy(), exp, err_msg=f"csr[{k}]")
