@@ -603,3 +603,56 @@ def test_device_graph_from_npy(tmp_path):
     want = O.build_csr_structure(h, t, r, g.num_entities)
     for k, (got, exp) in enumerate(zip(g.csr, want)):
         np.testing.assert_array_equal(got.cpu().numpy(), exp, err_msg=f"csr[{k}]")
+
+
+@pytest.mark.parametrize("variant", ["mask", "logit"])
+@pytest.mark.parametrize("engine", ["fused", "sparse"])
+def test_loops_masked_facts_and_sigmoid_path(variant, engine):
+    """Both hop loops with facts masked off (their messages are explicit zeros, dropped by the
+    normalisation) or with the sigmoid edge-score path, against the oracle, fwd and bwd."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import proof_scores
+    from minikg_dev_b200.sparse_loop import sparse_proof_scores
+    h, r, t, E, R = GRAPHS["hubby"]
+    rng = np.random.default_rng(31)
+    csr = O.build_csr_structure(h, t, r, E)
+    B, L, K, n = 6, 3, 3, 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    mask = np.ones(h.shape[0], bool)
+    if variant == "mask":
+        mask[rng.random(h.shape[0]) < 0.3] = False
+        ew = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+        is_score, scale = True, 1.0
+    else:
+        ew = rng.standard_normal(h.shape[0]).astype(np.float32)
+        is_score, scale = False, 0.7
+    cap = UNC if engine == "fused" else 9
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, ew, B, L, E, R, cap=cap, is_score=is_score,
+                                       scale=scale)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    wt = T(w_hops).requires_grad_(True)
+    sc = T(ew).requires_grad_(True)
+    mk = T(mask.astype(np.float32))
+    if engine == "fused":
+        out, _ = proof_scores(dg, T(heads), wt, sc, mask=mk, is_score=is_score, scale=scale)
+        got = out.detach().cpu().numpy()
+        want = np.zeros((B, E), np.float32)
+        want[final[0] // E, final[0] % E] = final[1]
+        np.testing.assert_array_equal(got != 0, want != 0)
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+        seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
+        gd = np.zeros((B, E), np.float32)
+        gd[final[0] // E, final[0] % E] = seed
+        (out * T(gd)).sum().backward()
+    else:
+        out, _ = sparse_proof_scores(dg, T(heads), wt, sc, mk, is_score, scale, cap, 0)
+        idx = out.indices().cpu().numpy()
+        np.testing.assert_array_equal(idx[0] * E + idx[1], final[0])
+        np.testing.assert_allclose(out.values().detach().cpu().numpy(), final[1], rtol=RTOL, atol=ATOL)
+        seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
+        (out.values() * T(seed)).sum().backward()
+    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, ew, B, L, E, R, is_score=is_score,
+                                  scale=scale, num_facts=h.shape[0])
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
