@@ -14,6 +14,10 @@ Semantics kept from the reference's CUDA path:
 * ``agg_mode == 1``: max per key, argmax = smallest original fact id among equal maxima
   (``tie_break=meta_edge``, fastlog_kernel.py:954-959); the backward sends each key's
   gradient to that message only.
+Reference environment flags kept: ``FASTLOG_STAGE_TIMING=1`` prints ``StageTiming`` lines per
+stage (prepare_inputs, cuda_forward — which here includes the coalescing —, save_ctx);
+``FASTLOG_SPARSE_DEBUG_COUNTS=1`` prints the raw message counts (``Sparse3DTopKCounts``);
+``FASTLOG_SPARSE_EDGE_GRAD=1`` returns the edge-score gradient as sparse COO.
 Differences: a ``mask_values`` of one element (the reference's 0-d ones tensor for huge
 graphs) is broadcast to every fact; the max path compares values through an
 order-preserving integer key, so ``-0.0`` ranks below ``+0.0``.
@@ -22,12 +26,27 @@ from __future__ import annotations
 
 import ctypes
 import os
+import time
 
 import torch
 from torch import autograd
 
 from . import _native as N
 from .graph import build_csr_structure, graph_from_csr  # noqa: F401  (re-exported)
+
+
+def _stage_timing() -> bool:
+    return os.environ.get("FASTLOG_STAGE_TIMING", "") == "1"
+
+
+def _stage_log(stage: str, t0: float) -> None:
+    """``FASTLOG_STAGE_TIMING=1``: one line per op stage after a device sync, in the reference's
+    format (fastlog_kernel.py:50-66)."""
+    if not _stage_timing():
+        return
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    print("StageTiming fastlog_kernel stage:{} seconds:{:.4f}".format(stage, time.perf_counter() - float(t0)))
 
 
 # Message store of the op: "auto" (key spaces above _HASH_MIN_KEYS count their messages -- one
@@ -68,6 +87,7 @@ def _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values
                  topk_edges, agg_mode, edge_weight_is_score, edge_weight_scale, dst_lo=0, dst_hi=0):
     """Forward of one hop on a ``DeviceGraph``; outputs hold the keys with e in [dst_lo, dst_hi)
     (the whole [0, E) when dst_hi <= dst_lo)."""
+    t_stage = time.perf_counter()
     lib = N.load()
     N.require_cuda(sp_value, "sp_value")
     dev = sp_value.device
@@ -85,6 +105,18 @@ def _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values
     p = N.HopParams(*params)
     nnz = int(b.numel())
     extent = (int(dst_hi) - int(dst_lo)) if int(dst_hi) > int(dst_lo) else E
+    _stage_log("sparse3d_topk.prepare_inputs", t_stage)
+    t_stage = time.perf_counter()
+    debug_counts = os.environ.get("FASTLOG_SPARSE_DEBUG_COUNTS", "") == "1"
+    if debug_counts:
+        # the reference's raw message counts (fastlog_kernel.py:940-949): ori / inv messages
+        # before coalescing, one identity message per entry
+        mcd = torch.empty(2, dtype=torch.int64, device=dev)
+        N.check(lib.mkg_hop_count_messages(ctypes.byref(g.struct), ctypes.byref(fr), ctypes.byref(p), mcd.data_ptr(),
+                                           N.error_word(dev).data_ptr(), N.stream_handle(dev)), "hop_count_messages")
+        m_ori, m_inv = (int(x) for x in mcd.tolist())
+        print("Sparse3DTopKCounts nnz={} ori_total={} inv_total={} ind_total={}".format(nnz, m_ori, m_inv, nnz),
+              flush=True)
     if ACCUM == "hash" or (ACCUM == "auto" and B * L * extent > _HASH_MIN_KEYS):
         # exact message counts decide between the dense key slab and hash tables
         mc = torch.empty(2, dtype=torch.int64, device=dev)
@@ -112,6 +144,8 @@ def _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values
         outs.append(torch.sparse_coo_tensor(idx, val, (B, L, E), is_coalesced=True))
         args.append(arg)
     del ws
+    _stage_log("sparse3d_topk.cuda_forward", t_stage)
+    t_stage = time.perf_counter()
     has_edge_weight = weight is not None and bool(getattr(weight, "requires_grad", False))
     if any(ctx.needs_input_grad):
         empty_i = torch.empty(0, dtype=torch.int64, device=dev)
@@ -129,6 +163,7 @@ def _hop_forward(ctx, g, sp_batch, sp_level, sp_entity, sp_value, w, mask_values
         ctx.edge_weight_scale = float(edge_weight_scale)
         ctx.weight_shape = tuple(weight.shape) if weight is not None else None
         ctx.weight_dtype = weight.dtype if weight is not None else None
+    _stage_log("sparse3d_topk.save_ctx", t_stage)
     return outs[0], outs[1], outs[2]
 
 

@@ -113,11 +113,21 @@ def _all_gather_padded(t: torch.Tensor, counts: list[int], group) -> list[torch.
 
 
 def _gather_counts(n: int, device, group) -> list[int]:
+    """Every rank's size; an impossible size (negative) raises the same error on all ranks,
+    after the exchange, so no rank is left waiting in a later collective."""
     world = dist.get_world_size(group)
     c = torch.tensor([n], dtype=torch.int64, device=device)
     out = [torch.empty_like(c) for _ in range(world)]
     dist.all_gather(out, c, group=group)
-    return [int(x) for x in torch.cat(out).tolist()]
+    counts = [int(x) for x in torch.cat(out).tolist()]
+    bad = [r for r, x in enumerate(counts) if x < 0]
+    if bad:
+        raise RuntimeError(f"sharded hop: rank(s) {bad} reported an invalid frontier size {[counts[r] for r in bad]}")
+    return counts
+
+
+def _frontier_size(keys: torch.Tensor) -> int:
+    return int(keys.numel())
 
 
 class _GatherFrontier(autograd.Function):
@@ -126,7 +136,7 @@ class _GatherFrontier(autograd.Function):
 
     @staticmethod
     def forward(ctx, keys, vals, group):
-        counts = _gather_counts(int(keys.numel()), keys.device, group)
+        counts = _gather_counts(_frontier_size(keys), keys.device, group)
         k_all = torch.cat(_all_gather_padded(keys, counts, group))
         v_all = torch.cat(_all_gather_padded(vals.detach(), counts, group))
         ctx.counts, ctx.group = counts, group

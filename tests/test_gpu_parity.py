@@ -656,3 +656,58 @@ def test_loops_masked_facts_and_sigmoid_path(variant, engine):
                                   scale=scale, num_facts=h.shape[0])
     np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+
+
+# ----------------------------------------------------------------------------- tracing, determinism
+def test_reference_trace_flags(monkeypatch, capsys):
+    """FASTLOG_STAGE_TIMING / FASTLOG_SPARSE_DEBUG_COUNTS print the reference's lines, with the
+    raw message counts the reference's fill kernel would produce."""
+    from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
+    monkeypatch.setenv("FASTLOG_STAGE_TIMING", "1")
+    monkeypatch.setenv("FASTLOG_SPARSE_DEBUG_COUNTS", "1")
+    h, r, t, E, R = GRAPHS["hubby"]
+    csr = O.build_csr_structure(h, t, r, E)
+    rng = np.random.default_rng(12)
+    B, L, n = 3, 2, 2 * R + 1
+    w = rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32)
+    fb, fl, fe, fv = _frontier(rng, B, L, E, per_row=20)
+    FastLogFunctionSparse3DTopK.apply(T(fb), T(fl), T(fe), T(fv), T(w), *csr_dev(csr), torch.ones((), device=DEV),
+                                      None, B, L, E, R, False, 7, 0)
+    out = capsys.readouterr().out
+    for stage in ("prepare_inputs", "cuda_forward", "save_ctx"):
+        assert f"StageTiming fastlog_kernel stage:sparse3d_topk.{stage} seconds:" in out
+    fwd = O.sparse3d_forward(fb, fl, fe, fv, w, csr, np.ones(h.shape[0], bool), None, B, L, E, R, cap=7)
+    line = [x for x in out.splitlines() if x.startswith("Sparse3DTopKCounts")][0]
+    assert line == (f"Sparse3DTopKCounts nnz={fb.shape[0]} ori_total={fwd['raw_ori']['edge'].shape[0]} "
+                    f"inv_total={fwd['raw_inv']['edge'].shape[0]} ind_total={fb.shape[0]}")
+
+
+def test_argmax_paths_are_deterministic():
+    """Max values, argmax facts and the decode are identical across repeated runs; the sum
+    paths' keys are identical (their fp32 values may differ in the last bits)."""
+    from minikg_dev_b200.fastlog_bridge import FastLogFunctionSparse3DTopK
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import decode_max, proof_scores
+    h, r, t, E, R = GRAPHS["hubby"]
+    csr = O.build_csr_structure(h, t, r, E)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    rng = np.random.default_rng(13)
+    B, L, K, n = 8, 3, 3, 2 * R + 1
+    heads = T(rng.integers(0, E, B).astype(np.int64))
+    w_hops = T(np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)]))
+    sc = T(rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32))
+    runs = [decode_max(dg, heads, w_hops, 50, sc) for _ in range(3)]
+    for res in runs[1:]:
+        assert torch.equal(res.raw, runs[0].raw) and torch.equal(res.tails, runs[0].tails)
+        assert torch.equal(res.scores, runs[0].scores)
+    fb, fl, fe, fv = _frontier(rng, 2, L, E, per_row=30)
+    outs = [FastLogFunctionSparse3DTopK.apply(T(fb), T(fl), T(fe), T(fv), w_hops[0][:2], *dg.csr,
+                                              torch.ones((), device=DEV), sc, 2, L, E, R, False, 5, 1, True, 1.0)
+            for _ in range(3)]
+    for o in outs[1:]:
+        for a, b in zip(o, outs[0]):
+            assert torch.equal(a.coalesce().indices(), b.coalesce().indices())
+            assert torch.equal(a.coalesce().values(), b.coalesce().values())
+    s1, _ = proof_scores(dg, heads, w_hops, sc)
+    s2, _ = proof_scores(dg, heads, w_hops, sc)
+    assert torch.equal(s1 != 0, s2 != 0)

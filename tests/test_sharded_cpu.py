@@ -168,3 +168,53 @@ def test_plan_dst_ranges_balances_messages():
         assert max(load) <= (int((m + 1).sum()) / world) + int(m.max()) + 1
     with pytest.raises(ValueError):
         plan_dst_ranges(torch.zeros(3, dtype=torch.int64), 4)
+
+
+# ----------------------------------------------------------------------------- failures (host only)
+def _fail_worker(rank, world, port, mode, out_q):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    from minikg_dev_b200 import sharded as S
+    h, r, t, E, R, heads, w, scores = _case(seed=4)
+    csr = O.build_csr_structure(h, t, r, E)
+    bounds = S.plan_dst_ranges(S.message_in_counts(torch.from_numpy(h), torch.from_numpy(t), E), world)
+    spec = S.ShardSpec(rank, world, bounds)
+    if mode == "dead" and rank == 1:
+        os._exit(0)  # the rank leaves between steps, with nothing in flight
+    if mode == "size" and rank == 1:
+        S._frontier_size = lambda keys: -5  # a corrupted size message
+    ew = torch.from_numpy(scores)
+
+    def hop(keys, v, w_h, lo, hi):
+        return _OracleRangeHop.apply(keys, v, w_h, ew, csr, E, R, O.UNCAPPED, lo, hi)
+
+    try:
+        S.sharded_proof_scores(spec, hop, torch.from_numpy(heads), torch.from_numpy(w), E)
+        out_q.put((rank, "no error"))
+    except Exception as exc:  # noqa: BLE001 - the test inspects the error text
+        out_q.put((rank, f"{type(exc).__name__}: {exc}"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+@pytest.mark.parametrize("mode", ["dead", "size"])
+def test_sharded_loop_reports_rank_failures(mode):
+    """A rank that exits, or that sends an impossible frontier size, ends the other ranks'
+    step with an error (process-group timeout 10 s, or the size check) instead of a hang."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fail_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    want = 1 if mode == "dead" else 2
+    res = dict(q.get(timeout=120) for _ in range(want))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] != "no error"
+    if mode == "size":
+        assert "invalid frontier size" in res[0] and "invalid frontier size" in res[1]
