@@ -102,6 +102,38 @@ class ProofRunner:
         self.p.bwd_events = None
         return grad_w, (grad_edge if want_edge_grad else None)
 
+    def capture(self, heads, w_hops, out, msgs, grad_out, edge_scores, grad_w, grad_edge=None, mask=None,
+                is_score: bool = True, scale: float = 1.0) -> "torch.cuda.CUDAGraph":
+        """One training step (edge-factor refresh, forward, backward) captured as a CUDA graph
+        over these buffers.  Write new inputs into ``heads`` / ``w_hops`` / ``edge_scores`` /
+        ``grad_out`` (and ``mask``) in place, then ``graph.replay()`` reruns the step with no
+        host work; results land in ``out``, ``msgs``, ``grad_w``, ``grad_edge``.  The library
+        does no host synchronisation inside a step, so the whole step is capturable."""
+        dev = self.graph.device
+        for name, t, dt in (("heads", heads, torch.int64), ("w_hops", w_hops, torch.float32),
+                            ("out", out, torch.float32), ("msgs", msgs, torch.int64),
+                            ("grad_out", grad_out, torch.float32), ("edge_scores", edge_scores, torch.float32),
+                            ("grad_w", grad_w, torch.float32)):
+            if t.device != dev or t.dtype != dt or not t.is_contiguous():
+                raise ValueError(f"capture: {name} must be a contiguous {dt} tensor on {dev}")
+        want_edge = grad_edge is not None
+
+        def step():
+            self.graph.set_edge_factor(mask, edge_scores, is_score, scale)
+            self.forward(heads, w_hops, out, msgs)
+            self.backward(grad_out, mask, edge_scores, is_score, scale, want_edge, grad_w, grad_edge)
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()  # warm-up outside the capture (lazy adjacency, kernel attributes)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        return graph
+
     def row_activity(self, hop: int) -> torch.Tensor:
         """uint8 [E]: entities holding a non-zero state value when hop ``hop`` starts."""
         lib = N.load()

@@ -711,3 +711,38 @@ def test_argmax_paths_are_deterministic():
     s1, _ = proof_scores(dg, heads, w_hops, sc)
     s2, _ = proof_scores(dg, heads, w_hops, sc)
     assert torch.equal(s1 != 0, s2 != 0)
+
+
+def test_fused_step_graph_replay_matches_eager():
+    """ProofRunner.capture: a replayed step equals the eager step, and new inputs written into
+    the captured buffers are picked up by the replay."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import ProofRunner
+    h, r, t, E, R = GRAPHS["g2"]
+    csr = O.build_csr_structure(h, t, r, E)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    rng = np.random.default_rng(21)
+    B, L, K, n = 6, 3, 3, 2 * R + 1
+    runner = ProofRunner(dg, B, L, K)
+    heads = T(rng.integers(0, E, B).astype(np.int64))
+    w_hops = T(np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)]))
+    sc = T(rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32))
+    G = T(rng.standard_normal((B, E)).astype(np.float32))
+    out = torch.empty((B, E), device=DEV)
+    msgs = torch.zeros(K, dtype=torch.int64, device=DEV)
+    gw = torch.empty((K, B, L, n), device=DEV)
+    ge = torch.empty(h.shape[0], device=DEV)
+    graph = runner.capture(heads, w_hops, out, msgs, G, sc, gw, ge)
+    for trial in range(2):
+        if trial == 1:  # new inputs in place
+            heads.copy_(T(rng.integers(0, E, B).astype(np.int64)))
+            w_hops.copy_(T(np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])))
+        graph.replay()
+        torch.cuda.synchronize()
+        got = (out.clone(), gw.clone(), ge.clone())
+        dg.set_edge_factor(None, sc, True, 1.0)
+        o2, _ = runner.forward(heads, w_hops)
+        gw2, ge2 = runner.backward(G, None, sc, True, 1.0, True)
+        np.testing.assert_allclose(got[0].cpu().numpy(), o2.cpu().numpy(), rtol=RTOL, atol=ATOL)
+        np.testing.assert_allclose(got[1].cpu().numpy(), gw2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(got[2].cpu().numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
