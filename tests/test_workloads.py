@@ -42,7 +42,8 @@ def workload(name: str):
         csr = O.build_csr_structure(kg.head, kg.tail, kg.rel, kg.num_entities)
         dg = DeviceGraph(tuple(T(a) for a in csr), kg.num_entities, kg.num_relations)
         inp = hop_inputs(kg, wl.B, wl.L, wl.hops, seed=0)
-        _CACHE.clear()  # one large graph on the device at a time
+        while len(_CACHE) >= 2:  # at most two graphs resident
+            _CACHE.pop(next(iter(_CACHE)))
         _CACHE[name] = (wl, kg, csr, dg, inp)
     return _CACHE[name]
 
@@ -153,6 +154,42 @@ def _duck(kg, wl, logits, scores_t):
                             r2triple=(T(kg.rel), None, mask), mask=mask, mask_float=mask.float())
     args = SimpleNamespace(kernel_topk_edges=wl.topk_edges, kernel_topk_nodes=wl.topk_nodes)
     return model, graph, args
+
+
+def test_first_hop_pruned_max_decode_kg_large():
+    """kg_large's decode: first-hop query pruning (decode_core.py:287-348) on the device graph,
+    then the capped max decode of the surviving heads, against the oracle on the same heads."""
+    from minikg_dev_b200.batching import first_hop_supported_entities, rule_first_hop_channels
+    from minikg_dev_b200.proof import decode_max_sparse
+    wl, kg, csr, dg, inp = workload("kg_large")
+    E, R, L = kg.num_entities, kg.num_relations, wl.L
+    rng = np.random.default_rng(23)
+    n = 2 * R + 1
+    logits = (rng.standard_normal((L, n)) * 3.0).astype(np.float32)  # one relation's first-hop rule logits
+    chans = rule_first_hop_channels(torch.softmax(torch.from_numpy(logits), dim=-1), 0.2)
+    assert chans.numel() > 0
+    supported = first_hop_supported_entities(dg, chans)
+    cand = T(rng.integers(0, E, 64).astype(np.int64))
+    kept = cand[supported[cand]]
+    # oracle restatement of the same pruning
+    chans_np = chans.numpy()
+    cache = O.rule_first_hop_cache(kg.head, kg.rel, kg.tail, np.ones(kg.num_triples, bool),
+                                   sorted({int(c) % R for c in chans_np if c < 2 * R}), R)
+    want_kept = O.rule_first_hop_query_heads(chans_np, cache, cand.cpu().numpy())
+    np.testing.assert_array_equal(kept.cpu().numpy(), want_kept)
+    Bk = int(kept.numel())
+    if Bk == 0:
+        return
+    w = inp.rule_weights[:, :1].repeat(Bk, axis=1)
+    final, tails, sc, counts = decode_max_sparse(dg, kept, T(w), 100, T(inp.edge_scores), cap=wl.topk_edges)
+    want, _ = O.proof_max_forward(kept.cpu().numpy(), w, csr, inp.edge_mask, inp.edge_scores, Bk, L, E, R,
+                                  cap=wl.topk_edges)
+    idx = final.indices().cpu().numpy()
+    np.testing.assert_array_equal(idx[0] * E + idx[1], want[0])
+    np.testing.assert_array_equal(final.values().cpu().numpy(), want[1])
+    ot, osc, _ = O.decode_topk(want, Bk, E, 100)
+    np.testing.assert_array_equal(tails.cpu().numpy(), ot)
+    np.testing.assert_array_equal(sc.cpu().numpy(), osc)
 
 
 @pytest.mark.parametrize("name", ["kg_large", "kg_web@0.02"])
