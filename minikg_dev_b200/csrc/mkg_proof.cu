@@ -27,7 +27,7 @@ constexpr int kFwdWarps = 8;
 constexpr int kBwdWarps = 8;
 constexpr int kTaskFirst = 1;    // task holds the row's first edges (adds the identity term)
 constexpr int kTaskPartial = 2;  // row split over several tasks: accumulate with atomics
-constexpr int kBatch = 8;        // edges whose rows are loaded together (8 x 16 B in flight per lane)
+constexpr int kBatch = 4;        // backward: edges whose dY rows are loaded together (4 x 16 B per lane)
 constexpr int kGrab = 4;         // tasks per queue atomic
 constexpr int kQueueStride = 32; // ints between two queue counters
 
@@ -156,16 +156,6 @@ __device__ __forceinline__ void f4_max_msg(float4& acc, const float4& x, const f
 }
 __device__ __forceinline__ int f4_count(const float4& v) {
   return (v.x != 0.f) + (v.y != 0.f) + (v.z != 0.f) + (v.w != 0.f);
-}
-
-// Loads this block's 128-column chunk of the rule weights into shared memory:
-// ws[ch * 128 + c] = Wt[ch][col0 + c].
-__device__ __forceinline__ void stage_weights(const float* __restrict__ wt, const ProofDims& q, int64_t col0,
-                                              float* ws) {
-  for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) {
-    int64_t ch = i / kChunk, c = i % kChunk;
-    ws[i] = (col0 + c < q.BLP) ? wt[ch * q.BLP + col0 + c] : 0.0f;
-  }
 }
 
 // Dynamic task queue: a warp takes kGrab consecutive tasks per atomic and requests the
@@ -698,25 +688,20 @@ __device__ __forceinline__ float edge_grad_scale(const EdgeFactor& f, int64_t fa
   return f.scale * (1.0f - sg);
 }
 
-// Reduce-scatter of 8 per-lane partial sums: afterwards lane l holds, for edge
-// ((l >> 2) & 7), the sum of that edge's partials over all 32 lanes (9 shuffles).
-__device__ __forceinline__ float reduce_scatter8(const float (&v)[8]) {
+// Reduce-scatter of 4 per-lane partial sums: afterwards lane l holds, for edge
+// ((l >> 3) & 3), the sum of that edge's partials over all 32 lanes (6 shuffles).
+__device__ __forceinline__ float reduce_scatter4(const float (&v)[4]) {
   const int lane = threadIdx.x & 31;
-  float a[4], b[2];
-  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float send = h4 ? v[k] : v[k + 4];
-    const float keep = h4 ? v[k + 4] : v[k];
-    a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
+  const bool h4 = lane & 16, h3 = lane & 8;
+  float a[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    const float send = h3 ? a[k] : a[k + 2];
-    const float keep = h3 ? a[k + 2] : a[k];
-    b[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    const float send = h4 ? v[k] : v[k + 2];
+    const float keep = h4 ? v[k + 2] : v[k];
+    a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
   }
-  float c = (h2 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h2 ? b[0] : b[1], 4);
+  float c = (h3 ? a[1] : a[0]) + __shfl_xor_sync(0xffffffffu, h3 ? a[0] : a[1], 8);
+  c += __shfl_xor_sync(0xffffffffu, c, 4);
   c += __shfl_xor_sync(0xffffffffu, c, 2);
   c += __shfl_xor_sync(0xffffffffu, c, 1);
   return c;
@@ -728,29 +713,32 @@ __device__ __forceinline__ float reduce_scatter8(const float (&v)[8]) {
 //   dEdge[f]  += (sum_c dY[d][c] X[s][c] w[ch][c]) m g(f)
 //   S_prev[c] += dX[s][c] Y_prev[s][c]                   (for the next lower hop)
 // Records of a push row come grouped by channel, so dY * m is summed per channel run and
-// folded into dX and dW once per run.  Only records whose destination row holds a
-// non-zero Y_h value in this chunk are visited (dY_h is zero elsewhere).
-__global__ void __launch_bounds__(kBwdWarps * 32, 2) bwd_pull_kernel(
+// folded into dX and dW once per run, and the edge-score gradient uses the run's X * W[ch]
+// (one rule-weight load per run).  Only records whose destination row holds a non-zero Y_h
+// value in this chunk are visited (dY_h is zero elsewhere).  Rule weights are read from
+// global memory (L1-resident chunk) so that only dW occupies shared memory: 3 blocks per SM.
+__global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
     const uint8_t* __restrict__ yact, const float* __restrict__ dy, const float* __restrict__ yprev,
     float* __restrict__ dx, float* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge,
     int64_t num_facts, EdgeFactor ef, int32_t* __restrict__ queue, unsigned* err) {
   extern __shared__ float smem[];
-  float* ws = smem;                         // [n][128] rule weights
-  float* dws = smem + q.n * kChunk;         // [n][128] their gradient (conflict-free: [ch][k][lane])
+  float* dws = smem;                        // [n][128] rule-weight gradient (conflict-free: [ch][k][lane])
   float* cs = dws + q.n * kChunk;           // [4][32] S_prev partials
   const int lane = threadIdx.x & 31;
   const int64_t chunk = blockIdx.y;
   const int64_t col0 = chunk * kChunk;
   const int64_t col = col0 + 4 * lane;
   const bool colok = col < q.BLP;
-  stage_weights(wt, q, col0, ws);
   for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) dws[i] = 0.0f;
   for (int i = threadIdx.x; i < kChunk; i += blockDim.x) cs[i] = 0.0f;
   __syncthreads();
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  const float4* wsv = reinterpret_cast<const float4*>(ws);
+  // rule weights of this chunk from global memory (L1-resident): W[ch] at wt + ch * BLP + col
+  auto wload = [&](int64_t ch) -> float4 {
+    return colok ? __ldg(reinterpret_cast<const float4*>(wt + ch * q.BLP + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
   float4 spart = zero;
   TaskCursor cursor(queue + chunk * kQueueStride, ntasks);
   int64_t t;
@@ -763,7 +751,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) bwd_pull_kernel(
       const float4 xr = colok ? *reinterpret_cast<const float4*>(x + row * q.BLP + col) : zero;
       if ((tk.w & kTaskFirst) && colok) {
         const float4 ds = *reinterpret_cast<const float4*>(dy + row * q.BLP + col);
-        const float4 wi = wsv[(q.n - 1) * 32 + lane];
+        const float4 wi = wload(q.n - 1);
         gx = f4_mul(ds, wi);
         float* dwi = dws + (q.n - 1) * kChunk;
         if (ds.x != 0.f) atomicAdd(dwi + 0 * 32 + lane, ds.x * xr.x);
@@ -773,9 +761,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) bwd_pull_kernel(
       }
       float4 run = zero;  // sum of dY * m over the current channel run
       int cur = -1;
+      float4 wcur = zero;  // W[cur] of this chunk, loaded once per run
+      float4 xw = zero;    // X[s] * W[cur]: the run's factor of the edge-score gradient
       auto flush = [&]() {
         if (cur < 0) return;
-        const float4 wc = wsv[cur * 32 + lane];
+        const float4 wc = wcur;
         gx.x = fmaf(run.x, wc.x, gx.x); gx.y = fmaf(run.y, wc.y, gx.y);
         gx.z = fmaf(run.z, wc.z, gx.z); gx.w = fmaf(run.w, wc.w, gx.w);
         float* dwc = dws + cur * kChunk;
@@ -818,23 +808,27 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 2) bwd_pull_kernel(
           for (int u = 0; u < kBatch; ++u) {
             ep[u] = 0.0f;
             if (!ok[u]) continue;
-            if (ch[u] != cur) { flush(); cur = ch[u]; }
+            if (ch[u] != cur) {
+              flush();
+              cur = ch[u];
+              wcur = wload(cur);
+              xw = f4_mul(xr, wcur);
+            }
             run.x = fmaf(gv[u].x, m[u], run.x); run.y = fmaf(gv[u].y, m[u], run.y);
             run.z = fmaf(gv[u].z, m[u], run.z); run.w = fmaf(gv[u].w, m[u], run.w);
             if (grad_edge != nullptr) {
-              const float4 wv = wsv[ch[u] * 32 + lane];
-              ep[u] = gv[u].x * xr.x * wv.x + gv[u].y * xr.y * wv.y + gv[u].z * xr.z * wv.z + gv[u].w * xr.w * wv.w;
+              ep[u] = gv[u].x * xw.x + gv[u].y * xw.y + gv[u].z * xw.z + gv[u].w * xw.w;
             }
           }
           if (grad_edge != nullptr) {
-            const float tot = reduce_scatter8(ep);
-            const int idx = (lane >> 2) & 7;
+            const float tot = reduce_scatter4(ep);
+            const int idx = (lane >> 3) & 3;
             int f = -1;
             float mm = 0.0f;
 #pragma unroll
             for (int u = 0; u < kBatch; ++u)
               if (idx == u && ok[u]) { f = fa[u]; mm = m[u]; }
-            if ((lane & 3) == 0 && f >= 0 && tot != 0.0f) {
+            if ((lane & 7) == 0 && f >= 0 && tot != 0.0f) {
               if (f < num_facts) atomicAdd(grad_edge + f, tot * mm * edge_grad_scale(ef, f));
               else raise_flag(err, MKG_DEV_BAD_FACT);
             }
@@ -989,7 +983,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __
   if (threadIdx.x == 0) counts[b] = m;
 }
 
-size_t bwd_smem(const ProofDims& q) { return 4 * (2 * (size_t)q.n * kChunk + kChunk); }
+size_t bwd_smem(const ProofDims& q) { return 4 * ((size_t)q.n * kChunk + kChunk); }
 
 // Columns per lane of the forward pull: 8 (two float4) for batches wider than 128
 // columns; MKG_FWD_VEC=1|2 overrides (a tuning knob).
