@@ -21,7 +21,8 @@ merges per-rank candidates (score descending, then tail ascending, decode_core.p
 candidates, with equal scores ordered by entity id.
 
 Gradients: the gather's backward all-reduces the frontier gradient and hands each rank the
-slice of its own entries; the column sums' backward all-reduces; inputs replicated on every
+slice of its own entries; the normalisation's written-out backward all-reduces its row sums
+(``_NormalizeMass``); inputs replicated on every
 rank (rule weights, edge scores) pass through ``replicated`` whose backward all-reduces, so
 every rank ends with the full gradient of the sum of all ranks' local results.  Every rank
 issues the same collectives in the same order, including for empty local frontiers.
@@ -86,19 +87,22 @@ def replicated(x: torch.Tensor, group=None) -> torch.Tensor:
     return _Replicated.apply(x, group)
 
 
-class _AllReduceSum(autograd.Function):
+class _Select(autograd.Function):
+    """``v[sel]`` for unique positions ``sel``; the backward writes the gradient back without
+    the accumulating index-put a general gather would need."""
+
     @staticmethod
-    def forward(ctx, x, group):
-        ctx.group = group
-        y = x.contiguous().clone()
-        dist.all_reduce(y, group=group)
-        return y
+    def forward(ctx, v, sel):
+        ctx.save_for_backward(sel)
+        ctx.n = int(v.numel())
+        return v[sel]
 
     @staticmethod
     def backward(ctx, g):
-        g = g.contiguous().clone()
-        dist.all_reduce(g, group=ctx.group)
-        return g, None
+        sel, = ctx.saved_tensors
+        out = torch.zeros(ctx.n, dtype=g.dtype, device=g.device)
+        out[sel] = g
+        return out, None
 
 
 def _all_gather_padded(t: torch.Tensor, counts: list[int], group) -> list[torch.Tensor]:
@@ -155,6 +159,52 @@ class _GatherFrontier(autograd.Function):
             off += c
         dist.all_reduce(pad, group=ctx.group)
         return None, pad[ctx.rank, : counts[ctx.rank]].clone(), None
+
+
+class _NormalizeMass(autograd.Function):
+    """normalize_sparse3d(.., 0, "mass") (drum.py:31-50) on this rank's key-sorted entries with
+    the per-(b, l) row sums all-reduced over ranks, then the optional state threshold:
+    ``x = (y / d) * min(d, 1)`` for y != 0; returns the kept positions (non-differentiable)
+    and their values.  The backward is written out -- ``dy = dx * c / d + g_d[row]`` with
+    ``g_d = sum_row(-dx * c * y / d^2) + [d <= 1] * sum_row(dx * y / d)``, the row sums again
+    all-reduced -- so no gather / index-put backward of torch runs on the entries."""
+
+    @staticmethod
+    def forward(ctx, y, rows, nrows: int, threshold: float, group):
+        yd = y.detach()
+        d = torch.zeros(nrows, dtype=yd.dtype, device=yd.device).index_add_(0, rows, yd)
+        dist.all_reduce(d, group=group)
+        dr = d[rows]
+        c = d.clamp_max(1.0)
+        nz = yd != 0
+        x = torch.where(nz, yd / dr * c[rows], torch.zeros_like(yd))
+        keep = x != 0
+        if threshold > 0:
+            keep &= x >= threshold
+        sel = torch.nonzero(keep, as_tuple=True)[0]
+        ctx.save_for_backward(yd, rows, d, sel)
+        ctx.group, ctx.nrows, ctx.n = group, nrows, int(yd.numel())
+        ctx.mark_non_differentiable(sel)
+        return sel, x[sel]
+
+    @staticmethod
+    def backward(ctx, _g_sel, gx_sel):
+        y, rows, d, sel = ctx.saved_tensors
+        gx = torch.zeros(ctx.n, dtype=gx_sel.dtype, device=gx_sel.device)
+        gx[sel] = gx_sel  # unique positions: no accumulation needed
+        nz = y != 0
+        dr = d[rows]
+        c = d.clamp_max(1.0)
+        q = torch.where(nz, y / dr, torch.zeros_like(y))
+        g_q = gx * c[rows]
+        zero = torch.zeros_like(y)
+        part = torch.zeros((2, ctx.nrows), dtype=y.dtype, device=y.device)
+        part[0].index_add_(0, rows, torch.where(nz, gx * q, zero))
+        part[1].index_add_(0, rows, torch.where(nz, -(g_q * y) / (dr * dr), zero))
+        dist.all_reduce(part, group=ctx.group)
+        g_d = part[1] + torch.where(d <= 1.0, part[0], torch.zeros_like(part[0]))
+        gy = torch.where(nz, g_q / dr + g_d[rows], zero)
+        return gy, None, None, None, None
 
 
 # ----------------------------------------------------------------------------- the loop
@@ -220,8 +270,8 @@ def _prune_global(keys, vals, E: int, topk_nodes: int, spec: ShardSpec):
     keep_ids = ids[o1][o2][:k]
     keep_ent = torch.zeros(hi - lo, dtype=torch.bool, device=dev)
     keep_ent[keep_ids[(keep_ids >= lo) & (keep_ids < hi)] - lo] = True
-    sel = keep_ent[ent - lo]
-    return keys[sel], vals[sel]
+    sel = torch.nonzero(keep_ent[ent - lo], as_tuple=True)[0]
+    return keys[sel], _Select.apply(vals, sel)
 
 
 def message_counter(graph, cap: int):
@@ -262,17 +312,9 @@ def sharded_proof_scores(spec: ShardSpec, hop_fn: HopFn, heads: torch.Tensor, w_
             msgs_out.append(msg_counter(k_all % E))
         # the op's (ori + inv + ind) for this rank's destinations, coalesced in key order
         keys, y = hop_fn(k_all, v_all, w_rep[h], lo, hi)
-        # normalize_sparse3d(.., 0, "mass") with global column sums
-        nz = y != 0
-        keys, y = keys[nz], y[nz]
-        rows = keys // E
-        d_loc = torch.zeros(B * L, dtype=y.dtype, device=dev).index_add(0, rows, y)
-        dsum = _AllReduceSum.apply(d_loc, spec.group)
-        x = y / dsum[rows] * dsum.clamp_max(1.0)[rows]
-        keep = x != 0
-        if threshold > 0:
-            keep &= x >= threshold
-        keys, vals = keys[keep], x[keep]
+        # normalize_sparse3d(.., 0, "mass") with global column sums, then the threshold
+        sel, vals = _NormalizeMass.apply(y, keys // E, B * L, float(threshold), spec.group)
+        keys = keys[sel]
     # sum_sp_3d: sum over rules
     be, e = keys // E, keys % E
     return _coalesce_sum((be // L) * E + e, vals)
