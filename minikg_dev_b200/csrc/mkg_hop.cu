@@ -26,6 +26,7 @@ constexpr int kTileThreads = 256;
 constexpr int kHubStageMax = 4096;  // rule-weight rows up to this many channels are staged in smem
 constexpr int64_t kHashRatio = 32;  // hash tables when 32 * msg_bound < key space
 constexpr int64_t kMinSlots = 1024;
+constexpr int64_t kMaxSlots = int64_t(1) << 30;  // CUB sorts take an int item count
 
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -903,6 +904,11 @@ int hop_forward(const mkg_graph* g, const mkg_frontier* fr, const float* w, cons
   if (rc) return rc;
   MKG_REQUIRE(counts_out, "hop_forward: counts_out is null");
   HopLayout lay = forward_layout(*p, fr->nnz);
+  if (lay.hash && (lay.capm > kMaxSlots || lay.capf > kMaxSlots)) {
+    set_error("hop_forward: %lld messages per direction exceed one hash table (2^30 slots); split the batch",
+              (long long)p->msg_bound);
+    return MKG_ERR_CAPACITY;
+  }
   MKG_REQUIRE(ws && ws_bytes >= lay.total, "hop_forward: workspace too small (%zu < %zu)", ws_bytes, lay.total);
   char* base = static_cast<char*>(ws);
   const int64_t BLE = lay.BLE, F = fr->nnz;
@@ -1075,6 +1081,11 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
                     fhead && ftail && frel,
                 "hop_backward: agg_mode 1 needs the forward outputs, their argmax facts and the fact table");
   HopLayout lay = backward_layout(*p, fr->nnz);
+  if (lay.hash && (lay.capm > kMaxSlots || lay.capf > kMaxSlots)) {
+    set_error("hop_backward: %lld messages per direction exceed one hash table (2^30 slots)",
+              (long long)p->msg_bound);
+    return MKG_ERR_CAPACITY;
+  }
   MKG_REQUIRE(ws && ws_bytes >= lay.total, "hop_backward: workspace too small (%zu < %zu)", ws_bytes, lay.total);
   const bool merge = p->merge_outputs != 0;
   const mkg_coo3* gl[3] = {g_ori, g_inv, g_ind};
