@@ -41,7 +41,8 @@ enum {
   MKG_DEV_BAD_KEY = 8u,    /* gradient COO key outside [B, L, E] */
   MKG_DEV_BAD_REL = 16u,   /* relation id outside [0, R) */
   MKG_DEV_TIMEOUT = 32u,   /* a bounded wait inside a kernel gave up */
-  MKG_DEV_TABLE_FULL = 64u /* a message hash table ran out of slots (msg_bound too small) */
+  MKG_DEV_TABLE_FULL = 64u, /* a message hash table ran out of slots (msg_bound too small) */
+  MKG_DEV_BAD_RULE_INDEX = 128u /* rule producer: relation outside [0, n) or query map outside [0, U) */
 };
 
 /* One direction of the reference CSR pair (fastlog_kernel.py:403-410 tuple order). */
@@ -328,6 +329,59 @@ int mkg_segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* v
  * key-sorted sparse state, without atomics on the few row bins.  No reference counterpart
  * (the reference coalesces and index_puts). */
 int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, mkg_stream stream);
+
+/* ------------------------------------------------------------ rule-weight producer */
+
+typedef struct mkg_rule_params {
+  int64_t n;   /* channels 2R + 1: rows of the relation embedding, outputs of the linear layer */
+  int64_t H;   /* embedding size = LSTM input and hidden size (1 .. 112) */
+  int64_t L;   /* rules: one bidirectional single-layer LSTM each */
+  int64_t K;   /* hops: the LSTM sequence has K + 1 steps, the last output is dropped */
+  int64_t U;   /* distinct target relations */
+  int64_t B;   /* queries */
+  float tau;   /* softmax temperature (tau_1) */
+  int32_t reserved;
+} mkg_rule_params;
+
+/* Rule logits of the shared parametrisation: replaces SupplyGatedDRUM._shared_rule_logits
+ * (drum.py:429-438) evaluated once per distinct target relation.  Parameters are fp32:
+ * emb [n, H]; w_ih, w_hh [L, 2, 4H, H] (direction 0 = forward, 1 = reverse; gate rows i, f,
+ * g, o as torch.nn.LSTM's weight_ih_l0 / weight_ih_l0_reverse); bias [L, 2, 4H] = b_ih + b_hh;
+ * w_lin [n, 2H], b_lin [n]; rel_u [U] (int64, in [0, n)).  Writes logits_u [U, K, L, n]
+ * (row u = the reference's output for a query of relation rel_u[u]) and keeps the LSTM
+ * activations in `saved` (mkg_rule_saved_bytes) for the backward. */
+size_t mkg_rule_saved_bytes(const mkg_rule_params* p);
+int mkg_rule_logits_forward(const mkg_rule_params* p, const float* emb, const float* w_ih,
+                            const float* w_hh, const float* bias, const float* w_lin,
+                            const float* b_lin, const int64_t* rel_u, float* logits_u, void* saved,
+                            size_t saved_bytes, unsigned* dev_err, mkg_stream stream);
+
+/* Gradients of mkg_rule_logits_forward for grad_logits_u [U, K, L, n]: grad_emb [n, H],
+ * grad_w_ih / grad_w_hh [L, 2, 4H, H], grad_bias [L, 2, 4H] (the gradient of b_ih and of
+ * b_hh alike), grad_w_lin [n, 2H], grad_b_lin [n], all overwritten; sums in a fixed order
+ * (no atomics). */
+size_t mkg_rule_backward_workspace_bytes(const mkg_rule_params* p);
+int mkg_rule_logits_backward(const mkg_rule_params* p, const float* emb, const float* w_ih,
+                             const float* w_hh, const float* w_lin, const int64_t* rel_u,
+                             const void* saved, size_t saved_bytes, const float* grad_logits_u,
+                             float* grad_emb, float* grad_w_ih, float* grad_w_hh, float* grad_bias,
+                             float* grad_w_lin, float* grad_b_lin, void* workspace,
+                             size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+
+/* Per-hop rule weights of the hop loop (proof.py:569-571, decode_core.py:304):
+ * w_hops[t, b, l, :] = softmax(logits_u[query_u[b], t, l, :] / tau), w_hops [K, B, L, n];
+ * query_u [B] (int64, in [0, U)). */
+int mkg_rule_softmax_forward(const mkg_rule_params* p, const float* logits_u, const int64_t* query_u,
+                             float* w_hops, unsigned* dev_err, mkg_stream stream);
+
+/* Gradient of mkg_rule_softmax_forward: grad_logits_u [U, K, L, n] (overwritten) from
+ * w_hops and grad_w_hops [K, B, L, n]; the queries of relation u are
+ * query_perm[query_ptr[u] .. query_ptr[u+1]) (int64 CSR), summed in that order. */
+size_t mkg_rule_softmax_workspace_bytes(const mkg_rule_params* p);
+int mkg_rule_softmax_backward(const mkg_rule_params* p, const float* w_hops, const float* grad_w_hops,
+                              const int64_t* query_ptr, const int64_t* query_perm,
+                              float* grad_logits_u, void* workspace, size_t workspace_bytes,
+                              unsigned* dev_err, mkg_stream stream);
 
 #ifdef __cplusplus
 }

@@ -5,6 +5,8 @@ Public surface:
   build_csr_structure, sum_sp_3d, sum_sparse3d_concat) and ``kernel_ops()``;
 * ``proof``: the fused multi-hop engine (``kernel_sparse_scores``, ``proof_scores``,
   ``decode_max``, ``decode_topk``);
+* ``rules``: the rule-weight producer (``build_rule_logits``, ``rule_weights``: the per-rule
+  bidirectional LSTMs, linear layer and per-hop softmax on the device);
 * ``graph``: device CSR build and ``DeviceGraph``;
 * ``synth``: seeded synthetic knowledge graphs of the benchmark shapes.
 The CUDA code lives in ``csrc/`` and is built into ``_lib/libminikg_b200.so`` by

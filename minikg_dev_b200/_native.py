@@ -20,7 +20,8 @@ MASK_NONE, MASK_U8, MASK_F32 = 0, 1, 2
 DEV_ERR_NAMES = {1: "frontier entry outside [B, L, E]", 2: "CSR column outside [0, E)",
                  4: "fact id outside [0, T)", 8: "gradient key outside [B, L, E]",
                  16: "relation id outside its range", 32: "a bounded wait inside a kernel gave up",
-                 64: "a message hash table ran out of slots (msg_bound too small)"}
+                 64: "a message hash table ran out of slots (msg_bound too small)",
+                 128: "rule producer: relation outside [0, n) or query map outside [0, U)"}
 
 vp = C.c_void_p
 i64 = C.c_int64
@@ -71,6 +72,11 @@ class ProofParams(C.Structure):
                 ("state_threshold", C.c_float), ("reserved", i32), ("fwd_events", vp), ("bwd_events", vp)]
 
 
+class RuleParams(C.Structure):
+    _fields_ = [("n", i64), ("H", i64), ("L", i64), ("K", i64), ("U", i64), ("B", i64), ("tau", C.c_float),
+                ("reserved", i32)]
+
+
 P = C.POINTER
 # name -> (restype, argtypes); every name here must be exported by the library
 SIGNATURES = {
@@ -107,6 +113,15 @@ SIGNATURES = {
     "mkg_decode_topk": (C.c_int, [vp, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_segment_sum_ordered": (C.c_int, [vp, i64, vp, vp, vp]),
     "mkg_segment_sum": (C.c_int, [vp, i64, vp, vp, vp]),
+    "mkg_rule_saved_bytes": (C.c_size_t, [P(RuleParams)]),
+    "mkg_rule_backward_workspace_bytes": (C.c_size_t, [P(RuleParams)]),
+    "mkg_rule_softmax_workspace_bytes": (C.c_size_t, [P(RuleParams)]),
+    "mkg_rule_logits_forward": (C.c_int, [P(RuleParams), vp, vp, vp, vp, vp, vp, vp, vp, vp, C.c_size_t, vp,
+                                          vp]),
+    "mkg_rule_logits_backward": (C.c_int, [P(RuleParams), vp, vp, vp, vp, vp, vp, C.c_size_t, vp, vp, vp, vp, vp,
+                                           vp, vp, vp, C.c_size_t, vp, vp]),
+    "mkg_rule_softmax_forward": (C.c_int, [P(RuleParams), vp, vp, vp, vp, vp]),
+    "mkg_rule_softmax_backward": (C.c_int, [P(RuleParams), vp, vp, vp, vp, vp, vp, C.c_size_t, vp, vp]),
 }
 
 _lib = None

@@ -20,6 +20,8 @@ from typing import Sequence
 import numpy as np
 import torch
 
+from . import rules
+
 
 @dataclass(frozen=True)
 class TnbBatchPlan:
@@ -67,10 +69,16 @@ def prepare_rule_first_hop_prune(model, relations: Sequence[int], facts, hard_su
     R = int(model.relation_count)
     active_by_relation: dict[int, list[int]] = {}
     with torch.no_grad():
-        for relation in relations:
-            logits = model.build_rule_logits(torch.tensor([relation], device=model.emb.device))
-            weights = torch.softmax(logits[:, 0, :, :] / model.tau_1, dim=-1)
-            active_by_relation[int(relation)] = rule_first_hop_channels(weights, threshold).cpu().tolist()
+        if rules.has_lstm_producer(model) and model.emb.is_cuda and len(relations):
+            # every relation at once through the device producer: hop-0 weights [U, L, n]
+            w0 = rules.rule_weights(model, torch.tensor([int(r) for r in relations], device=model.emb.device))[0]
+            for i, relation in enumerate(relations):
+                active_by_relation[int(relation)] = rule_first_hop_channels(w0[i:i + 1], threshold).cpu().tolist()
+        else:
+            for relation in relations:
+                logits = model.build_rule_logits(torch.tensor([relation], device=model.emb.device))
+                weights = torch.softmax(logits[:, 0, :, :] / model.tau_1, dim=-1)
+                active_by_relation[int(relation)] = rule_first_hop_channels(weights, threshold).cpu().tolist()
     wanted = sorted({c % R for chans in active_by_relation.values() for c in chans if c < 2 * R})
     ft = _facts_tensor(facts)
     dev = ft.device

@@ -38,7 +38,7 @@ using mkg::set_error;
 static cudaStream_t S(mkg_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 
 MKG_API const char* mkg_last_error(void) { return mkg::g_last_error; }
-MKG_API int mkg_abi_version(void) { return 4; }
+MKG_API int mkg_abi_version(void) { return 5; }
 
 MKG_API size_t mkg_csr_build_workspace_bytes(int64_t T, int64_t E, int64_t R) {
   return mkg::csr_build_workspace_bytes(T, E, R);
@@ -140,4 +140,38 @@ MKG_API int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* v
 MKG_API int mkg_segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out,
                                     mkg_stream st) {
   return mkg::segment_sum_ordered(seg_ptr, nseg, values, out, S(st));
+}
+
+MKG_API size_t mkg_rule_saved_bytes(const mkg_rule_params* p) { return mkg::rule_saved_bytes(p); }
+MKG_API size_t mkg_rule_backward_workspace_bytes(const mkg_rule_params* p) {
+  return mkg::rule_backward_workspace_bytes(p);
+}
+MKG_API size_t mkg_rule_softmax_workspace_bytes(const mkg_rule_params* p) {
+  return mkg::rule_softmax_workspace_bytes(p);
+}
+MKG_API int mkg_rule_logits_forward(const mkg_rule_params* p, const float* emb, const float* w_ih,
+                                    const float* w_hh, const float* bias, const float* w_lin, const float* b_lin,
+                                    const int64_t* rel_u, float* logits_u, void* saved, size_t saved_bytes,
+                                    unsigned* err, mkg_stream st) {
+  return mkg::rule_logits_forward(p, emb, w_ih, w_hh, bias, w_lin, b_lin, rel_u, logits_u, saved, saved_bytes, err,
+                                  S(st));
+}
+MKG_API int mkg_rule_logits_backward(const mkg_rule_params* p, const float* emb, const float* w_ih,
+                                     const float* w_hh, const float* w_lin, const int64_t* rel_u, const void* saved,
+                                     size_t saved_bytes, const float* grad_logits_u, float* grad_emb,
+                                     float* grad_w_ih, float* grad_w_hh, float* grad_bias, float* grad_w_lin,
+                                     float* grad_b_lin, void* ws, size_t ws_bytes, unsigned* err, mkg_stream st) {
+  return mkg::rule_logits_backward(p, emb, w_ih, w_hh, w_lin, rel_u, saved, saved_bytes, grad_logits_u, grad_emb,
+                                   grad_w_ih, grad_w_hh, grad_bias, grad_w_lin, grad_b_lin, ws, ws_bytes, err,
+                                   S(st));
+}
+MKG_API int mkg_rule_softmax_forward(const mkg_rule_params* p, const float* logits_u, const int64_t* query_u,
+                                     float* w_hops, unsigned* err, mkg_stream st) {
+  return mkg::rule_softmax_forward(p, logits_u, query_u, w_hops, err, S(st));
+}
+MKG_API int mkg_rule_softmax_backward(const mkg_rule_params* p, const float* w_hops, const float* grad_w_hops,
+                                      const int64_t* query_ptr, const int64_t* query_perm, float* grad_logits_u,
+                                      void* ws, size_t ws_bytes, unsigned* err, mkg_stream st) {
+  return mkg::rule_softmax_backward(p, w_hops, grad_w_hops, query_ptr, query_perm, grad_logits_u, ws, ws_bytes, err,
+                                    S(st));
 }

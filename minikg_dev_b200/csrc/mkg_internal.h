@@ -57,4 +57,22 @@ int decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* t
 int segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st);
 int segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st);
 
+// mkg_rules.cu
+size_t rule_saved_bytes(const mkg_rule_params* p);
+size_t rule_backward_workspace_bytes(const mkg_rule_params* p);
+size_t rule_softmax_workspace_bytes(const mkg_rule_params* p);
+int rule_logits_forward(const mkg_rule_params* p, const float* emb, const float* w_ih, const float* w_hh,
+                        const float* bias, const float* w_lin, const float* b_lin, const int64_t* rel_u,
+                        float* logits_u, void* saved, size_t saved_bytes, unsigned* err, cudaStream_t st);
+int rule_logits_backward(const mkg_rule_params* p, const float* emb, const float* w_ih, const float* w_hh,
+                         const float* w_lin, const int64_t* rel_u, const void* saved, size_t saved_bytes,
+                         const float* grad_logits_u, float* grad_emb, float* grad_w_ih, float* grad_w_hh,
+                         float* grad_bias, float* grad_w_lin, float* grad_b_lin, void* ws, size_t ws_bytes,
+                         unsigned* err, cudaStream_t st);
+int rule_softmax_forward(const mkg_rule_params* p, const float* logits_u, const int64_t* query_u, float* w_hops,
+                         unsigned* err, cudaStream_t st);
+int rule_softmax_backward(const mkg_rule_params* p, const float* w_hops, const float* grad_w_hops,
+                          const int64_t* query_ptr, const int64_t* query_perm, float* grad_logits_u, void* ws,
+                          size_t ws_bytes, unsigned* err, cudaStream_t st);
+
 }  // namespace mkg

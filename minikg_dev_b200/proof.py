@@ -26,6 +26,7 @@ import torch
 from . import _native as N
 from .fastlog_kernel import HopRange
 from .graph import DeviceGraph, build_csr_structure
+from .rules import rule_weights
 from .sparse_reducers import (max_sp_3d, normalize_sparse3d, prune_sparse3d_active_entities, sparse3d_max, sum_sp_3d,
                               sum_sparse3d_concat)
 
@@ -331,23 +332,24 @@ def kernel_sparse_scores(model, heads, rels, graph, args, is_training: bool, den
     """
     g = _device_graph_for(model, graph)
     B, L, E, R, K = heads.shape[0], model.rules, model.entity_count, model.relation_count, model.step
-    rule_logits = model.build_rule_logits(rels)
+    # rule weights of every hop, [K, B, L, n] (proof.py:524, 569-571): the LSTM producer and the
+    # softmax on the device (rules.py)
+    w_all = rule_weights(model, rels)
     edge_scores, mask, is_score, scale = _edge_inputs(model, graph, is_training)
     topk_edges = int(args.kernel_topk_edges)
     topk_nodes = int(args.kernel_topk_nodes)
     p_drop = float(getattr(getattr(model, "dropout", None), "p", 0.0) or 0.0)
     fused = topk_edges >= UNCAPPED and (topk_nodes <= 0 or topk_nodes >= E) and not (is_training and p_drop > 0)
     if fused:
-        w_hops = torch.stack([torch.softmax(rule_logits[:, h] / model.tau_1, dim=-1) for h in range(K)])
-        out, _ = HopLoopSum.apply(w_hops, edge_scores, heads, g, mask, is_score, scale, 0.0)
+        out, _ = HopLoopSum.apply(w_all, edge_scores, heads, g, mask, is_score, scale, 0.0)
         return out if dense else out.to_sparse_coo().coalesce()
-    w_hops = [torch.softmax(rule_logits[:, hop] / model.tau_1, dim=-1) for hop in range(K)]
     if not (is_training and p_drop > 0):
         # any cap / prune: the sparse loop fused around the op (merged outputs, written-out backward)
         from .sparse_loop import sparse_proof_scores
-        out, _ = sparse_proof_scores(g, heads, torch.stack(w_hops), edge_scores, mask, is_score, scale, topk_edges,
+        out, _ = sparse_proof_scores(g, heads, w_all, edge_scores, mask, is_score, scale, topk_edges,
                                      topk_nodes, 0.0, dense=dense)
         return out
+    w_hops = [w_all[hop] for hop in range(K)]
     # dropout while training: hop by hop, as the reference composes it
     out = sparse_hop_loop(g, heads, w_hops, edge_scores, mask, is_score, scale, topk_edges, topk_nodes,
                           dropout=model.dropout)

@@ -795,3 +795,173 @@ class RelationAccumulator:
     def counters(self):
         return [self.candidate_total, self.max_candidate_count, self.query_count, self.selected,
                 self.selected_wrong, self.new, self.new_true]
+
+
+# ----------------------------------------------------------------- rule-weight producer
+# SupplyGatedDRUM._shared_rule_logits / build_rule_logits (drum.py:429-467) and the per-hop
+# softmax of proof.py:569-571, per query row as the reference computes them, in float64.
+# ``params``: emb [n, H]; lstm: list over rules of dicts with w_ih, w_hh [2, 4H, H] and
+# b_ih, b_hh [2, 4H] (direction 0 = forward, 1 = reverse; torch.nn.LSTM gate rows i, f, g, o);
+# w_lin [n, 2H], b_lin [n].
+
+def _sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def _lstm_direction(xs, w_ih, w_hh, b, reverse):
+    """One LSTM direction over xs [S, B, H] (torch.nn.LSTM, drum.py:305): per step the
+    activated gates (i, f, g, o), c and h, indexed by time."""
+    S, B, H = xs.shape
+    h = np.zeros((B, H))
+    c = np.zeros((B, H))
+    gates, cs, hs = [None] * S, [None] * S, [None] * S
+    for t in (range(S - 1, -1, -1) if reverse else range(S)):
+        pre = xs[t] @ w_ih.T + h @ w_hh.T + b
+        i, f, g, o = _sigmoid(pre[:, :H]), _sigmoid(pre[:, H:2 * H]), np.tanh(pre[:, 2 * H:3 * H]), \
+            _sigmoid(pre[:, 3 * H:])
+        c = f * c + i * g
+        h = o * np.tanh(c)
+        gates[t], cs[t], hs[t] = (i, f, g, o), c, h
+    return gates, cs, hs
+
+
+def shared_rule_logits(params, rels, K):
+    """logits [B, K, L, n] of drum.py:429-438 (sequence [emb[rel]] * K + [emb[-1]]) and the
+    trace the backward needs."""
+    emb = np.asarray(params["emb"], np.float64)
+    rels = np.asarray(rels, np.int64)
+    B = rels.size
+    xs = np.stack([emb[rels]] * K + [np.broadcast_to(emb[-1], (B, emb.shape[1]))])  # [K+1, B, H]
+    w_lin = np.asarray(params["w_lin"], np.float64)
+    b_lin = np.asarray(params["b_lin"], np.float64)
+    out, trace = [], []
+    for lp in params["lstm"]:
+        dirs = []
+        for d in range(2):
+            b = np.asarray(lp["b_ih"][d], np.float64) + np.asarray(lp["b_hh"][d], np.float64)
+            dirs.append(_lstm_direction(xs, np.asarray(lp["w_ih"][d], np.float64),
+                                        np.asarray(lp["w_hh"][d], np.float64), b, reverse=d == 1))
+        o = np.concatenate([np.stack(dirs[0][2]), np.stack(dirs[1][2])], axis=-1)  # [K+1, B, 2H]
+        out.append(o[:K].transpose(1, 0, 2) @ w_lin.T + b_lin)                     # [B, K, n]
+        trace.append((dirs, o))
+    return np.stack(out, axis=2), (xs, trace)
+
+
+def invert_rule_logits(logits, R):
+    """tclm_invert_rule_logits (drum.py:238-243)."""
+    sw = np.concatenate([logits[..., R:2 * R], logits[..., :R], logits[..., 2 * R:]], axis=-1)
+    return sw[:, ::-1]
+
+
+def rule_softmax(logits, tau):
+    """w [K, B, L, n] = softmax(logits[:, hop] / tau) per hop (proof.py:571)."""
+    z = np.asarray(logits, np.float64) / tau
+    z = z - z.max(axis=-1, keepdims=True)
+    e = np.exp(z)
+    return (e / e.sum(axis=-1, keepdims=True)).transpose(1, 0, 2, 3)
+
+
+def rule_softmax_backward(w, grad_w, tau):
+    """d loss / d logits [B, K, L, n] from w, grad_w [K, B, L, n]."""
+    g = w * (grad_w - (w * grad_w).sum(axis=-1, keepdims=True)) / tau
+    return g.transpose(1, 0, 2, 3)
+
+
+def shared_rule_logits_backward(params, rels, K, trace, grad_logits):
+    """Gradients of shared_rule_logits for grad_logits [B, K, L, n] (BPTT of each direction):
+    dict of emb, w_lin, b_lin and per rule w_ih, w_hh, b (= grad of b_ih = grad of b_hh)."""
+    xs, rule_traces = trace
+    emb = np.asarray(params["emb"], np.float64)
+    w_lin = np.asarray(params["w_lin"], np.float64)
+    rels = np.asarray(rels, np.int64)
+    S, B, H = xs.shape
+    g_emb = np.zeros_like(emb)
+    g_wlin = np.zeros_like(w_lin)
+    g_blin = np.zeros(w_lin.shape[0])
+    rules = []
+    for l, (lp, (dirs, o)) in enumerate(zip(params["lstm"], rule_traces)):
+        gl = grad_logits[:, :, l, :].transpose(1, 0, 2)            # [K, B, n]
+        g_wlin += np.einsum("tbn,tbk->nk", gl, o[:K])
+        g_blin += gl.sum(axis=(0, 1))
+        g_o = np.zeros((S, B, 2 * H))
+        g_o[:K] = gl @ w_lin
+        per_dir = {"w_ih": [], "w_hh": [], "b": []}
+        g_x = np.zeros_like(xs)
+        for d in range(2):
+            gates, cs, hs = dirs[d]
+            w_ih = np.asarray(lp["w_ih"][d], np.float64)
+            w_hh = np.asarray(lp["w_hh"][d], np.float64)
+            order = list(range(S - 1, -1, -1)) if d == 1 else list(range(S))
+            gw_ih, gw_hh, gb = np.zeros_like(w_ih), np.zeros_like(w_hh), np.zeros(4 * H)
+            dh_next = np.zeros((B, H))
+            dc_next = np.zeros((B, H))
+            for s in range(S - 1, -1, -1):
+                t = order[s]
+                i, f, g, o_ = gates[t]
+                c = cs[t]
+                c_prev = cs[order[s - 1]] if s > 0 else np.zeros((B, H))
+                h_prev = hs[order[s - 1]] if s > 0 else np.zeros((B, H))
+                dh = dh_next + g_o[t, :, d * H:(d + 1) * H]
+                tc = np.tanh(c)
+                dc = dc_next + dh * o_ * (1 - tc * tc)
+                dpre = np.concatenate([dc * g * i * (1 - i), dc * c_prev * f * (1 - f), dc * i * (1 - g * g),
+                                       dh * tc * o_ * (1 - o_)], axis=1)
+                dc_next = dc * f
+                dh_next = dpre @ w_hh
+                g_x[t] += dpre @ w_ih
+                gw_ih += dpre.T @ xs[t]
+                gw_hh += dpre.T @ h_prev
+                gb += dpre.sum(axis=0)
+            per_dir["w_ih"].append(gw_ih)
+            per_dir["w_hh"].append(gw_hh)
+            per_dir["b"].append(gb)
+        np.add.at(g_emb, rels, g_x[:K].sum(axis=0))
+        g_emb[-1] += g_x[K].sum(axis=0)
+        rules.append({k: np.stack(v) for k, v in per_dir.items()})
+    return {"emb": g_emb, "w_lin": g_wlin, "b_lin": g_blin, "lstm": rules}
+
+
+def build_rule_logits(params, rels, K, R, penalty=0.0, invert=False, table_index=None, table=None):
+    """SupplyGatedDRUM.build_rule_logits (drum.py:440-467): the shared logits, or the target
+    table's rows where a relation has one (all mapped: the table alone), the same-relation
+    channel penalty, then the TCLM inversion.  Returns (logits [B, K, L, n], backward), where
+    backward(grad_logits) -> the gradient dict of shared_rule_logits_backward plus "table"."""
+    rels = np.asarray(rels, np.int64)
+    B = rels.size
+    trace, row, mapped = None, None, None
+    if table_index is not None:
+        row = np.asarray(table_index)[rels]
+        mapped = row >= 0
+        if mapped.all():
+            logits = np.asarray(table, np.float64)[row]
+        else:
+            logits, trace = shared_rule_logits(params, rels, K)
+            logits = logits.copy()
+            logits[mapped] = np.asarray(table, np.float64)[row[mapped]]
+    else:
+        logits, trace = shared_rule_logits(params, rels, K)
+    if penalty > 0:
+        logits = logits.copy()
+        rows = np.arange(B)
+        logits[rows, :, :, rels] -= penalty
+        logits[rows, :, :, rels + R] -= penalty
+    if invert:
+        logits = invert_rule_logits(logits, R)
+
+    def backward(grad_logits):
+        g = np.asarray(grad_logits, np.float64)
+        if invert:
+            g = invert_rule_logits(g, R)  # an involution
+        grads = {}
+        if table_index is not None:
+            gt = np.zeros(np.asarray(table).shape)
+            np.add.at(gt, row[mapped], g[mapped])
+            grads["table"] = gt
+            if trace is None:
+                return grads
+            g = g.copy()
+            g[mapped] = 0.0
+        grads.update(shared_rule_logits_backward(params, rels, K, trace, g))
+        return grads
+
+    return logits, backward

@@ -412,11 +412,51 @@ def accum_case(ref, out, rng):
                                      acc.selected_wrong, acc.new, acc.new_true], np.int64))
 
 
+def rules_case(ref, out, tag, R, H, K, L, B, tau, scale, seed, penalty=0.0, invert=False, table=None):
+    """The rule-weight producer: SupplyGatedDRUM.build_rule_logits (drum.py:440-467) and the
+    per-hop softmax of proof.py:571, forward and backward (loss = sum(w * G))."""
+    torch.manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    n = 2 * R + 1
+    model = ref.drum.SupplyGatedDRUM(
+        relation_channels=n, step=K, rules=L, entity_count=10, fact_count=4, emb_size=H, tau_1=tau, dropout=0.0,
+        top_k_entities=8, top_k_mask=8, use_topk=True, supply_temperature=0.2, hard_threshold=0.5,
+        rule_logit_init_scale=scale, rule_parametrization="target_table" if table is not None else "shared",
+        norm_epsilon=0.0, norm_availability="mass", same_relation_channel_penalty=penalty, model_base="drum",
+        target_table_relations=table)
+    if invert:
+        model._tclm_invert_rules = True
+    rels = rng.integers(0, R, B).astype(np.int64)
+    rels[: min(B, 3)] = rels[0]  # repeated relations
+    rels_t = torch.from_numpy(rels)
+    logits = model.build_rule_logits(rels_t)
+    w = torch.stack([torch.softmax(logits[:, h] / model.tau_1, dim=-1) for h in range(K)])
+    G = torch.from_numpy(rng.standard_normal(tuple(w.shape)).astype(np.float32))
+    (w * G).sum().backward()
+    pre = f"rl_{tag}_"
+    out[pre + "dims"] = np.array([R, H, K, L, B], np.int64)
+    out[pre + "tau"] = np.array([tau], np.float32)
+    out[pre + "penalty"] = np.array([penalty], np.float32)
+    out[pre + "invert"] = np.array([int(invert)], np.int64)
+    out[pre + "rels"] = rels
+    out[pre + "logits"] = logits.detach().numpy()
+    out[pre + "w"] = w.detach().numpy()
+    out[pre + "G"] = G.numpy()
+    for name, prm in model.named_parameters():
+        if name == "weight_param":
+            continue
+        key = name.replace(".", "__")
+        out[pre + "p_" + key] = prm.detach().numpy()
+        out[pre + "g_" + key] = (prm.grad if prm.grad is not None else torch.zeros_like(prm)).numpy()
+    if table is not None:
+        out[pre + "table_index"] = model.target_table_index.numpy()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
     ap.add_argument("--out", default=str(HERE))
-    ap.add_argument("--only", choices=("all", "prune", "accum"), default="all")
+    ap.add_argument("--only", choices=("all", "prune", "accum", "rules"), default="all")
     a = ap.parse_args()
     torch.set_num_threads(1)  # index_put_/scatter_add_ are then sequential in index order
     ref = import_reference(a.ref)
@@ -426,6 +466,16 @@ def main():
         np.savez_compressed(os.path.join(a.out, "golden_accum.npz"), **ac)
         print("wrote accum", len(ac))
         if a.only == "accum":
+            return
+    if a.only in ("all", "rules"):
+        rl = {}
+        rules_case(ref, rl, "a", R=9, H=48, K=3, L=2, B=12, tau=1.0, scale=1.0, seed=21)
+        rules_case(ref, rl, "b", R=51, H=64, K=2, L=2, B=40, tau=0.7, scale=0.01, seed=22)
+        rules_case(ref, rl, "c", R=6, H=16, K=3, L=2, B=7, tau=1.0, scale=1.0, seed=23, penalty=0.5, invert=True)
+        rules_case(ref, rl, "d", R=6, H=16, K=2, L=2, B=9, tau=1.0, scale=1.0, seed=24, table=[1, 2, 4])
+        np.savez_compressed(os.path.join(a.out, "golden_rules.npz"), **rl)
+        print("wrote rules", len(rl))
+        if a.only == "rules":
             return
     if a.only in ("all", "prune"):
         kg = sample_graph(900, 9, 9000, (("rel", ("zipf", 1.0)), ("head", (0.9, 2.0)), ("tail", (0.9, 2.0)),

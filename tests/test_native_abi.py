@@ -70,6 +70,7 @@ STRUCTS = {
                                     "merge_outputs"]),
     "mkg_proof_params": ("ProofParams", ["B", "L", "E", "R", "hops", "topk_edges", "state_threshold", "reserved",
                                          "fwd_events", "bwd_events"]),
+    "mkg_rule_params": ("RuleParams", ["n", "H", "L", "K", "U", "B", "tau", "reserved"]),
 }
 
 
