@@ -388,6 +388,42 @@ def run_ours(a, wl, kg, rank, world, local_rank):
         s1.synchronize()
         cap_ms.append(s0.elapsed_time(s1))
 
+    # rule-weight producer (per-rule BiLSTM -> linear -> per-hop softmax) for the same batch's
+    # target relations: random-init parameters of the reference model's shapes, fwd and fwd+bwd
+    from minikg_dev_b200 import rules
+    H = 48 if wl.name == "kg_small" else 64
+    torch.manual_seed(rank)
+    pm = torch.nn.Module()
+    pm.emb = torch.nn.Parameter(torch.randn(n, H) * 0.5)
+    pm.lstm = torch.nn.ModuleList(torch.nn.LSTM(H, H, 1, bidirectional=True) for _ in range(L))
+    pm.linear = torch.nn.Linear(2 * H, n)
+    pm.step, pm.relation_count, pm.tau_1 = K, kg.num_relations, 1.0
+    pm.to(dev)
+    q_rels = torch.randint(0, kg.num_relations, (B,), device=dev)
+    Gw = torch.randn(K, B, L, n, device=dev)
+
+    def producer_step(backward: bool):
+        pm.zero_grad(set_to_none=True)
+        w = rules.rule_weights(pm, q_rels)
+        if backward:
+            (w * Gw).sum().backward()
+
+    prod_ms = {}
+    for bw in (False, True):
+        for _ in range(3):
+            producer_step(bw)
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(max(3, a.steps // 2)):
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record()
+            producer_step(bw)
+            s1.record()
+            s1.synchronize()
+            ts.append(s0.elapsed_time(s1))
+        prod_ms[bw] = statistics.mean(ts)
+
     if rank != 0:
         return
     hbm, peak_kind = peaks()
@@ -425,6 +461,10 @@ def run_ours(a, wl, kg, rank, world, local_rank):
                    "gteps": M_cap / (statistics.mean(cap_ms) / 1e3) / 1e9,
                    "path": "sparse loop: per-hop op (exact 256-bucket cap, merged outputs) + device "
                            "normalisation, fwd+bwd"},
+        "rule_producer": {"ms_fwd": prod_ms[False], "ms_fwd_bwd": prod_ms[True], "queries": B,
+                          "distinct_relations": int(torch.unique(q_rels).numel()), "emb_size": H, "channels": n,
+                          "path": "per-relation BiLSTM + SGEMM linear layer + per-hop softmax (rules.rule_weights),"
+                                  " random-init parameters of the reference model's shapes"},
         "e2e": {"value": e2e_value, "unit": "GTEPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_total / a.steps},
         "gpu_launches": (7 + 7 * K) * a.steps,
