@@ -359,13 +359,22 @@ def run_ours(a, wl, kg, rank, world, local_rank):
         s1.synchronize()
         dec_ms.append(s0.elapsed_time(s1))
 
-    # capped row: the same batch with the reference's edge cap of 100 through the sparse loop
-    # (per-hop op with the exact 256-bucket cap and merged outputs, device normalisation,
-    # written-out backward), forward + backward
+    # capped row: the same batch with the reference's production edge cap of 100, forward +
+    # backward, on the fused loop (per-hop take tables of the capped rows; the path
+    # kernel_sparse_scores takes) and, for comparison, on the sparse loop (per-hop op with the
+    # 256-bucket cap and merged outputs, device normalisation, written-out backward)
+    from minikg_dev_b200.proof import proof_scores
     from minikg_dev_b200.sparse_loop import sparse_proof_scores
     cap = 100
 
     def capped_step():
+        wt = w_hops.detach().requires_grad_(True)
+        sc = scores.detach().requires_grad_(True)
+        out_c, msgs_c = proof_scores(g, heads, wt, sc, None, True, 1.0, 0.0, cap)
+        (out_c * G).sum().backward()
+        return msgs_c
+
+    def capped_sparse_step():
         wt = w_hops.detach().requires_grad_(True)
         sc = scores.detach().requires_grad_(True)
         out_c, msgs_c = sparse_proof_scores(g, heads, wt, sc, None, True, 1.0, cap, 0)
@@ -373,20 +382,26 @@ def run_ours(a, wl, kg, rank, world, local_rank):
         (out_c.values() * G[oi[0], oi[1]]).sum().backward()
         return msgs_c
 
-    for _ in range(2):
-        msgs_c = capped_step()
+    def time_steps(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(max(3, a.steps // 2)):
+            flush.zero_()
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record()
+            fn()
+            s1.record()
+            s1.synchronize()
+            ts.append(s0.elapsed_time(s1))
+        return ts
+
+    msgs_c = capped_step()
     M_cap = int(msgs_c.sum().item())
-    torch.cuda.synchronize()
-    cap_ms = []
-    for _ in range(max(3, a.steps // 2)):
-        flush.zero_()
-        s0 = torch.cuda.Event(enable_timing=True)
-        s1 = torch.cuda.Event(enable_timing=True)
-        s0.record()
-        capped_step()
-        s1.record()
-        s1.synchronize()
-        cap_ms.append(s0.elapsed_time(s1))
+    cap_ms = time_steps(capped_step)
+    cap_sparse_ms = time_steps(capped_sparse_step)
 
     # rule-weight producer (per-rule BiLSTM -> linear -> per-hop softmax) for the same batch's
     # target relations: random-init parameters of the reference model's shapes, fwd and fwd+bwd
@@ -459,8 +474,9 @@ def run_ours(a, wl, kg, rank, world, local_rank):
                          "note": "the headline step replayed as one CUDA graph (ProofRunner.capture)"},
         "capped": {"edge_cap": cap, "ms_per_step": statistics.mean(cap_ms), "messages_per_step": M_cap,
                    "gteps": M_cap / (statistics.mean(cap_ms) / 1e3) / 1e9,
-                   "path": "sparse loop: per-hop op (exact 256-bucket cap, merged outputs) + device "
-                           "normalisation, fwd+bwd"},
+                   "path": "fused loop with per-hop edge-cap take tables (the path kernel_sparse_scores "
+                           "takes for caps <= 255), fwd+bwd",
+                   "sparse_loop_ms_per_step": statistics.mean(cap_sparse_ms)},
         "rule_producer": {"ms_fwd": prod_ms[False], "ms_fwd_bwd": prod_ms[True], "queries": B,
                           "distinct_relations": int(torch.unique(q_rels).numel()), "emb_size": H, "channels": n,
                           "path": "per-relation BiLSTM + SGEMM linear layer + per-hop softmax (rules.rule_weights),"
@@ -553,7 +569,7 @@ def run_sharded(a, wl, kg, rank, world, local_rank):
 
 
 def run_capped(a, wl, kg):
-    """Only the capped (cap 100) sparse hop loop, fwd+bwd: the command profiles use."""
+    """Only the capped (cap 100) hop loop, fwd+bwd, on the fused loop and on the sparse loop."""
     import torch
     from minikg_dev_b200.graph import DeviceGraph
     from minikg_dev_b200.sparse_loop import sparse_proof_scores
@@ -567,7 +583,16 @@ def run_capped(a, wl, kg):
     s0 = torch.from_numpy(inp.edge_scores).to(dev)
     G = torch.randn((B, E), device=dev, generator=torch.Generator(device=dev).manual_seed(1234))
 
-    def step():
+    from minikg_dev_b200.proof import proof_scores
+
+    def fused_step():
+        wt = w0.detach().requires_grad_(True)
+        sc = s0.detach().requires_grad_(True)
+        out, msgs = proof_scores(g, heads, wt, sc, None, True, 1.0, 0.0, 100)
+        (out * G).sum().backward()
+        return msgs
+
+    def sparse_step():
         wt = w0.detach().requires_grad_(True)
         sc = s0.detach().requires_grad_(True)
         out, msgs = sparse_proof_scores(g, heads, wt, sc, None, True, 1.0, 100, 0)
@@ -575,21 +600,24 @@ def run_capped(a, wl, kg):
         (out.values() * G[oi[0], oi[1]]).sum().backward()
         return msgs
 
-    for _ in range(max(3, a.warmup)):
-        msgs = step()
-    torch.cuda.synchronize()
-    ms = []
-    for _ in range(a.steps):
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        step()
-        e1.record()
-        e1.synchronize()
-        ms.append(e0.elapsed_time(e1))
-    M = int(msgs.sum().item())
-    print(json.dumps({"engine": "capped", "workload": wl.name, "edge_cap": 100, "messages_per_step": M,
-                      "ms_per_step": statistics.mean(ms), "gteps": M / (statistics.mean(ms) / 1e3) / 1e9}))
+    res = {}
+    for name, step in (("fused", fused_step), ("sparse_loop", sparse_step)):
+        for _ in range(max(3, a.warmup)):
+            msgs = step()
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(a.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step()
+            e1.record()
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        M = int(msgs.sum().item())
+        res[name] = {"messages_per_step": M, "ms_per_step": statistics.mean(ms),
+                     "gteps": M / (statistics.mean(ms) / 1e3) / 1e9}
+    print(json.dumps({"engine": "capped", "workload": wl.name, "edge_cap": 100, **res}))
 
 
 def main():

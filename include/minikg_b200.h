@@ -178,6 +178,38 @@ int mkg_adjacency_build(const mkg_graph* g, mkg_adjacency adj, int64_t* num_task
 int mkg_adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, const mkg_edge_factor* f,
                              mkg_stream stream);
 
+/* Edge-cap index of the fused engine for one cap value (0 .. MKG_DENSE_CAP_MAX).  The
+ * reference caps every frontier entry (b, l, s) per direction at `cap` messages with the
+ * 256-bucket rule of fastlog.cu:2092-2195, 2273-2298: the relation groups of s's CSR row are
+ * bucketed by the rule weight w[b, l, channel]; groups above the threshold bucket take all
+ * their edges, groups below take none, threshold-bucket groups take in group order what is
+ * left of the cap, each its first edges in CSR order.  Only rows longer than the cap are
+ * affected ("capped rows"); every relation group of a capped row gets one row of a per-hop
+ * take table [num_groups, B*L] (uint8: edges taken per column), and every pull / push record
+ * sent by a capped row points at its group's row and its position inside the group. */
+#define MKG_DENSE_CAP_MAX 255
+typedef struct mkg_cap_index {
+  int64_t cap;
+  int64_t num_slots;             /* capped (entity, direction) rows */
+  int64_t num_groups;            /* relation groups of the capped rows: rows of the take table */
+  const int32_t* slot_entity;    /* [num_slots] */
+  const int32_t* slot_dir;       /* [num_slots] 0: ori (rows = heads), 1: inv (rows = tails) */
+  const int32_t* slot_group;     /* [num_slots] take-table row of the slot's first group */
+  const int32_t* pull_cap;       /* [2 * records] per pull record: (take row or -1, position in group) */
+  const int32_t* push_cap;       /* [2 * records] the same per push record */
+  const int32_t* capped_degree;  /* [E] min(out-degree ori, cap) + min(out-degree inv, cap) */
+} mkg_cap_index;
+
+/* Writes (num_slots, num_groups) of the index for `cap` to sizes_out (device int64[2]). */
+size_t mkg_cap_index_workspace_bytes(const mkg_graph* g);
+int mkg_cap_index_sizes(const mkg_graph* g, int64_t cap, int64_t* sizes_out, void* workspace,
+                        size_t workspace_bytes, mkg_stream stream);
+/* Fills the caller-allocated arrays of `index` (sizes from mkg_cap_index_sizes; the records of
+ * `adj` from mkg_adjacency_build).  No reference counterpart: the reference decides the cap
+ * per frontier entry while it expands messages (fastlog.cu:2114-2323). */
+int mkg_cap_index_build(const mkg_graph* g, const mkg_adjacency* adj, const mkg_cap_index* index,
+                        void* workspace, size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+
 /* ------------------------------------------------------------------ per-hop op */
 
 typedef struct mkg_hop_params {
@@ -268,6 +300,10 @@ typedef struct mkg_proof_params {
    * the transposed pull of hop h (backward), on the call's stream. */
   void* const* fwd_events;
   void* const* bwd_events;
+  /* Required when topk_edges < 2^60 (then 0 <= topk_edges <= MKG_DENSE_CAP_MAX): the cap
+   * index built for topk_edges.  Messages of capped rows not taken under the cap are left
+   * out of every hop, forward and backward, and of the message counts. */
+  const mkg_cap_index* cap_index;
 } mkg_proof_params;
 
 /* The whole hop loop of kernel_sparse_scores (proof.py:467-614, dropout off, no entity

@@ -69,7 +69,13 @@ class HopParams(C.Structure):
 
 class ProofParams(C.Structure):
     _fields_ = [("B", i64), ("L", i64), ("E", i64), ("R", i64), ("hops", i64), ("topk_edges", i64),
-                ("state_threshold", C.c_float), ("reserved", i32), ("fwd_events", vp), ("bwd_events", vp)]
+                ("state_threshold", C.c_float), ("reserved", i32), ("fwd_events", vp), ("bwd_events", vp),
+                ("cap_index", vp)]
+
+
+class CapIndex(C.Structure):
+    _fields_ = [("cap", i64), ("num_slots", i64), ("num_groups", i64), ("slot_entity", vp), ("slot_dir", vp),
+                ("slot_group", vp), ("pull_cap", vp), ("push_cap", vp), ("capped_degree", vp)]
 
 
 class RuleParams(C.Structure):
@@ -113,6 +119,9 @@ SIGNATURES = {
     "mkg_decode_topk": (C.c_int, [vp, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_segment_sum_ordered": (C.c_int, [vp, i64, vp, vp, vp]),
     "mkg_segment_sum": (C.c_int, [vp, i64, vp, vp, vp]),
+    "mkg_cap_index_workspace_bytes": (C.c_size_t, [P(Graph)]),
+    "mkg_cap_index_sizes": (C.c_int, [P(Graph), i64, vp, vp, C.c_size_t, vp]),
+    "mkg_cap_index_build": (C.c_int, [P(Graph), P(Adjacency), P(CapIndex), vp, C.c_size_t, vp, vp]),
     "mkg_rule_saved_bytes": (C.c_size_t, [P(RuleParams)]),
     "mkg_rule_backward_workspace_bytes": (C.c_size_t, [P(RuleParams)]),
     "mkg_rule_softmax_workspace_bytes": (C.c_size_t, [P(RuleParams)]),

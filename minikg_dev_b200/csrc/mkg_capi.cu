@@ -38,7 +38,7 @@ using mkg::set_error;
 static cudaStream_t S(mkg_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 
 MKG_API const char* mkg_last_error(void) { return mkg::g_last_error; }
-MKG_API int mkg_abi_version(void) { return 5; }
+MKG_API int mkg_abi_version(void) { return 6; }
 
 MKG_API size_t mkg_csr_build_workspace_bytes(int64_t T, int64_t E, int64_t R) {
   return mkg::csr_build_workspace_bytes(T, E, R);
@@ -174,4 +174,14 @@ MKG_API int mkg_rule_softmax_backward(const mkg_rule_params* p, const float* w_h
                                       void* ws, size_t ws_bytes, unsigned* err, mkg_stream st) {
   return mkg::rule_softmax_backward(p, w_hops, grad_w_hops, query_ptr, query_perm, grad_logits_u, ws, ws_bytes, err,
                                     S(st));
+}
+
+MKG_API size_t mkg_cap_index_workspace_bytes(const mkg_graph* g) { return mkg::cap_index_workspace_bytes(g); }
+MKG_API int mkg_cap_index_sizes(const mkg_graph* g, int64_t cap, int64_t* sizes_out, void* ws, size_t ws_bytes,
+                                mkg_stream st) {
+  return mkg::cap_index_sizes(g, cap, sizes_out, ws, ws_bytes, S(st));
+}
+MKG_API int mkg_cap_index_build(const mkg_graph* g, const mkg_adjacency* adj, const mkg_cap_index* index, void* ws,
+                                size_t ws_bytes, unsigned* err, mkg_stream st) {
+  return mkg::cap_index_build(g, adj, index, ws, ws_bytes, err, S(st));
 }

@@ -251,6 +251,77 @@ __global__ void adjacency_factor_kernel(mkg_adj_edge* __restrict__ recs, int64_t
   }
 }
 
+// ---------------------------------------------------------------- edge-cap index
+// flag[dir * E + e] = row e of direction dir is longer than the cap; ngrp = its group count
+// (0 when not capped); capdeg[e] = messages an active entry of e sends under the cap.
+// flag and ngrp carry one extra trailing 0 so that their exclusive scans end in the totals.
+__global__ void cap_rows_kernel(DirCSR ori, DirCSR inv, int64_t E, int64_t cap, int32_t* __restrict__ flag,
+                                int32_t* __restrict__ ngrp, int32_t* __restrict__ capdeg) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e <= E; e += (int64_t)gridDim.x * blockDim.x) {
+    if (e == E) { flag[2 * E] = 0; ngrp[2 * E] = 0; continue; }
+    const int64_t dori = ori.row_ptr[e + 1] - ori.row_ptr[e], dinv = inv.row_ptr[e + 1] - inv.row_ptr[e];
+    const bool fo = dori > cap, fi = dinv > cap;
+    flag[e] = fo;
+    flag[E + e] = fi;
+    ngrp[e] = fo ? ori.group_ptr[e + 1] - ori.group_ptr[e] : 0;
+    ngrp[E + e] = fi ? inv.group_ptr[e + 1] - inv.group_ptr[e] : 0;
+    if (capdeg) capdeg[e] = static_cast<int32_t>((dori < cap ? dori : cap) + (dinv < cap ? dinv : cap));
+  }
+}
+
+__global__ void cap_sizes_kernel(const int32_t* __restrict__ sidx, const int32_t* __restrict__ gbase, int64_t E,
+                                 int64_t* __restrict__ sizes) {
+  sizes[0] = sidx[2 * E];
+  sizes[1] = gbase[2 * E];
+}
+
+__global__ void cap_slots_kernel(const int32_t* __restrict__ flag, const int32_t* __restrict__ sidx,
+                                 const int32_t* __restrict__ gbase, int64_t E, int64_t num_slots,
+                                 int32_t* __restrict__ slot_entity, int32_t* __restrict__ slot_dir,
+                                 int32_t* __restrict__ slot_group, unsigned* err) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < 2 * E; i += (int64_t)gridDim.x * blockDim.x) {
+    if (!flag[i]) continue;
+    const int64_t si = sidx[i];
+    if (si < 0 || si >= num_slots) { raise_flag(err, MKG_DEV_BAD_ENTRY); continue; }
+    slot_entity[si] = static_cast<int32_t>(i % E);
+    slot_dir[si] = static_cast<int32_t>(i / E);
+    slot_group[si] = gbase[i];
+  }
+}
+
+// Per CSR position p of direction dir (row = the sending entity): fact_cap[dir][fact] =
+// (take-table row of p's relation group, p's position inside the group), or (-1, 0) when the
+// row is not capped.
+__global__ void cap_fact_kernel(DirCSR d, int dir, int64_t E, int64_t T, const int32_t* __restrict__ flag,
+                                const int32_t* __restrict__ gbase, int2* __restrict__ fact_cap, unsigned* err) {
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < T; p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t f = d.order[p];
+    if (f < 0 || f >= T) { raise_flag(err, MKG_DEV_BAD_FACT); continue; }
+    const int64_t row = row_of_position(d.row_ptr, E, p);
+    int2 out = make_int2(-1, 0);
+    if (flag[dir * E + row]) {
+      int64_t lo = d.group_ptr[row], hi = d.group_ptr[row + 1];  // group_start[lo] <= p
+      while (hi - lo > 1) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (d.group_start[mid] <= p) lo = mid; else hi = mid;
+      }
+      out = make_int2(static_cast<int32_t>(gbase[dir * E + row] + (lo - d.group_ptr[row])),
+                      static_cast<int32_t>(p - d.group_start[lo]));
+    }
+    fact_cap[dir * T + f] = out;
+  }
+}
+
+// Per record: the entry of its (direction, fact); channel < R is an ori message of the sender.
+__global__ void cap_records_kernel(const mkg_adj_edge* __restrict__ recs, int64_t count, int64_t T, int64_t R,
+                                   const int2* __restrict__ fact_cap, int2* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    const mkg_adj_edge r = recs[i];
+    const int dir = r.channel < R ? 0 : 1;
+    out[i] = (r.fact >= 0 && r.fact < T) ? fact_cap[dir * T + r.fact] : make_int2(-1, 0);
+  }
+}
+
 }  // namespace
 
 size_t csr_build_workspace_bytes(int64_t T, int64_t E, int64_t R) {
@@ -371,6 +442,103 @@ int adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, const mkg_edge_f
   MKG_LAUNCHED("adjacency_factor_kernel");
   adjacency_factor_kernel<<<persistent_blocks(8), 256, 0, st>>>(adj.push, count, g->num_facts, ef);
   MKG_LAUNCHED("adjacency_factor_kernel");
+  return MKG_OK;
+}
+
+// ---------------------------------------------------------------- edge-cap index
+namespace {
+struct CapWs {
+  int32_t* flag;
+  int32_t* ngrp;
+  int32_t* sidx;
+  int32_t* gbase;
+  int2* fact_cap;
+  void* temp;
+  size_t temp_bytes;
+};
+
+size_t cap_scan_bytes(int64_t E) {
+  size_t b = 0;
+  cub::DeviceScan::ExclusiveSum(nullptr, b, (int32_t*)nullptr, (int32_t*)nullptr, (int)(2 * E + 1));
+  return b;
+}
+
+CapWs cap_ws(void* ws, int64_t E, int64_t T) {
+  CapWs w;
+  char* p = static_cast<char*>(ws);
+  const size_t a = align256(4 * (size_t)(2 * E + 1));
+  w.flag = reinterpret_cast<int32_t*>(p); p += a;
+  w.ngrp = reinterpret_cast<int32_t*>(p); p += a;
+  w.sidx = reinterpret_cast<int32_t*>(p); p += a;
+  w.gbase = reinterpret_cast<int32_t*>(p); p += a;
+  w.fact_cap = reinterpret_cast<int2*>(p); p += align256(16 * (size_t)T);
+  w.temp = p;
+  w.temp_bytes = cap_scan_bytes(E);
+  return w;
+}
+
+// flags, group counts and their scans (slot index, first take-table row) for `cap`
+int cap_scan(const mkg_graph* g, int64_t cap, const CapWs& w, int32_t* capdeg, cudaStream_t st) {
+  const int64_t E = g->num_entities;
+  cap_rows_kernel<<<persistent_blocks(4), 256, 0, st>>>(make_dir(g->ori), make_dir(g->inv), E, cap, w.flag, w.ngrp,
+                                                        capdeg);
+  MKG_LAUNCHED("cap_rows_kernel");
+  size_t b = w.temp_bytes;
+  MKG_CUDA(cub::DeviceScan::ExclusiveSum(w.temp, b, w.flag, w.sidx, (int)(2 * E + 1), st));
+  b = w.temp_bytes;
+  MKG_CUDA(cub::DeviceScan::ExclusiveSum(w.temp, b, w.ngrp, w.gbase, (int)(2 * E + 1), st));
+  return MKG_OK;
+}
+}  // namespace
+
+size_t cap_index_workspace_bytes(const mkg_graph* g) {
+  if (!g) return 0;
+  const int64_t E = g->num_entities, T = g->num_facts;
+  return 4 * align256(4 * (size_t)(2 * E + 1)) + align256(16 * (size_t)T) + align256(cap_scan_bytes(E)) + 256;
+}
+
+int cap_index_sizes(const mkg_graph* g, int64_t cap, int64_t* sizes, void* ws, size_t ws_bytes, cudaStream_t st) {
+  MKG_REQUIRE(g && sizes && ws, "cap_index_sizes: null argument");
+  MKG_REQUIRE(cap >= 0 && cap <= MKG_DENSE_CAP_MAX, "cap_index: cap %lld outside [0, %d]", (long long)cap,
+              MKG_DENSE_CAP_MAX);
+  MKG_REQUIRE(2 * g->num_entities + 1 < (int64_t(1) << 31), "cap_index: too many entities");
+  MKG_REQUIRE(ws_bytes >= cap_index_workspace_bytes(g), "cap_index_sizes: workspace too small");
+  const CapWs w = cap_ws(ws, g->num_entities, g->num_facts);
+  if (int rc = cap_scan(g, cap, w, nullptr, st)) return rc;
+  cap_sizes_kernel<<<1, 1, 0, st>>>(w.sidx, w.gbase, g->num_entities, sizes);
+  MKG_LAUNCHED("cap_sizes_kernel");
+  return MKG_OK;
+}
+
+int cap_index_build(const mkg_graph* g, const mkg_adjacency* adj, const mkg_cap_index* ix, void* ws,
+                    size_t ws_bytes, unsigned* err, cudaStream_t st) {
+  MKG_REQUIRE(g && adj && ix && ws && adj->pull && adj->push, "cap_index_build: null argument");
+  MKG_REQUIRE(ix->cap >= 0 && ix->cap <= MKG_DENSE_CAP_MAX, "cap_index: cap %lld outside [0, %d]",
+              (long long)ix->cap, MKG_DENSE_CAP_MAX);
+  MKG_REQUIRE(ix->pull_cap && ix->push_cap && ix->capped_degree &&
+                  (ix->num_slots == 0 || (ix->slot_entity && ix->slot_dir && ix->slot_group)),
+              "cap_index_build: null output array");
+  MKG_REQUIRE(ws_bytes >= cap_index_workspace_bytes(g), "cap_index_build: workspace too small");
+  const int64_t E = g->num_entities, T = g->num_facts, R = g->num_relations;
+  const CapWs w = cap_ws(ws, E, T);
+  if (int rc = cap_scan(g, ix->cap, w, const_cast<int32_t*>(ix->capped_degree), st)) return rc;
+  const int blocks = persistent_blocks(4);
+  if (ix->num_slots > 0) {
+    cap_slots_kernel<<<blocks, 256, 0, st>>>(w.flag, w.sidx, w.gbase, E, ix->num_slots,
+                                             const_cast<int32_t*>(ix->slot_entity), const_cast<int32_t*>(ix->slot_dir),
+                                             const_cast<int32_t*>(ix->slot_group), err);
+    MKG_LAUNCHED("cap_slots_kernel");
+  }
+  cap_fact_kernel<<<blocks, 256, 0, st>>>(make_dir(g->ori), 0, E, T, w.flag, w.gbase, w.fact_cap, err);
+  MKG_LAUNCHED("cap_fact_kernel");
+  cap_fact_kernel<<<blocks, 256, 0, st>>>(make_dir(g->inv), 1, E, T, w.flag, w.gbase, w.fact_cap, err);
+  MKG_LAUNCHED("cap_fact_kernel");
+  cap_records_kernel<<<blocks, 256, 0, st>>>(adj->pull, 2 * T, T, R, w.fact_cap,
+                                             reinterpret_cast<int2*>(const_cast<int32_t*>(ix->pull_cap)));
+  MKG_LAUNCHED("cap_records_kernel");
+  cap_records_kernel<<<blocks, 256, 0, st>>>(adj->push, 2 * T, T, R, w.fact_cap,
+                                             reinterpret_cast<int2*>(const_cast<int32_t*>(ix->push_cap)));
+  MKG_LAUNCHED("cap_records_kernel");
   return MKG_OK;
 }
 

@@ -56,6 +56,7 @@ struct HopLayout {
   size_t off_val, off_hit, off_pk, off_lists, off_counts, off_blk, off_blkoff, off_cub, off_map, total;
   // hash: claimed keys, values (f32 / packed u64), their key-sorted copies, entry map values
   size_t off_tkey, off_tval, off_tpk, off_skey, off_sval, off_spk, off_mapkey;
+  size_t off_gw64;         // backward: rule-weight gradient accumulated in fp64
   size_t cub_bytes;
 
   int64_t slots(int t) const { return t < 2 ? capm : capf; }
@@ -155,6 +156,7 @@ HopLayout backward_layout(const mkg_hop_params& p, int64_t F) {
   }
   L.off_lists = o; o += a256(4 * (size_t)(3 * F + 3));
   L.off_counts = o; o += a256(4 * 4);
+  L.off_gw64 = o; o += a256(8 * (size_t)(p.B * p.L * p.n));
   L.total = o;
   return L;
 }
@@ -660,7 +662,7 @@ __global__ void scatter_grad_kernel(mkg_coo3 g, int64_t B, int64_t L, int64_t lo
 // grad_w[b,l,n-1] += g_ind * sv (fastlog.cu:2608-2644); also fills the key -> entry map
 // (full-range keys) used by the argmax backward.
 __global__ void backward_entry_init_kernel(Frontier f, HopCtx c, KeyTable ind_tab, const float* __restrict__ g_ind,
-                                           float* __restrict__ grad_sp, float* __restrict__ grad_w,
+                                           float* __restrict__ grad_sp, double* __restrict__ grad_w,
                                            KeyTable map_tab, int32_t* __restrict__ entry_map) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < f.F;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -677,7 +679,7 @@ __global__ void backward_entry_init_kernel(Frontier f, HopCtx c, KeyTable ind_ta
       float g = s >= 0 ? g_ind[s] : 0.0f;
       if (g != 0.0f) {
         gsp = g * c.w[wi];
-        atomicAdd(grad_w + wi, g * f.v[i]);
+        atomicAdd(grad_w + wi, static_cast<double>(g * f.v[i]));
       }
     }
     grad_sp[i] = gsp;
@@ -697,7 +699,7 @@ __device__ __forceinline__ float edge_grad_factor(const EdgeFactor& f, int64_t f
 // entry), grad_w += (g*m)*sv, grad_edge[fact] += (((g*sv)*w)*m)*factor.
 struct BwdVisit {
   GradStore gs;
-  float* grad_w;
+  double* grad_w;  // fp64 accumulator: every fp32 product added exactly, rounded once
   float* grad_edge;
   const EdgeFactor* f;
   float sv;
@@ -713,14 +715,14 @@ struct BwdVisit {
     float m = (*f)(fact);
     float gm = g * m;
     acc += gm * wv;
-    atomicAdd(grad_w + wbase + ch, gm * sv);
+    atomicAdd(grad_w + wbase + ch, static_cast<double>(gm * sv));
     if (grad_edge) atomicAdd(grad_edge + fact, (((g * sv) * wv) * m) * edge_grad_factor(*f, fact));
   }
 };
 
 __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict__ list,
                                 const int32_t* __restrict__ count, GradStore gs, float* __restrict__ grad_sp,
-                                float* __restrict__ grad_w, float* __restrict__ grad_edge) {
+                                double* __restrict__ grad_w, float* __restrict__ grad_edge) {
   const int64_t n = *count;
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n;
        k += (int64_t)gridDim.x * blockDim.x) {
@@ -739,7 +741,7 @@ __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict_
 
 __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
     Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count, GradStore gs,
-    float* __restrict__ grad_sp, float* __restrict__ grad_w, float* __restrict__ grad_edge) {
+    float* __restrict__ grad_sp, double* __restrict__ grad_w, float* __restrict__ grad_edge) {
   __shared__ int hist_all[kMidWarps][kNumBuckets];
   int* hist = hist_all[threadIdx.x >> 5];
   const int lane = threadIdx.x & 31;
@@ -767,7 +769,7 @@ __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
 
 __global__ void __launch_bounds__(kHubThreads) bwd_hub_kernel(
     Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count, GradStore gs,
-    float* __restrict__ grad_sp, float* __restrict__ grad_w, float* __restrict__ grad_edge) {
+    float* __restrict__ grad_sp, double* __restrict__ grad_w, float* __restrict__ grad_edge) {
   __shared__ float wstage[kHubStageMax];
   __shared__ int hist[kNumBuckets];
   __shared__ float part[kHubThreads / 32];
@@ -810,7 +812,7 @@ __global__ void bwd_argmax_kernel(int d, mkg_coo3 out, const int64_t* __restrict
                                   KeyTable gtab, const float* __restrict__ gvals, KeyTable map_tab,
                                   const int32_t* __restrict__ entry_map, const int32_t* __restrict__ fhead,
                                   const int32_t* __restrict__ ftail, const int16_t* __restrict__ frel,
-                                  float* __restrict__ grad_sp, float* __restrict__ grad_w,
+                                  float* __restrict__ grad_sp, double* __restrict__ grad_w,
                                   float* __restrict__ grad_edge) {
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < out.nnz;
        k += (int64_t)gridDim.x * blockDim.x) {
@@ -833,7 +835,7 @@ __global__ void bwd_argmax_kernel(int d, mkg_coo3 out, const int64_t* __restrict
     float wv = c.w[wi];
     float gm = g * m;
     atomicAdd(grad_sp + i, gm * wv);
-    atomicAdd(grad_w + wi, gm * sv);
+    atomicAdd(grad_w + wi, static_cast<double>(gm * sv));
     if (grad_edge) atomicAdd(grad_edge + fact, (((g * sv) * wv) * m) * edge_grad_factor(c.factor, fact));
   }
 }
@@ -1062,6 +1064,13 @@ int hop_emit(const mkg_hop_params* p, int64_t nnz, const void* ws, size_t ws_byt
   return MKG_OK;
 }
 
+namespace {
+__global__ void round_gw_kernel(const double* __restrict__ gw64, int64_t count, float* __restrict__ grad_w) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+    grad_w[i] = static_cast<float>(gw64[i]);
+}
+}  // namespace
+
 size_t hop_backward_workspace_bytes(const mkg_hop_params* p, int64_t nnz) {
   return backward_layout(*p, nnz).total + 256;
 }
@@ -1123,7 +1132,14 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
     }
   }
   MKG_CUDA(cudaMemsetAsync(counts, 0, 16, st));
-  MKG_CUDA(cudaMemsetAsync(grad_w, 0, 4 * (size_t)(p->B * p->L * p->n), st));
+  const int64_t nw = p->B * p->L * p->n;
+  double* gw64 = reinterpret_cast<double*>(base + lay.off_gw64);
+  MKG_CUDA(cudaMemsetAsync(gw64, 0, 8 * (size_t)nw, st));
+  auto finish = [&]() -> int {  // grad_w = the fp64 sums rounded once
+    round_gw_kernel<<<grid_for(nw, 256, persistent_blocks(2)), 256, 0, st>>>(gw64, nw, grad_w);
+    MKG_LAUNCHED("round_gw_kernel");
+    return MKG_OK;
+  };
   if (grad_edge) MKG_CUDA(cudaMemsetAsync(grad_edge, 0, 4 * (size_t)g->num_facts, st));
   if (merge) {  // one gradient store serves ori, inv and ind
     vals[1] = vals[2] = vals[0];
@@ -1135,21 +1151,21 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
         *gl[k], p->B, p->L, range_lo(*p), range_extent(*p), tabs[k], vals[k], err);
     MKG_LAUNCHED("scatter_grad_kernel");
   }
-  if (F == 0) return MKG_OK;
+  if (F == 0) return finish();
   HopCtx c = make_ctx(g, w, ef, p, err);
   Frontier f{fr->batch, fr->level, fr->entity, fr->value, F};
   backward_entry_init_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(
-      f, c, tabs[2], vals[2], grad_sp, grad_w, map_tab, emap);
+      f, c, tabs[2], vals[2], grad_sp, gw64, map_tab, emap);
   MKG_LAUNCHED("backward_entry_init_kernel");
   if (p->agg_mode == 0) {
     classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts, nullptr, nullptr,
                                                                              dense_table());
     MKG_LAUNCHED("classify_kernel");
     GradStore gs{{vals[0], vals[1]}, {tabs[0], tabs[1]}};
-    bwd_tail_kernel<<<persistent_blocks(8), 256, 0, st>>>(f, c, lists, counts, gs, grad_sp, grad_w, grad_edge);
-    bwd_mid_kernel<<<persistent_blocks(4), kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, gs, grad_sp, grad_w,
+    bwd_tail_kernel<<<persistent_blocks(8), 256, 0, st>>>(f, c, lists, counts, gs, grad_sp, gw64, grad_edge);
+    bwd_mid_kernel<<<persistent_blocks(4), kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, gs, grad_sp, gw64,
                                                                     grad_edge);
-    bwd_hub_kernel<<<persistent_blocks(2), kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, gs, grad_sp, grad_w,
+    bwd_hub_kernel<<<persistent_blocks(2), kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, gs, grad_sp, gw64,
                                                                  grad_edge);
     MKG_LAUNCHED("backward push kernels");
   } else {
@@ -1158,12 +1174,12 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
     for (int d = 0; d < 2; ++d) {
       if (outs[d]->nnz <= 0) continue;
       bwd_argmax_kernel<<<grid_for(outs[d]->nnz, 256, persistent_blocks(8)), 256, 0, st>>>(
-          d, *outs[d], args[d], f, c, tabs[d], vals[d], map_tab, emap, fhead, ftail, frel, grad_sp, grad_w,
+          d, *outs[d], args[d], f, c, tabs[d], vals[d], map_tab, emap, fhead, ftail, frel, grad_sp, gw64,
           grad_edge);
       MKG_LAUNCHED("bwd_argmax_kernel");
     }
   }
-  return MKG_OK;
+  return finish();
 }
 
 }  // namespace mkg

@@ -33,6 +33,8 @@ constexpr int kQueueStride = 32; // ints between two queue counters
 
 struct ProofDims {
   int64_t B, L, E, R, n, hops, BL, BLP, nch;
+  int64_t cap;      // edge cap of the capped loop, -1: uncapped
+  int64_t ngroups;  // rows of the per-hop take table (capped loop)
 };
 
 inline ProofDims proof_dims(const mkg_proof_params& p) {
@@ -41,6 +43,9 @@ inline ProofDims proof_dims(const mkg_proof_params& p) {
   d.BL = p.B * p.L;
   d.BLP = (d.BL + 3) / 4 * 4;
   d.nch = (d.BLP + kChunk - 1) / kChunk;
+  const bool capped = p.topk_edges < (int64_t(1) << 60) && p.cap_index != nullptr;
+  d.cap = capped ? p.topk_edges : -1;
+  d.ngroups = capped ? p.cap_index->num_groups : 0;
   return d;
 }
 
@@ -49,7 +54,7 @@ namespace {
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct ProofLayout {
-  size_t wt, x, y, d, act, yact, dxa, dxb, dy, s, dwt, queue, msgs, total;
+  size_t wt, x, y, d, act, yact, dxa, dxb, dy, s, dwt, queue, msgs, take, total;
 };
 
 ProofLayout proof_layout(const ProofDims& q) {
@@ -69,6 +74,7 @@ ProofLayout proof_layout(const ProofDims& q) {
   L.dwt = o; o += a256(4 * (size_t)q.n * q.BLP);
   L.queue = o; o += a256(4 * (size_t)(2 * q.hops * q.nch * kQueueStride));
   L.msgs = o; o += a256(8 * (size_t)(q.hops + 1));
+  L.take = o; o += a256((size_t)q.hops * q.ngroups * q.BLP);
   L.total = o;
   return L;
 }
@@ -91,6 +97,8 @@ struct Slab {
   float* dwt() const { return reinterpret_cast<float*>(base + lay.dwt); }
   int32_t* queue() const { return reinterpret_cast<int32_t*>(base + lay.queue); }
   int64_t* msgs() const { return reinterpret_cast<int64_t*>(base + lay.msgs); }
+  // edge-cap take table of hop h: [ngroups][BLP] edges taken per (capped group, column)
+  uint8_t* take(int64_t h) const { return reinterpret_cast<uint8_t*>(base + lay.take) + h * q.ngroups * q.BLP; }
 };
 
 // ------------------------------------------------------------------ setup kernels
@@ -118,7 +126,7 @@ __global__ void untranspose_dw_kernel(const float* __restrict__ dwt, ProofDims q
 // One-hot start: X0[head_b][b*L + l] = 1 for every rule l (proof.py:511-523).
 __global__ void init_state_kernel(const int64_t* __restrict__ heads, ProofDims q, float* __restrict__ x0,
                                   uint8_t* __restrict__ act0, const int32_t* __restrict__ push_ptr,
-                                  int64_t* __restrict__ msgs, unsigned* err) {
+                                  const int32_t* __restrict__ capdeg, int64_t* __restrict__ msgs, unsigned* err) {
   for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < q.BL;
        c += (int64_t)gridDim.x * blockDim.x) {
     int64_t b = c / q.L;
@@ -126,7 +134,8 @@ __global__ void init_state_kernel(const int64_t* __restrict__ heads, ProofDims q
     if (e < 0 || e >= q.E) { raise_flag(err, MKG_DEV_BAD_ENTRY); continue; }
     x0[e * q.BLP + c] = 1.0f;
     act0[e * q.nch + c / kChunk] = 1;
-    atomicAdd(reinterpret_cast<unsigned long long*>(msgs), (unsigned long long)(push_ptr[e + 1] - push_ptr[e]));
+    atomicAdd(reinterpret_cast<unsigned long long*>(msgs),
+              (unsigned long long)(capdeg ? capdeg[e] : push_ptr[e + 1] - push_ptr[e]));
   }
 }
 
@@ -216,6 +225,137 @@ __device__ __forceinline__ void load_lanes(Lanes<VEC>& out, const float* __restr
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
+// ------------------------------------------------------------------ edge cap
+// Take table of one hop, the edge cap of fastlog.cu:2092-2195, 2273-2298 for every capped
+// row (slot) and column c: the row's relation groups are bucketed by their rule weight
+// w[channel][c]; the threshold bucket tb is the largest bucket whose groups at or above it
+// hold at least cap edges; groups above tb take all their edges, groups below none, groups
+// in tb take, in group order, what is left of cap after the groups above.
+// take[row of group][c] = edges taken (its first ones in CSR order).  Block = (slot, tile of
+// kTakeCols columns), one thread per column; the buckets of up to kTakeGroups groups are
+// computed once into shared memory ([group][column] bytes), longer rows re-read the weights.
+constexpr int kTakeCols = 256;
+constexpr int kTakeGroups = 96;
+constexpr int kTakeHist = 32;  // bucket ranges narrower than this are counted in one pass
+
+__global__ void __launch_bounds__(kTakeCols) cap_take_kernel(
+    DirCSR ori, DirCSR inv, const int32_t* __restrict__ slot_entity, const int32_t* __restrict__ slot_dir,
+    const int32_t* __restrict__ slot_group, int64_t num_slots, ProofDims q, const float* __restrict__ wt,
+    const uint8_t* __restrict__ act, uint8_t* __restrict__ take, unsigned* err) {
+  __shared__ uint8_t bk[kTakeGroups * kTakeCols];     // [group][column] buckets
+  __shared__ uint16_t hist[kTakeHist * kTakeCols];    // [bucket - lowest][column] edges
+  __shared__ int32_t gcnt[kTakeGroups];               // group edge counts, clamped at 255
+  __shared__ int32_t grel[kTakeGroups];
+  const int tid = threadIdx.x;
+  const int64_t tiles = (q.BLP + kTakeCols - 1) / kTakeCols;
+  for (int64_t blk = blockIdx.x; blk < num_slots * tiles; blk += gridDim.x) {
+    const int64_t slot = blk / tiles;
+    const int64_t c = (blk % tiles) * kTakeCols + tid;
+    const int dir = slot_dir[slot];
+    const DirCSR d = dir == 0 ? ori : inv;
+    const int64_t e = slot_entity[slot];
+    // takes are read only where the sending row holds state (the pulls skip inactive chunks)
+    const int64_t ch0 = (blk % tiles) * (kTakeCols / kChunk);
+    bool tile_active = false;
+    for (int64_t k = ch0; k < ch0 + kTakeCols / kChunk && k < q.nch; ++k) tile_active = tile_active || act[e * q.nch + k];
+    if (!tile_active) continue;  // uniform over the block
+    const bool col_active = c < q.BLP && act[e * q.nch + c / kChunk] != 0;
+    const int64_t g0 = d.group_ptr[e];
+    const int G = static_cast<int>(d.group_ptr[e + 1] - g0);
+    const bool staged = G <= kTakeGroups;
+    const float* w = wt + (dir == 0 ? 0 : q.R) * q.BLP + (c < q.BLP ? c : 0);
+    // a relation outside [0, R) is flagged and counts as bucket 0
+    auto bucket_at = [&](int32_t rel) { return rel < 0 ? 0 : weight_bucket(w[(int64_t)rel * q.BLP]); };
+    auto rel_of = [&](int g) -> int32_t {
+      const int32_t rel = d.group_rel[g0 + g];
+      if (rel < 0 || rel >= q.R) { raise_flag(err, MKG_DEV_BAD_REL); return -1; }
+      return rel;
+    };
+    __syncthreads();  // the previous slot's shared arrays are consumed
+    if (staged) {
+      for (int g = tid; g < G; g += blockDim.x) {
+        const int32_t cnt = d.group_count[g0 + g];
+        gcnt[g] = cnt < 255 ? cnt : 255;
+        grel[g] = rel_of(g);
+      }
+    }
+    __syncthreads();
+    // Counts are clamped at 255: every comparison below is against cap <= 255, and a group
+    // counted before the threshold holds fewer than cap edges, so no decision changes.
+    auto count = [&](int g) -> int {
+      if (staged) return gcnt[g];
+      const int32_t cnt = d.group_count[g0 + g];
+      return cnt < 255 ? cnt : 255;
+    };
+    auto bucket = [&](int g) -> int { return staged ? bk[g * kTakeCols + tid] : bucket_at(rel_of(g)); };
+    int bmin = kNumBuckets - 1, bmax = 0;
+#pragma unroll 4
+    for (int g = 0; g < G; ++g) {
+      const int b = staged ? bucket_at(grel[g]) : bucket_at(rel_of(g));
+      if (staged) bk[g * kTakeCols + tid] = static_cast<uint8_t>(b);
+      bmin = b < bmin ? b : bmin;
+      bmax = b > bmax ? b : bmax;
+    }
+    if (!col_active) continue;
+    // tb: the largest bucket whose groups at or above it hold >= cap edges (a capped row holds
+    // more than cap, so tb >= bmin); before: the edges of the groups above tb
+    int tb = bmin, before = 0;
+    if (bmax - bmin < kTakeHist) {
+      for (int k = 0; k <= bmax - bmin; ++k) hist[k * kTakeCols + tid] = 0;
+      for (int g = 0; g < G; ++g) hist[(bucket(g) - bmin) * kTakeCols + tid] += static_cast<uint16_t>(count(g));
+      int cum = 0;
+      for (int k = bmax - bmin; k >= 0; --k) {
+        const int h = hist[k * kTakeCols + tid];
+        if (cum + h >= q.cap) { tb = bmin + k; before = cum; break; }
+        cum += h;
+      }
+    } else {
+      auto above = [&](int b) {
+        int n = 0;
+        for (int g = 0; g < G; ++g) n += bucket(g) >= b ? count(g) : 0;
+        return n;
+      };
+      int lo = bmin, hi = bmax;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (above(mid) >= q.cap) lo = mid; else hi = mid - 1;
+      }
+      tb = lo;
+      before = tb < bmax ? above(tb + 1) : 0;
+    }
+    const int remain = static_cast<int>(q.cap) - before;
+    int prior = 0;
+    uint8_t* out = take + (int64_t)slot_group[slot] * q.BLP + c;
+    for (int g = 0; g < G; ++g) {
+      const int b = bucket(g);
+      const int cnt = count(g);
+      int t = 0;
+      if (b > tb) {
+        t = cnt;
+      } else if (b == tb) {
+        t = remain - prior;
+        t = t < 0 ? 0 : (t > cnt ? cnt : t);
+        prior += cnt;
+      }
+      out[(int64_t)g * q.BLP] = static_cast<uint8_t>(t);
+    }
+  }
+}
+
+// The take word (4 columns) of a capped record, or all-taken (0xFFFFFFFF with position 0) for
+// a record of an uncapped row.
+__device__ __forceinline__ unsigned take_word(const uint8_t* __restrict__ take, int2 rc, int64_t c, int64_t BLP) {
+  return rc.x >= 0 ? __ldg(reinterpret_cast<const unsigned*>(take + (int64_t)rc.x * BLP + c)) : 0xFFFFFFFFu;
+}
+__device__ __forceinline__ float4 cap_masked(float4 v, unsigned t4, int pos) {
+  const unsigned p = static_cast<unsigned>(pos);
+  v.x = (t4 & 0xffu) > p ? v.x : 0.0f;
+  v.y = ((t4 >> 8) & 0xffu) > p ? v.y : 0.0f;
+  v.z = ((t4 >> 16) & 0xffu) > p ? v.z : 0.0f;
+  v.w = (t4 >> 24) > p ? v.w : 0.0f;
+  return v;
+}
+
 // ------------------------------------------------------------------ forward pull
 // One warp per task (a segment of <= 64 records of one pull row) and column chunk of
 // 128*VEC columns.  Per batch of 32 records, the records whose source row is active in this
@@ -226,12 +366,14 @@ __device__ __forceinline__ void load_lanes(Lanes<VEC>& out, const float* __restr
 // the output feed normalize_sparse3d.
 // MAX = true: max of the exact message values (X[src] * w[ch]) * m (sparse3d_max over the
 // op's ind / ori / inv outputs), rule weights read per record.
-template <bool MAX, int VEC>
+template <bool MAX, int VEC, bool CAP>
 __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
-    float* __restrict__ y, float* __restrict__ dsum, int32_t* __restrict__ queue, unsigned* err) {
+    float* __restrict__ y, float* __restrict__ dsum, int32_t* __restrict__ queue, const int2* __restrict__ rcap,
+    const uint8_t* __restrict__ take, unsigned* err) {
   __shared__ int4 recs[kFwdWarps][32];
+  __shared__ int2 rcs[kFwdWarps][CAP ? 32 : 1];  // capped records: (take row, position in group)
   __shared__ float cs[4 * 32 * VEC];  // column partial sums: cs[(v*4 + k)*32 + lane] = column 4*lane + k + 128*v
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t chunk = blockIdx.y;
@@ -261,27 +403,50 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
     for (int base = tk.y; base < tk.z; base += 32) {
       const int cnt = min(32, tk.z - base);
       int4 rec = make_int4(0, 0, 0, 0);
+      int2 rc = make_int2(-1, 0);
       bool live = false;
       if (lane < cnt) {
         rec = reinterpret_cast<const int4*>(edges)[base + lane];
+        if (CAP) rc = rcap[base + lane];
         if (rec.x < 0 || rec.x >= q.E || rec.y < 0 || rec.y >= q.n - 1) raise_flag(err, MKG_DEV_BAD_COL);
+        else if (CAP && rc.x >= q.ngroups) raise_flag(err, MKG_DEV_BAD_ENTRY);
         else live = active_vec<VEC>(act, rec.x, chunk, q.nch);
       }
       const unsigned mask = __ballot_sync(0xffffffffu, live);
       const int nact = __popc(mask);
-      if (live) recs[warp][__popc(mask & ((1u << lane) - 1u))] = rec;
+      if (live) {
+        const int slot = __popc(mask & ((1u << lane) - 1u));
+        recs[warp][slot] = rec;
+        if (CAP) rcs[warp][slot] = rc;
+      }
       __syncwarp();
       for (int k0 = 0; k0 < nact; k0 += 4) {
         int4 r[4];
         Lanes<VEC> xv[4];
+        unsigned tw[4][VEC];  // take words, loaded with the X rows (capped loop)
+        int tp[4];            // positions inside the capped groups
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           r[u] = (k0 + u < nact) ? recs[warp][k0 + u] : make_int4(0, -1, 0, 0);
-          if (r[u].y >= 0) load_lanes(xv[u], x + (int64_t)r[u].x * q.BLP, col, q.BLP);
+          if (r[u].y >= 0) {
+            load_lanes(xv[u], x + (int64_t)r[u].x * q.BLP, col, q.BLP);
+            if (CAP) {
+              const int2 cr = rcs[warp][k0 + u];
+              tp[u] = cr.x >= 0 ? cr.y : 0;
+#pragma unroll
+              for (int k = 0; k < VEC; ++k)
+                tw[u][k] = (col + 128 * k < q.BLP) ? take_word(take, cr, col + 128 * k, q.BLP) : 0u;
+            }
+          }
         }
+
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           if (r[u].y < 0) continue;
+          if (CAP) {
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) xv[u].v[k] = cap_masked(xv[u].v[k], tw[u][k], tp[u]);
+          }
           const float m = __int_as_float(r[u].w);
           if (MAX) {
             Lanes<VEC> wv;
@@ -368,11 +533,11 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
 
 // normalize_sparse3d(.., 0, "mass") (drum.py:31-51) on the dense state:
 // x = (y / d) * min(d, 1) where y != 0; optional threshold; activity flags and the
-// message count of the next hop (present entries x push degree).
+// message count of the next hop (present entries x push degree, or x the capped degree).
 __global__ void normalize_mass_kernel(const float* __restrict__ y, const float* __restrict__ dsum, ProofDims q,
                                       float threshold, float* __restrict__ x, uint8_t* __restrict__ act,
                                       uint8_t* __restrict__ yact, const int32_t* __restrict__ push_ptr,
-                                      int64_t* __restrict__ msgs) {
+                                      const int32_t* __restrict__ capdeg, int64_t* __restrict__ msgs) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -408,7 +573,7 @@ __global__ void normalize_mass_kernel(const float* __restrict__ y, const float* 
     if (lane == 0) {
       act[row * q.nch + chunk] = any ? 1 : 0;
       yact[row * q.nch + chunk] = yany ? 1 : 0;
-      if (tot) local_msgs += (long long)tot * (push_ptr[row + 1] - push_ptr[row]);
+      if (tot) local_msgs += (long long)tot * (capdeg ? capdeg[row] : push_ptr[row + 1] - push_ptr[row]);
     }
   }
   if (lane == 0 && local_msgs) atomicAdd(reinterpret_cast<unsigned long long*>(msgs), (unsigned long long)local_msgs);
@@ -521,7 +686,8 @@ int make_rows_map(CUtensorMap* map, const float* base, int64_t rows, int64_t col
 
 __global__ void normalize_plain_kernel(const float* __restrict__ y, const float* __restrict__ d, ProofDims q,
                                        float* __restrict__ x, uint8_t* __restrict__ act,
-                                       const int32_t* __restrict__ push_ptr, int64_t* __restrict__ msgs) {
+                                       const int32_t* __restrict__ push_ptr, const int32_t* __restrict__ capdeg,
+                                       int64_t* __restrict__ msgs) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -546,7 +712,7 @@ __global__ void normalize_plain_kernel(const float* __restrict__ y, const float*
     for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
     if (lane == 0) {
       act[row * q.nch + chunk] = any ? 1 : 0;
-      if (tot) local_msgs += (long long)tot * (push_ptr[row + 1] - push_ptr[row]);
+      if (tot) local_msgs += (long long)tot * (capdeg ? capdeg[row] : push_ptr[row + 1] - push_ptr[row]);
     }
   }
   if (lane == 0 && local_msgs) atomicAdd(reinterpret_cast<unsigned long long*>(msgs), (unsigned long long)local_msgs);
@@ -717,12 +883,14 @@ __device__ __forceinline__ float reduce_scatter4(const float (&v)[4]) {
 // (one rule-weight load per run).  Only records whose destination row holds a non-zero Y_h
 // value in this chunk are visited (dY_h is zero elsewhere).  Rule weights are read from
 // global memory (L1-resident chunk) so that only dW occupies shared memory: 3 blocks per SM.
+template <bool CAP>
 __global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
     const uint8_t* __restrict__ yact, const float* __restrict__ dy, const float* __restrict__ yprev,
     float* __restrict__ dx, float* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge,
-    int64_t num_facts, EdgeFactor ef, int32_t* __restrict__ queue, unsigned* err) {
+    int64_t num_facts, EdgeFactor ef, int32_t* __restrict__ queue, const int2* __restrict__ rcap,
+    const uint8_t* __restrict__ take, unsigned* err) {
   extern __shared__ float smem[];
   float* dws = smem;                        // [n][128] rule-weight gradient (conflict-free: [ch][k][lane])
   float* cs = dws + q.n * kChunk;           // [4][32] S_prev partials
@@ -778,10 +946,13 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
       for (int base = tk.y; base < tk.z; base += 32) {
         const int cnt = min(32, tk.z - base);
         int4 rec = make_int4(0, 0, 0, 0);
+        int2 rc = make_int2(-1, 0);
         bool live = false;
         if (lane < cnt) {
           rec = reinterpret_cast<const int4*>(edges)[base + lane];
+          if (CAP) rc = rcap[base + lane];
           if (rec.x < 0 || rec.x >= q.E || rec.y < 0 || rec.y >= q.n - 1) raise_flag(err, MKG_DEV_BAD_COL);
+          else if (CAP && rc.x >= q.ngroups) raise_flag(err, MKG_DEV_BAD_ENTRY);
           else live = yact[(int64_t)rec.x * q.nch + chunk] != 0;  // dY is zero where Y is
         }
         unsigned pending = __ballot_sync(0xffffffffu, live);
@@ -789,6 +960,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
           int nb[kBatch], ch[kBatch], fa[kBatch];
           float m[kBatch];
           bool ok[kBatch];
+          int src[kBatch];  // lane that loaded the record
 #pragma unroll
           for (int u = 0; u < kBatch; ++u) {
             ok[u] = pending != 0;
@@ -798,11 +970,24 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
             ch[u] = __shfl_sync(0xffffffffu, rec.y, jj);
             fa[u] = __shfl_sync(0xffffffffu, rec.z, jj);
             m[u] = __int_as_float(__shfl_sync(0xffffffffu, rec.w, jj));
+            src[u] = jj;
           }
           float4 gv[kBatch];
 #pragma unroll
           for (int u = 0; u < kBatch; ++u)
             gv[u] = (ok[u] && colok) ? *reinterpret_cast<const float4*>(dy + (int64_t)nb[u] * q.BLP + col) : zero;
+          if (CAP) {
+            unsigned tw[kBatch];
+            int tp[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+              const int2 cr = make_int2(__shfl_sync(0xffffffffu, rc.x, src[u]), __shfl_sync(0xffffffffu, rc.y, src[u]));
+              tw[u] = (ok[u] && colok) ? take_word(take, cr, col, q.BLP) : 0xFFFFFFFFu;
+              tp[u] = cr.x >= 0 ? cr.y : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) gv[u] = cap_masked(gv[u], tw[u], tp[u]);
+          }
           float ep[kBatch];
 #pragma unroll
           for (int u = 0; u < kBatch; ++u) {
@@ -1003,8 +1188,20 @@ int check_proof(const mkg_graph* g, const mkg_adjacency* adj, const mkg_proof_pa
   MKG_REQUIRE(adj->pull_tasks && adj->push_tasks && adj->num_pull_tasks > 0 && adj->num_push_tasks > 0 &&
                   adj->pull && adj->push && adj->pull_ptr && adj->push_ptr,
               "proof: adjacency has no task lists (call mkg_adjacency_build and read the task counts)");
-  MKG_REQUIRE(p->topk_edges >= (int64_t(1) << 60),
-              "proof: the fused loop runs uncapped hops; capped hops go through mkg_hop_forward");
+  if (p->topk_edges < (int64_t(1) << 60)) {
+    const mkg_cap_index* ix = p->cap_index;
+    if (p->topk_edges < 0 || p->topk_edges > MKG_DENSE_CAP_MAX) {
+      set_error("proof: the fused loop takes edge caps in [0, %d] (got %lld); larger caps go through "
+                "mkg_hop_forward", MKG_DENSE_CAP_MAX, (long long)p->topk_edges);
+      return MKG_ERR_UNSUPPORTED;
+    }
+    MKG_REQUIRE(ix != nullptr, "proof: a capped loop needs the cap index (mkg_cap_index_build)");
+    MKG_REQUIRE(ix->cap == p->topk_edges, "proof: the cap index was built for cap %lld, not %lld",
+                (long long)ix->cap, (long long)p->topk_edges);
+    MKG_REQUIRE(ix->pull_cap && ix->push_cap && ix->capped_degree && ix->num_slots >= 0 && ix->num_groups >= 0 &&
+                    (ix->num_slots == 0 || (ix->slot_entity && ix->slot_dir && ix->slot_group)),
+                "proof: incomplete cap index");
+  }
   ProofDims q = proof_dims(*p);
   MKG_REQUIRE(bwd_smem(q) <= 200 * 1024, "proof: too many relation channels (%lld) for the shared-memory "
               "staging of the rule weights", (long long)q.n);
@@ -1041,13 +1238,17 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
   MKG_CUDA(cudaMemsetAsync(S.d(0), 0, 4 * (size_t)q.hops * q.BLP, st));
   MKG_CUDA(cudaMemsetAsync(S.queue(), 0, 4 * (size_t)(q.hops * q.nch * kQueueStride), st));
   MKG_CUDA(cudaMemsetAsync(S.msgs(), 0, 8 * (size_t)(q.hops + 1), st));
-  init_state_kernel<<<grid_for(q.BL, 256, pb), 256, 0, st>>>(heads, q, S.x(0), S.act(0), adj->push_ptr, S.msgs(), err);
+  const mkg_cap_index* ix = q.cap >= 0 ? p->cap_index : nullptr;
+  const int32_t* capdeg = ix ? ix->capped_degree : nullptr;
+  const int2* pull_cap = ix ? reinterpret_cast<const int2*>(ix->pull_cap) : nullptr;
+  init_state_kernel<<<grid_for(q.BL, 256, pb), 256, 0, st>>>(heads, q, S.x(0), S.act(0), adj->push_ptr, capdeg,
+                                                             S.msgs(), err);
   MKG_LAUNCHED("init_state_kernel");
   // 256-column chunks (8 columns per lane) when the batch is wide enough
   const int vec = fwd_vec_knob(q);
   const int64_t nfch = (q.BLP + 128 * vec - 1) / (128 * vec);
-  const void* fwd_fn = max_mode ? (vec == 2 ? (const void*)fwd_pull_kernel<true, 2> : (const void*)fwd_pull_kernel<true, 1>)
-                                : (vec == 2 ? (const void*)fwd_pull_kernel<false, 2> : (const void*)fwd_pull_kernel<false, 1>);
+  const void* fwd_fn = max_mode ? (vec == 2 ? (const void*)fwd_pull_kernel<true, 2, false> : (const void*)fwd_pull_kernel<true, 1, false>)
+                                : (vec == 2 ? (const void*)fwd_pull_kernel<false, 2, false> : (const void*)fwd_pull_kernel<false, 1, false>);
   int resident = 0;
   MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fwd_fn, kFwdWarps * 32, 0));
   // one wave of resident blocks, split evenly over the column chunks
@@ -1055,6 +1256,13 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
                                         (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / nfch) + 1);
   for (int64_t h = 0; h < q.hops; ++h) {
     float* y = S.y(h);
+    if (ix && ix->num_slots > 0) {
+      const int64_t take_blocks = ix->num_slots * ((q.BLP + kTakeCols - 1) / kTakeCols);
+      cap_take_kernel<<<(unsigned)(take_blocks < (int64_t)pb * 8 ? take_blocks : (int64_t)pb * 8), kTakeCols, 0, st>>>(
+          make_dir(g->ori), make_dir(g->inv), ix->slot_entity, ix->slot_dir, ix->slot_group, ix->num_slots, q, S.wt(h),
+          S.act(h), S.take(h), err);
+      MKG_LAUNCHED("cap_take_kernel");
+    }
     zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, q, y);
     MKG_LAUNCHED("zero_partial_rows_kernel");
     dim3 grid(blocks_per_chunk, (unsigned)nfch);
@@ -1063,14 +1271,23 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
       const int4* tk = reinterpret_cast<const int4*>(adj->pull_tasks);
       const int64_t nt = adj->num_pull_tasks;
       float* ds = max_mode ? nullptr : S.d(h);
-      if (max_mode && vec == 2)
-        fwd_pull_kernel<true, 2><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
-      else if (max_mode)
-        fwd_pull_kernel<true, 1><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
-      else if (vec == 2)
-        fwd_pull_kernel<false, 2><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
-      else
-        fwd_pull_kernel<false, 1><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, S.queue() + h * q.nch * kQueueStride, err);
+      int32_t* qu = S.queue() + h * q.nch * kQueueStride;
+      const uint8_t* tk_h = ix ? S.take(h) : nullptr;
+#define MKG_FWD_PULL(M, V, C) \
+  fwd_pull_kernel<M, V, C><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, \
+                                                           qu, pull_cap, tk_h, err)
+      if (ix) {
+        if (max_mode && vec == 2) MKG_FWD_PULL(true, 2, true);
+        else if (max_mode) MKG_FWD_PULL(true, 1, true);
+        else if (vec == 2) MKG_FWD_PULL(false, 2, true);
+        else MKG_FWD_PULL(false, 1, true);
+      } else {
+        if (max_mode && vec == 2) MKG_FWD_PULL(true, 2, false);
+        else if (max_mode) MKG_FWD_PULL(true, 1, false);
+        else if (vec == 2) MKG_FWD_PULL(false, 2, false);
+        else MKG_FWD_PULL(false, 1, false);
+      }
+#undef MKG_FWD_PULL
     }
     MKG_LAUNCHED("fwd_pull_kernel");
     if (p->fwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->fwd_events[2 * h + 1]), st));
@@ -1081,13 +1298,13 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
       sequential_colsum_kernel<<<(unsigned)((q.BLP + 31) / 32), 64, 0, st>>>(ymap, q, S.d(h), err);
       MKG_LAUNCHED("sequential_colsum_kernel");
       if (h + 1 < q.hops) {
-        normalize_plain_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, S.x(h + 1), S.act(h + 1), adj->push_ptr,
+        normalize_plain_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, S.x(h + 1), S.act(h + 1), adj->push_ptr, capdeg,
                                                    S.msgs() + h + 1);
         MKG_LAUNCHED("normalize_plain_kernel");
       }
     } else {
       normalize_mass_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, p->state_threshold, S.x(h + 1), S.act(h + 1),
-                                                S.yact(h), adj->push_ptr, S.msgs() + h + 1);
+                                                S.yact(h), adj->push_ptr, capdeg, S.msgs() + h + 1);
       MKG_LAUNCHED("normalize_mass_kernel");
     }
   }
@@ -1131,10 +1348,13 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
   seed_grad_kernel<<<sgrid, dim3(32, 8), 0, st>>>(grad_out, S.x(q.hops), S.y(q.hops - 1), q, dx_cur, S.s(q.hops - 1));
   MKG_LAUNCHED("seed_grad_kernel");
   const size_t sm = bwd_smem(q);
-  rc = set_smem((const void*)bwd_pull_kernel, sm);
+  const mkg_cap_index* ix = q.cap >= 0 ? p->cap_index : nullptr;
+  const int2* push_cap = ix ? reinterpret_cast<const int2*>(ix->push_cap) : nullptr;
+  const void* bwd_fn = ix ? (const void*)bwd_pull_kernel<true> : (const void*)bwd_pull_kernel<false>;
+  rc = set_smem(bwd_fn, sm);
   if (rc) return rc;
   int resident = 0;
-  MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, bwd_pull_kernel, kBwdWarps * 32, sm));
+  MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, bwd_fn, kBwdWarps * 32, sm));
   const int blocks_per_chunk = grid_for(adj->num_push_tasks, kBwdWarps,
                                         (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / q.nch) + 1);
   for (int64_t h = q.hops - 1; h >= 0; --h) {
@@ -1148,10 +1368,20 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
     (void)slab;
     dim3 grid(blocks_per_chunk, (unsigned)q.nch);
     if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h]), st));
-    bwd_pull_kernel<<<grid, kBwdWarps * 32, sm, st>>>(
-        reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.yact(h), S.dy(),
-        h > 0 ? S.y(h - 1) : nullptr, dx_next, S.dwt(), h > 0 ? S.s(h - 1) : nullptr, grad_edge, g->num_facts, f,
-        S.queue() + (q.hops + h) * q.nch * kQueueStride, err);
+    {
+      const int4* tk = reinterpret_cast<const int4*>(adj->push_tasks);
+      int32_t* qu = S.queue() + (q.hops + h) * q.nch * kQueueStride;
+      if (ix)
+        bwd_pull_kernel<true><<<grid, kBwdWarps * 32, sm, st>>>(
+            tk, adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.yact(h), S.dy(),
+            h > 0 ? S.y(h - 1) : nullptr, dx_next, S.dwt(), h > 0 ? S.s(h - 1) : nullptr, grad_edge, g->num_facts, f,
+            qu, push_cap, S.take(h), err);
+      else
+        bwd_pull_kernel<false><<<grid, kBwdWarps * 32, sm, st>>>(
+            tk, adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.yact(h), S.dy(),
+            h > 0 ? S.y(h - 1) : nullptr, dx_next, S.dwt(), h > 0 ? S.s(h - 1) : nullptr, grad_edge, g->num_facts, f,
+            qu, nullptr, nullptr, err);
+    }
     MKG_LAUNCHED("bwd_pull_kernel");
     if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h + 1]), st));
     untranspose_dw_kernel<<<grid_for(q.BL * q.n, 256, pb), 256, 0, st>>>(S.dwt(), q, h, grad_w_hops);

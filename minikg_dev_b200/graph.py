@@ -114,6 +114,7 @@ class DeviceGraph:
         self._adj = None
         self._adj_keep = None
         self._facts = None
+        self._cap = {}
 
     @classmethod
     def from_triples(cls, head: torch.Tensor, rel: torch.Tensor, tail: torch.Tensor, num_entities: int,
@@ -178,6 +179,35 @@ class DeviceGraph:
             adj.num_push_tasks = int(n_push)
             self._adj, self._adj_keep = adj, keep
         return self._adj
+
+    def cap_index(self, cap: int) -> N.CapIndex:
+        """The fused engine's edge-cap index for ``cap`` (0 .. MKG_DENSE_CAP_MAX): per-hop take
+        tables are filled from it by the loop.  Built once per cap value and kept."""
+        cap = int(cap)
+        if cap not in self._cap:
+            lib = N.load()
+            dev, E, T = self.device, self.num_entities, self.num_facts
+            adj = self.adjacency()
+            ws = N.workspace(lib.mkg_cap_index_workspace_bytes(C_ref(self.struct)), dev)
+            sizes = torch.zeros(2, dtype=torch.int64, device=dev)
+            st = N.stream_handle(dev)
+            N.check(lib.mkg_cap_index_sizes(C_ref(self.struct), cap, sizes.data_ptr(), ws.data_ptr(), ws.numel(), st),
+                    "cap_index_sizes")
+            n_slots, n_groups = (int(x) for x in sizes.tolist())
+            keep = dict(slot_entity=torch.empty(max(n_slots, 1), dtype=torch.int32, device=dev),
+                        slot_dir=torch.empty(max(n_slots, 1), dtype=torch.int32, device=dev),
+                        slot_group=torch.empty(max(n_slots, 1), dtype=torch.int32, device=dev),
+                        pull_cap=torch.empty((2 * T, 2), dtype=torch.int32, device=dev),
+                        push_cap=torch.empty((2 * T, 2), dtype=torch.int32, device=dev),
+                        capped_degree=torch.empty(max(E, 1), dtype=torch.int32, device=dev))
+            ix = N.CapIndex(cap, n_slots, n_groups, *(keep[k].data_ptr() for k in
+                                                       ("slot_entity", "slot_dir", "slot_group", "pull_cap",
+                                                        "push_cap", "capped_degree")))
+            N.check(lib.mkg_cap_index_build(C_ref(self.struct), C_ref(adj), C_ref(ix), ws.data_ptr(), ws.numel(),
+                                            N.error_word(dev).data_ptr(), st), "cap_index_build")
+            N.raise_device_errors(dev)
+            self._cap[cap] = (ix, keep)
+        return self._cap[cap][0]
 
     def push_degree(self) -> torch.Tensor:
         self.adjacency()

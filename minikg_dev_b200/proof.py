@@ -12,9 +12,11 @@ whose dense state does not fit), with ``norm_sp_3d`` row sums added in key order
 (``mkg_segment_sum_ordered``) so its result stays bit-exact too.
 
 ``kernel_sparse_scores(model, heads, rels, graph, args, is_training)`` keeps the
-reference signature.  Hops the fused loop does not cover (an edge cap, entity pruning
-that is not a no-op, dropout while training) run hop by hop through
-``FastLogFunctionSparse3DTopK`` and the reducers, exactly as the reference composes them.
+reference signature.  The fused loop covers uncapped hops and edge caps up to
+DENSE_CAP_MAX (per-hop take tables of the capped rows, ``DeviceGraph.cap_index``) while the
+dense state fits on the device; larger caps, entity pruning that is not a no-op, or graphs
+too large for a dense state run the sparse loop (``sparse_loop.SparseHopLoop``), and dropout
+while training runs hop by hop as the reference composes it.
 """
 from __future__ import annotations
 
@@ -31,10 +33,28 @@ from .sparse_reducers import (max_sp_3d, normalize_sparse3d, prune_sparse3d_acti
                               sum_sparse3d_concat)
 
 UNCAPPED = 1 << 60
+DENSE_CAP_MAX = 255  # MKG_DENSE_CAP_MAX: edge caps the fused loop takes
 
 
-def _params(B, L, E, R, hops, threshold=0.0, topk_edges=UNCAPPED):
-    return N.ProofParams(int(B), int(L), int(E), int(R), int(hops), int(topk_edges), float(threshold), 0, None, None)
+def dense_cap(topk_edges: int) -> int | None:
+    """The fused loop's cap for the reference's ``topk_edges``: UNCAPPED, a cap in
+    [0, DENSE_CAP_MAX] (a cap <= 0 takes no edge), or None (larger caps: the sparse loop)."""
+    c = int(topk_edges)
+    if c >= UNCAPPED:
+        return UNCAPPED
+    c = max(c, 0)
+    return c if c <= DENSE_CAP_MAX else None
+
+
+def _params(graph: DeviceGraph, B, L, hops, threshold=0.0, topk_edges=UNCAPPED):
+    """Loop parameters; a capped loop carries the graph's cap index for ``topk_edges``."""
+    cap = dense_cap(topk_edges)
+    if cap is None:
+        raise ValueError(f"the fused loop takes edge caps up to {DENSE_CAP_MAX} (got {topk_edges})")
+    ix = graph.cap_index(cap) if cap < UNCAPPED else None
+    p = N.ProofParams(int(B), int(L), graph.num_entities, graph.num_relations, int(hops), int(cap), float(threshold), 0,
+                      None, None, ctypes.cast(ctypes.pointer(ix), ctypes.c_void_p) if ix is not None else None)
+    return p, ix
 
 
 class ProofRunner:
@@ -45,12 +65,13 @@ class ProofRunner:
     are recorded around the pull kernels of each hop.
     """
 
-    def __init__(self, graph: DeviceGraph, B: int, L: int, hops: int, threshold: float = 0.0):
+    def __init__(self, graph: DeviceGraph, B: int, L: int, hops: int, threshold: float = 0.0,
+                 topk_edges: int = UNCAPPED):
         lib = N.load()
         self.graph = graph
         self.B, self.L, self.K = int(B), int(L), int(hops)
         self.n = 2 * graph.num_relations + 1
-        self.p = _params(B, L, graph.num_entities, graph.num_relations, hops, threshold)
+        self.p, self._cap_ix = _params(graph, B, L, hops, threshold, topk_edges)
         self.ws = N.workspace(lib.mkg_proof_workspace_bytes(ctypes.byref(self.p)), graph.device)
         self._keep = []
 
@@ -149,12 +170,12 @@ class HopLoopSum(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, w_hops, edge_scores, heads, graph: DeviceGraph, mask, is_score: bool, scale: float,
-                threshold: float):
+                threshold: float, topk_edges: int = UNCAPPED):
         K, B, L, n = (int(s) for s in w_hops.shape)
         if n != 2 * graph.num_relations + 1:
             raise ValueError(f"w_hops has {n} channels, expected 2R+1 = {2 * graph.num_relations + 1}")
         graph.set_edge_factor(mask, edge_scores, is_score, scale)
-        runner = ProofRunner(graph, B, L, K, threshold)
+        runner = ProofRunner(graph, B, L, K, threshold, topk_edges)
         out, msgs = runner.forward(heads, w_hops)
         ctx.runner = runner
         ctx.mask, ctx.is_score, ctx.scale = mask, bool(is_score), float(scale)
@@ -173,14 +194,15 @@ class HopLoopSum(torch.autograd.Function):
         ge = None
         if grad_edge is not None:
             ge = grad_edge.view(ctx.edge_scores.shape).to(ctx.edge_scores.dtype)
-        return grad_w, ge, None, None, None, None, None, None
+        return grad_w, ge, None, None, None, None, None, None, None
 
 
 def proof_scores(graph: DeviceGraph, heads: torch.Tensor, w_hops: torch.Tensor, edge_scores: torch.Tensor | None,
                  mask: torch.Tensor | None = None, is_score: bool = True, scale: float = 1.0,
-                 threshold: float = 0.0):
-    """Dense raw scores ``[B, E]`` of the hop loop and the per-hop message counts ``[K]``."""
-    return HopLoopSum.apply(w_hops, edge_scores, heads, graph, mask, is_score, scale, threshold)
+                 threshold: float = 0.0, topk_edges: int = UNCAPPED):
+    """Dense raw scores ``[B, E]`` of the hop loop and the per-hop message counts ``[K]``;
+    ``topk_edges`` <= DENSE_CAP_MAX caps every entry's messages as the reference's op does."""
+    return HopLoopSum.apply(w_hops, edge_scores, heads, graph, mask, is_score, scale, threshold, topk_edges)
 
 
 @dataclass
@@ -193,8 +215,9 @@ class DecodeResult:
 
 def decode_max(graph: DeviceGraph, heads: torch.Tensor, w_hops: torch.Tensor, topk: int,
                edge_scores: torch.Tensor | None, mask: torch.Tensor | None = None, is_score: bool = True,
-               scale: float = 1.0) -> DecodeResult:
-    """Max-aggregation hop loop + decode order (score desc, tail asc), top-``topk`` per query."""
+               scale: float = 1.0, topk_edges: int = UNCAPPED) -> DecodeResult:
+    """Max-aggregation hop loop + decode order (score desc, tail asc), top-``topk`` per query
+    (``topk_edges`` <= DENSE_CAP_MAX: the reference's edge cap on every hop)."""
     lib = N.load()
     dev = graph.device
     K, B, L, n = (int(s) for s in w_hops.shape)
@@ -202,7 +225,7 @@ def decode_max(graph: DeviceGraph, heads: torch.Tensor, w_hops: torch.Tensor, to
     wf = w_hops.detach().to(torch.float32).contiguous()
     hd = heads.to(device=dev, dtype=torch.int64).contiguous()
     graph.set_edge_factor(mask, edge_scores, is_score, scale)
-    p = _params(B, L, E, R, K)
+    p, _ix = _params(graph, B, L, K, 0.0, topk_edges)
     ws = N.workspace(lib.mkg_decode_workspace_bytes(ctypes.byref(p), int(topk)), dev)
     raw = torch.empty((B, E), dtype=torch.float32, device=dev)
     tails = torch.empty((B, int(topk)), dtype=torch.int64, device=dev)
@@ -313,6 +336,22 @@ def _device_graph_for(model, graph) -> DeviceGraph:
     return model._b200_graph
 
 
+FUSED_MAX_CHANNELS = (200 * 1024 // 4 - 128) // 128  # the backward stages dW [n, 128] in shared memory
+
+
+def dense_state_fits(graph: DeviceGraph, B: int, L: int, hops: int, fraction: float = 0.5) -> bool:
+    """Whether the fused loop takes this graph: at most FUSED_MAX_CHANNELS relation channels,
+    and dense [E, B*L] states (every hop's, forward and backward) within ``fraction`` of the
+    device's free memory.  Other graphs run the sparse loop."""
+    if 2 * graph.num_relations + 1 > FUSED_MAX_CHANNELS:
+        return False
+    p = N.ProofParams(int(B), int(L), graph.num_entities, graph.num_relations, int(hops), UNCAPPED, 0.0, 0,
+                      None, None, None)
+    need = int(N.load().mkg_proof_workspace_bytes(ctypes.byref(p)))
+    free, _total = torch.cuda.mem_get_info(graph.device)
+    return need <= fraction * free
+
+
 def _edge_inputs(model, graph, is_training):
     """Edge scores / mask exactly as proof.py:525-550 picks them (score path)."""
     edge_scores = model.weight
@@ -339,9 +378,11 @@ def kernel_sparse_scores(model, heads, rels, graph, args, is_training: bool, den
     topk_edges = int(args.kernel_topk_edges)
     topk_nodes = int(args.kernel_topk_nodes)
     p_drop = float(getattr(getattr(model, "dropout", None), "p", 0.0) or 0.0)
-    fused = topk_edges >= UNCAPPED and (topk_nodes <= 0 or topk_nodes >= E) and not (is_training and p_drop > 0)
+    cap = dense_cap(topk_edges)
+    fused = (cap is not None and (topk_nodes <= 0 or topk_nodes >= E) and not (is_training and p_drop > 0)
+             and dense_state_fits(g, heads.shape[0], L, K))
     if fused:
-        out, _ = HopLoopSum.apply(w_all, edge_scores, heads, g, mask, is_score, scale, 0.0)
+        out, _ = HopLoopSum.apply(w_all, edge_scores, heads, g, mask, is_score, scale, 0.0, cap)
         return out if dense else out.to_sparse_coo().coalesce()
     if not (is_training and p_drop > 0):
         # any cap / prune: the sparse loop fused around the op (merged outputs, written-out backward)

@@ -407,6 +407,112 @@ def test_sparse_loop_vs_oracle(gname, cap, topk_nodes, accum):
     np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("gname", ["hubby", "g2"])
+@pytest.mark.parametrize("cap", [0, 1, 3, 9, 40])
+def test_fused_capped_loop_vs_oracle(gname, cap):
+    """The fused dense loop with the edge cap (per-hop take tables of the capped rows)."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import proof_scores
+    h, r, t, E, R = GRAPHS[gname]
+    rng = np.random.default_rng(cap + 7)
+    csr = O.build_csr_structure(h, t, r, E)
+    B, L, K, n = 12, 3, 3, 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    w_hops[:, 1, 0, :] = np.float32(1.0 / n)  # every group of a row in one bucket: ties decided by group order
+    scores = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    mask = np.ones(h.shape[0], bool)
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R, cap=cap)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    wt = T(w_hops).requires_grad_(True)
+    sc = T(scores).requires_grad_(True)
+    out, msgs = proof_scores(dg, T(heads), wt, sc, mask=None, topk_edges=cap)
+    want = np.zeros((B, E), np.float32)
+    b, e = final[0] // E, final[0] % E
+    want[b, e] = final[1]
+    got = out.detach().cpu().numpy()
+    np.testing.assert_array_equal(got != 0, want != 0)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    assert msgs.cpu().tolist() == [O.count_messages(tr["state"], csr, w_hops[k], L, E, R, cap=cap)
+                                   for k, tr in enumerate(trace)]
+    seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
+    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
+                                  num_facts=h.shape[0])
+    gd = np.zeros((B, E), np.float32)
+    gd[b, e] = seed
+    (out * T(gd)).sum().backward()
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("gname", ["hubby", "g2"])
+def test_cap_index_sizes(gname):
+    """Capped rows (out-degree above the cap, per direction) and their relation groups."""
+    from minikg_dev_b200.graph import DeviceGraph
+    h, r, t, E, R = GRAPHS[gname]
+    csr = O.build_csr_structure(h, t, r, E)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    for cap in (0, 3, 40, 255):
+        slots = groups = 0
+        capdeg = np.zeros(E, np.int64)
+        for rp, gp in ((csr[0], csr[8]), (csr[4], csr[12])):
+            deg = np.diff(rp.astype(np.int64))
+            ng = np.diff(gp.astype(np.int64))
+            slots += int((deg > cap).sum())
+            groups += int(ng[deg > cap].sum())
+            capdeg += np.minimum(deg, cap)
+        ix = dg.cap_index(cap)
+        assert (ix.num_slots, ix.num_groups) == (slots, groups)
+        np.testing.assert_array_equal(dg._cap[cap][1]["capped_degree"][:E].cpu().numpy(), capdeg)
+
+
+@pytest.mark.parametrize("gname", ["hubby", "g2"])
+@pytest.mark.parametrize("cap", [1, 9, 40])
+def test_fused_capped_max_decode_vs_oracle_bit_exact(gname, cap):
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import decode_max
+    h, r, t, E, R = GRAPHS[gname]
+    rng = np.random.default_rng(31 + cap)
+    csr = O.build_csr_structure(h, t, r, E)
+    B, L, K, n = 16, 3, 3, 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    w_hops[:, 0, 0, :] = np.float32(1.0 / n)
+    scores = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    scores[::3] = np.float32(0.5)
+    final, _ = O.proof_max_forward(heads, w_hops, csr, np.ones(h.shape[0], bool), scores, B, L, E, R, cap=cap)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    res = decode_max(dg, T(heads), T(w_hops), 100, T(scores), topk_edges=cap)
+    want = np.zeros((B, E), np.float32)
+    want[final[0] // E, final[0] % E] = final[1]
+    np.testing.assert_array_equal(res.raw.cpu().numpy(), want)
+    ot, osc, oc = O.decode_topk(final, B, E, 100)
+    np.testing.assert_array_equal(res.tails.cpu().numpy(), ot)
+    np.testing.assert_array_equal(res.scores.cpu().numpy(), osc)
+    np.testing.assert_array_equal(res.counts.cpu().numpy(), oc)
+
+
+@pytest.mark.parametrize("gname", ["g1", "g2"])
+def test_fused_capped_max_decode_vs_golden(gname):
+    """The fused capped decode on the reference's own CSR (its in-group order decides which
+    edges a capped group takes) against the reference's capped decode (cap 9)."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import decode_max
+    g = load_golden(gname)
+    E, R = int(g["E"][0]), int(g["R"][0])
+    heads, logits, scores = g["pr_heads"], g["pr_logits"], g["pr_scores"]
+    B, K, L, n = logits.shape
+    dg = DeviceGraph(csr_dev(tuple(g[f"csr{k}"] for k in range(16))), E, R)
+    k = g["dec_cap_tails"].shape[1]
+    res = decode_max(dg, T(heads), T(_w_hops_from_logits(logits)), k, T(scores), topk_edges=9)
+    idx = g["dec_cap_final_idx"]
+    want = np.zeros((B, E), np.float32)
+    want[idx[0], idx[1]] = g["dec_cap_final_val"]
+    np.testing.assert_array_equal(res.raw.cpu().numpy(), want)
+    np.testing.assert_array_equal(res.tails.cpu().numpy(), g["dec_cap_tails"])
+    np.testing.assert_allclose(res.scores.cpu().numpy(), g["dec_cap_scores"], rtol=0, atol=6e-8)
+
+
 @pytest.mark.parametrize("gname", ["g1", "g2"])
 def test_max_decode_vs_golden_bit_exact(gname):
     from minikg_dev_b200.graph import DeviceGraph

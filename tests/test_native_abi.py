@@ -69,7 +69,9 @@ STRUCTS = {
                                     "dst_hi", "msg_bound", "accum",
                                     "merge_outputs"]),
     "mkg_proof_params": ("ProofParams", ["B", "L", "E", "R", "hops", "topk_edges", "state_threshold", "reserved",
-                                         "fwd_events", "bwd_events"]),
+                                         "fwd_events", "bwd_events", "cap_index"]),
+    "mkg_cap_index": ("CapIndex", ["cap", "num_slots", "num_groups", "slot_entity", "slot_dir", "slot_group",
+                                   "pull_cap", "push_cap", "capped_degree"]),
     "mkg_rule_params": ("RuleParams", ["n", "H", "L", "K", "U", "B", "tau", "reserved"]),
 }
 

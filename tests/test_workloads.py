@@ -98,6 +98,33 @@ def test_fused_loop_subset_vs_oracle(name):
 
 
 @pytest.mark.parametrize("name", FUSED)
+def test_fused_capped_subset_vs_oracle(name):
+    """The reference's production edge cap (100) on the fused loop, full graph, a query subset."""
+    from minikg_dev_b200.proof import proof_scores
+    wl, kg, csr, dg, inp = workload(name)
+    E, R, L, K = kg.num_entities, kg.num_relations, wl.L, wl.hops
+    cap = 100
+    heads, w = inp.heads[:SUB], inp.rule_weights[:, :SUB]
+    final, trace = O.proof_sum_forward(heads, w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R, cap=cap,
+                                       threshold=wl.state_threshold)
+    wt = T(w).requires_grad_(True)
+    sc = T(inp.edge_scores).requires_grad_(True)
+    out, msgs = proof_scores(dg, T(heads), wt, sc, mask=None, threshold=wl.state_threshold, topk_edges=cap)
+    _assert_close(out.detach().cpu().numpy(), _dense(final[0], final[1], SUB, E), wl.state_threshold)
+    exp_msgs = [O.count_messages(tr["state"], csr, w[k], L, E, R, cap=cap) for k, tr in enumerate(trace)]
+    if wl.state_threshold > 0:
+        np.testing.assert_allclose(msgs.cpu().numpy(), exp_msgs, rtol=1e-3)
+    else:
+        assert msgs.cpu().tolist() == exp_msgs
+    seed = np.random.default_rng(5).standard_normal(final[0].shape[0]).astype(np.float32)
+    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
+                                  num_facts=kg.num_triples)
+    (out * T(_dense(final[0], seed, SUB, E))).sum().backward()
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+
+
+@pytest.mark.parametrize("name", FUSED)
 def test_fused_loop_full_batch(name):
     """Full B: the first queries match the oracle-checked subset run; per-query mass <= L."""
     from minikg_dev_b200.proof import proof_scores
