@@ -711,11 +711,12 @@ def test_device_graph_from_npy(tmp_path):
         np.testing.assert_array_equal(got.cpu().numpy(), exp, err_msg=f"csr[{k}]")
 
 
-@pytest.mark.parametrize("variant", ["mask", "logit"])
-@pytest.mark.parametrize("engine", ["fused", "sparse"])
+@pytest.mark.parametrize("variant", ["mask", "logit", "threshold"])
+@pytest.mark.parametrize("engine", ["fused", "fused_capped", "sparse"])
 def test_loops_masked_facts_and_sigmoid_path(variant, engine):
-    """Both hop loops with facts masked off (their messages are explicit zeros, dropped by the
-    normalisation) or with the sigmoid edge-score path, against the oracle, fwd and bwd."""
+    """Both hop loops (the fused one uncapped and with cap 9) with facts masked off (their
+    messages are explicit zeros, dropped by the normalisation), with the sigmoid edge-score
+    path, or with a state threshold, against the oracle, fwd and bwd."""
     from minikg_dev_b200.graph import DeviceGraph
     from minikg_dev_b200.proof import proof_scores
     from minikg_dev_b200.sparse_loop import sparse_proof_scores
@@ -726,22 +727,29 @@ def test_loops_masked_facts_and_sigmoid_path(variant, engine):
     heads = rng.integers(0, E, B).astype(np.int64)
     w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
     mask = np.ones(h.shape[0], bool)
-    if variant == "mask":
-        mask[rng.random(h.shape[0]) < 0.3] = False
-        ew = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
-        is_score, scale = True, 1.0
-    else:
+    thr = 0.0
+    if variant == "logit":
         ew = rng.standard_normal(h.shape[0]).astype(np.float32)
         is_score, scale = False, 0.7
+    else:
+        if variant == "mask":
+            mask[rng.random(h.shape[0]) < 0.3] = False
+        else:
+            thr = 2e-3
+        ew = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+        is_score, scale = True, 1.0
+    if variant == "threshold" and engine == "sparse":
+        pytest.skip("the sparse loop's threshold is covered by the workload tests")
     cap = UNC if engine == "fused" else 9
     final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, ew, B, L, E, R, cap=cap, is_score=is_score,
-                                       scale=scale)
+                                       scale=scale, threshold=thr)
     dg = DeviceGraph(csr_dev(csr), E, R)
     wt = T(w_hops).requires_grad_(True)
     sc = T(ew).requires_grad_(True)
     mk = T(mask.astype(np.float32))
-    if engine == "fused":
-        out, _ = proof_scores(dg, T(heads), wt, sc, mask=mk, is_score=is_score, scale=scale)
+    if engine != "sparse":
+        out, _ = proof_scores(dg, T(heads), wt, sc, mask=mk, is_score=is_score, scale=scale, threshold=thr,
+                              topk_edges=cap)
         got = out.detach().cpu().numpy()
         want = np.zeros((B, E), np.float32)
         want[final[0] // E, final[0] % E] = final[1]
