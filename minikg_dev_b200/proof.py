@@ -385,7 +385,8 @@ def kernel_sparse_scores(model, heads, rels, graph, args, is_training: bool, den
         out, _ = HopLoopSum.apply(w_all, edge_scores, heads, g, mask, is_score, scale, 0.0, cap)
         return out if dense else out.to_sparse_coo().coalesce()
     if not (is_training and p_drop > 0):
-        # any cap / prune: the sparse loop fused around the op (merged outputs, written-out backward)
+        # larger caps, pruning or a graph too large for the dense state: the sparse loop fused
+        # around the op (merged outputs, written-out backward)
         from .sparse_loop import sparse_proof_scores
         out, _ = sparse_proof_scores(g, heads, w_all, edge_scores, mask, is_score, scale, topk_edges,
                                      topk_nodes, 0.0, dense=dense)
