@@ -255,3 +255,27 @@ def test_gpu_producer_deterministic():
                      model.linear.weight.grad.clone()])
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+# ------------------------------------------------------------------------------ host logic (CPU)
+def test_group_queries_csr():
+    """Distinct relations, each query's row and the per-relation query CSR (stable order)."""
+    from minikg_dev_b200.rules import group_queries
+    rels = torch.tensor([5, 2, 5, 9, 2, 2, 7, 5])
+    rel_u, query_u, qptr, qperm = group_queries(rels)
+    assert rel_u.tolist() == [2, 5, 7, 9]
+    assert query_u.tolist() == [1, 0, 1, 3, 0, 0, 2, 1]
+    assert qptr.tolist() == [0, 3, 6, 7, 8]
+    assert qperm.tolist() == [1, 4, 5, 0, 2, 7, 6, 3]
+    for u in range(rel_u.numel()):
+        members = qperm[qptr[u]:qptr[u + 1]]
+        assert (rels[members] == rel_u[u]).all()
+
+
+def test_dense_cap_routing():
+    """The fused loop takes caps 0..255 (a cap <= 0 takes no edge) and uncapped hops."""
+    from minikg_dev_b200.proof import DENSE_CAP_MAX, UNCAPPED, dense_cap
+    assert dense_cap(UNCAPPED) == UNCAPPED and dense_cap(1 << 62) == UNCAPPED
+    assert dense_cap(100) == 100 and dense_cap(DENSE_CAP_MAX) == DENSE_CAP_MAX
+    assert dense_cap(0) == 0 and dense_cap(-3) == 0
+    assert dense_cap(DENSE_CAP_MAX + 1) is None and dense_cap(1000) is None
