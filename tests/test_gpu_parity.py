@@ -860,3 +860,48 @@ def test_fused_step_graph_replay_matches_eager():
         np.testing.assert_allclose(got[0].cpu().numpy(), o2.cpu().numpy(), rtol=RTOL, atol=ATOL)
         np.testing.assert_allclose(got[1].cpu().numpy(), gw2.cpu().numpy(), rtol=1e-4, atol=1e-5)
         np.testing.assert_allclose(got[2].cpu().numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+
+
+# ----------------------------------------------------------------------------- decode candidates
+@pytest.mark.parametrize("gname", ["g1", "g2"])
+@pytest.mark.parametrize("cap", [UNC, 9])
+def test_iter_decode_candidate_batches(gname, cap):
+    """decode_core.py:394-420 on the device: per microbatch every candidate of every row, bounded
+    and ordered (score desc, tail asc); against the oracle's sum loop + bound per row."""
+    from types import SimpleNamespace
+    from minikg_dev_b200.decode import iter_decode_candidate_batches, ordered_candidates
+    g = load_golden(gname)
+    E, R = int(g["E"][0]), int(g["R"][0])
+    heads, logits, scores = g["pr_heads"], g["pr_logits"], g["pr_scores"]
+    B, K, L, n = logits.shape
+    lg = T(logits)
+    model = SimpleNamespace(rules=L, entity_count=E, relation_count=R, step=K, tau_1=1.0, weight=T(scores),
+                            dropout=torch.nn.Identity(), build_rule_logits=lambda rels: lg[rels])
+    head_t, rel_t, tail_t = T(g["head"]), T(g["rel"]), T(g["tail"])
+    mask = torch.ones(head_t.shape[0], dtype=torch.bool, device=DEV)
+    graph = SimpleNamespace(e2triple=(head_t, None, mask), triple2e=(None, tail_t, mask), r2triple=(rel_t, None, mask),
+                            mask=mask, mask_float=mask.float())
+    args = SimpleNamespace(kernel_topk_edges=cap, kernel_topk_nodes=0, decode_proof_microbatch_size=4)
+    rows = {}
+    for a, b, cand in iter_decode_candidate_batches(model, T(heads), torch.arange(B, device=DEV), graph, args):
+        assert (a, b) in [(0, 4), (4, B)]
+        rows.update({a + r: v for r, v in cand.items()})
+    csr = O.build_csr_structure(g["head"], g["tail"], g["rel"], E)
+    final, _ = O.proof_sum_forward(heads, _w_hops_from_logits(logits), csr, np.ones(g["head"].shape[0], bool), scores,
+                                   B, L, E, R, cap=cap)
+    ot, osc, oc = O.decode_topk(final, B, E, E)
+    for r in range(B):
+        tails, sc = rows.get(r, (np.zeros(0, np.int64), np.zeros(0, np.float32)))
+        assert tails.size == oc[r]
+        want = dict(zip(ot[r, : oc[r]].tolist(), osc[r, : oc[r]].tolist()))
+        assert sorted(tails.tolist()) == sorted(want)
+        np.testing.assert_allclose(sc, [want[t] for t in tails.tolist()], rtol=1e-5, atol=1e-7)
+        # decode order on the device's own scores: score descending, then tail ascending
+        assert all((sc[i] > sc[i + 1]) or (sc[i] == sc[i + 1] and tails[i] < tails[i + 1]) for i in range(sc.size - 1))
+    # a capped candidate list is the prefix of the full one
+    raw = torch.zeros((B, E), device=DEV)
+    raw[torch.from_numpy(final[0] // E), torch.from_numpy(final[0] % E)] = T(final[1])
+    full_t, full_s, full_c = ordered_candidates(raw, 0)
+    top_t, top_s, top_c = ordered_candidates(raw, 5)
+    np.testing.assert_array_equal(top_c.cpu().numpy(), np.minimum(full_c.cpu().numpy(), 5))
+    np.testing.assert_array_equal(top_t.cpu().numpy(), full_t[:, :5].cpu().numpy())
