@@ -35,6 +35,7 @@ struct ProofDims {
   int64_t B, L, E, R, n, hops, BL, BLP, nch;
   int64_t cap;      // edge cap of the capped loop, -1: uncapped
   int64_t ngroups;  // rows of the per-hop take table (capped loop)
+  int64_t tblp;     // take-table row stride: BLP rounded up to 256 columns
 };
 
 inline ProofDims proof_dims(const mkg_proof_params& p) {
@@ -46,6 +47,7 @@ inline ProofDims proof_dims(const mkg_proof_params& p) {
   const bool capped = p.topk_edges < (int64_t(1) << 60) && p.cap_index != nullptr;
   d.cap = capped ? p.topk_edges : -1;
   d.ngroups = capped ? p.cap_index->num_groups : 0;
+  d.tblp = (d.BLP + 255) / 256 * 256;
   return d;
 }
 
@@ -74,7 +76,7 @@ ProofLayout proof_layout(const ProofDims& q) {
   L.dwt = o; o += a256(4 * (size_t)q.n * q.BLP);
   L.queue = o; o += a256(4 * (size_t)(2 * q.hops * q.nch * kQueueStride));
   L.msgs = o; o += a256(8 * (size_t)(q.hops + 1));
-  L.take = o; o += a256((size_t)q.hops * q.ngroups * q.BLP);
+  L.take = o; o += a256((size_t)q.hops * q.ngroups * q.tblp);
   L.total = o;
   return L;
 }
@@ -97,8 +99,9 @@ struct Slab {
   float* dwt() const { return reinterpret_cast<float*>(base + lay.dwt); }
   int32_t* queue() const { return reinterpret_cast<int32_t*>(base + lay.queue); }
   int64_t* msgs() const { return reinterpret_cast<int64_t*>(base + lay.msgs); }
-  // edge-cap take table of hop h: [ngroups][BLP] edges taken per (capped group, column)
-  uint8_t* take(int64_t h) const { return reinterpret_cast<uint8_t*>(base + lay.take) + h * q.ngroups * q.BLP; }
+  // edge-cap take table of hop h: [ngroups][tblp] edges taken per (capped group, column), columns
+  // permuted within each 256-column tile (take_offset)
+  uint8_t* take(int64_t h) const { return reinterpret_cast<uint8_t*>(base + lay.take) + h * q.ngroups * q.tblp; }
 };
 
 // ------------------------------------------------------------------ setup kernels
@@ -234,6 +237,19 @@ __device__ __forceinline__ void load_lanes(Lanes<VEC>& out, const float* __restr
 // take[row of group][c] = edges taken (its first ones in CSR order).  Block = (slot, tile of
 // kTakeCols columns), one thread per column; the buckets of up to kTakeGroups groups are
 // computed once into shared memory ([group][column] bytes), longer rows re-read the weights.
+// Byte offset of column c inside a take-table row.  Within each 256-column tile the 8 columns a
+// forward lane covers (c = 4 lane + i and 128 + 4 lane + i, i < 4) are contiguous: lane l's bytes
+// are [8 l, 8 l + 8), the first 4 for the lower 128 columns.  A forward lane reads its take bytes
+// with one 8-byte load, a backward lane (128-column chunks) with one 4-byte load.
+__host__ __device__ __forceinline__ int64_t take_offset(int64_t c) {
+  const int64_t w = c & 255;
+  return (c - w) + ((w & 127) >> 2) * 8 + (w >> 7) * 4 + (w & 3);
+}
+// first byte of the 4 take bytes of 128-column chunk `chunk`, lane `lane`
+__device__ __forceinline__ int64_t take_lane_offset(int64_t chunk, int lane) {
+  return (chunk >> 1) * 256 + lane * 8 + (chunk & 1) * 4;
+}
+
 constexpr int kTakeCols = 256;
 constexpr int kTakeGroups = 96;
 constexpr int kTakeHist = 32;  // bucket ranges narrower than this are counted in one pass
@@ -325,7 +341,7 @@ __global__ void __launch_bounds__(kTakeCols) cap_take_kernel(
     }
     const int remain = static_cast<int>(q.cap) - before;
     int prior = 0;
-    uint8_t* out = take + (int64_t)slot_group[slot] * q.BLP + c;
+    uint8_t* out = take + (int64_t)slot_group[slot] * q.tblp + take_offset(c);
     for (int g = 0; g < G; ++g) {
       const int b = bucket(g);
       const int cnt = count(g);
@@ -337,16 +353,12 @@ __global__ void __launch_bounds__(kTakeCols) cap_take_kernel(
         t = t < 0 ? 0 : (t > cnt ? cnt : t);
         prior += cnt;
       }
-      out[(int64_t)g * q.BLP] = static_cast<uint8_t>(t);
+      out[(int64_t)g * q.tblp] = static_cast<uint8_t>(t);
     }
   }
 }
 
-// The take word (4 columns) of a capped record, or all-taken (0xFFFFFFFF with position 0) for
-// a record of an uncapped row.
-__device__ __forceinline__ unsigned take_word(const uint8_t* __restrict__ take, int2 rc, int64_t c, int64_t BLP) {
-  return rc.x >= 0 ? __ldg(reinterpret_cast<const unsigned*>(take + (int64_t)rc.x * BLP + c)) : 0xFFFFFFFFu;
-}
+// A record of an uncapped row reads as all-taken (0xFFFFFFFF with position 0).
 __device__ __forceinline__ float4 cap_masked(float4 v, unsigned t4, int pos) {
   const unsigned p = static_cast<unsigned>(pos);
   v.x = (t4 & 0xffu) > p ? v.x : 0.0f;
@@ -433,9 +445,16 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
             if (CAP) {
               const int2 cr = rcs[warp][k0 + u];
               tp[u] = cr.x >= 0 ? cr.y : 0;
-#pragma unroll
-              for (int k = 0; k < VEC; ++k)
-                tw[u][k] = (col + 128 * k < q.BLP) ? take_word(take, cr, col + 128 * k, q.BLP) : 0u;
+              const uint8_t* tr = take + (int64_t)(cr.x >= 0 ? cr.x : 0) * q.tblp;
+              if (VEC == 2) {
+                const uint2 t8 = cr.x >= 0 ? __ldg(reinterpret_cast<const uint2*>(tr + chunk * 256 + lane * 8))
+                                           : make_uint2(0xFFFFFFFFu, 0xFFFFFFFFu);
+                tw[u][0] = t8.x;
+                tw[u][VEC - 1] = t8.y;
+              } else {
+                tw[u][0] = cr.x >= 0 ? __ldg(reinterpret_cast<const unsigned*>(tr + take_lane_offset(chunk, lane)))
+                                     : 0xFFFFFFFFu;
+              }
             }
           }
         }
@@ -982,7 +1001,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
 #pragma unroll
             for (int u = 0; u < kBatch; ++u) {
               const int2 cr = make_int2(__shfl_sync(0xffffffffu, rc.x, src[u]), __shfl_sync(0xffffffffu, rc.y, src[u]));
-              tw[u] = (ok[u] && colok) ? take_word(take, cr, col, q.BLP) : 0xFFFFFFFFu;
+              tw[u] = (ok[u] && colok && cr.x >= 0)
+                          ? __ldg(reinterpret_cast<const unsigned*>(take + (int64_t)cr.x * q.tblp +
+                                                                    take_lane_offset(chunk, lane)))
+                          : 0xFFFFFFFFu;
               tp[u] = cr.x >= 0 ? cr.y : 0;
             }
 #pragma unroll
