@@ -358,13 +358,15 @@ __global__ void __launch_bounds__(kTakeCols) cap_take_kernel(
   }
 }
 
-// A record of an uncapped row reads as all-taken (0xFFFFFFFF with position 0).
+// Keeps the columns of v whose take byte in t4 exceeds the record's position in its group
+// (one SIMD byte compare; a position >= 255 is never taken since takes are at most 255).
 __device__ __forceinline__ float4 cap_masked(float4 v, unsigned t4, int pos) {
-  const unsigned p = static_cast<unsigned>(pos);
-  v.x = (t4 & 0xffu) > p ? v.x : 0.0f;
-  v.y = ((t4 >> 8) & 0xffu) > p ? v.y : 0.0f;
-  v.z = ((t4 >> 16) & 0xffu) > p ? v.z : 0.0f;
-  v.w = (t4 >> 24) > p ? v.w : 0.0f;
+  const unsigned p = pos < 255 ? static_cast<unsigned>(pos) : 255u;
+  const unsigned m = __vcmpgtu4(t4, p * 0x01010101u);  // 0xff in every byte where take > pos
+  v.x = __int_as_float(__float_as_int(v.x) & static_cast<int>(__byte_perm(m, 0, 0x0000)));
+  v.y = __int_as_float(__float_as_int(v.y) & static_cast<int>(__byte_perm(m, 0, 0x1111)));
+  v.z = __int_as_float(__float_as_int(v.z) & static_cast<int>(__byte_perm(m, 0, 0x2222)));
+  v.w = __int_as_float(__float_as_int(v.w) & static_cast<int>(__byte_perm(m, 0, 0x3333)));
   return v;
 }
 
@@ -444,7 +446,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
             load_lanes(xv[u], x + (int64_t)r[u].x * q.BLP, col, q.BLP);
             if (CAP) {
               const int2 cr = rcs[warp][k0 + u];
-              tp[u] = cr.x >= 0 ? cr.y : 0;
+              tp[u] = cr.x >= 0 ? cr.y : -1;  // -1: a record of an uncapped row
               const uint8_t* tr = take + (int64_t)(cr.x >= 0 ? cr.x : 0) * q.tblp;
               if (VEC == 2) {
                 const uint2 t8 = cr.x >= 0 ? __ldg(reinterpret_cast<const uint2*>(tr + chunk * 256 + lane * 8))
@@ -462,7 +464,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           if (r[u].y < 0) continue;
-          if (CAP) {
+          if (CAP && tp[u] >= 0) {  // uniform over the warp (one record)
 #pragma unroll
             for (int k = 0; k < VEC; ++k) xv[u].v[k] = cap_masked(xv[u].v[k], tw[u][k], tp[u]);
           }
@@ -1005,10 +1007,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
                           ? __ldg(reinterpret_cast<const unsigned*>(take + (int64_t)cr.x * q.tblp +
                                                                     take_lane_offset(chunk, lane)))
                           : 0xFFFFFFFFu;
-              tp[u] = cr.x >= 0 ? cr.y : 0;
+              tp[u] = cr.x >= 0 ? cr.y : -1;  // -1: a record of an uncapped row
             }
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u) gv[u] = cap_masked(gv[u], tw[u], tp[u]);
+            for (int u = 0; u < kBatch; ++u)
+              if (tp[u] >= 0) gv[u] = cap_masked(gv[u], tw[u], tp[u]);  // uniform over the warp
           }
           float ep[kBatch];
 #pragma unroll
