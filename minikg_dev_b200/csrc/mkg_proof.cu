@@ -237,6 +237,8 @@ __device__ __forceinline__ void load_lanes(Lanes<VEC>& out, const float* __restr
 // take[row of group][c] = edges taken (its first ones in CSR order).  Block = (slot, tile of
 // kTakeCols columns), one thread per column; the buckets of up to kTakeGroups groups are
 // computed once into shared memory ([group][column] bytes), longer rows re-read the weights.
+// The threshold is found with two histogram passes over the groups (16 coarse bins, then the 16
+// buckets of the coarse bin that holds it), whatever the range of the buckets.
 // Byte offset of column c inside a take-table row.  Within each 256-column tile the 8 columns a
 // forward lane covers (c = 4 lane + i and 128 + 4 lane + i, i < 4) are contiguous: lane l's bytes
 // are [8 l, 8 l + 8), the first 4 for the lower 128 columns.  A forward lane reads its take bytes
@@ -252,32 +254,38 @@ __device__ __forceinline__ int64_t take_lane_offset(int64_t chunk, int lane) {
 
 constexpr int kTakeCols = 256;
 constexpr int kTakeGroups = 96;
-constexpr int kTakeHist = 32;  // bucket ranges narrower than this are counted in one pass
+constexpr int kTakeBins = 16;  // the 256 buckets searched as 16 coarse bins of 16 buckets each
+
+// h += n, saturated at 0xffff.  Exact for the searches below: they compare running sums against
+// cap <= 255 and stop at the first bin that reaches it, so only bins below cap are ever added up.
+__device__ __forceinline__ void add_saturated(uint16_t& h, int n) {
+  const int v = h + n;
+  h = static_cast<uint16_t>(v < 0xffff ? v : 0xffff);
+}
 
 __global__ void __launch_bounds__(kTakeCols) cap_take_kernel(
     DirCSR ori, DirCSR inv, const int32_t* __restrict__ slot_entity, const int32_t* __restrict__ slot_dir,
     const int32_t* __restrict__ slot_group, int64_t num_slots, ProofDims q, const float* __restrict__ wt,
     const uint8_t* __restrict__ act, uint8_t* __restrict__ take, unsigned* err) {
   __shared__ uint8_t bk[kTakeGroups * kTakeCols];     // [group][column] buckets
-  __shared__ uint16_t hist[kTakeHist * kTakeCols];    // [bucket - lowest][column] edges
+  __shared__ uint16_t hist[kTakeBins * kTakeCols];    // [bin][column] edges, coarse then fine level
   __shared__ int32_t gcnt[kTakeGroups];               // group edge counts, clamped at 255
   __shared__ int32_t grel[kTakeGroups];
   const int tid = threadIdx.x;
   const int64_t tiles = (q.BLP + kTakeCols - 1) / kTakeCols;
+  uint16_t* hcol = hist + tid;  // this column's bins, kTakeCols apart
   for (int64_t blk = blockIdx.x; blk < num_slots * tiles; blk += gridDim.x) {
     const int64_t slot = blk / tiles;
     const int64_t c = (blk % tiles) * kTakeCols + tid;
     const int dir = slot_dir[slot];
     const DirCSR d = dir == 0 ? ori : inv;
     const int64_t e = slot_entity[slot];
-    // takes are read only where the sending row holds state (the pulls skip inactive chunks)
-    const int64_t ch0 = (blk % tiles) * (kTakeCols / kChunk);
-    bool tile_active = false;
-    for (int64_t k = ch0; k < ch0 + kTakeCols / kChunk && k < q.nch; ++k) tile_active = tile_active || act[e * q.nch + k];
-    if (!tile_active) continue;  // uniform over the block
-    const bool col_active = c < q.BLP && act[e * q.nch + c / kChunk] != 0;
     const int64_t g0 = d.group_ptr[e];
     const int G = static_cast<int>(d.group_ptr[e + 1] - g0);
+    // only columns the pulls can read: the sending row's chunk holds state (inactive chunks are
+    // skipped there)
+    const bool col_active = c < q.BLP && act[e * q.nch + c / kChunk] != 0;
+    if (!__syncthreads_or(col_active)) continue;  // uniform over the block
     const bool staged = G <= kTakeGroups;
     const float* w = wt + (dir == 0 ? 0 : q.R) * q.BLP + (c < q.BLP ? c : 0);
     // a relation outside [0, R) is flagged and counts as bucket 0
@@ -296,6 +304,7 @@ __global__ void __launch_bounds__(kTakeCols) cap_take_kernel(
       }
     }
     __syncthreads();
+    if (!col_active) continue;
     // Counts are clamped at 255: every comparison below is against cap <= 255, and a group
     // counted before the threshold holds fewer than cap edges, so no decision changes.
     auto count = [&](int g) -> int {
@@ -304,56 +313,48 @@ __global__ void __launch_bounds__(kTakeCols) cap_take_kernel(
       return cnt < 255 ? cnt : 255;
     };
     auto bucket = [&](int g) -> int { return staged ? bk[g * kTakeCols + tid] : bucket_at(rel_of(g)); };
-    int bmin = kNumBuckets - 1, bmax = 0;
+    // tb: the largest bucket whose groups at or above it hold >= cap edges (a capped row holds
+    // more than cap); above: the edges of the groups above tb.  Coarse level: buckets >> 4.
+#pragma unroll
+    for (int k = 0; k < kTakeBins; ++k) hcol[k * kTakeCols] = 0;
 #pragma unroll 4
     for (int g = 0; g < G; ++g) {
       const int b = staged ? bucket_at(grel[g]) : bucket_at(rel_of(g));
       if (staged) bk[g * kTakeCols + tid] = static_cast<uint8_t>(b);
-      bmin = b < bmin ? b : bmin;
-      bmax = b > bmax ? b : bmax;
+      add_saturated(hcol[(b >> 4) * kTakeCols], count(g));
     }
-    if (!col_active) continue;
-    // tb: the largest bucket whose groups at or above it hold >= cap edges (a capped row holds
-    // more than cap, so tb >= bmin); before: the edges of the groups above tb
-    int tb = bmin, before = 0;
-    if (bmax - bmin < kTakeHist) {
-      for (int k = 0; k <= bmax - bmin; ++k) hist[k * kTakeCols + tid] = 0;
-      for (int g = 0; g < G; ++g) hist[(bucket(g) - bmin) * kTakeCols + tid] += static_cast<uint16_t>(count(g));
-      int cum = 0;
-      for (int k = bmax - bmin; k >= 0; --k) {
-        const int h = hist[k * kTakeCols + tid];
-        if (cum + h >= q.cap) { tb = bmin + k; before = cum; break; }
-        cum += h;
-      }
-    } else {
-      auto above = [&](int b) {
-        int n = 0;
-        for (int g = 0; g < G; ++g) n += bucket(g) >= b ? count(g) : 0;
-        return n;
-      };
-      int lo = bmin, hi = bmax;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (above(mid) >= q.cap) lo = mid; else hi = mid - 1;
-      }
-      tb = lo;
-      before = tb < bmax ? above(tb + 1) : 0;
+    int above = 0, cb = 0;
+    for (int k = kTakeBins - 1; k >= 0; --k) {
+      const int h = hcol[k * kTakeCols];
+      if (above + h >= q.cap || k == 0) { cb = k; break; }
+      above += h;
     }
-    const int remain = static_cast<int>(q.cap) - before;
-    int prior = 0;
-    uint8_t* out = take + (int64_t)slot_group[slot] * q.tblp + take_offset(c);
+    // fine level: the buckets of coarse bin cb
+#pragma unroll
+    for (int k = 0; k < kTakeBins; ++k) hcol[k * kTakeCols] = 0;
     for (int g = 0; g < G; ++g) {
       const int b = bucket(g);
+      if ((b >> 4) == cb) add_saturated(hcol[(b & 15) * kTakeCols], count(g));
+    }
+    int tb = cb * kTakeBins;
+    for (int k = kTakeBins - 1; k >= 0; --k) {
+      const int h = hcol[k * kTakeCols];
+      if (above + h >= q.cap || k == 0) { tb = cb * kTakeBins + k; break; }
+      above += h;
+    }
+    const int remain = static_cast<int>(q.cap) - above;
+    int prior = 0;
+    uint8_t* out = take + (int64_t)slot_group[slot] * q.tblp + take_offset(c);
+    for (int g = 0; g < G; ++g, out += q.tblp) {
+      const int b = bucket(g);
       const int cnt = count(g);
-      int t = 0;
-      if (b > tb) {
-        t = cnt;
-      } else if (b == tb) {
+      int t = b > tb ? cnt : 0;
+      if (b == tb) {
         t = remain - prior;
         t = t < 0 ? 0 : (t > cnt ? cnt : t);
         prior += cnt;
       }
-      out[(int64_t)g * q.tblp] = static_cast<uint8_t>(t);
+      *out = static_cast<uint8_t>(t);
     }
   }
 }
