@@ -778,61 +778,79 @@ __global__ void rows_to_queries_kernel(const float* __restrict__ x, const float*
 // ------------------------------------------------------------------ backward
 // Seed: dX_K[e][c] = G[b][e] where X_K[e][c] != 0 (the reference's sparse result carries
 // gradient only on its keys), and S[c] = sum_e dX_K[e][c] * Y_{K-1}[e][c].
-constexpr int kSeedTiles = 8;   // 32-entity tiles per block of seed_grad_kernel
+constexpr int kSeedTiles = 4;   // 32-entity tiles per block of seed_grad_kernel
 constexpr int kSeedMaxL = 16;   // rules whose column partials fit the block's shared memory
+constexpr int kSeedBatch = 4;   // float4s whose loads a thread issues together
 
-__global__ void seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
-                                 const float* __restrict__ ylast, ProofDims q, float* __restrict__ dx,
-                                 float* __restrict__ s) {
-  __shared__ float tile[32][33];
+// Block = 32 queries (the contiguous columns [32 L by, 32 L (by + 1)) of every row, 16-byte
+// aligned since BLP is a multiple of 4) x kSeedTiles tiles of 32 entities.  The G tile goes
+// through shared memory; X_K, Y_{K-1} and dX_K are then streamed row by row in float4s, so
+// every load and store of the slabs is coalesced.  A float4 that reaches past B L covers
+// padding columns, which hold zeros in X_K and get zeros in dX_K.
+__global__ void __launch_bounds__(256) seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
+                                                       const float* __restrict__ ylast, ProofDims q,
+                                                       float* __restrict__ dx, float* __restrict__ s) {
+  __shared__ float tile[32][33];          // [query][entity] of G
   __shared__ float part[32 * kSeedMaxL];  // this block's share of S for its 32 queries
+  const int tid = threadIdx.x;
   const int64_t b0 = blockIdx.y * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  const bool local = q.L <= kSeedMaxL;
-  for (int i = ty * 32 + tx; i < 32 * kSeedMaxL; i += 256) part[i] = 0.0f;
-  __syncthreads();
+  const int nb = static_cast<int>(q.B - b0 < 32 ? q.B - b0 : 32);
+  const int L = static_cast<int>(q.L);
+  const int64_t c0 = b0 * L;
+  const int width = nb * L;             // columns of the block's queries
+  const int nf4 = (width + 3) / 4;      // float4s per row (the last may reach into padding)
+  const bool local = L <= kSeedMaxL;
+  for (int i = tid; i < 32 * kSeedMaxL; i += 256) part[i] = 0.0f;
   for (int t = 0; t < kSeedTiles; ++t) {
     const int64_t e0 = ((int64_t)blockIdx.x * kSeedTiles + t) * 32;
     if (e0 >= q.E) break;
-    for (int r = ty; r < 32; r += 8) {
-      const int64_t b = b0 + r, e = e0 + tx;
-      tile[r][tx] = (b < q.B && e < q.E) ? g[b * q.E + e] : 0.0f;
+    const int rows = static_cast<int>(q.E - e0 < 32 ? q.E - e0 : 32);
+    __syncthreads();  // the previous tile is consumed (and part is zeroed)
+    for (int i = tid; i < 32 * 32; i += 256) {
+      const int b = i >> 5, e = i & 31;
+      tile[b][e] = (b < nb && e < rows) ? g[(b0 + b) * q.E + e0 + e] : 0.0f;
     }
     __syncthreads();
-    for (int r = ty; r < 32; r += 8) {
-      const int64_t e = e0 + r, b = b0 + tx;
-      if (e >= q.E || b >= q.B) continue;
-      const float gv = tile[tx][r];
-      for (int64_t l = 0; l < q.L; ++l) {
-        const int64_t c = b * q.L + l;
-        const float xv = xk[e * q.BLP + c];
-        const float dv = xv != 0.0f ? gv : 0.0f;
-        dx[e * q.BLP + c] = dv;
-        if (dv != 0.0f) {
-          const float contrib = dv * ylast[e * q.BLP + c];
-          if (local) atomicAdd(part + tx * q.L + l, contrib);
-          else atomicAdd(s + c, contrib);
+    const int n = rows * nf4;
+    for (int i0 = tid; i0 < n; i0 += 256 * kSeedBatch) {
+      float4 xv[kSeedBatch], yv[kSeedBatch];
+#pragma unroll
+      for (int u = 0; u < kSeedBatch; ++u) {
+        const int i = i0 + u * 256;
+        if (i < n) {
+          const int64_t off = (e0 + i / nf4) * q.BLP + c0 + 4 * (i % nf4);
+          xv[u] = *reinterpret_cast<const float4*>(xk + off);
+          yv[u] = *reinterpret_cast<const float4*>(ylast + off);
         }
       }
+#pragma unroll
+      for (int u = 0; u < kSeedBatch; ++u) {
+        const int i = i0 + u * 256;
+        if (i >= n) break;
+        const int r = i / nf4, j0 = 4 * (i % nf4);
+        const float xs[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+        const float ys[4] = {yv[u].x, yv[u].y, yv[u].z, yv[u].w};
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = j0 + k;
+          float dv = 0.0f;
+          if (j < width && xs[k] != 0.0f) dv = tile[j / L][r];
+          o[k] = dv;
+          if (dv != 0.0f) {
+            const float contrib = dv * ys[k];
+            if (local) atomicAdd(part + j, contrib);
+            else atomicAdd(s + c0 + j, contrib);
+          }
+        }
+        *reinterpret_cast<float4*>(dx + (e0 + r) * q.BLP + c0 + j0) = make_float4(o[0], o[1], o[2], o[3]);
+      }
     }
-    __syncthreads();
   }
   if (local) {
-    for (int i = ty * 32 + tx; i < 32 * q.L; i += 256) {
-      const int64_t b = b0 + i / q.L;
-      if (b < q.B && part[i] != 0.0f) atomicAdd(s + b0 * q.L + i, part[i]);
-    }
-  }
-}
-
-// Zero the padding columns of a slab that seed_grad_kernel does not write.
-__global__ void zero_pad_columns_kernel(float* __restrict__ slab, ProofDims q) {
-  const int64_t pad = q.BLP - q.BL;
-  if (pad <= 0) return;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < q.E * pad;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t e = i / pad, k = i % pad;
-    slab[e * q.BLP + q.BL + k] = 0.0f;
+    __syncthreads();
+    for (int j = tid; j < width; j += 256)
+      if (part[j] != 0.0f) atomicAdd(s + c0 + j, part[j]);
   }
 }
 
@@ -1368,10 +1386,8 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
   MKG_CUDA(cudaMemsetAsync(S.queue() + q.hops * q.nch * kQueueStride, 0, 4 * (size_t)(q.hops * q.nch * kQueueStride), st));
   float* dx_cur = S.dxa();
   float* dx_next = S.dxb();
-  zero_pad_columns_kernel<<<pb, 256, 0, st>>>(dx_cur, q);
-  MKG_LAUNCHED("zero_pad_columns_kernel");
   dim3 sgrid((unsigned)((q.E + 32 * kSeedTiles - 1) / (32 * kSeedTiles)), (unsigned)((q.B + 31) / 32));
-  seed_grad_kernel<<<sgrid, dim3(32, 8), 0, st>>>(grad_out, S.x(q.hops), S.y(q.hops - 1), q, dx_cur, S.s(q.hops - 1));
+  seed_grad_kernel<<<sgrid, 256, 0, st>>>(grad_out, S.x(q.hops), S.y(q.hops - 1), q, dx_cur, S.s(q.hops - 1));
   MKG_LAUNCHED("seed_grad_kernel");
   const size_t sm = bwd_smem(q);
   const mkg_cap_index* ix = q.cap >= 0 ? p->cap_index : nullptr;
