@@ -125,12 +125,17 @@ class ProofRunner:
         return grad_w, (grad_edge if want_edge_grad else None)
 
     def capture(self, heads, w_hops, out, msgs, grad_out, edge_scores, grad_w, grad_edge=None, mask=None,
-                is_score: bool = True, scale: float = 1.0) -> "torch.cuda.CUDAGraph":
+                is_score: bool = True, scale: float = 1.0, host_inputs=(), host_outputs=()) -> "torch.cuda.CUDAGraph":
         """One training step (edge-factor refresh, forward, backward) captured as a CUDA graph
         over these buffers.  Write new inputs into ``heads`` / ``w_hops`` / ``edge_scores`` /
         ``grad_out`` (and ``mask``) in place, then ``graph.replay()`` reruns the step with no
         host work; results land in ``out``, ``msgs``, ``grad_w``, ``grad_edge``.  The library
-        does no host synchronisation inside a step, so the whole step is capturable."""
+        does no host synchronisation inside a step, so the whole step is capturable.
+
+        ``host_inputs``: (device tensor, pinned host tensor) pairs copied host to device at the
+        start of every replay, so new inputs can be written into the host tensors instead;
+        ``host_outputs``: (pinned host tensor, device tensor) pairs copied device to host at its
+        end (read them after a synchronisation of the replaying stream)."""
         dev = self.graph.device
         for name, t, dt in (("heads", heads, torch.int64), ("w_hops", w_hops, torch.float32),
                             ("out", out, torch.float32), ("msgs", msgs, torch.int64),
@@ -138,12 +143,24 @@ class ProofRunner:
                             ("grad_w", grad_w, torch.float32)):
             if t.device != dev or t.dtype != dt or not t.is_contiguous():
                 raise ValueError(f"capture: {name} must be a contiguous {dt} tensor on {dev}")
+        host_inputs, host_outputs = list(host_inputs), list(host_outputs)
+        for kind, pairs, d_at in (("host_inputs", host_inputs, 0), ("host_outputs", host_outputs, 1)):
+            for pair in pairs:
+                d, h = pair[d_at], pair[1 - d_at]
+                if (d.device != dev or h.device.type != "cpu" or not h.is_pinned() or d.dtype != h.dtype
+                        or d.shape != h.shape or not d.is_contiguous() or not h.is_contiguous()):
+                    raise ValueError(f"capture: {kind} pairs a contiguous tensor on {dev} with a pinned "
+                                     "host tensor of the same shape and dtype")
         want_edge = grad_edge is not None
 
         def step():
+            for d, h in host_inputs:
+                d.copy_(h, non_blocking=True)
             self.graph.set_edge_factor(mask, edge_scores, is_score, scale)
             self.forward(heads, w_hops, out, msgs)
             self.backward(grad_out, mask, edge_scores, is_score, scale, want_edge, grad_w, grad_edge)
+            for h, d in host_outputs:
+                h.copy_(d, non_blocking=True)
 
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))

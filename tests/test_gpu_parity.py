@@ -862,6 +862,56 @@ def test_fused_step_graph_replay_matches_eager():
         np.testing.assert_allclose(got[2].cpu().numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
 
 
+def test_fused_step_graph_host_copies():
+    """ProofRunner.capture with host_inputs / host_outputs: inputs written into the pinned host
+    tensors reach the replay, results land in the pinned host outputs and equal the eager step;
+    a host tensor that is not pinned is refused."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import ProofRunner
+    h, r, t, E, R = GRAPHS["g2"]
+    csr = O.build_csr_structure(h, t, r, E)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    rng = np.random.default_rng(22)
+    B, L, K, n = 5, 2, 3, 2 * R + 1
+    runner = ProofRunner(dg, B, L, K)
+
+    def draw():
+        return (torch.from_numpy(rng.integers(0, E, B).astype(np.int64)),
+                torch.from_numpy(np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32)
+                                           for _ in range(K)])),
+                torch.from_numpy(rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)))
+
+    hh, wh, sh = (x.pin_memory() for x in draw())
+    heads, w_hops, sc = hh.to(DEV), wh.to(DEV), sh.to(DEV)
+    G = T(rng.standard_normal((B, E)).astype(np.float32))
+    out = torch.empty((B, E), device=DEV)
+    msgs = torch.zeros(K, dtype=torch.int64, device=DEV)
+    gw = torch.empty((K, B, L, n), device=DEV)
+    ge = torch.empty(h.shape[0], device=DEV)
+    mh = torch.empty(K, dtype=torch.int64).pin_memory()
+    gwh = torch.empty((K, B, L, n)).pin_memory()
+    geh = torch.empty(h.shape[0]).pin_memory()
+    with pytest.raises(ValueError, match="pinned"):
+        runner.capture(heads, w_hops, out, msgs, G, sc, gw, ge, host_inputs=[(heads, torch.zeros(B, dtype=torch.int64))])
+    graph = runner.capture(heads, w_hops, out, msgs, G, sc, gw, ge,
+                           host_inputs=[(heads, hh), (w_hops, wh), (sc, sh)],
+                           host_outputs=[(mh, msgs), (gwh, gw), (geh, ge)])
+    for trial in range(2):
+        if trial == 1:  # new inputs in the host tensors only
+            for dst, src in zip((hh, wh, sh), draw()):
+                dst.copy_(src)
+        graph.replay()
+        torch.cuda.synchronize()
+        got = (mh.clone(), gwh.clone(), geh.clone())
+        heads2, w2, sc2 = hh.to(DEV), wh.to(DEV), sh.to(DEV)
+        dg.set_edge_factor(None, sc2, True, 1.0)
+        _, m2 = runner.forward(heads2, w2)
+        gw2, ge2 = runner.backward(G, None, sc2, True, 1.0, True)
+        assert torch.equal(got[0], m2.cpu())
+        np.testing.assert_allclose(got[1].numpy(), gw2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(got[2].numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+
+
 # ----------------------------------------------------------------------------- decode candidates
 @pytest.mark.parametrize("gname", ["g1", "g2"])
 @pytest.mark.parametrize("cap", [UNC, 9])
