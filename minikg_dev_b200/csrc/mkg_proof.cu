@@ -856,32 +856,58 @@ __global__ void __launch_bounds__(256) seed_grad_kernel(const float* __restrict_
 
 // Gradient of x = (y / d) * min(d, 1) with d = column sum of y (only y != 0 entries):
 // dy = dx * (c / d) + S * coef, coef = -1 / d^2 when d > 1 and 0 when d <= 1 (where
-// min(d, 1) = d and the two terms cancel).
-__global__ void normalize_mass_backward_kernel(const float* __restrict__ dx, const float* __restrict__ y,
-                                               const float* __restrict__ dsum, const float* __restrict__ s,
-                                               ProofDims q, float* __restrict__ dy) {
-  const int64_t n4 = q.E * q.BLP / 4;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t col = (i * 4) % q.BLP;
-    const float4 g = reinterpret_cast<const float4*>(dx)[i];
-    const float4 v = reinterpret_cast<const float4*>(y)[i];
-    const float4 d = *reinterpret_cast<const float4*>(dsum + col);
-    const float4 sv = *reinterpret_cast<const float4*>(s + col);
-    float gi[4] = {g.x, g.y, g.z, g.w}, vi[4] = {v.x, v.y, v.z, v.w};
-    float di[4] = {d.x, d.y, d.z, d.w}, si[4] = {sv.x, sv.y, sv.z, sv.w}, o[4];
+// min(d, 1) = d and the two terms cancel).  A warp takes kNbTasks (row, 128-column chunk)
+// tasks at a time and skips the chunks where Y_h is zero (yact): dY is zero there, and the
+// backward pull reads dY only in chunks whose yact is set, so those chunks are not written.
+constexpr int kNbTasks = 4;
+
+__global__ void __launch_bounds__(256, 4) normalize_mass_backward_kernel(
+    const float* __restrict__ dx, const float* __restrict__ y, const float* __restrict__ dsum,
+    const float* __restrict__ s, const uint8_t* __restrict__ yact, ProofDims q, float* __restrict__ dy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t total = q.E * q.nch;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t t0 = warp0 * kNbTasks; t0 < total; t0 += nwarps * kNbTasks) {
+    const int64_t row0 = t0 / q.nch, chunk0 = t0 % q.nch;
+    bool on[kNbTasks];
+    float4 g[kNbTasks], v[kNbTasks];
+    {
+      int64_t row = row0, chunk = chunk0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float r = 0.0f;
-      if (vi[k] != 0.0f) {
-        const float dd = di[k];
-        const float c = fminf(dd, 1.0f);
-        const float coef = dd <= 1.0f ? 0.0f : -__fdiv_rn(1.0f, dd * dd);
-        r = gi[k] * __fdiv_rn(c, dd) + si[k] * coef;
+      for (int u = 0; u < kNbTasks; ++u) {
+        const int64_t col = chunk * kChunk + 4 * lane;
+        on[u] = t0 + u < total && col < q.BLP && yact[t0 + u] != 0;
+        g[u] = on[u] ? *reinterpret_cast<const float4*>(dx + row * q.BLP + col) : zero;
+        v[u] = on[u] ? *reinterpret_cast<const float4*>(y + row * q.BLP + col) : zero;
+        if (++chunk == q.nch) { chunk = 0; ++row; }
       }
-      o[k] = r;
     }
-    reinterpret_cast<float4*>(dy)[i] = make_float4(o[0], o[1], o[2], o[3]);
+    int64_t row = row0, chunk = chunk0;
+#pragma unroll
+    for (int u = 0; u < kNbTasks; ++u) {
+      const int64_t col = chunk * kChunk + 4 * lane;
+      if (on[u]) {
+        const float4 d = *reinterpret_cast<const float4*>(dsum + col);
+        const float4 sv = *reinterpret_cast<const float4*>(s + col);
+        float gi[4] = {g[u].x, g[u].y, g[u].z, g[u].w}, vi[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        float di[4] = {d.x, d.y, d.z, d.w}, si[4] = {sv.x, sv.y, sv.z, sv.w}, o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float r = 0.0f;
+          if (vi[k] != 0.0f) {
+            const float dd = di[k];
+            const float c = fminf(dd, 1.0f);
+            const float coef = dd <= 1.0f ? 0.0f : -__fdiv_rn(1.0f, dd * dd);
+            r = gi[k] * __fdiv_rn(c, dd) + si[k] * coef;
+          }
+          o[k] = r;
+        }
+        *reinterpret_cast<float4*>(dy + row * q.BLP + col) = make_float4(o[0], o[1], o[2], o[3]);
+      }
+      if (++chunk == q.nch) { chunk = 0; ++row; }
+    }
   }
 }
 
@@ -957,7 +983,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
     float4 gx = zero;
     if (active) {
       const float4 xr = colok ? *reinterpret_cast<const float4*>(x + row * q.BLP + col) : zero;
-      if ((tk.w & kTaskFirst) && colok) {
+      if ((tk.w & kTaskFirst) && colok && yact[row * q.nch + chunk] != 0) {  // dY_h[row] is zero elsewhere
         const float4 ds = *reinterpret_cast<const float4*>(dy + row * q.BLP + col);
         const float4 wi = wload(q.n - 1);
         gx = f4_mul(ds, wi);
@@ -1401,8 +1427,7 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
                                         (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / q.nch) + 1);
   for (int64_t h = q.hops - 1; h >= 0; --h) {
     // dY_h from dX_{h+1}
-    normalize_mass_backward_kernel<<<grid_for(q.E * q.BLP / 4, 256, pb * 2), 256, 0, st>>>(
-        dx_cur, S.y(h), S.d(h), S.s(h), q, S.dy());
+    normalize_mass_backward_kernel<<<pb, 256, 0, st>>>(dx_cur, S.y(h), S.d(h), S.s(h), S.yact(h), q, S.dy());
     MKG_LAUNCHED("normalize_mass_backward_kernel");
     MKG_CUDA(cudaMemsetAsync(S.dwt(), 0, 4 * (size_t)q.n * q.BLP, st));
     zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, q, dx_next);
