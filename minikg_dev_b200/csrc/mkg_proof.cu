@@ -378,15 +378,17 @@ __device__ __forceinline__ float4 cap_masked(float4 v, unsigned t4, int pos) {
 // MAX = false: sum aggregation.  Records of a row come grouped by channel, so m * X[src]
 // is summed per channel run and multiplied by the run's rule weights once (fp32 order
 // differs from the per-message products; the sum is within tolerance).  Column sums of
-// the output feed normalize_sparse3d.
+// the output feed normalize_sparse3d, and every (row, 128-column chunk) this warp adds a
+// non-zero value to is marked in yhint (zeroed before the forward), so that the normalisation
+// reads only those chunks.
 // MAX = true: max of the exact message values (X[src] * w[ch]) * m (sparse3d_max over the
 // op's ind / ori / inv outputs), rule weights read per record.
 template <bool MAX, int VEC, bool CAP>
 __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
-    float* __restrict__ y, float* __restrict__ dsum, int32_t* __restrict__ queue, const int2* __restrict__ rcap,
-    const uint8_t* __restrict__ take, unsigned* err) {
+    float* __restrict__ y, float* __restrict__ dsum, uint8_t* __restrict__ yhint, int32_t* __restrict__ queue,
+    const int2* __restrict__ rcap, const uint8_t* __restrict__ take, unsigned* err) {
   __shared__ int4 recs[kFwdWarps][32];
   __shared__ int2 rcs[kFwdWarps][CAP ? 32 : 1];  // capped records: (take row, position in group)
   __shared__ float cs[4 * 32 * VEC];  // column partial sums: cs[(v*4 + k)*32 + lane] = column 4*lane + k + 128*v
@@ -517,9 +519,13 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
 #pragma unroll
     for (int k = 0; k < VEC; ++k) {
       const int64_t c = col + 128 * k;
+      const float4 a = acc.v[k];
+      if (!MAX) {
+        const bool nz = c < q.BLP && (a.x != 0.f || a.y != 0.f || a.z != 0.f || a.w != 0.f);
+        if (__ballot_sync(0xffffffffu, nz) != 0u && lane == 0) yhint[row * q.nch + (col0 >> 7) + k] = 1;
+      }
       if (c >= q.BLP) continue;
       float* yr = y + row * q.BLP + c;
-      const float4 a = acc.v[k];
       if (tk.w & kTaskPartial) {
         if (MAX) {
           atomicMax(reinterpret_cast<int*>(yr) + 0, __float_as_int(a.x));
@@ -556,46 +562,78 @@ __global__ void __launch_bounds__(kFwdWarps * 32) fwd_pull_kernel(
 // normalize_sparse3d(.., 0, "mass") (drum.py:31-51) on the dense state:
 // x = (y / d) * min(d, 1) where y != 0; optional threshold; activity flags and the
 // message count of the next hop (present entries x push degree, or x the capped degree).
-__global__ void normalize_mass_kernel(const float* __restrict__ y, const float* __restrict__ dsum, ProofDims q,
-                                      float threshold, float* __restrict__ x, uint8_t* __restrict__ act,
-                                      uint8_t* __restrict__ yact, const int32_t* __restrict__ push_ptr,
-                                      const int32_t* __restrict__ capdeg, int64_t* __restrict__ msgs) {
+// yact holds on entry the forward pull's marks (chunks it added a non-zero value to; Y is zero
+// in the others) and on exit the exact flags of Y's non-zero chunks.  Unmarked chunks are not
+// read and get zeros in X, except where nothing reads them: the pulls read X only in chunks
+// whose 256-column pair (chunks 2j, 2j + 1) holds an active chunk, so a chunk whose pair has no
+// mark is skipped, on every hop but the last (read whole).  A warp takes kNormTasks (row,
+// chunk) tasks at a time, loads first.
+constexpr int kNormTasks = 4;
+
+__global__ void __launch_bounds__(256, 4) normalize_mass_kernel(
+    const float* __restrict__ y, const float* __restrict__ dsum, ProofDims q, float threshold, bool last_hop,
+    float* __restrict__ x, uint8_t* __restrict__ act, uint8_t* __restrict__ yact,
+    const int32_t* __restrict__ push_ptr, const int32_t* __restrict__ capdeg, int64_t* __restrict__ msgs) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t total = q.E * q.nch;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   long long local_msgs = 0;
-  for (int64_t task = warp0; task < q.E * q.nch; task += nwarps) {
-    const int64_t row = task / q.nch, chunk = task % q.nch;
-    const int64_t col = chunk * kChunk + 4 * lane;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    bool ynz = false;
-    if (col < q.BLP) {
-      const float4 v = *reinterpret_cast<const float4*>(y + row * q.BLP + col);
-      ynz = v.x != 0.f || v.y != 0.f || v.z != 0.f || v.w != 0.f;
-      const float4 d = *reinterpret_cast<const float4*>(dsum + col);
-      float vi[4] = {v.x, v.y, v.z, v.w}, di[4] = {d.x, d.y, d.z, d.w}, oi[4];
+  for (int64_t t0 = warp0 * kNormTasks; t0 < total; t0 += nwarps * kNormTasks) {
+    const int64_t row0 = t0 / q.nch, chunk0 = t0 % q.nch;
+    bool marked[kNormTasks], pair[kNormTasks];  // uniform over the warp
+    float4 v[kNormTasks];
+    {
+      int64_t row = row0, chunk = chunk0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float r = 0.0f;
-        if (vi[k] != 0.0f) {
-          r = __fdiv_rn(vi[k], di[k]) * fminf(di[k], 1.0f);
-          if (threshold > 0.0f && r < threshold) r = 0.0f;
-        }
-        oi[k] = r;
+      for (int u = 0; u < kNormTasks; ++u) {
+        const int64_t col = chunk * kChunk + 4 * lane;
+        const bool in = t0 + u < total;
+        marked[u] = in && yact[t0 + u] != 0;
+        pair[u] = marked[u] || (in && (chunk ^ 1) < q.nch && yact[row * q.nch + (chunk ^ 1)] != 0);
+        v[u] = (marked[u] && col < q.BLP) ? *reinterpret_cast<const float4*>(y + row * q.BLP + col) : zero;
+        if (++chunk == q.nch) { chunk = 0; ++row; }
       }
-      o = make_float4(oi[0], oi[1], oi[2], oi[3]);
-      *reinterpret_cast<float4*>(x + row * q.BLP + col) = o;
     }
-    const int nz = f4_count(o);
-    const unsigned any = __ballot_sync(0xffffffffu, nz > 0);
-    const unsigned yany = __ballot_sync(0xffffffffu, ynz);
-    int tot = nz;
+    int64_t row = row0, chunk = chunk0;
 #pragma unroll
-    for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
-    if (lane == 0) {
-      act[row * q.nch + chunk] = any ? 1 : 0;
-      yact[row * q.nch + chunk] = yany ? 1 : 0;
-      if (tot) local_msgs += (long long)tot * (capdeg ? capdeg[row] : push_ptr[row + 1] - push_ptr[row]);
+    for (int u = 0; u < kNormTasks; ++u) {
+      if (t0 + u >= total) break;  // uniform over the warp
+      const int64_t col = chunk * kChunk + 4 * lane;
+      float4 o = zero;
+      bool ynz = false;
+      if (marked[u] && col < q.BLP) {
+        const float4 vv = v[u];
+        ynz = vv.x != 0.f || vv.y != 0.f || vv.z != 0.f || vv.w != 0.f;
+        const float4 d = *reinterpret_cast<const float4*>(dsum + col);
+        float vi[4] = {vv.x, vv.y, vv.z, vv.w}, di[4] = {d.x, d.y, d.z, d.w}, oi[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float r = 0.0f;
+          if (vi[k] != 0.0f) {
+            r = __fdiv_rn(vi[k], di[k]) * fminf(di[k], 1.0f);
+            if (threshold > 0.0f && r < threshold) r = 0.0f;
+          }
+          oi[k] = r;
+        }
+        o = make_float4(oi[0], oi[1], oi[2], oi[3]);
+        *reinterpret_cast<float4*>(x + row * q.BLP + col) = o;
+      } else if ((pair[u] || last_hop) && col < q.BLP) {
+        *reinterpret_cast<float4*>(x + row * q.BLP + col) = zero;
+      }
+      const int nz = f4_count(o);
+      const unsigned any = __ballot_sync(0xffffffffu, nz > 0);
+      const unsigned yany = __ballot_sync(0xffffffffu, ynz);
+      int tot = nz;
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
+      if (lane == 0) {
+        act[row * q.nch + chunk] = any ? 1 : 0;
+        if (marked[u]) yact[row * q.nch + chunk] = yany ? 1 : 0;
+        if (tot) local_msgs += (long long)tot * (capdeg ? capdeg[row] : push_ptr[row + 1] - push_ptr[row]);
+      }
+      if (++chunk == q.nch) { chunk = 0; ++row; }
     }
   }
   if (lane == 0 && local_msgs) atomicAdd(reinterpret_cast<unsigned long long*>(msgs), (unsigned long long)local_msgs);
@@ -1304,7 +1342,8 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
   transpose_w_kernel<<<grid_for(q.hops * q.n * q.BLP, 256, pb), 256, 0, st>>>(w_hops, q, S.wt(0));
   MKG_LAUNCHED("transpose_w_kernel");
   MKG_CUDA(cudaMemsetAsync(S.x(0), 0, slab, st));
-  MKG_CUDA(cudaMemsetAsync(S.act(0), 0, (size_t)q.E * q.nch, st));
+  // activity flags of every hop and the chunk marks of Y (one range: act then yact)
+  MKG_CUDA(cudaMemsetAsync(S.act(0), 0, (S.lay.yact - S.lay.act) + (size_t)q.hops * q.E * q.nch, st));
   MKG_CUDA(cudaMemsetAsync(S.d(0), 0, 4 * (size_t)q.hops * q.BLP, st));
   MKG_CUDA(cudaMemsetAsync(S.queue(), 0, 4 * (size_t)(q.hops * q.nch * kQueueStride), st));
   MKG_CUDA(cudaMemsetAsync(S.msgs(), 0, 8 * (size_t)(q.hops + 1), st));
@@ -1341,11 +1380,12 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
       const int4* tk = reinterpret_cast<const int4*>(adj->pull_tasks);
       const int64_t nt = adj->num_pull_tasks;
       float* ds = max_mode ? nullptr : S.d(h);
+      uint8_t* yh = max_mode ? nullptr : S.yact(h);
       int32_t* qu = S.queue() + h * q.nch * kQueueStride;
       const uint8_t* tk_h = ix ? S.take(h) : nullptr;
 #define MKG_FWD_PULL(M, V, C) \
   fwd_pull_kernel<M, V, C><<<grid, kFwdWarps * 32, 0, st>>>(tk, nt, adj->pull, q, S.wt(h), S.x(h), S.act(h), y, ds, \
-                                                           qu, pull_cap, tk_h, err)
+                                                           yh, qu, pull_cap, tk_h, err)
       if (ix) {
         if (max_mode && vec == 2) MKG_FWD_PULL(true, 2, true);
         else if (max_mode) MKG_FWD_PULL(true, 1, true);
@@ -1373,8 +1413,8 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
         MKG_LAUNCHED("normalize_plain_kernel");
       }
     } else {
-      normalize_mass_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, p->state_threshold, S.x(h + 1), S.act(h + 1),
-                                                S.yact(h), adj->push_ptr, capdeg, S.msgs() + h + 1);
+      normalize_mass_kernel<<<pb, 256, 0, st>>>(y, S.d(h), q, p->state_threshold, h + 1 == q.hops, S.x(h + 1),
+                                                S.act(h + 1), S.yact(h), adj->push_ptr, capdeg, S.msgs() + h + 1);
       MKG_LAUNCHED("normalize_mass_kernel");
     }
   }

@@ -912,6 +912,43 @@ def test_fused_step_graph_host_copies():
         np.testing.assert_allclose(got[2].numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
 
 
+def test_fused_step_after_denser_step_matches_fresh_runner():
+    """The normalisation skips the state chunks that hold no value and leaves them as an earlier
+    step wrote them: a sparse step run after a dense one on the same runner equals the same step
+    on a fresh runner.  The three 128-column chunks get different heads, so rows whose chunk is
+    set next to an empty sibling chunk (both read by the 8-column forward lanes) occur."""
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.proof import ProofRunner
+    h, r, t, E, R = GRAPHS["hubby"]
+    csr = O.build_csr_structure(h, t, r, E)
+    dg = DeviceGraph(csr_dev(csr), E, R)
+    rng = np.random.default_rng(23)
+    B, L, K, n = 100, 3, 3, 2 * R + 1
+
+    def weights():
+        return T(np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)]))
+
+    sc = T(rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32))
+    G = T(rng.standard_normal((B, E)).astype(np.float32))
+    used = ProofRunner(dg, B, L, K)
+    dg.set_edge_factor(None, sc, True, 1.0)
+    used.forward(T(rng.integers(0, E, B).astype(np.int64)), weights())
+    used.backward(G, None, sc, True, 1.0, True)
+    heads = T(np.repeat(rng.choice(E, 3, replace=False), [43, 43, 14]).astype(np.int64))
+    w_hops = weights()
+    res = []
+    for runner in (used, ProofRunner(dg, B, L, K)):
+        dg.set_edge_factor(None, sc, True, 1.0)
+        o, m = runner.forward(heads, w_hops)
+        gw, ge = runner.backward(G, None, sc, True, 1.0, True)
+        res.append((o.clone(), m.clone(), gw.clone(), ge.clone()))
+    (o1, m1, gw1, ge1), (o2, m2, gw2, ge2) = res
+    assert torch.equal(m1, m2)
+    np.testing.assert_allclose(o1.cpu().numpy(), o2.cpu().numpy(), rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(gw1.cpu().numpy(), gw2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(ge1.cpu().numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+
+
 # ----------------------------------------------------------------------------- decode candidates
 @pytest.mark.parametrize("gname", ["g1", "g2"])
 @pytest.mark.parametrize("cap", [UNC, 9])
