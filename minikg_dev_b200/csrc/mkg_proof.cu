@@ -115,15 +115,64 @@ __global__ void transpose_w_kernel(const float* __restrict__ w, ProofDims q, flo
   }
 }
 
-// grad_w_hops[h][b][l][ch] = dWt[ch][b*L + l]
-__global__ void untranspose_dw_kernel(const float* __restrict__ dwt, ProofDims q, int64_t h,
-                                      float* __restrict__ gw) {
+// grad_w_hops[h][b][l][ch] = dWt[ch][b*L + l]; dWt is cleared behind the read for the next
+// lower hop (its padding columns receive nothing and stay zero).
+__global__ void untranspose_dw_kernel(float* __restrict__ dwt, ProofDims q, int64_t h, float* __restrict__ gw) {
   const int64_t total = q.BL * q.n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     int64_t ch = i % q.n, c = i / q.n;
     gw[h * total + i] = dwt[ch * q.BLP + c];
+    dwt[ch * q.BLP + c] = 0.0f;
   }
+}
+
+// Start of a forward, one launch for what must be zero before it: the activity flags and Y
+// marks of every hop (bytes [flags, flags + nflags)), the column sums, the forward's task-queue
+// counters, the message counts, the head rows of X_0 (the only rows of X_0 the hop-0 pull
+// reads, as act_0 is set only there; both halves of a 256-column pair are zeroed with the row)
+// and, for every hop, the rows of Y_h that several pull tasks add into.
+__global__ void forward_setup_kernel(const int64_t* __restrict__ heads, const int4* __restrict__ tasks, int64_t ntasks,
+                                     ProofDims q, uint8_t* __restrict__ flags, int64_t nflags,
+                                     float* __restrict__ y0, int64_t y_stride, float* __restrict__ x0,
+                                     float* __restrict__ d, int32_t* __restrict__ queue, int64_t nqueue,
+                                     int64_t* __restrict__ msgs) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  for (int64_t i = tid; i < nflags / 16; i += nthreads) reinterpret_cast<uint4*>(flags)[i] = z4;
+  for (int64_t i = nflags / 16 * 16 + tid; i < nflags; i += nthreads) flags[i] = 0;
+  for (int64_t i = tid; i < q.hops * q.BLP; i += nthreads) d[i] = 0.0f;
+  for (int64_t i = tid; i < nqueue; i += nthreads) queue[i] = 0;
+  for (int64_t i = tid; i <= q.hops; i += nthreads) msgs[i] = 0;
+  const int64_t row4 = q.BLP / 4;  // BLP is a multiple of 4
+  for (int64_t i = tid; i < q.B * row4; i += nthreads) {
+    const int64_t e = heads[i / row4];
+    if (e >= 0 && e < q.E) reinterpret_cast<uint4*>(x0 + e * q.BLP)[i % row4] = z4;  // bad heads: init_state flags them
+  }
+  const int lane = threadIdx.x & 31;
+  for (int64_t t = tid >> 5; t < ntasks; t += nthreads >> 5) {
+    const int4 tk = tasks[t];
+    if ((tk.w & (kTaskFirst | kTaskPartial)) != (kTaskFirst | kTaskPartial)) continue;
+    for (int64_t h = 0; h < q.hops; ++h) {
+      uint4* row = reinterpret_cast<uint4*>(y0 + h * y_stride + (int64_t)tk.x * q.BLP);
+      for (int64_t j = lane; j < row4; j += 32) row[j] = z4;
+    }
+  }
+}
+
+// Start of a backward: the edge-score gradient, the S sums of every hop, the backward's
+// task-queue counters and dWt.
+__global__ void backward_setup_kernel(ProofDims q, float* __restrict__ grad_edge, int64_t num_facts,
+                                      float* __restrict__ s, int32_t* __restrict__ queue, int64_t nqueue,
+                                      float* __restrict__ dwt) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  if (grad_edge)
+    for (int64_t i = tid; i < num_facts; i += nthreads) grad_edge[i] = 0.0f;
+  for (int64_t i = tid; i < q.hops * q.BLP; i += nthreads) s[i] = 0.0f;
+  for (int64_t i = tid; i < nqueue; i += nthreads) queue[i] = 0;
+  for (int64_t i = tid; i < q.n * q.BLP; i += nthreads) dwt[i] = 0.0f;
 }
 
 // One-hot start: X0[head_b][b*L + l] = 1 for every rule l (proof.py:511-523).
@@ -1341,12 +1390,11 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
   const int pb = persistent_blocks(4);
   transpose_w_kernel<<<grid_for(q.hops * q.n * q.BLP, 256, pb), 256, 0, st>>>(w_hops, q, S.wt(0));
   MKG_LAUNCHED("transpose_w_kernel");
-  MKG_CUDA(cudaMemsetAsync(S.x(0), 0, slab, st));
-  // activity flags of every hop and the chunk marks of Y (one range: act then yact)
-  MKG_CUDA(cudaMemsetAsync(S.act(0), 0, (S.lay.yact - S.lay.act) + (size_t)q.hops * q.E * q.nch, st));
-  MKG_CUDA(cudaMemsetAsync(S.d(0), 0, 4 * (size_t)q.hops * q.BLP, st));
-  MKG_CUDA(cudaMemsetAsync(S.queue(), 0, 4 * (size_t)(q.hops * q.nch * kQueueStride), st));
-  MKG_CUDA(cudaMemsetAsync(S.msgs(), 0, 8 * (size_t)(q.hops + 1), st));
+  forward_setup_kernel<<<pb, 256, 0, st>>>(
+      heads, reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, q, S.act(0),
+      (int64_t)(S.lay.yact - S.lay.act) + q.hops * q.E * q.nch, S.y(0), (int64_t)(a256(slab) / 4), S.x(0), S.d(0),
+      S.queue(), q.hops * q.nch * kQueueStride, S.msgs());
+  MKG_LAUNCHED("forward_setup_kernel");
   const mkg_cap_index* ix = q.cap >= 0 ? p->cap_index : nullptr;
   const int32_t* capdeg = ix ? ix->capped_degree : nullptr;
   const int2* pull_cap = ix ? reinterpret_cast<const int2*>(ix->pull_cap) : nullptr;
@@ -1372,8 +1420,6 @@ static int run_forward(const mkg_graph* g, const mkg_adjacency* adj, const int64
           S.act(h), S.take(h), err);
       MKG_LAUNCHED("cap_take_kernel");
     }
-    zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->pull_tasks), adj->num_pull_tasks, q, y);
-    MKG_LAUNCHED("zero_partial_rows_kernel");
     dim3 grid(blocks_per_chunk, (unsigned)nfch);
     if (p->fwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->fwd_events[2 * h]), st));
     {
@@ -1447,9 +1493,9 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
   const size_t slab = 4 * (size_t)q.E * q.BLP;
   const int pb = persistent_blocks(4);
   EdgeFactor f = make_factor(*ef);
-  if (grad_edge) MKG_CUDA(cudaMemsetAsync(grad_edge, 0, 4 * (size_t)g->num_facts, st));
-  MKG_CUDA(cudaMemsetAsync(S.s(0), 0, 4 * (size_t)q.hops * q.BLP, st));
-  MKG_CUDA(cudaMemsetAsync(S.queue() + q.hops * q.nch * kQueueStride, 0, 4 * (size_t)(q.hops * q.nch * kQueueStride), st));
+  backward_setup_kernel<<<pb, 256, 0, st>>>(q, grad_edge, g->num_facts, S.s(0), S.queue() + q.hops * q.nch * kQueueStride,
+                                            q.hops * q.nch * kQueueStride, S.dwt());
+  MKG_LAUNCHED("backward_setup_kernel");
   float* dx_cur = S.dxa();
   float* dx_next = S.dxb();
   dim3 sgrid((unsigned)((q.E + 32 * kSeedTiles - 1) / (32 * kSeedTiles)), (unsigned)((q.B + 31) / 32));
@@ -1469,7 +1515,6 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
     // dY_h from dX_{h+1}
     normalize_mass_backward_kernel<<<pb, 256, 0, st>>>(dx_cur, S.y(h), S.d(h), S.s(h), S.yact(h), q, S.dy());
     MKG_LAUNCHED("normalize_mass_backward_kernel");
-    MKG_CUDA(cudaMemsetAsync(S.dwt(), 0, 4 * (size_t)q.n * q.BLP, st));
     zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, q, dx_next);
     MKG_LAUNCHED("zero_partial_rows_kernel");
     (void)slab;
