@@ -502,7 +502,7 @@ def run_ours(a, wl, kg, rank, world, local_rank):
                 "ms_per_step": e2e_total / a.steps,
                 "path": "ProofRunner.capture with host_inputs / host_outputs (pinned host buffers), replayed",
                 "eager_value": e2e_eager_value, "eager_ms_per_step": e2e_eager_total / a.steps},
-        "gpu_launches": (8 + 6 * K) * a.steps,
+        "gpu_launches": (8 + 5 * K) * a.steps,
         "clocks": clocks.summary(),
     }
     if world == 1 and not a.no_cpu_baseline:

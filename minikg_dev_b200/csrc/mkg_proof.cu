@@ -191,20 +191,6 @@ __global__ void init_state_kernel(const int64_t* __restrict__ heads, ProofDims q
   }
 }
 
-// Zeroes the rows that several tasks add into (their first task carries both flags).
-__global__ void zero_partial_rows_kernel(const int4* __restrict__ tasks, int64_t ntasks, ProofDims q,
-                                         float* __restrict__ slab) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t t = warp0; t < ntasks; t += nwarps) {
-    int4 tk = tasks[t];
-    if ((tk.w & (kTaskFirst | kTaskPartial)) != (kTaskFirst | kTaskPartial)) continue;
-    float4* row = reinterpret_cast<float4*>(slab + (int64_t)tk.x * q.BLP);
-    for (int64_t j = lane; j < q.BLP / 4; j += 32) row[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-}
-
 __device__ __forceinline__ float4 f4_mul(const float4& a, const float4& b) {
   return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
 }
@@ -946,16 +932,25 @@ __global__ void __launch_bounds__(256) seed_grad_kernel(const float* __restrict_
 // min(d, 1) = d and the two terms cancel).  A warp takes kNbTasks (row, 128-column chunk)
 // tasks at a time and skips the chunks where Y_h is zero (yact): dY is zero there, and the
 // backward pull reads dY only in chunks whose yact is set, so those chunks are not written.
+// The same launch zeroes the rows of dx_next (the slab this hop's pull writes) that several push
+// tasks add into: this kernel does not read that slab, the previous hop's did.
 constexpr int kNbTasks = 4;
 
 __global__ void __launch_bounds__(256, 4) normalize_mass_backward_kernel(
     const float* __restrict__ dx, const float* __restrict__ y, const float* __restrict__ dsum,
-    const float* __restrict__ s, const uint8_t* __restrict__ yact, ProofDims q, float* __restrict__ dy) {
+    const float* __restrict__ s, const uint8_t* __restrict__ yact, ProofDims q, float* __restrict__ dy,
+    const int4* __restrict__ push_tasks, int64_t num_push_tasks, float* __restrict__ dx_next) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t total = q.E * q.nch;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t t = warp0; t < num_push_tasks; t += nwarps) {
+    const int4 tk = push_tasks[t];
+    if ((tk.w & (kTaskFirst | kTaskPartial)) != (kTaskFirst | kTaskPartial)) continue;
+    float4* row = reinterpret_cast<float4*>(dx_next + (int64_t)tk.x * q.BLP);
+    for (int64_t j = lane; j < q.BLP / 4; j += 32) row[j] = zero;
+  }
   for (int64_t t0 = warp0 * kNbTasks; t0 < total; t0 += nwarps * kNbTasks) {
     const int64_t row0 = t0 / q.nch, chunk0 = t0 % q.nch;
     bool on[kNbTasks];
@@ -1513,10 +1508,10 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
                                         (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / q.nch) + 1);
   for (int64_t h = q.hops - 1; h >= 0; --h) {
     // dY_h from dX_{h+1}
-    normalize_mass_backward_kernel<<<pb, 256, 0, st>>>(dx_cur, S.y(h), S.d(h), S.s(h), S.yact(h), q, S.dy());
+    normalize_mass_backward_kernel<<<pb, 256, 0, st>>>(dx_cur, S.y(h), S.d(h), S.s(h), S.yact(h), q, S.dy(),
+                                                       reinterpret_cast<const int4*>(adj->push_tasks),
+                                                       adj->num_push_tasks, dx_next);
     MKG_LAUNCHED("normalize_mass_backward_kernel");
-    zero_partial_rows_kernel<<<pb, 256, 0, st>>>(reinterpret_cast<const int4*>(adj->push_tasks), adj->num_push_tasks, q, dx_next);
-    MKG_LAUNCHED("zero_partial_rows_kernel");
     (void)slab;
     dim3 grid(blocks_per_chunk, (unsigned)q.nch);
     if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h]), st));
