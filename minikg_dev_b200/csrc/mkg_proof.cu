@@ -1030,9 +1030,10 @@ __device__ __forceinline__ float reduce_scatter4(const float (&v)[4]) {
 // folded into dX and dW once per run, and the edge-score gradient uses the run's X * W[ch]
 // (one rule-weight load per run).  Only records whose destination row holds a non-zero Y_h
 // value in this chunk are visited (dY_h is zero elsewhere).  Rule weights are read from
-// global memory (L1-resident chunk) so that only dW occupies shared memory: 3 blocks per SM.
+// global memory (L1-resident chunk) so that only dW occupies shared memory: 4 blocks per SM
+// (64 registers, a few bytes spilled; the capped loop, which spills more there, keeps 3).
 template <bool CAP>
-__global__ void __launch_bounds__(kBwdWarps * 32, 3) bwd_pull_kernel(
+__global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
     const uint8_t* __restrict__ yact, const float* __restrict__ dy, const float* __restrict__ yprev,
