@@ -852,28 +852,35 @@ __global__ void rows_to_queries_kernel(const float* __restrict__ x, const float*
 // Seed: dX_K[e][c] = G[b][e] where X_K[e][c] != 0 (the reference's sparse result carries
 // gradient only on its keys), and S[c] = sum_e dX_K[e][c] * Y_{K-1}[e][c].
 constexpr int kSeedTiles = 4;   // 32-entity tiles per block of seed_grad_kernel
-constexpr int kSeedMaxL = 16;   // rules whose column partials fit the block's shared memory
-constexpr int kSeedBatch = 4;   // float4s whose loads a thread issues together
+constexpr int kSeedRows = 4;    // rows whose loads a thread issues together
 
 // Block = 32 queries (the contiguous columns [32 L by, 32 L (by + 1)) of every row, 16-byte
 // aligned since BLP is a multiple of 4) x kSeedTiles tiles of 32 entities.  The G tile goes
-// through shared memory; X_K, Y_{K-1} and dX_K are then streamed row by row in float4s, so
-// every load and store of the slabs is coalesced.  A float4 that reaches past B L covers
-// padding columns, which hold zeros in X_K and get zeros in dX_K.
-__global__ void __launch_bounds__(256) seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
+// through shared memory; X_K, Y_{K-1} and dX_K are streamed in float4s.  A thread keeps one
+// float4 column of the segment for the whole block (rows step by 256 / float4s per row), so the
+// queries of its 4 columns are found once and its S partials stay in registers; they are summed
+// in shared memory at the end.  Segments wider than 256 float4s (L > 32) take several column
+// rounds and add S with global atomics.  A float4 that reaches past B L covers padding columns,
+// which hold zeros in X_K and get zeros in dX_K.
+__global__ void __launch_bounds__(256, 4) seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
                                                        const float* __restrict__ ylast, ProofDims q,
                                                        float* __restrict__ dx, float* __restrict__ s) {
-  __shared__ float tile[32][33];          // [query][entity] of G
-  __shared__ float part[32 * kSeedMaxL];  // this block's share of S for its 32 queries
+  __shared__ float tile[32][33];  // [query][entity] of G
+  __shared__ float part[1024];    // S of the block's columns (width <= 1024 on the register path)
   const int tid = threadIdx.x;
   const int64_t b0 = blockIdx.y * 32;
   const int nb = static_cast<int>(q.B - b0 < 32 ? q.B - b0 : 32);
   const int L = static_cast<int>(q.L);
   const int64_t c0 = b0 * L;
-  const int width = nb * L;             // columns of the block's queries
-  const int nf4 = (width + 3) / 4;      // float4s per row (the last may reach into padding)
-  const bool local = L <= kSeedMaxL;
-  for (int i = tid; i < 32 * kSeedMaxL; i += 256) part[i] = 0.0f;
+  const int width = nb * L;         // columns of the block's queries
+  const int nf4 = (width + 3) / 4;  // float4s per row (the last may reach into padding)
+  const bool fixed = nf4 <= 256;    // one column round: S partials in registers
+  const int cols = fixed ? nf4 : 256;
+  const int rpp = 256 / cols;       // rows per pass
+  const int cf = tid % cols, rr = tid / cols;
+  const bool worker = rr < rpp;
+  for (int i = tid; i < 1024; i += 256) part[i] = 0.0f;
+  float sacc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int t = 0; t < kSeedTiles; ++t) {
     const int64_t e0 = ((int64_t)blockIdx.x * kSeedTiles + t) * 32;
     if (e0 >= q.E) break;
@@ -884,43 +891,53 @@ __global__ void __launch_bounds__(256) seed_grad_kernel(const float* __restrict_
       tile[b][e] = (b < nb && e < rows) ? g[(b0 + b) * q.E + e0 + e] : 0.0f;
     }
     __syncthreads();
-    const int n = rows * nf4;
-    for (int i0 = tid; i0 < n; i0 += 256 * kSeedBatch) {
-      float4 xv[kSeedBatch], yv[kSeedBatch];
+    if (!worker) continue;
+    for (int f = cf; f < nf4; f += cols) {
+      const int j0 = 4 * f;
+      int bq[4];
+      bool ok[4];
 #pragma unroll
-      for (int u = 0; u < kSeedBatch; ++u) {
-        const int i = i0 + u * 256;
-        if (i < n) {
-          const int64_t off = (e0 + i / nf4) * q.BLP + c0 + 4 * (i % nf4);
-          xv[u] = *reinterpret_cast<const float4*>(xk + off);
-          yv[u] = *reinterpret_cast<const float4*>(ylast + off);
-        }
+      for (int k = 0; k < 4; ++k) {
+        ok[k] = j0 + k < width;
+        bq[k] = ok[k] ? (j0 + k) / L : 0;
       }
+      for (int r0 = rr; r0 < rows; r0 += rpp * kSeedRows) {
+        float4 xv[kSeedRows], yv[kSeedRows];
 #pragma unroll
-      for (int u = 0; u < kSeedBatch; ++u) {
-        const int i = i0 + u * 256;
-        if (i >= n) break;
-        const int r = i / nf4, j0 = 4 * (i % nf4);
-        const float xs[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
-        const float ys[4] = {yv[u].x, yv[u].y, yv[u].z, yv[u].w};
-        float o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int j = j0 + k;
-          float dv = 0.0f;
-          if (j < width && xs[k] != 0.0f) dv = tile[j / L][r];
-          o[k] = dv;
-          if (dv != 0.0f) {
-            const float contrib = dv * ys[k];
-            if (local) atomicAdd(part + j, contrib);
-            else atomicAdd(s + c0 + j, contrib);
+        for (int u = 0; u < kSeedRows; ++u) {
+          const int r = r0 + u * rpp;
+          if (r < rows) {
+            const int64_t off = (e0 + r) * q.BLP + c0 + j0;
+            xv[u] = *reinterpret_cast<const float4*>(xk + off);
+            yv[u] = *reinterpret_cast<const float4*>(ylast + off);
           }
         }
-        *reinterpret_cast<float4*>(dx + (e0 + r) * q.BLP + c0 + j0) = make_float4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+        for (int u = 0; u < kSeedRows; ++u) {
+          const int r = r0 + u * rpp;
+          if (r >= rows) break;
+          const float xs[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+          const float ys[4] = {yv[u].x, yv[u].y, yv[u].z, yv[u].w};
+          float o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float dv = (ok[k] && xs[k] != 0.0f) ? tile[bq[k]][r] : 0.0f;
+            o[k] = dv;
+            if (fixed) sacc[k] = fmaf(dv, ys[k], sacc[k]);
+            else if (dv != 0.0f) atomicAdd(s + c0 + j0 + k, dv * ys[k]);
+          }
+          *reinterpret_cast<float4*>(dx + (e0 + r) * q.BLP + c0 + j0) = make_float4(o[0], o[1], o[2], o[3]);
+        }
       }
     }
   }
-  if (local) {
+  if (fixed) {
+    if (worker) {
+      const int j0 = 4 * cf;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (j0 + k < width && sacc[k] != 0.0f) atomicAdd(part + j0 + k, sacc[k]);
+    }
     __syncthreads();
     for (int j = tid; j < width; j += 256)
       if (part[j] != 0.0f) atomicAdd(s + c0 + j, part[j]);
