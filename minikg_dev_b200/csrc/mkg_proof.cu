@@ -860,7 +860,7 @@ constexpr int kSeedRows = 4;    // rows whose loads a thread issues together
 // float4 column of the segment for the whole block (rows step by 256 / float4s per row), so the
 // queries of its 4 columns are found once and its S partials stay in registers; they are summed
 // in shared memory at the end.  Segments wider than 256 float4s (L > 32) take several column
-// rounds and add S with global atomics.  A float4 that reaches past B L covers padding columns,
+// passes and add S with global atomics.  A float4 that reaches past B L covers padding columns,
 // which hold zeros in X_K and get zeros in dX_K.
 __global__ void __launch_bounds__(256, 4) seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
                                                        const float* __restrict__ ylast, ProofDims q,
@@ -874,7 +874,7 @@ __global__ void __launch_bounds__(256, 4) seed_grad_kernel(const float* __restri
   const int64_t c0 = b0 * L;
   const int width = nb * L;         // columns of the block's queries
   const int nf4 = (width + 3) / 4;  // float4s per row (the last may reach into padding)
-  const bool fixed = nf4 <= 256;    // one column round: S partials in registers
+  const bool fixed = nf4 <= 256;    // one column pass: S partials in registers
   const int cols = fixed ? nf4 : 256;
   const int rpp = 256 / cols;       // rows per pass
   const int cf = tid % cols, rr = tid / cols;
