@@ -73,7 +73,7 @@ ProofLayout proof_layout(const ProofDims& q) {
   L.dxb = o; o += a256(slab);
   L.dy = o; o += a256(slab);
   L.s = o; o += a256(4 * (size_t)q.hops * q.BLP);
-  L.dwt = o; o += a256(4 * (size_t)q.n * q.BLP);
+  L.dwt = o; o += a256(8 * (size_t)q.n * q.BLP);  // fp64 accumulator
   L.queue = o; o += a256(4 * (size_t)(2 * q.hops * q.nch * kQueueStride));
   L.msgs = o; o += a256(8 * (size_t)(q.hops + 1));
   L.take = o; o += a256((size_t)q.hops * q.ngroups * q.tblp);
@@ -96,7 +96,7 @@ struct Slab {
   float* dxb() const { return reinterpret_cast<float*>(base + lay.dxb); }
   float* dy() const { return reinterpret_cast<float*>(base + lay.dy); }
   float* s(int64_t h) const { return reinterpret_cast<float*>(base + lay.s) + h * q.BLP; }
-  float* dwt() const { return reinterpret_cast<float*>(base + lay.dwt); }
+  double* dwt() const { return reinterpret_cast<double*>(base + lay.dwt); }
   int32_t* queue() const { return reinterpret_cast<int32_t*>(base + lay.queue); }
   int64_t* msgs() const { return reinterpret_cast<int64_t*>(base + lay.msgs); }
   // edge-cap take table of hop h: [ngroups][tblp] edges taken per (capped group, column), columns
@@ -115,15 +115,16 @@ __global__ void transpose_w_kernel(const float* __restrict__ w, ProofDims q, flo
   }
 }
 
-// grad_w_hops[h][b][l][ch] = dWt[ch][b*L + l]; dWt is cleared behind the read for the next
-// lower hop (its padding columns receive nothing and stay zero).
-__global__ void untranspose_dw_kernel(float* __restrict__ dwt, ProofDims q, int64_t h, float* __restrict__ gw) {
+// grad_w_hops[h][b][l][ch] = dWt[ch][b*L + l], rounded once from the fp64 accumulator; dWt is
+// cleared behind the read for the next lower hop (its padding columns receive nothing and stay
+// zero).
+__global__ void untranspose_dw_kernel(double* __restrict__ dwt, ProofDims q, int64_t h, float* __restrict__ gw) {
   const int64_t total = q.BL * q.n;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     int64_t ch = i % q.n, c = i / q.n;
-    gw[h * total + i] = dwt[ch * q.BLP + c];
-    dwt[ch * q.BLP + c] = 0.0f;
+    gw[h * total + i] = static_cast<float>(dwt[ch * q.BLP + c]);
+    dwt[ch * q.BLP + c] = 0.0;
   }
 }
 
@@ -165,14 +166,14 @@ __global__ void forward_setup_kernel(const int64_t* __restrict__ heads, const in
 // task-queue counters and dWt.
 __global__ void backward_setup_kernel(ProofDims q, float* __restrict__ grad_edge, int64_t num_facts,
                                       float* __restrict__ s, int32_t* __restrict__ queue, int64_t nqueue,
-                                      float* __restrict__ dwt) {
+                                      double* __restrict__ dwt) {
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   if (grad_edge)
     for (int64_t i = tid; i < num_facts; i += nthreads) grad_edge[i] = 0.0f;
   for (int64_t i = tid; i < q.hops * q.BLP; i += nthreads) s[i] = 0.0f;
   for (int64_t i = tid; i < nqueue; i += nthreads) queue[i] = 0;
-  for (int64_t i = tid; i < q.n * q.BLP; i += nthreads) dwt[i] = 0.0f;
+  for (int64_t i = tid; i < q.n * q.BLP; i += nthreads) dwt[i] = 0.0;
 }
 
 // One-hot start: X0[head_b][b*L + l] = 1 for every rule l (proof.py:511-523).
@@ -682,7 +683,10 @@ __global__ void __launch_bounds__(256, 4) normalize_mass_kernel(
 // 8 KB tile, each completing a "full" mbarrier); warp 0 waits for each tile in order, adds
 // it row by row (one lane per column, so the fp32 order stays strictly top to bottom) and
 // frees the slot on its "empty" mbarrier.  Every wait is bounded: one that gives up sets
-// MKG_DEV_TIMEOUT and the kernel runs on to its end.
+// MKG_DEV_TIMEOUT and a shared stop flag, after which the producer issues no further copy
+// and the consumer leaves its loop; before the block exits, one thread waits (bounded again)
+// on the full barrier of every tile that was issued but not consumed, so no copy into this
+// block's shared memory is left in flight.
 constexpr int kColsumRows = 64;
 constexpr int kColsumStages = 5;  // 5 x 8 KB ring (static shared memory stays under 48 KB)
 constexpr uint32_t kWaitPolls = 1u << 22;
@@ -704,40 +708,58 @@ __global__ void __launch_bounds__(64) sequential_colsum_kernel(const __grid_cons
   __shared__ __align__(128) float buf[kColsumStages][kColsumRows][32];
   __shared__ __align__(8) uint64_t full[kColsumStages];
   __shared__ __align__(8) uint64_t empty[kColsumStages];
+  __shared__ int stop;                  // set by whichever side gave up on a wait
+  __shared__ long long issued, consumed; // tiles copied in / added up
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t c0 = (int64_t)blockIdx.x * 32;
   const int ncols = (int)((q.BLP - c0) < 32 ? (q.BLP - c0) : 32);
   const int64_t ntiles = (q.E + kColsumRows - 1) / kColsumRows;
   constexpr uint32_t kTileBytes = kColsumRows * 32 * 4;  // out-of-range rows / columns arrive as zeros
+  volatile int* vstop = &stop;
+  // bounded wait that also gives up as soon as the other side has stopped
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if ((i & 1023u) == 1023u && *vstop) return false;
+    }
+    *vstop = 1;
+    raise_flag(err, MKG_DEV_TIMEOUT);
+    return false;
+  };
   if (threadIdx.x == 0) {
     for (int k = 0; k < kColsumStages; ++k) {
       mbar_init(&full[k], 1);
       mbar_init(&empty[k], 1);
     }
     mbar_init_fence();
+    stop = 0;
+    issued = 0;
+    consumed = 0;
   }
   __syncthreads();
+  float s = 0.0f;
   if (warp == 1) {  // producer
     if (lane == 0) {
-      for (int64_t t = 0; t < ntiles; ++t) {
+      int64_t t = 0;
+      for (; t < ntiles && !*vstop; ++t) {
         const int slot = (int)(t % kColsumStages);
         const int64_t round = t / kColsumStages;
         if (round > 0) {
-          if (!mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1), kWaitPolls)) raise_flag(err, MKG_DEV_TIMEOUT);
+          if (!wait(&empty[slot], (uint32_t)((round - 1) & 1))) break;
           fence_proxy_async_smem();
         }
         mbar_expect_tx(&full[slot], kTileBytes);
         tma_load_2d(&buf[slot][0][0], &ymap, (int32_t)c0, (int32_t)(t * kColsumRows), &full[slot]);
       }
+      issued = t;
     }
   } else {  // consumer
-    float s = 0.0f;
-    for (int64_t t = 0; t < ntiles; ++t) {
+    int64_t t = 0;
+    for (; t < ntiles; ++t) {
       const int slot = (int)(t % kColsumStages);
       const int64_t round = t / kColsumStages;
-      if (!mbar_wait_bounded(&full[slot], (uint32_t)(round & 1), kWaitPolls)) {
-        if (lane == 0) raise_flag(err, MKG_DEV_TIMEOUT);
-      }
+      const bool ok = wait(&full[slot], (uint32_t)(round & 1));  // every lane observes the phase
+      if (!__all_sync(0xffffffffu, ok)) break;
       const int64_t left = q.E - t * kColsumRows;
       const int rows = left < kColsumRows ? (int)left : kColsumRows;
       int r = 0;
@@ -752,8 +774,21 @@ __global__ void __launch_bounds__(64) sequential_colsum_kernel(const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    if (lane < ncols) d[c0 + lane] = fmaxf(s, 1e-7f);
+    if (lane == 0) consumed = t;
   }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // a copy that was issued but whose tile was never consumed must land before the block
+    // exits (its shared memory is released then); each wait is bounded
+    for (long long t = consumed; t < issued; ++t) {
+      const int slot = (int)(t % kColsumStages);
+      if (!mbar_wait_bounded(&full[slot], (uint32_t)((t / kColsumStages) & 1), kWaitPolls)) {
+        raise_flag(err, MKG_DEV_TIMEOUT);
+        break;
+      }
+    }
+  }
+  if (warp == 0 && lane < ncols) d[c0 + lane] = fmaxf(s, 1e-7f);
 }
 
 // Tensor map of a row-major [rows][cols] fp32 matrix with a 64 x 32 box (cols is a multiple
@@ -1054,7 +1089,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
     const uint8_t* __restrict__ yact, const float* __restrict__ dy, const float* __restrict__ yprev,
-    float* __restrict__ dx, float* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge,
+    float* __restrict__ dx, double* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge,
     int64_t num_facts, EdgeFactor ef, int32_t* __restrict__ queue, const int2* __restrict__ rcap,
     const uint8_t* __restrict__ take, unsigned* err) {
   extern __shared__ float smem[];
@@ -1217,7 +1252,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
   for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) {
     const int64_t ch = i / kChunk, r = i % kChunk, l = r % 32, k = r / 32;
     const int64_t c = col0 + 4 * l + k;
-    if (c < q.BLP && dws[i] != 0.0f) atomicAdd(dwt + ch * q.BLP + c, dws[i]);
+    if (c < q.BLP && dws[i] != 0.0f) atomicAdd(dwt + ch * q.BLP + c, static_cast<double>(dws[i]));
   }
   if (sprev != nullptr) {
     for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {

@@ -172,8 +172,9 @@ class _NormalizeMass(autograd.Function):
     @staticmethod
     def forward(ctx, y, rows, nrows: int, threshold: float, group):
         yd = y.detach()
-        d = torch.zeros(nrows, dtype=yd.dtype, device=yd.device).index_add_(0, rows, yd)
+        d = torch.zeros(nrows, dtype=torch.float64, device=yd.device).index_add_(0, rows, yd.double())
         dist.all_reduce(d, group=group)
+        d = d.to(yd.dtype)  # fp64 sums, rounded once
         dr = d[rows]
         c = d.clamp_max(1.0)
         nz = yd != 0
@@ -198,12 +199,12 @@ class _NormalizeMass(autograd.Function):
         q = torch.where(nz, y / dr, torch.zeros_like(y))
         g_q = gx * c[rows]
         zero = torch.zeros_like(y)
-        part = torch.zeros((2, ctx.nrows), dtype=y.dtype, device=y.device)
-        part[0].index_add_(0, rows, torch.where(nz, gx * q, zero))
-        part[1].index_add_(0, rows, torch.where(nz, -(g_q * y) / (dr * dr), zero))
+        part = torch.zeros((2, ctx.nrows), dtype=torch.float64, device=y.device)  # sums that cancel: fp64
+        part[0].index_add_(0, rows, torch.where(nz, gx * q, zero).double())
+        part[1].index_add_(0, rows, torch.where(nz, -(g_q * y) / (dr * dr), zero).double())
         dist.all_reduce(part, group=ctx.group)
         g_d = part[1] + torch.where(d <= 1.0, part[0], torch.zeros_like(part[0]))
-        gy = torch.where(nz, g_q / dr + g_d[rows], zero)
+        gy = torch.where(nz, (g_q.double() / dr.double() + g_d[rows]).to(y.dtype), zero)
         return gy, None, None, None, None
 
 

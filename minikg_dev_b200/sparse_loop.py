@@ -30,7 +30,7 @@ from .graph import DeviceGraph
 
 
 class _HopState:
-    __slots__ = ("keys_in", "vals_in", "prune_sel", "idx_y", "keys_y", "y", "d", "keep", "params", "n_pre", "seg")
+    __slots__ = ("keys_in", "vals_in", "prune_sel", "idx_y", "keys_y", "y", "d", "keep", "params", "n_pre")
 
 
 def _frontier_arrays(keys: torch.Tensor, L: int, E: int):
@@ -183,9 +183,8 @@ class SparseHopLoop(autograd.Function):
             msgs.append(m)
             y = st.y
             rows = st.keys_y // E
-            st.seg = torch.searchsorted(rows, torch.arange(B * L + 1, device=dev, dtype=rows.dtype))
             nz = y != 0
-            d = N.segment_sum(st.seg, y)  # rows are contiguous in key order; zeros add nothing
+            d = N.row_sums(st.keys_y, y, E, B * L).to(torch.float32)  # fp64 sums in key order, rounded once
             x = y / d[rows] * d.clamp_max(1.0)[rows]
             keep = nz & (x != 0)
             if threshold > 0:
@@ -229,10 +228,11 @@ class SparseHopLoop(autograd.Function):
             q = y / dr
             g_q = gx * c[rows]
             zero = torch.zeros_like(y)
-            g_c = N.segment_sum(st.seg, torch.where(nz, gx * q, zero))
-            g_d = N.segment_sum(st.seg, torch.where(nz, -(g_q * y) / (dr * dr), zero))
+            # row sums of the normalisation gradient in fp64 (they cancel: gradients of both signs)
+            g_c = N.row_sums(st.keys_y, torch.where(nz, gx * q, zero), E, B * L)
+            g_d = N.row_sums(st.keys_y, torch.where(nz, -(g_q * y) / (dr * dr), zero), E, B * L)
             g_d = g_d + torch.where(d <= 1.0, g_c, torch.zeros_like(g_c))
-            gy = torch.where(nz, g_q / dr + g_d[rows], torch.zeros_like(y))
+            gy = torch.where(nz, (g_q.double() / dr.double() + g_d[rows]).to(torch.float32), torch.zeros_like(y))
             grad_sp, gw, ge = _op_backward(g, st, ctx.wf[h], ctx.factor, gy, ctx.want_edge)
             grad_w[h] = gw
             if ge is not None:

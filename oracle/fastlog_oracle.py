@@ -31,16 +31,39 @@ Sums that the reference performs with ``scatter_add_`` / ``index_add_`` /
 ``index_put_(accumulate=True)`` on CPU are sequential in index order; this module
 reproduces them with ``np.add.at`` (sequential, float32).
 
+``float64_arithmetic()`` reruns the same restatement with every value held in float64
+(the per-hop cap decisions stay on the float32 rule weights, as the reference decides
+them): the exact value of the reference's computation, to which its own float32 results
+are rounded approximations.  The sum-loop gradient tests measure the CUDA path against
+it, because over several hops the reference's own float32 rounding already moves its
+gradients further from that value than the fp32 tolerance (measured in
+``tests/test_oracle_golden.py``).
+
 A sparse ``[B, L, E]`` tensor is a pair ``(keys, vals)``: sorted unique int64 keys
 ``(b*L + l)*E + e`` and float32 values.
 """
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 
-F32 = np.float32
+F32 = np.float32  # arithmetic type of the restatement (float64 inside float64_arithmetic())
 NUM_BUCKETS = 256
 UNCAPPED = 1 << 60
+
+
+@contextlib.contextmanager
+def float64_arithmetic():
+    """Run the restatement with float64 values and sums (test infrastructure: the exact
+    value of the reference computation for tolerance checks).  Not thread-safe."""
+    global F32
+    old = F32
+    F32 = np.float64
+    try:
+        yield
+    finally:
+        F32 = old
 
 
 # ----------------------------------------------------------------------------
@@ -132,7 +155,7 @@ def sigmoid_f32(x: np.ndarray) -> np.ndarray:
 
 def bucketize(x: np.ndarray) -> np.ndarray:
     """``min(max(int(x * 255.f), 0), 255)`` (fastlog.cu:16-20)."""
-    y = np.asarray(x, dtype=F32) * F32(NUM_BUCKETS - 1)
+    y = np.asarray(x, dtype=np.float32) * np.float32(NUM_BUCKETS - 1)  # float32 in every mode
     y = np.clip(y, -1.0, 256.0)
     return np.clip(np.trunc(y).astype(np.int64), 0, NUM_BUCKETS - 1)
 
@@ -557,7 +580,7 @@ def apply_threshold(state, threshold):
     if threshold <= 0:
         return state
     k, v = state
-    keep = v >= F32(threshold)
+    keep = v >= F32(np.float32(threshold))
     return k[keep], v[keep]
 
 

@@ -1,8 +1,10 @@
 """Parity of the CUDA path (through the C ABI) against the oracle and the golden vectors.
 
 Bar: integer / index / argmax / bucketing / decode results bit-exact; fp32 sums and
-gradients within rtol 1e-5, atol 1e-6 (multi-hop gradients, whose error compounds over
-three hops of sums, within rtol 1e-4, atol 1e-5).
+gradients within rtol 1e-5, atol 1e-6.  Hop-loop gradients are held to that bar against the
+oracle run in float64 arithmetic (``exact_loop_grads``): the reference's own fp32 result is a
+rounding of that value and already lies up to a few times the bar away from it after three
+hops of sums (measured in test_oracle_golden.py).
 """
 from __future__ import annotations
 
@@ -13,7 +15,7 @@ import pytest
 import torch
 
 from oracle import fastlog_oracle as O
-from tests.conftest import load_golden
+from tests.conftest import GRAD_ATOL, GRAD_RTOL, exact_loop_grads, load_golden, softmax_backward
 
 pytestmark = pytest.mark.gpu
 
@@ -334,12 +336,21 @@ def test_fused_loop_vs_golden(gname):
     seed = np.zeros((B, E), np.float32)
     seed[idx[0], idx[1]] = g["pr_unc_seed"]
     (out * T(seed)).sum().backward()
-    np.testing.assert_allclose(lg.grad.cpu().numpy(), g["pr_unc_grad_logits"], rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(sc.grad.cpu().numpy(), g["pr_unc_grad_edge"], rtol=1e-4, atol=1e-5)
+    # gradients: against the float64 run of the oracle on the golden inputs (the oracle's fp32
+    # run is pinned to the golden gradients in test_oracle_golden.py)
+    w_np = w_hops.detach().cpu().numpy()
+    csr = tuple(g[f"csr{k}"] for k in range(16))
+    gw, ge = exact_loop_grads(heads, w_np, csr, np.ones(g["head"].shape[0], bool), scores, B, L, E, R,
+                              idx[0] * E + idx[1], g["pr_unc_seed"], num_facts=g["head"].shape[0])
+    gl = softmax_backward(w_np, gw).transpose(1, 0, 2, 3)  # [K, B, L, n] -> [B, K, L, n]
+    np.testing.assert_allclose(lg.grad.cpu().numpy(), gl, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
-@pytest.mark.parametrize("gname", ["hubby", "g2"])
-@pytest.mark.parametrize("B,L,K", [(5, 3, 3), (40, 4, 2)])
+@pytest.mark.parametrize("gname,B,L,K", [(g, *s) for g in ("hubby", "g2") for s in ((5, 3, 3), (40, 4, 2))] +
+                         # 32 queries x 40 rules: a seed block's column segment spans 1,280 columns
+                         # (> 256 float4s), the backward seed's multi-pass path with global S sums
+                         [("g2", 32, 40, 2)])
 def test_fused_loop_vs_oracle(gname, B, L, K):
     from minikg_dev_b200.graph import DeviceGraph
     from minikg_dev_b200.proof import proof_scores
@@ -365,13 +376,12 @@ def test_fused_loop_vs_oracle(gname, B, L, K):
     exp_msgs = [O.count_messages(tr["state"], csr, w_hops[k], L, E, R) for k, tr in enumerate(trace)]
     assert msgs.cpu().tolist() == exp_msgs
     seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
-                                  num_facts=h.shape[0])
+    gw, ge = exact_loop_grads(heads, w_hops, csr, mask, scores, B, L, E, R, final[0], seed, num_facts=h.shape[0])
     gd = np.zeros((B, E), np.float32)
     gd[b, e] = seed
     (out * T(gd)).sum().backward()
-    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
 @pytest.mark.parametrize("gname", ["hubby", "g2"])
@@ -401,10 +411,10 @@ def test_sparse_loop_vs_oracle(gname, cap, topk_nodes, accum):
                                    for k, tr in enumerate(trace)]
     seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
     (out.values() * T(seed)).sum().backward()
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
-                                  num_facts=h.shape[0])
-    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+    gw, ge = exact_loop_grads(heads, w_hops, csr, mask, scores, B, L, E, R, final[0], seed, num_facts=h.shape[0],
+                              cap=cap, topk_nodes=topk_nodes)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
 @pytest.mark.parametrize("gname", ["hubby", "g2"])
@@ -436,13 +446,13 @@ def test_fused_capped_loop_vs_oracle(gname, cap):
     assert msgs.cpu().tolist() == [O.count_messages(tr["state"], csr, w_hops[k], L, E, R, cap=cap)
                                    for k, tr in enumerate(trace)]
     seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
-                                  num_facts=h.shape[0])
+    gw, ge = exact_loop_grads(heads, w_hops, csr, mask, scores, B, L, E, R, final[0], seed, num_facts=h.shape[0],
+                              cap=cap)
     gd = np.zeros((B, E), np.float32)
     gd[b, e] = seed
     (out * T(gd)).sum().backward()
-    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
 @pytest.mark.parametrize("gname", ["hubby", "g2"])
@@ -636,8 +646,14 @@ def test_kernel_sparse_scores_drop_in(gname, tag, cap, topk_nodes, accum):
         np.testing.assert_array_equal(idx, gi)
         np.testing.assert_allclose(out.values().detach().cpu().numpy(), g[tag + "_final_val"], rtol=RTOL, atol=ATOL)
         (out.values() * T(g[tag + "_seed"])).sum().backward()
-        np.testing.assert_allclose(lg.grad.cpu().numpy(), g[tag + "_grad_logits"], rtol=1e-4, atol=1e-5)
-        np.testing.assert_allclose(wt.grad.cpu().numpy(), g[tag + "_grad_edge"], rtol=1e-4, atol=1e-5)
+        w_np = _w_hops_from_logits(logits)
+        csr = tuple(g[f"csr{k}"] for k in range(16))
+        gw, ge = exact_loop_grads(heads, w_np, csr, np.ones(g["head"].shape[0], bool), scores, B, L, E, R,
+                                  idx[0] * E + idx[1], g[tag + "_seed"], num_facts=g["head"].shape[0],
+                                  topk_nodes=topk_nodes)
+        gl = softmax_backward(w_np, gw).transpose(1, 0, 2, 3)
+        np.testing.assert_allclose(lg.grad.cpu().numpy(), gl, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+        np.testing.assert_allclose(wt.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
     else:
         # capped: compare against the oracle on the build's own (stable) CSR
         csr = O.build_csr_structure(g["head"], g["tail"], g["rel"], E)
@@ -766,10 +782,10 @@ def test_loops_masked_facts_and_sigmoid_path(variant, engine):
         np.testing.assert_allclose(out.values().detach().cpu().numpy(), final[1], rtol=RTOL, atol=ATOL)
         seed = rng.standard_normal(final[0].shape[0]).astype(np.float32)
         (out.values() * T(seed)).sum().backward()
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, ew, B, L, E, R, is_score=is_score,
-                                  scale=scale, num_facts=h.shape[0])
-    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=1e-4, atol=1e-5)
+    gw, ge = exact_loop_grads(heads, w_hops, csr, mask, ew, B, L, E, R, final[0], seed, num_facts=h.shape[0],
+                              cap=cap, is_score=is_score, scale=scale, threshold=thr)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
 # ----------------------------------------------------------------------------- tracing, determinism
@@ -858,8 +874,8 @@ def test_fused_step_graph_replay_matches_eager():
         o2, _ = runner.forward(heads, w_hops)
         gw2, ge2 = runner.backward(G, None, sc, True, 1.0, True)
         np.testing.assert_allclose(got[0].cpu().numpy(), o2.cpu().numpy(), rtol=RTOL, atol=ATOL)
-        np.testing.assert_allclose(got[1].cpu().numpy(), gw2.cpu().numpy(), rtol=1e-4, atol=1e-5)
-        np.testing.assert_allclose(got[2].cpu().numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(got[1].cpu().numpy(), gw2.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
+        np.testing.assert_allclose(got[2].cpu().numpy(), ge2.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
 def test_fused_step_graph_host_copies():
@@ -908,8 +924,8 @@ def test_fused_step_graph_host_copies():
         _, m2 = runner.forward(heads2, w2)
         gw2, ge2 = runner.backward(G, None, sc2, True, 1.0, True)
         assert torch.equal(got[0], m2.cpu())
-        np.testing.assert_allclose(got[1].numpy(), gw2.cpu().numpy(), rtol=1e-4, atol=1e-5)
-        np.testing.assert_allclose(got[2].numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(got[1].numpy(), gw2.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
+        np.testing.assert_allclose(got[2].numpy(), ge2.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
 def test_fused_step_after_denser_step_matches_fresh_runner():
@@ -945,8 +961,8 @@ def test_fused_step_after_denser_step_matches_fresh_runner():
     (o1, m1, gw1, ge1), (o2, m2, gw2, ge2) = res
     assert torch.equal(m1, m2)
     np.testing.assert_allclose(o1.cpu().numpy(), o2.cpu().numpy(), rtol=RTOL, atol=ATOL)
-    np.testing.assert_allclose(gw1.cpu().numpy(), gw2.cpu().numpy(), rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(ge1.cpu().numpy(), ge2.cpu().numpy(), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(gw1.cpu().numpy(), gw2.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(ge1.cpu().numpy(), ge2.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
 # ----------------------------------------------------------------------------- decode candidates

@@ -18,7 +18,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from oracle import fastlog_oracle as O
-from tests.conftest import load_golden
+from tests.conftest import GRAD_ATOL, GRAD_RTOL, exact_loop_grads, load_golden
 
 
 def _free_port() -> int:
@@ -143,11 +143,12 @@ def test_sharded_loop_matches_single_process_oracle(world, cfg):
     np.testing.assert_array_equal(keys, final[0])
     np.testing.assert_allclose(vals, final[1], rtol=1e-5, atol=1e-6)
     seed_all = np.random.default_rng(99).standard_normal(B * E).astype(np.float32)
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed_all[final[0]]), w, csr, mask, scores, B, L, E, R,
-                                  num_facts=h.shape[0])
+    gw, ge = exact_loop_grads(heads, w, csr, mask, scores, B, L, E, R, final[0], seed_all[final[0]],
+                              num_facts=h.shape[0], cap=cfg["cap"], topk_nodes=cfg["topk_nodes"],
+                              threshold=cfg["threshold"])
     for x in res:  # the replicated inputs carry the full gradient on every rank
-        np.testing.assert_allclose(x[4], gw, rtol=1e-4, atol=1e-5)
-        np.testing.assert_allclose(x[5], ge, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(x[4], gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+        np.testing.assert_allclose(x[5], ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
     # the merge is exact: compare with the oracle's decode of the same (gathered) raw scores
     ot, osc, oc = O.decode_topk((keys, vals), B, E, cfg["k"])
     for x in res:
