@@ -8,11 +8,13 @@
 // Every GPU that loads this library holds that array until the process exits.
 //
 // In host code the array's name is only a host-side stand-in, not a device address, so the
-// address is looked up with cudaGetSymbolAddress once per device, on the first call made
-// while that device is current; that first call should therefore come before any stream
-// capture.  All calls share the array and it keeps the last call's contents: the counts
-// are cleared on every call, and calls that overlap on the GPU (for instance on two
-// streams at once) race on it.
+// address is looked up with cudaGetSymbolAddress while the call's device is current.  The
+// lookup is repeated on every call made outside a stream capture (after a cudaDeviceReset the
+// module is loaded again and the array can move); a call made while its stream is being
+// captured reuses the address of the last call outside a capture on that device, so the
+// first call on a device should come before any stream capture.  All calls share the array
+// and it keeps the last call's contents: the counts are cleared on every call, and calls
+// that overlap on the GPU (for instance on two streams at once) race on it.
 #include <mutex>
 
 #include <cub/cub.cuh>
@@ -34,16 +36,19 @@ constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mutex;
 void* g_noalloc_addr[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch for the current device (looked up once per device).
-int noalloc_scratch(void** out) {
+// Device address of g_noalloc_scratch for the current device: looked up again on every call
+// outside a stream capture, taken from the last such lookup while `st` is capturing.
+int noalloc_scratch(cudaStream_t st, void** out) {
   int dev = 0;
   MKG_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) {
     set_error("ind2ptr_noalloc: device ordinal %d out of range", dev);
     return MKG_ERR_ARG;
   }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  MKG_CUDA(cudaStreamIsCapturing(st, &cap));
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (cap == cudaStreamCaptureStatusNone || g_noalloc_addr[dev] == nullptr) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
@@ -84,7 +89,7 @@ MKG_API int mkg_ind2ptr_noalloc(const int64_t* index, int64_t n, int64_t size, i
     return MKG_ERR_CAPACITY;
   }
   void* base = nullptr;
-  int rc = noalloc_scratch(&base);
+  int rc = noalloc_scratch(st, &base);
   if (rc) return rc;
   int64_t* cnt = static_cast<int64_t*>(base);
   void* temp = static_cast<char*>(base) + kCountBytes;

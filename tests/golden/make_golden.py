@@ -1,8 +1,8 @@
 """Golden vectors for the relation-typed sparse hop, produced by the reference's own code.
 
-Run in a container that holds the reference checkout (it does not travel):
+Run where a checkout of the reference exists (it does not travel):
 
-    python tests/golden/make_golden.py --ref /root/reference
+    python tests/golden/make_golden.py --ref <path of the reference checkout>
 
 The reference's hop op (``FastLogFunctionSparse3DTopK``, fastlog_kernel.py:900-1107)
 calls a CUDA extension.  With no GPU here, the extension object it loads is replaced
@@ -454,7 +454,7 @@ def rules_case(ref, out, tag, R, H, K, L, B, tau, scale, seed, penalty=0.0, inve
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository (majh3/miniKG_dev)")
     ap.add_argument("--out", default=str(HERE))
     ap.add_argument("--only", choices=("all", "prune", "accum", "rules"), default="all")
     a = ap.parse_args()
