@@ -130,9 +130,11 @@ int mkg_ind2ptr(const int64_t* index, int64_t n, int64_t size, int64_t* ptr, voi
  * holding only the device pointers it was given): same inputs and output as mkg_ind2ptr,
  * no workspace argument.  No counterpart in the reference.  Its scratch is one static
  * device array of about 8.3 MiB that every GPU loading the library keeps until exit;
- * size is limited to MKG_NOALLOC_MAX_ROWS rows (larger: MKG_ERR_CAPACITY).  The first call
- * on a device looks the array up and should come before any stream capture; calls that
- * overlap on the GPU share the array and race. */
+ * size is limited to MKG_NOALLOC_MAX_ROWS rows (larger: MKG_ERR_CAPACITY).  Every call made
+ * outside a stream capture looks the array's device address up again (it can move after a
+ * cudaDeviceReset); a call inside a capture reuses the last such address, so the first call
+ * on a device should come before any stream capture.  Calls that overlap on the GPU share
+ * the array and race. */
 #define MKG_NOALLOC_MAX_ROWS (1 << 20)
 int mkg_ind2ptr_noalloc(const int64_t* index, int64_t n, int64_t size, int64_t* ptr, unsigned* dev_err,
                         mkg_stream stream);
@@ -365,6 +367,87 @@ int mkg_segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* v
  * key-sorted sparse state, without atomics on the few row bins.  No reference counterpart
  * (the reference coalesces and index_puts). */
 int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, mkg_stream stream);
+
+/* ------------------------------------------------------------ key-slab hop engine */
+
+/* The uncapped sum hop of kernel_sparse_scores (proof.py:569-609: the op of
+ * FastLogFunctionSparse3DTopK forward, fastlog.cu:2678-2806 with topk_edges uncapped, then the
+ * coalescing of _coalesce_sparse3d_reduce, fastlog_kernel.py:81-104, and sum_sparse3d_concat,
+ * fastlog_bridge.py:26-42) for large graphs with sparse frontiers.  Output keys of one call
+ * lie in a window: (b, l) rows [row0, row0 + nrows) x destination entities [lo, lo + extent)
+ * of a key space (row) * E + e.  A *store* of mkg_slab_store_bytes(nrows * extent) bytes
+ * holds one fp32 slot per key and a touched bit per slot; the caller zero-fills it once and
+ * every mkg_slab_emit / clearing mkg_slab_take leaves what it read at zero again. */
+typedef struct mkg_slab_window {
+  int64_t E;       /* entities of the key space */
+  int64_t row0;    /* first row (b * L + l, or b for [B, E] keys) of the window */
+  int64_t nrows;   /* rows in the window */
+  int64_t lo;      /* first destination entity */
+  int64_t extent;  /* destination entities [lo, lo + extent) */
+} mkg_slab_window;
+
+size_t mkg_slab_store_bytes(int64_t slots);
+size_t mkg_slab_expand_workspace_bytes(int64_t nnz);
+/* Adds every message of the frontier (keys (b * L + l) * E + s with values, all in the
+ * window's rows) to the store: for each record of push row s (mkg_adjacency.push, or a push
+ * list restricted to destinations in [lo, lo + extent)) the value (x * w[b, l, channel]) *
+ * factor at key (b, l, neighbour), plus (identity != 0) x * w[b, l, n - 1] at (b, l, s).
+ * w is [B * L, n].  Zero-valued messages are left out (the hop loop drops zeros after its
+ * normalisation).  Replaces the forward op of the uncapped hop (see above). */
+int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, const int64_t* keys, const float* vals,
+                    int64_t nnz, const float* w, int64_t n, int32_t identity, const mkg_slab_window* win,
+                    void* store, void* workspace, size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+/* Number of touched keys in the store -> count_out (device int64).  The workspace (also read
+ * by mkg_slab_emit) keeps per-tile offsets. */
+size_t mkg_slab_collect_workspace_bytes(int64_t slots);
+int mkg_slab_count(const mkg_slab_window* win, const void* store, void* workspace, size_t workspace_bytes,
+                   int64_t* count_out, mkg_stream stream);
+/* Writes the touched keys in ascending order (global keys (row0 + r) * E + lo + e) with their
+ * values, clears them in the store and, when row_sums != NULL, adds each row's values to
+ * row_sums[r] in fp64 (the column sums of normalize_sparse3d, drum.py:31-51). */
+int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* workspace, size_t workspace_bytes,
+                  int64_t count, int64_t* keys_out, float* vals_out, double* row_sums, mkg_stream stream);
+/* Writes (mode 0) or adds with a touched mark (mode 1) values at keys whose row is
+ * (key / E) / row_div (row_div = L maps (b, l, e) to the [B, E] key b * E + e: sum_sp_3d,
+ * fastlog_bridge.py:17-23). */
+int mkg_slab_put(const mkg_slab_window* win, void* store, const int64_t* keys, const float* vals, int64_t nnz,
+                 int64_t row_div, int32_t mode, unsigned* dev_err, mkg_stream stream);
+/* out[i] = the store's value at keys[i] (row (key / E) / row_div), cleared when clear != 0;
+ * out may be NULL (clear only). */
+int mkg_slab_take(const mkg_slab_window* win, void* store, const int64_t* keys, int64_t nnz, int64_t row_div,
+                  float* out, int32_t clear, unsigned* dev_err, mkg_stream stream);
+/* Backward of mkg_slab_expand with the hop's output gradient held in the store (mode 0 puts):
+ * grad_sp[i] += sum g m w[ch], grad_w[(b * L + l) * n + ch] += sum (g m) x, grad_edge[f] +=
+ * g x w[ch] m dm/df -- replaces fastlog_backward_sparse3d_topk_cuda (fastlog.h:123-134,
+ * fastlog.cu:3037-3109) with the edge-score gradient of fastlog_kernel.py:1032-1098.
+ * grad_sp and grad_w are fp64 accumulators, grad_edge fp32; all are added to, not set. */
+int mkg_slab_expand_backward(const int32_t* push_ptr, const mkg_adj_edge* push, const int64_t* keys,
+                             const float* vals, int64_t nnz, const float* w, int64_t n, int32_t identity,
+                             const mkg_slab_window* win, const void* store, const mkg_edge_factor* ef,
+                             int64_t num_facts, double* grad_sp, double* grad_w, float* grad_edge, void* workspace,
+                             size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+/* out[r] += sum of vals over the entries of row r (key / E - row0) in fp64; keys ascending.
+ * The per-(b, l) sums of normalize_sparse3d and of its gradient (drum.py:31-51). */
+int mkg_row_sums(const int64_t* keys, int64_t nnz, int64_t E, int64_t row0, int64_t nrows, const float* vals,
+                 double* out, unsigned* dev_err, mkg_stream stream);
+/* out[i] = (float) in[i]. */
+int mkg_f64_to_f32(const double* in, int64_t n, float* out, mkg_stream stream);
+
+/* ------------------------------------------------------------ bridge reducers */
+
+/* Reduce-by-key of COO entries: replaces the torch coalescing behind sum_sparse3d_concat /
+ * sum_sp_3d (src/fastlog_bridge.py:17-42) and the argsort / unique_consecutive /
+ * scatter_reduce sequence of max_sp_3d / sparse3d_max (src/model_mmDRUM_kernel_sp.py:85-140,
+ * 184-270).  keys (int64, >= 0, below 2^key_bits) with values; outputs in ascending key
+ * order, one per distinct key: mode 0 the sum (fp64, rounded once), mode 1 the maximum, ties
+ * to the earliest entry in input order.  out_keys / out_vals hold up to n entries;
+ * count_out (device int64) receives the number written.  inverse [n] (may be NULL): output
+ * index of each input entry; arg [n] (mode 1, may be NULL): the input entry that won each
+ * output. */
+size_t mkg_reduce_by_key_workspace_bytes(int64_t n);
+int mkg_reduce_by_key(const int64_t* keys, const float* vals, int64_t n, int32_t mode, int32_t key_bits,
+                      int64_t* out_keys, float* out_vals, int64_t* count_out, int64_t* inverse, int64_t* arg,
+                      void* workspace, size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
 
 /* ------------------------------------------------------------ rule-weight producer */
 

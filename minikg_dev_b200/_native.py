@@ -78,6 +78,10 @@ class CapIndex(C.Structure):
                 ("slot_group", vp), ("pull_cap", vp), ("push_cap", vp), ("capped_degree", vp)]
 
 
+class SlabWindow(C.Structure):
+    _fields_ = [("E", i64), ("row0", i64), ("nrows", i64), ("lo", i64), ("extent", i64)]
+
+
 class RuleParams(C.Structure):
     _fields_ = [("n", i64), ("H", i64), ("L", i64), ("K", i64), ("U", i64), ("B", i64), ("tau", C.c_float),
                 ("reserved", i32)]
@@ -122,6 +126,20 @@ SIGNATURES = {
     "mkg_cap_index_workspace_bytes": (C.c_size_t, [P(Graph)]),
     "mkg_cap_index_sizes": (C.c_int, [P(Graph), i64, vp, vp, C.c_size_t, vp]),
     "mkg_cap_index_build": (C.c_int, [P(Graph), P(Adjacency), P(CapIndex), vp, C.c_size_t, vp, vp]),
+    "mkg_slab_store_bytes": (C.c_size_t, [i64]),
+    "mkg_slab_expand_workspace_bytes": (C.c_size_t, [i64]),
+    "mkg_slab_expand": (C.c_int, [vp, vp, vp, vp, i64, vp, i64, i32, P(SlabWindow), vp, vp, C.c_size_t, vp, vp]),
+    "mkg_slab_collect_workspace_bytes": (C.c_size_t, [i64]),
+    "mkg_slab_count": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, vp, vp]),
+    "mkg_slab_emit": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, i64, vp, vp, vp, vp]),
+    "mkg_slab_put": (C.c_int, [P(SlabWindow), vp, vp, vp, i64, i64, i32, vp, vp]),
+    "mkg_slab_take": (C.c_int, [P(SlabWindow), vp, vp, i64, i64, vp, i32, vp, vp]),
+    "mkg_slab_expand_backward": (C.c_int, [vp, vp, vp, vp, i64, vp, i64, i32, P(SlabWindow), vp, P(EdgeFactor),
+                                           i64, vp, vp, vp, vp, C.c_size_t, vp, vp]),
+    "mkg_row_sums": (C.c_int, [vp, i64, i64, i64, i64, vp, vp, vp, vp]),
+    "mkg_f64_to_f32": (C.c_int, [vp, i64, vp, vp]),
+    "mkg_reduce_by_key_workspace_bytes": (C.c_size_t, [i64]),
+    "mkg_reduce_by_key": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, C.c_size_t, vp, vp]),
     "mkg_rule_saved_bytes": (C.c_size_t, [P(RuleParams)]),
     "mkg_rule_backward_workspace_bytes": (C.c_size_t, [P(RuleParams)]),
     "mkg_rule_softmax_workspace_bytes": (C.c_size_t, [P(RuleParams)]),
@@ -216,6 +234,17 @@ def segment_sum(seg_ptr: torch.Tensor, values: torch.Tensor, ordered: bool = Fal
     fn = load().mkg_segment_sum_ordered if ordered else load().mkg_segment_sum
     check(fn(sp.data_ptr(), nseg, v.data_ptr(), out.data_ptr(), stream_handle(v.device)), "segment_sum")
     return out
+
+
+def row_sums(keys: torch.Tensor, values: torch.Tensor, E: int, nrows: int, row0: int = 0) -> torch.Tensor:
+    """fp64 [nrows]: the sum of ``values`` over each row ``key // E - row0`` of the ascending
+    ``keys`` (int64 device tensors), accumulated in fp64."""
+    k = keys.to(torch.int64).contiguous()
+    v = values.detach().to(torch.float32).contiguous()
+    out = torch.zeros(max(int(nrows), 1), dtype=torch.float64, device=v.device)
+    check(load().mkg_row_sums(k.data_ptr(), int(k.numel()), int(E), int(row0), int(nrows), v.data_ptr(),
+                              out.data_ptr(), error_word(v.device).data_ptr(), stream_handle(v.device)), "row_sums")
+    return out[: int(nrows)]
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:

@@ -115,6 +115,7 @@ class DeviceGraph:
         self._adj_keep = None
         self._facts = None
         self._cap = {}
+        self.factor_writes = 0  # set_edge_factor calls so far (a caller can tell its factors are current)
 
     @classmethod
     def from_triples(cls, head: torch.Tensor, rel: torch.Tensor, tail: torch.Tensor, num_entities: int,
@@ -220,6 +221,7 @@ class DeviceGraph:
         f = N.edge_factor(mask, weight, is_score, scale, keep)
         N.check(lib.mkg_adjacency_set_factor(C_ref(self.struct), self.adjacency(), C_ref(f),
                                              N.stream_handle(self.device)), "adjacency_set_factor")
+        self.factor_writes += 1
 
     # -------------------------------------------------------------- per-fact endpoints
     def fact_table(self):

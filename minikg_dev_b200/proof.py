@@ -401,6 +401,12 @@ def kernel_sparse_scores(model, heads, rels, graph, args, is_training: bool, den
     if fused:
         out, _ = HopLoopSum.apply(w_all, edge_scores, heads, g, mask, is_score, scale, 0.0, cap)
         return out if dense else out.to_sparse_coo().coalesce()
+    if cap == UNCAPPED and not (is_training and p_drop > 0):
+        # uncapped hops on a graph the dense state does not take: the key-slab loop
+        from .slab_loop import slab_engine, slab_proof_scores
+        out, _ = slab_proof_scores(slab_engine(g), heads, w_all, edge_scores, mask, is_score, scale, topk_nodes,
+                                   0.0, dense=dense)
+        return out
     if not (is_training and p_drop > 0):
         # larger caps, pruning or a graph too large for the dense state: the sparse loop fused
         # around the op (merged outputs, written-out backward)

@@ -1,0 +1,491 @@
+"""The uncapped sum hop loop on the key-slab engine (large graphs, sparse frontiers).
+
+``kernel_sparse_scores`` (proof.py:467-614, sum path, dropout off) composes per hop the
+``prune_sparse3d_active_entities`` prune (drum.py:54-80), the op (fastlog_kernel.py:900-984
+with ``topk_edges`` uncapped), ``sum_sparse3d_concat`` (fastlog_bridge.py:26-42) and
+``normalize_sparse3d(.., 0, "mass")`` (drum.py:31-51), then ``sum_sp_3d``
+(fastlog_bridge.py:17-23).  ``SlabHopLoop`` runs that loop on the key-slab kernels of
+``csrc/mkg_slab.cu``:
+
+* a hop's messages (ori, inv and identity at once: the concat-sum) are added into a store
+  with one fp32 slot per output key of a window of (b, l) rows and a touched bit per slot;
+  the touched keys come out key-sorted by a bitmap popcount scan, with fp64 row sums for the
+  normalisation, and the store is left zeroed for the next use -- no sort, no hash table;
+* the normalisation is elementwise on the emitted values; the final sum over rules is one
+  more pass through the store (keys ``(b, l, e)`` added at ``(b, e)``);
+* the backward is written out: the normalisation gradient with fp64 row sums, then the
+  transposed walk with the output gradient held in the store (fp64 entry and rule-weight
+  accumulators), hop by hop down to the first.
+
+With a ``ShardSpec`` the loop is destination-partitioned over ranks (one process per GPU):
+rank k owns the entities ``[lo_k, hi_k)``, keeps only the push records whose destination it
+owns (so every message is walked by exactly one rank), all-gathers the frontier each hop and
+all-reduces the normalisation's row sums; the backward all-reduces the frontier gradient, the
+row sums of the normalisation gradient, and at the end the rule-weight and edge-score
+gradients.  Every rank issues the same collectives in the same order.  With one process the
+same code runs without collectives.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import autograd
+
+from . import _native as N
+from .graph import DeviceGraph
+
+STORE_FRACTION = 0.45   # at most this share of the free device memory for the slab store
+
+
+class SlabEngine:
+    """Resident state of the key-slab loop on one GPU: the push list (the graph's, or only the
+    records whose destination lies in ``[lo, hi)``), a zero-kept slab store and its window size.
+
+    ``store_bytes`` caps the store (default: ``STORE_FRACTION`` of the free memory when first
+    sized); a window then covers as many (b, l) rows of the destination range as fit, and a
+    hop whose rows exceed it runs window by window."""
+
+    def __init__(self, graph: DeviceGraph, lo: int = 0, hi: int = 0, store_bytes: int | None = None):
+        self.g = graph
+        self.dev = graph.device
+        E = graph.num_entities
+        self.lo, self.hi = (int(lo), int(hi)) if hi > lo else (0, E)
+        self.extent = self.hi - self.lo
+        graph.adjacency()
+        keep = graph._adj_keep
+        self.full_ptr = keep["push_ptr"]
+        self.full_push = keep["push"]
+        self.full_degree = (self.full_ptr[1:] - self.full_ptr[:-1]).to(torch.int64)
+        if self.lo == 0 and self.hi == E:
+            self.ptr, self.push, self.sel = self.full_ptr, self.full_push, None
+        else:
+            nbr = self.full_push[:, 0]
+            mine = (nbr >= self.lo) & (nbr < self.hi)
+            self.sel = torch.nonzero(mine, as_tuple=True)[0]
+            self.push = self.full_push[self.sel].contiguous()
+            rows = torch.repeat_interleave(torch.arange(E, device=self.dev), self.full_degree)
+            cnt = torch.bincount(rows[self.sel], minlength=E)
+            self.ptr = torch.zeros(E + 1, dtype=torch.int32, device=self.dev)
+            self.ptr[1:] = torch.cumsum(cnt, 0).to(torch.int32)
+            del rows, cnt, mine, nbr
+        self._store_cap = store_bytes
+        self._budget_bound = False
+        self.store = None
+        self.rows_per_window = 0
+        # when a list: (kind, hop-local index, start event, end event, algorithmic bytes) per
+        # expansion launch, for roofline accounting (adds host synchronisations; off by default)
+        self.trace = None
+        self._groups = None
+
+    @property
+    def records(self) -> int:
+        return int(self.push.shape[0])
+
+    def set_edge_factor(self, mask, weight, is_score: bool, scale: float) -> None:
+        """Rewrites the factor field of the push records from the mask / edge scores."""
+        self.g.set_edge_factor(mask, weight, is_score, scale)
+        if self.sel is not None:
+            self.push[:, 3] = self.full_push[self.sel, 3]
+
+    def ensure_store(self, rows: int) -> None:
+        """Sizes the zero-kept store: ``rows`` (b, l) rows of the destination range, or as many
+        as the budget holds (then kept: the budget does not grow)."""
+        lib = N.load()
+        if self.store is not None and (self.rows_per_window >= rows or self._budget_bound):
+            return
+        budget = self._store_cap
+        if budget is None:
+            free, _ = torch.cuda.mem_get_info(self.dev)
+            budget = int(STORE_FRACTION * (free + (self.store.numel() if self.store is not None else 0)))
+        per_row = int(lib.mkg_slab_store_bytes(self.extent * 64)) / 64.0
+        fit = max(1, min(int(rows), int(budget // per_row)))
+        self._budget_bound = fit < rows
+        self.store = None
+        nbytes = int(lib.mkg_slab_store_bytes(fit * self.extent))
+        self.store = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
+        self.rows_per_window = fit
+
+    def window(self, row0: int, nrows: int) -> N.SlabWindow:
+        return N.SlabWindow(self.g.num_entities, int(row0), int(nrows), self.lo, self.extent)
+
+
+# ----------------------------------------------------------------------------- kernels, windowed
+def _windows(total_rows: int, per: int):
+    for r0 in range(0, total_rows, per):
+        yield r0, min(per, total_rows - r0)
+
+
+def _row_slices(keys: torch.Tensor, E: int, div: int, bounds) -> list[tuple[int, int]]:
+    """Positions [a, b) of the ascending ``keys`` whose row ``(key // E) // div`` falls in each
+    window ``[r0, r0 + n)``."""
+    if keys.numel() == 0:
+        return [(0, 0) for _ in bounds]
+    edges = torch.tensor([r0 * div * E for r0, _ in bounds] + [(bounds[-1][0] + bounds[-1][1]) * div * E],
+                         dtype=torch.int64, device=keys.device)
+    pos = torch.searchsorted(keys, edges).tolist()
+    return [(pos[i], pos[i + 1]) for i in range(len(bounds))]
+
+
+def _events(eng: SlabEngine):
+    if eng.trace is None:
+        return None
+    ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    ev[0].record()
+    return ev
+
+
+def _collect(eng: SlabEngine, win, want_rows: bool):
+    """Emits the touched keys of the store (ascending) with values and fp64 row sums."""
+    lib = N.load()
+    dev = eng.dev
+    st = N.stream_handle(dev)
+    slots = win.nrows * win.extent
+    ws = N.workspace(lib.mkg_slab_collect_workspace_bytes(slots), dev)
+    cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+    N.check(lib.mkg_slab_count(ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(), ws.numel(), cnt.data_ptr(),
+                               st), "slab_count")
+    U = int(cnt.item())
+    keys = torch.empty(U, dtype=torch.int64, device=dev)
+    vals = torch.empty(U, dtype=torch.float32, device=dev)
+    rs = torch.zeros(win.nrows, dtype=torch.float64, device=dev) if want_rows else None
+    N.check(lib.mkg_slab_emit(ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(), ws.numel(), U,
+                              keys.data_ptr(), vals.data_ptr(), N.ptr(rs), st), "slab_emit")
+    return keys, vals, rs
+
+
+def graph_bytes(eng: SlabEngine, keys) -> int:
+    """Compulsory graph bytes of a hop whose frontier holds ``keys``: per distinct source its
+    records (4 B neighbour + 4 B edge score each), relation groups (10 B each: 2 B relation, 4 B
+    start, 4 B count) and row pointers (8 B)."""
+    if keys.numel() == 0:
+        return 0
+    E = eng.g.num_entities
+    if eng._groups is None:
+        c = eng.g.csr
+        eng._groups = ((c[8][1:] - c[8][:-1]) + (c[12][1:] - c[12][:-1])).to(torch.int64)
+    src = torch.unique(keys % E)
+    deg = (eng.ptr[1:] - eng.ptr[:-1]).to(torch.int64)[src]
+    grp = torch.where(deg > 0, eng._groups[src], torch.zeros_like(deg))
+    return int((deg * 8 + grp * 10 + 8).sum())
+
+
+def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int):
+    """One hop's concat-summed output over the engine's destinations: (keys ascending, values,
+    fp64 row sums [BL])."""
+    lib = N.load()
+    dev = eng.dev
+    E = eng.g.num_entities
+    n = int(w_h.shape[-1])
+    wf = w_h.detach().to(torch.float32).reshape(BL, n).contiguous()
+    if keys.numel() and (int(keys[0]) < 0 or int(keys[-1]) >= BL * E):
+        raise RuntimeError("slab hop: a frontier key lies outside [B, L, E]")
+    eng.ensure_store(BL)
+    bounds = list(_windows(BL, eng.rows_per_window))
+    slices = _row_slices(keys, E, 1, bounds)
+    out_k, out_v = [], []
+    d = torch.zeros(BL, dtype=torch.float64, device=dev)
+    st = N.stream_handle(dev)
+    err = N.error_word(dev).data_ptr()
+    for (r0, nr), (a, b) in zip(bounds, slices):
+        win = eng.window(r0, nr)
+        if b > a:
+            k = keys[a:b].contiguous()
+            v = vals[a:b].detach().to(torch.float32).contiguous()
+            ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(b - a), dev)
+            ev = _events(eng)
+            N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), b - a,
+                                        wf.data_ptr(), n, 1, ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(),
+                                        ws.numel(), err, st), "slab_expand")
+            if ev is not None:
+                ev[1].record()
+            ko, vo, rs = _collect(eng, win, True)
+            if ev is not None:  # frontier in + output out (12 B per key: 8 B key, 4 B value), rule weights
+                eng.trace.append(("fwd", ev[0], ev[1], graph_bytes(eng, k) + 12 * (b - a) + 12 * ko.numel()
+                                  + nr * n * 4))
+            out_k.append(ko)
+            out_v.append(vo)
+            d[r0:r0 + nr] = rs
+    if not out_k:
+        return (torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev), d)
+    return torch.cat(out_k), torch.cat(out_v), d
+
+
+def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, gy, factor, grad_w64, grad_edge):
+    """Transposed walk of one hop: the frontier entries' fp64 gradient; adds to ``grad_w64``
+    ([BL, n], fp64) and ``grad_edge`` ([T], fp32)."""
+    lib = N.load()
+    dev = eng.dev
+    E = eng.g.num_entities
+    n = int(w_h.shape[-1])
+    wf = w_h.detach().to(torch.float32).reshape(BL, n).contiguous()
+    bounds = list(_windows(BL, eng.rows_per_window))
+    sl_in = _row_slices(keys, E, 1, bounds)
+    sl_y = _row_slices(keys_y, E, 1, bounds)
+    gsp = torch.zeros(keys.numel(), dtype=torch.float64, device=dev)
+    st = N.stream_handle(dev)
+    err = N.error_word(dev).data_ptr()
+    gyf = gy.to(torch.float32).contiguous()
+    for (r0, nr), (a, b), (ya, yb) in zip(bounds, sl_in, sl_y):
+        if b <= a:
+            continue
+        win = eng.window(r0, nr)
+        ky = keys_y[ya:yb]
+        if yb > ya:
+            N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), gyf[ya:yb].data_ptr(),
+                                     yb - ya, 1, 0, err, st), "slab_put")
+        k = keys[a:b].contiguous()
+        v = vals[a:b].detach().to(torch.float32).contiguous()
+        ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(b - a), dev)
+        g_part = gsp[a:b]
+        ev = _events(eng)
+        N.check(lib.mkg_slab_expand_backward(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                             b - a, wf.data_ptr(), n, 1, ctypes.byref(win), eng.store.data_ptr(),
+                                             ctypes.byref(factor), eng.g.num_facts, g_part.data_ptr(),
+                                             grad_w64.data_ptr(), N.ptr(grad_edge), ws.data_ptr(), ws.numel(), err,
+                                             st), "slab_expand_backward")
+        if ev is not None:  # grad-in at the outputs, frontier re-read, grad-out, weights, edge grads
+            ev[1].record()
+            eng.trace.append(("bwd", ev[0], ev[1], graph_bytes(eng, k) + 12 * (yb - ya) + 12 * (b - a) + 4 * (b - a)
+                              + nr * n * 4 + (4 * eng.g.num_facts if grad_edge is not None else 0)))
+        if yb > ya:
+            N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), yb - ya, 1, None, 1,
+                                      err, st), "slab_take")
+    return gsp
+
+
+def sum_over_rules(eng: SlabEngine, keys, vals, B: int, L: int):
+    """sum_sp_3d: ``(b, l, e)`` entries added at ``(b, e)``; returns ascending ``b * E + e`` keys
+    and values (the store's windows then run over queries)."""
+    lib = N.load()
+    dev = eng.dev
+    E = eng.g.num_entities
+    eng.ensure_store(B)
+    bounds = list(_windows(B, eng.rows_per_window))
+    slices = _row_slices(keys, E, L, bounds)
+    st = N.stream_handle(dev)
+    err = N.error_word(dev).data_ptr()
+    ok, ov = [], []
+    vf = vals.detach().to(torch.float32).contiguous()
+    for (r0, nr), (a, b) in zip(bounds, slices):
+        if b <= a:
+            continue
+        win = eng.window(r0, nr)
+        N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), keys[a:b].data_ptr(), vf[a:b].data_ptr(),
+                                 b - a, L, 1, err, st), "slab_put")
+        k, v, _ = _collect(eng, win, False)
+        ok.append(k)
+        ov.append(v)
+    if not ok:
+        return torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev)
+    return torch.cat(ok), torch.cat(ov)
+
+
+def spread_over_rules(eng: SlabEngine, out_keys, g_out, keys, B: int, L: int):
+    """Backward of ``sum_over_rules``: the gradient at every ``(b, l, e)`` entry is the output
+    gradient at ``(b, e)``."""
+    lib = N.load()
+    dev = eng.dev
+    E = eng.g.num_entities
+    bounds = list(_windows(B, eng.rows_per_window))
+    sl_out = _row_slices(out_keys, E, 1, bounds)
+    sl_in = _row_slices(keys, E, L, bounds)
+    st = N.stream_handle(dev)
+    err = N.error_word(dev).data_ptr()
+    g = torch.zeros(keys.numel(), dtype=torch.float32, device=dev)
+    gf = g_out.to(torch.float32).contiguous()
+    for (r0, nr), (oa, ob), (a, b) in zip(bounds, sl_out, sl_in):
+        if ob <= oa or b <= a:
+            continue
+        win = eng.window(r0, nr)
+        ko = out_keys[oa:ob]
+        N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), ko.data_ptr(), gf[oa:ob].data_ptr(),
+                                 ob - oa, 1, 0, err, st), "slab_put")
+        N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), keys[a:b].data_ptr(), b - a, L,
+                                  g[a:b].data_ptr(), 0, err, st), "slab_take")
+        N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ko.data_ptr(), ob - oa, 1, None, 1, err,
+                                  st), "slab_take")
+    return g
+
+
+# ----------------------------------------------------------------------------- the loop
+class _Hop:
+    __slots__ = ("keys_in", "vals_in", "n_own", "offset", "prune_sel", "n_pre", "keys_y", "y", "d", "keep")
+
+
+def _all_reduce(t, spec):
+    if spec is not None and spec.world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, group=spec.group)
+    return t
+
+
+def _gather(keys, vals, spec):
+    """All ranks' frontier entries in rank order (ascending keys within each rank); returns
+    (keys, values, this rank's offset)."""
+    if spec is None or spec.world == 1:
+        return keys, vals, 0
+    from .sharded import _all_gather_padded, _gather_counts
+    counts = _gather_counts(int(keys.numel()), keys.device, spec.group)
+    k_all = torch.cat(_all_gather_padded(keys, counts, spec.group))
+    v_all = torch.cat(_all_gather_padded(vals.detach(), counts, spec.group))
+    off = sum(counts[: spec.rank])
+    # expansion windows need ascending keys: sort the gathered entries (ranks own disjoint keys)
+    order = torch.argsort(k_all)
+    return k_all[order], v_all[order], (off, order)
+
+
+def _prune(keys, vals, E, topk_nodes, spec):
+    if topk_nodes <= 0:
+        return keys, vals, None
+    if spec is None or spec.world == 1:
+        from .sparse_loop import _prune as prune_local
+        return prune_local(keys, vals, E, topk_nodes)
+    from .sharded import _prune_global
+    n_before = keys.numel()
+    k2, v2 = _prune_global(keys, vals.detach(), E, topk_nodes, spec)
+    if k2.numel() == n_before:
+        return keys, vals, None
+    sel = torch.searchsorted(keys, k2)
+    return k2, v2, sel
+
+
+class SlabHopLoop(autograd.Function):
+    """``(w_hops [K, B, L, n], edge_scores [T]) -> (keys b * E + e, values, messages [K])`` of the
+    uncapped sum hop loop on the key-slab engine; gradients for ``w_hops`` and ``edge_scores``.
+    With a ``ShardSpec`` each rank returns its own entities' part of the result, and every rank
+    receives the full gradients."""
+
+    @staticmethod
+    def forward(ctx, w_hops, edge_scores, heads, eng: SlabEngine, mask, is_score: bool, scale: float,
+                topk_nodes: int, threshold: float, spec):
+        N.require_cuda(w_hops, "w_hops")
+        K, B, L, n = (int(s) for s in w_hops.shape)
+        g = eng.g
+        E = g.num_entities
+        if n != 2 * g.num_relations + 1:
+            raise ValueError(f"w_hops has {n} channels, expected 2R+1 = {2 * g.num_relations + 1}")
+        dev = eng.dev
+        BL = B * L
+        eng.set_edge_factor(mask, edge_scores.detach() if edge_scores is not None else None, is_score, scale)
+        factor_write = g.factor_writes
+        wf = w_hops.detach().to(torch.float32).contiguous()
+        hd = heads.to(device=dev, dtype=torch.int64)
+        keys = (torch.arange(BL, device=dev) * E + hd.repeat_interleave(L))
+        own = (hd.repeat_interleave(L) >= eng.lo) & (hd.repeat_interleave(L) < eng.hi)
+        keys = torch.sort(keys[own]).values
+        vals = torch.ones(keys.numel(), dtype=torch.float32, device=dev)
+        hops, msgs = [], []
+        for h in range(K):
+            st = _Hop()
+            st.n_pre = int(keys.numel())
+            keys, vals, st.prune_sel = _prune(keys, vals, E, int(topk_nodes), spec)
+            st.n_own = int(keys.numel())
+            k_all, v_all, st.offset = _gather(keys, vals, spec)
+            st.keys_in, st.vals_in = k_all, v_all
+            msgs.append(eng.full_degree[k_all % E].sum())
+            ky, y, d = expand_forward(eng, k_all, v_all, wf[h], BL)
+            _all_reduce(d, spec)
+            d32 = d.to(torch.float32)
+            rows = ky // E
+            dr = d32[rows]
+            x = y / dr * d32.clamp_max(1.0)[rows]
+            keep = x != 0
+            if threshold > 0:
+                keep &= x >= threshold
+            st.keys_y, st.y, st.d, st.keep = ky, y, d32, keep
+            keys, vals = ky[keep], x[keep]
+            hops.append(st)
+        out_keys, out_vals = sum_over_rules(eng, keys, vals, B, L)
+        ctx.hops, ctx.eng, ctx.spec = hops, eng, spec
+        ctx.factor_write = factor_write
+        ctx.final_keys = keys
+        ctx.out_keys = out_keys
+        ctx.wf, ctx.shape = wf, (K, B, L, n)
+        ctx.mask, ctx.is_score, ctx.scale = mask, bool(is_score), float(scale)
+        ctx.edge_scores = edge_scores.detach() if edge_scores is not None else None
+        ctx.want_edge = edge_scores is not None and ctx.needs_input_grad[1]
+        ctx.edge_shape = tuple(edge_scores.shape) if edge_scores is not None else None
+        ctx.edge_dtype = edge_scores.dtype if edge_scores is not None else None
+        ctx.mark_non_differentiable(out_keys)
+        m_t = torch.stack(msgs) if msgs else torch.zeros(0, dtype=torch.int64, device=dev)
+        ctx.mark_non_differentiable(m_t)
+        return out_keys, out_vals, m_t
+
+    @staticmethod
+    def backward(ctx, _g_keys, g_vals, _g_msgs):
+        eng, spec = ctx.eng, ctx.spec
+        g = eng.g
+        E = g.num_entities
+        K, B, L, n = ctx.shape
+        BL = B * L
+        dev = eng.dev
+        # the factor field may have been rewritten since the forward (another loop on this graph)
+        if g.factor_writes != ctx.factor_write:
+            eng.set_edge_factor(ctx.mask, ctx.edge_scores, ctx.is_score, ctx.scale)
+        keep_alive = []
+        factor = N.edge_factor(ctx.mask, ctx.edge_scores, ctx.is_score, ctx.scale, keep_alive)
+        grad_w64 = torch.zeros((K, BL, n), dtype=torch.float64, device=dev)
+        grad_edge = torch.zeros(g.num_facts, dtype=torch.float32, device=dev) if ctx.want_edge else None
+        g_state = spread_over_rules(eng, ctx.out_keys, g_vals, ctx.final_keys, B, L)
+        for h in range(K - 1, -1, -1):
+            st = ctx.hops[h]
+            y, d = st.y, st.d
+            rows = st.keys_y // E
+            nz = y != 0
+            gx = torch.zeros_like(y)
+            gx[st.keep] = g_state
+            dr = d[rows]
+            c = d.clamp_max(1.0)
+            q = y / dr
+            g_q = gx * c[rows]
+            zero = torch.zeros_like(y)
+            part = torch.stack([N.row_sums(st.keys_y, torch.where(nz, gx * q, zero), E, BL),
+                                N.row_sums(st.keys_y, torch.where(nz, -(g_q * y) / (dr * dr), zero), E, BL)])
+            _all_reduce(part, spec)
+            g_d = part[1] + torch.where(d <= 1.0, part[0], torch.zeros_like(part[0]))
+            gy = torch.where(nz, (g_q.double() / dr.double() + g_d[rows]).to(torch.float32), zero)
+            gsp = expand_backward(eng, st.keys_in, st.vals_in, ctx.wf[h], BL, st.keys_y, gy, factor, grad_w64[h],
+                                  grad_edge)
+            if spec is not None and spec.world > 1:
+                _all_reduce(gsp, spec)
+                off, order = st.offset
+                mine = torch.empty_like(gsp)
+                mine[order] = gsp          # back to rank order of the gather
+                gsp = mine[off: off + st.n_own]
+            grad_sp = gsp.to(torch.float32)
+            if st.prune_sel is not None:
+                full = torch.zeros(st.n_pre, dtype=torch.float32, device=dev)
+                full[st.prune_sel] = grad_sp
+                grad_sp = full
+            g_state = grad_sp
+        _all_reduce(grad_w64, spec)
+        if grad_edge is not None:
+            _all_reduce(grad_edge, spec)
+        N.raise_device_errors(dev)
+        gw = grad_w64.to(torch.float32).view(K, B, L, n)
+        ge = grad_edge.view(ctx.edge_shape).to(ctx.edge_dtype) if grad_edge is not None else None
+        return gw, ge, None, None, None, None, None, None, None, None
+
+
+def slab_engine(graph: DeviceGraph) -> SlabEngine:
+    """The whole-range engine of ``graph``, made once and kept with it."""
+    eng = getattr(graph, "_slab_engine", None)
+    if eng is None:
+        eng = SlabEngine(graph)
+        graph._slab_engine = eng
+    return eng
+
+
+def slab_proof_scores(engine: SlabEngine, heads: torch.Tensor, w_hops: torch.Tensor,
+                      edge_scores: torch.Tensor | None, mask: torch.Tensor | None = None, is_score: bool = True,
+                      scale: float = 1.0, topk_nodes: int = 0, threshold: float = 0.0, spec=None,
+                      dense: bool = False):
+    """The loop's result as a sparse ``[B, E]`` tensor (``dense=True``: dense; with ``spec``:
+    this rank's entities) and the per-hop message counts."""
+    K, B, L, n = (int(s) for s in w_hops.shape)
+    E = engine.g.num_entities
+    keys, vals, msgs = SlabHopLoop.apply(w_hops, edge_scores, heads, engine, mask, is_score, scale, int(topk_nodes),
+                                         float(threshold), spec)
+    out = torch.sparse_coo_tensor(torch.stack([keys // E, keys % E]), vals, (B, E), is_coalesced=True)
+    return (out.to_dense() if dense else out), msgs

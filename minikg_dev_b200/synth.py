@@ -48,6 +48,7 @@ class Workload:
     state_threshold: float = 0.0  # harness rule: drop state values below this after each hop
     gen: tuple = ()               # generator knobs, see _sample_graph
     note: str = ""
+    capped_row: int = 1 << 60     # the reference's production edge cap for this dataset shape
 
 
 UNCAPPED = 1 << 60
@@ -63,24 +64,28 @@ WORKLOADS = {
     "kg_mid": Workload(
         "kg_mid", E=17050, R=51, T=206205, B=256, L=3, hops=3,
         gen=(("rel", ("zipf", 1.0)), ("head", (1 / 1.1, 2.0)), ("tail", (1 / 1.1, 2.0)),
-             ("hubs", (0.05, 0.40))),
+             ("hubs", (0.05, 0.40))), capped_row=100,
         note="17,050 entities / 51 relations / 206,205 triples; relation Zipf 1.0, degree power law 2.1, "
              "5% hub entities receive 40% of edges"),
     "kg_skew": Workload(
-        "kg_skew", E=123182, R=37, T=1089040, B=512, L=3, hops=3, state_threshold=1e-4,
+        "kg_skew", E=123182, R=37, T=1089040, B=512, L=3, hops=3, state_threshold=1e-4, capped_row=100,
         gen=(("rel", ("top2", 0.70, 1.0)), ("head", (0.8, 2.0)), ("tail", (1.3, "max:50000"))),
         note="123,182 entities / 37 relations / 1,089,040 triples; top-2 relations hold 70%, "
              "in-degree Zipf 1.3 with max in-degree ~50k; state threshold 1e-4"),
+    # frontier bound: the reference's entity prune (drum.py:54-80) at 0.5% of the entities
     "kg_large": Workload(
-        "kg_large", E=4594485, R=822, T=20624575, B=256, L=4, hops=2, topk_edges=100,
+        "kg_large", E=4594485, R=822, T=20624575, B=256, L=4, hops=2, topk_nodes=22972, capped_row=100,
         gen=(("rel", ("zipf_prefix", 1.2, 0.70)), ("head", (1.0, 10.0)), ("tail", (1.0, 10.0))),
         note="4,594,485 entities / 822 relations / 20,624,575 triples; relation Zipf 1.2 truncated "
-             "to the 70% prefix, degree power law 2.0"),
+             "to the 70% prefix, degree power law 2.0; uncapped, frontier pruned to <= 0.5% of the "
+             "entities (22,972)"),
+    # frontier bound: the entity prune at 1M entities (<= 1M nonzeros per query and rule)
     "kg_web": Workload(
-        "kg_web", E=86054151, R=14824, T=338586276, B=128, L=4, hops=2, topk_edges=50,
+        "kg_web", E=86054151, R=14824, T=338586276, B=128, L=4, hops=2, topk_nodes=1000000, capped_row=50,
         gen=(("rel", ("zipf_prefix", 1.3, 0.80)), ("head", (1.0, 10.0)), ("tail", (1 / 0.9, "max:1000000"))),
         note="86,054,151 entities / 14,824 relations / 338,586,276 triples; relation Zipf 1.3 "
-             "truncated to the 80% prefix, in-degree power law 1.9, max hub ~1M"),
+             "truncated to the 80% prefix, in-degree power law 1.9, max hub ~1M; uncapped, frontier "
+             "pruned to 1M entities"),
 }
 
 
@@ -257,8 +262,9 @@ def scaled_workload(name: str, factor: float) -> Workload:
     gen = tuple((k, v) if not (k in ("head", "tail") and isinstance(v[1], str))
                 else (k, (v[0], "max:%d" % max(8, int(float(v[1][4:]) * factor)))) for k, v in wl.gen)
     return Workload(f"{name}@{factor:g}", E=E, R=wl.R, T=T, B=wl.B, L=wl.L, hops=wl.hops,
-                    topk_edges=wl.topk_edges, topk_nodes=wl.topk_nodes,
-                    state_threshold=wl.state_threshold, gen=gen, note=wl.note + f" (scaled x{factor:g})")
+                    topk_edges=wl.topk_edges, topk_nodes=int(wl.topk_nodes * factor) if wl.topk_nodes else 0,
+                    state_threshold=wl.state_threshold, gen=gen, note=wl.note + f" (scaled x{factor:g})",
+                    capped_row=wl.capped_row)
 
 
 @dataclass

@@ -1,0 +1,256 @@
+"""Parity of the key-slab hop loop (``slab_loop.SlabHopLoop``, csrc/mkg_slab.cu) on the GPU.
+
+The uncapped sum loop of proof.py:467-614 against the oracle: result keys and per-hop message
+counts exact, values within rtol 1e-5 / atol 1e-6 of the fp32 oracle, rule-weight and
+edge-score gradients within the same bar of the oracle's float64 run.  Also: the store's
+row windows (a store too small for all rows), destination ranges whose union is the whole
+hop, the store left zeroed after every use, and the loop over two GPUs with NCCL.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fastlog_oracle as O
+from tests.conftest import GRAD_ATOL, GRAD_RTOL, exact_loop_grads
+from tests.test_gpu_parity import GRAPHS, T, csr_dev
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+DEV = torch.device("cuda", 0)
+
+
+def _case(gname, B, L, K, seed, mask_frac=0.0):
+    h, r, t, E, R = GRAPHS[gname]
+    rng = np.random.default_rng(seed)
+    n = 2 * R + 1
+    heads = rng.integers(0, E, B).astype(np.int64)
+    w_hops = np.stack([rng.dirichlet(np.ones(n), size=(B, L)).astype(np.float32) for _ in range(K)])
+    scores = rng.uniform(0.05, 1.0, h.shape[0]).astype(np.float32)
+    mask = rng.random(h.shape[0]) >= mask_frac
+    return h, r, t, E, R, heads, w_hops, scores, mask
+
+
+def _engine(h, r, t, E, R, **kw):
+    from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.slab_loop import SlabEngine
+    csr = O.build_csr_structure(h, t, r, E)
+    return csr, SlabEngine(DeviceGraph(csr_dev(csr), E, R), **kw)
+
+
+def _store_is_zero(eng) -> bool:
+    return eng.store is None or int(torch.count_nonzero(eng.store).item()) == 0
+
+
+@pytest.mark.parametrize("gname,B,L,K,topk_nodes,thr,mask_frac", [
+    ("hubby", 6, 3, 3, 0, 0.0, 0.0),
+    ("g2", 6, 3, 3, 0, 0.0, 0.0),
+    ("hubby", 40, 4, 2, 0, 0.0, 0.0),
+    ("hubby", 6, 3, 3, 150, 0.0, 0.0),
+    ("g2", 12, 3, 3, 0, 2e-3, 0.0),
+    ("hubby", 8, 2, 3, 0, 0.0, 0.3),
+])
+def test_slab_loop_vs_oracle(gname, B, L, K, topk_nodes, thr, mask_frac):
+    from minikg_dev_b200.slab_loop import slab_proof_scores
+    h, r, t, E, R, heads, w_hops, scores, mask = _case(gname, B, L, K, B * 10 + K + topk_nodes, mask_frac)
+    csr, eng = _engine(h, r, t, E, R)
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R, topk_nodes=topk_nodes,
+                                       threshold=thr)
+    wt = T(w_hops).requires_grad_(True)
+    sc = T(scores).requires_grad_(True)
+    mk = T(mask.astype(np.float32)) if mask_frac > 0 else None
+    out, msgs = slab_proof_scores(eng, T(heads), wt, sc, mk, True, 1.0, topk_nodes, thr)
+    out = out.coalesce()
+    idx = out.indices().cpu().numpy()
+    got_k, got_v = idx[0] * E + idx[1], out.values().detach().cpu().numpy()
+    if thr > 0:  # a value within rounding of the threshold may be kept by one summation order only
+        common, ia, ib = np.intersect1d(got_k, final[0], return_indices=True)
+        assert common.size >= final[0].size - 2 and common.size >= got_k.size - 2
+        np.testing.assert_allclose(got_v[ia], final[1][ib], rtol=RTOL, atol=ATOL)
+    else:
+        np.testing.assert_array_equal(got_k, final[0])
+        np.testing.assert_allclose(got_v, final[1], rtol=RTOL, atol=ATOL)
+    assert msgs.cpu().tolist() == [O.count_messages(tr["state"], csr, w_hops[k], L, E, R)
+                                   for k, tr in enumerate(trace)]
+    seed = np.random.default_rng(7).standard_normal(got_k.shape[0]).astype(np.float32)
+    (out.values() * T(seed)).sum().backward()
+    gw, ge = exact_loop_grads(heads, w_hops, csr, mask, scores, B, L, E, R, got_k, seed, num_facts=h.shape[0],
+                              topk_nodes=topk_nodes, threshold=thr)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    torch.cuda.synchronize()
+    assert _store_is_zero(eng)
+
+
+def test_slab_loop_row_windows_match_one_window():
+    """A store of a few rows runs each hop window by window: same keys, values and gradients."""
+    from minikg_dev_b200 import _native as N
+    from minikg_dev_b200.slab_loop import slab_proof_scores
+    h, r, t, E, R, heads, w_hops, scores, mask = _case("hubby", 9, 3, 3, 5)
+    res = []
+    for store_bytes in (None, int(N.load().mkg_slab_store_bytes(4 * E))):
+        _, eng = _engine(h, r, t, E, R, store_bytes=store_bytes)
+        wt = T(w_hops).requires_grad_(True)
+        sc = T(scores).requires_grad_(True)
+        out, msgs = slab_proof_scores(eng, T(heads), wt, sc)
+        out = out.coalesce()
+        (out.values() * torch.linspace(-1, 1, out.values().numel(), device=DEV)).sum().backward()
+        res.append((out.indices(), out.values().detach(), msgs, wt.grad, sc.grad, eng.rows_per_window))
+        assert _store_is_zero(eng)
+    (i1, v1, m1, gw1, ge1, p1), (i2, v2, m2, gw2, ge2, p2) = res
+    assert p1 == 27 and p2 == 4
+    assert torch.equal(i1, i2) and torch.equal(m1, m2)
+    np.testing.assert_allclose(v2.cpu().numpy(), v1.cpu().numpy(), rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(gw2.cpu().numpy(), gw1.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    np.testing.assert_allclose(ge2.cpu().numpy(), ge1.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
+
+
+def test_slab_hop_destination_ranges_add_up():
+    """Engines holding only the push records of one destination range each: their hop outputs
+    partition the whole-range output, and their row sums add up to its row sums."""
+    from minikg_dev_b200.sharded import message_in_counts, plan_dst_ranges
+    from minikg_dev_b200.slab_loop import expand_forward
+    h, r, t, E, R, heads, w_hops, scores, mask = _case("hubby", 5, 3, 1, 11)
+    csr, full = _engine(h, r, t, E, R)
+    B, L = 5, 3
+    full.set_edge_factor(None, T(scores), True, 1.0)
+    rng = np.random.default_rng(3)
+    keys = np.unique(rng.integers(0, B * L * E, 400))
+    vals = rng.uniform(0.01, 1.0, keys.shape[0]).astype(np.float32)
+    kf, vf, df = expand_forward(full, T(keys), T(vals), T(w_hops[0]), B * L)
+    bounds = plan_dst_ranges(message_in_counts(torch.from_numpy(h), torch.from_numpy(t), E), 3)
+    ks, vs, ds = [], [], torch.zeros_like(df)
+    from minikg_dev_b200.slab_loop import SlabEngine
+    for k in range(3):
+        eng = SlabEngine(full.g, bounds[k], bounds[k + 1])
+        eng.set_edge_factor(None, T(scores), True, 1.0)
+        kk, vv, dd = expand_forward(eng, T(keys), T(vals), T(w_hops[0]), B * L)
+        e = (kk % E).cpu().numpy()
+        assert ((e >= bounds[k]) & (e < bounds[k + 1])).all()
+        ks.append(kk)
+        vs.append(vv)
+        ds += dd
+        assert _store_is_zero(eng)
+    kc, vc = torch.cat(ks), torch.cat(vs)
+    o = torch.argsort(kc)
+    assert torch.equal(kc[o], kf)
+    np.testing.assert_allclose(vc[o].cpu().numpy(), vf.cpu().numpy(), rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(ds.cpu().numpy(), df.cpu().numpy(), rtol=1e-6, atol=1e-9)  # fp32 values summed in another order
+    # the oracle's concat-sum of the same hop
+    fb, fl, fe = O.split3(keys, L, E)
+    fwd = O.sparse3d_forward(fb, fl, fe, vals, w_hops[0], csr, np.ones(h.shape[0], bool), scores, B, L, E, R,
+                             is_score=True)
+    want_k, want_v = O.sum_sparse3d_concat(fwd["ori"], fwd["inv"], fwd["ind"])
+    nz = want_v != 0
+    np.testing.assert_array_equal(kf.cpu().numpy(), want_k[nz])
+    np.testing.assert_allclose(vf.cpu().numpy(), want_v[nz], rtol=RTOL, atol=ATOL)
+
+
+def test_slab_bad_frontier_entity_is_reported():
+    """A frontier key outside [B, L, E] is refused on the host; one outside the window's rows
+    reaching the kernel is flagged, not followed, and the context stays usable."""
+    import ctypes
+    from minikg_dev_b200 import _native as N
+    from minikg_dev_b200.slab_loop import expand_forward
+    h, r, t, E, R, heads, w_hops, scores, mask = _case("g2", 2, 2, 1, 1)
+    _, eng = _engine(h, r, t, E, R)
+    keys = T(np.array([3, 2 * 2 * E + 5], np.int64))  # the second row is beyond B * L = 4
+    with pytest.raises(RuntimeError, match="outside"):
+        expand_forward(eng, keys, T(np.ones(2, np.float32)), T(w_hops[0]), 4)
+    lib = N.load()
+    eng.ensure_store(4)
+    win = eng.window(0, 1)  # rows [0, 1): the key of row 1 is outside the window
+    k1 = T(np.array([3, E + 5], np.int64))
+    v1 = T(np.ones(2, np.float32))
+    wf = T(w_hops[0]).reshape(4, -1).contiguous()
+    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(2), DEV)
+    N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k1.data_ptr(), v1.data_ptr(), 2,
+                                wf.data_ptr(), wf.shape[1], 1, ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(),
+                                ws.numel(), N.error_word(DEV).data_ptr(), N.stream_handle(DEV)), "slab_expand")
+    with pytest.raises(RuntimeError, match="outside"):
+        N.raise_device_errors(DEV)
+    eng.store.zero_()  # the accepted key's messages are still in the store
+    torch.cuda.synchronize()
+    assert torch.ones(4, device=DEV).sum().item() == 4.0
+
+
+# ----------------------------------------------------------------------------- two GPUs
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, case, out_q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from minikg_dev_b200.graph import DeviceGraph
+        from minikg_dev_b200.sharded import ShardSpec, message_in_counts, plan_dst_ranges
+        from minikg_dev_b200.slab_loop import SlabEngine, SlabHopLoop
+        h, r, t, E, R, heads, w_hops, scores, topk_nodes = case
+        tt = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)  # noqa: E731
+        g = DeviceGraph.from_triples(tt(h), tt(r), tt(t), E, R)
+        bounds = plan_dst_ranges(message_in_counts(tt(h), tt(t), E), world)
+        spec = ShardSpec(rank, world, bounds)
+        eng = SlabEngine(g, spec.lo, spec.hi)
+        wt = tt(w_hops).requires_grad_(True)
+        sc = tt(scores).requires_grad_(True)
+        keys, vals, msgs = SlabHopLoop.apply(wt, sc, tt(heads), eng, None, True, 1.0, topk_nodes, 0.0, spec)
+        B = heads.shape[0]
+        seed_all = torch.from_numpy(np.random.default_rng(99).standard_normal(B * E).astype(np.float32)).to(dev)
+        (vals * seed_all[keys]).sum().backward()
+        torch.cuda.synchronize()
+        out_q.put((rank, keys.cpu().numpy(), vals.detach().cpu().numpy(), wt.grad.cpu().numpy(),
+                   sc.grad.cpu().numpy(), msgs.cpu().numpy(), bounds))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("topk_nodes", [0, 150])
+def test_slab_loop_two_gpus_vs_oracle(topk_nodes):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    h, r, t, E, R, heads, w_hops, scores, mask = _case("hubby", 7, 3, 3, 17)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    case = (h, r, t, E, R, heads, w_hops, scores, topk_nodes)
+    procs = [ctx.Process(target=_rank_main, args=(rk, 2, port, case, q)) for rk in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=600) for _ in range(2)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    csr = O.build_csr_structure(h, t, r, E)
+    B, L = heads.shape[0], w_hops.shape[2]
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R, topk_nodes=topk_nodes)
+    bounds = res[0][6]
+    for rank, x in enumerate(res):
+        e = x[1] % E
+        assert ((e >= bounds[rank]) & (e < bounds[rank + 1])).all()
+    keys = np.concatenate([x[1] for x in res])
+    vals = np.concatenate([x[2] for x in res])
+    o = np.argsort(keys, kind="stable")
+    np.testing.assert_array_equal(keys[o], final[0])
+    np.testing.assert_allclose(vals[o], final[1], rtol=RTOL, atol=ATOL)
+    want_msgs = [O.count_messages(tr["state"], csr, w_hops[k], L, E, R) for k, tr in enumerate(trace)]
+    seed_all = np.random.default_rng(99).standard_normal(B * E).astype(np.float32)
+    gw, ge = exact_loop_grads(heads, w_hops, csr, mask, scores, B, L, E, R, final[0], seed_all[final[0]],
+                              num_facts=h.shape[0], topk_nodes=topk_nodes)
+    for x in res:
+        assert x[5].tolist() == want_msgs
+        np.testing.assert_allclose(x[3], gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+        np.testing.assert_allclose(x[4], ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)

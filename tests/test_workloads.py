@@ -16,12 +16,12 @@ import pytest
 import torch
 
 from oracle import fastlog_oracle as O
+from tests.conftest import GRAD_ATOL, GRAD_RTOL, exact_loop_grads, softmax_backward
 
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda", 0)
 RTOL, ATOL = 1e-5, 1e-6
-GRAD_RTOL, GRAD_ATOL = 1e-4, 1e-5
 SUB = 4  # queries checked against the oracle
 
 _CACHE: dict = {}
@@ -90,8 +90,8 @@ def test_fused_loop_subset_vs_oracle(name):
     else:
         assert msgs.cpu().tolist() == exp_msgs
     seed = np.random.default_rng(3).standard_normal(final[0].shape[0]).astype(np.float32)
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
-                                  num_facts=kg.num_triples)
+    gw, ge = exact_loop_grads(heads, w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R, final[0], seed,
+                              num_facts=kg.num_triples, threshold=wl.state_threshold)
     (out * T(_dense(final[0], seed, SUB, E))).sum().backward()
     np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
     np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
@@ -117,8 +117,8 @@ def test_fused_capped_subset_vs_oracle(name):
     else:
         assert msgs.cpu().tolist() == exp_msgs
     seed = np.random.default_rng(5).standard_normal(final[0].shape[0]).astype(np.float32)
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
-                                  num_facts=kg.num_triples)
+    gw, ge = exact_loop_grads(heads, w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R, final[0], seed,
+                              num_facts=kg.num_triples, cap=cap, threshold=wl.state_threshold)
     (out * T(_dense(final[0], seed, SUB, E))).sum().backward()
     np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
     np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
@@ -126,24 +126,30 @@ def test_fused_capped_subset_vs_oracle(name):
 
 @pytest.mark.parametrize("name", FUSED)
 def test_fused_loop_full_batch(name):
-    """Full B: the first queries match the oracle-checked subset run; per-query mass <= L."""
+    """Full B: the first queries match the oracle-checked subset run; per-query mass <= L; the
+    full batch's rule-weight gradient of the first queries (queries are independent) is held to
+    the bar against the oracle's float64 run of those queries."""
     from minikg_dev_b200.proof import proof_scores
     wl, kg, csr, dg, inp = workload(name)
-    E, B, L = kg.num_entities, wl.B, wl.L
+    E, R, B, L = kg.num_entities, kg.num_relations, wl.B, wl.L
     sc = T(inp.edge_scores)
     wt = T(inp.rule_weights).requires_grad_(True)
     out, msgs = proof_scores(dg, T(inp.heads), wt, sc, mask=None, threshold=wl.state_threshold)
     seed = torch.randn(B, E, device=DEV, generator=torch.Generator(DEV).manual_seed(1)) * (out != 0)
     (out * seed).sum().backward()
-    ws = T(inp.rule_weights[:, :SUB]).requires_grad_(True)
-    sub, _ = proof_scores(dg, T(inp.heads[:SUB]), ws, sc, mask=None, threshold=wl.state_threshold)
-    (sub * seed[:SUB]).sum().backward()
+    sub, _ = proof_scores(dg, T(inp.heads[:SUB]), T(inp.rule_weights[:, :SUB]), sc, mask=None,
+                          threshold=wl.state_threshold)
     full = out.detach()
     assert torch.isfinite(full).all() and (full >= 0).all()
     assert (full.sum(dim=1) <= L * (1 + 1e-5)).all()
     _assert_close(full[:SUB].cpu().numpy(), sub.detach().cpu().numpy(), wl.state_threshold)
-    np.testing.assert_allclose(wt.grad[:, :SUB].cpu().numpy(), ws.grad.cpu().numpy(), rtol=GRAD_RTOL,
-                               atol=GRAD_ATOL)
+    heads, w = inp.heads[:SUB], inp.rule_weights[:, :SUB]
+    final, _ = O.proof_sum_forward(heads, w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
+                                   threshold=wl.state_threshold)
+    s_np = seed[:SUB].cpu().numpy().reshape(-1)[final[0]]
+    gw, _ = exact_loop_grads(heads, w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R, final[0], s_np,
+                             num_facts=kg.num_triples, threshold=wl.state_threshold)
+    np.testing.assert_allclose(wt.grad[:, :SUB].cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
     assert int(msgs.sum()) > 0
 
 
@@ -168,7 +174,7 @@ def test_max_decode_full_batch_vs_oracle(name):
 CAPPED = ["kg_large", "kg_web@0.02"]
 
 
-def _duck(kg, wl, logits, scores_t):
+def _duck(kg, wl, logits, scores_t, cap, topk_nodes):
     """The model / graph / args surface kernel_sparse_scores reads (proof.py:467-614); the
     CSR is built from the triples on the device, as on the reference's first call."""
     K, B, L, n = logits.shape
@@ -179,7 +185,7 @@ def _duck(kg, wl, logits, scores_t):
     mask = torch.ones(kg.num_triples, dtype=torch.bool, device=DEV)
     graph = SimpleNamespace(e2triple=(T(kg.head), None, mask), triple2e=(None, T(kg.tail), mask),
                             r2triple=(T(kg.rel), None, mask), mask=mask, mask_float=mask.float())
-    args = SimpleNamespace(kernel_topk_edges=wl.topk_edges, kernel_topk_nodes=wl.topk_nodes)
+    args = SimpleNamespace(kernel_topk_edges=cap, kernel_topk_nodes=topk_nodes)
     return model, graph, args
 
 
@@ -208,9 +214,9 @@ def test_first_hop_pruned_max_decode_kg_large():
     if Bk == 0:
         return
     w = inp.rule_weights[:, :1].repeat(Bk, axis=1)
-    final, tails, sc, counts = decode_max_sparse(dg, kept, T(w), 100, T(inp.edge_scores), cap=wl.topk_edges)
+    final, tails, sc, counts = decode_max_sparse(dg, kept, T(w), 100, T(inp.edge_scores), cap=wl.capped_row)
     want, _ = O.proof_max_forward(kept.cpu().numpy(), w, csr, inp.edge_mask, inp.edge_scores, Bk, L, E, R,
-                                  cap=wl.topk_edges)
+                                  cap=wl.capped_row)
     idx = final.indices().cpu().numpy()
     np.testing.assert_array_equal(idx[0] * E + idx[1], want[0])
     np.testing.assert_array_equal(final.values().cpu().numpy(), want[1])
@@ -227,9 +233,9 @@ def test_capped_max_decode_subset_vs_oracle(name):
     E, R, L = kg.num_entities, kg.num_relations, wl.L
     w = inp.rule_weights[:, :SUB]
     final, tails, sc, counts = decode_max_sparse(dg, T(inp.heads[:SUB]), T(w), 100, T(inp.edge_scores),
-                                                 cap=wl.topk_edges)
+                                                 cap=wl.capped_row)
     want, _ = O.proof_max_forward(inp.heads[:SUB], w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
-                                  cap=wl.topk_edges)
+                                  cap=wl.capped_row)
     idx = final.indices().cpu().numpy()
     np.testing.assert_array_equal(idx[0] * E + idx[1], want[0])
     np.testing.assert_array_equal(final.values().cpu().numpy(), want[1])
@@ -253,11 +259,11 @@ def test_hop_op_keys_beyond_32_bits():
     fb, fl, fe = O.split3(keys, L, E)
     fv = rng.uniform(0.05, 1.0, keys.shape[0]).astype(np.float32)
     w = inp.rule_weights[0]
-    fwd = O.sparse3d_forward(fb, fl, fe, fv, w, csr, inp.edge_mask, inp.edge_scores, B, L, E, R, cap=wl.topk_edges,
+    fwd = O.sparse3d_forward(fb, fl, fe, fv, w, csr, inp.edge_mask, inp.edge_scores, B, L, E, R, cap=wl.capped_row,
                              agg_mode=0, is_score=True)
     o, i, d = FastLogFunctionSparse3DTopK.apply(T(fb), T(fl), T(fe), T(fv), T(w), *dg.csr,
                                                 torch.ones((), device=DEV), T(inp.edge_scores), B, L, E, R, False,
-                                                wl.topk_edges, 0, True, 1.0)
+                                                wl.capped_row, 0, True, 1.0)
     for name, t in (("ori", o), ("inv", i), ("ind", d)):
         t = t.coalesce()
         idx = t.indices().cpu().numpy()
@@ -268,27 +274,67 @@ def test_hop_op_keys_beyond_32_bits():
 
 
 @pytest.mark.parametrize("name", CAPPED)
-def test_capped_hops_subset_vs_oracle(name):
+@pytest.mark.parametrize("capped", [False, True])
+def test_large_graph_hops_subset_vs_oracle(name, capped):
+    """kernel_sparse_scores on the full large graphs, a query subset: uncapped with the
+    workload's frontier prune (the key-slab loop) and with the production edge cap (the sparse
+    loop); keys exact, values and gradients at the bar."""
     from minikg_dev_b200.proof import kernel_sparse_scores
     wl, kg, csr, dg, inp = workload(name)
     E, R, L, K = kg.num_entities, kg.num_relations, wl.L, wl.hops
+    cap = wl.capped_row if capped else wl.topk_edges
     heads = inp.heads[:SUB]
     logits = T(inp.rule_logits[:, :SUB]).requires_grad_(True)
     sc = T(inp.edge_scores).requires_grad_(True)
-    model, graph, args = _duck(kg, wl, logits, sc)
+    model, graph, args = _duck(kg, wl, logits, sc, cap, wl.topk_nodes)
     out = kernel_sparse_scores(model, T(heads), T(np.zeros(SUB, np.int64)), graph, args, is_training=True).coalesce()
     # the oracle gets the device's own softmax: a one-ulp weight difference can move a cap bucket
     w = torch.softmax(logits.detach(), dim=-1).cpu().numpy()
     final, trace = O.proof_sum_forward(heads, w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
-                                       cap=wl.topk_edges, topk_nodes=wl.topk_nodes)
+                                       cap=cap, topk_nodes=wl.topk_nodes)
     idx = out.indices().cpu().numpy()
     np.testing.assert_array_equal(idx[0] * E + idx[1], final[0])
     np.testing.assert_allclose(out.values().detach().cpu().numpy(), final[1], rtol=RTOL, atol=ATOL)
     seed = np.random.default_rng(5).standard_normal(final[0].shape[0]).astype(np.float32)
     (out.values() * T(seed)).sum().backward()
-    gw, ge = O.proof_sum_backward(trace, (final[0], seed), w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R,
-                                  num_facts=kg.num_triples)
-    lg_cpu = torch.from_numpy(inp.rule_logits[:, :SUB]).requires_grad_(True)
-    want_gl, = torch.autograd.grad(torch.softmax(lg_cpu, dim=-1), lg_cpu, torch.from_numpy(gw))
-    np.testing.assert_allclose(logits.grad.cpu().numpy(), want_gl.numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    gw, ge = exact_loop_grads(heads, w, csr, inp.edge_mask, inp.edge_scores, SUB, L, E, R, final[0], seed,
+                              num_facts=kg.num_triples, cap=cap, topk_nodes=wl.topk_nodes)
+    np.testing.assert_allclose(logits.grad.cpu().numpy(), softmax_backward(w, gw), rtol=GRAD_RTOL, atol=GRAD_ATOL)
     np.testing.assert_allclose(sc.grad.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+
+
+def test_slab_loop_full_batch_kg_large():
+    """The uncapped 4.59M-entity loop at its full batch (256 queries x 4 rules, 2 hops): the
+    first queries equal the oracle-checked subset run (the frontier prune at 0.5% of the
+    entities does not cut the hop-1 frontier, so queries stay independent), every value is
+    finite and positive, each query's mass is at most L, and the message count is the sum of
+    the frontier's out-degrees."""
+    from minikg_dev_b200.slab_loop import slab_engine, slab_proof_scores
+    wl, kg, csr, dg, inp = workload("kg_large")
+    E, B, L = kg.num_entities, wl.B, wl.L
+    eng = slab_engine(dg)
+    sc = T(inp.edge_scores).requires_grad_(True)
+    wt = T(inp.rule_weights).requires_grad_(True)
+    out, msgs = slab_proof_scores(eng, T(inp.heads), wt, sc, None, True, 1.0, wl.topk_nodes)
+    out = out.coalesce()
+    vals = out.values()
+    assert torch.isfinite(vals).all() and (vals > 0).all()
+    per_q = torch.zeros(B, device=DEV).index_add_(0, out.indices()[0], vals.detach())
+    assert (per_q <= L * (1 + 1e-5)).all()
+    seed = torch.randn(vals.numel(), device=DEV, generator=torch.Generator(DEV).manual_seed(4))
+    (vals * seed).sum().backward()
+    sub, _ = slab_proof_scores(eng, T(inp.heads[:SUB]), T(inp.rule_weights[:, :SUB]), sc.detach(), None, True, 1.0,
+                               wl.topk_nodes)
+    sub = sub.coalesce()
+    first = out.indices()[0] < SUB
+    assert torch.equal(out.indices()[:, first], sub.indices())
+    np.testing.assert_allclose(vals.detach()[first].cpu().numpy(), sub.values().detach().cpu().numpy(), rtol=RTOL,
+                               atol=ATOL)
+    # the full batch's gradient of the first queries against the oracle's float64 run of them
+    si = sub.indices().cpu().numpy()
+    gw, _ = exact_loop_grads(inp.heads[:SUB], inp.rule_weights[:, :SUB], csr, inp.edge_mask, inp.edge_scores, SUB,
+                             L, E, kg.num_relations, si[0] * E + si[1], seed[first].cpu().numpy(),
+                             num_facts=kg.num_triples, topk_nodes=wl.topk_nodes)
+    np.testing.assert_allclose(wt.grad[:, :SUB].cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+    assert int(msgs[0]) == int(dg.push_degree()[T(inp.heads)].sum()) * L
+    assert int(msgs.sum()) > 10_000_000
