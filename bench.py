@@ -1,22 +1,25 @@
 #!/usr/bin/env python
 """Benchmark of the relation-typed sparse hop path (MiniKG proof loop) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload kg_mid] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload kg_large] [--impl ours|reference]
 
-A step is one training pass of the hop loop over one query batch: the forward of every
-hop (op + concat + mass normalisation, then the sum over rules) and its backward to the
-per-hop rule weights and the edge scores, on the 17,050-entity / 51-relation /
-206,205-triple synthetic graph with 256 queries x 3 rules x 3 hops, uncapped, captured once
-as a CUDA graph and replayed (``ProofRunner.capture``; the eager step is reported beside it and
-supplies the per-kernel roofline times).  The metric is edge-messages per second (GTEPS): the
-messages of all hops (frontier entries x their taken out-edges, both directions) divided by the
-fwd+bwd step time.  Under torchrun
-every rank runs its own 256 queries on a replica of the graph (query-batch sharding, weak
-scaling, no collective in the data path); ``value`` sums all ranks' messages over the
-slowest rank's time.
+A step is one training pass of the hop loop over one query batch: the forward of every hop
+(the op of every frontier entry's messages, the concat-sum, the mass normalisation; then the
+sum over rules) and its backward to the per-hop rule weights and the edge scores.  The metric
+is edge-messages per second (GTEPS): the messages of all hops (frontier entries x their
+out-edges, both directions) divided by the fwd+bwd step time.
 
-Prints one JSON line (rank 0).  ``--impl reference`` times the reference algorithm
-(the numpy oracle port of the reference's CPU path) on the host cores instead.
+Default workload: the 4,594,485-entity / 822-relation / 20,624,575-triple graph, 256 queries
+x 4 rules x 2 hops, uncapped, frontier pruned to <= 0.5% of the entities
+(``prune_sparse3d_active_entities`` at 22,972 entities), on the key-slab engine
+(``slab_loop.SlabHopLoop``).  Under torchrun the same batch is destination-partitioned over
+the ranks (rank k owns an entity range and walks only the messages into it; frontier
+all-gather and row-sum all-reduce per hop over NCCL): strong scaling, ``value`` = the
+step's messages over the slowest rank's time.  Workloads with a dense state (kg_small,
+kg_mid, kg_skew) run the fused loop instead, as query-batch replicas under torchrun.
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the reference algorithm (the numpy
+oracle port of the reference's CPU path) on the host cores instead.
 """
 from __future__ import annotations
 
@@ -39,6 +42,7 @@ sys.path.insert(0, str(ROOT))
 from minikg_dev_b200.synth import WORKLOADS, hop_inputs, workload_graph  # noqa: E402
 
 METRIC = "GTEPS (edge-msgs/s) per hop fwd+bwd & argmax decode; % of HBM roofline"
+SLAB_WORKLOADS = ("kg_large", "kg_web")
 
 
 def parse():
@@ -46,13 +50,15 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="kg_mid")
+    ap.add_argument("--workload", default="kg_large")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="headline only (no kg_mid / capped / decode blocks)")
     ap.add_argument("--cpu-sample-queries", type=int, default=0, help="0: pick automatically")
-    ap.add_argument("--engine", default="fused", choices=["fused", "sharded", "capped"],
-                    help="sharded: destination-partitioned capped hop loop (kg_large / kg_web shapes); "
-                         "capped: only the capped sparse loop of the workload (for profiling)")
+    ap.add_argument("--queries", type=int, default=0, help="override the workload's query batch (profiling)")
+    ap.add_argument("--engine", default="auto", choices=["auto", "slab", "fused", "sharded", "capped"],
+                    help="auto: slab for the large graphs, fused otherwise; sharded: the capped sparse loop "
+                         "destination-partitioned; capped: only the capped loops of the workload")
     return ap.parse_args()
 
 
@@ -122,15 +128,42 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def timed(fn, steps, flush=None, stream_events=True):
+    """Device time (ms) of each of ``steps`` calls, CUDA events around each, L2 flushed before."""
+    import torch
+    out = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        fn()
+        s1.record()
+        s1.synchronize()
+        out.append(s0.elapsed_time(s1))
+    return out
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 # ----------------------------------------------------------------------------- CPU side
 _W = {}
 
 
-def _worker_init(head, rel, tail, E, R, heads, w_hops, scores, cap):
+def _worker_init(head, rel, tail, E, R, heads, w_hops, scores, cap, topk_nodes=0):
     """Spawned worker: keeps the graph, its oracle CSR and the batch inputs."""
     sys.path.insert(0, str(ROOT))
     from oracle import fastlog_oracle as O
-    _W.update(head=head, E=E, R=R, heads=heads, w_hops=w_hops, scores=scores, cap=cap,
+    _W.update(head=head, E=E, R=R, heads=heads, w_hops=w_hops, scores=scores, cap=cap, topk_nodes=topk_nodes,
               csr=O.build_csr_structure(head, tail, rel, E))
 
 
@@ -143,17 +176,18 @@ def _oracle_queries(query_ids):
     E, R, csr, scores, cap = _W["E"], _W["R"], _W["csr"], _W["scores"], _W["cap"]
     B, L = heads.shape[0], w_hops.shape[2]
     mask = np.ones(_W["head"].shape[0], bool)
-    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R, cap=cap)
+    final, trace = O.proof_sum_forward(heads, w_hops, csr, mask, scores, B, L, E, R, cap=cap,
+                                       topk_nodes=_W["topk_nodes"])
     seed = np.random.default_rng(0).standard_normal(final[0].shape[0]).astype(np.float32)
     O.proof_sum_backward(trace, (final[0], seed), w_hops, csr, mask, scores, B, L, E, R,
                          num_facts=_W["head"].shape[0])
     return sum(O.count_messages(tr["state"], csr, w_hops[k], L, E, R, cap) for k, tr in enumerate(trace))
 
 
-def cpu_sample(kg, inp, queries: int, cap: int):
+def cpu_sample(kg, inp, queries: int, cap: int, topk_nodes: int = 0):
     """(messages, seconds) of the oracle on the first ``queries`` queries, one thread."""
     _worker_init(kg.head, kg.rel, kg.tail, kg.num_entities, kg.num_relations, inp.heads, inp.rule_weights,
-                 inp.edge_scores, cap)
+                 inp.edge_scores, cap, topk_nodes)
     t0 = time.perf_counter()
     msgs = _oracle_queries(list(range(queries)))
     return msgs, time.perf_counter() - t0
@@ -165,15 +199,17 @@ def run_reference(a, wl, kg, rank, world):
         return
     import multiprocessing as mp
     inp = hop_inputs(kg, wl.B, wl.L, wl.hops, seed=0)
-    cores = os.cpu_count() or 1
-    per = max(1, a.cpu_sample_queries or 2)
+    cores = min(os.cpu_count() or 1, 32)
+    per = max(1, a.cpu_sample_queries or (1 if wl.name in SLAB_WORKLOADS else 2))
     n_q = min(wl.B, per * cores)
     chunks = [list(range(i, min(i + per, n_q))) for i in range(0, n_q, per)]
-    ctx = mp.get_context("spawn")
+    # the oracle's CSR is built once here and inherited by forked workers (this process never
+    # initialises CUDA, so forking is safe)
+    _worker_init(kg.head, kg.rel, kg.tail, kg.num_entities, kg.num_relations, inp.heads, inp.rule_weights,
+                 inp.edge_scores, wl.topk_edges, wl.topk_nodes)
+    ctx = mp.get_context("fork")
     times, msgs_all = [], []
-    with ctx.Pool(processes=min(cores, len(chunks)), initializer=_worker_init,
-                  initargs=(kg.head, kg.rel, kg.tail, kg.num_entities, kg.num_relations, inp.heads,
-                            inp.rule_weights, inp.edge_scores, wl.topk_edges)) as pool:
+    with ctx.Pool(processes=min(cores, len(chunks))) as pool:
         for it in range(a.warmup + a.steps):
             t0 = time.perf_counter()
             msgs = sum(pool.map(_oracle_queries, chunks))
@@ -184,9 +220,11 @@ def run_reference(a, wl, kg, rank, world):
     value = sum(msgs_all) / sum(times) / 1e9
     line = {"metric": METRIC, "value": value, "unit": "GTEPS", "n_gpus": a.gpus, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": 1e3 * statistics.mean(times), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "scaling": "strong" if wl.name in SLAB_WORKLOADS else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
             "config": {"workload": wl.name, "queries_per_step": n_q, "rules": wl.L, "hops": wl.hops,
-                       "entities": wl.E, "relations": wl.R, "triples": wl.T, "edge_cap": "uncapped"},
+                       "entities": wl.E, "relations": wl.R, "triples": wl.T, "edge_cap": "uncapped",
+                       "topk_nodes": wl.topk_nodes},
             "cpu_baseline": {"value": value, "unit": "GTEPS", "cores": min(cores, len(chunks)), "kind": "port",
                              "sample": f"{n_q} of {wl.B} queries per step, fwd+bwd of all {wl.hops} hops, numpy "
                                        f"oracle port of the reference CPU path in {len(chunks)} spawned processes"},
@@ -194,20 +232,20 @@ def run_reference(a, wl, kg, rank, world):
     print(json.dumps(line), flush=True)
 
 
-# ----------------------------------------------------------------------------- GPU side
-def run_ours(a, wl, kg, rank, world, local_rank):
+# ----------------------------------------------------------------------------- GPU: fused loop (dense state)
+def fused_block(a, wl, kg, rank, world, local_rank):
+    """The fused loop on a workload whose dense state fits (kg_mid shape): replayed CUDA-graph
+    step, eager per-kernel roofline, e2e through the public API, max decode, capped row and the
+    rule producer.  Returns the measurement dict (every rank)."""
     import torch
     import torch.distributed as dist
     from minikg_dev_b200.graph import DeviceGraph
     from minikg_dev_b200.proof import ProofRunner
 
     dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
     inp = hop_inputs(kg, wl.B, wl.L, wl.hops, seed=rank)
-    head = torch.from_numpy(kg.head).to(dev)
-    rel = torch.from_numpy(kg.rel).to(dev)
-    tail = torch.from_numpy(kg.tail).to(dev)
-    g = DeviceGraph.from_triples(head, rel, tail, kg.num_entities, kg.num_relations)
+    g = DeviceGraph.from_triples(*(torch.from_numpy(x).to(dev) for x in (kg.head, kg.rel, kg.tail)),
+                                 kg.num_entities, kg.num_relations)
     g.adjacency()
     B, L, K, E, T = wl.B, wl.L, wl.hops, kg.num_entities, kg.num_triples
     n = 2 * kg.num_relations + 1
@@ -240,21 +278,29 @@ def run_ours(a, wl, kg, rank, world, local_rank):
     msgs_host = [int(x) for x in msgs.cpu()]
     M = sum(msgs_host)
 
-    # compulsory bytes per hop (pull of hop h reads the state entering hop h)
+    # compulsory bytes per hop: the pull of hop h reads the state entering hop h; a state is
+    # charged dense (E x B L x 4 B) only where the fused loop holds it dense and it is dense,
+    # sparse frontiers at 12 B per entry (8 B key, 4 B value)
     push_deg = g.push_degree()
     c = g.csr
     grp = ((c[8][1:] - c[8][:-1]) + (c[12][1:] - c[12][:-1])).to(torch.int64)
-    graph_bytes = []
-    for h in range(K):
-        act = runner.row_activity(h).bool()
-        graph_bytes.append(int((push_deg[act] * 8 + grp[act] * 10 + 16).sum().item()))
     BL = B * L
     dense = E * BL * 4
-    fwd_bytes = [gb + 2 * dense + BL * n * 4 for gb in graph_bytes]
-    bwd_bytes = [gb + 3 * dense + BL * n * 4 + T * 4 for gb in graph_bytes]
+    graph_bytes, in_bytes, out_bytes = [], [], []
+    acts = [runner.row_activity(h).bool() for h in range(K)]
+    for h in range(K):
+        act = acts[h]
+        graph_bytes.append(int((push_deg[act] * 8 + grp[act] * 10 + 16).sum().item()))
+    # entries of each state: read back from the active rows of the next hop (an upper bound of nnz)
+    nnz_in = [B * L] + [int(acts[h + 1].sum().item()) * BL for h in range(K - 1)]
+    for h in range(K):
+        in_bytes.append(min(dense, nnz_in[h] * 12))
+        out_bytes.append(min(dense, (nnz_in[h + 1] if h + 1 < K else E * BL) * 12))
+    fwd_bytes = [graph_bytes[h] + in_bytes[h] + out_bytes[h] + BL * n * 4 for h in range(K)]
+    bwd_bytes = [graph_bytes[h] + out_bytes[h] + 2 * in_bytes[h] + BL * n * 4 + T * 4 for h in range(K)]
+    # decode: the same hops with packed 8-byte (value, arg) outputs
+    dec_bytes = sum(graph_bytes[h] + in_bytes[h] + out_bytes[h] * 16 // 12 + BL * n * 4 for h in range(K))
 
-    # eager steps: the library records events around every pull kernel (the roofline's
-    # per-launch times; events cannot be timed inside a CUDA graph)
     torch.cuda.synchronize()
     eager_ms, fwd_ms, bwd_ms = [], [], []
     for _ in range(a.steps):
@@ -269,8 +315,6 @@ def run_ours(a, wl, kg, rank, world, local_rank):
         fwd_ms.append([ev_f[2 * h].elapsed_time(ev_f[2 * h + 1]) for h in range(K)])
         bwd_ms.append([ev_b[2 * h].elapsed_time(ev_b[2 * h + 1]) for h in range(K)])
 
-    # the headline: the same step (edge-factor refresh, forward, backward) captured once as a
-    # CUDA graph (ProofRunner.capture, public API) and replayed, L2 flushed before every step
     cg = runner.capture(heads, w_hops, out, msgs, G, scores, grad_w, grad_edge)
     for _ in range(max(3, a.warmup)):
         cg.replay()
@@ -278,36 +322,20 @@ def run_ours(a, wl, kg, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    step_ms = []
     with ClockSampler(local_rank) as clocks:
-        for _ in range(a.steps):
-            flush.zero_()
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record()
-            cg.replay()
-            s1.record()
-            s1.synchronize()
-            step_ms.append(s0.elapsed_time(s1))
+        step_ms = timed(cg.replay, a.steps, flush)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     del cg
-    total_ms = float(sum(step_ms))
+    total_ms = max_over_ranks(float(sum(step_ms)), world, dev)
     M_all = M
     if world > 1:
-        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
         mm = torch.tensor([M], device=dev, dtype=torch.int64)
         dist.all_reduce(mm, op=dist.ReduceOp.SUM)
         M_all = int(mm.item())
     value = M_all * a.steps / (total_ms / 1e3) / 1e9
 
-    # end to end through the public API, host buffers, copies inside the timed region: the
-    # step captured with its host copies (ProofRunner.capture with host_inputs / host_outputs)
-    # and replayed; the same step with the copies launched eagerly is reported beside it.  The
-    # step's results read back: message counts, rule-weight and edge-score gradients.
     heads_h = torch.from_numpy(inp.heads).pin_memory()
     w_h = torch.from_numpy(inp.rule_weights).pin_memory()
     scores_h = torch.from_numpy(inp.edge_scores).pin_memory()
@@ -318,71 +346,54 @@ def run_ours(a, wl, kg, rank, world, local_rank):
     d2h = msgs_h.numel() * 8 + gw_h.numel() * 4 + ge_h.numel() * 4
     copies_in = [(heads, heads_h), (w_hops, w_h), (scores, scores_h)]
     copies_out = [(msgs_h, msgs), (gw_h, grad_w), (ge_h, grad_edge)]
-
-    def e2e_eager_step():
-        for d, h in copies_in:
-            d.copy_(h, non_blocking=True)
-        g.set_edge_factor(None, scores, True, 1.0)
-        runner.forward(heads, w_hops, out, msgs)
-        runner.backward(G, None, scores, True, 1.0, True, grad_w, grad_edge)
-        for h, d in copies_out:
-            h.copy_(d, non_blocking=True)
-
     e2e_graph = runner.capture(heads, w_hops, out, msgs, G, scores, grad_w, grad_edge,
                                host_inputs=copies_in, host_outputs=copies_out)
-
-    def time_e2e(fn):
-        for _ in range(max(3, a.warmup)):
-            fn()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        times = []
-        for _ in range(a.steps):
-            flush.zero_()
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record()
-            fn()
-            s1.record()
-            s1.synchronize()
-            times.append(s0.elapsed_time(s1))
-        total = float(sum(times))
-        if world > 1:
-            t = torch.tensor([total], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            total = float(t.item())
-        return total
-
-    e2e_total = time_e2e(e2e_graph.replay)
-    e2e_eager_total = time_e2e(e2e_eager_step)
+    for _ in range(max(3, a.warmup)):
+        e2e_graph.replay()
+    torch.cuda.synchronize()
+    e2e_total = max_over_ranks(float(sum(timed(e2e_graph.replay, a.steps, flush))), world, dev)
     del e2e_graph
     e2e_value = M_all * a.steps / (e2e_total / 1e3) / 1e9
-    e2e_eager_value = M_all * a.steps / (e2e_eager_total / 1e3) / 1e9
 
-    # max-argmax decode (forward only) of the same batch, top-100 answers per query
+    res = {"workload": wl.name, "value": value, "ms_per_step": total_ms / a.steps, "messages_per_step": M_all,
+           "messages_per_hop": msgs_host, "clocks": clocks.summary(),
+           "eager_ms_per_step": statistics.mean(eager_ms),
+           "e2e": {"value": e2e_value, "unit": "GTEPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                   "ms_per_step": e2e_total / a.steps,
+                   "path": "ProofRunner.capture with host_inputs / host_outputs (pinned host buffers), replayed"}}
+    if rank != 0 or world > 1:
+        return res
+    hbm, peak_kind = peaks()
+    fwd_avg = [statistics.mean(x[h] for x in fwd_ms) for h in range(K)]
+    bwd_avg = [statistics.mean(x[h] for x in bwd_ms) for h in range(K)]
+
+    def kern(avg, byts):
+        return {"ms_per_launch": sum(avg) / K, "bytes_per_launch": sum(byts) / K,
+                "gbs": sum(byts) / (sum(avg) / 1e3) / 1e9, "ms_per_hop": avg, "bytes_per_hop": byts,
+                "frac_per_hop": [b / (t / 1e3) / 1e9 / hbm for b, t in zip(byts, avg)]}
+    kernels = {"fwd_pull_kernel": kern(fwd_avg, fwd_bytes), "bwd_pull_kernel": kern(bwd_avg, bwd_bytes)}
+    dom = max(kernels, key=lambda k: kernels[k]["ms_per_launch"])
+    traffic = None
+    tfile = ROOT / "profiles" / f"traffic_{wl.name}.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(dom)
+    res["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": kernels[dom]["gbs"], "peak": hbm, "unit": "GB/s",
+                       "frac": kernels[dom]["gbs"] / hbm, "peak_kind": peak_kind, "traffic": traffic}
+    res["kernels"] = kernels
+
     from minikg_dev_b200.proof import decode_max
     for _ in range(2):
         decode_max(g, heads, w_hops, 100, scores)
     torch.cuda.synchronize()
-    dec_ms = []
-    for _ in range(max(3, a.steps // 2)):
-        flush.zero_()
-        s0 = torch.cuda.Event(enable_timing=True)
-        s1 = torch.cuda.Event(enable_timing=True)
-        s0.record()
-        decode_max(g, heads, w_hops, 100, scores)
-        s1.record()
-        s1.synchronize()
-        dec_ms.append(s0.elapsed_time(s1))
+    dec_ms = statistics.mean(timed(lambda: decode_max(g, heads, w_hops, 100, scores), max(3, a.steps // 2), flush))
+    res["decode"] = {"ms": dec_ms, "topk": 100, "gteps": M / (dec_ms / 1e3) / 1e9,
+                     "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms / 1e3) / 1e9, "peak": hbm,
+                                  "unit": "GB/s", "frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm,
+                                  "bytes": dec_bytes, "note": "all hops' compulsory bytes (packed 8-byte maxima) "
+                                                              "over the whole decode time, top-k included"}}
 
-    # capped row: the same batch with the reference's production edge cap of 100, forward +
-    # backward, on the fused loop (per-hop take tables of the capped rows; the path
-    # kernel_sparse_scores takes) and, for comparison, on the sparse loop (per-hop op with the
-    # 256-bucket cap and merged outputs, device normalisation, written-out backward)
     from minikg_dev_b200.proof import proof_scores
-    from minikg_dev_b200.sparse_loop import sparse_proof_scores
-    cap = 100
+    cap = wl.capped_row
 
     def capped_step():
         wt = w_hops.detach().requires_grad_(True)
@@ -391,39 +402,17 @@ def run_ours(a, wl, kg, rank, world, local_rank):
         (out_c * G).sum().backward()
         return msgs_c
 
-    def capped_sparse_step():
-        wt = w_hops.detach().requires_grad_(True)
-        sc = scores.detach().requires_grad_(True)
-        out_c, msgs_c = sparse_proof_scores(g, heads, wt, sc, None, True, 1.0, cap, 0)
-        oi = out_c.indices()
-        (out_c.values() * G[oi[0], oi[1]]).sum().backward()
-        return msgs_c
-
-    def time_steps(fn):
-        for _ in range(2):
-            fn()
-        torch.cuda.synchronize()
-        ts = []
-        for _ in range(max(3, a.steps // 2)):
-            flush.zero_()
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record()
-            fn()
-            s1.record()
-            s1.synchronize()
-            ts.append(s0.elapsed_time(s1))
-        return ts
-
     msgs_c = capped_step()
     M_cap = int(msgs_c.sum().item())
-    cap_ms = time_steps(capped_step)
-    cap_sparse_ms = time_steps(capped_sparse_step)
+    for _ in range(2):
+        capped_step()
+    cap_ms = statistics.mean(timed(capped_step, max(3, a.steps // 2), flush))
+    res["capped"] = {"edge_cap": cap, "ms_per_step": cap_ms, "messages_per_step": M_cap,
+                     "gteps": M_cap / (cap_ms / 1e3) / 1e9,
+                     "path": "fused loop with per-hop edge-cap take tables, fwd+bwd"}
 
-    # rule-weight producer (per-rule BiLSTM -> linear -> per-hop softmax) for the same batch's
-    # target relations: random-init parameters of the reference model's shapes, fwd and fwd+bwd
     from minikg_dev_b200 import rules
-    H = 48 if wl.name == "kg_small" else 64
+    H = 64
     torch.manual_seed(rank)
     pm = torch.nn.Module()
     pm.emb = torch.nn.Parameter(torch.randn(n, H) * 0.5)
@@ -445,67 +434,36 @@ def run_ours(a, wl, kg, rank, world, local_rank):
         for _ in range(3):
             producer_step(bw)
         torch.cuda.synchronize()
-        ts = []
-        for _ in range(max(3, a.steps // 2)):
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record()
-            producer_step(bw)
-            s1.record()
-            s1.synchronize()
-            ts.append(s0.elapsed_time(s1))
-        prod_ms[bw] = statistics.mean(ts)
+        prod_ms[bw] = statistics.mean(timed(lambda: producer_step(bw), max(3, a.steps // 2)))
+    res["rule_producer"] = {"ms_fwd": prod_ms[False], "ms_fwd_bwd": prod_ms[True], "queries": B,
+                            "distinct_relations": int(torch.unique(q_rels).numel()), "emb_size": H, "channels": n}
+    res["gpu_launches_per_step"] = 8 + 5 * K
+    return res
 
+
+def run_fused(a, wl, kg, rank, world, local_rank):
+    """Fused-loop workload as the headline (query-batch replicas under torchrun)."""
+    res = fused_block(a, wl, kg, rank, world, local_rank)
     if rank != 0:
         return
-    hbm, peak_kind = peaks()
-    fwd_avg = [statistics.mean(x[h] for x in fwd_ms) for h in range(K)]
-    bwd_avg = [statistics.mean(x[h] for x in bwd_ms) for h in range(K)]
-    kernels = {
-        "fwd_pull_kernel": {"ms_per_launch": sum(fwd_avg) / K, "bytes_per_launch": sum(fwd_bytes) / K,
-                            "gbs": sum(fwd_bytes) / (sum(fwd_avg) / 1e3) / 1e9, "ms_per_hop": fwd_avg},
-        "bwd_pull_kernel": {"ms_per_launch": sum(bwd_avg) / K, "bytes_per_launch": sum(bwd_bytes) / K,
-                            "gbs": sum(bwd_bytes) / (sum(bwd_avg) / 1e3) / 1e9, "ms_per_hop": bwd_avg},
-    }
-    dom = max(kernels, key=lambda k: kernels[k]["ms_per_launch"])
-    traffic = None
-    tfile = ROOT / "profiles" / f"traffic_{wl.name}.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get(dom)
-    line = {
-        "metric": METRIC, "value": value, "unit": "GTEPS", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": total_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded; shapes of the reference workload)",
-        "config": {"workload": wl.name, "entities": E, "relations": kg.num_relations, "triples": T,
-                   "queries_per_gpu": B, "global_queries": B * world, "rules": L, "hops": K,
-                   "edge_cap": "uncapped", "parallelism": f"query-batch x{world}" if world > 1 else "single GPU",
-                   "l2": "flushed (256 MB write) before every timed step",
-                   "step": "fwd+bwd of the fused loop replayed as one CUDA graph (ProofRunner.capture)",
-                   "messages_per_step": M_all, "messages_per_hop": msgs_host},
-        "roofline": {"bound": "hbm", "kernel": dom, "achieved": kernels[dom]["gbs"], "peak": hbm, "unit": "GB/s",
-                     "frac": kernels[dom]["gbs"] / hbm, "peak_kind": peak_kind, "traffic": traffic},
-        "kernels": kernels,
-        "decode": {"ms": statistics.mean(dec_ms), "topk": 100,
-                   "gteps": M / (statistics.mean(dec_ms) / 1e3) / 1e9},
-        "eager": {"ms_per_step": statistics.mean(eager_ms), "gteps": M / (statistics.mean(eager_ms) / 1e3) / 1e9,
-                  "note": "the same step launched eagerly (per-kernel events for the roofline)"},
-        "capped": {"edge_cap": cap, "ms_per_step": statistics.mean(cap_ms), "messages_per_step": M_cap,
-                   "gteps": M_cap / (statistics.mean(cap_ms) / 1e3) / 1e9,
-                   "path": "fused loop with per-hop edge-cap take tables (the path kernel_sparse_scores "
-                           "takes for caps <= 255), fwd+bwd",
-                   "sparse_loop_ms_per_step": statistics.mean(cap_sparse_ms)},
-        "rule_producer": {"ms_fwd": prod_ms[False], "ms_fwd_bwd": prod_ms[True], "queries": B,
-                          "distinct_relations": int(torch.unique(q_rels).numel()), "emb_size": H, "channels": n,
-                          "path": "per-relation BiLSTM + SGEMM linear layer + per-hop softmax (rules.rule_weights),"
-                                  " random-init parameters of the reference model's shapes"},
-        "e2e": {"value": e2e_value, "unit": "GTEPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_total / a.steps,
-                "path": "ProofRunner.capture with host_inputs / host_outputs (pinned host buffers), replayed",
-                "eager_value": e2e_eager_value, "eager_ms_per_step": e2e_eager_total / a.steps},
-        "gpu_launches": (8 + 5 * K) * a.steps,
-        "clocks": clocks.summary(),
-    }
+    B, L, K = wl.B, wl.L, wl.hops
+    line = {"metric": METRIC, "value": res["value"], "unit": "GTEPS", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; shapes of the reference workload)",
+            "config": {"workload": wl.name, "entities": kg.num_entities, "relations": kg.num_relations,
+                       "triples": kg.num_triples, "queries_per_gpu": B, "global_queries": B * world, "rules": L,
+                       "hops": K, "edge_cap": "uncapped",
+                       "parallelism": f"query-batch x{world}" if world > 1 else "single GPU",
+                       "l2": "flushed (256 MB write) before every timed step",
+                       "step": "fwd+bwd of the fused loop replayed as one CUDA graph (ProofRunner.capture)",
+                       "messages_per_step": res["messages_per_step"], "messages_per_hop": res["messages_per_hop"]},
+            "e2e": res["e2e"], "gpu_launches": res["gpu_launches_per_step"] * a.steps if world == 1 else None,
+            "clocks": res["clocks"]}
+    for k in ("roofline", "kernels", "decode", "capped", "rule_producer"):
+        if k in res:
+            line[k] = res[k]
     if world == 1 and not a.no_cpu_baseline:
+        inp = hop_inputs(kg, B, L, K, seed=0)
         q = a.cpu_sample_queries or 24
         msgs_cpu, secs = cpu_sample(kg, inp, q, wl.topk_edges)
         line["cpu_baseline"] = {"value": msgs_cpu / secs / 1e9, "unit": "GTEPS", "cores": 1, "kind": "port",
@@ -514,13 +472,19 @@ def run_ours(a, wl, kg, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
-def run_sharded(a, wl, kg, rank, world, local_rank):
-    """The destination-partitioned capped hop loop: every rank holds the whole CSR and owns an
-    entity range; the query batch is the workload's (strong scaling over ranks)."""
+# ----------------------------------------------------------------------------- GPU: key-slab loop (large graphs)
+def _seed_of(keys):
+    """A fixed pseudo-random output gradient in [-1, 1) per result key (b * E + e)."""
     import torch
-    import torch.distributed as dist
-    from minikg_dev_b200 import sharded as S
+    h = (keys * 2654435761 + 40503) % 1000003
+    return h.to(torch.float32) / 500001.5 - 1.0
+
+
+def run_slab(a, wl, kg, rank, world, local_rank):
+    import torch
     from minikg_dev_b200.graph import DeviceGraph
+    from minikg_dev_b200.sharded import ShardSpec, message_in_counts, plan_dst_ranges
+    from minikg_dev_b200.slab_loop import SlabEngine, SlabHopLoop, slab_proof_scores
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -530,8 +494,205 @@ def run_sharded(a, wl, kg, rank, world, local_rank):
         kg = KG(wl.name, wl.E, wl.R, np.broadcast_to(np.int8(0), (wl.T,)), np.empty(0), np.empty(0),
                 meta={"generator": "device"})
     else:
-        head_d, rel_d, tail_d = (torch.from_numpy(a).to(dev) for a in (kg.head, kg.rel, kg.tail))
+        head_d, rel_d, tail_d = (torch.from_numpy(x).to(dev) for x in (kg.head, kg.rel, kg.tail))
+    B = a.queries or wl.B
+    L, K, E, T = wl.L, wl.hops, kg.num_entities, kg.num_triples
+    n = 2 * kg.num_relations + 1
+    inp = hop_inputs(kg, B, L, K, seed=0)
+    g = DeviceGraph.from_triples(head_d, rel_d, tail_d, E, kg.num_relations)
+    spec, bounds = None, [0, E]
+    if world > 1:
+        bounds = plan_dst_ranges(message_in_counts(head_d, tail_d, E), world)
+        spec = ShardSpec(rank, world, bounds)
+    del head_d, rel_d, tail_d
+    eng = SlabEngine(g, bounds[rank], bounds[rank + 1]) if world > 1 else SlabEngine(g)
+    heads = torch.from_numpy(inp.heads).to(dev)
+    w_hops = torch.from_numpy(inp.rule_weights).to(dev)
+    scores = torch.from_numpy(inp.edge_scores).to(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        wt = w_hops.detach().requires_grad_(True)
+        sc = scores.detach().requires_grad_(True)
+        keys, vals, msgs = SlabHopLoop.apply(wt, sc, heads, eng, None, True, 1.0, wl.topk_nodes,
+                                             wl.state_threshold, spec)
+        (vals * _seed_of(keys)).sum().backward()
+        return msgs
+
+    for _ in range(max(3, a.warmup)):
+        msgs = step()
+    torch.cuda.synchronize()
+    msgs_host = [int(x) for x in msgs.cpu()]
+    M = sum(msgs_host)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        step_ms = timed(step, a.steps, flush)
+    torch.cuda.synchronize()
+    total_ms = max_over_ranks(float(sum(step_ms)), world, dev)
+    value = M * a.steps / (total_ms / 1e3) / 1e9
+
+    # kernels of this library launched by one step (torch's own elementwise kernels not counted)
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    launches = sum(1 for e in prof.events()
+                   if e.device_type == torch.autograd.DeviceType.CUDA and "mkg::" in e.name)
+
+    # roofline: a traced step records events and algorithmic bytes around every expansion launch
+    eng.trace = []
+    step()
+    torch.cuda.synchronize()
+    trace, eng.trace = eng.trace, None
+    kinds = {}
+    for kind, e0, e1, byts in trace:
+        d = kinds.setdefault(kind, {"ms": [], "bytes": []})
+        d["ms"].append(e0.elapsed_time(e1))
+        d["bytes"].append(byts)
+
+    # end to end through the public API (slab_proof_scores): the batch's query heads and rule
+    # weights copied host -> device from pinned memory, the loss, message counts and rule-weight
+    # gradient copied back; edge scores are resident model parameters (their gradient stays on
+    # the device, as in training)
+    heads_h = torch.from_numpy(inp.heads).pin_memory()
+    w_h = torch.from_numpy(inp.rule_weights).pin_memory()
+    loss_h = torch.empty(1, pin_memory=True)
+    msgs_h = torch.empty(K, dtype=torch.int64, pin_memory=True)
+    gw_h = torch.empty((K, B, L, n), pin_memory=True)
+    heads_d = torch.empty_like(heads)
+    w_d = torch.empty_like(w_hops)
+
+    def e2e_step():
+        heads_d.copy_(heads_h, non_blocking=True)
+        w_d.copy_(w_h, non_blocking=True)
+        wt = w_d.detach().requires_grad_(True)
+        sc = scores.detach().requires_grad_(True)
+        out, m = slab_proof_scores(eng, heads_d, wt, sc, None, True, 1.0, wl.topk_nodes, wl.state_threshold, spec)
+        idx = out.indices()
+        loss = (out.values() * _seed_of(idx[0] * E + idx[1])).sum()
+        loss.backward()
+        loss_h.copy_(loss.detach().reshape(1), non_blocking=True)
+        msgs_h.copy_(m, non_blocking=True)
+        gw_h.copy_(wt.grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_total = max_over_ranks(float(sum(timed(e2e_step, a.steps, flush))), world, dev)
+    e2e_value = M * a.steps / (e2e_total / 1e3) / 1e9
+    h2d = heads_h.numel() * 8 + w_h.numel() * 4
+    d2h = 4 + msgs_h.numel() * 8 + gw_h.numel() * 4
+
+    extras = {}
+    if world == 1 and not a.no_extras:
+        extras = slab_extras(a, wl, kg, g, eng, heads, w_hops, scores, flush, B)
+    if rank != 0:
+        return
+    hbm, peak_kind = peaks()
+    kernels = {}
+    for kind, d in kinds.items():
+        name = "slab_expand_kernel" if kind == "fwd" else "slab_expand_backward_kernel"
+        kernels[name] = {"launches": len(d["ms"]), "ms_per_launch": sum(d["ms"]) / len(d["ms"]),
+                         "bytes_per_launch": sum(d["bytes"]) / len(d["ms"]),
+                         "gbs": sum(d["bytes"]) / (sum(d["ms"]) / 1e3) / 1e9, "ms_per_hop": d["ms"],
+                         "bytes_per_hop": d["bytes"],
+                         "frac_per_hop": [b / (t / 1e3) / 1e9 / hbm for b, t in zip(d["bytes"], d["ms"])]}
+    dom = max(kernels, key=lambda k: sum(kernels[k]["ms_per_hop"]))
+    traffic = None
+    tfile = ROOT / "profiles" / f"traffic_{wl.name}.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(dom)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GTEPS", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": total_ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded; shapes of the reference workload)",
+        "config": {"workload": wl.name, "entities": E, "relations": kg.num_relations, "triples": T, "queries": B,
+                   "rules": L, "hops": K, "edge_cap": "uncapped", "topk_nodes": wl.topk_nodes,
+                   "engine": "key-slab hop loop (slab_loop.SlabHopLoop), fwd+bwd",
+                   "parallelism": f"dst-partition x{world} (NCCL frontier all-gather, row-sum all-reduce)"
+                   if world > 1 else "single GPU", "bounds": bounds if world > 1 else None,
+                   "graph_generator": kg.meta.get("generator", "host"),
+                   "l2": "flushed (256 MB write) before every timed step; graph lists and store exceed L2",
+                   "messages_per_step": M, "messages_per_hop": msgs_host},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": kernels[dom]["gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": kernels[dom]["gbs"] / hbm, "peak_kind": peak_kind, "traffic": traffic},
+        "kernels": kernels,
+        "e2e": {"value": e2e_value, "unit": "GTEPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_total / a.steps,
+                "path": "slab_proof_scores (sparse [B, E] result) with pinned-host query heads and rule weights "
+                        "in, loss / message counts / rule-weight gradient out"},
+        "gpu_launches": launches * a.steps, "clocks": clocks.summary(),
+    }
+    line.update(extras)
+    if world == 1 and not a.no_cpu_baseline:
+        q = a.cpu_sample_queries or 32
+        msgs_cpu, secs = cpu_sample(kg, inp, q, wl.topk_edges, wl.topk_nodes)
+        line["cpu_baseline"] = {"value": msgs_cpu / secs / 1e9, "unit": "GTEPS", "cores": 1, "kind": "port",
+                                "sample": f"{q} of {B} queries, fwd+bwd of all {K} hops ({msgs_cpu} messages in "
+                                          f"{secs:.1f} s), numpy oracle port of the reference CPU path"}
+    print(json.dumps(line), flush=True)
+
+
+def slab_extras(a, wl, kg, g, eng, heads, w_hops, scores, flush, B):
+    """Single-GPU extras beside the headline: the production-cap row of the same batch (sparse
+    loop), its max decode, and the kg_mid fused block."""
+    import torch
+    from minikg_dev_b200.proof import decode_max_sparse
+    from minikg_dev_b200.sparse_loop import sparse_proof_scores
+    E = kg.num_entities
+    out = {}
+    cap = wl.capped_row
+
+    def capped_step():
+        wt = w_hops.detach().requires_grad_(True)
+        sc = scores.detach().requires_grad_(True)
+        o, m = sparse_proof_scores(g, heads, wt, sc, None, True, 1.0, cap, wl.topk_nodes)
+        idx = o.indices()
+        (o.values() * _seed_of(idx[0] * E + idx[1])).sum().backward()
+        return m
+
+    m = capped_step()
+    M_cap = int(m.sum())
+    ms = statistics.mean(timed(capped_step, 3, flush))
+    out["capped"] = {"edge_cap": cap, "ms_per_step": ms, "messages_per_step": M_cap, "gteps": M_cap / ms / 1e6,
+                     "path": "sparse hop loop (merged per-hop op, hash message store), fwd+bwd"}
+
+    # the large graphs' decode: the max-aggregation loop with the production cap, top-100
+    dec = lambda: decode_max_sparse(g, heads, w_hops, 100, scores, cap=cap)  # noqa: E731
+    dec()
+    dms = statistics.mean(timed(dec, 3, flush))
+    out["decode"] = {"ms": dms, "topk": 100, "edge_cap": cap, "gteps": M_cap / dms / 1e6,
+                     "path": "proof.decode_max_sparse (max op with argmax, ordered row sums, device top-k)"}
+
+    # the mid-size graph's fused loop (dense state), its decode, capped row and rule producer
+    mid = WORKLOADS["kg_mid"]
+    mid_kg = workload_graph("kg_mid", seed=0)
+    res = fused_block(a, mid, mid_kg, 0, 1, 0)
+    out["kg_mid"] = res
+    return out
+
+
+# ----------------------------------------------------------------------------- GPU: capped sparse loop, sharded
+def run_sharded(a, wl, kg, rank, world, local_rank):
+    """The destination-partitioned capped sparse loop (production cap of the workload)."""
+    import torch
+    import torch.distributed as dist
+    from minikg_dev_b200 import sharded as S
+    from minikg_dev_b200.graph import DeviceGraph
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if kg is None:
+        from minikg_dev_b200.synth import KG, sample_graph_device
+        head_d, rel_d, tail_d = sample_graph_device(wl.E, wl.R, wl.T, wl.gen, seed=0, device=dev)
+        kg = KG(wl.name, wl.E, wl.R, np.broadcast_to(np.int8(0), (wl.T,)), np.empty(0), np.empty(0),
+                meta={"generator": "device"})
+    else:
+        head_d, rel_d, tail_d = (torch.from_numpy(x).to(dev) for x in (kg.head, kg.rel, kg.tail))
     B, L, K, E, T = wl.B, wl.L, wl.hops, kg.num_entities, kg.num_triples
+    cap = wl.capped_row
     inp = hop_inputs(kg, B, L, K, seed=0)
     g = DeviceGraph.from_triples(head_d, rel_d, tail_d, E, kg.num_relations)
     bounds = S.plan_dst_ranges(S.message_in_counts(head_d, tail_d, E), world)
@@ -540,103 +701,37 @@ def run_sharded(a, wl, kg, rank, world, local_rank):
     heads = torch.from_numpy(inp.heads).to(dev)
     w0 = torch.from_numpy(inp.rule_weights).to(dev)
     s0 = torch.from_numpy(inp.edge_scores).to(dev)
-    counter = S.message_counter(g, wl.topk_edges)
-    seed = torch.randn(B * E, device=dev, generator=torch.Generator(device=dev).manual_seed(1234))
+    counter = S.message_counter(g, cap)
 
     def step():
         wt = w0.detach().requires_grad_(True)
         sc = s0.detach().requires_grad_(True)
-        hop = S.cuda_hop_fn(g, None, S.replicated(sc, spec.group), wl.topk_edges, True, 1.0)
+        hop = S.cuda_hop_fn(g, None, S.replicated(sc, spec.group), cap, True, 1.0)
         msgs = []
         keys, vals = S.sharded_proof_scores(spec, hop, heads, wt, E, threshold=wl.state_threshold,
                                             topk_nodes=wl.topk_nodes, msg_counter=counter, msgs_out=msgs)
-        (vals * seed[keys]).sum().backward()
-        return torch.stack(msgs), wt.grad, sc.grad
+        (vals * _seed_of(keys)).sum().backward()
+        return torch.stack(msgs)
 
     for _ in range(max(3, a.warmup)):
-        msgs, _, _ = step()
+        msgs = step()
     M = int(msgs.sum().item())
     dist.barrier()
     torch.cuda.synchronize()
-    step_ms = []
     with ClockSampler(local_rank) as clocks:
-        for _ in range(a.steps):
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            step()
-            e1.record()
-            e1.synchronize()
-            step_ms.append(e0.elapsed_time(e1))
-    torch.cuda.synchronize()
-    dist.barrier()
-    t = torch.tensor([float(sum(step_ms))], device=dev, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
+        step_ms = timed(step, a.steps)
+    total_ms = max_over_ranks(float(sum(step_ms)), world, dev)
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": M * a.steps / (total_ms / 1e3) / 1e9, "unit": "GTEPS",
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": total_ms / a.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "engine": "sharded",
+            "data": "synthetic", "engine": "sharded capped sparse loop",
             "config": {"workload": wl.name, "entities": E, "relations": kg.num_relations, "triples": T,
-                       "queries": B, "rules": L, "hops": K, "topk_edges": wl.topk_edges,
+                       "queries": B, "rules": L, "hops": K, "edge_cap": cap,
                        "graph_generator": kg.meta.get("generator", "host"),
-                       "parallelism": f"dst-partition x{world}", "bounds": bounds,
-                       "l2": "state and inputs exceed L2"},
+                       "parallelism": f"dst-partition x{world}", "bounds": bounds},
             "messages_per_step": M, "clocks": clocks.summary()}), flush=True)
-
-
-def run_capped(a, wl, kg):
-    """Only the capped (cap 100) hop loop, fwd+bwd, on the fused loop and on the sparse loop."""
-    import torch
-    from minikg_dev_b200.graph import DeviceGraph
-    from minikg_dev_b200.sparse_loop import sparse_proof_scores
-    dev = torch.device("cuda", 0)
-    B, L, K, E = wl.B, wl.L, wl.hops, kg.num_entities
-    inp = hop_inputs(kg, B, L, K, seed=0)
-    g = DeviceGraph.from_triples(torch.from_numpy(kg.head).to(dev), torch.from_numpy(kg.rel).to(dev),
-                                 torch.from_numpy(kg.tail).to(dev), E, kg.num_relations)
-    heads = torch.from_numpy(inp.heads).to(dev)
-    w0 = torch.from_numpy(inp.rule_weights).to(dev)
-    s0 = torch.from_numpy(inp.edge_scores).to(dev)
-    G = torch.randn((B, E), device=dev, generator=torch.Generator(device=dev).manual_seed(1234))
-
-    from minikg_dev_b200.proof import proof_scores
-
-    def fused_step():
-        wt = w0.detach().requires_grad_(True)
-        sc = s0.detach().requires_grad_(True)
-        out, msgs = proof_scores(g, heads, wt, sc, None, True, 1.0, 0.0, 100)
-        (out * G).sum().backward()
-        return msgs
-
-    def sparse_step():
-        wt = w0.detach().requires_grad_(True)
-        sc = s0.detach().requires_grad_(True)
-        out, msgs = sparse_proof_scores(g, heads, wt, sc, None, True, 1.0, 100, 0)
-        oi = out.indices()
-        (out.values() * G[oi[0], oi[1]]).sum().backward()
-        return msgs
-
-    res = {}
-    for name, step in (("fused", fused_step), ("sparse_loop", sparse_step)):
-        for _ in range(max(3, a.warmup)):
-            msgs = step()
-        torch.cuda.synchronize()
-        ms = []
-        for _ in range(a.steps):
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            step()
-            e1.record()
-            e1.synchronize()
-            ms.append(e0.elapsed_time(e1))
-        M = int(msgs.sum().item())
-        res[name] = {"messages_per_step": M, "ms_per_step": statistics.mean(ms),
-                     "gteps": M / (statistics.mean(ms) / 1e3) / 1e9}
-    print(json.dumps({"engine": "capped", "workload": wl.name, "edge_cap": 100, **res}))
 
 
 def main():
@@ -645,15 +740,18 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     wl = WORKLOADS[a.workload]
-    # graphs above 5e7 facts are drawn on the GPU by the sharded engine itself
-    kg = None if (a.engine == "sharded" and wl.T > 50_000_000) else workload_graph(a.workload, seed=0)
+    engine = a.engine
+    if engine == "auto":
+        engine = "slab" if wl.name in SLAB_WORKLOADS else "fused"
+    # graphs above 5e7 facts are drawn on the GPU by the GPU engines themselves
+    host_graph = wl.T <= 50_000_000 or a.impl == "reference"
+    if a.impl == "reference" and rank != 0:
+        return
+    kg = workload_graph(a.workload, seed=0) if host_graph else None
     if a.impl == "reference":
         run_reference(a, wl, kg, rank, world)
         return
-    if a.engine == "capped":
-        run_capped(a, wl, kg)
-        return
-    distributed = world > 1 or a.engine == "sharded"
+    distributed = world > 1 or engine == "sharded"
     if distributed:
         import torch
         import torch.distributed as dist
@@ -661,13 +759,15 @@ def main():
         if world == 1:
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
             os.environ.setdefault("MASTER_PORT", "29531")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), rank=rank, world_size=world,
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), rank=rank, world_size=world,
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if a.engine == "sharded":
+        if engine == "slab":
+            run_slab(a, wl, kg, rank, world, local_rank)
+        elif engine == "sharded":
             run_sharded(a, wl, kg, rank, world, local_rank)
         else:
-            run_ours(a, wl, kg, rank, world, local_rank)
+            run_fused(a, wl, kg, rank, world, local_rank)
     finally:
         if distributed:
             import torch.distributed as dist
