@@ -533,13 +533,15 @@ def run_slab(a, wl, kg, rank, world, local_rank):
     total_ms = max_over_ranks(float(sum(step_ms)), world, dev)
     value = M * a.steps / (total_ms / 1e3) / 1e9
 
-    # kernels of this library launched by one step (torch's own elementwise kernels not counted)
+    # kernels of this library launched by one step: its own and the CUB scans compiled into it
+    # (torch's elementwise / CUB kernels, in torch's namespaces, not counted)
     from torch.profiler import ProfilerActivity, profile
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step()
         torch.cuda.synchronize()
     launches = sum(1 for e in prof.events()
-                   if e.device_type == torch.autograd.DeviceType.CUDA and "mkg::" in e.name)
+                   if e.device_type == torch.autograd.DeviceType.CUDA
+                   and ("mkg::" in e.name or e.name.startswith("void cub::")))
 
     # roofline: a traced step records events and algorithmic bytes around every expansion launch
     eng.trace = []

@@ -176,9 +176,13 @@ size_t mkg_adjacency_workspace_bytes(int64_t num_entities);
  * messages per frontier entry, fastlog.cu:2197-2323). */
 int mkg_adjacency_build(const mkg_graph* g, mkg_adjacency adj, int64_t* num_tasks_out, void* workspace,
                         size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
-/* Rewrites the factor field of every record from the current mask / edge scores. */
+/* Rewrites the factor field of every record from the current mask / edge scores; a list
+ * whose pointer (adj.pull or adj.push) is NULL is left as it is.  mkg_records_set_factor does
+ * the same for any record array (e.g. a rank's push records of its own destinations). */
 int mkg_adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, const mkg_edge_factor* f,
                              mkg_stream stream);
+int mkg_records_set_factor(mkg_adj_edge* records, int64_t count, int64_t num_facts, const mkg_edge_factor* f,
+                           mkg_stream stream);
 
 /* Edge-cap index of the fused engine for one cap value (0 .. MKG_DENSE_CAP_MAX).  The
  * reference caps every frontier entry (b, l, s) per direction at `cap` messages with the
@@ -430,6 +434,22 @@ int mkg_slab_expand_backward(const int32_t* push_ptr, const mkg_adj_edge* push, 
  * The per-(b, l) sums of normalize_sparse3d and of its gradient (drum.py:31-51). */
 int mkg_row_sums(const int64_t* keys, int64_t nnz, int64_t E, int64_t row0, int64_t nrows, const float* vals,
                  double* out, unsigned* dev_err, mkg_stream stream);
+/* normalize_sparse3d(.., 0, "mass") (drum.py:31-51) on key-sorted entries: x = (y / d) *
+ * min(d, 1) with d = row_sums[key / E - row0] (fp32).  dropped (device int64) receives the
+ * number of results that are zero or, when threshold > 0, below it (the entries the loop
+ * then drops). */
+int mkg_mass_normalize(const int64_t* keys, const float* y, int64_t n, int64_t E, int64_t row0, int64_t nrows,
+                       const float* row_sums, float threshold, float* x, int64_t* dropped, unsigned* dev_err,
+                       mkg_stream stream);
+/* Its gradient in two calls (a caller spanning several GPUs all-reduces `sums` in between):
+ * mkg_mass_normalize_grad_sums adds sums[0][r] += gx * y / d and sums[1][r] += -(gx * min(d, 1)
+ * * y) / d^2 over row r's entries (fp64, [2, nrows]); mkg_mass_normalize_grad writes
+ * gy = gx * min(d, 1) / d + sums[1][r] + [d <= 1] sums[0][r] (zero where y is zero). */
+int mkg_mass_normalize_grad_sums(const int64_t* keys, const float* y, const float* gx, int64_t n, int64_t E,
+                                 int64_t row0, int64_t nrows, const float* row_sums, double* sums, unsigned* dev_err,
+                                 mkg_stream stream);
+int mkg_mass_normalize_grad(const int64_t* keys, const float* y, const float* gx, int64_t n, int64_t E, int64_t row0,
+                            int64_t nrows, const float* row_sums, const double* sums, float* gy, mkg_stream stream);
 /* out[i] = (float) in[i]. */
 int mkg_f64_to_f32(const double* in, int64_t n, float* out, mkg_stream stream);
 

@@ -102,6 +102,7 @@ SIGNATURES = {
     "mkg_adjacency_workspace_bytes": (C.c_size_t, [i64]),
     "mkg_adjacency_build": (C.c_int, [P(Graph), Adjacency, vp, vp, C.c_size_t, vp, vp]),
     "mkg_adjacency_set_factor": (C.c_int, [P(Graph), Adjacency, P(EdgeFactor), vp]),
+    "mkg_records_set_factor": (C.c_int, [vp, i64, i64, P(EdgeFactor), vp]),
     "mkg_hop_forward_workspace_bytes": (C.c_size_t, [P(HopParams), i64]),
     "mkg_hop_forward": (C.c_int, [P(Graph), P(Frontier), vp, P(EdgeFactor), P(HopParams), vp, C.c_size_t, vp,
                                   vp, vp]),
@@ -138,6 +139,9 @@ SIGNATURES = {
                                            i64, vp, vp, vp, vp, C.c_size_t, vp, vp]),
     "mkg_row_sums": (C.c_int, [vp, i64, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_f64_to_f32": (C.c_int, [vp, i64, vp, vp]),
+    "mkg_mass_normalize": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, C.c_float, vp, vp, vp, vp]),
+    "mkg_mass_normalize_grad_sums": (C.c_int, [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp]),
+    "mkg_mass_normalize_grad": (C.c_int, [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_reduce_by_key_workspace_bytes": (C.c_size_t, [i64]),
     "mkg_reduce_by_key": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, C.c_size_t, vp, vp]),
     "mkg_rule_saved_bytes": (C.c_size_t, [P(RuleParams)]),

@@ -72,6 +72,10 @@ MKG_API int mkg_adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, cons
                                      mkg_stream st) {
   return mkg::adjacency_set_factor(g, adj, f, S(st));
 }
+MKG_API int mkg_records_set_factor(mkg_adj_edge* records, int64_t count, int64_t num_facts, const mkg_edge_factor* f,
+                                   mkg_stream st) {
+  return mkg::records_set_factor(records, count, num_facts, f, S(st));
+}
 
 MKG_API int mkg_hop_count_messages(const mkg_graph* g, const mkg_frontier* f, const mkg_hop_params* p,
                                    int64_t* counts, unsigned* err, mkg_stream st) {

@@ -438,9 +438,23 @@ int adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, const mkg_edge_f
   MKG_REQUIRE(g && f, "adjacency_set_factor: null argument");
   EdgeFactor ef = make_factor(*f);
   const int64_t count = 2 * g->num_facts;
-  adjacency_factor_kernel<<<persistent_blocks(8), 256, 0, st>>>(adj.pull, count, g->num_facts, ef);
-  MKG_LAUNCHED("adjacency_factor_kernel");
-  adjacency_factor_kernel<<<persistent_blocks(8), 256, 0, st>>>(adj.push, count, g->num_facts, ef);
+  if (adj.pull != nullptr) {  // a list passed as NULL keeps its factors
+    adjacency_factor_kernel<<<persistent_blocks(8), 256, 0, st>>>(adj.pull, count, g->num_facts, ef);
+    MKG_LAUNCHED("adjacency_factor_kernel");
+  }
+  if (adj.push != nullptr) {
+    adjacency_factor_kernel<<<persistent_blocks(8), 256, 0, st>>>(adj.push, count, g->num_facts, ef);
+    MKG_LAUNCHED("adjacency_factor_kernel");
+  }
+  return MKG_OK;
+}
+
+int records_set_factor(mkg_adj_edge* recs, int64_t count, int64_t num_facts, const mkg_edge_factor* f,
+                       cudaStream_t st) {
+  MKG_REQUIRE(f && count >= 0 && num_facts >= 0 && (recs || count == 0), "records_set_factor: bad argument");
+  if (count == 0) return MKG_OK;
+  adjacency_factor_kernel<<<grid_for(count, 256, persistent_blocks(8)), 256, 0, st>>>(recs, count, num_facts,
+                                                                                     make_factor(*f));
   MKG_LAUNCHED("adjacency_factor_kernel");
   return MKG_OK;
 }

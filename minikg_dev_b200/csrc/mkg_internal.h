@@ -21,6 +21,8 @@ size_t adjacency_workspace_bytes(int64_t E);
 int adjacency_build(const mkg_graph* g, mkg_adjacency adj, int64_t* num_tasks, void* ws, size_t ws_bytes,
                     unsigned* err, cudaStream_t st);
 int adjacency_set_factor(const mkg_graph* g, mkg_adjacency adj, const mkg_edge_factor* f, cudaStream_t st);
+int records_set_factor(mkg_adj_edge* recs, int64_t count, int64_t num_facts, const mkg_edge_factor* f,
+                       cudaStream_t st);
 size_t cap_index_workspace_bytes(const mkg_graph* g);
 int cap_index_sizes(const mkg_graph* g, int64_t cap, int64_t* sizes, void* ws, size_t ws_bytes, cudaStream_t st);
 int cap_index_build(const mkg_graph* g, const mkg_adjacency* adj, const mkg_cap_index* ix, void* ws,

@@ -152,16 +152,33 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_kernel(ExpandArgs 
       const int64_t r = rb + u * 32 + lane;
       rec[u] = r < re ? a.push[r] : make_int4(-1, 0, 0, 0);
     }
+    // the lane's records in three rounds, each with all of its memory operations in flight:
+    // rule-weight loads, then the adds, then the touched bits of the slots found at zero
+    constexpr int kU = kChunkRecs / 32;
+    int64_t slot[kU];
+    float wv[kU];
 #pragma unroll
-    for (int u = 0; u < kChunkRecs / 32; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int d = rec[u].x, ch = rec[u].y;
+      slot[u] = -1;
+      wv[u] = 0.0f;
       if (d < 0) continue;
       if (d >= a.win.E || ch < 0 || ch >= a.n - 1) { raise_flag(a.err, MKG_DEV_BAD_COL); continue; }
       const int64_t e = (int64_t)d - a.win.lo;
       if (e < 0 || e >= a.win.extent) continue;  // another rank's destination
-      const float v = (x * __ldg(wrow + ch)) * __int_as_float(rec[u].w);
-      if (v != 0.0f) touch_add(st, lrow * a.win.extent + e, v);
+      slot[u] = lrow * a.win.extent + e;
+      wv[u] = __ldg(wrow + ch);
     }
+    float old[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const float v = (x * wv[u]) * __int_as_float(rec[u].w);
+      old[u] = 1.0f;  // no add: nothing to mark
+      if (slot[u] >= 0 && v != 0.0f) old[u] = atomicAdd(st.val + slot[u], v);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (old[u] == 0.0f) atomicOr(st.bits + (slot[u] >> 5), 1u << (slot[u] & 31));
   }
 }
 
@@ -181,25 +198,54 @@ __global__ void __launch_bounds__(kTileThreads) slab_count_kernel(const uint32_t
   if (threadIdx.x == 0) blk[blockIdx.x] = total;
 }
 
-// Block b owns bitmap words [b * kTileWords, (b + 1) * kTileWords), visited 256 consecutive
-// words at a time; a block scan of the popcounts places every set bit at its rank, so the
-// keys come out in slot order = key order, and each word is cleared after it is read.  This
-// pass only stores (no dependent loads per bit); slab_gather_kernel then reads the values.
+// Block b owns bitmap words [b * kTileWords, (b + 1) * kTileWords) (the tile slab_count_kernel
+// counted); every set bit is placed at its rank, so the keys come out in slot order = key
+// order, and each word is cleared after it is read.  This pass only stores (no dependent loads
+// per bit); slab_gather_kernel then reads the values.
 __global__ void __launch_bounds__(kTileThreads) slab_emit_keys_kernel(Store st, Window win, int64_t words,
                                                                      const int64_t* __restrict__ blk_off,
                                                                      int64_t count, int64_t* __restrict__ keys_out) {
-  typedef cub::BlockScan<int, kTileThreads> Scan;
-  __shared__ typename Scan::TempStorage tmp;
-  const int64_t w0 = blockIdx.x * kTileWords;
-  int64_t base = blk_off[blockIdx.x];
-  for (int k = 0; k < kWordsPerThread; ++k) {
-    const int64_t wi = w0 + (int64_t)k * kTileThreads + threadIdx.x;
+  // warp w of the block owns the tile's words [w * 1024, (w + 1) * 1024), lane l reads words
+  // w * 1024 + k * 32 + l: one pass counts the warp's bits, a scan of the 8 warp counts in
+  // shared memory places each warp, a second pass emits with a warp scan per 32 words
+  constexpr int kWarps = kTileThreads / 32;
+  constexpr int kSpan = (int)(kTileWords / kWarps);  // words per warp
+  __shared__ long long warp_base[kWarps];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int64_t wb = blockIdx.x * kTileWords + (int64_t)wid * kSpan;
+  int c = 0;
+#pragma unroll 8
+  for (int k = 0; k < kSpan / 32; ++k) {
+    const int64_t wi = wb + k * 32 + lane;
+    if (wi < words) c += __popc(st.bits[wi]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if (lane == 0) warp_base[wid] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long run = blk_off[blockIdx.x];
+    for (int w = 0; w < kWarps; ++w) {
+      const long long t = warp_base[w];
+      warp_base[w] = run;
+      run += t;
+    }
+  }
+  __syncthreads();
+  int64_t base = warp_base[wid];
+  for (int k = 0; k < kSpan / 32; ++k) {
+    const int64_t wi = wb + k * 32 + lane;
     uint32_t word = wi < words ? st.bits[wi] : 0u;
-    int pos, tot;
-    Scan(tmp).ExclusiveSum(__popc(word), pos, tot);
-    __syncthreads();  // tmp reused next round
+    const int pc = __popc(word);
+    int incl = pc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
     if (word) {
-      int64_t p = base + pos;
+      int64_t p = base + (incl - pc);
       st.bits[wi] = 0u;
       while (word) {
         const int j = __ffs(word) - 1;
@@ -304,13 +350,14 @@ __global__ void slab_take_kernel(Store st, Window win, const int64_t* __restrict
 }
 
 // ------------------------------------------------------------------ backward expansion
-__device__ __forceinline__ float grad_scale(const EdgeFactor& f, int64_t fact) {
+// d m / d weight divided out of m, from the record's own factor m = [mask] * score: where the
+// mask is on, m is the score itself (weight, or sigmoid(weight * scale) rounded to fp32), so
+// 1 / max(weight, 1e-12) = 1 / max(m, 1e-12) and scale * (1 - sigmoid) = scale * (1 - m); where
+// it is off m = 0 and the contribution is zero either way.  No per-message read of the weights.
+__device__ __forceinline__ float grad_scale(const EdgeFactor& f, float m) {
   if (f.weight == nullptr) return 0.0f;
-  const float ew = f.weight[fact];
-  if (f.is_score) return 1.0f / fmaxf(ew, 1e-12f);
-  const float z = -ew * f.scale;
-  const float sg = static_cast<float>(1.0 / (1.0 + exp(static_cast<double>(z))));
-  return f.scale * (1.0f - sg);
+  if (f.is_score) return 1.0f / fmaxf(m, 1e-12f);
+  return f.scale * (1.0f - m);
 }
 
 __global__ void __launch_bounds__(kExpandThreads) slab_expand_backward_kernel(
@@ -351,29 +398,38 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_backward_kernel(
       const int64_t r = rb + u * 32 + lane;
       rec[u] = r < re ? a.push[r] : make_int4(-1, 0, 0, 0);
     }
+    // all of the lane's gradient lookups and rule-weight loads go out before any is used
+    constexpr int kU = kChunkRecs / 32;
+    float gl[kU], wl[kU];
+    bool lv[kU];
 #pragma unroll
-    for (int u = 0; u < kChunkRecs / 32; ++u) {
-      const int d = rec[u].x;
-      int ch = rec[u].y;
-      float g = 0.0f;
+    for (int u = 0; u < kU; ++u) {
+      const int d = rec[u].x, ch = rec[u].y;
       bool live = d >= 0;
       if (live && (d >= a.win.E || ch < 0 || ch >= a.n - 1)) { raise_flag(a.err, MKG_DEV_BAD_COL); live = false; }
       const int64_t e = (int64_t)d - a.win.lo;
       if (live && (e < 0 || e >= a.win.extent)) live = false;
-      if (live) g = gstore[lrow * a.win.extent + e];
+      lv[u] = live;
+      gl[u] = live ? gstore[lrow * a.win.extent + e] : 0.0f;
+      wl[u] = live ? __ldg(wrow + ch) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      int ch = rec[u].y;
+      const bool live = lv[u];
+      const float g = gl[u];
       const float m = __int_as_float(rec[u].w);
       const float gm = g * m;
-      float wv = 0.0f, part = 0.0f;
+      const float wv = wl[u];
+      float part = 0.0f;
       if (live && gm != 0.0f) {
-        wv = __ldg(wrow + ch);
         gsp += (double)(gm * wv);
         part = gm * x;
       }
       if (live && g != 0.0f && grad_edge != nullptr) {
-        if (wv == 0.0f) wv = __ldg(wrow + ch);
         const int f = rec[u].z;
         if (f >= 0 && f < num_facts) {
-          const float contrib = (((g * x) * wv) * m) * grad_scale(ef, f);
+          const float contrib = (((g * x) * wv) * m) * grad_scale(ef, m);
           if (contrib != 0.0f) atomicAdd(grad_edge + f, contrib);
         } else {
           raise_flag(a.err, MKG_DEV_BAD_FACT);
@@ -447,6 +503,105 @@ __global__ void __launch_bounds__(kTileThreads) row_sums_kernel(const int64_t* _
     __syncthreads();
     for (int i = threadIdx.x; i < span; i += kTileThreads)
       if (bins[i] != 0.0) atomicAdd(out + first_row + i, bins[i]);
+  }
+}
+
+// ------------------------------------------------------------------ mass normalisation
+// normalize_sparse3d(.., 0, "mass") on a key-sorted state (drum.py:31-51): x = (y / d) *
+// min(d, 1) with d the row's sum (fp32 division and product, as torch computes them); counts
+// the zeros the result holds (entries the hop loop then drops) and the entries under a state
+// threshold.
+__global__ void mass_norm_kernel(const int64_t* __restrict__ keys, const float* __restrict__ y, int64_t n, int64_t E,
+                                 int64_t row0, int64_t nrows, const float* __restrict__ d, float thr,
+                                 float* __restrict__ x, unsigned long long* __restrict__ dropped, unsigned* err) {
+  unsigned long long local = 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = keys[i] / E - row0;
+    float v = 0.0f;
+    if (r < 0 || r >= nrows) {
+      raise_flag(err, MKG_DEV_BAD_KEY);
+    } else {
+      const float dr = d[r];
+      v = __fdiv_rn(y[i], dr) * fminf(dr, 1.0f);
+    }
+    x[i] = v;
+    if (v == 0.0f || (thr > 0.0f && v < thr)) ++local;
+  }
+  local = __reduce_add_sync(0xffffffffu, (unsigned)local);
+  if ((threadIdx.x & 31) == 0 && local) atomicAdd(dropped, local);
+}
+
+// Row sums of the normalisation gradient's two terms (fp64): sums[0][r] += gx * q and
+// sums[1][r] += -(gx * c * y) / (d * d), q = y / d, c = min(d, 1), over the rows' entries.
+__global__ void __launch_bounds__(kTileThreads) mass_norm_grad_sums_kernel(
+    const int64_t* __restrict__ keys, const float* __restrict__ y, const float* __restrict__ gx, int64_t n, int64_t E,
+    int64_t row0, int64_t nrows, const float* __restrict__ d, double* __restrict__ sums, unsigned* err) {
+  __shared__ double bins[2][kRowBins];
+  const int64_t i0 = blockIdx.x * (int64_t)kTileThreads * kRowSumItems;
+  if (i0 >= n) return;
+  const int64_t i1 = min(i0 + (int64_t)kTileThreads * kRowSumItems, n);
+  const int64_t first_row = keys[i0] / E - row0;
+  const int64_t span = keys[i1 - 1] / E - row0 - first_row + 1;
+  const bool binned = span >= 1 && span <= kRowBins;
+  if (binned)
+    for (int i = threadIdx.x; i < 2 * kRowBins; i += kTileThreads) bins[i / kRowBins][i % kRowBins] = 0.0;
+  __syncthreads();
+  int64_t cur = -1;
+  double a0 = 0.0, a1 = 0.0;
+  auto flush = [&]() {
+    if (cur < 0) return;
+    if (binned) {
+      atomicAdd(&bins[0][cur - first_row], a0);
+      atomicAdd(&bins[1][cur - first_row], a1);
+    } else {
+      atomicAdd(sums + cur, a0);
+      atomicAdd(sums + nrows + cur, a1);
+    }
+  };
+  for (int u = 0; u < kRowSumItems; ++u) {
+    const int64_t i = i0 + (int64_t)threadIdx.x * kRowSumItems + u;
+    if (i >= i1) break;
+    const int64_t r = keys[i] / E - row0;
+    if (r < 0 || r >= nrows || (binned && (r < first_row || r >= first_row + span))) {
+      raise_flag(err, MKG_DEV_BAD_KEY);
+      continue;
+    }
+    const float yv = y[i];
+    if (yv == 0.0f) continue;
+    if (r != cur) { flush(); cur = r; a0 = 0.0; a1 = 0.0; }
+    const float dr = d[r];
+    const float g = gx[i];
+    const float q = __fdiv_rn(yv, dr);
+    const float gq = g * fminf(dr, 1.0f);
+    a0 += (double)(g * q);
+    a1 += (double)__fdiv_rn(-(gq * yv), dr * dr);
+  }
+  flush();
+  if (binned) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < span; i += kTileThreads) {
+      if (bins[0][i] != 0.0) atomicAdd(sums + first_row + i, bins[0][i]);
+      if (bins[1][i] != 0.0) atomicAdd(sums + nrows + first_row + i, bins[1][i]);
+    }
+  }
+}
+
+// gy = (gx * c) / d + g_d[row] with g_d = sums[1] + [d <= 1] sums[0] (fp64, rounded once);
+// zero where y is zero.
+__global__ void mass_norm_grad_kernel(const int64_t* __restrict__ keys, const float* __restrict__ y,
+                                      const float* __restrict__ gx, int64_t n, int64_t E, int64_t row0,
+                                      int64_t nrows, const float* __restrict__ d, const double* __restrict__ sums,
+                                      float* __restrict__ gy) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = keys[i] / E - row0;
+    float out = 0.0f;
+    if (r >= 0 && r < nrows && y[i] != 0.0f) {
+      const float dr = d[r];
+      const float gq = gx[i] * fminf(dr, 1.0f);
+      const double gd = sums[nrows + r] + (dr <= 1.0f ? sums[r] : 0.0);
+      out = static_cast<float>((double)gq / (double)dr + gd);
+    }
+    gy[i] = out;
   }
 }
 
@@ -631,6 +786,49 @@ MKG_API int mkg_row_sums(const int64_t* keys, int64_t nnz, int64_t E, int64_t ro
   MKG_REQUIRE(blocks < INT32_MAX, "row_sums: too many entries");
   row_sums_kernel<<<(unsigned)blocks, kTileThreads, 0, st>>>(keys, nnz, E, row0, nrows, vals, out, dev_err);
   MKG_LAUNCHED("row_sums_kernel");
+  return MKG_OK;
+}
+
+MKG_API int mkg_mass_normalize(const int64_t* keys, const float* y, int64_t n, int64_t E, int64_t row0, int64_t nrows,
+                               const float* row_sums, float threshold, float* x, int64_t* dropped, unsigned* dev_err,
+                               mkg_stream stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MKG_REQUIRE(E > 0 && nrows > 0 && row0 >= 0 && n >= 0 && dropped, "mass_normalize: bad argument");
+  MKG_CUDA(cudaMemsetAsync(dropped, 0, sizeof(int64_t), st));
+  if (n == 0) return MKG_OK;
+  MKG_REQUIRE(keys && y && row_sums && x, "mass_normalize: null argument");
+  mass_norm_kernel<<<grid_for(n, 256, persistent_blocks(8)), 256, 0, st>>>(
+      keys, y, n, E, row0, nrows, row_sums, threshold, x, reinterpret_cast<unsigned long long*>(dropped), dev_err);
+  MKG_LAUNCHED("mass_norm_kernel");
+  return MKG_OK;
+}
+
+MKG_API int mkg_mass_normalize_grad_sums(const int64_t* keys, const float* y, const float* gx, int64_t n, int64_t E,
+                                         int64_t row0, int64_t nrows, const float* row_sums, double* sums,
+                                         unsigned* dev_err, mkg_stream stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MKG_REQUIRE(E > 0 && nrows > 0 && row0 >= 0 && n >= 0, "mass_normalize_grad_sums: bad sizes");
+  if (n == 0) return MKG_OK;
+  MKG_REQUIRE(keys && y && gx && row_sums && sums, "mass_normalize_grad_sums: null argument");
+  const int64_t per = (int64_t)kTileThreads * kRowSumItems;
+  const int64_t blocks = (n + per - 1) / per;
+  MKG_REQUIRE(blocks < INT32_MAX, "mass_normalize_grad_sums: too many entries");
+  mass_norm_grad_sums_kernel<<<(unsigned)blocks, kTileThreads, 0, st>>>(keys, y, gx, n, E, row0, nrows, row_sums,
+                                                                         sums, dev_err);
+  MKG_LAUNCHED("mass_norm_grad_sums_kernel");
+  return MKG_OK;
+}
+
+MKG_API int mkg_mass_normalize_grad(const int64_t* keys, const float* y, const float* gx, int64_t n, int64_t E,
+                                    int64_t row0, int64_t nrows, const float* row_sums, const double* sums, float* gy,
+                                    mkg_stream stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MKG_REQUIRE(E > 0 && nrows > 0 && row0 >= 0 && n >= 0, "mass_normalize_grad: bad sizes");
+  if (n == 0) return MKG_OK;
+  MKG_REQUIRE(keys && y && gx && row_sums && sums && gy, "mass_normalize_grad: null argument");
+  mass_norm_grad_kernel<<<grid_for(n, 256, persistent_blocks(8)), 256, 0, st>>>(keys, y, gx, n, E, row0, nrows,
+                                                                                 row_sums, sums, gy);
+  MKG_LAUNCHED("mass_norm_grad_kernel");
   return MKG_OK;
 }
 

@@ -215,12 +215,18 @@ class DeviceGraph:
         p = self._adj_keep["push_ptr"]
         return (p[1:] - p[:-1]).to(torch.int64)
 
-    def set_edge_factor(self, mask, weight, is_score: bool, scale: float) -> None:
+    def set_edge_factor(self, mask, weight, is_score: bool, scale: float, push_only: bool = False) -> None:
+        """Writes the edge factor of every neighbour-list record; ``push_only`` leaves the pull
+        list's factors as they were (the key-slab loop reads only the push list)."""
         lib = N.load()
         keep = []
         f = N.edge_factor(mask, weight, is_score, scale, keep)
-        N.check(lib.mkg_adjacency_set_factor(C_ref(self.struct), self.adjacency(), C_ref(f),
-                                             N.stream_handle(self.device)), "adjacency_set_factor")
+        adj = self.adjacency()
+        if push_only:
+            adj = N.Adjacency(None, None, adj.push_ptr, adj.push, adj.pull_tasks, adj.num_pull_tasks,
+                              adj.push_tasks, adj.num_push_tasks)
+        N.check(lib.mkg_adjacency_set_factor(C_ref(self.struct), adj, C_ref(f), N.stream_handle(self.device)),
+                "adjacency_set_factor")
         self.factor_writes += 1
 
     # -------------------------------------------------------------- per-fact endpoints

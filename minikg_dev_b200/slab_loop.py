@@ -83,10 +83,16 @@ class SlabEngine:
         return int(self.push.shape[0])
 
     def set_edge_factor(self, mask, weight, is_score: bool, scale: float) -> None:
-        """Rewrites the factor field of the push records from the mask / edge scores."""
-        self.g.set_edge_factor(mask, weight, is_score, scale)
-        if self.sel is not None:
-            self.push[:, 3] = self.full_push[self.sel, 3]
+        """Rewrites the factor field of this engine's push records from the mask / edge scores
+        (a rank-local list: only its own records)."""
+        if self.sel is None:
+            self.g.set_edge_factor(mask, weight, is_score, scale, push_only=True)
+            return
+        keep = []
+        f = N.edge_factor(mask, weight, is_score, scale, keep)
+        N.check(N.load().mkg_records_set_factor(self.push.data_ptr(), self.records, self.g.num_facts,
+                                                ctypes.byref(f), N.stream_handle(self.dev)), "records_set_factor")
+        self.g.factor_writes += 1
 
     def ensure_store(self, rows: int) -> None:
         """Sizes the zero-kept store: ``rows`` (b, l) rows of the destination range, or as many
@@ -118,9 +124,12 @@ def _windows(total_rows: int, per: int):
 
 def _row_slices(keys: torch.Tensor, E: int, div: int, bounds) -> list[tuple[int, int]]:
     """Positions [a, b) of the ascending ``keys`` whose row ``(key // E) // div`` falls in each
-    window ``[r0, r0 + n)``."""
+    window ``[r0, r0 + n)``.  One window takes every key (no host synchronisation): keys outside
+    its rows are then flagged by the kernels."""
     if keys.numel() == 0:
         return [(0, 0) for _ in bounds]
+    if len(bounds) == 1:
+        return [(0, int(keys.numel()))]
     edges = torch.tensor([r0 * div * E for r0, _ in bounds] + [(bounds[-1][0] + bounds[-1][1]) * div * E],
                          dtype=torch.int64, device=keys.device)
     pos = torch.searchsorted(keys, edges).tolist()
@@ -170,15 +179,16 @@ def graph_bytes(eng: SlabEngine, keys) -> int:
     return int((deg * 8 + grp * 10 + 8).sum())
 
 
-def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int):
+def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True):
     """One hop's concat-summed output over the engine's destinations: (keys ascending, values,
-    fp64 row sums [BL])."""
+    fp64 row sums [BL]).  ``check``: refuse frontier keys outside [B, L, E] on the host (the
+    loop, whose keys are its own outputs, skips that synchronisation)."""
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
     n = int(w_h.shape[-1])
     wf = w_h.detach().to(torch.float32).reshape(BL, n).contiguous()
-    if keys.numel() and (int(keys[0]) < 0 or int(keys[-1]) >= BL * E):
+    if check and keys.numel() and (int(keys[0]) < 0 or int(keys[-1]) >= BL * E):
         raise RuntimeError("slab hop: a frontier key lies outside [B, L, E]")
     eng.ensure_store(BL)
     bounds = list(_windows(BL, eng.rows_per_window))
@@ -308,6 +318,37 @@ def spread_over_rules(eng: SlabEngine, out_keys, g_out, keys, B: int, L: int):
     return g
 
 
+def _mass_normalize(keys, y, E: int, BL: int, d32, threshold: float):
+    """(x = (y / d) * min(d, 1) per entry, number of entries the loop drops: zero or under the
+    threshold)."""
+    lib = N.load()
+    dev = y.device
+    x = torch.empty_like(y)
+    dropped = torch.zeros(1, dtype=torch.int64, device=dev)
+    N.check(lib.mkg_mass_normalize(keys.data_ptr(), y.data_ptr(), int(y.numel()), E, 0, BL, d32.data_ptr(),
+                                   float(threshold), x.data_ptr(), dropped.data_ptr(), N.error_word(dev).data_ptr(),
+                                   N.stream_handle(dev)), "mass_normalize")
+    return x, int(dropped.item())
+
+
+def _mass_normalize_grad(keys, y, gx, E: int, BL: int, d32, spec):
+    """Gradient of the mass normalisation at its input: row sums of both terms in fp64
+    (all-reduced over ranks), then the per-entry gradient."""
+    lib = N.load()
+    dev = y.device
+    sums = torch.zeros((2, BL), dtype=torch.float64, device=dev)
+    n = int(y.numel())
+    st = N.stream_handle(dev)
+    N.check(lib.mkg_mass_normalize_grad_sums(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL,
+                                             d32.data_ptr(), sums.data_ptr(), N.error_word(dev).data_ptr(), st),
+            "mass_normalize_grad_sums")
+    _all_reduce(sums, spec)
+    gy = torch.empty_like(y)
+    N.check(lib.mkg_mass_normalize_grad(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL, d32.data_ptr(),
+                                        sums.data_ptr(), gy.data_ptr(), st), "mass_normalize_grad")
+    return gy
+
+
 # ----------------------------------------------------------------------------- the loop
 class _Hop:
     __slots__ = ("keys_in", "vals_in", "n_own", "offset", "prune_sel", "n_pre", "keys_y", "y", "d", "keep")
@@ -321,33 +362,27 @@ def _all_reduce(t, spec):
 
 
 def _gather(keys, vals, spec):
-    """All ranks' frontier entries in rank order (ascending keys within each rank); returns
-    (keys, values, this rank's offset)."""
+    """The whole frontier on every rank, ascending keys (ranks own disjoint keys); returns
+    (keys, values, (this rank's offset in rank order, the sorting permutation) or None)."""
     if spec is None or spec.world == 1:
-        return keys, vals, 0
+        return keys, vals, None
     from .sharded import _all_gather_padded, _gather_counts
     counts = _gather_counts(int(keys.numel()), keys.device, spec.group)
     k_all = torch.cat(_all_gather_padded(keys, counts, spec.group))
     v_all = torch.cat(_all_gather_padded(vals.detach(), counts, spec.group))
     off = sum(counts[: spec.rank])
-    # expansion windows need ascending keys: sort the gathered entries (ranks own disjoint keys)
+    # expansion windows need ascending keys: sort the gathered entries
     order = torch.argsort(k_all)
     return k_all[order], v_all[order], (off, order)
 
 
-def _prune(keys, vals, E, topk_nodes, spec):
+def _prune(keys, vals, E, topk_nodes):
+    """prune_sparse3d_active_entities (drum.py:54-80) on the whole frontier (every rank holds
+    it after the gather, so every rank selects the same entries)."""
     if topk_nodes <= 0:
         return keys, vals, None
-    if spec is None or spec.world == 1:
-        from .sparse_loop import _prune as prune_local
-        return prune_local(keys, vals, E, topk_nodes)
-    from .sharded import _prune_global
-    n_before = keys.numel()
-    k2, v2 = _prune_global(keys, vals.detach(), E, topk_nodes, spec)
-    if k2.numel() == n_before:
-        return keys, vals, None
-    sel = torch.searchsorted(keys, k2)
-    return k2, v2, sel
+    from .sparse_loop import _prune as prune_state
+    return prune_state(keys, vals, E, topk_nodes)
 
 
 class SlabHopLoop(autograd.Function):
@@ -371,6 +406,8 @@ class SlabHopLoop(autograd.Function):
         factor_write = g.factor_writes
         wf = w_hops.detach().to(torch.float32).contiguous()
         hd = heads.to(device=dev, dtype=torch.int64)
+        if bool(((hd < 0) | (hd >= E)).any()):
+            raise ValueError(f"query heads must lie in [0, {E})")
         keys = (torch.arange(BL, device=dev) * E + hd.repeat_interleave(L))
         own = (hd.repeat_interleave(L) >= eng.lo) & (hd.repeat_interleave(L) < eng.hi)
         keys = torch.sort(keys[own]).values
@@ -378,25 +415,28 @@ class SlabHopLoop(autograd.Function):
         hops, msgs = [], []
         for h in range(K):
             st = _Hop()
-            st.n_pre = int(keys.numel())
-            keys, vals, st.prune_sel = _prune(keys, vals, E, int(topk_nodes), spec)
             st.n_own = int(keys.numel())
             k_all, v_all, st.offset = _gather(keys, vals, spec)
+            st.n_pre = int(k_all.numel())
+            k_all, v_all, st.prune_sel = _prune(k_all, v_all, E, int(topk_nodes))
             st.keys_in, st.vals_in = k_all, v_all
             msgs.append(eng.full_degree[k_all % E].sum())
-            ky, y, d = expand_forward(eng, k_all, v_all, wf[h], BL)
+            ky, y, d = expand_forward(eng, k_all, v_all, wf[h], BL, check=False)
             _all_reduce(d, spec)
             d32 = d.to(torch.float32)
-            rows = ky // E
-            dr = d32[rows]
-            x = y / dr * d32.clamp_max(1.0)[rows]
-            keep = x != 0
-            if threshold > 0:
-                keep &= x >= threshold
-            st.keys_y, st.y, st.d, st.keep = ky, y, d32, keep
-            keys, vals = ky[keep], x[keep]
+            x = _mass_normalize(ky, y, E, BL, d32, threshold)
+            st.keys_y, st.y, st.d, st.keep = ky, y, d32, None
+            if x[1]:  # some results are zero or under the threshold: the loop drops them
+                keep = x[0] != 0
+                if threshold > 0:
+                    keep &= x[0] >= threshold
+                st.keep = keep
+                keys, vals = ky[keep], x[0][keep]
+            else:
+                keys, vals = ky, x[0]
             hops.append(st)
         out_keys, out_vals = sum_over_rules(eng, keys, vals, B, L)
+        N.raise_device_errors(dev)  # an out-of-range index any kernel of the forward met
         ctx.hops, ctx.eng, ctx.spec = hops, eng, spec
         ctx.factor_write = factor_write
         ctx.final_keys = keys
@@ -430,35 +470,25 @@ class SlabHopLoop(autograd.Function):
         g_state = spread_over_rules(eng, ctx.out_keys, g_vals, ctx.final_keys, B, L)
         for h in range(K - 1, -1, -1):
             st = ctx.hops[h]
-            y, d = st.y, st.d
-            rows = st.keys_y // E
-            nz = y != 0
-            gx = torch.zeros_like(y)
-            gx[st.keep] = g_state
-            dr = d[rows]
-            c = d.clamp_max(1.0)
-            q = y / dr
-            g_q = gx * c[rows]
-            zero = torch.zeros_like(y)
-            part = torch.stack([N.row_sums(st.keys_y, torch.where(nz, gx * q, zero), E, BL),
-                                N.row_sums(st.keys_y, torch.where(nz, -(g_q * y) / (dr * dr), zero), E, BL)])
-            _all_reduce(part, spec)
-            g_d = part[1] + torch.where(d <= 1.0, part[0], torch.zeros_like(part[0]))
-            gy = torch.where(nz, (g_q.double() / dr.double() + g_d[rows]).to(torch.float32), zero)
+            if st.keep is None:
+                gx = g_state.to(torch.float32).contiguous()
+            else:
+                gx = torch.zeros_like(st.y)
+                gx[st.keep] = g_state
+            gy = _mass_normalize_grad(st.keys_y, st.y, gx, E, BL, st.d, spec)
             gsp = expand_backward(eng, st.keys_in, st.vals_in, ctx.wf[h], BL, st.keys_y, gy, factor, grad_w64[h],
                                   grad_edge)
-            if spec is not None and spec.world > 1:
+            if st.prune_sel is not None:  # back to the frontier before the prune
+                full = torch.zeros(st.n_pre, dtype=gsp.dtype, device=dev)
+                full[st.prune_sel] = gsp
+                gsp = full
+            if st.offset is not None:  # several ranks: sum the partials, keep this rank's entries
                 _all_reduce(gsp, spec)
                 off, order = st.offset
                 mine = torch.empty_like(gsp)
                 mine[order] = gsp          # back to rank order of the gather
                 gsp = mine[off: off + st.n_own]
-            grad_sp = gsp.to(torch.float32)
-            if st.prune_sel is not None:
-                full = torch.zeros(st.n_pre, dtype=torch.float32, device=dev)
-                full[st.prune_sel] = grad_sp
-                grad_sp = full
-            g_state = grad_sp
+            g_state = gsp.to(torch.float32)
         _all_reduce(grad_w64, spec)
         if grad_edge is not None:
             _all_reduce(grad_edge, spec)

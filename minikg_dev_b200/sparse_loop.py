@@ -27,6 +27,8 @@ from torch import autograd
 from . import _native as N
 from . import fastlog_kernel as FK
 from .graph import DeviceGraph
+from .slab_loop import _mass_normalize, _mass_normalize_grad
+from .sparse_reducers import _reduce
 
 
 class _HopState:
@@ -181,21 +183,20 @@ class SparseHopLoop(autograd.Function):
             st.keys_in, st.vals_in = keys, vals
             st.idx_y, st.keys_y, st.y, st.params, m = _op_forward(g, keys, vals, wf[h], factor, B, L, cap, keep_alive)
             msgs.append(m)
-            y = st.y
-            rows = st.keys_y // E
-            nz = y != 0
-            d = N.row_sums(st.keys_y, y, E, B * L).to(torch.float32)  # fp64 sums in key order, rounded once
-            x = y / d[rows] * d.clamp_max(1.0)[rows]
-            keep = nz & (x != 0)
-            if threshold > 0:
-                keep &= x >= threshold
-            st.d, st.keep = d, keep
-            keys, vals = st.keys_y[keep], x[keep]
+            d = N.row_sums(st.keys_y, st.y, E, B * L).to(torch.float32)  # fp64 sums in key order, rounded once
+            x, dropped = _mass_normalize(st.keys_y, st.y, E, B * L, d, threshold)
+            st.d, st.keep = d, None
+            if dropped:  # zeros (explicit zero messages) or values under the threshold leave the state
+                keep = x != 0
+                if threshold > 0:
+                    keep &= x >= threshold
+                st.keep = keep
+                keys, vals = st.keys_y[keep], x[keep]
+            else:
+                keys, vals = st.keys_y, x
             hops.append(st)
-        # sum_sp_3d: the sum over rules
-        be, e = keys // E, keys % E
-        out_keys, inv = torch.unique((be // L) * E + e, sorted=True, return_inverse=True)
-        out_vals = torch.zeros(out_keys.numel(), dtype=torch.float32, device=dev).index_add_(0, inv, vals)
+        # sum_sp_3d: the sum over rules, coalesced on the device (fp64 run sums)
+        out_keys, out_vals, inv, _ = _reduce(((keys // E) // L) * E + keys % E, vals, 0)
         ctx.hops, ctx.inv, ctx.g = hops, inv, g
         ctx.factor, ctx.keep_alive = factor, keep_alive
         ctx.wf, ctx.shape = wf, (K, B, L, n)
@@ -218,21 +219,13 @@ class SparseHopLoop(autograd.Function):
         g_state = g_vals.to(torch.float32)[ctx.inv]
         for h in range(K - 1, -1, -1):
             st = ctx.hops[h]
-            y, d = st.y, st.d
-            rows = st.keys_y // E
-            nz = y != 0
-            gx = torch.zeros_like(y)
-            gx[st.keep] = g_state
-            dr = d[rows]
-            c = d.clamp_max(1.0)
-            q = y / dr
-            g_q = gx * c[rows]
-            zero = torch.zeros_like(y)
-            # row sums of the normalisation gradient in fp64 (they cancel: gradients of both signs)
-            g_c = N.row_sums(st.keys_y, torch.where(nz, gx * q, zero), E, B * L)
-            g_d = N.row_sums(st.keys_y, torch.where(nz, -(g_q * y) / (dr * dr), zero), E, B * L)
-            g_d = g_d + torch.where(d <= 1.0, g_c, torch.zeros_like(g_c))
-            gy = torch.where(nz, (g_q.double() / dr.double() + g_d[rows]).to(torch.float32), torch.zeros_like(y))
+            if st.keep is None:
+                gx = g_state.to(torch.float32).contiguous()
+            else:
+                gx = torch.zeros_like(st.y)
+                gx[st.keep] = g_state
+            # the normalisation gradient: both row sums in one fp64 pass, then per entry
+            gy = _mass_normalize_grad(st.keys_y, st.y, gx, E, B * L, st.d, None)
             grad_sp, gw, ge = _op_backward(g, st, ctx.wf[h], ctx.factor, gy, ctx.want_edge)
             grad_w[h] = gw
             if ge is not None:
