@@ -661,7 +661,29 @@ def slab_extras(a, wl, kg, g, eng, heads, w_hops, scores, flush, B):
     out["capped"] = {"edge_cap": cap, "ms_per_step": ms, "messages_per_step": M_cap, "gteps": M_cap / ms / 1e6,
                      "path": "sparse hop loop (merged per-hop op, hash message store), fwd+bwd"}
 
-    # the large graphs' decode: the max-aggregation loop with the production cap, top-100
+    # the configuration's decode, uncapped: the max-aggregation loop on the key-slab store, top-100
+    from minikg_dev_b200.slab_loop import slab_decode_max
+    hbm, peak_kind = peaks()
+    mlist = []
+    slab_decode_max(eng, heads, w_hops, 100, scores, msgs_out=mlist)
+    M_dec = int(torch.stack(mlist).sum())
+    udec = lambda: slab_decode_max(eng, heads, w_hops, 100, scores)  # noqa: E731
+    udms = statistics.mean(timed(udec, 3, flush))
+    eng.trace = []
+    udec()
+    torch.cuda.synchronize()
+    trace, eng.trace = eng.trace, None
+    hop_ms = [e0.elapsed_time(e1) for _, e0, e1, _ in trace]
+    hop_bytes = [byts for _, _, _, byts in trace]
+    gbs = sum(hop_bytes) / (sum(hop_ms) / 1e3) / 1e9
+    out["decode_uncapped"] = {
+        "ms": udms, "topk": 100, "edge_cap": "uncapped", "messages": M_dec, "gteps": M_dec / udms / 1e6,
+        "path": "slab_loop.slab_decode_max (atomicMax key slab, ordered row sums, max over rules, device top-k)",
+        "roofline": {"bound": "hbm", "kernel": "slab_expand_kernel (max mode)", "achieved": gbs, "peak": hbm,
+                     "unit": "GB/s", "frac": gbs / hbm, "peak_kind": peak_kind, "ms_per_hop": hop_ms,
+                     "bytes_per_hop": hop_bytes}}
+
+    # the production-cap decode of the same batch: the max-aggregation sparse loop, top-100
     dec = lambda: decode_max_sparse(g, heads, w_hops, 100, scores, cap=cap)  # noqa: E731
     dec()
     dms = statistics.mean(timed(dec, 3, flush))

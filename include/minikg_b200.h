@@ -397,10 +397,14 @@ size_t mkg_slab_expand_workspace_bytes(int64_t nnz);
  * list restricted to destinations in [lo, lo + extent)) the value (x * w[b, l, channel]) *
  * factor at key (b, l, neighbour), plus (identity != 0) x * w[b, l, n - 1] at (b, l, s).
  * w is [B * L, n].  Zero-valued messages are left out (the hop loop drops zeros after its
- * normalisation).  Replaces the forward op of the uncapped hop (see above). */
+ * normalisation).  agg_mode 0 adds the messages of a key (the sum hop, see above); agg_mode 1
+ * keeps their maximum (the values of the max-aggregation hop, op agg_mode 1 followed by
+ * sparse3d_max(ind, ori, inv), model_mmDRUM_kernel_sp.py:237-270, 388-445; the values must be
+ * non-negative, as the loop's are). */
 int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, const int64_t* keys, const float* vals,
-                    int64_t nnz, const float* w, int64_t n, int32_t identity, const mkg_slab_window* win,
-                    void* store, void* workspace, size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+                    int64_t nnz, const float* w, int64_t n, int32_t identity, int32_t agg_mode,
+                    const mkg_slab_window* win, void* store, void* workspace, size_t workspace_bytes,
+                    unsigned* dev_err, mkg_stream stream);
 /* Number of touched keys in the store -> count_out (device int64).  The workspace (also read
  * by mkg_slab_emit) keeps per-tile offsets. */
 size_t mkg_slab_collect_workspace_bytes(int64_t slots);
@@ -411,7 +415,8 @@ int mkg_slab_count(const mkg_slab_window* win, const void* store, void* workspac
  * row_sums[r] in fp64 (the column sums of normalize_sparse3d, drum.py:31-51). */
 int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* workspace, size_t workspace_bytes,
                   int64_t count, int64_t* keys_out, float* vals_out, double* row_sums, mkg_stream stream);
-/* Writes (mode 0) or adds with a touched mark (mode 1) values at keys whose row is
+/* Writes (mode 0), adds with a touched mark (mode 1) or raises to the maximum with a touched
+ * mark (mode 2: max_sp_3d's max over rules with row_div = L) values at keys whose row is
  * (key / E) / row_div (row_div = L maps (b, l, e) to the [B, E] key b * E + e: sum_sp_3d,
  * fastlog_bridge.py:17-23). */
 int mkg_slab_put(const mkg_slab_window* win, void* store, const int64_t* keys, const float* vals, int64_t nnz,

@@ -72,8 +72,16 @@ __device__ __forceinline__ int64_t slot_of(const Window& w, int64_t key, int64_t
   return row * w.extent + e;
 }
 
-__device__ __forceinline__ void touch_add(const Store& s, int64_t slot, float v) {
-  const float old = atomicAdd(s.val + slot, v);
+// Adds (sum) or raises to (max) a slot; returns the slot's previous value.  The max works on
+// the float's bits as an unsigned integer, which orders non-negative floats correctly (the
+// hop loop's messages are non-negative).
+__device__ __forceinline__ float slot_accumulate(float* p, float v, int max_mode) {
+  if (max_mode) return __uint_as_float(atomicMax(reinterpret_cast<unsigned*>(p), __float_as_uint(v)));
+  return atomicAdd(p, v);
+}
+
+__device__ __forceinline__ void touch_add(const Store& s, int64_t slot, float v, int max_mode = 0) {
+  const float old = slot_accumulate(s.val + slot, v, max_mode);
   if (old == 0.0f) atomicOr(s.bits + (slot >> 5), 1u << (slot & 31));
 }
 
@@ -115,6 +123,7 @@ struct ExpandArgs {
   const float* w;            // [B * L, n]
   int64_t n;
   int identity;
+  int max_mode;              // 1: slots keep the largest message (values must be >= 0)
   Window win;
   unsigned* err;
 };
@@ -141,7 +150,7 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_kernel(ExpandArgs 
     const int64_t k = c - a.chunk_ptr[i];
     if (k == 0 && lane == 0 && a.identity && s >= a.win.lo && s < a.win.lo + a.win.extent) {
       const float v = x * wrow[a.n - 1];
-      if (v != 0.0f) touch_add(st, lrow * a.win.extent + (s - a.win.lo), v);
+      if (v != 0.0f) touch_add(st, lrow * a.win.extent + (s - a.win.lo), v, a.max_mode);
     }
     const int64_t rb = a.push_ptr[s] + k * kChunkRecs;
     const int64_t re = min(rb + kChunkRecs, (int64_t)a.push_ptr[s + 1]);
@@ -174,7 +183,7 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_kernel(ExpandArgs 
     for (int u = 0; u < kU; ++u) {
       const float v = (x * wv[u]) * __int_as_float(rec[u].w);
       old[u] = 1.0f;  // no add: nothing to mark
-      if (slot[u] >= 0 && v != 0.0f) old[u] = atomicAdd(st.val + slot[u], v);
+      if (slot[u] >= 0 && v != 0.0f) old[u] = slot_accumulate(st.val + slot[u], v, a.max_mode);
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u)
@@ -334,7 +343,7 @@ __global__ void slab_put_kernel(Store st, Window win, const int64_t* __restrict_
     if (slot < 0) { raise_flag(err, MKG_DEV_BAD_KEY); continue; }
     const float v = vals[i];
     if (mode == 0) st.val[slot] = v;
-    else if (v != 0.0f) touch_add(st, slot, v);
+    else if (v != 0.0f) touch_add(st, slot, v, mode == 2);
   }
 }
 
@@ -659,19 +668,20 @@ MKG_API size_t mkg_slab_expand_workspace_bytes(int64_t nnz) {
 }
 
 MKG_API int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, const int64_t* keys, const float* vals,
-                            int64_t nnz, const float* w, int64_t n, int32_t identity, const mkg_slab_window* win,
-                            void* store, void* workspace, size_t workspace_bytes, unsigned* dev_err,
-                            mkg_stream stream) {
+                            int64_t nnz, const float* w, int64_t n, int32_t identity, int32_t agg_mode,
+                            const mkg_slab_window* win, void* store, void* workspace, size_t workspace_bytes,
+                            unsigned* dev_err, mkg_stream stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   MKG_REQUIRE(window_ok(win), "slab_expand: bad window");
   MKG_REQUIRE(nnz >= 0 && n >= 1 && n <= INT32_MAX, "slab_expand: bad sizes");
+  MKG_REQUIRE(agg_mode == 0 || agg_mode == 1, "slab_expand: agg_mode must be 0 (sum) or 1 (max)");
   if (nnz == 0) return MKG_OK;
   MKG_REQUIRE(push_ptr && push && keys && vals && w && store && workspace, "slab_expand: null argument");
   MKG_REQUIRE(nnz < INT32_MAX, "slab_expand: frontier of %lld entries exceeds the scan limit", (long long)nnz);
   int64_t* cp = nullptr;
   int rc = build_chunks(push_ptr, keys, nnz, win->E, workspace, workspace_bytes, &cp, dev_err, st);
   if (rc) return rc;
-  ExpandArgs a{push_ptr, reinterpret_cast<const int4*>(push), keys, vals, nnz, cp, w, n, identity,
+  ExpandArgs a{push_ptr, reinterpret_cast<const int4*>(push), keys, vals, nnz, cp, w, n, identity, agg_mode,
                make_window(*win), dev_err};
   slab_expand_kernel<<<expand_grid(nnz), kExpandThreads, 0, st>>>(a, make_store(store, win->nrows * win->extent));
   MKG_LAUNCHED("slab_expand_kernel");
@@ -731,7 +741,7 @@ MKG_API int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* w
 MKG_API int mkg_slab_put(const mkg_slab_window* win, void* store, const int64_t* keys, const float* vals, int64_t nnz,
                          int64_t row_div, int32_t mode, unsigned* dev_err, mkg_stream stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  MKG_REQUIRE(window_ok(win) && store && row_div >= 1 && (mode == 0 || mode == 1) && nnz >= 0, "slab_put: bad argument");
+  MKG_REQUIRE(window_ok(win) && store && row_div >= 1 && mode >= 0 && mode <= 2 && nnz >= 0, "slab_put: bad argument");
   if (nnz == 0) return MKG_OK;
   MKG_REQUIRE(keys && vals, "slab_put: null argument");
   slab_put_kernel<<<grid_for(nnz, 256, persistent_blocks(8)), 256, 0, st>>>(
@@ -767,7 +777,7 @@ MKG_API int mkg_slab_expand_backward(const int32_t* push_ptr, const mkg_adj_edge
   int64_t* cp = nullptr;
   int rc = build_chunks(push_ptr, keys, nnz, win->E, workspace, workspace_bytes, &cp, dev_err, st);
   if (rc) return rc;
-  ExpandArgs a{push_ptr, reinterpret_cast<const int4*>(push), keys, vals, nnz, cp, w, n, identity,
+  ExpandArgs a{push_ptr, reinterpret_cast<const int4*>(push), keys, vals, nnz, cp, w, n, identity, 0,
                make_window(*win), dev_err};
   slab_expand_backward_kernel<<<expand_grid(nnz), kExpandThreads, 0, st>>>(
       a, static_cast<const float*>(store), make_factor(*ef), num_facts, grad_sp, grad_w, grad_edge);

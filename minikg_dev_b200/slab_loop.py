@@ -179,10 +179,11 @@ def graph_bytes(eng: SlabEngine, keys) -> int:
     return int((deg * 8 + grp * 10 + 8).sum())
 
 
-def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True):
+def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True, agg_mode: int = 0):
     """One hop's concat-summed output over the engine's destinations: (keys ascending, values,
-    fp64 row sums [BL]).  ``check``: refuse frontier keys outside [B, L, E] on the host (the
-    loop, whose keys are its own outputs, skips that synchronisation)."""
+    fp64 row sums [BL]; zeros for ``agg_mode`` 1, which keeps each key's largest message
+    instead).  ``check``: refuse frontier keys outside [B, L, E] on the host (the loop, whose
+    keys are its own outputs, skips that synchronisation)."""
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
@@ -205,17 +206,18 @@ def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True
             ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(b - a), dev)
             ev = _events(eng)
             N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), b - a,
-                                        wf.data_ptr(), n, 1, ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(),
-                                        ws.numel(), err, st), "slab_expand")
+                                        wf.data_ptr(), n, 1, int(agg_mode), ctypes.byref(win), eng.store.data_ptr(),
+                                        ws.data_ptr(), ws.numel(), err, st), "slab_expand")
             if ev is not None:
                 ev[1].record()
-            ko, vo, rs = _collect(eng, win, True)
+            ko, vo, rs = _collect(eng, win, agg_mode == 0)
             if ev is not None:  # frontier in + output out (12 B per key: 8 B key, 4 B value), rule weights
                 eng.trace.append(("fwd", ev[0], ev[1], graph_bytes(eng, k) + 12 * (b - a) + 12 * ko.numel()
                                   + nr * n * 4))
             out_k.append(ko)
             out_v.append(vo)
-            d[r0:r0 + nr] = rs
+            if rs is not None:
+                d[r0:r0 + nr] = rs
     if not out_k:
         return (torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev), d)
     return torch.cat(out_k), torch.cat(out_v), d
@@ -264,9 +266,10 @@ def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, gy, facto
     return gsp
 
 
-def sum_over_rules(eng: SlabEngine, keys, vals, B: int, L: int):
-    """sum_sp_3d: ``(b, l, e)`` entries added at ``(b, e)``; returns ascending ``b * E + e`` keys
-    and values (the store's windows then run over queries)."""
+def sum_over_rules(eng: SlabEngine, keys, vals, B: int, L: int, take_max: bool = False):
+    """sum_sp_3d: ``(b, l, e)`` entries added at ``(b, e)`` (``take_max``: max_sp_3d's maximum
+    instead, for non-negative values); returns ascending ``b * E + e`` keys and values (the
+    store's windows then run over queries)."""
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
@@ -282,7 +285,7 @@ def sum_over_rules(eng: SlabEngine, keys, vals, B: int, L: int):
             continue
         win = eng.window(r0, nr)
         N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), keys[a:b].data_ptr(), vf[a:b].data_ptr(),
-                                 b - a, L, 1, err, st), "slab_put")
+                                 b - a, L, 2 if take_max else 1, err, st), "slab_put")
         k, v, _ = _collect(eng, win, False)
         ok.append(k)
         ov.append(v)
@@ -519,3 +522,49 @@ def slab_proof_scores(engine: SlabEngine, heads: torch.Tensor, w_hops: torch.Ten
                                          float(threshold), spec)
     out = torch.sparse_coo_tensor(torch.stack([keys // E, keys % E]), vals, (B, E), is_coalesced=True)
     return (out.to_dense() if dense else out), msgs
+
+
+@torch.no_grad()
+def slab_decode_max(engine: SlabEngine, heads: torch.Tensor, w_hops: torch.Tensor, topk: int,
+                    edge_scores: torch.Tensor | None, mask: torch.Tensor | None = None, is_score: bool = True,
+                    scale: float = 1.0, msgs_out: list | None = None):
+    """The max-aggregation loop of src/model_mmDRUM_kernel_sp.py:388-445, uncapped, on the
+    key-slab store: per hop every key keeps its largest message (the op with ``agg_mode=1``
+    followed by ``sparse3d_max(ind, ori, inv)``: the value of a maximum does not depend on which
+    tied message wins), then ``norm_sp_3d`` (row sums added one by one in key order, as the
+    reference's CPU ``index_put_``, clamped at 1e-7; zeros dropped); after the last hop the max
+    over rules (``norm_sp_3d_max``); then the decode order of ordered_tail_scores
+    (decode_core.py:350-363) on the bounded scores, ``topk`` per query.  Bit-exact with the
+    reference.  Returns (keys ``b * E + e`` ascending, raw scores, tails [B, topk] -1 padded,
+    bounded scores [B, topk], counts [B]); with ``msgs_out`` the message count of every hop is
+    appended (device scalars)."""
+    from .proof import sparse_topk
+    N.require_cuda(w_hops, "w_hops")
+    K, B, L, n = (int(s) for s in w_hops.shape)
+    eng = engine
+    E = eng.g.num_entities
+    if eng.lo != 0 or eng.hi != E:
+        raise ValueError("slab_decode_max runs on a whole-range engine")
+    dev = eng.dev
+    BL = B * L
+    eng.set_edge_factor(mask, edge_scores.detach() if edge_scores is not None else None, is_score, scale)
+    wf = w_hops.detach().to(torch.float32).contiguous()
+    hd = heads.to(device=dev, dtype=torch.int64)
+    if bool(((hd < 0) | (hd >= E)).any()):
+        raise ValueError(f"query heads must lie in [0, {E})")
+    keys = torch.sort(torch.arange(BL, device=dev) * E + hd.repeat_interleave(L)).values
+    vals = torch.ones(BL, dtype=torch.float32, device=dev)
+    for h in range(K):
+        if msgs_out is not None:
+            msgs_out.append(eng.full_degree[keys % E].sum())
+        ky, y, _ = expand_forward(eng, keys, vals, wf[h], BL, check=False, agg_mode=1)
+        rows = ky // E
+        seg = torch.searchsorted(rows, torch.arange(BL + 1, device=dev, dtype=rows.dtype))
+        d = N.segment_sum(seg, y, ordered=True).clamp(min=1e-7)
+        x = y / d[rows]
+        keep = torch.nonzero(x != 0, as_tuple=True)[0]
+        keys, vals = ky[keep], x[keep]
+    out_keys, out_vals = sum_over_rules(eng, keys, vals, B, L, take_max=True)
+    N.raise_device_errors(dev)
+    tails, scores, counts = sparse_topk(out_keys, out_vals, B, E, int(topk))
+    return out_keys, out_vals, tails, scores, counts

@@ -171,13 +171,34 @@ def test_slab_bad_frontier_entity_is_reported():
     wf = T(w_hops[0]).reshape(4, -1).contiguous()
     ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(2), DEV)
     N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k1.data_ptr(), v1.data_ptr(), 2,
-                                wf.data_ptr(), wf.shape[1], 1, ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(),
+                                wf.data_ptr(), wf.shape[1], 1, 0, ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(),
                                 ws.numel(), N.error_word(DEV).data_ptr(), N.stream_handle(DEV)), "slab_expand")
     with pytest.raises(RuntimeError, match="outside"):
         N.raise_device_errors(DEV)
     eng.store.zero_()  # the accepted key's messages are still in the store
     torch.cuda.synchronize()
     assert torch.ones(4, device=DEV).sum().item() == 4.0
+
+
+@pytest.mark.parametrize("gname,B,L,K,store_rows", [("hubby", 9, 3, 3, 0), ("g2", 6, 3, 3, 0), ("hubby", 9, 3, 2, 4)])
+def test_slab_decode_max_bit_exact(gname, B, L, K, store_rows):
+    """The uncapped max-aggregation decode on the key-slab store (also window by window):
+    raw scores, tails and bounded scores bit-exact against the oracle."""
+    from minikg_dev_b200 import _native as N
+    from minikg_dev_b200.slab_loop import slab_decode_max
+    h, r, t, E, R, heads, w_hops, scores, mask = _case(gname, B, L, K, 31 + B)
+    kw = {"store_bytes": int(N.load().mkg_slab_store_bytes(store_rows * E))} if store_rows else {}
+    csr, eng = _engine(h, r, t, E, R, **kw)
+    keys, raw, tails, sc, counts = slab_decode_max(eng, T(heads), T(w_hops), 20, T(scores))
+    final, _ = O.proof_max_forward(heads, w_hops, csr, mask, scores, B, L, E, R)
+    np.testing.assert_array_equal(keys.cpu().numpy(), final[0])
+    np.testing.assert_array_equal(raw.cpu().numpy(), final[1])
+    ot, osc, oc = O.decode_topk(final, B, E, 20)
+    np.testing.assert_array_equal(tails.cpu().numpy(), ot)
+    np.testing.assert_array_equal(sc.cpu().numpy(), osc)
+    np.testing.assert_array_equal(counts.cpu().numpy(), oc)
+    torch.cuda.synchronize()
+    assert _store_is_zero(eng)
 
 
 # ----------------------------------------------------------------------------- two GPUs
