@@ -358,6 +358,14 @@ int mkg_proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int
 int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails,
                     float* scores, int64_t* counts, mkg_stream stream);
 
+/* The same decode ordering on a sparse [B, E] result: keys [nnz] (b * E + e, ascending) and
+ * raw values [nnz]; every stored entry is a candidate (as proof.py:729-758 takes the rows of
+ * the sparse tensor).  One block per query finds its row by binary search; keys of rows
+ * outside [0, B) are ignored.  tails [B, topk] (-1 padded), scores [B, topk], counts [B];
+ * topk in [1, 1024]. */
+int mkg_sparse_topk(const int64_t* keys, const float* vals, int64_t nnz, int64_t B, int64_t E, int64_t topk,
+                    int64_t* tails, float* scores, int64_t* counts, mkg_stream stream);
+
 /* out[s] = values[seg_ptr[s]] + values[seg_ptr[s] + 1] + ... + values[seg_ptr[s+1] - 1],
  * added one by one in index order in fp32 (device pointers; seg_ptr [nseg + 1], int64).
  * The row sums of norm_sp_3d (src/model_mmDRUM_kernel_sp.py:39-52) over a coalesced COO

@@ -122,6 +122,7 @@ SIGNATURES = {
     "mkg_proof_decode_max": (C.c_int, [P(Graph), P(Adjacency), vp, vp, P(ProofParams), i64, vp, vp, vp, vp, vp,
                                        C.c_size_t, vp, vp]),
     "mkg_decode_topk": (C.c_int, [vp, i64, i64, i64, vp, vp, vp, vp]),
+    "mkg_sparse_topk": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_segment_sum_ordered": (C.c_int, [vp, i64, vp, vp, vp]),
     "mkg_segment_sum": (C.c_int, [vp, i64, vp, vp, vp]),
     "mkg_cap_index_workspace_bytes": (C.c_size_t, [P(Graph)]),

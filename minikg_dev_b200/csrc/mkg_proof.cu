@@ -72,7 +72,7 @@ ProofLayout proof_layout(const ProofDims& q) {
   L.dxa = o; o += a256(slab);
   L.dxb = o; o += a256(slab);
   L.dy = o; o += a256(slab);
-  L.s = o; o += a256(4 * (size_t)q.hops * q.BLP);
+  L.s = o; o += a256(8 * (size_t)q.hops * q.BLP);  // fp64: S sums dX Y terms of both signs
   L.dwt = o; o += a256(8 * (size_t)q.n * q.BLP);  // fp64 accumulator
   L.queue = o; o += a256(4 * (size_t)(2 * q.hops * q.nch * kQueueStride));
   L.msgs = o; o += a256(8 * (size_t)(q.hops + 1));
@@ -95,7 +95,7 @@ struct Slab {
   float* dxa() const { return reinterpret_cast<float*>(base + lay.dxa); }
   float* dxb() const { return reinterpret_cast<float*>(base + lay.dxb); }
   float* dy() const { return reinterpret_cast<float*>(base + lay.dy); }
-  float* s(int64_t h) const { return reinterpret_cast<float*>(base + lay.s) + h * q.BLP; }
+  double* s(int64_t h) const { return reinterpret_cast<double*>(base + lay.s) + h * q.BLP; }
   double* dwt() const { return reinterpret_cast<double*>(base + lay.dwt); }
   int32_t* queue() const { return reinterpret_cast<int32_t*>(base + lay.queue); }
   int64_t* msgs() const { return reinterpret_cast<int64_t*>(base + lay.msgs); }
@@ -165,13 +165,13 @@ __global__ void forward_setup_kernel(const int64_t* __restrict__ heads, const in
 // Start of a backward: the edge-score gradient, the S sums of every hop, the backward's
 // task-queue counters and dWt.
 __global__ void backward_setup_kernel(ProofDims q, float* __restrict__ grad_edge, int64_t num_facts,
-                                      float* __restrict__ s, int32_t* __restrict__ queue, int64_t nqueue,
+                                      double* __restrict__ s, int32_t* __restrict__ queue, int64_t nqueue,
                                       double* __restrict__ dwt) {
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   if (grad_edge)
     for (int64_t i = tid; i < num_facts; i += nthreads) grad_edge[i] = 0.0f;
-  for (int64_t i = tid; i < q.hops * q.BLP; i += nthreads) s[i] = 0.0f;
+  for (int64_t i = tid; i < q.hops * q.BLP; i += nthreads) s[i] = 0.0;
   for (int64_t i = tid; i < nqueue; i += nthreads) queue[i] = 0;
   for (int64_t i = tid; i < q.n * q.BLP; i += nthreads) dwt[i] = 0.0;
 }
@@ -899,9 +899,9 @@ constexpr int kSeedRows = 4;    // rows whose loads a thread issues together
 // which hold zeros in X_K and get zeros in dX_K.
 __global__ void __launch_bounds__(256, 4) seed_grad_kernel(const float* __restrict__ g, const float* __restrict__ xk,
                                                        const float* __restrict__ ylast, ProofDims q,
-                                                       float* __restrict__ dx, float* __restrict__ s) {
+                                                       float* __restrict__ dx, double* __restrict__ s) {
   __shared__ float tile[32][33];  // [query][entity] of G
-  __shared__ float part[1024];    // S of the block's columns (width <= 1024 on the register path)
+  __shared__ double part[1024];   // S of the block's columns (width <= 1024 on the register path)
   const int tid = threadIdx.x;
   const int64_t b0 = blockIdx.y * 32;
   const int nb = static_cast<int>(q.B - b0 < 32 ? q.B - b0 : 32);
@@ -914,8 +914,8 @@ __global__ void __launch_bounds__(256, 4) seed_grad_kernel(const float* __restri
   const int rpp = 256 / cols;       // rows per pass
   const int cf = tid % cols, rr = tid / cols;
   const bool worker = rr < rpp;
-  for (int i = tid; i < 1024; i += 256) part[i] = 0.0f;
-  float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i = tid; i < 1024; i += 256) part[i] = 0.0;
+  float sacc[4] = {0.f, 0.f, 0.f, 0.f};  // over at most 128 rows; fp64 from the block sums on
   for (int t = 0; t < kSeedTiles; ++t) {
     const int64_t e0 = ((int64_t)blockIdx.x * kSeedTiles + t) * 32;
     if (e0 >= q.E) break;
@@ -959,7 +959,7 @@ __global__ void __launch_bounds__(256, 4) seed_grad_kernel(const float* __restri
             const float dv = (ok[k] && xs[k] != 0.0f) ? tile[bq[k]][r] : 0.0f;
             o[k] = dv;
             if (fixed) sacc[k] = fmaf(dv, ys[k], sacc[k]);
-            else if (dv != 0.0f) atomicAdd(s + c0 + j0 + k, dv * ys[k]);
+            else if (dv != 0.0f) atomicAdd(s + c0 + j0 + k, (double)(dv * ys[k]));
           }
           *reinterpret_cast<float4*>(dx + (e0 + r) * q.BLP + c0 + j0) = make_float4(o[0], o[1], o[2], o[3]);
         }
@@ -971,11 +971,11 @@ __global__ void __launch_bounds__(256, 4) seed_grad_kernel(const float* __restri
       const int j0 = 4 * cf;
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        if (j0 + k < width && sacc[k] != 0.0f) atomicAdd(part + j0 + k, sacc[k]);
+        if (j0 + k < width && sacc[k] != 0.0f) atomicAdd(part + j0 + k, (double)sacc[k]);
     }
     __syncthreads();
     for (int j = tid; j < width; j += 256)
-      if (part[j] != 0.0f) atomicAdd(s + c0 + j, part[j]);
+      if (part[j] != 0.0) atomicAdd(s + c0 + j, part[j]);
   }
 }
 
@@ -990,7 +990,7 @@ constexpr int kNbTasks = 4;
 
 __global__ void __launch_bounds__(256, 4) normalize_mass_backward_kernel(
     const float* __restrict__ dx, const float* __restrict__ y, const float* __restrict__ dsum,
-    const float* __restrict__ s, const uint8_t* __restrict__ yact, ProofDims q, float* __restrict__ dy,
+    const double* __restrict__ s, const uint8_t* __restrict__ yact, ProofDims q, float* __restrict__ dy,
     const int4* __restrict__ push_tasks, int64_t num_push_tasks, float* __restrict__ dx_next) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -1024,9 +1024,12 @@ __global__ void __launch_bounds__(256, 4) normalize_mass_backward_kernel(
       const int64_t col = chunk * kChunk + 4 * lane;
       if (on[u]) {
         const float4 d = *reinterpret_cast<const float4*>(dsum + col);
-        const float4 sv = *reinterpret_cast<const float4*>(s + col);
+        // S rounded to fp32 once, from its fp64 sum
+        const double2 s01 = *reinterpret_cast<const double2*>(s + col);
+        const double2 s23 = *reinterpret_cast<const double2*>(s + col + 2);
         float gi[4] = {g[u].x, g[u].y, g[u].z, g[u].w}, vi[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-        float di[4] = {d.x, d.y, d.z, d.w}, si[4] = {sv.x, sv.y, sv.z, sv.w}, o[4];
+        float di[4] = {d.x, d.y, d.z, d.w}, o[4];
+        const float si[4] = {(float)s01.x, (float)s01.y, (float)s23.x, (float)s23.y};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           float r = 0.0f;
@@ -1089,26 +1092,26 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
     const uint8_t* __restrict__ yact, const float* __restrict__ dy, const float* __restrict__ yprev,
-    float* __restrict__ dx, double* __restrict__ dwt, float* __restrict__ sprev, float* __restrict__ grad_edge,
+    float* __restrict__ dx, double* __restrict__ dwt, double* __restrict__ sprev, float* __restrict__ grad_edge,
     int64_t num_facts, EdgeFactor ef, int32_t* __restrict__ queue, const int2* __restrict__ rcap,
     const uint8_t* __restrict__ take, unsigned* err) {
   extern __shared__ float smem[];
   float* dws = smem;                        // [n][128] rule-weight gradient (conflict-free: [ch][k][lane])
-  float* cs = dws + q.n * kChunk;           // [4][32] S_prev partials
+  // [4][32] S_prev partials in fp64 (dX Y terms of both signs cancel in S)
+  double* cs = reinterpret_cast<double*>(dws + q.n * kChunk);
   const int lane = threadIdx.x & 31;
   const int64_t chunk = blockIdx.y;
   const int64_t col0 = chunk * kChunk;
   const int64_t col = col0 + 4 * lane;
   const bool colok = col < q.BLP;
   for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) dws[i] = 0.0f;
-  for (int i = threadIdx.x; i < kChunk; i += blockDim.x) cs[i] = 0.0f;
+  for (int i = threadIdx.x; i < kChunk; i += blockDim.x) cs[i] = 0.0;
   __syncthreads();
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   // rule weights of this chunk from global memory (L1-resident): W[ch] at wt + ch * BLP + col
   auto wload = [&](int64_t ch) -> float4 {
     return colok ? __ldg(reinterpret_cast<const float4*>(wt + ch * q.BLP + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
   };
-  float4 spart = zero;
   TaskCursor cursor(queue + chunk * kQueueStride, ntasks);
   int64_t t;
   while (cursor.next(t)) {
@@ -1237,17 +1240,15 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
       } else {
         *reinterpret_cast<float4*>(dr) = gx;
       }
-      if (sprev != nullptr && active) {
+      if (sprev != nullptr && active) {  // each product added once, in fp64
         const float4 yp = *reinterpret_cast<const float4*>(yprev + row * q.BLP + col);
-        spart.x = fmaf(gx.x, yp.x, spart.x); spart.y = fmaf(gx.y, yp.y, spart.y);
-        spart.z = fmaf(gx.z, yp.z, spart.z); spart.w = fmaf(gx.w, yp.w, spart.w);
+        if (yp.x != 0.f) atomicAdd(cs + 0 * 32 + lane, (double)(gx.x * yp.x));
+        if (yp.y != 0.f) atomicAdd(cs + 1 * 32 + lane, (double)(gx.y * yp.y));
+        if (yp.z != 0.f) atomicAdd(cs + 2 * 32 + lane, (double)(gx.z * yp.z));
+        if (yp.w != 0.f) atomicAdd(cs + 3 * 32 + lane, (double)(gx.w * yp.w));
       }
     }
   }
-  atomicAdd(cs + 0 * 32 + lane, spart.x);
-  atomicAdd(cs + 1 * 32 + lane, spart.y);
-  atomicAdd(cs + 2 * 32 + lane, spart.z);
-  atomicAdd(cs + 3 * 32 + lane, spart.w);
   __syncthreads();
   for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) {
     const int64_t ch = i / kChunk, r = i % kChunk, l = r % 32, k = r / 32;
@@ -1258,7 +1259,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
     for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {
       const int l = i % 32, k = i / 32;
       const int64_t c = col0 + 4 * l + k;
-      if (c < q.BLP && cs[i] != 0.0f) atomicAdd(sprev + c, cs[i]);
+      if (c < q.BLP && cs[i] != 0.0) atomicAdd(sprev + c, cs[i]);
     }
   }
 }
@@ -1278,8 +1279,45 @@ __device__ __forceinline__ unsigned long long candidate_key(float raw, int64_t e
          static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(e));
 }
 
-__global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __restrict__ raw, int64_t B,
-                                                                 int64_t E, int64_t k, int64_t* __restrict__ tails,
+// every stored entry is a candidate (a sparse state's explicit zeros get score 0)
+__device__ __forceinline__ unsigned long long stored_candidate_key(float raw, int64_t e) {
+  const float xv = fmaxf(raw, 0.0f);
+  const float ex = static_cast<float>(exp(-static_cast<double>(xv)));
+  const float score = 1.0f - ex;
+  return (static_cast<unsigned long long>(__float_as_uint(score)) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(e));
+}
+
+// Row sources of the decode top-k: a dense [B, E] raw-score array (zeros are absent entries),
+// or a key-sorted sparse state (keys b * E + e ascending; every stored entry is a candidate).
+struct DenseTopkRows {
+  const float* raw;
+  int64_t E;
+  __device__ void range(int64_t b, int64_t& lo, int64_t& hi) const { lo = b * E; hi = lo + E; }
+  __device__ unsigned long long key(int64_t i, int64_t lo) const { return candidate_key(raw[i], i - lo); }
+};
+
+struct SparseTopkRows {
+  const int64_t* keys;
+  const float* vals;
+  int64_t nnz, E;
+  __device__ int64_t lower_bound(int64_t v) const {
+    int64_t lo = 0, hi = nnz;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (keys[mid] < v) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+  }
+  __device__ void range(int64_t b, int64_t& lo, int64_t& hi) const {
+    lo = lower_bound(b * E);
+    hi = lower_bound((b + 1) * E);
+  }
+  __device__ unsigned long long key(int64_t i, int64_t) const { return stored_candidate_key(vals[i], keys[i] % E); }
+};
+
+template <class Rows>
+__global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(Rows rows, int64_t k, int64_t* __restrict__ tails,
                                                                  float* __restrict__ scores,
                                                                  int64_t* __restrict__ counts) {
   typedef cub::BlockReduce<long long, kTopkThreads> CandReduce;
@@ -1291,11 +1329,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __
   __shared__ int nsel;
   __shared__ long long ncand_s;
   const int64_t b = blockIdx.x;
-  const float* row = raw + b * E;
+  int64_t lo, hi;
+  rows.range(b, lo, hi);
   if (threadIdx.x == 0) { ncand_s = 0; nsel = 0; prefix_s = 0ull; }
   __syncthreads();
   long long my = 0;
-  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) my += row[e] != 0.0f;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) my += rows.key(i, lo) != 0ull;
   my = CandReduce(reduce_tmp).Sum(my);
   if (threadIdx.x == 0) { ncand_s = my; need_s = my < k ? my : k; }
   __syncthreads();
@@ -1309,8 +1348,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __
     for (int shift = 56; shift >= 0; shift -= 8) {
       for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
       __syncthreads();
-      for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
-        unsigned long long key = candidate_key(row[e], e);
+      for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const unsigned long long key = rows.key(i, lo);
         if (key != 0ull && (key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1u);
       }
       __syncthreads();
@@ -1332,8 +1371,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __
     }
     thresh = prefix;  // keys are unique (distinct tails): exactly kk keys are >= thresh
   }
-  for (int64_t e = threadIdx.x; e < E; e += blockDim.x) {
-    unsigned long long key = candidate_key(row[e], e);
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const unsigned long long key = rows.key(i, lo);
     if (key != 0ull && key >= thresh) {
       int pos = atomicAdd(&nsel, 1);
       if (pos < kTopkMax) sel[pos] = key;
@@ -1373,7 +1412,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(const float* __
   if (threadIdx.x == 0) counts[b] = m;
 }
 
-size_t bwd_smem(const ProofDims& q) { return 4 * ((size_t)q.n * kChunk + kChunk); }
+size_t bwd_smem(const ProofDims& q) { return 4 * (size_t)q.n * kChunk + 8 * (size_t)kChunk; }
 
 // Columns per lane of the forward pull: 8 (two float4) for batches wider than 128
 // columns; MKG_FWD_VEC=1|2 overrides (a tuning knob).
@@ -1625,20 +1664,65 @@ int proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int64_t
   MKG_REQUIRE(tails && scores && counts, "decode: null output");
   int rc = run_forward(g, adj, heads, w_hops, p, true, ws, ws_bytes, out_scores, nullptr, err, st);
   if (rc) return rc;
-  topk_rows_kernel<<<(unsigned)p->B, kTopkThreads, 0, st>>>(out_scores, p->B, p->E, topk, tails, scores, counts);
+  topk_rows_kernel<<<(unsigned)p->B, kTopkThreads, 0, st>>>(DenseTopkRows{out_scores, p->E}, topk, tails, scores,
+                                                             counts);
   MKG_LAUNCHED("topk_rows_kernel");
   return MKG_OK;
 }
 
 namespace {
 // One thread per segment: a sequential fp32 chain in index order.
-__global__ void segment_sum_ordered_kernel(const int64_t* __restrict__ seg_ptr, int64_t nseg,
-                                           const float* __restrict__ values, float* __restrict__ out) {
-  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < nseg;
-       s += (int64_t)gridDim.x * blockDim.x) {
+// One warp per segment: the warp stages kOrdChunk values at a time through shared memory with
+// coalesced loads, and lane 0 adds them one by one in index order (the sum is a single fp32
+// chain, as a sequential CPU loop forms it).  The loads of the next chunk are issued before lane
+// 0 starts on the current one, so memory latency overlaps the dependent adds.
+constexpr int kOrdWarps = 4;
+constexpr int kOrdPerLane = 32;
+constexpr int kOrdChunk = 32 * kOrdPerLane;
+
+__global__ void __launch_bounds__(kOrdWarps * 32) segment_sum_ordered_kernel(const int64_t* __restrict__ seg_ptr,
+                                                                           int64_t nseg,
+                                                                           const float* __restrict__ values,
+                                                                           float* __restrict__ out) {
+  __shared__ __align__(16) float buf[kOrdWarps][kOrdChunk];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float* sb = buf[w];
+  for (int64_t s = blockIdx.x * (int64_t)kOrdWarps + w; s < nseg; s += (int64_t)gridDim.x * kOrdWarps) {
+    const int64_t b = seg_ptr[s], e = seg_ptr[s + 1];
+    float r[kOrdPerLane];
+#pragma unroll
+    for (int k = 0; k < kOrdPerLane; ++k) {
+      const int64_t i = b + k * 32 + lane;
+      r[k] = i < e ? values[i] : 0.0f;
+    }
     float acc = 0.0f;
-    for (int64_t i = seg_ptr[s]; i < seg_ptr[s + 1]; ++i) acc = __fadd_rn(acc, values[i]);
-    out[s] = acc;
+    for (int64_t c0 = b; c0 < e; c0 += kOrdChunk) {
+#pragma unroll
+      for (int k = 0; k < kOrdPerLane; ++k) sb[k * 32 + lane] = r[k];
+      __syncwarp();
+      const int64_t c1 = c0 + kOrdChunk;
+      if (c1 < e) {
+#pragma unroll
+        for (int k = 0; k < kOrdPerLane; ++k) {
+          const int64_t i = c1 + k * 32 + lane;
+          r[k] = i < e ? values[i] : 0.0f;
+        }
+      }
+      if (lane == 0) {
+        const int m = static_cast<int>(e - c0 < kOrdChunk ? e - c0 : kOrdChunk);
+        const int m4 = m & ~3;
+        for (int j = 0; j < m4; j += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(sb + j);
+          acc = __fadd_rn(acc, v.x);
+          acc = __fadd_rn(acc, v.y);
+          acc = __fadd_rn(acc, v.z);
+          acc = __fadd_rn(acc, v.w);
+        }
+        for (int j = m4; j < m; ++j) acc = __fadd_rn(acc, sb[j]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) out[s] = acc;
   }
 }
 // One block per segment: strided partial sums, then a block reduction.
@@ -1670,7 +1754,8 @@ int segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* value
   MKG_REQUIRE(nseg >= 0, "segment_sum_ordered: negative segment count");
   if (nseg == 0) return MKG_OK;
   MKG_REQUIRE(seg_ptr && values && out, "segment_sum_ordered: null argument");
-  segment_sum_ordered_kernel<<<grid_for(nseg, 128, persistent_blocks(8)), 128, 0, st>>>(seg_ptr, nseg, values, out);
+  segment_sum_ordered_kernel<<<grid_for(nseg, kOrdWarps, persistent_blocks(16)), kOrdWarps * 32, 0, st>>>(
+      seg_ptr, nseg, values, out);
   MKG_LAUNCHED("segment_sum_ordered_kernel");
   return MKG_OK;
 }
@@ -1680,7 +1765,19 @@ int decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* t
   MKG_REQUIRE(raw && tails && scores && counts, "decode_topk: null argument");
   MKG_REQUIRE(topk >= 1 && topk <= kTopkMax, "decode_topk: topk must lie in [1, %d]", kTopkMax);
   MKG_REQUIRE(B >= 1 && E >= 1 && E < (int64_t(1) << 32) - 1, "decode_topk: bad sizes");
-  topk_rows_kernel<<<(unsigned)B, kTopkThreads, 0, st>>>(raw, B, E, topk, tails, scores, counts);
+  topk_rows_kernel<<<(unsigned)B, kTopkThreads, 0, st>>>(DenseTopkRows{raw, E}, topk, tails, scores, counts);
+  MKG_LAUNCHED("topk_rows_kernel");
+  return MKG_OK;
+}
+
+int sparse_topk(const int64_t* keys, const float* vals, int64_t nnz, int64_t B, int64_t E, int64_t topk,
+                int64_t* tails, float* scores, int64_t* counts, cudaStream_t st) {
+  MKG_REQUIRE(tails && scores && counts && (nnz == 0 || (keys && vals)), "sparse_topk: null argument");
+  MKG_REQUIRE(topk >= 1 && topk <= kTopkMax, "sparse_topk: topk must lie in [1, %d]", kTopkMax);
+  MKG_REQUIRE(nnz >= 0 && B >= 1 && E >= 1 && E < (int64_t(1) << 32) - 1 && B <= (int64_t(1) << 62) / E,
+              "sparse_topk: bad sizes");
+  topk_rows_kernel<<<(unsigned)B, kTopkThreads, 0, st>>>(SparseTopkRows{keys, vals, nnz, E}, topk, tails, scores,
+                                                          counts);
   MKG_LAUNCHED("topk_rows_kernel");
   return MKG_OK;
 }

@@ -289,9 +289,23 @@ def norm_sp_3d_ordered(s: torch.Tensor) -> torch.Tensor:
 def sparse_topk(keys: torch.Tensor, vals: torch.Tensor, B: int, E: int, k: int):
     """Decode order on sparse raw scores (keys ``b * E + e``): bound ``1 - exp(-max(x, 0))``
     (exp rounded from double, then the fp32 difference), score descending, tail ascending,
-    ``k`` per query (proof.py:642-649, 729-758; decode_core.py:350-363).
+    ``k`` per query (proof.py:642-649, 729-758; decode_core.py:350-363).  ``keys`` ascending.
     Returns (tails [B, k] -1 padded, scores [B, k], counts [B])."""
     dev = vals.device
+    if 1 <= k <= 1024:  # one block per query: radix select + sort (mkg_sparse_topk)
+        lib = N.load()
+        N.require_cuda(vals, "vals")
+        kc = keys.to(torch.int64).contiguous()
+        vc = vals.detach().to(torch.float32).contiguous()
+        tails = torch.empty((B, k), dtype=torch.int64, device=dev)
+        scores = torch.empty((B, k), dtype=torch.float32, device=dev)
+        counts = torch.empty(B, dtype=torch.int64, device=dev)
+        N.check(lib.mkg_sparse_topk(N.ptr(kc), N.ptr(vc), int(kc.numel()), int(B), int(E), int(k), tails.data_ptr(),
+                                    scores.data_ptr(), counts.data_ptr(), N.stream_handle(dev)), "sparse_topk")
+        return tails, scores, counts
+    # longer candidate lists: three stable sorts (tail, then score, then query)
+    inside = (keys >= 0) & (keys < B * E)
+    keys, vals = keys[inside], vals[inside]
     sc = 1.0 - torch.exp(-vals.detach().clamp_min(0.0).double()).float()
     b, t = keys // E, keys % E
     o = torch.sort(t, stable=True).indices

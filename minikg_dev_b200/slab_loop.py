@@ -257,9 +257,11 @@ def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, gy, facto
                                              grad_w64.data_ptr(), N.ptr(grad_edge), ws.data_ptr(), ws.numel(), err,
                                              st), "slab_expand_backward")
         if ev is not None:  # grad-in at the outputs, frontier re-read, grad-out, weights, edge grads
-            ev[1].record()
+            ev[1].record()  # (4 B per edge-score gradient touched: at most one per message, at most T)
+            local_deg = (eng.ptr[1:] - eng.ptr[:-1]).to(torch.int64)
+            touched = min(eng.g.num_facts, int(local_deg[k % E].sum())) if grad_edge is not None else 0
             eng.trace.append(("bwd", ev[0], ev[1], graph_bytes(eng, k) + 12 * (yb - ya) + 12 * (b - a) + 4 * (b - a)
-                              + nr * n * 4 + (4 * eng.g.num_facts if grad_edge is not None else 0)))
+                              + nr * n * 4 + 4 * touched))
         if yb > ya:
             N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), yb - ya, 1, None, 1,
                                       err, st), "slab_take")

@@ -618,6 +618,31 @@ def test_decode_topk_ties_and_short_rows():
         np.testing.assert_array_equal(counts.cpu().numpy(), oc)
 
 
+def test_sparse_topk_ties_zeros_and_short_rows():
+    """mkg_sparse_topk (k <= 1024) and the sort path (k > 1024) against the oracle's decode on a
+    sparse state: explicit zeros and negative values are candidates with score 0, tied scores
+    order by tail, empty rows and rows shorter than k, keys of rows past B ignored."""
+    from minikg_dev_b200.proof import sparse_topk
+    rng = np.random.default_rng(6)
+    B, E = 7, 5000
+    keys, vals = [], []
+    for b in range(B + 1):  # row B lies outside the batch
+        m = [5, 150, 4999, 0, 1300, 7, 2048, 40][b]
+        cols = np.sort(rng.choice(E, m, replace=False))
+        keys.append(b * E + cols)
+        vals.append(rng.choice(np.array([0.5, 0.25, 1.5, 3.0, 1e-9, 0.0, -2.0], np.float32), m))
+    keys, vals = np.concatenate(keys).astype(np.int64), np.concatenate(vals)
+    inside = keys < B * E
+    for k in (1, 10, 100, 1024, 1500):
+        tails, scores, counts = sparse_topk(T(keys), T(vals), B, E, k)
+        ot, osc, oc = O.decode_topk((keys[inside], vals[inside]), B, E, k)
+        np.testing.assert_array_equal(tails.cpu().numpy(), ot)
+        np.testing.assert_array_equal(scores.cpu().numpy(), osc)
+        np.testing.assert_array_equal(counts.cpu().numpy(), oc)
+    tails, scores, counts = sparse_topk(T(keys[:0]), T(vals[:0]), B, E, 5)
+    assert counts.sum().item() == 0 and (tails == -1).all().item()
+
+
 # ----------------------------------------------------------------------------- drop-in
 @pytest.mark.parametrize("gname", ["g1", "g2"])
 @pytest.mark.parametrize("tag,cap,topk_nodes", [("pr_unc", UNC, 0), ("pr_cap", 9, 0), ("pr_prune", UNC, 40)])
