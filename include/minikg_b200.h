@@ -362,9 +362,12 @@ int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_
  * raw values [nnz]; every stored entry is a candidate (as proof.py:729-758 takes the rows of
  * the sparse tensor).  One block per query finds its row by binary search; keys of rows
  * outside [0, B) are ignored.  tails [B, topk] (-1 padded), scores [B, topk], counts [B];
- * topk in [1, 1024]. */
+ * topk in [1, 1024].  The workspace (mkg_sparse_topk_workspace_bytes(nnz) bytes) holds every
+ * entry's candidate key, formed once. */
+size_t mkg_sparse_topk_workspace_bytes(int64_t nnz);
 int mkg_sparse_topk(const int64_t* keys, const float* vals, int64_t nnz, int64_t B, int64_t E, int64_t topk,
-                    int64_t* tails, float* scores, int64_t* counts, mkg_stream stream);
+                    int64_t* tails, float* scores, int64_t* counts, void* workspace, size_t workspace_bytes,
+                    mkg_stream stream);
 
 /* out[s] = values[seg_ptr[s]] + values[seg_ptr[s] + 1] + ... + values[seg_ptr[s+1] - 1],
  * added one by one in index order in fp32 (device pointers; seg_ptr [nseg + 1], int64).
@@ -389,7 +392,13 @@ int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, f
  * lie in a window: (b, l) rows [row0, row0 + nrows) x destination entities [lo, lo + extent)
  * of a key space (row) * E + e.  A *store* of mkg_slab_store_bytes(nrows * extent) bytes
  * holds one fp32 slot per key and a touched bit per slot; the caller zero-fills it once and
- * every mkg_slab_emit / clearing mkg_slab_take leaves what it read at zero again. */
+ * every mkg_slab_emit / clearing mkg_slab_take leaves what it read at zero again.  Slots are
+ * entity-major (slot (e - lo) * nrows + (row - row0)), and keys come out of mkg_slab_emit in
+ * that order: ascending entity, then ascending row ("entity-major order").  A frontier or a
+ * key list spanning several row windows is passed whole to each window's call; entries of
+ * other rows are skipped (mkg_slab_expand, mkg_slab_expand_backward always; mkg_slab_put and
+ * mkg_slab_take with MKG_SLAB_OTHER_ROWS). */
+#define MKG_SLAB_OTHER_ROWS 16
 typedef struct mkg_slab_window {
   int64_t E;       /* entities of the key space */
   int64_t row0;    /* first row (b * L + l, or b for [B, E] keys) of the window */
@@ -400,8 +409,9 @@ typedef struct mkg_slab_window {
 
 size_t mkg_slab_store_bytes(int64_t slots);
 size_t mkg_slab_expand_workspace_bytes(int64_t nnz);
-/* Adds every message of the frontier (keys (b * L + l) * E + s with values, all in the
- * window's rows) to the store: for each record of push row s (mkg_adjacency.push, or a push
+/* Adds every message of the frontier entries in the window's rows (keys (b * L + l) * E + s
+ * with values, in any order; entity-major order keeps the atomics of neighbouring entries in
+ * the same sectors) to the store: for each record of push row s (mkg_adjacency.push, or a push
  * list restricted to destinations in [lo, lo + extent)) the value (x * w[b, l, channel]) *
  * factor at key (b, l, neighbour), plus (identity != 0) x * w[b, l, n - 1] at (b, l, s).
  * w is [B * L, n].  Zero-valued messages are left out (the hop loop drops zeros after its
@@ -418,19 +428,21 @@ int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, const int
 size_t mkg_slab_collect_workspace_bytes(int64_t slots);
 int mkg_slab_count(const mkg_slab_window* win, const void* store, void* workspace, size_t workspace_bytes,
                    int64_t* count_out, mkg_stream stream);
-/* Writes the touched keys in ascending order (global keys (row0 + r) * E + lo + e) with their
- * values, clears them in the store and, when row_sums != NULL, adds each row's values to
+/* Writes the touched keys in entity-major order (global keys (row0 + r) * E + lo + e) with
+ * their values, clears them in the store and, when row_sums != NULL, adds each row's values to
  * row_sums[r] in fp64 (the column sums of normalize_sparse3d, drum.py:31-51). */
 int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* workspace, size_t workspace_bytes,
                   int64_t count, int64_t* keys_out, float* vals_out, double* row_sums, mkg_stream stream);
 /* Writes (mode 0), adds with a touched mark (mode 1) or raises to the maximum with a touched
  * mark (mode 2: max_sp_3d's max over rules with row_div = L) values at keys whose row is
  * (key / E) / row_div (row_div = L maps (b, l, e) to the [B, E] key b * E + e: sum_sp_3d,
- * fastlog_bridge.py:17-23). */
+ * fastlog_bridge.py:17-23).  mode | MKG_SLAB_OTHER_ROWS skips keys of rows outside the
+ * window; any other key outside it sets MKG_DEV_BAD_KEY. */
 int mkg_slab_put(const mkg_slab_window* win, void* store, const int64_t* keys, const float* vals, int64_t nnz,
                  int64_t row_div, int32_t mode, unsigned* dev_err, mkg_stream stream);
-/* out[i] = the store's value at keys[i] (row (key / E) / row_div), cleared when clear != 0;
- * out may be NULL (clear only). */
+/* out[i] = the store's value at keys[i] (row (key / E) / row_div), cleared when clear & 1;
+ * out may be NULL (clear only).  clear | MKG_SLAB_OTHER_ROWS skips keys of rows outside the
+ * window (their out[i] is left as it was). */
 int mkg_slab_take(const mkg_slab_window* win, void* store, const int64_t* keys, int64_t nnz, int64_t row_div,
                   float* out, int32_t clear, unsigned* dev_err, mkg_stream stream);
 /* Backward of mkg_slab_expand with the hop's output gradient held in the store (mode 0 puts):
@@ -447,7 +459,7 @@ int mkg_slab_expand_backward(const int32_t* push_ptr, const mkg_adj_edge* push, 
  * The per-(b, l) sums of normalize_sparse3d and of its gradient (drum.py:31-51). */
 int mkg_row_sums(const int64_t* keys, int64_t nnz, int64_t E, int64_t row0, int64_t nrows, const float* vals,
                  double* out, unsigned* dev_err, mkg_stream stream);
-/* normalize_sparse3d(.., 0, "mass") (drum.py:31-51) on key-sorted entries: x = (y / d) *
+/* normalize_sparse3d(.., 0, "mass") (drum.py:31-51) on entries in any order: x = (y / d) *
  * min(d, 1) with d = row_sums[key / E - row0] (fp32).  dropped (device int64) receives the
  * number of results that are zero or, when threshold > 0, below it (the entries the loop
  * then drops). */
@@ -456,11 +468,17 @@ int mkg_mass_normalize(const int64_t* keys, const float* y, int64_t n, int64_t E
                        mkg_stream stream);
 /* Its gradient in two calls (a caller spanning several GPUs all-reduces `sums` in between):
  * mkg_mass_normalize_grad_sums adds sums[0][r] += gx * y / d and sums[1][r] += -(gx * min(d, 1)
- * * y) / d^2 over row r's entries (fp64, [2, nrows]); mkg_mass_normalize_grad writes
+ * * y) / d^2 over row r's entries (fp64, [2, nrows]; entries in any order); mkg_mass_normalize_grad writes
  * gy = gx * min(d, 1) / d + sums[1][r] + [d <= 1] sums[0][r] (zero where y is zero). */
 int mkg_mass_normalize_grad_sums(const int64_t* keys, const float* y, const float* gx, int64_t n, int64_t E,
                                  int64_t row0, int64_t nrows, const float* row_sums, double* sums, unsigned* dev_err,
                                  mkg_stream stream);
+/* mkg_mass_normalize_grad with gy written into a slab store at the keys' slots (the mode-0
+ * mkg_slab_put before mkg_slab_expand_backward) instead of an array; every key must lie in
+ * the window (else MKG_DEV_BAD_KEY). */
+int mkg_mass_normalize_grad_put(const int64_t* keys, const float* y, const float* gx, int64_t n, int64_t E,
+                                int64_t row0, int64_t nrows, const float* row_sums, const double* sums,
+                                const mkg_slab_window* win, void* store, unsigned* dev_err, mkg_stream stream);
 int mkg_mass_normalize_grad(const int64_t* keys, const float* y, const float* gx, int64_t n, int64_t E, int64_t row0,
                             int64_t nrows, const float* row_sums, const double* sums, float* gy, mkg_stream stream);
 /* out[i] = (float) in[i]. */
@@ -477,6 +495,19 @@ int mkg_f64_to_f32(const double* in, int64_t n, float* out, mkg_stream stream);
  * count_out (device int64) receives the number written.  inverse [n] (may be NULL): output
  * index of each input entry; arg [n] (mode 1, may be NULL): the input entry that won each
  * output. */
+/* sum_sp_3d / max_sp_3d (fastlog_bridge.py:17-23, model_mmDRUM_kernel_sp.py:184-236) on a
+ * [B, L, E] state in entity-major order (keys (b * L + l) * E + e by ascending e, then row; the
+ * order mkg_slab_emit writes): the rules of one (e, b) are adjacent, so each run is folded in
+ * rule order (mode 0: fp32 sum, l ascending; mode 1: maximum) with no sort of the entries, and
+ * one stable radix pass over the query puts the results in ascending b * E + e order.
+ * out_keys / out_vals hold up to n results; count_out (device int64) receives their number;
+ * out_pos [n] (may be NULL): each entry's result index.  Entries out of that order set
+ * MKG_DEV_BAD_KEY. */
+size_t mkg_rule_sum_workspace_bytes(int64_t n);
+int mkg_rule_sum(const int64_t* keys, const float* vals, int64_t n, int64_t E, int64_t L, int64_t B, int32_t mode,
+                 int64_t* out_keys, float* out_vals, int64_t* out_pos, int64_t* count_out, void* workspace,
+                 size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+
 size_t mkg_reduce_by_key_workspace_bytes(int64_t n);
 int mkg_reduce_by_key(const int64_t* keys, const float* vals, int64_t n, int32_t mode, int32_t key_bits,
                       int64_t* out_keys, float* out_vals, int64_t* count_out, int64_t* inverse, int64_t* arg,

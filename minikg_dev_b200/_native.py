@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libminikg_b200.so"
 
 MKG_OK = 0
 MASK_NONE, MASK_U8, MASK_F32 = 0, 1, 2
+SLAB_OTHER_ROWS = 16  # MKG_SLAB_OTHER_ROWS
 DEV_ERR_NAMES = {1: "frontier entry outside [B, L, E]", 2: "CSR column outside [0, E)",
                  4: "fact id outside [0, T)", 8: "gradient key outside [B, L, E]",
                  16: "relation id outside its range", 32: "a bounded wait inside a kernel gave up",
@@ -122,7 +123,8 @@ SIGNATURES = {
     "mkg_proof_decode_max": (C.c_int, [P(Graph), P(Adjacency), vp, vp, P(ProofParams), i64, vp, vp, vp, vp, vp,
                                        C.c_size_t, vp, vp]),
     "mkg_decode_topk": (C.c_int, [vp, i64, i64, i64, vp, vp, vp, vp]),
-    "mkg_sparse_topk": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, vp, vp, vp]),
+    "mkg_sparse_topk_workspace_bytes": (C.c_size_t, [i64]),
+    "mkg_sparse_topk": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, C.c_size_t, vp]),
     "mkg_segment_sum_ordered": (C.c_int, [vp, i64, vp, vp, vp]),
     "mkg_segment_sum": (C.c_int, [vp, i64, vp, vp, vp]),
     "mkg_cap_index_workspace_bytes": (C.c_size_t, [P(Graph)]),
@@ -144,6 +146,9 @@ SIGNATURES = {
     "mkg_mass_normalize": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, C.c_float, vp, vp, vp, vp]),
     "mkg_mass_normalize_grad_sums": (C.c_int, [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_mass_normalize_grad": (C.c_int, [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp]),
+    "mkg_mass_normalize_grad_put": (C.c_int, [vp, vp, vp, i64, i64, i64, i64, vp, vp, P(SlabWindow), vp, vp, vp]),
+    "mkg_rule_sum_workspace_bytes": (C.c_size_t, [i64]),
+    "mkg_rule_sum": (C.c_int, [vp, vp, i64, i64, i64, i64, i32, vp, vp, vp, vp, vp, C.c_size_t, vp, vp]),
     "mkg_reduce_by_key_workspace_bytes": (C.c_size_t, [i64]),
     "mkg_reduce_by_key": (C.c_int, [vp, vp, i64, i32, i32, vp, vp, vp, vp, vp, vp, C.c_size_t, vp, vp]),
     "mkg_rule_saved_bytes": (C.c_size_t, [P(RuleParams)]),

@@ -138,9 +138,11 @@ MKG_API int mkg_decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk
                             int64_t* counts, mkg_stream st) {
   return mkg::decode_topk(raw, B, E, topk, tails, scores, counts, S(st));
 }
+MKG_API size_t mkg_sparse_topk_workspace_bytes(int64_t nnz) { return mkg::sparse_topk_workspace_bytes(nnz); }
 MKG_API int mkg_sparse_topk(const int64_t* keys, const float* vals, int64_t nnz, int64_t B, int64_t E, int64_t topk,
-                            int64_t* tails, float* scores, int64_t* counts, mkg_stream st) {
-  return mkg::sparse_topk(keys, vals, nnz, B, E, topk, tails, scores, counts, S(st));
+                            int64_t* tails, float* scores, int64_t* counts, void* ws, size_t ws_bytes,
+                            mkg_stream st) {
+  return mkg::sparse_topk(keys, vals, nnz, B, E, topk, tails, scores, counts, ws, ws_bytes, S(st));
 }
 MKG_API int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, mkg_stream st) {
   return mkg::segment_sum(seg_ptr, nseg, values, out, S(st));

@@ -60,8 +60,9 @@ int proof_decode_max(const mkg_graph* g, const mkg_adjacency* adj, const int64_t
                      int64_t* counts, void* ws, size_t ws_bytes, unsigned* err, cudaStream_t st);
 int decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* tails, float* scores,
                 int64_t* counts, cudaStream_t st);
+size_t sparse_topk_workspace_bytes(int64_t nnz);
 int sparse_topk(const int64_t* keys, const float* vals, int64_t nnz, int64_t B, int64_t E, int64_t topk,
-                int64_t* tails, float* scores, int64_t* counts, cudaStream_t st);
+                int64_t* tails, float* scores, int64_t* counts, void* ws, size_t ws_bytes, cudaStream_t st);
 int segment_sum_ordered(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st);
 int segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, float* out, cudaStream_t st);
 

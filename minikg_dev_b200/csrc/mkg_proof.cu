@@ -1297,9 +1297,16 @@ struct DenseTopkRows {
   __device__ unsigned long long key(int64_t i, int64_t lo) const { return candidate_key(raw[i], i - lo); }
 };
 
+// candidate keys of a sparse state, formed once (the radix passes read them again and again)
+__global__ void sparse_candidate_keys_kernel(const int64_t* __restrict__ keys, const float* __restrict__ vals,
+                                             int64_t nnz, int64_t E, unsigned long long* __restrict__ cand) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nnz; i += (int64_t)gridDim.x * blockDim.x)
+    cand[i] = stored_candidate_key(vals[i], keys[i] % E);
+}
+
 struct SparseTopkRows {
   const int64_t* keys;
-  const float* vals;
+  const unsigned long long* cand;
   int64_t nnz, E;
   __device__ int64_t lower_bound(int64_t v) const {
     int64_t lo = 0, hi = nnz;
@@ -1313,7 +1320,7 @@ struct SparseTopkRows {
     lo = lower_bound(b * E);
     hi = lower_bound((b + 1) * E);
   }
-  __device__ unsigned long long key(int64_t i, int64_t) const { return stored_candidate_key(vals[i], keys[i] % E); }
+  __device__ unsigned long long key(int64_t i, int64_t) const { return cand[i]; }
 };
 
 template <class Rows>
@@ -1770,13 +1777,21 @@ int decode_topk(const float* raw, int64_t B, int64_t E, int64_t topk, int64_t* t
   return MKG_OK;
 }
 
+size_t sparse_topk_workspace_bytes(int64_t nnz) { return nnz > 0 ? 8 * (size_t)nnz : 0; }
+
 int sparse_topk(const int64_t* keys, const float* vals, int64_t nnz, int64_t B, int64_t E, int64_t topk,
-                int64_t* tails, float* scores, int64_t* counts, cudaStream_t st) {
-  MKG_REQUIRE(tails && scores && counts && (nnz == 0 || (keys && vals)), "sparse_topk: null argument");
+                int64_t* tails, float* scores, int64_t* counts, void* ws, size_t ws_bytes, cudaStream_t st) {
+  MKG_REQUIRE(tails && scores && counts && (nnz == 0 || (keys && vals && ws)), "sparse_topk: null argument");
   MKG_REQUIRE(topk >= 1 && topk <= kTopkMax, "sparse_topk: topk must lie in [1, %d]", kTopkMax);
   MKG_REQUIRE(nnz >= 0 && B >= 1 && E >= 1 && E < (int64_t(1) << 32) - 1 && B <= (int64_t(1) << 62) / E,
               "sparse_topk: bad sizes");
-  topk_rows_kernel<<<(unsigned)B, kTopkThreads, 0, st>>>(SparseTopkRows{keys, vals, nnz, E}, topk, tails, scores,
+  MKG_REQUIRE(ws_bytes >= sparse_topk_workspace_bytes(nnz), "sparse_topk: workspace too small");
+  auto* cand = static_cast<unsigned long long*>(ws);
+  if (nnz > 0) {
+    sparse_candidate_keys_kernel<<<grid_for(nnz, 256, persistent_blocks(8)), 256, 0, st>>>(keys, vals, nnz, E, cand);
+    MKG_LAUNCHED("sparse_candidate_keys_kernel");
+  }
+  topk_rows_kernel<<<(unsigned)B, kTopkThreads, 0, st>>>(SparseTopkRows{keys, cand, nnz, E}, topk, tails, scores,
                                                           counts);
   MKG_LAUNCHED("topk_rows_kernel");
   return MKG_OK;

@@ -300,8 +300,10 @@ def sparse_topk(keys: torch.Tensor, vals: torch.Tensor, B: int, E: int, k: int):
         tails = torch.empty((B, k), dtype=torch.int64, device=dev)
         scores = torch.empty((B, k), dtype=torch.float32, device=dev)
         counts = torch.empty(B, dtype=torch.int64, device=dev)
+        ws = N.workspace(lib.mkg_sparse_topk_workspace_bytes(int(kc.numel())), dev)
         N.check(lib.mkg_sparse_topk(N.ptr(kc), N.ptr(vc), int(kc.numel()), int(B), int(E), int(k), tails.data_ptr(),
-                                    scores.data_ptr(), counts.data_ptr(), N.stream_handle(dev)), "sparse_topk")
+                                    scores.data_ptr(), counts.data_ptr(), ws.data_ptr(), ws.numel(),
+                                    N.stream_handle(dev)), "sparse_topk")
         return tails, scores, counts
     # longer candidate lists: three stable sorts (tail, then score, then query)
     inside = (keys >= 0) & (keys < B * E)

@@ -8,19 +8,24 @@ with ``topk_edges`` uncapped), ``sum_sparse3d_concat`` (fastlog_bridge.py:26-42)
 ``csrc/mkg_slab.cu``:
 
 * a hop's messages (ori, inv and identity at once: the concat-sum) are added into a store
-  with one fp32 slot per output key of a window of (b, l) rows and a touched bit per slot;
-  the touched keys come out key-sorted by a bitmap popcount scan, with fp64 row sums for the
-  normalisation, and the store is left zeroed for the next use -- no sort, no hash table;
-* the normalisation is elementwise on the emitted values; the final sum over rules is one
-  more pass through the store (keys ``(b, l, e)`` added at ``(b, e)``);
+  with one fp32 slot per output key of a window of (b, l) rows and a touched bit per slot,
+  entity-major (a destination's rows adjacent: the rules of one query share their frontier
+  entities, so their messages land in the same sectors); the touched keys come out in
+  entity-major order (ascending entity, then row) by a bitmap popcount scan, with fp64 row
+  sums for the normalisation, and the store is left zeroed for the next use -- no sort, no
+  hash table.  Frontiers stay in that order from hop to hop;
+* the normalisation is elementwise on the emitted values; the final sum over rules is a
+  reduce-by-key to the ``(b, e)`` keys (``mkg_reduce_by_key``: sorted output, and the inverse
+  map that spreads the result's gradient back over the rules);
 * the backward is written out: the normalisation gradient with fp64 row sums, then the
   transposed walk with the output gradient held in the store (fp64 entry and rule-weight
   accumulators), hop by hop down to the first.
 
 With a ``ShardSpec`` the loop is destination-partitioned over ranks (one process per GPU):
 rank k owns the entities ``[lo_k, hi_k)``, keeps only the push records whose destination it
-owns (so every message is walked by exactly one rank), all-gathers the frontier each hop and
-all-reduces the normalisation's row sums; the backward all-reduces the frontier gradient, the
+owns (so every message is walked by exactly one rank), all-gathers the frontier each hop (the
+ranks' entity-major lists, concatenated in rank order, are the whole frontier in entity-major
+order) and all-reduces the normalisation's row sums; the backward all-reduces the frontier gradient, the
 row sums of the normalisation gradient, and at the end the rule-weight and edge-score
 gradients.  Every rank issues the same collectives in the same order.  With one process the
 same code runs without collectives.
@@ -122,18 +127,18 @@ def _windows(total_rows: int, per: int):
         yield r0, min(per, total_rows - r0)
 
 
-def _row_slices(keys: torch.Tensor, E: int, div: int, bounds) -> list[tuple[int, int]]:
-    """Positions [a, b) of the ascending ``keys`` whose row ``(key // E) // div`` falls in each
-    window ``[r0, r0 + n)``.  One window takes every key (no host synchronisation): keys outside
-    its rows are then flagged by the kernels."""
+def entity_major(keys: torch.Tensor, vals: torch.Tensor, E: int, BL: int):
+    """``(keys, vals)`` reordered to entity-major order (ascending entity, then row)."""
     if keys.numel() == 0:
-        return [(0, 0) for _ in bounds]
-    if len(bounds) == 1:
-        return [(0, int(keys.numel()))]
-    edges = torch.tensor([r0 * div * E for r0, _ in bounds] + [(bounds[-1][0] + bounds[-1][1]) * div * E],
-                         dtype=torch.int64, device=keys.device)
-    pos = torch.searchsorted(keys, edges).tolist()
-    return [(pos[i], pos[i + 1]) for i in range(len(bounds))]
+        return keys, vals
+    order = torch.sort((keys % E) * BL + keys // E).indices
+    return keys[order], vals[order]
+
+
+def _other_rows(bounds) -> int:
+    """The put / take flag that skips keys of other row windows (several windows only: with one
+    window every key must lie in it)."""
+    return N.SLAB_OTHER_ROWS if len(bounds) > 1 else 0
 
 
 def _events(eng: SlabEngine):
@@ -180,147 +185,141 @@ def graph_bytes(eng: SlabEngine, keys) -> int:
 
 
 def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True, agg_mode: int = 0):
-    """One hop's concat-summed output over the engine's destinations: (keys ascending, values,
-    fp64 row sums [BL]; zeros for ``agg_mode`` 1, which keeps each key's largest message
-    instead).  ``check``: refuse frontier keys outside [B, L, E] on the host (the loop, whose
-    keys are its own outputs, skips that synchronisation)."""
+    """One hop's concat-summed output over the engine's destinations: (keys in entity-major order
+    within each row window, windows in row order; values; fp64 row sums [BL], zeros for
+    ``agg_mode`` 1, which keeps each key's largest message instead).  The frontier may come in
+    any order (entity-major keeps neighbouring atomics in the same sectors).  ``check``: refuse
+    frontier keys outside [B, L, E] on the host (the loop, whose keys are its own outputs,
+    skips that synchronisation)."""
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
     n = int(w_h.shape[-1])
     wf = w_h.detach().to(torch.float32).reshape(BL, n).contiguous()
-    if check and keys.numel() and (int(keys[0]) < 0 or int(keys[-1]) >= BL * E):
+    if check and keys.numel() and (int(keys.min()) < 0 or int(keys.max()) >= BL * E):
         raise RuntimeError("slab hop: a frontier key lies outside [B, L, E]")
     eng.ensure_store(BL)
     bounds = list(_windows(BL, eng.rows_per_window))
-    slices = _row_slices(keys, E, 1, bounds)
     out_k, out_v = [], []
     d = torch.zeros(BL, dtype=torch.float64, device=dev)
     st = N.stream_handle(dev)
     err = N.error_word(dev).data_ptr()
-    for (r0, nr), (a, b) in zip(bounds, slices):
-        win = eng.window(r0, nr)
-        if b > a:
-            k = keys[a:b].contiguous()
-            v = vals[a:b].detach().to(torch.float32).contiguous()
-            ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(b - a), dev)
-            ev = _events(eng)
-            N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), b - a,
-                                        wf.data_ptr(), n, 1, int(agg_mode), ctypes.byref(win), eng.store.data_ptr(),
-                                        ws.data_ptr(), ws.numel(), err, st), "slab_expand")
-            if ev is not None:
-                ev[1].record()
-            ko, vo, rs = _collect(eng, win, agg_mode == 0)
-            if ev is not None:  # frontier in + output out (12 B per key: 8 B key, 4 B value), rule weights
-                eng.trace.append(("fwd", ev[0], ev[1], graph_bytes(eng, k) + 12 * (b - a) + 12 * ko.numel()
-                                  + nr * n * 4))
-            out_k.append(ko)
-            out_v.append(vo)
-            if rs is not None:
-                d[r0:r0 + nr] = rs
-    if not out_k:
+    nk = int(keys.numel())
+    if nk == 0:
         return (torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev), d)
+    k = keys.contiguous()
+    v = vals.detach().to(torch.float32).contiguous()
+    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk), dev)
+    for r0, nr in bounds:  # every window takes the whole frontier and walks the entries of its rows
+        win = eng.window(r0, nr)
+        ev = _events(eng)
+        N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), nk,
+                                    wf.data_ptr(), n, 1, int(agg_mode), ctypes.byref(win), eng.store.data_ptr(),
+                                    ws.data_ptr(), ws.numel(), err, st), "slab_expand")
+        if ev is not None:
+            ev[1].record()
+        ko, vo, rs = _collect(eng, win, agg_mode == 0)
+        if ev is not None:  # frontier in + output out (12 B per key: 8 B key, 4 B value), rule weights
+            mine = k[((k // E) >= r0) & ((k // E) < r0 + nr)] if len(bounds) > 1 else k
+            eng.trace.append(("fwd", ev[0], ev[1], graph_bytes(eng, mine) + 12 * int(mine.numel())
+                              + 12 * ko.numel() + nr * n * 4))
+        out_k.append(ko)
+        out_v.append(vo)
+        if rs is not None:
+            d[r0:r0 + nr] = rs
+    if len(out_k) == 1:
+        return out_k[0], out_v[0], d
     return torch.cat(out_k), torch.cat(out_v), d
 
 
 def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, gy, factor, grad_w64, grad_edge):
     """Transposed walk of one hop: the frontier entries' fp64 gradient; adds to ``grad_w64``
-    ([BL, n], fp64) and ``grad_edge`` ([T], fp32)."""
+    ([BL, n], fp64) and ``grad_edge`` ([T], fp32).  ``gy`` None: the output gradient is
+    already in the store (``_mass_normalize_grad`` with the engine; one window)."""
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
     n = int(w_h.shape[-1])
     wf = w_h.detach().to(torch.float32).reshape(BL, n).contiguous()
     bounds = list(_windows(BL, eng.rows_per_window))
-    sl_in = _row_slices(keys, E, 1, bounds)
-    sl_y = _row_slices(keys_y, E, 1, bounds)
-    gsp = torch.zeros(keys.numel(), dtype=torch.float64, device=dev)
+    if gy is None and len(bounds) != 1:
+        raise ValueError("expand_backward: a gradient already in the store needs a one-window store")
+    other = _other_rows(bounds)
+    nk, ny = int(keys.numel()), int(keys_y.numel())
+    gsp = torch.zeros(nk, dtype=torch.float64, device=dev)
     st = N.stream_handle(dev)
     err = N.error_word(dev).data_ptr()
-    gyf = gy.to(torch.float32).contiguous()
-    for (r0, nr), (a, b), (ya, yb) in zip(bounds, sl_in, sl_y):
-        if b <= a:
-            continue
+    ky = keys_y.contiguous()
+    if nk == 0:
+        if gy is None and ny:  # leave the store zeroed
+            N.check(lib.mkg_slab_take(ctypes.byref(eng.window(0, BL)), eng.store.data_ptr(), ky.data_ptr(), ny, 1,
+                                      None, 1, err, st), "slab_take")
+        return gsp
+    gyf = gy.to(torch.float32).contiguous() if gy is not None else None
+    k = keys.contiguous()
+    v = vals.detach().to(torch.float32).contiguous()
+    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk), dev)
+    for r0, nr in bounds:  # every window takes the whole frontier and walks the entries of its rows
         win = eng.window(r0, nr)
-        ky = keys_y[ya:yb]
-        if yb > ya:
-            N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), gyf[ya:yb].data_ptr(),
-                                     yb - ya, 1, 0, err, st), "slab_put")
-        k = keys[a:b].contiguous()
-        v = vals[a:b].detach().to(torch.float32).contiguous()
-        ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(b - a), dev)
-        g_part = gsp[a:b]
+        if ny and gyf is not None:
+            N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), gyf.data_ptr(), ny, 1,
+                                     other, err, st), "slab_put")
         ev = _events(eng)
         N.check(lib.mkg_slab_expand_backward(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                             b - a, wf.data_ptr(), n, 1, ctypes.byref(win), eng.store.data_ptr(),
-                                             ctypes.byref(factor), eng.g.num_facts, g_part.data_ptr(),
+                                             nk, wf.data_ptr(), n, 1, ctypes.byref(win), eng.store.data_ptr(),
+                                             ctypes.byref(factor), eng.g.num_facts, gsp.data_ptr(),
                                              grad_w64.data_ptr(), N.ptr(grad_edge), ws.data_ptr(), ws.numel(), err,
                                              st), "slab_expand_backward")
         if ev is not None:  # grad-in at the outputs, frontier re-read, grad-out, weights, edge grads
             ev[1].record()  # (4 B per edge-score gradient touched: at most one per message, at most T)
+            inw = lambda x: x[((x // E) >= r0) & ((x // E) < r0 + nr)] if len(bounds) > 1 else x  # noqa: E731
+            mine, mine_y = inw(k), inw(ky)
             local_deg = (eng.ptr[1:] - eng.ptr[:-1]).to(torch.int64)
-            touched = min(eng.g.num_facts, int(local_deg[k % E].sum())) if grad_edge is not None else 0
-            eng.trace.append(("bwd", ev[0], ev[1], graph_bytes(eng, k) + 12 * (yb - ya) + 12 * (b - a) + 4 * (b - a)
-                              + nr * n * 4 + 4 * touched))
-        if yb > ya:
-            N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), yb - ya, 1, None, 1,
-                                      err, st), "slab_take")
+            touched = min(eng.g.num_facts, int(local_deg[mine % E].sum())) if grad_edge is not None else 0
+            eng.trace.append(("bwd", ev[0], ev[1], graph_bytes(eng, mine) + 12 * int(mine_y.numel())
+                              + 16 * int(mine.numel()) + nr * n * 4 + 4 * touched))
+        if ny:
+            N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), ny, 1, None,
+                                      1 | other, err, st), "slab_take")
     return gsp
 
 
-def sum_over_rules(eng: SlabEngine, keys, vals, B: int, L: int, take_max: bool = False):
-    """sum_sp_3d: ``(b, l, e)`` entries added at ``(b, e)`` (``take_max``: max_sp_3d's maximum
-    instead, for non-negative values); returns ascending ``b * E + e`` keys and values (the
-    store's windows then run over queries)."""
-    lib = N.load()
-    dev = eng.dev
+def sum_over_rules(eng: SlabEngine, keys, vals, B: int, L: int, take_max: bool = False,
+                   entity_major_state: bool = False):
+    """sum_sp_3d (fastlog_bridge.py:17-23): ``(b, l, e)`` entries (any order) added at ``(b, e)``
+    (``take_max``: max_sp_3d's maximum instead); returns ascending ``b * E + e`` keys, their
+    values and the inverse map (each entry's output position) for the backward.  One
+    reduce-by-key (``mkg_reduce_by_key``: fp64 sums rounded once; maxima exact), or, for a state
+    in entity-major order (``entity_major_state``: the output of a one-window store), the
+    rule runs folded in place (``mkg_rule_sum``: fp32 sums in rule order) and one radix pass
+    over the query."""
     E = eng.g.num_entities
-    eng.ensure_store(B)
-    bounds = list(_windows(B, eng.rows_per_window))
-    slices = _row_slices(keys, E, L, bounds)
-    st = N.stream_handle(dev)
-    err = N.error_word(dev).data_ptr()
-    ok, ov = [], []
-    vf = vals.detach().to(torch.float32).contiguous()
-    for (r0, nr), (a, b) in zip(bounds, slices):
-        if b <= a:
-            continue
-        win = eng.window(r0, nr)
-        N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), keys[a:b].data_ptr(), vf[a:b].data_ptr(),
-                                 b - a, L, 2 if take_max else 1, err, st), "slab_put")
-        k, v, _ = _collect(eng, win, False)
-        ok.append(k)
-        ov.append(v)
-    if not ok:
-        return torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev)
-    return torch.cat(ok), torch.cat(ov)
+    if entity_major_state:
+        lib = N.load()
+        dev = vals.device
+        n = int(keys.numel())
+        k = keys.contiguous()
+        v = vals.detach().to(torch.float32).contiguous()
+        ok = torch.empty(n, dtype=torch.int64, device=dev)
+        ov = torch.empty(n, dtype=torch.float32, device=dev)
+        pos = torch.empty(n, dtype=torch.int64, device=dev)
+        cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+        ws = N.workspace(lib.mkg_rule_sum_workspace_bytes(n), dev)
+        N.check(lib.mkg_rule_sum(N.ptr(k), N.ptr(v), n, E, L, B, 1 if take_max else 0, N.ptr(ok), N.ptr(ov),
+                                 N.ptr(pos), cnt.data_ptr(), ws.data_ptr(), ws.numel(), N.error_word(dev).data_ptr(),
+                                 N.stream_handle(dev)), "rule_sum")
+        U = int(cnt.item())
+        return ok[:U], ov[:U], pos
+    from .sparse_reducers import _reduce
+    keys2 = (keys // E) // L * E + keys % E
+    uk, uv, inv, _ = _reduce(keys2, vals, 1 if take_max else 0, key_bits=max(1, int(B * E - 1).bit_length()))
+    return uk, uv, inv
 
 
-def spread_over_rules(eng: SlabEngine, out_keys, g_out, keys, B: int, L: int):
+def spread_over_rules(g_out, inv):
     """Backward of ``sum_over_rules``: the gradient at every ``(b, l, e)`` entry is the output
     gradient at ``(b, e)``."""
-    lib = N.load()
-    dev = eng.dev
-    E = eng.g.num_entities
-    bounds = list(_windows(B, eng.rows_per_window))
-    sl_out = _row_slices(out_keys, E, 1, bounds)
-    sl_in = _row_slices(keys, E, L, bounds)
-    st = N.stream_handle(dev)
-    err = N.error_word(dev).data_ptr()
-    g = torch.zeros(keys.numel(), dtype=torch.float32, device=dev)
-    gf = g_out.to(torch.float32).contiguous()
-    for (r0, nr), (oa, ob), (a, b) in zip(bounds, sl_out, sl_in):
-        if ob <= oa or b <= a:
-            continue
-        win = eng.window(r0, nr)
-        ko = out_keys[oa:ob]
-        N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), ko.data_ptr(), gf[oa:ob].data_ptr(),
-                                 ob - oa, 1, 0, err, st), "slab_put")
-        N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), keys[a:b].data_ptr(), b - a, L,
-                                  g[a:b].data_ptr(), 0, err, st), "slab_take")
-        N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ko.data_ptr(), ob - oa, 1, None, 1, err,
-                                  st), "slab_take")
-    return g
+    return g_out.to(torch.float32)[inv]
 
 
 def _mass_normalize(keys, y, E: int, BL: int, d32, threshold: float):
@@ -336,18 +335,26 @@ def _mass_normalize(keys, y, E: int, BL: int, d32, threshold: float):
     return x, int(dropped.item())
 
 
-def _mass_normalize_grad(keys, y, gx, E: int, BL: int, d32, spec):
+def _mass_normalize_grad(keys, y, gx, E: int, BL: int, d32, spec, eng: SlabEngine | None = None):
     """Gradient of the mass normalisation at its input: row sums of both terms in fp64
-    (all-reduced over ranks), then the per-entry gradient."""
+    (all-reduced over ranks), then the per-entry gradient.  With ``eng`` (a store whose one
+    window holds every row) the gradient is written straight into the store at the keys'
+    slots, ready for ``expand_backward(..., gy=None)``, and None is returned."""
     lib = N.load()
     dev = y.device
     sums = torch.zeros((2, BL), dtype=torch.float64, device=dev)
     n = int(y.numel())
     st = N.stream_handle(dev)
+    err = N.error_word(dev).data_ptr()
     N.check(lib.mkg_mass_normalize_grad_sums(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL,
-                                             d32.data_ptr(), sums.data_ptr(), N.error_word(dev).data_ptr(), st),
-            "mass_normalize_grad_sums")
+                                             d32.data_ptr(), sums.data_ptr(), err, st), "mass_normalize_grad_sums")
     _all_reduce(sums, spec)
+    if eng is not None:
+        win = eng.window(0, BL)
+        N.check(lib.mkg_mass_normalize_grad_put(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL,
+                                                d32.data_ptr(), sums.data_ptr(), ctypes.byref(win),
+                                                eng.store.data_ptr(), err, st), "mass_normalize_grad_put")
+        return None
     gy = torch.empty_like(y)
     N.check(lib.mkg_mass_normalize_grad(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL, d32.data_ptr(),
                                         sums.data_ptr(), gy.data_ptr(), st), "mass_normalize_grad")
@@ -367,18 +374,16 @@ def _all_reduce(t, spec):
 
 
 def _gather(keys, vals, spec):
-    """The whole frontier on every rank, ascending keys (ranks own disjoint keys); returns
-    (keys, values, (this rank's offset in rank order, the sorting permutation) or None)."""
+    """The whole frontier on every rank: the ranks' lists concatenated in rank order (ranks own
+    ascending entity ranges, so entity-major lists stay entity-major); returns (keys, values,
+    this rank's offset in the concatenation, or None)."""
     if spec is None or spec.world == 1:
         return keys, vals, None
     from .sharded import _all_gather_padded, _gather_counts
     counts = _gather_counts(int(keys.numel()), keys.device, spec.group)
     k_all = torch.cat(_all_gather_padded(keys, counts, spec.group))
     v_all = torch.cat(_all_gather_padded(vals.detach(), counts, spec.group))
-    off = sum(counts[: spec.rank])
-    # expansion windows need ascending keys: sort the gathered entries
-    order = torch.argsort(k_all)
-    return k_all[order], v_all[order], (off, order)
+    return k_all, v_all, sum(counts[: spec.rank])
 
 
 def _prune(keys, vals, E, topk_nodes):
@@ -415,7 +420,7 @@ class SlabHopLoop(autograd.Function):
             raise ValueError(f"query heads must lie in [0, {E})")
         keys = (torch.arange(BL, device=dev) * E + hd.repeat_interleave(L))
         own = (hd.repeat_interleave(L) >= eng.lo) & (hd.repeat_interleave(L) < eng.hi)
-        keys = torch.sort(keys[own]).values
+        keys, _ = entity_major(keys[own], keys[own], E, BL)
         vals = torch.ones(keys.numel(), dtype=torch.float32, device=dev)
         hops, msgs = [], []
         for h in range(K):
@@ -440,12 +445,12 @@ class SlabHopLoop(autograd.Function):
             else:
                 keys, vals = ky, x[0]
             hops.append(st)
-        out_keys, out_vals = sum_over_rules(eng, keys, vals, B, L)
+        out_keys, out_vals, inv = sum_over_rules(eng, keys, vals, B, L,
+                                                 entity_major_state=eng.rows_per_window >= BL)
         N.raise_device_errors(dev)  # an out-of-range index any kernel of the forward met
         ctx.hops, ctx.eng, ctx.spec = hops, eng, spec
         ctx.factor_write = factor_write
-        ctx.final_keys = keys
-        ctx.out_keys = out_keys
+        ctx.rule_inv = inv
         ctx.wf, ctx.shape = wf, (K, B, L, n)
         ctx.mask, ctx.is_score, ctx.scale = mask, bool(is_score), float(scale)
         ctx.edge_scores = edge_scores.detach() if edge_scores is not None else None
@@ -472,7 +477,7 @@ class SlabHopLoop(autograd.Function):
         factor = N.edge_factor(ctx.mask, ctx.edge_scores, ctx.is_score, ctx.scale, keep_alive)
         grad_w64 = torch.zeros((K, BL, n), dtype=torch.float64, device=dev)
         grad_edge = torch.zeros(g.num_facts, dtype=torch.float32, device=dev) if ctx.want_edge else None
-        g_state = spread_over_rules(eng, ctx.out_keys, g_vals, ctx.final_keys, B, L)
+        g_state = spread_over_rules(g_vals, ctx.rule_inv)
         for h in range(K - 1, -1, -1):
             st = ctx.hops[h]
             if st.keep is None:
@@ -480,7 +485,8 @@ class SlabHopLoop(autograd.Function):
             else:
                 gx = torch.zeros_like(st.y)
                 gx[st.keep] = g_state
-            gy = _mass_normalize_grad(st.keys_y, st.y, gx, E, BL, st.d, spec)
+            one_window = eng.store is not None and eng.rows_per_window >= BL
+            gy = _mass_normalize_grad(st.keys_y, st.y, gx, E, BL, st.d, spec, eng if one_window else None)
             gsp = expand_backward(eng, st.keys_in, st.vals_in, ctx.wf[h], BL, st.keys_y, gy, factor, grad_w64[h],
                                   grad_edge)
             if st.prune_sel is not None:  # back to the frontier before the prune
@@ -489,10 +495,7 @@ class SlabHopLoop(autograd.Function):
                 gsp = full
             if st.offset is not None:  # several ranks: sum the partials, keep this rank's entries
                 _all_reduce(gsp, spec)
-                off, order = st.offset
-                mine = torch.empty_like(gsp)
-                mine[order] = gsp          # back to rank order of the gather
-                gsp = mine[off: off + st.n_own]
+                gsp = gsp[st.offset: st.offset + st.n_own]
             g_state = gsp.to(torch.float32)
         _all_reduce(grad_w64, spec)
         if grad_edge is not None:
@@ -554,19 +557,24 @@ def slab_decode_max(engine: SlabEngine, heads: torch.Tensor, w_hops: torch.Tenso
     hd = heads.to(device=dev, dtype=torch.int64)
     if bool(((hd < 0) | (hd >= E)).any()):
         raise ValueError(f"query heads must lie in [0, {E})")
-    keys = torch.sort(torch.arange(BL, device=dev) * E + hd.repeat_interleave(L)).values
+    keys = torch.arange(BL, device=dev) * E + hd.repeat_interleave(L)
+    keys, _ = entity_major(keys, keys, E, BL)
     vals = torch.ones(BL, dtype=torch.float32, device=dev)
     for h in range(K):
         if msgs_out is not None:
             msgs_out.append(eng.full_degree[keys % E].sum())
         ky, y, _ = expand_forward(eng, keys, vals, wf[h], BL, check=False, agg_mode=1)
         rows = ky // E
-        seg = torch.searchsorted(rows, torch.arange(BL + 1, device=dev, dtype=rows.dtype))
-        d = N.segment_sum(seg, y, ordered=True).clamp(min=1e-7)
+        # each row's entries in ascending entity order (a stable sort by row of the
+        # entity-major list), summed one by one in that order
+        by_row = torch.sort(rows, stable=True)
+        seg = torch.searchsorted(by_row.values, torch.arange(BL + 1, device=dev, dtype=rows.dtype))
+        d = N.segment_sum(seg, y[by_row.indices], ordered=True).clamp(min=1e-7)
         x = y / d[rows]
         keep = torch.nonzero(x != 0, as_tuple=True)[0]
         keys, vals = ky[keep], x[keep]
-    out_keys, out_vals = sum_over_rules(eng, keys, vals, B, L, take_max=True)
+    out_keys, out_vals, _ = sum_over_rules(eng, keys, vals, B, L, take_max=True,
+                                           entity_major_state=eng.rows_per_window >= BL)
     N.raise_device_errors(dev)
     tails, scores, counts = sparse_topk(out_keys, out_vals, B, E, int(topk))
     return out_keys, out_vals, tails, scores, counts

@@ -51,8 +51,9 @@ def _coo(keys, vals, shape) -> torch.Tensor:
     return torch.sparse_coo_tensor(_unflat(keys, shape), vals, shape, is_coalesced=True)
 
 
-def _reduce(keys: torch.Tensor, vals: torch.Tensor, mode: int):
-    """(unique keys ascending, reduced values, inverse [n], arg [U]) of ``mkg_reduce_by_key``."""
+def _reduce(keys: torch.Tensor, vals: torch.Tensor, mode: int, key_bits: int | None = None):
+    """(unique keys ascending, reduced values, inverse [n], arg [U]) of ``mkg_reduce_by_key``;
+    ``key_bits`` bounds the keys (default: read from the largest key)."""
     lib = N.load()
     dev = vals.device
     n = int(keys.numel())
@@ -63,7 +64,7 @@ def _reduce(keys: torch.Tensor, vals: torch.Tensor, mode: int):
     inv = torch.empty(n, dtype=torch.int64, device=dev)
     arg = torch.empty(n, dtype=torch.int64, device=dev) if mode == 1 else None
     cnt = torch.zeros(1, dtype=torch.int64, device=dev)
-    bits = max(1, int(k.max()).bit_length()) if n else 1
+    bits = key_bits if key_bits is not None else (max(1, int(k.max()).bit_length()) if n else 1)
     ws = N.workspace(lib.mkg_reduce_by_key_workspace_bytes(n), dev)
     N.check(lib.mkg_reduce_by_key(k.data_ptr(), v.data_ptr(), n, mode, min(bits, 63), ok.data_ptr(), ov.data_ptr(),
                                   cnt.data_ptr(), inv.data_ptr(), N.ptr(arg), ws.data_ptr(), ws.numel(),

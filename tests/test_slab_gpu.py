@@ -124,6 +124,11 @@ def test_slab_hop_destination_ranges_add_up():
     keys = np.unique(rng.integers(0, B * L * E, 400))
     vals = rng.uniform(0.01, 1.0, keys.shape[0]).astype(np.float32)
     kf, vf, df = expand_forward(full, T(keys), T(vals), T(w_hops[0]), B * L)
+    # entity-major output: ascending entity, then row
+    em = ((kf % E) * (B * L) + kf // E).cpu().numpy()
+    assert (np.diff(em) > 0).all()
+    o = torch.argsort(kf)
+    kf, vf = kf[o], vf[o]
     bounds = plan_dst_ranges(message_in_counts(torch.from_numpy(h), torch.from_numpy(t), E), 3)
     ks, vs, ds = [], [], torch.zeros_like(df)
     from minikg_dev_b200.slab_loop import SlabEngine
@@ -153,11 +158,12 @@ def test_slab_hop_destination_ranges_add_up():
 
 
 def test_slab_bad_frontier_entity_is_reported():
-    """A frontier key outside [B, L, E] is refused on the host; one outside the window's rows
-    reaching the kernel is flagged, not followed, and the context stays usable."""
+    """A frontier key outside [B, L, E] is refused on the host; a negative key reaching the
+    kernel is flagged, not followed, and the context stays usable; a key of a row outside the
+    window belongs to another window's pass and is skipped without a flag."""
     import ctypes
     from minikg_dev_b200 import _native as N
-    from minikg_dev_b200.slab_loop import expand_forward
+    from minikg_dev_b200.slab_loop import _collect, expand_forward
     h, r, t, E, R, heads, w_hops, scores, mask = _case("g2", 2, 2, 1, 1)
     _, eng = _engine(h, r, t, E, R)
     keys = T(np.array([3, 2 * 2 * E + 5], np.int64))  # the second row is beyond B * L = 4
@@ -165,19 +171,27 @@ def test_slab_bad_frontier_entity_is_reported():
         expand_forward(eng, keys, T(np.ones(2, np.float32)), T(w_hops[0]), 4)
     lib = N.load()
     eng.ensure_store(4)
-    win = eng.window(0, 1)  # rows [0, 1): the key of row 1 is outside the window
-    k1 = T(np.array([3, E + 5], np.int64))
-    v1 = T(np.ones(2, np.float32))
     wf = T(w_hops[0]).reshape(4, -1).contiguous()
-    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(2), DEV)
-    N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k1.data_ptr(), v1.data_ptr(), 2,
-                                wf.data_ptr(), wf.shape[1], 1, 0, ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(),
-                                ws.numel(), N.error_word(DEV).data_ptr(), N.stream_handle(DEV)), "slab_expand")
+
+    def expand(win, k):
+        v = T(np.ones(k.numel(), np.float32))
+        ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(k.numel()), DEV)
+        N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), k.numel(),
+                                    wf.data_ptr(), wf.shape[1], 1, 0, ctypes.byref(win), eng.store.data_ptr(),
+                                    ws.data_ptr(), ws.numel(), N.error_word(DEV).data_ptr(), N.stream_handle(DEV)),
+                "slab_expand")
+
+    win = eng.window(0, 1)  # rows [0, 1)
+    expand(win, T(np.array([3, -7], np.int64)))
     with pytest.raises(RuntimeError, match="outside"):
         N.raise_device_errors(DEV)
-    eng.store.zero_()  # the accepted key's messages are still in the store
+    _collect(eng, win, False)  # the accepted key's messages leave the store
+    expand(win, T(np.array([3, E + 5], np.int64)))  # row 1: another window's entry
+    N.raise_device_errors(DEV)
+    ko, _, _ = _collect(eng, win, False)
+    assert ko.numel() > 0 and bool(((ko // E) == 0).all())
     torch.cuda.synchronize()
-    assert torch.ones(4, device=DEV).sum().item() == 4.0
+    assert _store_is_zero(eng)
 
 
 @pytest.mark.parametrize("gname,B,L,K,store_rows", [("hubby", 9, 3, 3, 0), ("g2", 6, 3, 3, 0), ("hubby", 9, 3, 2, 4)])
