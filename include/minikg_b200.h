@@ -418,21 +418,23 @@ size_t mkg_slab_expand_workspace_bytes(int64_t nnz);
  * normalisation).  agg_mode 0 adds the messages of a key (the sum hop, see above); agg_mode 1
  * keeps their maximum (the values of the max-aggregation hop, op agg_mode 1 followed by
  * sparse3d_max(ind, ori, inv), model_mmDRUM_kernel_sp.py:237-270, 388-445; the values must be
- * non-negative, as the loop's are). */
+ * non-negative, as the loop's are).  row_sums (agg_mode 0, may be NULL): [nrows] fp64, each
+ * window row's added message values are added to row_sums[r] (the column sums of
+ * normalize_sparse3d, drum.py:31-51: the sum of the row's output values, summed exactly in
+ * fp64 from the messages rather than from their fp32 per-key totals). */
 int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, const int64_t* keys, const float* vals,
                     int64_t nnz, const float* w, int64_t n, int32_t identity, int32_t agg_mode,
-                    const mkg_slab_window* win, void* store, void* workspace, size_t workspace_bytes,
-                    unsigned* dev_err, mkg_stream stream);
+                    const mkg_slab_window* win, void* store, double* row_sums, void* workspace,
+                    size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
 /* Number of touched keys in the store -> count_out (device int64).  The workspace (also read
  * by mkg_slab_emit) keeps per-tile offsets. */
 size_t mkg_slab_collect_workspace_bytes(int64_t slots);
 int mkg_slab_count(const mkg_slab_window* win, const void* store, void* workspace, size_t workspace_bytes,
                    int64_t* count_out, mkg_stream stream);
 /* Writes the touched keys in entity-major order (global keys (row0 + r) * E + lo + e) with
- * their values, clears them in the store and, when row_sums != NULL, adds each row's values to
- * row_sums[r] in fp64 (the column sums of normalize_sparse3d, drum.py:31-51). */
+ * their values and clears them in the store. */
 int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* workspace, size_t workspace_bytes,
-                  int64_t count, int64_t* keys_out, float* vals_out, double* row_sums, mkg_stream stream);
+                  int64_t count, int64_t* keys_out, float* vals_out, mkg_stream stream);
 /* Writes (mode 0), adds with a touched mark (mode 1) or raises to the maximum with a touched
  * mark (mode 2: max_sp_3d's max over rules with row_div = L) values at keys whose row is
  * (key / E) / row_div (row_div = L maps (b, l, e) to the [B, E] key b * E + e: sum_sp_3d,

@@ -132,11 +132,11 @@ SIGNATURES = {
     "mkg_cap_index_build": (C.c_int, [P(Graph), P(Adjacency), P(CapIndex), vp, C.c_size_t, vp, vp]),
     "mkg_slab_store_bytes": (C.c_size_t, [i64]),
     "mkg_slab_expand_workspace_bytes": (C.c_size_t, [i64]),
-    "mkg_slab_expand": (C.c_int, [vp, vp, vp, vp, i64, vp, i64, i32, i32, P(SlabWindow), vp, vp, C.c_size_t, vp,
-                                  vp]),
+    "mkg_slab_expand": (C.c_int, [vp, vp, vp, vp, i64, vp, i64, i32, i32, P(SlabWindow), vp, vp, vp, C.c_size_t,
+                                  vp, vp]),
     "mkg_slab_collect_workspace_bytes": (C.c_size_t, [i64]),
     "mkg_slab_count": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, vp, vp]),
-    "mkg_slab_emit": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, i64, vp, vp, vp, vp]),
+    "mkg_slab_emit": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, i64, vp, vp, vp]),
     "mkg_slab_put": (C.c_int, [P(SlabWindow), vp, vp, vp, i64, i64, i32, vp, vp]),
     "mkg_slab_take": (C.c_int, [P(SlabWindow), vp, vp, i64, i64, vp, i32, vp, vp]),
     "mkg_slab_expand_backward": (C.c_int, [vp, vp, vp, vp, i64, vp, i64, i32, P(SlabWindow), vp, P(EdgeFactor),

@@ -50,6 +50,23 @@ __device__ __forceinline__ void raise_flag(unsigned* err, unsigned bit) {
   if (err) atomicOr(err, bit);
 }
 
+// Division of a non-negative key (below 2^52) by a fixed divisor through its fp64 reciprocal:
+// the product's truncation is off by at most one, which one remainder test corrects.  A
+// 64-bit integer division is a long emulated sequence on the GPU; this is a multiply, two
+// conversions and a compare.
+struct FastDiv {
+  int64_t d;
+  double inv;
+  __host__ __device__ static FastDiv of(int64_t d) { return FastDiv{d, d > 0 ? 1.0 / (double)d : 0.0}; }
+  __device__ __forceinline__ int64_t div(int64_t n) const {
+    int64_t q = static_cast<int64_t>(static_cast<double>(n) * inv);
+    const int64_t r = n - q * d;
+    if (r < 0) --q;
+    else if (r >= d) ++q;
+    return q;
+  }
+};
+
 // Order-preserving 32-bit key of a float (larger float -> larger key; -0 < +0).
 __device__ __forceinline__ uint32_t float_order_key(float v) {
   uint32_t b = __float_as_uint(v);

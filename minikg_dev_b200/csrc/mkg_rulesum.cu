@@ -49,19 +49,31 @@ RuleSumLayout rule_sum_layout(int64_t n) {
   return L;
 }
 
-// (e, b) of an entry as one ascending composite (entity-major order of runs)
-__device__ __forceinline__ int64_t run_code(int64_t key, int64_t E, int64_t L, int64_t B) {
-  return (key % E) * B + (key / E) / L;
+// entity e and query b of a key (b * L + l) * E + e: one 64-bit division, the row's division
+// by L in 32 bits when the row fits
+__device__ __forceinline__ void split_key(int64_t key, const FastDiv& E, int64_t L, int64_t& e, int64_t& b) {
+  const int64_t q = E.div(key);
+  e = key - q * E.d;
+  b = (q <= 0x7fffffff && L <= 0x7fffffff) ? (int64_t)((uint32_t)q / (uint32_t)L) : q / L;
 }
 
-__global__ void rule_heads_kernel(const int64_t* __restrict__ keys, int64_t n, int64_t E, int64_t L, int64_t B,
+// (e, b) of an entry as one ascending composite (entity-major order of runs)
+__device__ __forceinline__ int64_t run_code(int64_t key, const FastDiv& E, int64_t L, int64_t B) {
+  int64_t e, b;
+  split_key(key, E, L, e, b);
+  return e * B + b;
+}
+
+__global__ void rule_heads_kernel(const int64_t* __restrict__ keys, int64_t n, FastDiv E, int64_t L, int64_t B,
                                   int32_t* __restrict__ head, int32_t* __restrict__ run_b, int32_t* __restrict__ iota,
                                   unsigned* err) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t k = keys[i];
     run_b[i] = static_cast<int32_t>(B);  // sentinel: overwritten for the runs that exist
     iota[i] = static_cast<int32_t>(i);
-    if (k < 0 || (k / E) / L >= B) {
+    int64_t e = 0, b = 0;
+    if (k >= 0) split_key(k, E, L, e, b);
+    if (k < 0 || b >= B) {
       raise_flag(err, MKG_DEV_BAD_KEY);
       head[i] = 0;
       continue;
@@ -69,7 +81,7 @@ __global__ void rule_heads_kernel(const int64_t* __restrict__ keys, int64_t n, i
     int32_t h = 1;
     if (i > 0) {
       const int64_t kp = keys[i - 1];
-      const int64_t c = run_code(k, E, L, B), cp = kp >= 0 ? run_code(kp, E, L, B) : -1;
+      const int64_t c = e * B + b, cp = kp >= 0 ? run_code(kp, E, L, B) : -1;
       if (c == cp) h = 0;
       else if (c < cp) raise_flag(err, MKG_DEV_BAD_KEY);  // not entity-major: runs would split
     }
@@ -80,23 +92,21 @@ __global__ void rule_heads_kernel(const int64_t* __restrict__ keys, int64_t n, i
 // scan[i] = number of runs up to and including entry i; a head folds its run
 template <bool MAX>
 __global__ void rule_runs_kernel(const int64_t* __restrict__ keys, const float* __restrict__ vals, int64_t n,
-                                 int64_t E, int64_t L, int64_t B, const int32_t* __restrict__ scan,
+                                 FastDiv E, int64_t L, int64_t B, const int32_t* __restrict__ scan,
                                  int32_t* __restrict__ run_b, int64_t* __restrict__ run_e,
                                  float* __restrict__ run_v, int64_t* __restrict__ count) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     if (i == n - 1) *count = scan[i];
     const int32_t r = scan[i] - 1;
     if (r < 0 || (i > 0 && scan[i - 1] == scan[i])) continue;  // not a run head
-    const int64_t k = keys[i];
-    const int64_t code = run_code(k, E, L, B);
+    // the run is every following entry with the same run number (a bad key, flagged by the
+    // heads pass, would fold into the run before it)
     float acc = vals[i];
-    for (int64_t j = i + 1; j < n && scan[j] == scan[i]; ++j) {
-      const int64_t kj = keys[j];
-      if (kj < 0 || run_code(kj, E, L, B) != code) break;
-      acc = MAX ? fmaxf(acc, vals[j]) : __fadd_rn(acc, vals[j]);
-    }
-    run_b[r] = static_cast<int32_t>((k / E) / L);
-    run_e[r] = k % E;
+    for (int64_t j = i + 1; j < n && scan[j] == scan[i]; ++j) acc = MAX ? fmaxf(acc, vals[j]) : __fadd_rn(acc, vals[j]);
+    int64_t e, b;
+    split_key(keys[i], E, L, e, b);
+    run_b[r] = static_cast<int32_t>(b);
+    run_e[r] = e;
     run_v[r] = acc;
   }
 }
@@ -165,13 +175,14 @@ MKG_API int mkg_rule_sum(const int64_t* keys, const float* vals, int64_t n, int6
   void* temp = w + Ly.temp;
   size_t tb = Ly.temp_bytes;
   const int grid = grid_for(n, 256, persistent_blocks(8));
-  rule_heads_kernel<<<grid, 256, 0, st>>>(keys, n, E, L, B, scan, run_b, iota, dev_err);
+  const FastDiv fe = FastDiv::of(E);
+  rule_heads_kernel<<<grid, 256, 0, st>>>(keys, n, fe, L, B, scan, run_b, iota, dev_err);
   MKG_LAUNCHED("rule_heads_kernel");
   MKG_CUDA(cub::DeviceScan::InclusiveSum(temp, tb, scan, scan, (int)n, st));
   if (mode == 1)
-    rule_runs_kernel<true><<<grid, 256, 0, st>>>(keys, vals, n, E, L, B, scan, run_b, run_e, run_v, count);
+    rule_runs_kernel<true><<<grid, 256, 0, st>>>(keys, vals, n, fe, L, B, scan, run_b, run_e, run_v, count);
   else
-    rule_runs_kernel<false><<<grid, 256, 0, st>>>(keys, vals, n, E, L, B, scan, run_b, run_e, run_v, count);
+    rule_runs_kernel<false><<<grid, 256, 0, st>>>(keys, vals, n, fe, L, B, scan, run_b, run_e, run_v, count);
   MKG_LAUNCHED("rule_runs_kernel");
   // stable: runs of one query keep their ascending-entity order
   MKG_CUDA(cub::DeviceRadixSort::SortPairs(temp, tb, run_b, sorted_b, iota, perm, (int)n, 0, bits_for(B), st));

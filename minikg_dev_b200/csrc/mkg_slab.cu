@@ -5,8 +5,9 @@
 // The output of a hop lives in a *slab store*: one fp32 slot per output key of a window of
 // (b, l) rows x a destination range, plus one "touched" bit per slot.  A message adds its
 // value to its slot with one atomic reduction and sets the slot's bit with another (neither
-// returns a value, so no thread waits on them).  The touched keys then come out in ascending key order by a popcount scan of the
-// bitmap -- no sort, no hash table -- and the emit clears every slot and bit it read, so the
+// returns a value, so no thread waits on them).  The touched keys then come out in slot order
+// (entity-major, below) by a popcount scan of the bitmap -- no sort, no hash table -- and the
+// emit clears every slot and bit it read, so the
 // store is all zeros again after each use (the caller zero-fills it once, when it is made).
 //
 // Messages of a frontier entry (b, l, s, x) are the records of push row s ({neighbour d,
@@ -35,7 +36,7 @@ constexpr int kTileThreads = 256;
 constexpr int kWordsPerThread = 32;
 constexpr int64_t kTileWords = (int64_t)kTileThreads * kWordsPerThread;  // bitmap words per collect block
 constexpr int kRowBins = 256;             // row-sum bins of one emit / row-sum block
-constexpr int kEmitStage = 512;           // keys a warp of the emit stages before writing them
+constexpr int kEmitStage = 128;           // keys a warp of the emit stages before writing them
 
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -44,6 +45,7 @@ size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 // destinations, land in one 32-byte sector of values and in one bitmap word.
 struct Window {
   int64_t E, row0, nrows, lo, extent;
+  FastDiv fe;  // key -> row
   __host__ __device__ int64_t slot(int64_t lrow, int64_t le) const { return le * nrows + lrow; }
 };
 
@@ -51,7 +53,15 @@ bool window_ok(const mkg_slab_window* w) {
   return w && w->E > 0 && w->row0 >= 0 && w->nrows > 0 && w->lo >= 0 && w->extent > 0 && w->lo + w->extent <= w->E;
 }
 
-Window make_window(const mkg_slab_window& w) { return Window{w.E, w.row0, w.nrows, w.lo, w.extent}; }
+Window make_window(const mkg_slab_window& w) {
+  return Window{w.E, w.row0, w.nrows, w.lo, w.extent, FastDiv::of(w.E)};
+}
+
+// row of a non-negative key divided by row_div (1, or L for the (b, e) keys of a sum over rules)
+__device__ __forceinline__ int64_t div_rows(int64_t q, int64_t row_div) {
+  if (row_div == 1) return q;
+  return (q <= 0x7fffffff && row_div <= 0x7fffffff) ? (int64_t)((uint32_t)q / (uint32_t)row_div) : q / row_div;
+}
 
 struct Store {
   float* val;
@@ -67,11 +77,12 @@ Store make_store(void* base, int64_t slots) {
 
 int64_t bitmap_words(int64_t slots) { return (slots + 31) / 32; }
 
-// slot of a global key (row * E + e), with rows grouped by row_div (the sum over rules maps
-// (b * L + l) to b with row_div = L); -1 when outside the window
+// slot of a global key (row * E + e, key >= 0), with rows grouped by row_div (the sum over
+// rules maps (b * L + l) to b with row_div = L); -1 when outside the window
 __device__ __forceinline__ int64_t slot_of(const Window& w, int64_t key, int64_t row_div) {
-  const int64_t row = (key / w.E) / row_div - w.row0;
-  const int64_t e = key % w.E - w.lo;
+  const int64_t q = w.fe.div(key);
+  const int64_t row = div_rows(q, row_div) - w.row0;
+  const int64_t e = key - q * w.E - w.lo;
   if (row < 0 || row >= w.nrows || e < 0 || e >= w.extent) return -1;
   return w.slot(row, e);
 }
@@ -79,8 +90,9 @@ __device__ __forceinline__ int64_t slot_of(const Window& w, int64_t key, int64_t
 // 1 when the key's row (after row_div) lies outside the window's rows but its entity inside
 // the destination range: a key of another row window
 __device__ __forceinline__ bool other_rows(const Window& w, int64_t key, int64_t row_div) {
-  const int64_t row = (key / w.E) / row_div - w.row0;
-  const int64_t e = key % w.E - w.lo;
+  const int64_t q = w.fe.div(key);
+  const int64_t row = div_rows(q, row_div) - w.row0;
+  const int64_t e = key - q * w.E - w.lo;
   return (row < 0 || row >= w.nrows) && e >= 0 && e < w.extent;
 }
 
@@ -129,7 +141,7 @@ __device__ __forceinline__ int64_t chunk_entry(const int64_t* __restrict__ ptr, 
   int64_t lo = 0, hi = nnz - 1;
   while (lo < hi) {
     const int64_t mid = (lo + hi + 1) >> 1;
-    if (ptr[mid] <= c) lo = mid; else hi = mid - 1;
+    if (__ldg(ptr + mid) <= c) lo = mid; else hi = mid - 1;  // read-only path: the top levels stay in L1
   }
   return lo;
 }
@@ -147,6 +159,7 @@ struct ExpandArgs {
   int max_mode;              // 1: slots keep the largest message (values must be >= 0)
   Window win;
   unsigned* err;
+  double* rsum;              // forward, sum mode, may be null: [nrows] row sums of the added messages
 };
 
 // ------------------------------------------------------------------ forward expansion
@@ -169,17 +182,19 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_kernel(ExpandArgs 
     const float x = a.vals[i];
     const float* wrow = a.w + row * a.n;
     const int64_t k = c - a.chunk_ptr[i];
+    double part = 0.0;  // the lane's added message values (the row sum of the normalisation)
     if (k == 0 && lane == 0 && a.identity && s >= a.win.lo && s < a.win.lo + a.win.extent) {
       const float v = x * wrow[a.n - 1];
       if (v != 0.0f) {
         const int64_t sl = a.win.slot(lrow, s - a.win.lo);
         slot_reduce(st.val + sl, v, a.max_mode);
         atomicOr(st.bits + (sl >> 5), 1u << (sl & 31));
+        part += (double)v;
       }
     }
     const int64_t rb = a.push_ptr[s] + k * kChunkRecs;
     const int64_t re = min(rb + kChunkRecs, (int64_t)a.push_ptr[s + 1]);
-    if (x == 0.0f) continue;
+    if (x != 0.0f) {
     int4 rec[kChunkRecs / 32];
 #pragma unroll
     for (int u = 0; u < kChunkRecs / 32; ++u) {
@@ -210,7 +225,15 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_kernel(ExpandArgs 
       if (slot[u] >= 0 && v != 0.0f) {
         slot_reduce(st.val + slot[u], v, a.max_mode);
         atomicOr(st.bits + (slot[u] >> 5), 1u << (slot[u] & 31));
+        part += (double)v;
       }
+    }
+    }
+    // one fp64 row-sum atomic per chunk: every message of a chunk lies in its entry's row
+    if (a.rsum != nullptr) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0 && part != 0.0) atomicAdd(a.rsum + lrow, part);
     }
   }
 }
@@ -233,24 +256,26 @@ __global__ void __launch_bounds__(kTileThreads) slab_count_kernel(const uint32_t
 
 // Block b owns bitmap words [b * kTileWords, (b + 1) * kTileWords) (the tile slab_count_kernel
 // counted); every set bit is placed at its rank, so the keys come out in slot order
-// (entity-major), and each word is cleared after it is read.  This pass only stores (no
-// dependent loads per bit); slab_gather_kernel then reads the values.
-__global__ void __launch_bounds__(kTileThreads) slab_emit_keys_kernel(Store st, Window win, int64_t words,
-                                                                     const int64_t* __restrict__ blk_off,
-                                                                     int64_t count, int64_t* __restrict__ keys_out) {
+// (entity-major), and each word is cleared after it is read.
+__global__ void __launch_bounds__(kTileThreads) slab_emit_kernel(Store st, Window win, int64_t words,
+                                                                const int64_t* __restrict__ blk_off, int64_t count,
+                                                                int64_t* __restrict__ keys_out) {
   // warp w of the block owns the tile's words [w * 1024, (w + 1) * 1024), lane l reads words
   // w * 1024 + k * 32 + l: one pass counts the warp's bits, a scan of the 8 warp counts in
   // shared memory places each warp, a second pass emits with a warp scan per 32 words
   constexpr int kWarps = kTileThreads / 32;
   constexpr int kSpan = (int)(kTileWords / kWarps);  // words per warp
   __shared__ long long warp_base[kWarps];
+  __shared__ uint32_t wsm[kWarps][kSpan];  // the warp's words, loaded once (all loads in flight)
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int64_t wb = blockIdx.x * kTileWords + (int64_t)wid * kSpan;
   int c = 0;
 #pragma unroll 8
   for (int k = 0; k < kSpan / 32; ++k) {
     const int64_t wi = wb + k * 32 + lane;
-    if (wi < words) c += __popc(st.bits[wi]);
+    const uint32_t wv = wi < words ? st.bits[wi] : 0u;
+    wsm[wid][k * 32 + lane] = wv;
+    c += __popc(wv);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
@@ -265,14 +290,18 @@ __global__ void __launch_bounds__(kTileThreads) slab_emit_keys_kernel(Store st, 
     }
   }
   __syncthreads();
-  // The keys of 32 words (up to 1024) are placed in a per-warp shared buffer at their rank and
-  // written out by the whole warp, kEmitStage at a time: coalesced stores even where the
-  // entity-major bitmap packs many bits into neighbouring words.
+  // The slots of 32 words (up to 1024 set bits) are placed in a per-warp shared buffer at their
+  // rank, kEmitStage at a time; the whole warp then writes their keys (coalesced stores even
+  // where the entity-major bitmap packs many bits into neighbouring words).  The values are
+  // left to slab_gather_kernel: loading them here put one memory round trip behind every
+  // non-empty group of words (measured: 1.0 -> 3.2 ms per launch on the 4.6 M-entity hop).
   __shared__ long long stage[kWarps][kEmitStage];
+  const FastDiv win_rows = FastDiv::of(win.nrows);  // slot -> entity
   int64_t base = warp_base[wid];
   for (int k = 0; k < kSpan / 32; ++k) {
+    const uint32_t word0 = wsm[wid][k * 32 + lane];
+    if (__ballot_sync(0xffffffffu, word0 != 0u) == 0u) continue;  // most groups are empty
     const int64_t wi = wb + k * 32 + lane;
-    const uint32_t word0 = wi < words ? st.bits[wi] : 0u;
     const int pc = __popc(word0);
     int incl = pc;
 #pragma unroll
@@ -281,30 +310,23 @@ __global__ void __launch_bounds__(kTileThreads) slab_emit_keys_kernel(Store st, 
       if (lane >= o) incl += y;
     }
     const int tot = __shfl_sync(0xffffffffu, incl, 31);
-    if (tot == 0) continue;
     if (word0) st.bits[wi] = 0u;
-    // the word's first slot as (entity, row) once; rows then advance bit by bit
-    const int64_t s0 = wi * 32;
-    const int64_t le0 = s0 / win.nrows;
-    const int64_t r0 = s0 - le0 * win.nrows;
     for (int pass = 0; pass < tot; pass += kEmitStage) {
       uint32_t word = word0;
       int q = incl - pc;  // rank of the lane's first bit among the 32 words' bits
       while (word) {
         const int j = __ffs(word) - 1;
         word &= word - 1;
-        if (q >= pass && q < pass + kEmitStage) {
-          int64_t r = r0 + j, le = le0;
-          while (r >= win.nrows) { r -= win.nrows; ++le; }
-          stage[wid][q - pass] = (win.row0 + r) * win.E + win.lo + le;
-        }
+        if (q >= pass && q < pass + kEmitStage) stage[wid][q - pass] = wi * 32 + j;
         ++q;
       }
       __syncwarp();
       const int m = tot - pass < kEmitStage ? tot - pass : kEmitStage;
       for (int t = lane; t < m; t += 32) {
         const int64_t p = base + pass + t;
-        if (p < count) keys_out[p] = stage[wid][t];
+        const int64_t sl = stage[wid][t];
+        const int64_t le = win_rows.div(sl);
+        if (p < count) keys_out[p] = (win.row0 + (sl - le * win.nrows)) * win.E + win.lo + le;
       }
       __syncwarp();
     }
@@ -313,34 +335,25 @@ __global__ void __launch_bounds__(kTileThreads) slab_emit_keys_kernel(Store st, 
 }
 
 // Values of the emitted keys: a block walks tiles of kTileThreads * kGatherItems outputs, each
-// thread kGatherItems of them a block width apart (neighbouring lanes read neighbouring keys and,
-// in the entity-major store, neighbouring slots), issues their slot loads together, clears the
-// slots and writes the values.  Row sums (optional, fp64) go to shared bins of all the window's
-// rows, added to the output once per block (global atomics when the window has more rows).
+// thread kGatherItems of them a block width apart (neighbouring lanes read neighbouring keys
+// and, in the entity-major store, neighbouring slots), issues their slot loads together, clears
+// the slots and writes the values.
 constexpr int kGatherItems = 8;
-constexpr int kMaxBinRows = 2048;  // 16 KB of fp64 bins
 __global__ void __launch_bounds__(kTileThreads) slab_gather_kernel(Store st, Window win,
                                                                   const int64_t* __restrict__ keys, int64_t count,
-                                                                  float* __restrict__ vals_out,
-                                                                  double* __restrict__ rsum) {
-  __shared__ double bins[kMaxBinRows];
-  const bool binned = rsum != nullptr && win.nrows <= kMaxBinRows;
-  if (binned)
-    for (int64_t i = threadIdx.x; i < win.nrows; i += kTileThreads) bins[i] = 0.0;
-  __syncthreads();
+                                                                  float* __restrict__ vals_out) {
   constexpr int64_t kTile = (int64_t)kTileThreads * kGatherItems;
   for (int64_t i0 = blockIdx.x * kTile; i0 < count; i0 += (int64_t)gridDim.x * kTile) {
-    int64_t slot[kGatherItems], row[kGatherItems];
+    int64_t slot[kGatherItems];
     float v[kGatherItems];
 #pragma unroll
     for (int u = 0; u < kGatherItems; ++u) {
       const int64_t i = i0 + u * kTileThreads + threadIdx.x;
       slot[u] = -1;
-      row[u] = -1;
       if (i < count) {
         const int64_t k = keys[i];
-        row[u] = k / win.E - win.row0;
-        slot[u] = win.slot(row[u], k % win.E - win.lo);
+        const int64_t q = win.fe.div(k);
+        slot[u] = win.slot(q - win.row0, k - q * win.E - win.lo);
       }
     }
 #pragma unroll
@@ -350,18 +363,11 @@ __global__ void __launch_bounds__(kTileThreads) slab_gather_kernel(Store st, Win
       if (slot[u] < 0) continue;
       st.val[slot[u]] = 0.0f;
       vals_out[i0 + u * kTileThreads + threadIdx.x] = v[u];
-      if (rsum != nullptr) {
-        if (binned) atomicAdd(&bins[row[u]], (double)v[u]);
-        else atomicAdd(rsum + row[u], (double)v[u]);
-      }
     }
   }
-  if (binned) {
-    __syncthreads();
-    for (int64_t i = threadIdx.x; i < win.nrows; i += kTileThreads)
-      if (bins[i] != 0.0) atomicAdd(rsum + i, bins[i]);
-  }
 }
+
+constexpr int kMaxBinRows = 2048;  // 16 KB of fp64 row bins per block (gradient row sums)
 
 // ------------------------------------------------------------------ put / take
 __global__ void slab_put_kernel(Store st, Window win, const int64_t* __restrict__ keys, const float* __restrict__ vals,
@@ -563,12 +569,12 @@ __global__ void __launch_bounds__(kTileThreads) row_sums_kernel(const int64_t* _
 // min(d, 1) with d the row's sum (fp32 division and product, as torch computes them); counts
 // the zeros the result holds (entries the hop loop then drops) and the entries under a state
 // threshold.
-__global__ void mass_norm_kernel(const int64_t* __restrict__ keys, const float* __restrict__ y, int64_t n, int64_t E,
+__global__ void mass_norm_kernel(const int64_t* __restrict__ keys, const float* __restrict__ y, int64_t n, FastDiv E,
                                  int64_t row0, int64_t nrows, const float* __restrict__ d, float thr,
                                  float* __restrict__ x, unsigned long long* __restrict__ dropped, unsigned* err) {
   unsigned long long local = 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = keys[i] / E - row0;
+    const int64_t r = E.div(keys[i]) - row0;
     float v = 0.0f;
     if (r < 0 || r >= nrows) {
       raise_flag(err, MKG_DEV_BAD_KEY);
@@ -588,7 +594,7 @@ __global__ void mass_norm_kernel(const int64_t* __restrict__ keys, const float* 
 // (any entry order).  One wave of blocks, each with shared bins of every row (up to
 // kMaxBinRows rows; global atomics beyond), added to the output once per block.
 __global__ void __launch_bounds__(kTileThreads) mass_norm_grad_sums_kernel(
-    const int64_t* __restrict__ keys, const float* __restrict__ y, const float* __restrict__ gx, int64_t n, int64_t E,
+    const int64_t* __restrict__ keys, const float* __restrict__ y, const float* __restrict__ gx, int64_t n, FastDiv E,
     int64_t row0, int64_t nrows, const float* __restrict__ d, double* __restrict__ sums, unsigned* err) {
   __shared__ double bins[2][kMaxBinRows];
   const bool binned = nrows <= kMaxBinRows;
@@ -596,7 +602,7 @@ __global__ void __launch_bounds__(kTileThreads) mass_norm_grad_sums_kernel(
     for (int64_t i = threadIdx.x; i < nrows; i += kTileThreads) { bins[0][i] = 0.0; bins[1][i] = 0.0; }
   __syncthreads();
   for (int64_t i = blockIdx.x * (int64_t)kTileThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kTileThreads) {
-    const int64_t r = keys[i] / E - row0;
+    const int64_t r = E.div(keys[i]) - row0;
     if (r < 0 || r >= nrows) {
       raise_flag(err, MKG_DEV_BAD_KEY);
       continue;
@@ -632,12 +638,12 @@ __global__ void __launch_bounds__(kTileThreads) mass_norm_grad_sums_kernel(
 // transposed walk) instead of into an array.
 template <bool PUT>
 __global__ void mass_norm_grad_kernel(const int64_t* __restrict__ keys, const float* __restrict__ y,
-                                      const float* __restrict__ gx, int64_t n, int64_t E, int64_t row0,
+                                      const float* __restrict__ gx, int64_t n, FastDiv E, int64_t row0,
                                       int64_t nrows, const float* __restrict__ d, const double* __restrict__ sums,
                                       float* __restrict__ gy, Store st, Window win, unsigned* err) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t k = keys[i];
-    const int64_t r = k / E - row0;
+    const int64_t r = E.div(k) - row0;
     float out = 0.0f;
     if (r >= 0 && r < nrows && y[i] != 0.0f) {
       const float dr = d[r];
@@ -735,9 +741,10 @@ MKG_API size_t mkg_slab_expand_workspace_bytes(int64_t nnz) {
 
 MKG_API int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, const int64_t* keys, const float* vals,
                             int64_t nnz, const float* w, int64_t n, int32_t identity, int32_t agg_mode,
-                            const mkg_slab_window* win, void* store, void* workspace, size_t workspace_bytes,
-                            unsigned* dev_err, mkg_stream stream) {
+                            const mkg_slab_window* win, void* store, double* row_sums, void* workspace,
+                            size_t workspace_bytes, unsigned* dev_err, mkg_stream stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  MKG_REQUIRE(row_sums == nullptr || agg_mode == 0, "slab_expand: row sums belong to the sum hop (agg_mode 0)");
   MKG_REQUIRE(window_ok(win), "slab_expand: bad window");
   MKG_REQUIRE(nnz >= 0 && n >= 1 && n <= INT32_MAX, "slab_expand: bad sizes");
   MKG_REQUIRE(agg_mode == 0 || agg_mode == 1, "slab_expand: agg_mode must be 0 (sum) or 1 (max)");
@@ -748,7 +755,7 @@ MKG_API int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, c
   int rc = build_chunks(push_ptr, keys, nnz, *win, workspace, workspace_bytes, &cp, dev_err, st);
   if (rc) return rc;
   ExpandArgs a{push_ptr, reinterpret_cast<const int4*>(push), keys, vals, nnz, cp, w, n, identity, agg_mode,
-               make_window(*win), dev_err};
+               make_window(*win), dev_err, row_sums};
   slab_expand_kernel<<<expand_grid(nnz), kExpandThreads, 0, st>>>(a, make_store(store, win->nrows * win->extent));
   MKG_LAUNCHED("slab_expand_kernel");
   return MKG_OK;
@@ -781,7 +788,7 @@ MKG_API int mkg_slab_count(const mkg_slab_window* win, const void* store, void* 
 }
 
 MKG_API int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* workspace, size_t workspace_bytes,
-                          int64_t count, int64_t* keys_out, float* vals_out, double* row_sums, mkg_stream stream) {
+                          int64_t count, int64_t* keys_out, float* vals_out, mkg_stream stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   MKG_REQUIRE(window_ok(win) && store && workspace, "slab_emit: bad argument");
   MKG_REQUIRE(count >= 0 && (count == 0 || (keys_out && vals_out)), "slab_emit: bad output");
@@ -789,15 +796,13 @@ MKG_API int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* w
   const int64_t words = bitmap_words(slots), nblk = collect_blocks(slots);
   MKG_REQUIRE(workspace_bytes >= mkg_slab_collect_workspace_bytes(slots), "slab_emit: workspace too small");
   const Store s = make_store(store, slots);
-  slab_emit_keys_kernel<<<(unsigned)nblk, kTileThreads, 0, st>>>(s, make_window(*win), words,
-                                                                 static_cast<const int64_t*>(workspace), count,
-                                                                 keys_out);
-  MKG_LAUNCHED("slab_emit_keys_kernel");
+  slab_emit_kernel<<<(unsigned)nblk, kTileThreads, 0, st>>>(s, make_window(*win), words,
+                                                            static_cast<const int64_t*>(workspace), count, keys_out);
+  MKG_LAUNCHED("slab_emit_kernel");
   if (count > 0) {
-    // one wave of resident blocks: each adds its row bins to the output once
-    const int gblocks = grid_for(count, kTileThreads * kGatherItems, resident_grid(slab_gather_kernel, kTileThreads));
-    slab_gather_kernel<<<(unsigned)gblocks, kTileThreads, 0, st>>>(s, make_window(*win), keys_out, count, vals_out,
-                                                                     row_sums);
+    const int64_t per = (int64_t)kTileThreads * kGatherItems;
+    const int gblocks = grid_for(count, (int)per, persistent_blocks(16));
+    slab_gather_kernel<<<(unsigned)gblocks, kTileThreads, 0, st>>>(s, make_window(*win), keys_out, count, vals_out);
     MKG_LAUNCHED("slab_gather_kernel");
   }
   return MKG_OK;
@@ -845,7 +850,7 @@ MKG_API int mkg_slab_expand_backward(const int32_t* push_ptr, const mkg_adj_edge
   int rc = build_chunks(push_ptr, keys, nnz, *win, workspace, workspace_bytes, &cp, dev_err, st);
   if (rc) return rc;
   ExpandArgs a{push_ptr, reinterpret_cast<const int4*>(push), keys, vals, nnz, cp, w, n, identity, 0,
-               make_window(*win), dev_err};
+               make_window(*win), dev_err, nullptr};
   slab_expand_backward_kernel<<<expand_backward_grid(nnz), kExpandThreads, 0, st>>>(
       a, static_cast<const float*>(store), make_factor(*ef), num_facts, grad_sp, grad_w, grad_edge);
   MKG_LAUNCHED("slab_expand_backward_kernel");
@@ -875,7 +880,7 @@ MKG_API int mkg_mass_normalize(const int64_t* keys, const float* y, int64_t n, i
   if (n == 0) return MKG_OK;
   MKG_REQUIRE(keys && y && row_sums && x, "mass_normalize: null argument");
   mass_norm_kernel<<<stride_grid(mass_norm_kernel, n), 256, 0, st>>>(
-      keys, y, n, E, row0, nrows, row_sums, threshold, x, reinterpret_cast<unsigned long long*>(dropped), dev_err);
+      keys, y, n, FastDiv::of(E), row0, nrows, row_sums, threshold, x, reinterpret_cast<unsigned long long*>(dropped), dev_err);
   MKG_LAUNCHED("mass_norm_kernel");
   return MKG_OK;
 }
@@ -888,7 +893,7 @@ MKG_API int mkg_mass_normalize_grad_sums(const int64_t* keys, const float* y, co
   if (n == 0) return MKG_OK;
   MKG_REQUIRE(keys && y && gx && row_sums && sums, "mass_normalize_grad_sums: null argument");
   const int blocks = stride_grid(mass_norm_grad_sums_kernel, n, kTileThreads);
-  mass_norm_grad_sums_kernel<<<(unsigned)blocks, kTileThreads, 0, st>>>(keys, y, gx, n, E, row0, nrows, row_sums,
+  mass_norm_grad_sums_kernel<<<(unsigned)blocks, kTileThreads, 0, st>>>(keys, y, gx, n, FastDiv::of(E), row0, nrows, row_sums,
                                                                          sums, dev_err);
   MKG_LAUNCHED("mass_norm_grad_sums_kernel");
   return MKG_OK;
@@ -902,7 +907,7 @@ MKG_API int mkg_mass_normalize_grad(const int64_t* keys, const float* y, const f
   if (n == 0) return MKG_OK;
   MKG_REQUIRE(keys && y && gx && row_sums && sums && gy, "mass_normalize_grad: null argument");
   mass_norm_grad_kernel<false><<<stride_grid(mass_norm_grad_kernel<false>, n), 256, 0, st>>>(
-      keys, y, gx, n, E, row0, nrows, row_sums, sums, gy, Store{}, Window{}, nullptr);
+      keys, y, gx, n, FastDiv::of(E), row0, nrows, row_sums, sums, gy, Store{}, Window{}, nullptr);
   MKG_LAUNCHED("mass_norm_grad_kernel");
   return MKG_OK;
 }
@@ -917,7 +922,7 @@ MKG_API int mkg_mass_normalize_grad_put(const int64_t* keys, const float* y, con
   if (n == 0) return MKG_OK;
   MKG_REQUIRE(keys && y && gx && row_sums && sums && store, "mass_normalize_grad_put: null argument");
   mass_norm_grad_kernel<true><<<stride_grid(mass_norm_grad_kernel<true>, n), 256, 0, st>>>(
-      keys, y, gx, n, E, row0, nrows, row_sums, sums, nullptr, make_store(store, win->nrows * win->extent),
+      keys, y, gx, n, FastDiv::of(E), row0, nrows, row_sums, sums, nullptr, make_store(store, win->nrows * win->extent),
       make_window(*win), dev_err);
   MKG_LAUNCHED("mass_norm_grad_kernel");
   return MKG_OK;

@@ -149,8 +149,8 @@ def _events(eng: SlabEngine):
     return ev
 
 
-def _collect(eng: SlabEngine, win, want_rows: bool):
-    """Emits the touched keys of the store (ascending) with values and fp64 row sums."""
+def _collect(eng: SlabEngine, win):
+    """Emits the touched keys of the store (entity-major order) with their values."""
     lib = N.load()
     dev = eng.dev
     st = N.stream_handle(dev)
@@ -162,10 +162,9 @@ def _collect(eng: SlabEngine, win, want_rows: bool):
     U = int(cnt.item())
     keys = torch.empty(U, dtype=torch.int64, device=dev)
     vals = torch.empty(U, dtype=torch.float32, device=dev)
-    rs = torch.zeros(win.nrows, dtype=torch.float64, device=dev) if want_rows else None
     N.check(lib.mkg_slab_emit(ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(), ws.numel(), U,
-                              keys.data_ptr(), vals.data_ptr(), N.ptr(rs), st), "slab_emit")
-    return keys, vals, rs
+                              keys.data_ptr(), vals.data_ptr(), st), "slab_emit")
+    return keys, vals
 
 
 def graph_bytes(eng: SlabEngine, keys) -> int:
@@ -213,20 +212,19 @@ def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True
     for r0, nr in bounds:  # every window takes the whole frontier and walks the entries of its rows
         win = eng.window(r0, nr)
         ev = _events(eng)
+        rs = d[r0:r0 + nr].data_ptr() if agg_mode == 0 else None  # the expansion adds its row sums
         N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), nk,
-                                    wf.data_ptr(), n, 1, int(agg_mode), ctypes.byref(win), eng.store.data_ptr(),
+                                    wf.data_ptr(), n, 1, int(agg_mode), ctypes.byref(win), eng.store.data_ptr(), rs,
                                     ws.data_ptr(), ws.numel(), err, st), "slab_expand")
         if ev is not None:
             ev[1].record()
-        ko, vo, rs = _collect(eng, win, agg_mode == 0)
+        ko, vo = _collect(eng, win)
         if ev is not None:  # frontier in + output out (12 B per key: 8 B key, 4 B value), rule weights
             mine = k[((k // E) >= r0) & ((k // E) < r0 + nr)] if len(bounds) > 1 else k
             eng.trace.append(("fwd", ev[0], ev[1], graph_bytes(eng, mine) + 12 * int(mine.numel())
                               + 12 * ko.numel() + nr * n * 4))
         out_k.append(ko)
         out_v.append(vo)
-        if rs is not None:
-            d[r0:r0 + nr] = rs
     if len(out_k) == 1:
         return out_k[0], out_v[0], d
     return torch.cat(out_k), torch.cat(out_v), d

@@ -177,7 +177,7 @@ def test_slab_bad_frontier_entity_is_reported():
         v = T(np.ones(k.numel(), np.float32))
         ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(k.numel()), DEV)
         N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), k.numel(),
-                                    wf.data_ptr(), wf.shape[1], 1, 0, ctypes.byref(win), eng.store.data_ptr(),
+                                    wf.data_ptr(), wf.shape[1], 1, 0, ctypes.byref(win), eng.store.data_ptr(), None,
                                     ws.data_ptr(), ws.numel(), N.error_word(DEV).data_ptr(), N.stream_handle(DEV)),
                 "slab_expand")
 
@@ -185,10 +185,10 @@ def test_slab_bad_frontier_entity_is_reported():
     expand(win, T(np.array([3, -7], np.int64)))
     with pytest.raises(RuntimeError, match="outside"):
         N.raise_device_errors(DEV)
-    _collect(eng, win, False)  # the accepted key's messages leave the store
+    _collect(eng, win)  # the accepted key's messages leave the store
     expand(win, T(np.array([3, E + 5], np.int64)))  # row 1: another window's entry
     N.raise_device_errors(DEV)
-    ko, _, _ = _collect(eng, win, False)
+    ko, _ = _collect(eng, win)
     assert ko.numel() > 0 and bool(((ko // E) == 0).all())
     torch.cuda.synchronize()
     assert _store_is_zero(eng)
