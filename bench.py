@@ -549,9 +549,9 @@ def run_slab(a, wl, kg, rank, world, local_rank):
     torch.cuda.synchronize()
     trace, eng.trace = eng.trace, None
     kinds = {}
-    for kind, e0, e1, byts in trace:
-        d = kinds.setdefault(kind, {"ms": [], "bytes": []})
-        d["ms"].append(e0.elapsed_time(e1))
+    for kind, evs, byts in trace:  # one entry per hop: its destination tiles' launches
+        d = kinds.setdefault(kind, {"ms": [], "bytes": [], "tiles": len(evs)})
+        d["ms"].append(sum(e0.elapsed_time(e1) for e0, e1 in evs))
         d["bytes"].append(byts)
 
     # end to end through the public API (slab_proof_scores): the batch's query heads and rule
@@ -596,8 +596,11 @@ def run_slab(a, wl, kg, rank, world, local_rank):
     kernels = {}
     for kind, d in kinds.items():
         name = "slab_expand_kernel" if kind == "fwd" else "slab_expand_backward_kernel"
-        kernels[name] = {"launches": len(d["ms"]), "ms_per_launch": sum(d["ms"]) / len(d["ms"]),
-                         "bytes_per_launch": sum(d["bytes"]) / len(d["ms"]),
+        # a hop runs one launch per destination tile: its time is their sum, its bytes the hop's
+        kernels[name] = {"launches": len(d["ms"]) * d["tiles"], "destination_tiles": d["tiles"],
+                         "ms_per_launch": sum(d["ms"]) / (len(d["ms"]) * d["tiles"]),
+                         "ms_per_hop_mean": sum(d["ms"]) / len(d["ms"]),
+                         "bytes_per_hop_mean": sum(d["bytes"]) / len(d["ms"]),
                          "gbs": sum(d["bytes"]) / (sum(d["ms"]) / 1e3) / 1e9, "ms_per_hop": d["ms"],
                          "bytes_per_hop": d["bytes"],
                          "frac_per_hop": [b / (t / 1e3) / 1e9 / hbm for b, t in zip(d["bytes"], d["ms"])]}
@@ -673,8 +676,8 @@ def slab_extras(a, wl, kg, g, eng, heads, w_hops, scores, flush, B):
     udec()
     torch.cuda.synchronize()
     trace, eng.trace = eng.trace, None
-    hop_ms = [e0.elapsed_time(e1) for _, e0, e1, _ in trace]
-    hop_bytes = [byts for _, _, _, byts in trace]
+    hop_ms = [sum(e0.elapsed_time(e1) for e0, e1 in evs) for _, evs, _ in trace]
+    hop_bytes = [byts for _, _, byts in trace]
     gbs = sum(hop_bytes) / (sum(hop_ms) / 1e3) / 1e9
     out["decode_uncapped"] = {
         "ms": udms, "topk": 100, "edge_cap": "uncapped", "messages": M_dec, "gteps": M_dec / udms / 1e6,

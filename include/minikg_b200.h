@@ -396,9 +396,11 @@ int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, f
  * entity-major (slot (e - lo) * nrows + (row - row0)), and keys come out of mkg_slab_emit in
  * that order: ascending entity, then ascending row ("entity-major order").  A frontier or a
  * key list spanning several row windows is passed whole to each window's call; entries of
- * other rows are skipped (mkg_slab_expand, mkg_slab_expand_backward always; mkg_slab_put and
- * mkg_slab_take with MKG_SLAB_OTHER_ROWS). */
-#define MKG_SLAB_OTHER_ROWS 16
+ * other rows are skipped by mkg_slab_expand and mkg_slab_expand_backward.  A destination range
+ * may also be cut into tiles, each a window of its own with a push list restricted to its
+ * destinations (a tile's updates then stay in L2); mkg_slab_put and mkg_slab_take given
+ * MKG_SLAB_SKIP_OUTSIDE skip the keys outside their window (other rows or other tiles). */
+#define MKG_SLAB_SKIP_OUTSIDE 16
 typedef struct mkg_slab_window {
   int64_t E;       /* entities of the key space */
   int64_t row0;    /* first row (b * L + l, or b for [B, E] keys) of the window */
@@ -438,12 +440,12 @@ int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* workspace
 /* Writes (mode 0), adds with a touched mark (mode 1) or raises to the maximum with a touched
  * mark (mode 2: max_sp_3d's max over rules with row_div = L) values at keys whose row is
  * (key / E) / row_div (row_div = L maps (b, l, e) to the [B, E] key b * E + e: sum_sp_3d,
- * fastlog_bridge.py:17-23).  mode | MKG_SLAB_OTHER_ROWS skips keys of rows outside the
- * window; any other key outside it sets MKG_DEV_BAD_KEY. */
+ * fastlog_bridge.py:17-23).  mode | MKG_SLAB_SKIP_OUTSIDE skips the keys outside the window;
+ * without it such a key (and always a negative one) sets MKG_DEV_BAD_KEY. */
 int mkg_slab_put(const mkg_slab_window* win, void* store, const int64_t* keys, const float* vals, int64_t nnz,
                  int64_t row_div, int32_t mode, unsigned* dev_err, mkg_stream stream);
 /* out[i] = the store's value at keys[i] (row (key / E) / row_div), cleared when clear & 1;
- * out may be NULL (clear only).  clear | MKG_SLAB_OTHER_ROWS skips keys of rows outside the
+ * out may be NULL (clear only).  clear | MKG_SLAB_SKIP_OUTSIDE skips the keys outside the
  * window (their out[i] is left as it was). */
 int mkg_slab_take(const mkg_slab_window* win, void* store, const int64_t* keys, int64_t nnz, int64_t row_div,
                   float* out, int32_t clear, unsigned* dev_err, mkg_stream stream);

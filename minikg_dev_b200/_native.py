@@ -17,7 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libminikg_b200.so"
 
 MKG_OK = 0
 MASK_NONE, MASK_U8, MASK_F32 = 0, 1, 2
-SLAB_OTHER_ROWS = 16  # MKG_SLAB_OTHER_ROWS
+SLAB_SKIP_OUTSIDE = 16  # MKG_SLAB_SKIP_OUTSIDE
 DEV_ERR_NAMES = {1: "frontier entry outside [B, L, E]", 2: "CSR column outside [0, E)",
                  4: "fact id outside [0, T)", 8: "gradient key outside [B, L, E]",
                  16: "relation id outside its range", 32: "a bounded wait inside a kernel gave up",

@@ -87,14 +87,6 @@ __device__ __forceinline__ int64_t slot_of(const Window& w, int64_t key, int64_t
   return w.slot(row, e);
 }
 
-// 1 when the key's row (after row_div) lies outside the window's rows but its entity inside
-// the destination range: a key of another row window
-__device__ __forceinline__ bool other_rows(const Window& w, int64_t key, int64_t row_div) {
-  const int64_t q = w.fe.div(key);
-  const int64_t row = div_rows(q, row_div) - w.row0;
-  const int64_t e = key - q * w.E - w.lo;
-  return (row < 0 || row >= w.nrows) && e >= 0 && e < w.extent;
-}
 
 // Adds (sum) or raises to (max) a slot; returns the slot's previous value.  The max works on
 // the float's bits as an unsigned integer, which orders non-negative floats correctly (the
@@ -372,13 +364,13 @@ constexpr int kMaxBinRows = 2048;  // 16 KB of fp64 row bins per block (gradient
 // ------------------------------------------------------------------ put / take
 __global__ void slab_put_kernel(Store st, Window win, const int64_t* __restrict__ keys, const float* __restrict__ vals,
                                 int64_t nnz, int64_t row_div, int mode, unsigned* err) {
-  const bool skip_other = (mode & MKG_SLAB_OTHER_ROWS) != 0;
+  const bool skip_outside = (mode & MKG_SLAB_SKIP_OUTSIDE) != 0;
   const int op = mode & 3;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nnz; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t k = keys[i];
     const int64_t slot = k < 0 ? -1 : slot_of(win, k, row_div);
     if (slot < 0) {
-      if (!(skip_other && k >= 0 && other_rows(win, k, row_div))) raise_flag(err, MKG_DEV_BAD_KEY);
+      if (!(skip_outside && k >= 0)) raise_flag(err, MKG_DEV_BAD_KEY);
       continue;
     }
     const float v = vals[i];
@@ -388,16 +380,16 @@ __global__ void slab_put_kernel(Store st, Window win, const int64_t* __restrict_
 }
 
 // out (may be NULL) receives the slot values of the keys; keys skipped as another window's
-// (MKG_SLAB_OTHER_ROWS) leave their out entry as it was
+// (MKG_SLAB_SKIP_OUTSIDE) leave their out entry as it was
 __global__ void slab_take_kernel(Store st, Window win, const int64_t* __restrict__ keys, int64_t nnz, int64_t row_div,
                                  float* __restrict__ out, int clear, unsigned* err) {
-  const bool skip_other = (clear & MKG_SLAB_OTHER_ROWS) != 0;
+  const bool skip_outside = (clear & MKG_SLAB_SKIP_OUTSIDE) != 0;
   const bool zero = (clear & 1) != 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nnz; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t k = keys[i];
     const int64_t slot = k < 0 ? -1 : slot_of(win, k, row_div);
     if (slot < 0) {
-      if (skip_other && k >= 0 && other_rows(win, k, row_div)) continue;
+      if (skip_outside && k >= 0) continue;
       raise_flag(err, MKG_DEV_BAD_KEY);
       if (out) out[i] = 0.0f;
       continue;
@@ -811,8 +803,8 @@ MKG_API int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* w
 MKG_API int mkg_slab_put(const mkg_slab_window* win, void* store, const int64_t* keys, const float* vals, int64_t nnz,
                          int64_t row_div, int32_t mode, unsigned* dev_err, mkg_stream stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  MKG_REQUIRE(window_ok(win) && store && row_div >= 1 && (mode & ~MKG_SLAB_OTHER_ROWS) >= 0 &&
-                  (mode & ~MKG_SLAB_OTHER_ROWS) <= 2 && nnz >= 0,
+  MKG_REQUIRE(window_ok(win) && store && row_div >= 1 && (mode & ~MKG_SLAB_SKIP_OUTSIDE) >= 0 &&
+                  (mode & ~MKG_SLAB_SKIP_OUTSIDE) <= 2 && nnz >= 0,
               "slab_put: bad argument");
   if (nnz == 0) return MKG_OK;
   MKG_REQUIRE(keys && vals, "slab_put: null argument");

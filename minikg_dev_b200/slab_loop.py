@@ -41,17 +41,43 @@ from . import _native as N
 from .graph import DeviceGraph
 
 STORE_FRACTION = 0.45   # at most this share of the free device memory for the slab store
+# destinations per tile (a tile's touched sectors stay in the 126 MB L2): measured on the
+# 4.6 M-entity step, 1 / 2 / 4 / 8 tiles gave 10.94 / 10.34 / 10.04 / 10.49 ms
+TILE_ENTITIES = 1_200_000
+
+
+def _restrict(full_ptr, full_push, full_degree, lo: int, hi: int, E: int):
+    """(ptr [E + 1] int32, records, positions in the full list) of the push records whose
+    destination lies in [lo, hi)."""
+    dev = full_push.device
+    nbr = full_push[:, 0]
+    sel = torch.nonzero((nbr >= lo) & (nbr < hi), as_tuple=True)[0]
+    push = full_push[sel].contiguous()
+    rows = torch.repeat_interleave(torch.arange(E, device=dev), full_degree)
+    cnt = torch.bincount(rows[sel], minlength=E)
+    ptr = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+    ptr[1:] = torch.cumsum(cnt, 0).to(torch.int32)
+    return ptr, push, sel
 
 
 class SlabEngine:
     """Resident state of the key-slab loop on one GPU: the push list (the graph's, or only the
-    records whose destination lies in ``[lo, hi)``), a zero-kept slab store and its window size.
+    records whose destination lies in ``[lo, hi)``), cut into destination *tiles*, a zero-kept
+    slab store and its window size.
+
+    A tile is a sub-range of the destinations with its own push list (the records that reach
+    it): a hop's expansion (and its backward walk) is one launch per tile, each touching only
+    its tile's part of the entity-major store, whose sectors then stay in L2 (a whole 4.6
+    M-entity range's touched sectors do not: every message then fetched and wrote back its
+    sector); the collect, the gradient's put and the clearing run once over the whole window.
+    ``dst_tiles`` (default: one per ``TILE_ENTITIES`` destinations) sets their number.
 
     ``store_bytes`` caps the store (default: ``STORE_FRACTION`` of the free memory when first
-    sized); a window then covers as many (b, l) rows of the destination range as fit, and a
-    hop whose rows exceed it runs window by window."""
+    sized); a window then covers as many (b, l) rows of the destination range as fit, and a hop
+    whose rows exceed it runs window by window."""
 
-    def __init__(self, graph: DeviceGraph, lo: int = 0, hi: int = 0, store_bytes: int | None = None):
+    def __init__(self, graph: DeviceGraph, lo: int = 0, hi: int = 0, store_bytes: int | None = None,
+                 dst_tiles: int | None = None):
         self.g = graph
         self.dev = graph.device
         E = graph.num_entities
@@ -62,18 +88,23 @@ class SlabEngine:
         self.full_ptr = keep["push_ptr"]
         self.full_push = keep["push"]
         self.full_degree = (self.full_ptr[1:] - self.full_ptr[:-1]).to(torch.int64)
-        if self.lo == 0 and self.hi == E:
-            self.ptr, self.push, self.sel = self.full_ptr, self.full_push, None
+        nt = int(dst_tiles) if dst_tiles else max(1, -(-self.extent // TILE_ENTITIES))
+        nt = max(1, min(nt, self.extent))
+        edges = [self.lo + (self.extent * t) // nt for t in range(nt + 1)]
+        # tiles: (lo, extent, ptr, push); a single tile over the whole graph shares its lists
+        self.tiles = []
+        if nt == 1 and self.lo == 0 and self.hi == E:
+            self.tiles.append((0, E, self.full_ptr, self.full_push))
+            self.ptr, self._shared = self.full_ptr, True
         else:
-            nbr = self.full_push[:, 0]
-            mine = (nbr >= self.lo) & (nbr < self.hi)
-            self.sel = torch.nonzero(mine, as_tuple=True)[0]
-            self.push = self.full_push[self.sel].contiguous()
-            rows = torch.repeat_interleave(torch.arange(E, device=self.dev), self.full_degree)
-            cnt = torch.bincount(rows[self.sel], minlength=E)
+            for t in range(nt):
+                ptr_t, push_t, _ = _restrict(self.full_ptr, self.full_push, self.full_degree, edges[t], edges[t + 1], E)
+                self.tiles.append((edges[t], edges[t + 1] - edges[t], ptr_t, push_t))
+            # the engine's whole-range degrees (for byte accounting)
             self.ptr = torch.zeros(E + 1, dtype=torch.int32, device=self.dev)
-            self.ptr[1:] = torch.cumsum(cnt, 0).to(torch.int32)
-            del rows, cnt, mine, nbr
+            for _, _, ptr_t, _ in self.tiles:
+                self.ptr += ptr_t
+            self._shared = False
         self._store_cap = store_bytes
         self._budget_bound = False
         self.store = None
@@ -85,18 +116,20 @@ class SlabEngine:
 
     @property
     def records(self) -> int:
-        return int(self.push.shape[0])
+        return sum(int(push.shape[0]) for _, _, _, push in self.tiles)
 
     def set_edge_factor(self, mask, weight, is_score: bool, scale: float) -> None:
         """Rewrites the factor field of this engine's push records from the mask / edge scores
-        (a rank-local list: only its own records)."""
-        if self.sel is None:
+        (tile lists: each holds copies of its records)."""
+        if self._shared:
             self.g.set_edge_factor(mask, weight, is_score, scale, push_only=True)
             return
         keep = []
         f = N.edge_factor(mask, weight, is_score, scale, keep)
-        N.check(N.load().mkg_records_set_factor(self.push.data_ptr(), self.records, self.g.num_facts,
-                                                ctypes.byref(f), N.stream_handle(self.dev)), "records_set_factor")
+        for _, _, _, push in self.tiles:
+            N.check(N.load().mkg_records_set_factor(push.data_ptr(), int(push.shape[0]), self.g.num_facts,
+                                                    ctypes.byref(f), N.stream_handle(self.dev)),
+                    "records_set_factor")
         self.g.factor_writes += 1
 
     def ensure_store(self, rows: int) -> None:
@@ -135,18 +168,16 @@ def entity_major(keys: torch.Tensor, vals: torch.Tensor, E: int, BL: int):
     return keys[order], vals[order]
 
 
-def _other_rows(bounds) -> int:
-    """The put / take flag that skips keys of other row windows (several windows only: with one
-    window every key must lie in it)."""
-    return N.SLAB_OTHER_ROWS if len(bounds) > 1 else 0
-
-
 def _events(eng: SlabEngine):
     if eng.trace is None:
         return None
     ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     ev[0].record()
     return ev
+
+
+def _in_rows(x, E: int, r0: int, nr: int, whole: bool):
+    return x if whole else x[((x // E) >= r0) & ((x // E) < r0 + nr)]
 
 
 def _collect(eng: SlabEngine, win):
@@ -186,10 +217,11 @@ def graph_bytes(eng: SlabEngine, keys) -> int:
 def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True, agg_mode: int = 0):
     """One hop's concat-summed output over the engine's destinations: (keys in entity-major order
     within each row window, windows in row order; values; fp64 row sums [BL], zeros for
-    ``agg_mode`` 1, which keeps each key's largest message instead).  The frontier may come in
-    any order (entity-major keeps neighbouring atomics in the same sectors).  ``check``: refuse
-    frontier keys outside [B, L, E] on the host (the loop, whose keys are its own outputs,
-    skips that synchronisation)."""
+    ``agg_mode`` 1, which keeps each key's largest message instead; the output's [a, b) part of
+    every row window, in window order).  The frontier may come in any order
+    (entity-major keeps neighbouring atomics in the same sectors).  ``check``: refuse frontier
+    keys outside [B, L, E] on the host (the loop, whose keys are its own outputs, skips that
+    synchronisation)."""
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
@@ -205,80 +237,91 @@ def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True
     err = N.error_word(dev).data_ptr()
     nk = int(keys.numel())
     if nk == 0:
-        return (torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev), d)
+        return (torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev), d,
+                [(0, 0)] * len(bounds))
     k = keys.contiguous()
     v = vals.detach().to(torch.float32).contiguous()
     ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk), dev)
+    parts, pos = [], 0
     for r0, nr in bounds:  # every window takes the whole frontier and walks the entries of its rows
+        rs = d[r0:r0 + nr].data_ptr() if agg_mode == 0 else None  # the expansions add their row sums
         win = eng.window(r0, nr)
-        ev = _events(eng)
-        rs = d[r0:r0 + nr].data_ptr() if agg_mode == 0 else None  # the expansion adds its row sums
-        N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), nk,
-                                    wf.data_ptr(), n, 1, int(agg_mode), ctypes.byref(win), eng.store.data_ptr(), rs,
-                                    ws.data_ptr(), ws.numel(), err, st), "slab_expand")
-        if ev is not None:
-            ev[1].record()
+        evs = []
+        for t, (_, _, ptr_t, push_t) in enumerate(eng.tiles):  # one launch per destination tile
+            ev = _events(eng)  # (the same window; the first tile's launch adds the identity messages)
+            N.check(lib.mkg_slab_expand(ptr_t.data_ptr(), push_t.data_ptr(), k.data_ptr(), v.data_ptr(), nk,
+                                        wf.data_ptr(), n, int(t == 0), int(agg_mode), ctypes.byref(win),
+                                        eng.store.data_ptr(), rs, ws.data_ptr(), ws.numel(), err, st), "slab_expand")
+            if ev is not None:
+                ev[1].record()
+                evs.append(ev)
         ko, vo = _collect(eng, win)
-        if ev is not None:  # frontier in + output out (12 B per key: 8 B key, 4 B value), rule weights
-            mine = k[((k // E) >= r0) & ((k // E) < r0 + nr)] if len(bounds) > 1 else k
-            eng.trace.append(("fwd", ev[0], ev[1], graph_bytes(eng, mine) + 12 * int(mine.numel())
-                              + 12 * ko.numel() + nr * n * 4))
         out_k.append(ko)
         out_v.append(vo)
+        parts.append((pos, pos + int(ko.numel())))
+        pos += int(ko.numel())
+        if evs:  # one hop of this window: frontier in + output out (12 B per key: 8 B key, 4 B
+            # value), rule weights; its time is the sum over the tiles' expansions
+            mine = _in_rows(k, E, r0, nr, len(bounds) == 1)
+            eng.trace.append(("fwd", evs, graph_bytes(eng, mine) + 12 * int(mine.numel()) + 12 * int(ko.numel())
+                              + nr * n * 4))
     if len(out_k) == 1:
-        return out_k[0], out_v[0], d
-    return torch.cat(out_k), torch.cat(out_v), d
+        return out_k[0], out_v[0], d, parts
+    return torch.cat(out_k), torch.cat(out_v), d, parts
 
 
-def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, gy, factor, grad_w64, grad_edge):
+def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, parts, put_grad, factor, grad_w64,
+                    grad_edge):
     """Transposed walk of one hop: the frontier entries' fp64 gradient; adds to ``grad_w64``
-    ([BL, n], fp64) and ``grad_edge`` ([T], fp32).  ``gy`` None: the output gradient is
-    already in the store (``_mass_normalize_grad`` with the engine; one window)."""
+    ([BL, n], fp64) and ``grad_edge`` ([T], fp32).  The hop's output ``keys_y`` came from the
+    forward in the row-window parts ``parts``; ``put_grad(win, a, b)`` writes the output
+    gradient of ``keys_y[a:b]`` into the store's window ``win`` before the window's walks (one
+    per destination tile), which clears those keys after them."""
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
     n = int(w_h.shape[-1])
     wf = w_h.detach().to(torch.float32).reshape(BL, n).contiguous()
     bounds = list(_windows(BL, eng.rows_per_window))
-    if gy is None and len(bounds) != 1:
-        raise ValueError("expand_backward: a gradient already in the store needs a one-window store")
-    other = _other_rows(bounds)
-    nk, ny = int(keys.numel()), int(keys_y.numel())
+    if len(parts) != len(bounds):
+        raise RuntimeError("expand_backward: the store's windows changed since the forward")
+    nk = int(keys.numel())
     gsp = torch.zeros(nk, dtype=torch.float64, device=dev)
+    if nk == 0:
+        return gsp
     st = N.stream_handle(dev)
     err = N.error_word(dev).data_ptr()
     ky = keys_y.contiguous()
-    if nk == 0:
-        if gy is None and ny:  # leave the store zeroed
-            N.check(lib.mkg_slab_take(ctypes.byref(eng.window(0, BL)), eng.store.data_ptr(), ky.data_ptr(), ny, 1,
-                                      None, 1, err, st), "slab_take")
-        return gsp
-    gyf = gy.to(torch.float32).contiguous() if gy is not None else None
     k = keys.contiguous()
     v = vals.detach().to(torch.float32).contiguous()
     ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk), dev)
-    for r0, nr in bounds:  # every window takes the whole frontier and walks the entries of its rows
+    for (r0, nr), (a, b) in zip(bounds, parts):  # every window takes the whole frontier
         win = eng.window(r0, nr)
-        if ny and gyf is not None:
-            N.check(lib.mkg_slab_put(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), gyf.data_ptr(), ny, 1,
-                                     other, err, st), "slab_put")
-        ev = _events(eng)
-        N.check(lib.mkg_slab_expand_backward(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                             nk, wf.data_ptr(), n, 1, ctypes.byref(win), eng.store.data_ptr(),
-                                             ctypes.byref(factor), eng.g.num_facts, gsp.data_ptr(),
-                                             grad_w64.data_ptr(), N.ptr(grad_edge), ws.data_ptr(), ws.numel(), err,
-                                             st), "slab_expand_backward")
-        if ev is not None:  # grad-in at the outputs, frontier re-read, grad-out, weights, edge grads
-            ev[1].record()  # (4 B per edge-score gradient touched: at most one per message, at most T)
-            inw = lambda x: x[((x // E) >= r0) & ((x // E) < r0 + nr)] if len(bounds) > 1 else x  # noqa: E731
-            mine, mine_y = inw(k), inw(ky)
+        if b > a:
+            put_grad(win, a, b)
+        evs = []
+        for t, (_, _, ptr_t, push_t) in enumerate(eng.tiles):  # one walk per destination tile
+            ev = _events(eng)  # (the first tile's walk takes the identity messages)
+            N.check(lib.mkg_slab_expand_backward(ptr_t.data_ptr(), push_t.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                 nk, wf.data_ptr(), n, int(t == 0), ctypes.byref(win),
+                                                 eng.store.data_ptr(),
+                                                 ctypes.byref(factor), eng.g.num_facts, gsp.data_ptr(),
+                                                 grad_w64.data_ptr(), N.ptr(grad_edge), ws.data_ptr(), ws.numel(),
+                                                 err, st), "slab_expand_backward")
+            if ev is not None:
+                ev[1].record()
+                evs.append(ev)
+        if b > a:
+            N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ky[a:b].data_ptr(), b - a, 1, None, 1,
+                                      err, st), "slab_take")
+        if evs:  # grad-in at the outputs, frontier re-read, grad-out, weights, edge grads (4 B per
+            # edge-score gradient touched: at most one per message, at most T); time summed over tiles
+            whole = len(bounds) == 1
+            mine, mine_y = _in_rows(k, E, r0, nr, whole), _in_rows(ky, E, r0, nr, whole)
             local_deg = (eng.ptr[1:] - eng.ptr[:-1]).to(torch.int64)
             touched = min(eng.g.num_facts, int(local_deg[mine % E].sum())) if grad_edge is not None else 0
-            eng.trace.append(("bwd", ev[0], ev[1], graph_bytes(eng, mine) + 12 * int(mine_y.numel())
+            eng.trace.append(("bwd", evs, graph_bytes(eng, mine) + 12 * int(mine_y.numel())
                               + 16 * int(mine.numel()) + nr * n * 4 + 4 * touched))
-        if ny:
-            N.check(lib.mkg_slab_take(ctypes.byref(win), eng.store.data_ptr(), ky.data_ptr(), ny, 1, None,
-                                      1 | other, err, st), "slab_take")
     return gsp
 
 
@@ -333,26 +376,42 @@ def _mass_normalize(keys, y, E: int, BL: int, d32, threshold: float):
     return x, int(dropped.item())
 
 
-def _mass_normalize_grad(keys, y, gx, E: int, BL: int, d32, spec, eng: SlabEngine | None = None):
-    """Gradient of the mass normalisation at its input: row sums of both terms in fp64
-    (all-reduced over ranks), then the per-entry gradient.  With ``eng`` (a store whose one
-    window holds every row) the gradient is written straight into the store at the keys'
-    slots, ready for ``expand_backward(..., gy=None)``, and None is returned."""
+def _mass_normalize_grad_sums(keys, y, gx, E: int, BL: int, d32, spec):
+    """Row sums of both terms of the mass normalisation's gradient, fp64 [2, BL], all-reduced
+    over ranks."""
     lib = N.load()
     dev = y.device
     sums = torch.zeros((2, BL), dtype=torch.float64, device=dev)
+    N.check(lib.mkg_mass_normalize_grad_sums(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), int(y.numel()), E, 0, BL,
+                                             d32.data_ptr(), sums.data_ptr(), N.error_word(dev).data_ptr(),
+                                             N.stream_handle(dev)), "mass_normalize_grad_sums")
+    return _all_reduce(sums, spec)
+
+
+def _grad_putter(eng: SlabEngine, keys, y, gx, BL: int, d32, sums):
+    """``put_grad(win, a, b)`` for ``expand_backward``: the normalisation's gradient of entries
+    [a, b) written straight into the store's window (``mkg_mass_normalize_grad_put``)."""
+    lib = N.load()
+    dev = y.device
+    E = eng.g.num_entities
+    k, yy, g = keys.contiguous(), y.contiguous(), gx.contiguous()
+
+    def put(win, a: int, b: int):
+        N.check(lib.mkg_mass_normalize_grad_put(k[a:b].data_ptr(), yy[a:b].data_ptr(), g[a:b].data_ptr(), b - a, E, 0,
+                                                BL, d32.data_ptr(), sums.data_ptr(), ctypes.byref(win),
+                                                eng.store.data_ptr(), N.error_word(dev).data_ptr(),
+                                                N.stream_handle(dev)), "mass_normalize_grad_put")
+    return put
+
+
+def _mass_normalize_grad(keys, y, gx, E: int, BL: int, d32, spec):
+    """Gradient of the mass normalisation at its input: row sums of both terms in fp64
+    (all-reduced over ranks), then the per-entry gradient."""
+    lib = N.load()
+    dev = y.device
     n = int(y.numel())
     st = N.stream_handle(dev)
-    err = N.error_word(dev).data_ptr()
-    N.check(lib.mkg_mass_normalize_grad_sums(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL,
-                                             d32.data_ptr(), sums.data_ptr(), err, st), "mass_normalize_grad_sums")
-    _all_reduce(sums, spec)
-    if eng is not None:
-        win = eng.window(0, BL)
-        N.check(lib.mkg_mass_normalize_grad_put(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL,
-                                                d32.data_ptr(), sums.data_ptr(), ctypes.byref(win),
-                                                eng.store.data_ptr(), err, st), "mass_normalize_grad_put")
-        return None
+    sums = _mass_normalize_grad_sums(keys, y, gx, E, BL, d32, spec)
     gy = torch.empty_like(y)
     N.check(lib.mkg_mass_normalize_grad(keys.data_ptr(), y.data_ptr(), gx.data_ptr(), n, E, 0, BL, d32.data_ptr(),
                                         sums.data_ptr(), gy.data_ptr(), st), "mass_normalize_grad")
@@ -361,7 +420,7 @@ def _mass_normalize_grad(keys, y, gx, E: int, BL: int, d32, spec, eng: SlabEngin
 
 # ----------------------------------------------------------------------------- the loop
 class _Hop:
-    __slots__ = ("keys_in", "vals_in", "n_own", "offset", "prune_sel", "n_pre", "keys_y", "y", "d", "keep")
+    __slots__ = ("keys_in", "vals_in", "n_own", "offset", "prune_sel", "n_pre", "keys_y", "y", "d", "keep", "parts")
 
 
 def _all_reduce(t, spec):
@@ -429,7 +488,7 @@ class SlabHopLoop(autograd.Function):
             k_all, v_all, st.prune_sel = _prune(k_all, v_all, E, int(topk_nodes))
             st.keys_in, st.vals_in = k_all, v_all
             msgs.append(eng.full_degree[k_all % E].sum())
-            ky, y, d = expand_forward(eng, k_all, v_all, wf[h], BL, check=False)
+            ky, y, d, st.parts = expand_forward(eng, k_all, v_all, wf[h], BL, check=False)
             _all_reduce(d, spec)
             d32 = d.to(torch.float32)
             x = _mass_normalize(ky, y, E, BL, d32, threshold)
@@ -483,10 +542,10 @@ class SlabHopLoop(autograd.Function):
             else:
                 gx = torch.zeros_like(st.y)
                 gx[st.keep] = g_state
-            one_window = eng.store is not None and eng.rows_per_window >= BL
-            gy = _mass_normalize_grad(st.keys_y, st.y, gx, E, BL, st.d, spec, eng if one_window else None)
-            gsp = expand_backward(eng, st.keys_in, st.vals_in, ctx.wf[h], BL, st.keys_y, gy, factor, grad_w64[h],
-                                  grad_edge)
+            sums = _mass_normalize_grad_sums(st.keys_y, st.y, gx, E, BL, st.d, spec)
+            put = _grad_putter(eng, st.keys_y, st.y, gx, BL, st.d, sums)
+            gsp = expand_backward(eng, st.keys_in, st.vals_in, ctx.wf[h], BL, st.keys_y, st.parts, put, factor,
+                                  grad_w64[h], grad_edge)
             if st.prune_sel is not None:  # back to the frontier before the prune
                 full = torch.zeros(st.n_pre, dtype=gsp.dtype, device=dev)
                 full[st.prune_sel] = gsp
@@ -561,7 +620,7 @@ def slab_decode_max(engine: SlabEngine, heads: torch.Tensor, w_hops: torch.Tenso
     for h in range(K):
         if msgs_out is not None:
             msgs_out.append(eng.full_degree[keys % E].sum())
-        ky, y, _ = expand_forward(eng, keys, vals, wf[h], BL, check=False, agg_mode=1)
+        ky, y, _, _ = expand_forward(eng, keys, vals, wf[h], BL, check=False, agg_mode=1)
         rows = ky // E
         # each row's entries in ascending entity order (a stable sort by row of the
         # entity-major list), summed one by one in that order

@@ -111,6 +111,39 @@ def test_slab_loop_row_windows_match_one_window():
     np.testing.assert_allclose(ge2.cpu().numpy(), ge1.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
+@pytest.mark.parametrize("tiles,store_rows", [(3, 0), (4, 4)])
+def test_slab_loop_destination_tiles_match_one_tile(tiles, store_rows):
+    """Destination tiles (each its own push list and store pass), alone and with row windows:
+    the same keys, values, message counts and gradients as one tile, and the oracle's."""
+    from minikg_dev_b200 import _native as N
+    from minikg_dev_b200.slab_loop import slab_proof_scores
+    h, r, t, E, R, heads, w_hops, scores, mask = _case("hubby", 9, 3, 3, 41)
+    res = []
+    for kw in ({}, {"dst_tiles": tiles, **({"store_bytes": int(N.load().mkg_slab_store_bytes(store_rows * E))}
+                                           if store_rows else {})}):
+        csr, eng = _engine(h, r, t, E, R, **kw)
+        wt = T(w_hops).requires_grad_(True)
+        sc = T(scores).requires_grad_(True)
+        out, msgs = slab_proof_scores(eng, T(heads), wt, sc)
+        out = out.coalesce()
+        (out.values() * torch.linspace(-1, 1, out.values().numel(), device=DEV)).sum().backward()
+        res.append((out.indices(), out.values().detach(), msgs, wt.grad, sc.grad, len(eng.tiles)))
+        assert _store_is_zero(eng)
+    (i1, v1, m1, gw1, ge1, n1), (i2, v2, m2, gw2, ge2, n2) = res
+    assert n1 == 1 and n2 == tiles
+    assert torch.equal(i1, i2) and torch.equal(m1, m2)
+    np.testing.assert_allclose(v2.cpu().numpy(), v1.cpu().numpy(), rtol=RTOL, atol=ATOL)
+    final, _ = O.proof_sum_forward(heads, w_hops, csr, mask, scores, 9, 3, E, R)
+    idx = i2.cpu().numpy()
+    np.testing.assert_array_equal(idx[0] * E + idx[1], final[0])
+    np.testing.assert_allclose(v2.cpu().numpy(), final[1], rtol=RTOL, atol=ATOL)
+    seed = np.linspace(-1, 1, final[0].shape[0]).astype(np.float32)
+    gw, ge = exact_loop_grads(heads, w_hops, csr, mask, scores, 9, 3, E, R, final[0], seed, num_facts=h.shape[0])
+    for gwx, gex in ((gw1, ge1), (gw2, ge2)):  # both against the float64 run (not one against the other)
+        np.testing.assert_allclose(gwx.cpu().numpy(), gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+        np.testing.assert_allclose(gex.cpu().numpy(), ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+
+
 def test_slab_hop_destination_ranges_add_up():
     """Engines holding only the push records of one destination range each: their hop outputs
     partition the whole-range output, and their row sums add up to its row sums."""
@@ -123,7 +156,7 @@ def test_slab_hop_destination_ranges_add_up():
     rng = np.random.default_rng(3)
     keys = np.unique(rng.integers(0, B * L * E, 400))
     vals = rng.uniform(0.01, 1.0, keys.shape[0]).astype(np.float32)
-    kf, vf, df = expand_forward(full, T(keys), T(vals), T(w_hops[0]), B * L)
+    kf, vf, df, _ = expand_forward(full, T(keys), T(vals), T(w_hops[0]), B * L)
     # entity-major output: ascending entity, then row
     em = ((kf % E) * (B * L) + kf // E).cpu().numpy()
     assert (np.diff(em) > 0).all()
@@ -135,7 +168,7 @@ def test_slab_hop_destination_ranges_add_up():
     for k in range(3):
         eng = SlabEngine(full.g, bounds[k], bounds[k + 1])
         eng.set_edge_factor(None, T(scores), True, 1.0)
-        kk, vv, dd = expand_forward(eng, T(keys), T(vals), T(w_hops[0]), B * L)
+        kk, vv, dd, _ = expand_forward(eng, T(keys), T(vals), T(w_hops[0]), B * L)
         e = (kk % E).cpu().numpy()
         assert ((e >= bounds[k]) & (e < bounds[k + 1])).all()
         ks.append(kk)
@@ -176,7 +209,8 @@ def test_slab_bad_frontier_entity_is_reported():
     def expand(win, k):
         v = T(np.ones(k.numel(), np.float32))
         ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(k.numel()), DEV)
-        N.check(lib.mkg_slab_expand(eng.ptr.data_ptr(), eng.push.data_ptr(), k.data_ptr(), v.data_ptr(), k.numel(),
+        _, _, ptr0, push0 = eng.tiles[0]
+        N.check(lib.mkg_slab_expand(ptr0.data_ptr(), push0.data_ptr(), k.data_ptr(), v.data_ptr(), k.numel(),
                                     wf.data_ptr(), wf.shape[1], 1, 0, ctypes.byref(win), eng.store.data_ptr(), None,
                                     ws.data_ptr(), ws.numel(), N.error_word(DEV).data_ptr(), N.stream_handle(DEV)),
                 "slab_expand")
@@ -194,14 +228,16 @@ def test_slab_bad_frontier_entity_is_reported():
     assert _store_is_zero(eng)
 
 
-@pytest.mark.parametrize("gname,B,L,K,store_rows", [("hubby", 9, 3, 3, 0), ("g2", 6, 3, 3, 0), ("hubby", 9, 3, 2, 4)])
-def test_slab_decode_max_bit_exact(gname, B, L, K, store_rows):
-    """The uncapped max-aggregation decode on the key-slab store (also window by window):
-    raw scores, tails and bounded scores bit-exact against the oracle."""
+@pytest.mark.parametrize("gname,B,L,K,store_rows,tiles", [("hubby", 9, 3, 3, 0, 1), ("g2", 6, 3, 3, 0, 1),
+                                                          ("hubby", 9, 3, 2, 4, 1), ("hubby", 9, 3, 3, 0, 3)])
+def test_slab_decode_max_bit_exact(gname, B, L, K, store_rows, tiles):
+    """The uncapped max-aggregation decode on the key-slab store (also window by window, and
+    tile by tile): raw scores, tails and bounded scores bit-exact against the oracle."""
     from minikg_dev_b200 import _native as N
     from minikg_dev_b200.slab_loop import slab_decode_max
     h, r, t, E, R, heads, w_hops, scores, mask = _case(gname, B, L, K, 31 + B)
     kw = {"store_bytes": int(N.load().mkg_slab_store_bytes(store_rows * E))} if store_rows else {}
+    kw["dst_tiles"] = tiles
     csr, eng = _engine(h, r, t, E, R, **kw)
     keys, raw, tails, sc, counts = slab_decode_max(eng, T(heads), T(w_hops), 20, T(scores))
     final, _ = O.proof_max_forward(heads, w_hops, csr, mask, scores, B, L, E, R)
