@@ -436,10 +436,19 @@ def _gather(keys, vals, spec):
     this rank's offset in the concatenation, or None)."""
     if spec is None or spec.world == 1:
         return keys, vals, None
-    from .sharded import _all_gather_padded, _gather_counts
+    import torch.distributed as dist
+    from .sharded import _gather_counts
     counts = _gather_counts(int(keys.numel()), keys.device, spec.group)
-    k_all = torch.cat(_all_gather_padded(keys, counts, spec.group))
-    v_all = torch.cat(_all_gather_padded(vals.detach(), counts, spec.group))
+    # keys and the values' fp32 bits in one [m, 2] int64 payload: one collective per hop
+    m = max(max(counts), 1)
+    pad = torch.zeros((m, 2), dtype=torch.int64, device=keys.device)
+    pad[: keys.numel(), 0] = keys
+    pad[: keys.numel(), 1] = vals.detach().to(torch.float32).contiguous().view(torch.int32).to(torch.int64)
+    out = torch.empty((spec.world * m, 2), dtype=torch.int64, device=keys.device)
+    dist.all_gather_into_tensor(out, pad, group=spec.group)
+    rows = torch.cat([out[r * m: r * m + c] for r, c in enumerate(counts)])
+    k_all = rows[:, 0].contiguous()
+    v_all = rows[:, 1].to(torch.int32).view(torch.float32)
     return k_all, v_all, sum(counts[: spec.rank])
 
 

@@ -219,3 +219,40 @@ def test_sharded_loop_reports_rank_failures(mode):
     assert res[0] != "no error"
     if mode == "size":
         assert "invalid frontier size" in res[0] and "invalid frontier size" in res[1]
+
+
+# ----------------------------------------------------------------------------- slab frontier gather
+def _gather_worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from minikg_dev_b200.sharded import ShardSpec
+        from minikg_dev_b200.slab_loop import _gather
+        n = [3, 0, 5][rank]  # ragged, one rank empty
+        keys = torch.arange(n, dtype=torch.int64) + 100 * rank
+        vals = torch.tensor([-0.0, 1e-30, 3.5, float("inf"), 2.0 ** -126][:n], dtype=torch.float32) + 0.25 * rank
+        k_all, v_all, off = _gather(keys, vals, ShardSpec(rank, world, [0, 10, 20, 30]))
+        out_q.put((rank, k_all.numpy(), v_all.numpy().view(np.int32), off, vals.numpy().view(np.int32)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_slab_frontier_gather_packs_keys_and_value_bits():
+    """slab_loop._gather: one all-gather of [keys, fp32 bits] rows; every rank receives the
+    ranks' lists concatenated in rank order, the values bit for bit, and its own offset."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=120) for _ in range(3)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want_k = np.concatenate([np.arange([3, 0, 5][r]) + 100 * r for r in range(3)])
+    want_v = np.concatenate([x[4] for x in res])
+    for rank, k_all, v_bits, off, _ in res:
+        np.testing.assert_array_equal(k_all, want_k)
+        np.testing.assert_array_equal(v_bits, want_v)
+        assert off == [0, 3, 3][rank]
