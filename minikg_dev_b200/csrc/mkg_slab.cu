@@ -436,8 +436,8 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_backward_kernel(
     if (k == 0 && lane == 0 && a.identity && s >= a.win.lo && s < a.win.lo + a.win.extent) {
       const float g = gstore[a.win.slot(lrow, s - a.win.lo)];
       if (g != 0.0f) {
-        gsp += (double)(g * wrow[a.n - 1]);
-        atomicAdd(gwrow + (a.n - 1), (double)(g * x));
+        gsp += (double)g * (double)wrow[a.n - 1];
+        atomicAdd(gwrow + (a.n - 1), (double)g * (double)x);
       }
     }
     const int64_t rb = a.push_ptr[s] + k * kChunkRecs;
@@ -469,12 +469,14 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_backward_kernel(
       const bool live = lv[u];
       const float g = gl[u];
       const float m = __int_as_float(rec[u].w);
-      const float gm = g * m;
       const float wv = wl[u];
-      float part = 0.0f;
-      if (live && gm != 0.0f) {
-        gsp += (double)(gm * wv);
-        part = gm * x;
+      // the products in fp64 (each exact): the rule-weight and entry gradients are sums whose
+      // terms cancel, where fp32-rounded terms drifted past 1e-5 of the result
+      const double gm = (double)g * (double)m;
+      double dp = 0.0;
+      if (live && gm != 0.0) {
+        gsp += gm * (double)wv;
+        dp = gm * (double)x;
       }
       if (live && g != 0.0f && grad_edge != nullptr) {
         const int f = rec[u].z;
@@ -487,8 +489,7 @@ __global__ void __launch_bounds__(kExpandThreads) slab_expand_backward_kernel(
       }
       // grad_w: records come grouped by channel, so a warp adds one fp64 partial per channel run
       if (!live) ch = -1;
-      double dp = (double)part;
-      const unsigned any = __ballot_sync(0xffffffffu, part != 0.0f);
+      const unsigned any = __ballot_sync(0xffffffffu, dp != 0.0);
       if (any) {
         const int prev = __shfl_up_sync(0xffffffffu, ch, 1);
         const bool head = lane == 0 || prev != ch;
@@ -605,8 +606,9 @@ __global__ void __launch_bounds__(kTileThreads) mass_norm_grad_sums_kernel(
     const float g = gx[i];
     const float q = __fdiv_rn(yv, dr);
     const float gq = g * fminf(dr, 1.0f);
-    const double a0 = (double)(g * q);
-    const double a1 = (double)__fdiv_rn(-(gq * yv), dr * dr);
+    // the terms in fp64: the row sums cancel
+    const double a0 = (double)g * (double)q;
+    const double a1 = -((double)gq * (double)yv) / ((double)dr * (double)dr);
     if (binned) {
       atomicAdd(&bins[0][r], a0);
       atomicAdd(&bins[1][r], a1);

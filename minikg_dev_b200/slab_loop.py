@@ -633,8 +633,9 @@ def slab_decode_max(engine: SlabEngine, heads: torch.Tensor, w_hops: torch.Tenso
         rows = ky // E
         # each row's entries in ascending entity order (a stable sort by row of the
         # entity-major list), summed one by one in that order
-        by_row = torch.sort(rows, stable=True)
-        seg = torch.searchsorted(by_row.values, torch.arange(BL + 1, device=dev, dtype=rows.dtype))
+        # (rows fit 16 bits for up to 32,767 (b, l) rows: a two-pass radix sort)
+        by_row = torch.sort(rows.to(torch.int16) if BL <= 32767 else rows, stable=True)
+        seg = torch.searchsorted(by_row.values.to(torch.int64), torch.arange(BL + 1, device=dev, dtype=torch.int64))
         d = N.segment_sum(seg, y[by_row.indices], ordered=True).clamp(min=1e-7)
         x = y / d[rows]
         keep = torch.nonzero(x != 0, as_tuple=True)[0]
