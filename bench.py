@@ -549,10 +549,11 @@ def run_slab(a, wl, kg, rank, world, local_rank):
     torch.cuda.synchronize()
     trace, eng.trace = eng.trace, None
     kinds = {}
-    for kind, evs, byts in trace:  # one entry per hop: its destination tiles' launches
-        d = kinds.setdefault(kind, {"ms": [], "bytes": [], "tiles": len(evs)})
+    for kind, evs, byts, tiles in trace:  # one entry per hop: its launches (groups of tiles)
+        d = kinds.setdefault(kind, {"ms": [], "bytes": [], "tiles": tiles, "launches": 0})
         d["ms"].append(sum(e0.elapsed_time(e1) for e0, e1 in evs))
         d["bytes"].append(byts)
+        d["launches"] += len(evs)
 
     # end to end through the public API (slab_proof_scores): the batch's query heads and rule
     # weights copied host -> device from pinned memory, the loss, message counts and rule-weight
@@ -596,9 +597,10 @@ def run_slab(a, wl, kg, rank, world, local_rank):
     kernels = {}
     for kind, d in kinds.items():
         name = "slab_expand_kernel" if kind == "fwd" else "slab_expand_backward_kernel"
-        # a hop runs one launch per destination tile: its time is their sum, its bytes the hop's
-        kernels[name] = {"launches": len(d["ms"]) * d["tiles"], "destination_tiles": d["tiles"],
-                         "ms_per_launch": sum(d["ms"]) / (len(d["ms"]) * d["tiles"]),
+        # a hop runs one launch per group of destination tiles: its time is their sum, its bytes
+        # the hop's
+        kernels[name] = {"launches": d["launches"], "destination_tiles": d["tiles"],
+                         "ms_per_launch": sum(d["ms"]) / d["launches"],
                          "ms_per_hop_mean": sum(d["ms"]) / len(d["ms"]),
                          "bytes_per_hop_mean": sum(d["bytes"]) / len(d["ms"]),
                          "gbs": sum(d["bytes"]) / (sum(d["ms"]) / 1e3) / 1e9, "ms_per_hop": d["ms"],
@@ -676,8 +678,8 @@ def slab_extras(a, wl, kg, g, eng, heads, w_hops, scores, flush, B):
     udec()
     torch.cuda.synchronize()
     trace, eng.trace = eng.trace, None
-    hop_ms = [sum(e0.elapsed_time(e1) for e0, e1 in evs) for _, evs, _ in trace]
-    hop_bytes = [byts for _, _, byts in trace]
+    hop_ms = [sum(e0.elapsed_time(e1) for e0, e1 in evs) for _, evs, _, _ in trace]
+    hop_bytes = [byts for _, _, byts, _ in trace]
     gbs = sum(hop_bytes) / (sum(hop_ms) / 1e3) / 1e9
     out["decode_uncapped"] = {
         "ms": udms, "topk": 100, "edge_cap": "uncapped", "messages": M_dec, "gteps": M_dec / udms / 1e6,

@@ -397,8 +397,9 @@ int mkg_segment_sum(const int64_t* seg_ptr, int64_t nseg, const float* values, f
  * that order: ascending entity, then ascending row ("entity-major order").  A frontier or a
  * key list spanning several row windows is passed whole to each window's call; entries of
  * other rows are skipped by mkg_slab_expand and mkg_slab_expand_backward.  A destination range
- * may also be cut into tiles, each a window of its own with a push list restricted to its
- * destinations (a tile's updates then stay in L2); mkg_slab_put and mkg_slab_take given
+ * may also be cut into tiles, each with a push list restricted to its destinations, walked
+ * tile by tile in one launch (mkg_slab_expand_tiles: a tile's updates then stay in L2); a tile
+ * may also be given a window of its own, and mkg_slab_put and mkg_slab_take given
  * MKG_SLAB_SKIP_OUTSIDE skip the keys outside their window (other rows or other tiles). */
 #define MKG_SLAB_SKIP_OUTSIDE 16
 typedef struct mkg_slab_window {
@@ -428,6 +429,18 @@ int mkg_slab_expand(const int32_t* push_ptr, const mkg_adj_edge* push, const int
                     int64_t nnz, const float* w, int64_t n, int32_t identity, int32_t agg_mode,
                     const mkg_slab_window* win, void* store, double* row_sums, void* workspace,
                     size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+/* mkg_slab_expand over the push lists of ntiles destination tiles (1..MKG_SLAB_MAX_TILES) in
+ * one launch: push_ptrs / pushes are host arrays of the tiles' device lists (each [E + 1] /
+ * records restricted to the tile's destinations; together every record of the window's range
+ * once).  Work runs tile by tile, so the store sectors being updated at any time are one
+ * tile's.  The identity messages (identity != 0) are added once, with tile 0.  Workspace:
+ * mkg_slab_expand_workspace_bytes(nnz * ntiles). */
+#define MKG_SLAB_MAX_TILES 8
+int mkg_slab_expand_tiles(int32_t ntiles, const int32_t* const* push_ptrs, const mkg_adj_edge* const* pushes,
+                          const int64_t* keys, const float* vals, int64_t nnz, const float* w, int64_t n,
+                          int32_t identity, int32_t agg_mode, const mkg_slab_window* win, void* store,
+                          double* row_sums, void* workspace, size_t workspace_bytes, unsigned* dev_err,
+                          mkg_stream stream);
 /* Number of touched keys in the store -> count_out (device int64).  The workspace (also read
  * by mkg_slab_emit) keeps per-tile offsets. */
 size_t mkg_slab_collect_workspace_bytes(int64_t slots);
@@ -437,6 +450,14 @@ int mkg_slab_count(const mkg_slab_window* win, const void* store, void* workspac
  * their values and clears them in the store. */
 int mkg_slab_emit(const mkg_slab_window* win, void* store, const void* workspace, size_t workspace_bytes,
                   int64_t count, int64_t* keys_out, float* vals_out, mkg_stream stream);
+/* mkg_slab_emit of a sum hop with its normalisation (normalize_sparse3d(.., 0, "mass"),
+ * drum.py:31-51) applied in the same pass: y_out the raw values, x_out = (y / d) * min(d, 1)
+ * with d = row_sums[key row - row0] (fp32; the window's rows, complete and, across GPUs,
+ * all-reduced), as mkg_mass_normalize; dropped (device int64) receives the number of results
+ * that are zero or, when threshold > 0, below it. */
+int mkg_slab_emit_normalized(const mkg_slab_window* win, void* store, const void* workspace, size_t workspace_bytes,
+                             int64_t count, const float* row_sums, float threshold, int64_t* keys_out, float* y_out,
+                             float* x_out, int64_t* dropped, mkg_stream stream);
 /* Writes (mode 0), adds with a touched mark (mode 1) or raises to the maximum with a touched
  * mark (mode 2: max_sp_3d's max over rules with row_div = L) values at keys whose row is
  * (key / E) / row_div (row_div = L maps (b, l, e) to the [B, E] key b * E + e: sum_sp_3d,
@@ -459,6 +480,14 @@ int mkg_slab_expand_backward(const int32_t* push_ptr, const mkg_adj_edge* push, 
                              const mkg_slab_window* win, const void* store, const mkg_edge_factor* ef,
                              int64_t num_facts, double* grad_sp, double* grad_w, float* grad_edge, void* workspace,
                              size_t workspace_bytes, unsigned* dev_err, mkg_stream stream);
+/* mkg_slab_expand_backward over ntiles destination tiles in one launch (as
+ * mkg_slab_expand_tiles; the identity messages' gradient taken once, with tile 0). */
+int mkg_slab_expand_backward_tiles(int32_t ntiles, const int32_t* const* push_ptrs, const mkg_adj_edge* const* pushes,
+                                   const int64_t* keys, const float* vals, int64_t nnz, const float* w, int64_t n,
+                                   int32_t identity, const mkg_slab_window* win, const void* store,
+                                   const mkg_edge_factor* ef, int64_t num_facts, double* grad_sp, double* grad_w,
+                                   float* grad_edge, void* workspace, size_t workspace_bytes, unsigned* dev_err,
+                                   mkg_stream stream);
 /* out[r] += sum of vals over the entries of row r (key / E - row0) in fp64; keys ascending.
  * The per-(b, l) sums of normalize_sparse3d and of its gradient (drum.py:31-51). */
 int mkg_row_sums(const int64_t* keys, int64_t nnz, int64_t E, int64_t row0, int64_t nrows, const float* vals,

@@ -18,6 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libminikg_b200.so"
 MKG_OK = 0
 MASK_NONE, MASK_U8, MASK_F32 = 0, 1, 2
 SLAB_SKIP_OUTSIDE = 16  # MKG_SLAB_SKIP_OUTSIDE
+SLAB_MAX_TILES = 8  # MKG_SLAB_MAX_TILES
 DEV_ERR_NAMES = {1: "frontier entry outside [B, L, E]", 2: "CSR column outside [0, E)",
                  4: "fact id outside [0, T)", 8: "gradient key outside [B, L, E]",
                  16: "relation id outside its range", 32: "a bounded wait inside a kernel gave up",
@@ -134,13 +135,19 @@ SIGNATURES = {
     "mkg_slab_expand_workspace_bytes": (C.c_size_t, [i64]),
     "mkg_slab_expand": (C.c_int, [vp, vp, vp, vp, i64, vp, i64, i32, i32, P(SlabWindow), vp, vp, vp, C.c_size_t,
                                   vp, vp]),
+    "mkg_slab_expand_tiles": (C.c_int, [i32, vp, vp, vp, vp, i64, vp, i64, i32, i32, P(SlabWindow), vp, vp, vp,
+                                        C.c_size_t, vp, vp]),
     "mkg_slab_collect_workspace_bytes": (C.c_size_t, [i64]),
     "mkg_slab_count": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, vp, vp]),
     "mkg_slab_emit": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, i64, vp, vp, vp]),
+    "mkg_slab_emit_normalized": (C.c_int, [P(SlabWindow), vp, vp, C.c_size_t, i64, vp, C.c_float, vp, vp, vp, vp,
+                                           vp]),
     "mkg_slab_put": (C.c_int, [P(SlabWindow), vp, vp, vp, i64, i64, i32, vp, vp]),
     "mkg_slab_take": (C.c_int, [P(SlabWindow), vp, vp, i64, i64, vp, i32, vp, vp]),
     "mkg_slab_expand_backward": (C.c_int, [vp, vp, vp, vp, i64, vp, i64, i32, P(SlabWindow), vp, P(EdgeFactor),
                                            i64, vp, vp, vp, vp, C.c_size_t, vp, vp]),
+    "mkg_slab_expand_backward_tiles": (C.c_int, [i32, vp, vp, vp, vp, i64, vp, i64, i32, P(SlabWindow), vp,
+                                                 P(EdgeFactor), i64, vp, vp, vp, vp, C.c_size_t, vp, vp]),
     "mkg_row_sums": (C.c_int, [vp, i64, i64, i64, i64, vp, vp, vp, vp]),
     "mkg_f64_to_f32": (C.c_int, [vp, i64, vp, vp]),
     "mkg_mass_normalize": (C.c_int, [vp, vp, i64, i64, i64, i64, vp, C.c_float, vp, vp, vp, vp]),

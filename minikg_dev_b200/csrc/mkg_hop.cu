@@ -57,6 +57,7 @@ struct HopLayout {
   // hash: claimed keys, values (f32 / packed u64), their key-sorted copies, entry map values
   size_t off_tkey, off_tval, off_tpk, off_skey, off_sval, off_spk, off_mapkey;
   size_t off_gw64;         // backward: rule-weight gradient accumulated in fp64
+  size_t off_gsp64;        // backward: frontier-entry gradient accumulated in fp64
   size_t cub_bytes;
 
   int64_t slots(int t) const { return t < 2 ? capm : capf; }
@@ -157,6 +158,7 @@ HopLayout backward_layout(const mkg_hop_params& p, int64_t F) {
   L.off_lists = o; o += a256(4 * (size_t)(3 * F + 3));
   L.off_counts = o; o += a256(4 * 4);
   L.off_gw64 = o; o += a256(8 * (size_t)(p.B * p.L * p.n));
+  L.off_gsp64 = o; o += a256(8 * (size_t)(F > 0 ? F : 1));
   L.total = o;
   return L;
 }
@@ -660,26 +662,28 @@ __global__ void scatter_grad_kernel(mkg_coo3 g, int64_t B, int64_t L, int64_t lo
 
 // Identity channel: grad_sp[i] = g_ind(key_i) * w[b,l,n-1] (initialises grad_sp) and
 // grad_w[b,l,n-1] += g_ind * sv (fastlog.cu:2608-2644); also fills the key -> entry map
-// (full-range keys) used by the argmax backward.
+// (full-range keys) used by the argmax backward.  The entry and rule-weight gradients are fp64
+// sums of fp64 products (rounded once at the end): both are sums whose terms cancel, where
+// fp32-rounded terms drifted past 1e-5 of the result.
 __global__ void backward_entry_init_kernel(Frontier f, HopCtx c, KeyTable ind_tab, const float* __restrict__ g_ind,
-                                           float* __restrict__ grad_sp, double* __restrict__ grad_w,
+                                           double* __restrict__ grad_sp, double* __restrict__ grad_w,
                                            KeyTable map_tab, int32_t* __restrict__ entry_map) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < f.F;
        i += (int64_t)gridDim.x * blockDim.x) {
     int64_t b, l, e;
-    if (!load_entry(f, c, i, b, l, e)) { grad_sp[i] = 0.0f; continue; }
+    if (!load_entry(f, c, i, b, l, e)) { grad_sp[i] = 0.0; continue; }
     if (entry_map) {
       const int64_t s = map_tab.insert(static_cast<unsigned long long>((b * c.L + l) * c.E + e), c.err);
       if (s >= 0) entry_map[s] = static_cast<int32_t>(i);
     }
-    float gsp = 0.0f;
+    double gsp = 0.0;
     if (!c.wot_i && in_range(c, e)) {
       const int64_t wi = (b * c.L + l) * c.n + (c.n - 1);
       const int64_t s = ind_tab.find(static_cast<unsigned long long>(out_key0(c, b, l) + e));
       float g = s >= 0 ? g_ind[s] : 0.0f;
       if (g != 0.0f) {
-        gsp = g * c.w[wi];
-        atomicAdd(grad_w + wi, static_cast<double>(g * f.v[i]));
+        gsp = (double)g * (double)c.w[wi];
+        atomicAdd(grad_w + wi, (double)g * (double)f.v[i]);
       }
     }
     grad_sp[i] = gsp;
@@ -704,7 +708,7 @@ struct BwdVisit {
   const EdgeFactor* f;
   float sv;
   int64_t key0, wbase;
-  float acc;
+  double acc;  // the entry's gradient (fp64 products, fp64 sum)
   int64_t lo, Eo;
   __device__ __forceinline__ void operator()(int d, int64_t dst, int64_t ch, float wv, int64_t fact) {
     if (static_cast<uint64_t>(dst - lo) >= static_cast<uint64_t>(Eo)) return;  // another shard's destination
@@ -713,15 +717,15 @@ struct BwdVisit {
     float g = gs.val[d][s];
     if (g == 0.0f) return;
     float m = (*f)(fact);
-    float gm = g * m;
-    acc += gm * wv;
-    atomicAdd(grad_w + wbase + ch, static_cast<double>(gm * sv));
+    const double gm = (double)g * (double)m;
+    acc += gm * (double)wv;
+    atomicAdd(grad_w + wbase + ch, gm * (double)sv);
     if (grad_edge) atomicAdd(grad_edge + fact, (((g * sv) * wv) * m) * edge_grad_factor(*f, fact));
   }
 };
 
 __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict__ list,
-                                const int32_t* __restrict__ count, GradStore gs, float* __restrict__ grad_sp,
+                                const int32_t* __restrict__ count, GradStore gs, double* __restrict__ grad_sp,
                                 double* __restrict__ grad_w, float* __restrict__ grad_edge) {
   const int64_t n = *count;
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < n;
@@ -741,7 +745,7 @@ __global__ void bwd_tail_kernel(Frontier f, HopCtx c, const int32_t* __restrict_
 
 __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
     Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count, GradStore gs,
-    float* __restrict__ grad_sp, double* __restrict__ grad_w, float* __restrict__ grad_edge) {
+    double* __restrict__ grad_sp, double* __restrict__ grad_w, float* __restrict__ grad_edge) {
   __shared__ int hist_all[kMidWarps][kNumBuckets];
   int* hist = hist_all[threadIdx.x >> 5];
   const int lane = threadIdx.x & 31;
@@ -762,17 +766,17 @@ __global__ void __launch_bounds__(kMidWarps * 32) bwd_mid_kernel(
         warp_capped_direction(c, d, e, wrow, hist, vis);
       }
     }
-    float tot = warp_sum(vis.acc);
+    const double tot = warp_sum_f64(vis.acc);
     if (lane == 0) grad_sp[i] += tot;
   }
 }
 
 __global__ void __launch_bounds__(kHubThreads) bwd_hub_kernel(
     Frontier f, HopCtx c, const int32_t* __restrict__ list, const int32_t* __restrict__ count, GradStore gs,
-    float* __restrict__ grad_sp, double* __restrict__ grad_w, float* __restrict__ grad_edge) {
+    double* __restrict__ grad_sp, double* __restrict__ grad_w, float* __restrict__ grad_edge) {
   __shared__ float wstage[kHubStageMax];
   __shared__ int hist[kNumBuckets];
-  __shared__ float part[kHubThreads / 32];
+  __shared__ double part[kHubThreads / 32];
   const int64_t n = *count;
   for (int64_t k = blockIdx.x; k < n; k += gridDim.x) {
     const int64_t i = list[k];
@@ -794,11 +798,11 @@ __global__ void __launch_bounds__(kHubThreads) bwd_hub_kernel(
         warp_capped_direction(c, d, e, wrow, hist, vis);
       }
     }
-    float ws = warp_sum(vis.acc);
+    const double ws = warp_sum_f64(vis.acc);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ws;
     __syncthreads();
     if (threadIdx.x == 0) {
-      float t = 0.0f;
+      double t = 0.0;
       for (int q = 0; q < kHubThreads / 32; ++q) t += part[q];
       grad_sp[i] += t;
     }
@@ -812,7 +816,7 @@ __global__ void bwd_argmax_kernel(int d, mkg_coo3 out, const int64_t* __restrict
                                   KeyTable gtab, const float* __restrict__ gvals, KeyTable map_tab,
                                   const int32_t* __restrict__ entry_map, const int32_t* __restrict__ fhead,
                                   const int32_t* __restrict__ ftail, const int16_t* __restrict__ frel,
-                                  float* __restrict__ grad_sp, double* __restrict__ grad_w,
+                                  double* __restrict__ grad_sp, double* __restrict__ grad_w,
                                   float* __restrict__ grad_edge) {
   for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < out.nnz;
        k += (int64_t)gridDim.x * blockDim.x) {
@@ -833,9 +837,9 @@ __global__ void bwd_argmax_kernel(int d, mkg_coo3 out, const int64_t* __restrict
     float sv = f.v[i];
     int64_t wi = (b * c.L + l) * c.n + ch;
     float wv = c.w[wi];
-    float gm = g * m;
-    atomicAdd(grad_sp + i, gm * wv);
-    atomicAdd(grad_w + wi, static_cast<double>(gm * sv));
+    const double gm = (double)g * (double)m;
+    atomicAdd(grad_sp + i, gm * (double)wv);
+    atomicAdd(grad_w + wi, gm * (double)sv);
     if (grad_edge) atomicAdd(grad_edge + fact, (((g * sv) * wv) * m) * edge_grad_factor(c.factor, fact));
   }
 }
@@ -1135,9 +1139,14 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
   const int64_t nw = p->B * p->L * p->n;
   double* gw64 = reinterpret_cast<double*>(base + lay.off_gw64);
   MKG_CUDA(cudaMemsetAsync(gw64, 0, 8 * (size_t)nw, st));
-  auto finish = [&]() -> int {  // grad_w = the fp64 sums rounded once
+  double* gsp64 = reinterpret_cast<double*>(base + lay.off_gsp64);
+  auto finish = [&]() -> int {  // grad_w and grad_sp = the fp64 sums rounded once
     round_gw_kernel<<<grid_for(nw, 256, persistent_blocks(2)), 256, 0, st>>>(gw64, nw, grad_w);
     MKG_LAUNCHED("round_gw_kernel");
+    if (fr->nnz > 0) {
+      round_gw_kernel<<<grid_for(fr->nnz, 256, persistent_blocks(2)), 256, 0, st>>>(gsp64, fr->nnz, grad_sp);
+      MKG_LAUNCHED("round_gw_kernel");
+    }
     return MKG_OK;
   };
   if (grad_edge) MKG_CUDA(cudaMemsetAsync(grad_edge, 0, 4 * (size_t)g->num_facts, st));
@@ -1155,17 +1164,17 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
   HopCtx c = make_ctx(g, w, ef, p, err);
   Frontier f{fr->batch, fr->level, fr->entity, fr->value, F};
   backward_entry_init_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(
-      f, c, tabs[2], vals[2], grad_sp, gw64, map_tab, emap);
+      f, c, tabs[2], vals[2], gsp64, gw64, map_tab, emap);
   MKG_LAUNCHED("backward_entry_init_kernel");
   if (p->agg_mode == 0) {
     classify_kernel<<<grid_for(F, 256, persistent_blocks(8)), 256, 0, st>>>(f, c, lists, counts, nullptr, nullptr,
                                                                              dense_table());
     MKG_LAUNCHED("classify_kernel");
     GradStore gs{{vals[0], vals[1]}, {tabs[0], tabs[1]}};
-    bwd_tail_kernel<<<persistent_blocks(8), 256, 0, st>>>(f, c, lists, counts, gs, grad_sp, gw64, grad_edge);
-    bwd_mid_kernel<<<persistent_blocks(4), kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, gs, grad_sp, gw64,
+    bwd_tail_kernel<<<persistent_blocks(8), 256, 0, st>>>(f, c, lists, counts, gs, gsp64, gw64, grad_edge);
+    bwd_mid_kernel<<<persistent_blocks(4), kMidWarps * 32, 0, st>>>(f, c, lists + F, counts + 1, gs, gsp64, gw64,
                                                                     grad_edge);
-    bwd_hub_kernel<<<persistent_blocks(2), kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, gs, grad_sp, gw64,
+    bwd_hub_kernel<<<persistent_blocks(2), kHubThreads, 0, st>>>(f, c, lists + 2 * F, counts + 2, gs, gsp64, gw64,
                                                                  grad_edge);
     MKG_LAUNCHED("backward push kernels");
   } else {
@@ -1174,7 +1183,7 @@ int hop_backward(const mkg_graph* g, const mkg_frontier* fr, const float* w, con
     for (int d = 0; d < 2; ++d) {
       if (outs[d]->nnz <= 0) continue;
       bwd_argmax_kernel<<<grid_for(outs[d]->nnz, 256, persistent_blocks(8)), 256, 0, st>>>(
-          d, *outs[d], args[d], f, c, tabs[d], vals[d], map_tab, emap, fhead, ftail, frel, grad_sp, gw64,
+          d, *outs[d], args[d], f, c, tabs[d], vals[d], map_tab, emap, fhead, ftail, frel, gsp64, gw64,
           grad_edge);
       MKG_LAUNCHED("bwd_argmax_kernel");
     }

@@ -1087,7 +1087,10 @@ __device__ __forceinline__ float reduce_scatter4(const float (&v)[4]) {
 // value in this chunk are visited (dY_h is zero elsewhere).  Rule weights are read from
 // global memory (L1-resident chunk) so that only dW occupies shared memory: 4 blocks per SM
 // (64 registers, a few bytes spilled; the capped loop, which spills more there, keeps 3).
-template <bool CAP>
+// Acc: the shared-memory accumulator of the rule-weight gradient, double where [n, 128] of it
+// fits (each fp64 product added once: the fp32 partials of many terms of both signs drifted past
+// 1e-5 of the result), float for wider channel counts.
+template <bool CAP, typename Acc>
 __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
     const int4* __restrict__ tasks, int64_t ntasks, const mkg_adj_edge* __restrict__ edges, ProofDims q,
     const float* __restrict__ wt, const float* __restrict__ x, const uint8_t* __restrict__ act,
@@ -1095,8 +1098,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
     float* __restrict__ dx, double* __restrict__ dwt, double* __restrict__ sprev, float* __restrict__ grad_edge,
     int64_t num_facts, EdgeFactor ef, int32_t* __restrict__ queue, const int2* __restrict__ rcap,
     const uint8_t* __restrict__ take, unsigned* err) {
-  extern __shared__ float smem[];
-  float* dws = smem;                        // [n][128] rule-weight gradient (conflict-free: [ch][k][lane])
+  extern __shared__ double smem[];
+  Acc* dws = reinterpret_cast<Acc*>(smem);  // [n][128] rule-weight gradient (conflict-free: [ch][k][lane])
   // [4][32] S_prev partials in fp64 (dX Y terms of both signs cancel in S)
   double* cs = reinterpret_cast<double*>(dws + q.n * kChunk);
   const int lane = threadIdx.x & 31;
@@ -1104,7 +1107,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
   const int64_t col0 = chunk * kChunk;
   const int64_t col = col0 + 4 * lane;
   const bool colok = col < q.BLP;
-  for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) dws[i] = 0.0f;
+  for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) dws[i] = Acc(0);
   for (int i = threadIdx.x; i < kChunk; i += blockDim.x) cs[i] = 0.0;
   __syncthreads();
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1125,11 +1128,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
         const float4 ds = *reinterpret_cast<const float4*>(dy + row * q.BLP + col);
         const float4 wi = wload(q.n - 1);
         gx = f4_mul(ds, wi);
-        float* dwi = dws + (q.n - 1) * kChunk;
-        if (ds.x != 0.f) atomicAdd(dwi + 0 * 32 + lane, ds.x * xr.x);
-        if (ds.y != 0.f) atomicAdd(dwi + 1 * 32 + lane, ds.y * xr.y);
-        if (ds.z != 0.f) atomicAdd(dwi + 2 * 32 + lane, ds.z * xr.z);
-        if (ds.w != 0.f) atomicAdd(dwi + 3 * 32 + lane, ds.w * xr.w);
+        Acc* dwi = dws + (q.n - 1) * kChunk;
+        if (ds.x != 0.f) atomicAdd(dwi + 0 * 32 + lane, Acc(ds.x) * Acc(xr.x));
+        if (ds.y != 0.f) atomicAdd(dwi + 1 * 32 + lane, Acc(ds.y) * Acc(xr.y));
+        if (ds.z != 0.f) atomicAdd(dwi + 2 * 32 + lane, Acc(ds.z) * Acc(xr.z));
+        if (ds.w != 0.f) atomicAdd(dwi + 3 * 32 + lane, Acc(ds.w) * Acc(xr.w));
       }
       float4 run = zero;  // sum of dY * m over the current channel run
       int cur = -1;
@@ -1140,11 +1143,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
         const float4 wc = wcur;
         gx.x = fmaf(run.x, wc.x, gx.x); gx.y = fmaf(run.y, wc.y, gx.y);
         gx.z = fmaf(run.z, wc.z, gx.z); gx.w = fmaf(run.w, wc.w, gx.w);
-        float* dwc = dws + cur * kChunk;
-        if (run.x != 0.f) atomicAdd(dwc + 0 * 32 + lane, run.x * xr.x);
-        if (run.y != 0.f) atomicAdd(dwc + 1 * 32 + lane, run.y * xr.y);
-        if (run.z != 0.f) atomicAdd(dwc + 2 * 32 + lane, run.z * xr.z);
-        if (run.w != 0.f) atomicAdd(dwc + 3 * 32 + lane, run.w * xr.w);
+        Acc* dwc = dws + cur * kChunk;
+        if (run.x != 0.f) atomicAdd(dwc + 0 * 32 + lane, Acc(run.x) * Acc(xr.x));
+        if (run.y != 0.f) atomicAdd(dwc + 1 * 32 + lane, Acc(run.y) * Acc(xr.y));
+        if (run.z != 0.f) atomicAdd(dwc + 2 * 32 + lane, Acc(run.z) * Acc(xr.z));
+        if (run.w != 0.f) atomicAdd(dwc + 3 * 32 + lane, Acc(run.w) * Acc(xr.w));
         run = zero;
       };
       for (int base = tk.y; base < tk.z; base += 32) {
@@ -1253,7 +1256,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, CAP ? 3 : 4) bwd_pull_kernel(
   for (int64_t i = threadIdx.x; i < q.n * kChunk; i += blockDim.x) {
     const int64_t ch = i / kChunk, r = i % kChunk, l = r % 32, k = r / 32;
     const int64_t c = col0 + 4 * l + k;
-    if (c < q.BLP && dws[i] != 0.0f) atomicAdd(dwt + ch * q.BLP + c, static_cast<double>(dws[i]));
+    if (c < q.BLP && dws[i] != Acc(0)) atomicAdd(dwt + ch * q.BLP + c, static_cast<double>(dws[i]));
   }
   if (sprev != nullptr) {
     for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {
@@ -1419,7 +1422,11 @@ __global__ void __launch_bounds__(kTopkThreads) topk_rows_kernel(Rows rows, int6
   if (threadIdx.x == 0) counts[b] = m;
 }
 
-size_t bwd_smem(const ProofDims& q) { return 4 * (size_t)q.n * kChunk + 8 * (size_t)kChunk; }
+constexpr size_t kBwdSmemMax = 200 * 1024;
+// shared memory of the backward pull with fp64 (f64) or fp32 rule-weight partials
+size_t bwd_smem(const ProofDims& q, bool f64 = false) {
+  return (f64 ? 8 : 4) * (size_t)q.n * kChunk + 8 * (size_t)kChunk;
+}
 
 // Columns per lane of the forward pull: 8 (two float4) for batches wider than 128
 // columns; MKG_FWD_VEC=1|2 overrides (a tuning knob).
@@ -1454,7 +1461,7 @@ int check_proof(const mkg_graph* g, const mkg_adjacency* adj, const mkg_proof_pa
                 "proof: incomplete cap index");
   }
   ProofDims q = proof_dims(*p);
-  MKG_REQUIRE(bwd_smem(q) <= 200 * 1024, "proof: too many relation channels (%lld) for the shared-memory "
+  MKG_REQUIRE(bwd_smem(q) <= kBwdSmemMax, "proof: too many relation channels (%lld) for the shared-memory "
               "staging of the rule weights", (long long)q.n);
   return MKG_OK;
 }
@@ -1595,14 +1602,26 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
   dim3 sgrid((unsigned)((q.E + 32 * kSeedTiles - 1) / (32 * kSeedTiles)), (unsigned)((q.B + 31) / 32));
   seed_grad_kernel<<<sgrid, 256, 0, st>>>(grad_out, S.x(q.hops), S.y(q.hops - 1), q, dx_cur, S.s(q.hops - 1));
   MKG_LAUNCHED("seed_grad_kernel");
-  const size_t sm = bwd_smem(q);
   const mkg_cap_index* ix = q.cap >= 0 ? p->cap_index : nullptr;
   const int2* push_cap = ix ? reinterpret_cast<const int2*>(ix->push_cap) : nullptr;
-  const void* bwd_fn = ix ? (const void*)bwd_pull_kernel<true> : (const void*)bwd_pull_kernel<false>;
-  rc = set_smem(bwd_fn, sm);
+  // fp64 rule-weight partials wherever they keep the fp32 variant's blocks per SM (few relation
+  // channels); fp32 where the doubled shared memory would cost occupancy (measured on the
+  // 51-relation workload: 2 instead of 4 blocks per SM, 1.45 -> 1.83 ms per step)
+  const void* fn32 = ix ? (const void*)bwd_pull_kernel<true, float> : (const void*)bwd_pull_kernel<false, float>;
+  const void* fn64 = ix ? (const void*)bwd_pull_kernel<true, double> : (const void*)bwd_pull_kernel<false, double>;
+  int occ32 = 0, occ64 = 0;
+  rc = set_smem(fn32, bwd_smem(q, false));
   if (rc) return rc;
-  int resident = 0;
-  MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, bwd_fn, kBwdWarps * 32, sm));
+  MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ32, fn32, kBwdWarps * 32, bwd_smem(q, false)));
+  if (bwd_smem(q, true) <= kBwdSmemMax) {
+    rc = set_smem(fn64, bwd_smem(q, true));
+    if (rc) return rc;
+    MKG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ64, fn64, kBwdWarps * 32, bwd_smem(q, true)));
+  }
+  const bool f64 = occ64 >= 1 && occ64 >= occ32;
+  const void* bwd_fn = f64 ? fn64 : fn32;
+  const size_t sm = bwd_smem(q, f64);
+  const int resident = f64 ? occ64 : occ32;
   const int blocks_per_chunk = grid_for(adj->num_push_tasks, kBwdWarps,
                                         (int)((int64_t)num_sms() * (resident > 0 ? resident : 1) / q.nch) + 1);
   for (int64_t h = q.hops - 1; h >= 0; --h) {
@@ -1617,16 +1636,19 @@ int proof_backward(const mkg_graph* g, const mkg_adjacency* adj, const float* w_
     {
       const int4* tk = reinterpret_cast<const int4*>(adj->push_tasks);
       int32_t* qu = S.queue() + (q.hops + h) * q.nch * kQueueStride;
-      if (ix)
-        bwd_pull_kernel<true><<<grid, kBwdWarps * 32, sm, st>>>(
+      auto launch = [&](auto kernel, const int2* rcap, const uint8_t* take) {
+        kernel<<<grid, kBwdWarps * 32, sm, st>>>(
             tk, adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.yact(h), S.dy(),
             h > 0 ? S.y(h - 1) : nullptr, dx_next, S.dwt(), h > 0 ? S.s(h - 1) : nullptr, grad_edge, g->num_facts, f,
-            qu, push_cap, S.take(h), err);
-      else
-        bwd_pull_kernel<false><<<grid, kBwdWarps * 32, sm, st>>>(
-            tk, adj->num_push_tasks, adj->push, q, S.wt(h), S.x(h), S.act(h), S.yact(h), S.dy(),
-            h > 0 ? S.y(h - 1) : nullptr, dx_next, S.dwt(), h > 0 ? S.s(h - 1) : nullptr, grad_edge, g->num_facts, f,
-            qu, nullptr, nullptr, err);
+            qu, rcap, take, err);
+      };
+      if (ix) {
+        if (f64) launch(bwd_pull_kernel<true, double>, push_cap, S.take(h));
+        else launch(bwd_pull_kernel<true, float>, push_cap, S.take(h));
+      } else {
+        if (f64) launch(bwd_pull_kernel<false, double>, nullptr, nullptr);
+        else launch(bwd_pull_kernel<false, float>, nullptr, nullptr);
+      }
     }
     MKG_LAUNCHED("bwd_pull_kernel");
     if (p->bwd_events) MKG_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(p->bwd_events[2 * h + 1]), st));

@@ -66,10 +66,11 @@ class SlabEngine:
     slab store and its window size.
 
     A tile is a sub-range of the destinations with its own push list (the records that reach
-    it): a hop's expansion (and its backward walk) is one launch per tile, each touching only
-    its tile's part of the entity-major store, whose sectors then stay in L2 (a whole 4.6
-    M-entity range's touched sectors do not: every message then fetched and wrote back its
-    sector); the collect, the gradient's put and the clearing run once over the whole window.
+    it): a hop's expansion (and its backward walk) is one launch that walks the tiles in turn
+    (up to ``SLAB_MAX_TILES`` per launch), so the updates in flight touch only one tile's part
+    of the entity-major store, whose sectors then stay in L2 (a whole 4.6 M-entity range's
+    touched sectors do not: every message then fetched and wrote back its sector); the
+    collect, the gradient's put and the clearing run once over the whole window.
     ``dst_tiles`` (default: one per ``TILE_ENTITIES`` destinations) sets their number.
 
     ``store_bytes`` caps the store (default: ``STORE_FRACTION`` of the free memory when first
@@ -105,12 +106,20 @@ class SlabEngine:
             for _, _, ptr_t, _ in self.tiles:
                 self.ptr += ptr_t
             self._shared = False
+        # launch groups of at most SLAB_MAX_TILES tiles: (count, host arrays of the tiles' device
+        # list pointers); each group's expansion is one launch walking its tiles in turn
+        self.tile_groups = []
+        for g0 in range(0, len(self.tiles), N.SLAB_MAX_TILES):
+            grp = self.tiles[g0:g0 + N.SLAB_MAX_TILES]
+            ptrs = (ctypes.c_void_p * len(grp))(*[p.data_ptr() for _, _, p, _ in grp])
+            recs = (ctypes.c_void_p * len(grp))(*[r.data_ptr() for _, _, _, r in grp])
+            self.tile_groups.append((len(grp), ptrs, recs))
         self._store_cap = store_bytes
         self._budget_bound = False
         self.store = None
         self.rows_per_window = 0
-        # when a list: (kind, hop-local index, start event, end event, algorithmic bytes) per
-        # expansion launch, for roofline accounting (adds host synchronisations; off by default)
+        # when a list: (kind, [(start, end) event per launch], algorithmic bytes, tiles) per hop
+        # window, for roofline accounting (adds host synchronisations; off by default)
         self.trace = None
         self._groups = None
 
@@ -180,8 +189,10 @@ def _in_rows(x, E: int, r0: int, nr: int, whole: bool):
     return x if whole else x[((x // E) >= r0) & ((x // E) < r0 + nr)]
 
 
-def _collect(eng: SlabEngine, win):
-    """Emits the touched keys of the store (entity-major order) with their values."""
+def _collect(eng: SlabEngine, win, norm=None):
+    """Emits the touched keys of the store (entity-major order) with their values; with ``norm``
+    = (fp32 row sums of the window's rows, threshold) also their mass-normalised values and a
+    device count of the results the loop drops (``mkg_slab_emit_normalized``)."""
     lib = N.load()
     dev = eng.dev
     st = N.stream_handle(dev)
@@ -193,9 +204,17 @@ def _collect(eng: SlabEngine, win):
     U = int(cnt.item())
     keys = torch.empty(U, dtype=torch.int64, device=dev)
     vals = torch.empty(U, dtype=torch.float32, device=dev)
-    N.check(lib.mkg_slab_emit(ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(), ws.numel(), U,
-                              keys.data_ptr(), vals.data_ptr(), st), "slab_emit")
-    return keys, vals
+    if norm is None:
+        N.check(lib.mkg_slab_emit(ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(), ws.numel(), U,
+                                  keys.data_ptr(), vals.data_ptr(), st), "slab_emit")
+        return keys, vals
+    d32, threshold = norm
+    x = torch.empty(U, dtype=torch.float32, device=dev)
+    dropped = torch.zeros(1, dtype=torch.int64, device=dev)
+    N.check(lib.mkg_slab_emit_normalized(ctypes.byref(win), eng.store.data_ptr(), ws.data_ptr(), ws.numel(), U,
+                                         d32.data_ptr(), float(threshold), keys.data_ptr(), vals.data_ptr(),
+                                         x.data_ptr(), dropped.data_ptr(), st), "slab_emit_normalized")
+    return keys, vals, x, dropped
 
 
 def graph_bytes(eng: SlabEngine, keys) -> int:
@@ -214,14 +233,23 @@ def graph_bytes(eng: SlabEngine, keys) -> int:
     return int((deg * 8 + grp * 10 + 8).sum())
 
 
-def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True, agg_mode: int = 0):
+def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True, agg_mode: int = 0,
+                   normalize=None):
     """One hop's concat-summed output over the engine's destinations: (keys in entity-major order
     within each row window, windows in row order; values; fp64 row sums [BL], zeros for
     ``agg_mode`` 1, which keeps each key's largest message instead; the output's [a, b) part of
     every row window, in window order).  The frontier may come in any order
     (entity-major keeps neighbouring atomics in the same sectors).  ``check``: refuse frontier
     keys outside [B, L, E] on the host (the loop, whose keys are its own outputs, skips that
-    synchronisation)."""
+    synchronisation).
+
+    ``normalize`` = (ShardSpec or None, threshold), sum hop only: the hop's mass normalisation
+    (drum.py:31-51) with the row sums all-reduced over ranks (one all-reduce per hop on every
+    path); returns (keys, raw values, fp32 row sums [BL], parts, normalised values, number of
+    them the loop drops).  With one row window the values are normalised as they are gathered
+    (``mkg_slab_emit_normalized``), otherwise by a pass over the emitted values."""
+    if normalize is not None and agg_mode != 0:
+        raise ValueError("expand_forward: the normalisation belongs to the sum hop (agg_mode 0)")
     lib = N.load()
     dev = eng.dev
     E = eng.g.num_entities
@@ -236,26 +264,35 @@ def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True
     st = N.stream_handle(dev)
     err = N.error_word(dev).data_ptr()
     nk = int(keys.numel())
+    fused = normalize is not None and len(bounds) == 1 and nk > 0
     if nk == 0:
-        return (torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev), d,
-                [(0, 0)] * len(bounds))
+        ko, vo = torch.empty(0, dtype=torch.int64, device=dev), torch.empty(0, dtype=torch.float32, device=dev)
+        if normalize is not None:
+            return _normalized(ko, vo, d, [(0, 0)] * len(bounds), normalize, E, BL)
+        return ko, vo, d, [(0, 0)] * len(bounds)
     k = keys.contiguous()
     v = vals.detach().to(torch.float32).contiguous()
-    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk), dev)
+    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk * eng.tile_groups[0][0]), dev)
     parts, pos = [], 0
     for r0, nr in bounds:  # every window takes the whole frontier and walks the entries of its rows
         rs = d[r0:r0 + nr].data_ptr() if agg_mode == 0 else None  # the expansions add their row sums
         win = eng.window(r0, nr)
         evs = []
-        for t, (_, _, ptr_t, push_t) in enumerate(eng.tiles):  # one launch per destination tile
-            ev = _events(eng)  # (the same window; the first tile's launch adds the identity messages)
-            N.check(lib.mkg_slab_expand(ptr_t.data_ptr(), push_t.data_ptr(), k.data_ptr(), v.data_ptr(), nk,
-                                        wf.data_ptr(), n, int(t == 0), int(agg_mode), ctypes.byref(win),
-                                        eng.store.data_ptr(), rs, ws.data_ptr(), ws.numel(), err, st), "slab_expand")
+        for gi, (nt, ptrs, recs) in enumerate(eng.tile_groups):  # one launch per group of tiles
+            ev = _events(eng)  # (the same window; the first tile adds the identity messages)
+            N.check(lib.mkg_slab_expand_tiles(nt, ctypes.addressof(ptrs), ctypes.addressof(recs), k.data_ptr(),
+                                              v.data_ptr(), nk, wf.data_ptr(), n, int(gi == 0), int(agg_mode),
+                                              ctypes.byref(win), eng.store.data_ptr(), rs, ws.data_ptr(), ws.numel(),
+                                              err, st), "slab_expand")
             if ev is not None:
                 ev[1].record()
                 evs.append(ev)
-        ko, vo = _collect(eng, win)
+        if fused:  # the whole of d is this window's: final once all-reduced
+            _all_reduce(d, normalize[0])
+            d32 = d.to(torch.float32)
+            ko, vo, xo, dro = _collect(eng, win, (d32, normalize[1]))
+        else:
+            ko, vo = _collect(eng, win)
         out_k.append(ko)
         out_v.append(vo)
         parts.append((pos, pos + int(ko.numel())))
@@ -264,10 +301,23 @@ def expand_forward(eng: SlabEngine, keys, vals, w_h, BL: int, check: bool = True
             # value), rule weights; its time is the sum over the tiles' expansions
             mine = _in_rows(k, E, r0, nr, len(bounds) == 1)
             eng.trace.append(("fwd", evs, graph_bytes(eng, mine) + 12 * int(mine.numel()) + 12 * int(ko.numel())
-                              + nr * n * 4))
-    if len(out_k) == 1:
-        return out_k[0], out_v[0], d, parts
-    return torch.cat(out_k), torch.cat(out_v), d, parts
+                              + nr * n * 4, len(eng.tiles)))
+    ko, vo = (out_k[0], out_v[0]) if len(out_k) == 1 else (torch.cat(out_k), torch.cat(out_v))
+    if fused:
+        return ko, vo, d32, parts, xo, int(dro.item())
+    if normalize is not None:
+        return _normalized(ko, vo, d, parts, normalize, E, BL)
+    return ko, vo, d, parts
+
+
+def _normalized(keys, y, d, parts, normalize, E: int, BL: int):
+    """expand_forward's normalised result by a separate pass: the row sums all-reduced, then
+    ``mkg_mass_normalize``."""
+    spec, threshold = normalize
+    _all_reduce(d, spec)
+    d32 = d.to(torch.float32)
+    x, dropped = _mass_normalize(keys, y, E, BL, d32, threshold)
+    return keys, y, d32, parts, x, dropped
 
 
 def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, parts, put_grad, factor, grad_w64,
@@ -294,20 +344,20 @@ def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, parts, pu
     ky = keys_y.contiguous()
     k = keys.contiguous()
     v = vals.detach().to(torch.float32).contiguous()
-    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk), dev)
+    ws = N.workspace(lib.mkg_slab_expand_workspace_bytes(nk * eng.tile_groups[0][0]), dev)
     for (r0, nr), (a, b) in zip(bounds, parts):  # every window takes the whole frontier
         win = eng.window(r0, nr)
         if b > a:
             put_grad(win, a, b)
         evs = []
-        for t, (_, _, ptr_t, push_t) in enumerate(eng.tiles):  # one walk per destination tile
-            ev = _events(eng)  # (the first tile's walk takes the identity messages)
-            N.check(lib.mkg_slab_expand_backward(ptr_t.data_ptr(), push_t.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                                 nk, wf.data_ptr(), n, int(t == 0), ctypes.byref(win),
-                                                 eng.store.data_ptr(),
-                                                 ctypes.byref(factor), eng.g.num_facts, gsp.data_ptr(),
-                                                 grad_w64.data_ptr(), N.ptr(grad_edge), ws.data_ptr(), ws.numel(),
-                                                 err, st), "slab_expand_backward")
+        for gi, (nt, ptrs, recs) in enumerate(eng.tile_groups):  # one walk per group of tiles
+            ev = _events(eng)  # (the first tile takes the identity messages)
+            N.check(lib.mkg_slab_expand_backward_tiles(nt, ctypes.addressof(ptrs), ctypes.addressof(recs),
+                                                       k.data_ptr(), v.data_ptr(), nk, wf.data_ptr(), n,
+                                                       int(gi == 0), ctypes.byref(win), eng.store.data_ptr(),
+                                                       ctypes.byref(factor), eng.g.num_facts, gsp.data_ptr(),
+                                                       grad_w64.data_ptr(), N.ptr(grad_edge), ws.data_ptr(),
+                                                       ws.numel(), err, st), "slab_expand_backward")
             if ev is not None:
                 ev[1].record()
                 evs.append(ev)
@@ -321,7 +371,7 @@ def expand_backward(eng: SlabEngine, keys, vals, w_h, BL: int, keys_y, parts, pu
             local_deg = (eng.ptr[1:] - eng.ptr[:-1]).to(torch.int64)
             touched = min(eng.g.num_facts, int(local_deg[mine % E].sum())) if grad_edge is not None else 0
             eng.trace.append(("bwd", evs, graph_bytes(eng, mine) + 12 * int(mine_y.numel())
-                              + 16 * int(mine.numel()) + nr * n * 4 + 4 * touched))
+                              + 16 * int(mine.numel()) + nr * n * 4 + 4 * touched, len(eng.tiles)))
     return gsp
 
 
@@ -497,19 +547,17 @@ class SlabHopLoop(autograd.Function):
             k_all, v_all, st.prune_sel = _prune(k_all, v_all, E, int(topk_nodes))
             st.keys_in, st.vals_in = k_all, v_all
             msgs.append(eng.full_degree[k_all % E].sum())
-            ky, y, d, st.parts = expand_forward(eng, k_all, v_all, wf[h], BL, check=False)
-            _all_reduce(d, spec)
-            d32 = d.to(torch.float32)
-            x = _mass_normalize(ky, y, E, BL, d32, threshold)
+            ky, y, d32, st.parts, x, dropped = expand_forward(eng, k_all, v_all, wf[h], BL, check=False,
+                                                               normalize=(spec, threshold))
             st.keys_y, st.y, st.d, st.keep = ky, y, d32, None
-            if x[1]:  # some results are zero or under the threshold: the loop drops them
-                keep = x[0] != 0
+            if dropped:  # some results are zero or under the threshold: the loop drops them
+                keep = x != 0
                 if threshold > 0:
-                    keep &= x[0] >= threshold
+                    keep &= x >= threshold
                 st.keep = keep
-                keys, vals = ky[keep], x[0][keep]
+                keys, vals = ky[keep], x[keep]
             else:
-                keys, vals = ky, x[0]
+                keys, vals = ky, x
             hops.append(st)
         out_keys, out_vals, inv = sum_over_rules(eng, keys, vals, B, L,
                                                  entity_major_state=eng.rows_per_window >= BL)

@@ -111,10 +111,12 @@ def test_slab_loop_row_windows_match_one_window():
     np.testing.assert_allclose(ge2.cpu().numpy(), ge1.cpu().numpy(), rtol=GRAD_RTOL, atol=GRAD_ATOL)
 
 
-@pytest.mark.parametrize("tiles,store_rows", [(3, 0), (4, 4)])
+@pytest.mark.parametrize("tiles,store_rows", [(3, 0), (4, 4), (11, 0)])
 def test_slab_loop_destination_tiles_match_one_tile(tiles, store_rows):
-    """Destination tiles (each its own push list and store pass), alone and with row windows:
-    the same keys, values, message counts and gradients as one tile, and the oracle's."""
+    """Destination tiles (each its own push list, walked tile by tile in one launch; 11 tiles
+    take two launches, 8 + 3, the identity messages with the first), alone and with row
+    windows: the same keys, values, message counts and gradients as one tile, and the
+    oracle's."""
     from minikg_dev_b200 import _native as N
     from minikg_dev_b200.slab_loop import slab_proof_scores
     h, r, t, E, R, heads, w_hops, scores, mask = _case("hubby", 9, 3, 3, 41)
@@ -325,3 +327,86 @@ def test_slab_loop_two_gpus_vs_oracle(topk_nodes):
         assert x[5].tolist() == want_msgs
         np.testing.assert_allclose(x[3], gw, rtol=GRAD_RTOL, atol=GRAD_ATOL)
         np.testing.assert_allclose(x[4], ge, rtol=GRAD_RTOL, atol=GRAD_ATOL)
+
+
+def _rule_sum_reference(keys, vals, E, L, take_max):
+    """sum_sp_3d / max_sp_3d on an entity-major list, written out: each run of entries with
+    one (e, b) folded in list order (fp32), the runs stably ordered by (b, e); each entry's
+    output index."""
+    e, b = keys % E, (keys // E) // L
+    runs, owner = [], np.empty(keys.size, np.int64)
+    i = 0
+    while i < keys.size:
+        acc, j = np.float32(vals[i]), i
+        while j + 1 < keys.size and e[j + 1] == e[i] and b[j + 1] == b[i]:
+            j += 1
+            acc = np.maximum(acc, vals[j]) if take_max else np.float32(acc + vals[j])
+        owner[i:j + 1] = len(runs)
+        runs.append((b[i], e[i], acc))
+        i = j + 1
+    order = sorted(range(len(runs)), key=lambda r: (runs[r][0], runs[r][1]))
+    rank = np.empty(len(runs), np.int64)
+    rank[order] = np.arange(len(runs))
+    out_k = np.array([runs[r][0] * E + runs[r][1] for r in order], np.int64)
+    out_v = np.array([runs[r][2] for r in order], np.float32)
+    return out_k, out_v, rank[owner] if keys.size else owner
+
+
+def _rule_sum_gpu(keys, vals, E, L, B, take_max):
+    from minikg_dev_b200 import _native as N
+    lib = N.load()
+    n = int(keys.size)
+    k, v = T(keys), T(vals)
+    ok = torch.empty(max(n, 1), dtype=torch.int64, device=DEV)
+    ov = torch.empty(max(n, 1), dtype=torch.float32, device=DEV)
+    pos = torch.empty(max(n, 1), dtype=torch.int64, device=DEV)
+    cnt = torch.full((1,), -1, dtype=torch.int64, device=DEV)
+    ws = N.workspace(lib.mkg_rule_sum_workspace_bytes(n), DEV)
+    N.check(lib.mkg_rule_sum(N.ptr(k), N.ptr(v), n, E, L, B, int(take_max), ok.data_ptr(), ov.data_ptr(),
+                             pos.data_ptr(), cnt.data_ptr(), N.ptr(ws), ws.numel(), N.error_word(DEV).data_ptr(),
+                             N.stream_handle(DEV)), "rule_sum")
+    N.raise_device_errors(DEV)
+    U = int(cnt.item())
+    return ok[:U].cpu().numpy(), ov[:U].cpu().numpy(), pos[:n].cpu().numpy()
+
+
+@pytest.mark.parametrize("E,B,L,n,take_max", [
+    (5000, 300, 4, 20000, False),   # counting placement: 10 blocks, runs across block and warp edges
+    (5000, 300, 4, 20000, True),
+    (900, 3, 2, 5000, False),       # many runs of one query in every warp item
+    (4000, 1, 1, 3000, False),      # one rule, one query: every entry its own run
+    (2000, 1500, 3, 12000, False),  # more queries than the counting placement takes: radix pipeline
+    (2000, 1500, 3, 12000, True),
+    (10, 4, 4, 0, False),           # empty
+])
+def test_rule_sum_entity_major(E, B, L, n, take_max):
+    """mkg_rule_sum on entity-major lists (the slab emit's order) against the written-out fold:
+    result keys, their positions and values bit-exact (fp32 sums in rule order; maxima)."""
+    rng = np.random.default_rng(n + B)
+    # about n entries: (e, b) pairs, each with a random non-empty subset of its L rules (runs of
+    # 1 .. L entries), in entity-major order (ascending entity, then row)
+    m = min(E * B, max(1, int(n / (0.7 * L + 0.3)))) if n else 0
+    pairs = rng.choice(E * B, size=m, replace=False).astype(np.int64)
+    take = rng.random((m, L)) < 0.7
+    take[np.arange(m), rng.integers(0, L, m)] = True
+    ii, ll = np.nonzero(take)
+    keys = (pairs[ii] % B * L + ll) * E + pairs[ii] // B
+    keys = keys[np.lexsort((keys // E, keys % E))].astype(np.int64)
+    vals = rng.uniform(0.01, 1.0, keys.size).astype(np.float32)
+    rk, rv, rpos = _rule_sum_reference(keys, vals, E, L, take_max)
+    gk, gv, gpos = _rule_sum_gpu(keys, vals, E, L, B, take_max)
+    np.testing.assert_array_equal(gk, rk)
+    np.testing.assert_array_equal(gv.view(np.uint32), rv.view(np.uint32))
+    np.testing.assert_array_equal(gpos, rpos)
+
+
+def test_rule_sum_refuses_unordered_and_bad_keys():
+    """An entry out of entity-major order, or outside [B, L, E], raises the device flag."""
+    E, B, L = 50, 4, 2
+    keys = np.array([0 * E + 3, 1 * E + 3, 0 * E + 7], np.int64)  # entity 3, 3, 7: ordered
+    vals = np.ones(3, np.float32)
+    _rule_sum_gpu(keys, vals, E, L, B, False)
+    with pytest.raises(RuntimeError):
+        _rule_sum_gpu(keys[[2, 0, 1]], vals, E, L, B, False)
+    with pytest.raises(RuntimeError):
+        _rule_sum_gpu(np.array([3, B * L * E + 1], np.int64), vals[:2], E, L, B, False)
