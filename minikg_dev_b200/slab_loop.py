@@ -534,9 +534,11 @@ class SlabHopLoop(autograd.Function):
         hd = heads.to(device=dev, dtype=torch.int64)
         if bool(((hd < 0) | (hd >= E)).any()):
             raise ValueError(f"query heads must lie in [0, {E})")
-        keys = (torch.arange(BL, device=dev) * E + hd.repeat_interleave(L))
-        own = (hd.repeat_interleave(L) >= eng.lo) & (hd.repeat_interleave(L) < eng.hi)
-        keys, _ = entity_major(keys[own], keys[own], E, BL)
+        src = hd.repeat_interleave(L)
+        keys = torch.arange(BL, device=dev) * E + src
+        if eng.lo > 0 or eng.hi < E:  # a destination range: this rank's heads only
+            keys = keys[(src >= eng.lo) & (src < eng.hi)]
+        keys, _ = entity_major(keys, keys, E, BL)
         vals = torch.ones(keys.numel(), dtype=torch.float32, device=dev)
         hops, msgs = [], []
         for h in range(K):
