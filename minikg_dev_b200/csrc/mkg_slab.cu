@@ -415,17 +415,17 @@ __global__ void __launch_bounds__(kTileThreads) slab_gather_kernel(Store st, Win
   unsigned long long drop = 0;
   for (int64_t i0 = blockIdx.x * kTile; i0 < count; i0 += (int64_t)gridDim.x * kTile) {
     int64_t slot[kGatherItems];
-    int32_t lrow[kGatherItems];
+    float dr[kGatherItems];  // NORM: the key's row sum, loaded with the slot (its latency overlaps)
     float v[kGatherItems];
 #pragma unroll
     for (int u = 0; u < kGatherItems; ++u) {
       const int64_t i = i0 + u * kTileThreads + threadIdx.x;
       slot[u] = -1;
-      lrow[u] = 0;
+      dr[u] = 1.0f;
       if (i < count) {
         const int64_t k = keys[i];
         const int64_t q = win.fe.div(k);
-        lrow[u] = static_cast<int32_t>(q - win.row0);
+        if (NORM) dr[u] = nm.d[q - win.row0];
         slot[u] = win.slot(q - win.row0, k - q * win.E - win.lo);
       }
     }
@@ -435,11 +435,14 @@ __global__ void __launch_bounds__(kTileThreads) slab_gather_kernel(Store st, Win
     for (int u = 0; u < kGatherItems; ++u) {
       if (slot[u] < 0) continue;
       st.val[slot[u]] = 0.0f;
-      const int64_t i = i0 + u * kTileThreads + threadIdx.x;
-      vals_out[i] = v[u];
-      if (NORM) {
-        const float dr = nm.d[lrow[u]];
-        const float x = __fdiv_rn(v[u], dr) * fminf(dr, 1.0f);
+      vals_out[i0 + u * kTileThreads + threadIdx.x] = v[u];
+    }
+    if (NORM) {  // after the stores: the slots no longer live while the divisions run
+#pragma unroll
+      for (int u = 0; u < kGatherItems; ++u) {
+        const int64_t i = i0 + u * kTileThreads + threadIdx.x;
+        if (i >= count) continue;
+        const float x = __fdiv_rn(v[u], dr[u]) * fminf(dr[u], 1.0f);
         nm.x[i] = x;
         if (x == 0.0f || (nm.thr > 0.0f && x < nm.thr)) ++drop;
       }
